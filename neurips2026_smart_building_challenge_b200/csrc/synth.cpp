@@ -1,0 +1,830 @@
+// Synthetic SBB1 scenario generator (C ABI in include/sbgen.h).
+//
+// Every section the reference C core reads is written here from a seeded
+// synthetic building. Section names, dtypes and meanings follow the
+// reference's baker (complete_port/pysim/bake_scenario.py:62-196,
+// complete_port/pysim/bake_env.py:25-396) because the blob is an interchange
+// format; the values are this generator's own.
+//
+// Thermal matrix. With cap = C*A_cell/dt, face conductances G, Dirichlet
+// exterior conductance dir, convective exposure exp(h) and an interior-mass
+// node per cell (conductance Gm, capacity Cm):
+//   A = diag(cap + dir + exp + Gm*(1-gain)) + Laplacian(G)
+//   mass_retained = (Cm/dt)/(Cm/dt+Gm), mass_gained = Gm/(Cm/dt+Gm),
+//   mass_coupling = Gm*mass_retained
+// which is the system the C core's forcing (complete_port/csim/sb_fdm.c:146-152)
+// and mass update (sb_fdm.c:183-185) imply. A is symmetric positive definite,
+// so it is factored without pivoting as B = P A P^T = L D L^T with a
+// nested-dissection P, and written as unit-lower L (diagonal stored) and
+// U = D L^T in CSC with perm_r = perm_c = P^-1, the SuperLU convention
+// sb_lu.c:5-34 replays (x = work[perm_c], work = b[inv(perm_r)]).
+#include "sbgen.h"
+#include "sbb.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <utility>
+#include <vector>
+
+namespace {
+
+const double kPi = 3.14159265358979323846;
+
+struct Rng {  // splitmix64
+    uint64_t s;
+    explicit Rng(uint64_t seed) : s(seed * 0x2545F4914F6CDD1DULL + 0x9E3779B97F4A7C15ULL) {}
+    uint64_t next() {
+        uint64_t z = (s += 0x9E3779B97F4A7C15ULL);
+        z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+        z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+        return z ^ (z >> 31);
+    }
+    double uni() { return (double)(next() >> 11) * (1.0 / 9007199254740992.0); }
+    double uni(double a, double b) { return a + (b - a) * uni(); }
+    int below(int n) { int v = (int)(uni() * n); return v < n ? v : n - 1; }
+    double normal() {
+        double u1 = uni(), u2 = uni();
+        if (u1 < 1e-300) u1 = 1e-300;
+        return std::sqrt(-2.0 * std::log(u1)) * std::cos(2.0 * kPi * u2);
+    }
+    template <class T> void shuffle(std::vector<T>& v) {
+        for (int i = (int)v.size() - 1; i > 0; i--) std::swap(v[i], v[below(i + 1)]);
+    }
+};
+
+struct Rect {
+    int r0, c0, r1, c1;
+    int h() const { return r1 - r0; }
+    int w() const { return c1 - c0; }
+};
+
+struct Factor {
+    int n = 0;
+    std::vector<int32_t> Lp, Li, Up, Ui, perm;  // perm = perm_r = perm_c
+    std::vector<double> Lx, Ux;
+};
+
+// Nested-dissection order of the solved cells of the grid rectangle:
+// both halves first, then the separator line across the longer side.
+void nd_order(int r0, int c0, int r1, int c1, int ncols, const std::vector<int>& row_of,
+              std::vector<int>& out) {
+    int h = r1 - r0, w = c1 - c0;
+    if (h <= 0 || w <= 0) return;
+    if (h * w <= 12 || (h <= 2 && w <= 2)) {
+        for (int r = r0; r < r1; r++)
+            for (int c = c0; c < c1; c++)
+                if (row_of[r * ncols + c] >= 0) out.push_back(row_of[r * ncols + c]);
+        return;
+    }
+    if (h >= w) {
+        int m = r0 + h / 2;
+        nd_order(r0, c0, m, c1, ncols, row_of, out);
+        nd_order(m + 1, c0, r1, c1, ncols, row_of, out);
+        for (int c = c0; c < c1; c++)
+            if (row_of[m * ncols + c] >= 0) out.push_back(row_of[m * ncols + c]);
+    } else {
+        int m = c0 + w / 2;
+        nd_order(r0, c0, r1, m, ncols, row_of, out);
+        nd_order(r0, m + 1, r1, c1, ncols, row_of, out);
+        for (int r = r0; r < r1; r++)
+            if (row_of[r * ncols + m] >= 0) out.push_back(row_of[r * ncols + m]);
+    }
+}
+
+// Right-looking sparse LDL^T of B = A[p][:,p] on sorted column lists.
+// A is given as symmetric adjacency (off-diagonal per row) plus diagonal.
+bool ldlt(int n, const std::vector<double>& diagA,
+          const std::vector<std::vector<std::pair<int, double>>>& offA, const std::vector<int>& p,
+          Factor& F) {
+    std::vector<int> ip(n);
+    for (int i = 0; i < n; i++) ip[p[i]] = i;
+    std::vector<std::vector<std::pair<int, double>>> col(n);
+    std::vector<double> d(n);
+    for (int t = 0; t < n; t++) {
+        int j = ip[t];
+        d[j] = diagA[t];
+        for (auto& e : offA[t]) {
+            int i = ip[e.first];
+            if (i > j) col[j].push_back({i, e.second});
+        }
+    }
+    for (auto& c : col) std::sort(c.begin(), c.end());
+    std::vector<std::pair<int, double>> merged;
+    for (int j = 0; j < n; j++) {
+        const double dj = d[j];
+        if (!(dj > 0.0)) return false;
+        auto& cj = col[j];
+        for (auto& e : cj) e.second /= dj;
+        for (size_t a = 0; a < cj.size(); a++) {
+            const int ia = cj[a].first;
+            const double f = cj[a].second * dj;
+            d[ia] -= f * cj[a].second;
+            auto& ca = col[ia];
+            merged.clear();
+            size_t x = 0, y = a + 1;
+            while (x < ca.size() || y < cj.size()) {
+                if (y >= cj.size() || (x < ca.size() && ca[x].first < cj[y].first)) {
+                    merged.push_back(ca[x++]);
+                } else if (x >= ca.size() || cj[y].first < ca[x].first) {
+                    merged.push_back({cj[y].first, -f * cj[y].second});
+                    y++;
+                } else {
+                    merged.push_back({ca[x].first, ca[x].second - f * cj[y].second});
+                    x++;
+                    y++;
+                }
+            }
+            ca.swap(merged);
+        }
+    }
+    F.n = n;
+    F.Lp.assign(n + 1, 0);
+    for (int j = 0; j < n; j++) F.Lp[j + 1] = F.Lp[j] + 1 + (int32_t)col[j].size();
+    F.Li.resize(F.Lp[n]);
+    F.Lx.resize(F.Lp[n]);
+    std::vector<std::vector<std::pair<int, double>>> ucol(n);
+    for (int j = 0; j < n; j++) {
+        int q = F.Lp[j];
+        F.Li[q] = j;
+        F.Lx[q] = 1.0;
+        q++;
+        for (auto& e : col[j]) {
+            F.Li[q] = e.first;
+            F.Lx[q] = e.second;
+            q++;
+            ucol[e.first].push_back({j, d[j] * e.second});
+        }
+    }
+    F.Up.assign(n + 1, 0);
+    for (int j = 0; j < n; j++) F.Up[j + 1] = F.Up[j] + 1 + (int32_t)ucol[j].size();
+    F.Ui.resize(F.Up[n]);
+    F.Ux.resize(F.Up[n]);
+    for (int j = 0; j < n; j++) {
+        int q = F.Up[j];
+        for (auto& e : ucol[j]) { F.Ui[q] = e.first; F.Ux[q] = e.second; q++; }
+        F.Ui[q] = j;
+        F.Ux[q] = d[j];
+    }
+    F.perm.resize(n);
+    for (int i = 0; i < n; i++) F.perm[p[i]] = i;  // perm_r = perm_c = inv(p)
+    return true;
+}
+
+// x = A^-1 b through the stored factors, in the replay order of
+// complete_port/csim/sb_lu.c:38-63 (used only for the solref self-check).
+void replay_solve(const Factor& F, const std::vector<double>& b, std::vector<double>& x) {
+    const int n = F.n;
+    std::vector<int> ir(n);
+    for (int i = 0; i < n; i++) ir[F.perm[i]] = i;
+    std::vector<double> w(n);
+    for (int i = 0; i < n; i++) w[i] = b[ir[i]];
+    for (int j = 0; j < n; j++)
+        for (int q = F.Lp[j]; q < F.Lp[j + 1]; q++)
+            if (F.Li[q] != j) w[F.Li[q]] -= F.Lx[q] * w[j];
+    for (int j = n - 1; j >= 0; j--) {
+        w[j] /= F.Ux[F.Up[j + 1] - 1];
+        for (int q = F.Up[j]; q < F.Up[j + 1] - 1; q++) w[F.Ui[q]] -= F.Ux[q] * w[j];
+    }
+    x.resize(n);
+    for (int k = 0; k < n; k++) x[k] = w[F.perm[k]];
+}
+
+struct Calendar {
+    int day, hour, month, dow;  // dow: 0 Sunday
+    double hod;                 // fractional hour of day
+    bool workday;
+};
+
+Calendar calendar_at(const SbGenParams& P, long step) {
+    static const int mlen[12] = {31, 28, 31, 30, 31, 30, 31, 31, 30, 31, 30, 31};
+    double t = (double)step * P.dt_sec + P.start_hour * 3600.0;
+    long day_off = (long)std::floor(t / 86400.0);
+    double sec = t - (double)day_off * 86400.0;
+    Calendar c;
+    c.day = (int)(P.start_doy + day_off);
+    c.hod = sec / 3600.0;
+    c.hour = (int)std::floor(c.hod);
+    c.dow = ((c.day % 7) + 7) % 7;  // day 0 = 2023-01-01, a Sunday
+    c.workday = c.dow >= 1 && c.dow <= 5;
+    int d = ((c.day % 365) + 365) % 365, m = 0;
+    while (m < 11 && d >= mlen[m]) d -= mlen[m++];
+    c.month = m + 1;
+    return c;
+}
+
+bool comfort_at(const SbGenParams& P, double t_off_sec, long step) {
+    double t = (double)step * P.dt_sec + P.start_hour * 3600.0 + t_off_sec;
+    long day_off = (long)std::floor(t / 86400.0);
+    double hod = (t - (double)day_off * 86400.0) / 3600.0;
+    int dow = (((P.start_doy + (int)day_off) % 7) + 7) % 7;
+    bool wd = dow >= 1 && dow <= 5;
+    return wd && hod >= 6.0 && hod < 19.0;
+}
+
+struct Built {
+    sbb::Writer w;
+    int64_t n = 0, nnzL = 0, nnzU = 0;
+};
+
+std::string build(const SbGenParams& P, Built& out) {
+    const int R = P.rows, C = P.cols, ncv = R * C;
+    if (R < 4 || C < 4 || P.n_rooms < 1 || P.n_ahu < 1 || P.n_ahu > P.n_rooms)
+        return "invalid grid/room/AHU counts";
+    if (P.n_steps < 1 || P.dt_sec <= 0.0) return "invalid episode length";
+    Rng rng(P.layout_seed);
+    const double cv = P.cv_size_cm / 100.0;
+    const double a_cell = cv * cv;
+    const double wall_h = 3.0;
+    const double a_face = cv * wall_h;
+
+    // --- rooms: recursive rectangular partition ---
+    std::vector<Rect> rects{{0, 0, R, C}};
+    while ((int)rects.size() < P.n_rooms) {
+        int best = -1;
+        for (int i = 0; i < (int)rects.size(); i++) {
+            const Rect& r = rects[i];
+            if (std::max(r.h(), r.w()) < 4) continue;
+            if (best < 0 || r.h() * r.w() > rects[best].h() * rects[best].w()) best = i;
+        }
+        if (best < 0) return "grid too small for the requested room count";
+        Rect r = rects[best], a = r, b = r;
+        if (r.h() >= r.w()) {
+            int cut = r.r0 + std::min(std::max((int)std::lround(r.h() * rng.uni(0.35, 0.65)), 2), r.h() - 2);
+            a.r1 = cut;
+            b.r0 = cut;
+        } else {
+            int cut = r.c0 + std::min(std::max((int)std::lround(r.w() * rng.uni(0.35, 0.65)), 2), r.w() - 2);
+            a.c1 = cut;
+            b.c0 = cut;
+        }
+        rects[best] = a;
+        rects.push_back(b);
+    }
+    std::sort(rects.begin(), rects.end(),
+              [](const Rect& x, const Rect& y) { return x.r0 != y.r0 ? x.r0 < y.r0 : x.c0 < y.c0; });
+    const int nz = P.n_rooms;
+    std::vector<int> zone_of(ncv, -1);
+    for (int z = 0; z < nz; z++)
+        for (int r = rects[z].r0; r < rects[z].r1; r++)
+            for (int c = rects[z].c0; c < rects[z].c1; c++) zone_of[r * C + c] = z;
+    for (int r = 0; r < P.notch_rows && r < R; r++)
+        for (int c = C - P.notch_cols; c < C; c++)
+            if (c >= 0) zone_of[r * C + c] = -1;
+    std::vector<std::vector<int>> zcells(nz);
+    for (int p = 0; p < ncv; p++)
+        if (zone_of[p] >= 0) zcells[zone_of[p]].push_back(p);
+    for (int z = 0; z < nz; z++)
+        if (zcells[z].empty()) return "exterior notch swallows a whole room";
+
+    // --- solved cells (every interior cell, ascending) ---
+    std::vector<int> row_of(ncv, -1);
+    std::vector<int64_t> solved;
+    for (int p = 0; p < ncv; p++)
+        if (zone_of[p] >= 0) {
+            row_of[p] = (int)solved.size();
+            solved.push_back(p);
+        }
+    const int n = (int)solved.size();
+
+    // --- materials and conductances ---
+    std::vector<double> u_ext(nz);
+    for (int z = 0; z < nz; z++) u_ext[z] = rng.uni(0.3, 0.6);
+    std::map<std::pair<int, int>, double> u_int;
+    auto wall_u = [&](int z1, int z2) {
+        auto key = std::make_pair(std::min(z1, z2), std::max(z1, z2));
+        auto it = u_int.find(key);
+        if (it != u_int.end()) return it->second;
+        double u = rng.uni(1.5, 3.0);
+        u_int[key] = u;
+        return u;
+    };
+    const double g_air = 30.0;  // well-mixed air between cells of one room, W/K
+    const double a_win = 0.3;   // convective ambient face per exterior side, m^2
+    const double k_env = 0.8;   // envelope conductivity, W/mK
+    std::vector<double> cap(n), dir(n, 0.0), gm(n, 0.0), ret(n, 1.0), gain(n, 0.0), mc(n, 0.0);
+    std::vector<double> hor(ncv, cv), ver(ncv, cv), cond(ncv, k_env), af0(ncv, 0.0), af1(ncv, 0.0);
+    std::vector<double> diagA(n, 0.0);
+    std::vector<std::vector<std::pair<int, double>>> offA(n);
+    for (int t = 0; t < n; t++) {
+        const int p = (int)solved[t];
+        const int r = p / C, c = p % C, z = zone_of[p];
+        cap[t] = rng.uni(1.0e5, 2.0e5) * a_cell / P.dt_sec;
+        if (rng.uni() < 0.25) {
+            const double Gm = 8.0, cm_rate = 4.0e5 / P.dt_sec;
+            gm[t] = Gm;
+            ret[t] = cm_rate / (cm_rate + Gm);
+            gain[t] = Gm / (cm_rate + Gm);
+            mc[t] = Gm * ret[t];
+        }
+        const int dr[4] = {-1, 1, 0, 0}, dc[4] = {0, 0, -1, 1};
+        for (int k = 0; k < 4; k++) {
+            int r2 = r + dr[k], c2 = c + dc[k];
+            bool outside = r2 < 0 || r2 >= R || c2 < 0 || c2 >= C || zone_of[r2 * C + c2] < 0;
+            if (outside) {
+                dir[t] += u_ext[z] * a_face;
+                if (k < 2) af0[p] += a_win; else af1[p] += a_win;
+                continue;
+            }
+            const int p2 = r2 * C + c2, z2 = zone_of[p2];
+            double g;
+            if (z2 == z) {
+                g = g_air;
+                // partition faces: keyed on the unordered cell pair so both sides agree
+                if (P.dense_walls) {
+                    uint64_t key = (uint64_t)std::min(p, p2) * 1000003ULL + (uint64_t)std::max(p, p2);
+                    Rng fr(P.layout_seed ^ (key * 0x9E3779B97F4A7C15ULL));
+                    if (fr.uni() < 0.12) g = fr.uni(1.5, 3.0) * a_face;
+                }
+            } else {
+                g = wall_u(z, z2) * a_face;
+            }
+            diagA[t] += g;
+            offA[t].push_back({row_of[p2], -g});
+        }
+    }
+    const double h_conv = 8.8;
+    std::vector<double> expo(n, 0.0);
+    for (int t = 0; t < n; t++) {
+        const int p = (int)solved[t];
+        double e = 0.0;
+        if (af0[p] > 0.0) e += h_conv * af0[p] / (1.0 + h_conv * 0.5 * hor[p] / cond[p]);
+        if (af1[p] > 0.0) e += h_conv * af1[p] / (1.0 + h_conv * 0.5 * ver[p] / cond[p]);
+        expo[t] = e;
+        diagA[t] += cap[t] + dir[t] + e + gm[t] * (1.0 - gain[t]);
+    }
+
+    // --- factor ---
+    std::vector<int> order;
+    order.reserve(n);
+    nd_order(0, 0, R, C, C, row_of, order);
+    if ((int)order.size() != n) return "internal: ordering lost cells";
+    Factor F;
+    if (!ldlt(n, diagA, offA, order, F)) return "factorization hit a non-positive pivot";
+    out.n = n;
+    out.nnzL = F.Lp[n];
+    out.nnzU = F.Up[n];
+
+    // A_system in CSC (symmetric: columns = rows)
+    std::vector<int32_t> Ap(n + 1, 0), Ai;
+    std::vector<double> Ax;
+    for (int t = 0; t < n; t++) {
+        std::vector<std::pair<int, double>> colv = offA[t];
+        colv.push_back({t, diagA[t]});
+        std::sort(colv.begin(), colv.end());
+        for (auto& e : colv) { Ai.push_back(e.first); Ax.push_back(e.second); }
+        Ap[t + 1] = (int32_t)Ai.size();
+    }
+    std::vector<double> sb(n), sx;
+    for (int t = 0; t < n; t++) sb[t] = std::sin(0.1 * t + 1.0);
+    replay_solve(F, sb, sx);
+    {
+        double rn = 0.0, bn = 0.0;
+        for (int t = 0; t < n; t++) {
+            double acc = 0.0;
+            for (int q = Ap[t]; q < Ap[t + 1]; q++) acc += Ax[q] * sx[Ai[q]];
+            rn = std::max(rn, std::fabs(acc - sb[t]));
+            bn = std::max(bn, std::fabs(sb[t]));
+        }
+        if (!(rn <= 1e-9 * bn)) return "factor self-check failed (residual too large)";
+    }
+
+    // --- HVAC topology ---
+    const int nv = nz, na = P.n_ahu, k = nv;
+    std::vector<int> vz(nv), cvi(k), ahu_of_zone(nz);
+    for (int v = 0; v < nv; v++) vz[v] = v;
+    rng.shuffle(vz);
+    for (int c = 0; c < k; c++) cvi[c] = c;
+    rng.shuffle(cvi);
+    for (int z = 0; z < nz; z++) ahu_of_zone[z] = (int)((int64_t)z * na / nz);
+    std::vector<int> vav_of_zone(nz);
+    for (int v = 0; v < nv; v++) vav_of_zone[vz[v]] = v;
+
+    sbb::Writer& w = out.w;
+    w.add_str("generator", "sbgen synthetic scenario");
+    w.add_i64("grid", {R, C});
+    std::vector<double> tinit(ncv);
+    std::vector<double> zone_t0(nz);
+    for (int z = 0; z < nz; z++) zone_t0[z] = 293.15 + rng.uni(-1.0, 1.0);
+    // weather first: exterior cells start at the first ambient value
+    Rng wr(P.climate_seed);
+    const long T = P.n_steps;
+    std::vector<double> amb(T + 1);
+    {
+        const double sd_innov = P.ar_sigma_k * std::sqrt(std::max(0.0, 1.0 - P.ar_phi * P.ar_phi));
+        double ar = P.ar_sigma_k * wr.normal();
+        for (long s = 0; s <= T; s++) {
+            if (s > 0) ar = P.ar_phi * ar + sd_innov * wr.normal();
+            Calendar c = calendar_at(P, s);
+            amb[s] = 273.15 + P.t_mean_c + P.t_amp_k * std::sin(2.0 * kPi * (c.hod - 9.0) / 24.0) + ar;
+        }
+    }
+    for (int p = 0; p < ncv; p++) tinit[p] = zone_of[p] >= 0 ? zone_t0[zone_of[p]] : amb[0];
+    w.add_f64("temp_init", tinit);
+    w.add_f64("cv_size_cm", {P.cv_size_cm});
+    w.add_f64("initial_temp", {293.15});
+
+    // rooms: 0 = exterior_space (the notch), 1.. = physical zones
+    std::vector<int32_t> room_off{0}, room_cells;
+    std::string room_names = "exterior_space";
+    for (int p = 0; p < ncv; p++)
+        if (zone_of[p] < 0) { room_cells.push_back(p / C); room_cells.push_back(p % C); }
+    room_off.push_back((int32_t)room_cells.size() / 2);
+    for (int z = 0; z < nz; z++) {
+        for (int p : zcells[z]) { room_cells.push_back(p / C); room_cells.push_back(p % C); }
+        room_off.push_back((int32_t)room_cells.size() / 2);
+        room_names += "\nroom_" + std::to_string(z + 1);
+    }
+    w.add_str("room_names", room_names);
+    w.add_i32("room_offsets", room_off);
+    w.add_i32("room_cells", room_cells);
+
+    w.add_i64("solved", solved);
+    w.add_f64("dirichlet_conductance", dir);
+    w.add_f64("capacitance_rate", cap);
+    w.add_f64("mass_coupling", mc);
+    w.add_f64("mass_retained", ret);
+    w.add_f64("mass_gained", gain);
+    std::vector<double> minit(n);
+    for (int t = 0; t < n; t++) minit[t] = tinit[solved[t]];
+    w.add_f64("mass_temp_init", minit);
+    w.add_f64("horizontal", hor);
+    w.add_f64("vertical", ver);
+    w.add_f64("solver_conductivity", cond);
+    w.add_f64("ambient_face_areas_0", af0);
+    w.add_f64("ambient_face_areas_1", af1);
+    w.add_f64("convection_coefficient", {h_conv});
+    w.add_i64("A_system_shape", {n, n});
+    w.add_i32("A_system_indptr", Ap);
+    w.add_i32("A_system_indices", Ai);
+    w.add_f64("A_system_data", Ax);
+    w.add_i32("lu_perm_r", F.perm);
+    w.add_i32("lu_perm_c", F.perm);
+    w.add_i64("lu_L_shape", {n, n});
+    w.add_i32("lu_L_indptr", F.Lp);
+    w.add_i32("lu_L_indices", F.Li);
+    w.add_f64("lu_L_data", F.Lx);
+    w.add_i64("lu_U_shape", {n, n});
+    w.add_i32("lu_U_indptr", F.Up);
+    w.add_i32("lu_U_indices", F.Ui);
+    w.add_f64("lu_U_data", F.Ux);
+    w.add_f64("solref_b", sb);
+    w.add_f64("solref_x", sx);
+
+    // --- air side: each coupled VAV heats/cools and senses its zone uniformly ---
+    {
+        std::vector<int32_t> ap{0}, ai, sp{0}, si, xp{0}, xi;
+        std::vector<double> ax, sx2, xx;
+        for (int c = 0; c < k; c++) {
+            const int z = vz[cvi[c]];
+            const double wgt = 1.0 / (double)zcells[z].size();
+            for (int p : zcells[z]) { ai.push_back(row_of[p]); ax.push_back(wgt); }
+            ap.push_back((int32_t)ai.size());
+            for (int p : zcells[z]) { si.push_back(row_of[p]); sx2.push_back(wgt); }
+            sp.push_back((int32_t)si.size());
+        }
+        std::vector<int> col_of_zone(nz);
+        for (int c = 0; c < k; c++) col_of_zone[vz[cvi[c]]] = c;
+        for (int p = 0; p < ncv; p++) {
+            if (zone_of[p] >= 0) {
+                const int z = zone_of[p];
+                xi.push_back(col_of_zone[z]);
+                xx.push_back(1.0 / (double)zcells[z].size());
+            }
+            xp.push_back((int32_t)xi.size());
+        }
+        w.add_i64("applied_shape", {n, k});
+        w.add_i32("applied_indptr", ap);
+        w.add_i32("applied_indices", ai);
+        w.add_f64("applied_data", ax);
+        w.add_i64("sensed_shape", {k, n});
+        w.add_i32("sensed_indptr", sp);
+        w.add_i32("sensed_indices", si);
+        w.add_f64("sensed_data", sx2);
+        w.add_i64("air_side_sensed_shape", {ncv, k});
+        w.add_i32("air_side_sensed_indptr", xp);
+        w.add_i32("air_side_sensed_indices", xi);
+        w.add_f64("air_side_sensed_data", xx);
+    }
+
+    // --- convection: each physical room, candidates within Chebyshev distance ---
+    {
+        std::vector<int32_t> coff{0}, ccells, cand_off, cand_idx;
+        for (int z = 0; z < nz; z++) {
+            const int base = (int)ccells.size() / 2;
+            const auto& cells = zcells[z];
+            for (int p : cells) { ccells.push_back(p / C); ccells.push_back(p % C); }
+            coff.push_back((int32_t)ccells.size() / 2);
+            for (size_t a = 0; a < cells.size(); a++) {
+                cand_off.push_back((int32_t)cand_idx.size());
+                const int ra = cells[a] / C, ca = cells[a] % C;
+                for (size_t b = 0; b < cells.size(); b++) {
+                    if (a == b) continue;
+                    const int rb = cells[b] / C, cb = cells[b] % C;
+                    if (std::abs(ra - rb) <= P.conv_distance && std::abs(ca - cb) <= P.conv_distance)
+                        cand_idx.push_back(base + (int32_t)b);
+                }
+            }
+        }
+        cand_off.push_back((int32_t)cand_idx.size());
+        w.add_f64("conv_p", {P.conv_p});
+        w.add_f64("conv_distance", {(double)P.conv_distance});
+        w.add_i64("conv_seed", {P.conv_seed});
+        w.add_i32("conv_room_offsets", coff);
+        w.add_i32("conv_room_cells", ccells);
+        w.add_i32("conv_cand_offsets", cand_off);
+        w.add_i32("conv_cand_idx", cand_idx);
+    }
+
+    w.add_f64("internal_gain_w_per_m2", {10.0});
+    w.add_f64("internal_gain_standby_fraction", {0.2});
+    w.add_f64("occupant_sensible_heat_w", {70.0});
+
+    // --- HVAC constants ---
+    std::vector<double> vav_const(nv * 9), ahu_const(na * 9);
+    std::vector<double> ahu_maxflow(na, 0.0);
+    for (int v = 0; v < nv; v++) {
+        const int z = vz[v];
+        const double maxflow = 0.0016 * (double)zcells[z].size() * rng.uni(0.8, 1.2);
+        ahu_maxflow[ahu_of_zone[z]] += maxflow;
+        double* c = &vav_const[v * 9];
+        c[0] = maxflow;
+        c[1] = rng.uni(0.4, 1.0);   // reheat water flow factor
+        c[2] = rng.uni(0.1, 0.2);   // min damper
+        c[3] = 318.15;              // max discharge air temperature
+        c[4] = 500.0;               // static pressure at max flow
+        c[5] = 294.15;
+        c[6] = 297.15;
+        c[7] = 0.5;
+        c[8] = 0.0;
+    }
+    for (int a = 0; a < na; a++) {
+        double* c = &ahu_const[a * 9];
+        c[0] = 0.7;
+        c[1] = 0.8 * ahu_maxflow[a];
+        c[2] = 100.0;
+        c[3] = 0.9;
+        c[4] = 3.5;
+        c[5] = 0.6;
+        c[6] = 286.15;
+        c[7] = 400.0;
+        c[8] = 1.0;
+    }
+    w.add("ahu_const", sbb::F64, ahu_const.data(), {(uint64_t)na, 9});
+    w.add("vav_const", sbb::F64, vav_const.data(), {(uint64_t)nv, 9});
+    {
+        std::vector<int32_t> voff, vidx, vahu, zoff{0}, zidx, cvv(cvi.begin(), cvi.end()), pri;
+        for (int v = 0; v <= nv; v++) voff.push_back(v);
+        for (int v = 0; v < nv; v++) { vidx.push_back(vz[v]); vahu.push_back(ahu_of_zone[vz[v]]); }
+        for (int z = 0; z < nz; z++) { zidx.push_back(vav_of_zone[z]); zoff.push_back(z + 1); }
+        for (int z = 0; z < nz; z++) pri.push_back(z + 1);
+        std::vector<double> zarea(nz);
+        for (int z = 0; z < nz; z++) zarea[z] = (double)zcells[z].size();
+        w.add_i32("vav_zone_offsets", voff);
+        w.add_i32("vav_zone_idx", vidx);
+        w.add_i32("vav_ahu_idx", vahu);
+        w.add_i32("coupled_vav_idx", cvv);
+        w.add_i32("zone_vav_offsets", zoff);
+        w.add_i32("zone_vav_idx", zidx);
+        w.add_i32("phys_room_idx", pri);
+        w.add_f64("zone_area", zarea);
+    }
+    w.add_f64("hws_header_resistance", {0.002});
+    w.add_f64("hws_is_boiler", {1.0});
+    w.add_f64("boiler_const", {333.15, 323.15, 0.5, 0.25, 5.0, 2.0, 0.5, 1.5, 0.05, 0.05});
+    w.add_f64("pump_const", {12.0, 0.7});
+
+    // --- actions: per AHU [sat sp, static sp, recirc, run], HWS [supply T sp, dp sp, run], per VAV [damper, reheat]
+    {
+        std::vector<uint8_t> kind, act, disc;
+        std::vector<int32_t> idx;
+        std::vector<double> mn, mx;
+        auto push = [&](int kd, int ix, int ac, int ds, double lo, double hi) {
+            kind.push_back((uint8_t)kd); idx.push_back(ix); act.push_back((uint8_t)ac);
+            disc.push_back((uint8_t)ds); mn.push_back(lo); mx.push_back(hi);
+        };
+        for (int a = 0; a < na; a++) {
+            push(0, a, 0, 0, 283.15, 293.15);
+            push(0, a, 1, 0, 100.0, 1000.0);
+            push(0, a, 2, 0, 0.0, 0.9);
+            push(0, a, 3, 1, 0.0, 1.0);
+        }
+        push(2, 0, 0, 0, 310.15, 353.15);
+        push(2, 0, 1, 0, 0.5, 2.0);
+        push(2, 0, 2, 1, 0.0, 1.0);
+        for (int v = 0; v < nv; v++) {
+            push(1, v, 0, 0, 0.0, 1.0);
+            push(1, v, 1, 0, 0.0, 1.0);
+        }
+        std::vector<double> mnr(kind.size(), -1.0), mxr(kind.size(), 1.0);
+        w.add_u8("act_owner_kind", kind);
+        w.add_i32("act_owner_index", idx);
+        w.add_u8("act_actuator", act);
+        w.add_u8("act_is_discrete", disc);
+        w.add_f64("act_min_native", mn);
+        w.add_f64("act_max_native", mx);
+        w.add_f64("act_min_norm", mnr);
+        w.add_f64("act_max_norm", mxr);
+    }
+
+    // --- observation layout: AHU ids 0..9, VAV ids 0..5, HWS ids 0..6 ---
+    const int n_aux = 7;
+    {
+        std::vector<uint8_t> fk, fo;
+        std::vector<int32_t> fi;
+        std::vector<double> fm, fv;
+        auto push = [&](int kd, int ix, int id, double mean, double var) {
+            fk.push_back((uint8_t)kd); fi.push_back(ix); fo.push_back((uint8_t)id);
+            fm.push_back(mean); fv.push_back(var);
+        };
+        for (int a = 0; a < na; a++) {
+            const double mf = ahu_const[a * 9 + 1];
+            push(0, a, 0, nv / (2.0 * na), (nv / (2.0 * na)) * (nv / (2.0 * na)));
+            push(0, a, 1, 400.0, 40000.0);
+            push(0, a, 2, 0.5 * mf, 0.25 * mf * mf);
+            push(0, a, 3, 288.0, 9.0);
+            push(0, a, 4, 0.5, 0.25);
+            push(0, a, 5, 0.5, 0.09);
+            push(0, a, 6, 0.2 * mf, 0.04 * mf * mf);
+            push(0, a, 7, 0.5, 0.25);
+            push(0, a, 8, 0.6, 0.09);
+            push(0, a, 9, 273.15 + P.t_mean_c, 100.0);
+        }
+        for (int v = 0; v < nv; v++) {
+            push(1, v, 0, 0.3, 0.1);
+            push(1, v, 1, 0.5, 0.1);
+            push(1, v, 2, vav_const[v * 9], 0.0);
+            push(1, v, 3, 297.0, 4.0);
+            push(1, v, 4, 293.0, 4.0);
+            push(1, v, 5, 295.0, 9.0);
+        }
+        push(2, 0, 0, 1.2, 0.3);
+        push(2, 0, 1, 333.0, 100.0);
+        push(2, 0, 2, 1.2, 0.3);
+        push(2, 0, 3, 0.5, 0.25);
+        push(2, 0, 4, (double)nv, 1.0);
+        push(2, 0, 5, 0.5, 0.25);
+        push(2, 0, 6, 333.0, 100.0);
+        // deterministic interleave so kinds are mixed in the field order
+        std::vector<int> perm(fk.size());
+        for (size_t i = 0; i < perm.size(); i++) perm[i] = (int)i;
+        rng.shuffle(perm);
+        std::vector<uint8_t> fk2, fo2;
+        std::vector<int32_t> fi2;
+        std::vector<double> fm2, fv2;
+        for (int i : perm) {
+            fk2.push_back(fk[i]); fi2.push_back(fi[i]); fo2.push_back(fo[i]);
+            fm2.push_back(fm[i]); fv2.push_back(fv[i]);
+        }
+        w.add_u8("f_dev_kind", fk2);
+        w.add_i32("f_dev_idx", fi2);
+        w.add_u8("f_obs_id", fo2);
+        w.add_f64("f_norm_mean", fm2);
+        w.add_f64("f_norm_var", fv2);
+        w.add_i64("n_dev", {(int64_t)fk2.size()});
+        w.add_i64("n_aux", {n_aux});
+    }
+
+    // --- calendars, schedules, weather ---
+    {
+        std::vector<double> aux((size_t)(T + 1) * (n_aux - 1));
+        std::vector<double> sc(T + 1), sh(T + 1), sco(T + 1);
+        std::vector<int64_t> oh(T + 1), rh(T + 1), rm(T + 1);
+        std::vector<uint8_t> ow(T + 1), rw(T + 1);
+        for (long s = 0; s <= T; s++) {
+            Calendar c = calendar_at(P, s);
+            bool cm = comfort_at(P, 0.0, s);
+            double* a = &aux[(size_t)s * (n_aux - 1)];
+            a[0] = std::cos(2.0 * kPi * c.hod / 24.0);
+            a[1] = std::sin(2.0 * kPi * c.hod / 24.0);
+            a[2] = std::cos(2.0 * kPi * c.dow / 7.0);
+            a[3] = std::sin(2.0 * kPi * c.dow / 7.0);
+            a[4] = cm ? 1.0 : 0.0;
+            a[5] = comfort_at(P, 3600.0, s) ? 1.0 : 0.0;
+            sc[s] = cm ? 1.0 : 0.0;
+            sh[s] = cm ? 294.15 : 288.15;
+            sco[s] = cm ? 297.15 : 301.15;
+            oh[s] = c.hour;
+            ow[s] = c.workday ? 1 : 0;
+            rh[s] = c.hour;
+            rm[s] = c.month;
+            rw[s] = c.workday ? 1 : 0;
+        }
+        w.add("aux_time", sbb::F64, aux.data(), {(uint64_t)(T + 1), (uint64_t)(n_aux - 1)});
+        w.add_f64("obs_meta", {1.0, 1.0, 1.0, (double)T, P.dt_sec});
+        w.add_f64("sched_comfort", sc);
+        w.add_f64("sched_heat_sp", sh);
+        w.add_f64("sched_cool_sp", sco);
+        w.add_f64("weather_ambient", amb);
+        std::vector<double> wconv(T, h_conv);
+        w.add_f64("weather_convection", wconv);
+        w.add_i64("occ_hour", oh);
+        w.add_u8("occ_workday", ow);
+        Calendar cm1 = calendar_at(P, -1);
+        w.add_i64("occ_hour_m1", {cm1.hour});
+        w.add_u8("occ_workday_m1", {(uint8_t)(cm1.workday ? 1 : 0)});
+        w.add_i64("rew_hour", rh);
+        w.add_i64("rew_month", rm);
+        w.add_u8("rew_workday", rw);
+        w.add_f64("occ_params", {(double)P.zone_assignment, 7.0, 9.0, 17.0, 19.0, P.dt_sec});
+        w.add_i64("occ_seed", {P.occ_seed});
+    }
+
+    // --- reward tables ($ and kg per joule; the normalised terms are unit-free) ---
+    {
+        const double J = 3.6e6;
+        const double scale = (double)nz / 41.0;
+        w.add_f64("reward_scalars", {50.0, 0.0, 1.5, 60.0e3 * scale, 120.0e3 * scale, 0.5, 0.25, 0.25});
+        std::vector<double> wd(24), we(24), ec(24), gp(12);
+        for (int h = 0; h < 24; h++) {
+            wd[h] = ((h >= 12 && h < 18) ? 0.25 : 0.10) / J;
+            we[h] = 0.10 / J;
+            ec[h] = (0.4 + 0.1 * std::sin(2.0 * kPi * h / 24.0)) / J;
+        }
+        for (int m = 0; m < 12; m++) gp[m] = (0.04 + 0.01 * std::cos(2.0 * kPi * m / 12.0)) / J;
+        w.add_f64("elec_weekday_price", wd);
+        w.add_f64("elec_weekend_price", we);
+        w.add_f64("elec_carbon_rate", ec);
+        w.add_f64("gas_month_price", gp);
+        w.add_f64("gas_carbon_rate", {0.18 / J});
+    }
+    return "";
+}
+
+}  // namespace
+
+extern "C" int sbgen_preset(int config, int index, SbGenParams* o) {
+    if (!o) return -1;
+    memset(o, 0, sizeof(*o));
+    o->n_steps = 8640;
+    o->start_doy = 15;  // Monday 2023-01-16; the month rolls into February
+    o->start_hour = 0;
+    o->zone_assignment = 5;
+    o->conv_distance = 2;
+    o->cv_size_cm = 50.0;
+    o->dt_sec = 300.0;
+    o->ar_phi = 0.98;
+    o->ar_sigma_k = 1.0;
+    o->conv_p = 0.1;
+    if (config == 1) {
+        if (index != 0) return -1;
+        o->rows = 64; o->cols = 48; o->n_rooms = 41; o->n_ahu = 1;
+        o->t_mean_c = 15.0; o->t_amp_k = 8.0;
+        o->layout_seed = 101; o->climate_seed = 0;
+        o->occ_seed = 17321; o->conv_seed = 5;
+        return 0;
+    }
+    if (config == 2) {
+        if (index < 0 || index >= 30) return -1;
+        static const int rooms[6] = {41, 49, 57, 65, 73, 81};
+        static const int ahus[6] = {1, 2, 2, 3, 3, 4};
+        static const int gr[6] = {64, 64, 64, 72, 72, 80};
+        static const int gc[6] = {48, 48, 56, 56, 64, 64};
+        static const double tmean[5] = {-5.0, 5.0, 15.0, 25.0, 32.0};
+        static const double tamp[5] = {4.0, 5.5, 7.0, 8.5, 10.0};
+        const int L = index / 5, c = index % 5;
+        o->rows = gr[L]; o->cols = gc[L]; o->n_rooms = rooms[L]; o->n_ahu = ahus[L];
+        o->t_mean_c = tmean[c]; o->t_amp_k = tamp[c];
+        o->layout_seed = 1000 + (uint64_t)L;
+        o->climate_seed = 2000 + 10 * (uint64_t)L + (uint64_t)c;
+        o->occ_seed = 17321 + 7 * index;
+        o->conv_seed = 5 + index;
+        return 0;
+    }
+    if (config == 3) {
+        if (index != 0) return -1;
+        o->rows = 128; o->cols = 96; o->n_rooms = 81; o->n_ahu = 4; o->dense_walls = 1;
+        o->t_mean_c = 15.0; o->t_amp_k = 8.0;
+        o->layout_seed = 303; o->climate_seed = 3;
+        o->occ_seed = 17321; o->conv_seed = 5;
+        return 0;
+    }
+    return -1;
+}
+
+extern "C" int sbgen_write(const char* path, const SbGenParams* p, char* err, int errlen) {
+    auto fail = [&](const std::string& m) {
+        if (err && errlen > 0) snprintf(err, (size_t)errlen, "%s", m.c_str());
+        return -1;
+    };
+    if (!path || !p) return fail("null argument");
+    Built b;
+    std::string e = build(*p, b);
+    if (!e.empty()) return fail(e);
+    e = b.w.write(path);
+    if (!e.empty()) return fail(e);
+    return 0;
+}
+
+extern "C" int sbgen_factor_stats(const SbGenParams* p, int64_t* n, int64_t* nnz_l, int64_t* nnz_u) {
+    if (!p) return -1;
+    Built b;
+    if (!build(*p, b).empty()) return -1;
+    if (n) *n = b.n;
+    if (nnz_l) *nnz_l = b.nnzL;
+    if (nnz_u) *nnz_u = b.nnzU;
+    return 0;
+}

@@ -1,0 +1,86 @@
+/* TEST INFRASTRUCTURE: the oracle ABI (sbo.h) over the C restatement.
+ * Reset/step order restates the reference CPU env,
+ * complete_port/pufferlib_cpu_env.h:187-257. */
+#include <stdlib.h>
+#include <string.h>
+
+#include "sbo.h"
+#include "sbo_internal.h"
+
+struct SboEnv {
+    SboScn scn;
+    SboState st;
+};
+
+SboEnv* sbo_create(const char* path, int max_steps) {
+    SboEnv* e = (SboEnv*)calloc(1, sizeof(SboEnv));
+    if (!e) return NULL;
+    if (sbo_scn_load(&e->scn, path, max_steps) != 0 || e->scn.n_cont > SBO_CONT ||
+        e->scn.n_disc > SBO_DISC || e->scn.n_dev + e->scn.n_aux > SBO_OBS) {
+        sbo_scn_free(&e->scn);
+        free(e);
+        return NULL;
+    }
+    sbo_state_alloc(&e->st, &e->scn);
+    return e;
+}
+
+void sbo_destroy(SboEnv* e) {
+    if (!e) return;
+    sbo_state_free(&e->st);
+    sbo_scn_free(&e->scn);
+    free(e);
+}
+
+void sbo_dims(const SboEnv* e, int* out) {
+    const SboScn* s = &e->scn;
+    out[0] = s->ncv; out[1] = s->n; out[2] = s->k; out[3] = s->nz; out[4] = s->nv; out[5] = s->na;
+    out[6] = s->nact; out[7] = s->n_cont; out[8] = s->n_disc; out[9] = s->n_dev + s->n_aux;
+}
+
+static void write_obs(SboEnv* e, int j, float* obs) {
+    sbo_observe(&e->st, &e->scn, j, obs);
+    for (int i = e->scn.n_dev + e->scn.n_aux; i < SBO_OBS; i++) obs[i] = 0.0f;
+}
+
+void sbo_reset(SboEnv* e, float* obs) {
+    sbo_sim_reset(&e->st, &e->scn);
+    sbo_occ_advance(&e->st, &e->scn, e->scn.hour_m1, e->scn.wd_m1);   /* prime [ts_-1, ts_0) */
+    e->st.step = 0;
+    memset(e->st.native, 0, sizeof(e->st.native));
+    write_obs(e, 0, obs);
+    sbo_occ_advance(&e->st, &e->scn, (int)e->scn.o_hour[0], (int)e->scn.o_wd[0]);
+}
+
+void sbo_step(SboEnv* e, const float* act, float* obs, float* reward, float* terminal,
+              double* reward_f64, double* parts12, double* log8) {
+    SboScn* s = &e->scn;
+    SboState* st = &e->st;
+    sbo_decode(s, act, st->native);
+    sbo_apply_native(st, s, st->native);
+    sbo_sim_step(st, s);
+    st->step += 1;
+    write_obs(e, st->step, obs);
+    sbo_occ_advance(st, s, (int)s->o_hour[st->step], (int)s->o_wd[st->step]);
+    const double rew = sbo_reward(st, s, st->step, parts12, log8);
+    if (reward) *reward = (float)rew;
+    if (reward_f64) *reward_f64 = rew;
+    const int done = st->step >= s->max_steps;
+    if (terminal) *terminal = done ? 1.0f : 0.0f;
+    if (done) sbo_reset(e, obs);
+}
+
+void sbo_get_temp(const SboEnv* e, double* out) {
+    memcpy(out, e->st.temp, sizeof(double) * (size_t)e->scn.ncv);
+}
+
+void sbo_get_mass(const SboEnv* e, double* out) {
+    memcpy(out, e->st.mass, sizeof(double) * (size_t)e->scn.n);
+}
+
+int sbo_step_index(const SboEnv* e) { return e->st.step; }
+
+void sbo_reseed(SboEnv* e) {
+    sbo_mt_seed(&e->st.orng, e->scn.occ_seed);
+    sbo_mt_seed(&e->st.crng, e->scn.conv_seed);
+}
