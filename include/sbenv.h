@@ -1,0 +1,156 @@
+/* Batched Smart Buildings HVAC environment on B200 -- C ABI.
+ *
+ * Drop-in for the reference's PufferLib 5.0 GPU env backend
+ * (complete_port/gpu/smart_buildings.cu:3307-3323, PUF_BACKEND PUF_GPU with
+ * PUF_HAS_LIVE_LOG and PUF_HAS_MASK_INIT, smart_buildings.cu:94-95,65): the same
+ * entry points, argument meanings, buffer layouts and episode semantics. The
+ * whole step runs on the device on the stream bound with puf_bind_stream; the
+ * host only enqueues kernels, so puf_step can be captured in a CUDA graph.
+ *
+ * Buffer layout (the trainer owns these device buffers; the env writes them in place):
+ *   observations  float [n][SB_OBS]   real fields first, zero tail
+ *   actions       float [n][SB_NUM_ATNS] = [SB_CONT continuous in [-1,1]][SB_DISC run bits]
+ *   rewards       float [n]
+ *   terminals     float [n]            1.0 on the step that ends an episode
+ * (complete_port/gpu/smart_buildings.cu:33-71, complete_port/pufferlib_cpu_env.h:50-80)
+ *
+ * Errors: the reference abort()s on a bad configuration
+ * (complete_port/pufferlib_cpu_env.h:316-358). Here puf_vec_create returns
+ * NULL and every call records a one-line reason readable with sb_last_error();
+ * device-side faults the kernels detect (a bounded wait that expired, a corrupt
+ * schedule chunk) are latched in a device status word reported by
+ * sb_device_status(). Nothing traps and no wait is unbounded. */
+#ifndef SBENV_H
+#define SBENV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SB_OBS 1024
+#define SB_CONT 256
+#define SB_DISC 16
+#define SB_NUM_ATNS (SB_CONT + SB_DISC)
+#define SB_MASK_WIDTH (SB_CONT + 2 * SB_DISC)
+#define SB_NPARTS_ENV 8
+
+typedef float obs_t;
+typedef struct CUstream_st* sb_stream_t; /* == cudaStream_t */
+
+/* Per-env episode log (complete_port/gpu/smart_buildings.cu:101-115). Fields are
+ * sums over completed episodes; the trainer divides by n. */
+typedef struct Log {
+    float perf;
+    float score;
+    float episode_return;
+    float episode_length;
+    float comfort_dev_K;
+    float worst_dev_K;
+    float out_of_band_frac;
+    float productivity;
+    float energy_cost_norm;
+    float carbon_norm;
+    float elec_kwh;
+    float gas_kwh;
+    float n;
+} Log;
+
+/* One environment record; an array of n of them is returned by puf_vec_create
+ * in managed memory (smart_buildings.cu:116-143). The step writes log / ep_* /
+ * step on the device; the host reads them only after synchronising. */
+typedef struct Env {
+    Log log;
+    float ep_ret;
+    float ep_part[SB_NPARTS_ENV];
+    float ep_worst;
+    int num_agents;
+    int tag;
+    int boundary_reached;
+    int step;
+    int max_steps;
+    int n_act, n_cont, n_disc;
+    int loaded;
+    unsigned int rng;
+    int seed;
+    int env_id;
+    int scenario;
+} Env;
+
+/* PufferLib's keyword dictionary, minimal layout: a key with a numeric value
+ * and/or a string value. dict_find returns NULL for a missing key. */
+typedef struct DictItem {
+    const char* key;
+    double value;
+    const char* str;
+} DictItem;
+typedef struct Dict {
+    DictItem* items;
+    int size;
+    int capacity;
+} Dict;
+
+Dict* sb_dict_new(int capacity);
+void sb_dict_free(Dict* d);
+DictItem* dict_find(Dict* d, const char* key);
+void dict_set(Dict* d, const char* key, double value);
+void dict_set_str(Dict* d, const char* key, const char* value);
+
+/* ---- the PufferLib GPU-backend entry points ---- */
+
+/* n envs over the scenarios named by kwargs "blob" (one .sbb path) or
+ * "blob_dir" (every *.sbb in the directory; env SB_BLOB_DIR as fallback),
+ * spread round-robin by building (smart_buildings.cu:2497-2560). Other keys:
+ * groups (scenario count, 0 = n/32), max_steps (0 = the blob's episode
+ * length), merge_weathers (share one solver group across weathers of a
+ * building, default 1), reward_scale (default 1). Returns NULL on error. */
+Env* puf_vec_create(int n, Dict* kwargs, obs_t* observations, float* actions, float* rewards,
+                    float* terminals);
+void puf_bind_stream(sb_stream_t stream);
+void puf_init(Env* env, Dict* kwargs);
+/* Restarts every env: state from the blob, occupancy primed, reset observation written. */
+void puf_reset(Env* envs);
+/* One batched step of every env (device only, graph-capturable). */
+void puf_step(Env* envs);
+void puf_render(Env* env);
+void puf_close(Env* env);
+void puf_log(Log* log, Dict* out);
+/* Step-level metrics since the previous call, per scenario as scenario/<name>/... */
+void puf_live_log(Env* envs, Dict* out);
+/* Fills the trainer's [nagents][width] action mask (device pointer): active
+ * continuous heads and active discrete categories 1, padding 0. */
+void puf_mask_init(unsigned char* mask, int width, int nagents);
+
+/* ---- additions for hosts without PufferLib (no counterpart in the reference) ---- */
+
+/* Last error text of this thread ("" if none). */
+const char* sb_last_error(void);
+/* Device status word: 0, or the first kernel-detected error code: 1 a solve
+ * schedule chunk never arrived (bounded wait expired), 2 a corrupt schedule
+ * chunk, 3 a convection swap list overflow. */
+int sb_device_status(void);
+/* Shape of the loaded batch: out[8] = {n_env, n_scenarios, n_groups, obs_len_max,
+ * n_cont_max, n_disc_max, slab_ctas, kernels_per_step}. */
+void sb_shape(int* out);
+/* Per-env observation length / scenario index (host arrays of n). */
+void sb_env_info(int* obs_len, int* scenario);
+/* Copies one env's temperature field (cell order, n_cvs doubles) to host memory. */
+int sb_get_temp(int env, double* out, int n_cvs);
+/* Copies one env's interior-mass temperatures (solved-cell order) to host memory. */
+int sb_get_mass(int env, double* out, int n_solved);
+/* Copies the last step's per-env reward (double) and log terms [n][8] to host memory. */
+int sb_get_reward_f64(double* reward, double* parts);
+/* Number of hot-path kernel launches one puf_step enqueues. */
+int sb_kernels_per_step(void);
+/* Host-only: the device solve schedule of a blob's factor (sweep 0 = L, 1 = U)
+ * as the byte stream the solve kernel streams into shared memory. Returns 0, 1
+ * if cap is too small (*used then holds the size), -1 on error. */
+int sb_solve_schedule(const char* blob_path, int sweep, uint8_t* out, size_t cap, size_t* used,
+                      uint32_t* nchunks);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SBENV_H */

@@ -1,0 +1,760 @@
+// Host orchestration and the C ABI (include/sbenv.h) of the batched env.
+//
+// Reference interface: complete_port/gpu/smart_buildings.cu:2497-3323
+// (puf_vec_create, puf_bind_stream, puf_init, puf_reset, puf_step, puf_close,
+// puf_log, puf_live_log, puf_mask_init). One step enqueues, on the bound
+// stream and one forked side stream:
+//   k_rng   (side)  per-scenario convection permutation + occupancy chains
+//   k_pre   (main)  decode, actuators, zone sensing, VAV/AHU/boiler pre-step
+//   k_solve (main)  fused thermal solve over slabs of envs in shared memory
+//   k_post  (main, after joining the side stream) convection apply, boiler,
+//           observation, reward, episode log, in-step restart
+// No host synchronisation, allocation or attribute change happens inside
+// puf_step, so a caller can capture it in a CUDA graph.
+#include <cuda_runtime.h>
+#include <dirent.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/sbenv.h"
+#include "k_post.cuh"
+#include "k_pre.cuh"
+#include "k_rng.cuh"
+#include "k_solve.cuh"
+#include "tables.h"
+
+using namespace sbenv;
+
+namespace {
+
+thread_local std::string g_err;
+void set_err(const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_err = buf;
+}
+
+#define CK(call)                                                                      \
+    do {                                                                              \
+        cudaError_t e_ = (call);                                                      \
+        if (e_ != cudaSuccess) {                                                      \
+            set_err("%s failed: %s", #call, cudaGetErrorString(e_));                  \
+            return false;                                                             \
+        }                                                                             \
+    } while (0)
+
+// Device allocations owned by the engine.
+struct DevArena {
+    std::vector<void*> ptrs;
+    ~DevArena() { release(); }
+    void release() {
+        for (void* p : ptrs) cudaFree(p);
+        ptrs.clear();
+    }
+    template <class T> T* upload(const std::vector<T>& v, bool& ok) {
+        if (!ok) return nullptr;
+        const size_t nb = std::max<size_t>(v.size() * sizeof(T), 16);
+        void* p = nullptr;
+        if (cudaMalloc(&p, nb) != cudaSuccess) { ok = false; set_err("cudaMalloc(%zu) failed", nb); return nullptr; }
+        ptrs.push_back(p);
+        if (!v.empty() && cudaMemcpy(p, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice) != cudaSuccess) {
+            ok = false;
+            set_err("upload failed");
+        }
+        return static_cast<T*>(p);
+    }
+    template <class T> T* zeros(size_t count, bool& ok) {
+        if (!ok) return nullptr;
+        const size_t nb = std::max<size_t>(count * sizeof(T), 16);
+        void* p = nullptr;
+        if (cudaMalloc(&p, nb) != cudaSuccess) { ok = false; set_err("cudaMalloc(%zu) failed", nb); return nullptr; }
+        ptrs.push_back(p);
+        if (cudaMemset(p, 0, nb) != cudaSuccess) { ok = false; set_err("cudaMemset failed"); }
+        return static_cast<T*>(p);
+    }
+};
+
+struct Engine {
+    int n_env = 0;
+    std::vector<std::unique_ptr<sbb::Reader>> blobs;
+    std::vector<HostGroup> hg;
+    std::vector<HostScn> hs;
+    std::vector<GroupDev> gd;
+    std::vector<ScnDev> sd;
+    std::vector<EnvIndex> ei;
+    std::vector<SlabDesc> slabs;
+    StepCtx ctx{};
+    DevArena arena;
+    StepCtx* d_ctx = nullptr;
+    SlabDesc* d_slabs = nullptr;
+    int* d_scn_step = nullptr;
+    RngOut* d_rng_out = nullptr;
+    Env* envs = nullptr;          // managed
+    cudaStream_t stream = nullptr, own_stream = nullptr, side = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    size_t smem_solve = 0, smem_pre = 0, smem_post = 0, smem_rng = 0;
+    int max_ncv = 0;
+    bool ready = false;
+    ~Engine() { destroy(); }
+    void destroy() {
+        if (side) cudaStreamDestroy(side);
+        if (own_stream) cudaStreamDestroy(own_stream);
+        if (ev_fork) cudaEventDestroy(ev_fork);
+        if (ev_join) cudaEventDestroy(ev_join);
+        side = own_stream = nullptr;
+        ev_fork = ev_join = nullptr;
+        if (envs) cudaFree(envs);
+        envs = nullptr;
+        arena.release();
+        ready = false;
+    }
+};
+
+Engine* g_eng = nullptr;
+
+bool ends_with(const std::string& s, const char* suf) {
+    const size_t m = strlen(suf);
+    return s.size() >= m && s.compare(s.size() - m, m, suf) == 0;
+}
+
+std::vector<std::string> list_blobs(const std::string& dir) {
+    std::vector<std::string> out;
+    DIR* d = opendir(dir.c_str());
+    if (!d) return out;
+    while (dirent* e = readdir(d))
+        if (ends_with(e->d_name, ".sbb")) out.push_back(dir + "/" + e->d_name);
+    closedir(d);
+    std::sort(out.begin(), out.end());
+    // building-first round robin (smart_buildings.cu:2434-2455): <building>__<weather>.sbb
+    std::vector<std::string> keys, blds, ordered;
+    for (auto& p : out) {
+        std::string base = p.substr(p.find_last_of('/') + 1);
+        std::string bld = base.substr(0, base.find("__"));
+        keys.push_back(bld);
+        if (std::find(blds.begin(), blds.end(), bld) == blds.end()) blds.push_back(bld);
+    }
+    std::vector<int> used(out.size(), 0);
+    while (ordered.size() < out.size())
+        for (auto& b : blds)
+            for (size_t i = 0; i < out.size(); i++)
+                if (!used[i] && keys[i] == b) { ordered.push_back(out[i]); used[i] = 1; break; }
+    return ordered;
+}
+
+const char* kw_str(Dict* kw, const char* key) {
+    DictItem* it = kw ? dict_find(kw, key) : nullptr;
+    return (it && it->str && it->str[0]) ? it->str : nullptr;
+}
+double kw_num(Dict* kw, const char* key, double dflt) {
+    DictItem* it = kw ? dict_find(kw, key) : nullptr;
+    return it ? it->value : dflt;
+}
+
+StateLayout make_layout(int na, int nv, int nz, int k) {
+    StateLayout L{};
+    int d = 0, i = 0;
+    auto D = [&](int cnt) { int o = d; d += cnt; return o; };
+    auto I = [&](int cnt) { int o = i; i += cnt; return o; };
+    L.ahu_rec = D(na); L.ahu_sat = D(na); L.ahu_fan = D(na); L.ahu_flow = D(na);
+    L.v_damp = D(nv); L.v_reh = D(nv); L.v_ratio = D(nv); L.v_hsp = D(nv); L.v_csp = D(nv);
+    L.v_dcmd = D(nv); L.v_rcmd = D(nv); L.v_sense = D(nv); L.v_area = D(nv);
+    L.qdiv = D(nz); L.ag = D(k); L.aT = D(k); L.coil = D(k); L.V = D(nz);
+    L.ff_sum = D(1); L.pump_head = D(1); L.b_sp = D(1); L.b_ret = D(1); L.b_cur = D(1); L.b_step = D(1);
+    L.reheat_w = D(1);
+    L.ahu_run = I(na); L.ahu_creq = I(na); L.v_mode = I(nv); L.v_prev = I(nv); L.v_dset = I(nv); L.v_rset = I(nv);
+    L.hws_req = I(1); L.hws_run = I(1); L.pump_run = I(1); L.step = I(1); L.gen = I(1); L.active = I(1);
+    L.nd = (d + 1) & ~1;
+    L.ni = (i + 3) & ~3;
+    return L;
+}
+
+bool launch_step(Engine& E) {
+    CK(cudaEventRecord(E.ev_fork, E.stream));
+    CK(cudaStreamWaitEvent(E.side, E.ev_fork, 0));
+    k_rng<<<(unsigned)E.sd.size(), 32, E.smem_rng, E.side>>>(E.d_ctx, E.d_scn_step, E.d_rng_out, 0);
+    CK(cudaGetLastError());
+    CK(cudaEventRecord(E.ev_join, E.side));
+    k_pre<<<(unsigned)E.n_env, 128, E.smem_pre, E.stream>>>(E.d_ctx);
+    CK(cudaGetLastError());
+    k_solve<<<(unsigned)E.slabs.size(), kSolveThreads, E.smem_solve, E.stream>>>(E.d_ctx, E.d_slabs);
+    CK(cudaGetLastError());
+    CK(cudaStreamWaitEvent(E.stream, E.ev_join, 0));
+    k_post<<<(unsigned)E.n_env, 128, E.smem_post, E.stream>>>(E.d_ctx);
+    CK(cudaGetLastError());
+    return true;
+}
+
+bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew, float* term) {
+    // ---- scenarios ----
+    std::vector<std::string> paths;
+    if (const char* one = kw_str(kw, "blob")) {
+        paths.push_back(one);
+    } else {
+        const char* dir = kw_str(kw, "blob_dir");
+        if (!dir) dir = getenv("SB_BLOB_DIR");
+        if (dir && dir[0]) paths = list_blobs(dir);
+        if (paths.empty()) {
+            set_err("no scenario: set kwargs blob or blob_dir (or SB_BLOB_DIR)");
+            return false;
+        }
+    }
+    if (n < 1) { set_err("n must be >= 1"); return false; }
+    int G = (int)kw_num(kw, "groups", 0.0);
+    if (G <= 0) G = n / 32;
+    G = std::max(1, std::min(G, std::min((int)paths.size(), n)));
+    std::vector<int> scnt(G);
+    for (int i = 0; i < G; i++) scnt[i] = n / G + (i < n % G ? 1 : 0);
+    const bool merge = kw_num(kw, "merge_weathers", 1.0) != 0.0;
+    const int max_steps_kw = (int)kw_num(kw, "max_steps", 0.0);
+    for (int i = 0; i < G; i++) {
+        auto r = std::make_unique<sbb::Reader>();
+        std::string e = r->open(paths[i]);
+        if (!e.empty()) { set_err("%s", e.c_str()); return false; }
+        E.blobs.push_back(std::move(r));
+    }
+    // ---- groups: scenarios with identical geometry share solver tables ----
+    std::vector<int> scn_group(G, -1);
+    std::vector<int> group_rep;
+    for (int i = 0; i < G; i++) {
+        if (merge)
+            for (size_t c = 0; c < group_rep.size(); c++)
+                if (same_geometry(*E.blobs[group_rep[c]], *E.blobs[i])) { scn_group[i] = (int)c; break; }
+        if (scn_group[i] < 0) { scn_group[i] = (int)group_rep.size(); group_rep.push_back(i); }
+    }
+    const int NG = (int)group_rep.size();
+    E.hg.resize(NG);
+    for (int c = 0; c < NG; c++) {
+        std::string e = build_group(*E.blobs[group_rep[c]], E.hg[c]);
+        if (!e.empty()) { set_err("%s: %s", paths[group_rep[c]].c_str(), e.c_str()); return false; }
+    }
+    E.hs.resize(G);
+    for (int i = 0; i < G; i++) {
+        std::string e = build_scenario(*E.blobs[i], E.hg[scn_group[i]], max_steps_kw, E.hs[i]);
+        if (!e.empty()) { set_err("%s: %s", paths[i].c_str(), e.c_str()); return false; }
+        E.hs[i].group = scn_group[i];
+    }
+    // ---- env layout: groups in order, scenarios of a group contiguous ----
+    int na_max = 0, nv_max = 0, nz_max = 0, k_max = 0;
+    for (auto& s : E.hs) {
+        na_max = std::max(na_max, s.na); nv_max = std::max(nv_max, s.nv);
+        nz_max = std::max(nz_max, s.nz); k_max = std::max(k_max, s.k);
+    }
+    const StateLayout L = make_layout(na_max, nv_max, nz_max, k_max);
+    E.n_env = n;
+    bool ok = true;
+    E.sd.resize(G);
+    E.gd.resize(NG);
+    std::vector<int> scn_env0(G);
+    int env_cursor = 0;
+    for (int c = 0; c < NG; c++) {
+        GroupDev& gd = E.gd[c];
+        memset(&gd, 0, sizeof(gd));
+        gd.env0 = env_cursor;
+        for (int i = 0; i < G; i++)
+            if (scn_group[i] == c) { scn_env0[i] = env_cursor; env_cursor += scnt[i]; }
+        gd.n_env = env_cursor - gd.env0;
+    }
+    // ---- upload group tables ----
+    size_t smem_cap = 0;
+    {
+        int dev = 0, optin = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        smem_cap = (size_t)optin;
+    }
+    const size_t solve_fixed = (size_t)kRingSlots * kRingSlotBytes + 256;
+    for (int c = 0; c < NG; c++) {
+        HostGroup& h = E.hg[c];
+        GroupDev& gd = E.gd[c];
+        gd.n = h.n; gd.ncv = h.ncv; gd.k = h.k; gd.nz = h.nz;
+        gd.sigma_identity = 1;
+        gd.stride = ((h.n + 15) & ~15) + 2;
+        int B = 8;
+        while (B > 1 && (size_t)B * gd.stride * 8 + solve_fixed + 1024 > smem_cap) B /= 2;
+        if ((size_t)B * gd.stride * 8 + solve_fixed + 1024 > smem_cap) {
+            set_err("group %d: one env's field (%d cells) exceeds shared memory", c, h.n);
+            return false;
+        }
+        gd.slab_envs = B;
+        E.smem_solve = std::max(E.smem_solve, (size_t)B * gd.stride * 8 + solve_fixed);
+        gd.cap = E.arena.upload(h.cap, ok); gd.dirx = E.arena.upload(h.dirx, ok);
+        gd.mc = E.arena.upload(h.mc, ok); gd.ret = E.arena.upload(h.ret, ok); gd.gain = E.arena.upload(h.gain, ok);
+        gd.zone_of_row = E.arena.upload(h.zone_of_row, ok);
+        auto put_sweep = [&](const HostSweep& hsw, Sweep& s) {
+            s.stream = E.arena.upload(hsw.bytes, ok);
+            s.nchunks = (uint32_t)hsw.chunk_bytes.size();
+            for (int q = 0; q < kRingSlots; q++)
+                s.first_bytes[q] = q < (int)hsw.chunk_bytes.size() ? hsw.chunk_bytes[q] : 0;
+        };
+        put_sweep(h.fwd, gd.fwd);
+        put_sweep(h.bwd, gd.bwd);
+        gd.sn_p = E.arena.upload(h.sn_p, ok); gd.sn_pos = E.arena.upload(h.sn_pos, ok);
+        gd.sn_x = E.arena.upload(h.sn_x, ok);
+        gd.ap_rp = E.arena.upload(h.ap_rp, ok); gd.ap_col = E.arena.upload(h.ap_col, ok);
+        gd.ap_x = E.arena.upload(h.ap_x, ok); gd.S = E.arena.upload(h.S, ok);
+        gd.room_off = E.arena.upload(h.room_off, ok); gd.room_pos = E.arena.upload(h.room_pos, ok);
+        gd.cell_of_pos = E.arena.upload(h.cell_of_pos, ok); gd.pos_of_cell = E.arena.upload(h.pos_of_cell, ok);
+        gd.cv_off = E.arena.upload(h.cv_off, ok); gd.cv_pos = E.arena.upload(h.cv_pos, ok);
+        gd.cand_off = E.arena.upload(h.cand_off, ok); gd.cand_idx = E.arena.upload(h.cand_idx, ok);
+        gd.conv_nrooms = (int)h.cv_off.size() - 1;
+        gd.conv_maxroom = h.conv_maxroom;
+        gd.T = E.arena.zeros<double>((size_t)gd.n_env * h.ncv, ok);
+        gd.M = E.arena.zeros<double>((size_t)gd.n_env * h.n, ok);
+        for (int e0 = 0; e0 < gd.n_env; e0 += B) E.slabs.push_back({c, gd.env0 + e0, std::min(B, gd.n_env - e0), 0});
+        E.max_ncv = std::max(E.max_ncv, h.ncv);
+        E.smem_pre = std::max(E.smem_pre, sizeof(double) * (size_t)(h.ncv + 2 * nz_max + nv_max + 2 * na_max + 2 * k_max));
+        E.smem_post = std::max(E.smem_post, sizeof(double) * (size_t)(2 * h.ncv + 3 * nz_max + 2 * nv_max));
+        const size_t rng_b = 4 * (size_t)(624 + 1248) + 4 * (size_t)(h.cv_off.back() + 2 * h.conv_maxroom);
+        E.smem_rng = std::max(E.smem_rng, rng_b);
+    }
+    // ---- scenario tables + random streams ----
+    for (int i = 0; i < G; i++) {
+        HostScn& h = E.hs[i];
+        ScnDev& s = E.sd[i];
+        memset(&s, 0, sizeof(s));
+        s.group = scn_group[i]; s.env0 = scn_env0[i]; s.n_env = scnt[i]; s.scn_index = i;
+        s.na = h.na; s.nv = h.nv; s.nz = h.nz; s.k = h.k; s.nact = h.nact; s.n_cont = h.n_cont;
+        s.n_disc = h.n_disc; s.n_dev = h.n_dev; s.n_aux = h.n_aux; s.max_steps = h.max_steps;
+        s.assign = h.assign; s.ea = h.ea; s.la = h.la; s.ed = h.ed; s.ld = h.ld;
+        s.hour_m1 = h.hour_m1; s.wd_m1 = h.wd_m1; s.tmean_needed = h.tmean_needed;
+        s.p_arr = h.p_arr; s.p_dep = h.p_dep; s.dt = h.dt; s.internal_w = h.internal_w; s.standby = h.standby;
+        s.occ_w = h.occ_w; s.cv_area = h.cv_area; s.header_res = h.header_res; s.pump_eff = h.pump_eff;
+        s.pump_head0 = h.pump_head0; s.gas_carbon = h.gas_carbon; s.conv_p = h.conv_p; s.conv_dist = h.conv_dist;
+        for (int q = 0; q < 10; q++) s.boiler[q] = h.boiler[q];
+        s.boiler_cond = h.boiler_cond;
+        s.amb = E.arena.upload(h.amb, ok); s.s_comf = E.arena.upload(h.s_comf, ok);
+        s.s_heat = E.arena.upload(h.s_heat, ok); s.s_cool = E.arena.upload(h.s_cool, ok);
+        s.aux = E.arena.upload(h.aux, ok);
+        s.o_hour = E.arena.upload(h.o_hour, ok); s.r_hour = E.arena.upload(h.r_hour, ok);
+        s.r_month = E.arena.upload(h.r_month, ok); s.o_wd = E.arena.upload(h.o_wd, ok);
+        s.r_wd = E.arena.upload(h.r_wd, ok);
+        s.ahu_c = E.arena.upload(h.ahu_c, ok); s.vav_c = E.arena.upload(h.vav_c, ok);
+        s.zarea = E.arena.upload(h.zarea, ok);
+        s.vz_off = E.arena.upload(h.vz_off, ok); s.vz_idx = E.arena.upload(h.vz_idx, ok);
+        s.v_ahu = E.arena.upload(h.v_ahu, ok); s.coupled = E.arena.upload(h.coupled, ok);
+        s.zv_off = E.arena.upload(h.zv_off, ok); s.zv_idx = E.arena.upload(h.zv_idx, ok);
+        s.proom = E.arena.upload(h.proom, ok); s.room_ncell = E.arena.upload(h.room_ncell, ok);
+        s.a_kind = E.arena.upload(h.a_kind, ok); s.a_act = E.arena.upload(h.a_act, ok);
+        s.a_disc = E.arena.upload(h.a_disc, ok); s.a_idx = E.arena.upload(h.a_idx, ok);
+        s.a_slot = E.arena.upload(h.a_slot, ok);
+        s.a_mn = E.arena.upload(h.a_mn, ok); s.a_mx = E.arena.upload(h.a_mx, ok);
+        s.a_mnr = E.arena.upload(h.a_mnr, ok); s.a_mxr = E.arena.upload(h.a_mxr, ok);
+        s.f_kind = E.arena.upload(h.f_kind, ok); s.f_id = E.arena.upload(h.f_id, ok);
+        s.f_idx = E.arena.upload(h.f_idx, ok); s.f_mean = E.arena.upload(h.f_mean, ok);
+        s.f_var = E.arena.upload(h.f_var, ok);
+        s.rw = E.arena.upload(h.rw, ok); s.e_wd = E.arena.upload(h.e_wd, ok); s.e_we = E.arena.upload(h.e_we, ok);
+        s.e_c = E.arena.upload(h.e_c, ok); s.g_p = E.arena.upload(h.g_p, ok);
+        s.temp_init = E.arena.upload(h.temp_init, ok); s.mass_init = E.arena.upload(h.mass_init, ok);
+        // streams seeded like the reference's init_genrand, position 624 (regenerate first)
+        auto seeded = [](uint32_t seed) {
+            std::vector<uint32_t> m(625);
+            m[0] = seed;
+            for (int q = 1; q < 624; q++) m[q] = 1812433253u * (m[q - 1] ^ (m[q - 1] >> 30)) + (uint32_t)q;
+            m[624] = 624;
+            return m;
+        };
+        s.conv_mt = E.arena.upload(seeded(h.conv_seed), ok);
+        s.occ_mt = E.arena.upload(seeded(h.occ_seed), ok);
+        s.occ_state0 = E.arena.zeros<int>((size_t)h.nz * std::max(h.assign, 1), ok);
+        const HostGroup& hgp = E.hg[scn_group[i]];
+        s.conv_pairs = E.arena.zeros<int32_t>(2 * (size_t)hgp.ncv + 2, ok);
+        s.conv_npairs = E.arena.zeros<int>(1, ok);
+        s.conv_scratch = nullptr;
+    }
+    for (int i = 0; i < G; i++) E.smem_rng = std::max(E.smem_rng, 4 * (size_t)(624 + 1248) + 4 * (size_t)E.hs[i].nz * E.hs[i].assign);
+    // ---- env index ----
+    E.ei.resize(n);
+    for (int i = 0; i < G; i++)
+        for (int q = 0; q < scnt[i]; q++) {
+            const int env = scn_env0[i] + q;
+            E.ei[env] = {scn_group[i], i, env - E.gd[scn_group[i]].env0, q == 0 ? 1 : 0};
+        }
+    // ---- context ----
+    StepCtx& C = E.ctx;
+    C.n_env = n;
+    C.n_groups = NG;
+    C.n_scns = G;
+    C.lay = L;
+    C.groups = E.arena.upload(E.gd, ok);
+    C.scns = E.arena.upload(E.sd, ok);
+    C.envs = E.arena.upload(E.ei, ok);
+    C.Dst = E.arena.zeros<double>((size_t)n * L.nd, ok);
+    C.Ist = E.arena.zeros<int32_t>((size_t)n * L.ni, ok);
+    C.actions = act;
+    C.obs = obs;
+    C.rewards = rew;
+    C.terminals = term;
+    C.reward_scale = (float)kw_num(kw, "reward_scale", 1.0);
+    if (!(C.reward_scale > 0.0f)) C.reward_scale = 1.0f;
+    C.rew_f64 = E.arena.zeros<double>(n, ok);
+    C.parts_out = E.arena.zeros<double>((size_t)n * kParts, ok);
+    C.epret_d = E.arena.zeros<double>(n, ok);
+    C.live = E.arena.zeros<double>(2 + kParts, ok);
+    C.live_scn = E.arena.zeros<double>((size_t)G * 4, ok);
+    C.ep_scn = E.arena.zeros<double>((size_t)G * 2, ok);
+    C.status = E.arena.zeros<int>(1, ok);
+    C.nz_max = nz_max;
+    double* vbuf = E.arena.zeros<double>((size_t)3 * G * nz_max, ok);
+    C.V_step = vbuf;
+    C.V_prime = vbuf + (size_t)G * nz_max;
+    C.V_zero = vbuf + (size_t)2 * G * nz_max;
+    std::vector<RngOut> ro(G);
+    for (int i = 0; i < G; i++)
+        ro[i] = {vbuf + (size_t)i * nz_max, vbuf + (size_t)(G + i) * nz_max, vbuf + (size_t)(2 * G + i) * nz_max};
+    E.d_rng_out = E.arena.upload(ro, ok);
+    E.d_scn_step = E.arena.zeros<int>(G, ok);
+    E.d_slabs = E.arena.upload(E.slabs, ok);
+    if (!ok) return false;
+    // per-env state that persists across resets (pump head set once at init, sb_sim.c:71-75)
+    {
+        std::vector<double> Dh((size_t)n * L.nd, 0.0);
+        for (int env = 0; env < n; env++) Dh[(size_t)env * L.nd + L.pump_head] = E.hs[E.ei[env].scn].pump_head0;
+        CK(cudaMemcpy(C.Dst, Dh.data(), Dh.size() * sizeof(double), cudaMemcpyHostToDevice));
+    }
+    // managed Env records
+    CK(cudaMallocManaged((void**)&E.envs, sizeof(Env) * (size_t)n));
+    memset(E.envs, 0, sizeof(Env) * (size_t)n);
+    for (int env = 0; env < n; env++) {
+        const HostScn& s = E.hs[E.ei[env].scn];
+        Env& r = E.envs[env];
+        r.num_agents = 1;
+        r.max_steps = s.max_steps;
+        r.n_act = s.nact; r.n_cont = s.n_cont; r.n_disc = s.n_disc;
+        r.loaded = 1;
+        r.env_id = env;
+        r.scenario = E.ei[env].scn;
+    }
+    C.env_records = E.envs;
+    E.d_ctx = E.arena.upload(std::vector<StepCtx>{C}, ok);
+    if (!ok) return false;
+    // ---- launch configuration (once; never inside a step) ----
+    if (E.smem_solve > smem_cap) { set_err("solve kernel needs %zu B of shared memory", E.smem_solve); return false; }
+    CK(cudaFuncSetAttribute(k_solve, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_solve));
+    CK(cudaFuncSetAttribute(k_pre, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_pre));
+    CK(cudaFuncSetAttribute(k_post, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_post));
+    CK(cudaFuncSetAttribute(k_reset, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_post));
+    CK(cudaFuncSetAttribute(k_rng, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_rng));
+    CK(cudaStreamCreateWithFlags(&E.own_stream, cudaStreamNonBlocking));
+    CK(cudaStreamCreateWithFlags(&E.side, cudaStreamNonBlocking));
+    CK(cudaEventCreateWithFlags(&E.ev_fork, cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&E.ev_join, cudaEventDisableTiming));
+    if (!E.stream) E.stream = E.own_stream;
+    CK(cudaDeviceSynchronize());
+    E.ready = true;
+    return true;
+}
+
+bool do_reset(Engine& E) {
+    CK(cudaEventRecord(E.ev_fork, E.stream));
+    CK(cudaStreamWaitEvent(E.side, E.ev_fork, 0));
+    k_rng<<<(unsigned)E.sd.size(), 32, E.smem_rng, E.side>>>(E.d_ctx, E.d_scn_step, E.d_rng_out, 1);
+    CK(cudaGetLastError());
+    CK(cudaEventRecord(E.ev_join, E.side));
+    CK(cudaStreamWaitEvent(E.stream, E.ev_join, 0));
+    k_reset<<<(unsigned)E.n_env, 128, E.smem_post, E.stream>>>(E.d_ctx);
+    CK(cudaGetLastError());
+    CK(cudaStreamSynchronize(E.stream));
+    return true;
+}
+
+}  // namespace
+
+// ============================== C ABI ==============================
+
+extern "C" {
+
+Dict* sb_dict_new(int capacity) {
+    Dict* d = (Dict*)calloc(1, sizeof(Dict));
+    if (!d) return nullptr;
+    d->capacity = capacity > 0 ? capacity : 16;
+    d->items = (DictItem*)calloc((size_t)d->capacity, sizeof(DictItem));
+    return d;
+}
+
+void sb_dict_free(Dict* d) {
+    if (!d) return;
+    for (int i = 0; i < d->size; i++) {
+        free((void*)d->items[i].key);
+        free((void*)d->items[i].str);
+    }
+    free(d->items);
+    free(d);
+}
+
+DictItem* dict_find(Dict* d, const char* key) {
+    if (!d || !key) return nullptr;
+    for (int i = 0; i < d->size; i++)
+        if (d->items[i].key && strcmp(d->items[i].key, key) == 0) return &d->items[i];
+    return nullptr;
+}
+
+static DictItem* dict_slot(Dict* d, const char* key) {
+    DictItem* it = dict_find(d, key);
+    if (it) return it;
+    if (d->size == d->capacity) {
+        const int cap = d->capacity * 2;
+        DictItem* ni = (DictItem*)realloc(d->items, sizeof(DictItem) * (size_t)cap);
+        if (!ni) return nullptr;
+        memset(ni + d->capacity, 0, sizeof(DictItem) * (size_t)(cap - d->capacity));
+        d->items = ni;
+        d->capacity = cap;
+    }
+    it = &d->items[d->size++];
+    it->key = strdup(key);
+    return it;
+}
+
+void dict_set(Dict* d, const char* key, double value) {
+    if (!d || !key) return;
+    DictItem* it = dict_slot(d, key);
+    if (it) it->value = value;
+}
+
+void dict_set_str(Dict* d, const char* key, const char* value) {
+    if (!d || !key) return;
+    DictItem* it = dict_slot(d, key);
+    if (!it) return;
+    free((void*)it->str);
+    it->str = value ? strdup(value) : nullptr;
+}
+
+const char* sb_last_error(void) { return g_err.c_str(); }
+
+Env* puf_vec_create(int n, Dict* kwargs, obs_t* observations, float* actions, float* rewards, float* terminals) {
+    g_err.clear();
+    if (!observations || !actions || !rewards || !terminals) {
+        set_err("puf_vec_create: null buffer");
+        return nullptr;
+    }
+    delete g_eng;
+    g_eng = new Engine();
+    if (!build_engine(*g_eng, n, kwargs, observations, actions, rewards, terminals)) {
+        const std::string keep = g_err;
+        delete g_eng;
+        g_eng = nullptr;
+        g_err = keep;
+        return nullptr;
+    }
+    return g_eng->envs;
+}
+
+void puf_bind_stream(sb_stream_t s) {
+    if (g_eng && s) g_eng->stream = reinterpret_cast<cudaStream_t>(s);
+}
+
+void puf_init(Env* env, Dict* kwargs) {
+    (void)kwargs;
+    if (env) memset(&env->log, 0, sizeof(env->log));
+}
+
+void puf_reset(Env* envs) {
+    (void)envs;
+    if (!g_eng || !g_eng->ready) { set_err("puf_reset: no env batch"); return; }
+    Engine& E = *g_eng;
+    if (cudaStreamSynchronize(E.stream) != cudaSuccess) { set_err("puf_reset: stream error"); return; }
+    if (cudaMemsetAsync(E.d_scn_step, 0, sizeof(int) * E.sd.size(), E.stream) != cudaSuccess) {
+        set_err("puf_reset: memset failed");
+        return;
+    }
+    for (int env = 0; env < E.n_env; env++) {
+        E.envs[env].step = 0;
+        E.envs[env].ep_ret = 0.0f;
+        E.envs[env].ep_worst = 0.0f;
+        for (int q = 0; q < SB_NPARTS_ENV; q++) E.envs[env].ep_part[q] = 0.0f;
+    }
+    if (!do_reset(E)) return;
+}
+
+void puf_step(Env* envs) {
+    (void)envs;
+    if (!g_eng || !g_eng->ready) { set_err("puf_step: no env batch"); return; }
+    launch_step(*g_eng);
+}
+
+void puf_render(Env* env) { (void)env; }
+
+void puf_close(Env* env) {
+    (void)env;
+    if (g_eng) {
+        cudaDeviceSynchronize();
+        delete g_eng;
+        g_eng = nullptr;
+    }
+}
+
+void puf_log(Log* log, Dict* out) {
+    if (!log || !out) return;
+    dict_set(out, "perf", log->perf);
+    dict_set(out, "score", log->score);
+    dict_set(out, "episode_return", log->episode_return);
+    dict_set(out, "episode_length", log->episode_length);
+    dict_set(out, "comfort_dev_K", log->comfort_dev_K);
+    dict_set(out, "worst_dev_K", log->worst_dev_K);
+    dict_set(out, "out_of_band_frac", log->out_of_band_frac);
+    dict_set(out, "productivity", log->productivity);
+    dict_set(out, "energy_cost_norm", log->energy_cost_norm);
+    dict_set(out, "carbon_norm", log->carbon_norm);
+    dict_set(out, "elec_kwh", log->elec_kwh);
+    dict_set(out, "gas_kwh", log->gas_kwh);
+    dict_set(out, "n", log->n);
+}
+
+void puf_live_log(Env* envs, Dict* out) {
+    (void)envs;
+    if (!g_eng || !out) return;
+    Engine& E = *g_eng;
+    if (cudaStreamSynchronize(E.stream) != cudaSuccess) return;
+    double h[2 + kParts];
+    std::vector<double> hs(E.sd.size() * 4), he(E.sd.size() * 2);
+    cudaMemcpy(h, E.ctx.live, sizeof(h), cudaMemcpyDeviceToHost);
+    cudaMemcpy(hs.data(), E.ctx.live_scn, hs.size() * sizeof(double), cudaMemcpyDeviceToHost);
+    cudaMemcpy(he.data(), E.ctx.ep_scn, he.size() * sizeof(double), cudaMemcpyDeviceToHost);
+    cudaMemset(E.ctx.live, 0, sizeof(h));
+    cudaMemset(E.ctx.live_scn, 0, hs.size() * sizeof(double));
+    cudaMemset(E.ctx.ep_scn, 0, he.size() * sizeof(double));
+    for (size_t i = 0; i < E.sd.size(); i++) {
+        if (hs[i * 4 + 2] > 0.0) {
+            dict_set(out, ("scenario/" + E.hs[i].name + "/reward").c_str(), hs[i * 4] / hs[i * 4 + 2]);
+            dict_set(out, ("scenario/" + E.hs[i].name + "/comfort_dev_K").c_str(), hs[i * 4 + 1] / hs[i * 4 + 2]);
+        }
+        if (he[i * 2 + 1] > 0.0)
+            dict_set(out, ("scenario/" + E.hs[i].name + "/episode_score").c_str(), -he[i * 2] / he[i * 2 + 1]);
+    }
+    const double c = h[0];
+    if (c <= 0.0) return;
+    const double dt = E.hs.empty() ? 300.0 : E.hs[0].dt;
+    dict_set(out, "live/reward", h[1] / c);
+    dict_set(out, "live/productivity", h[2] / c);
+    dict_set(out, "live/energy_cost_norm", h[3] / c);
+    dict_set(out, "live/carbon_norm", h[4] / c);
+    dict_set(out, "live/comfort_dev_K", h[5] / c);
+    dict_set(out, "live/worst_dev_K", h[6] / c);
+    dict_set(out, "live/out_of_band_frac", h[7] / c);
+    dict_set(out, "live/elec_kw", h[8] / c * 3600.0 / dt);
+    dict_set(out, "live/gas_kw", h[9] / c * 3600.0 / dt);
+}
+
+void puf_mask_init(unsigned char* mask, int width, int nagents) {
+    if (!g_eng) { set_err("puf_mask_init: no env batch"); return; }
+    if (width < 1 || width > SB_MASK_WIDTH || nagents != g_eng->n_env) {
+        set_err("puf_mask_init: width %d / agents %d do not match the batch", width, nagents);
+        return;
+    }
+    std::vector<unsigned char> host((size_t)nagents * width, 0);
+    for (int env = 0; env < nagents; env++) {
+        const HostScn& s = g_eng->hs[g_eng->ei[env].scn];
+        unsigned char* m = host.data() + (size_t)env * width;
+        for (int h = 0; h < SB_CONT && h < width; h++) m[h] = h < s.n_cont ? 1 : 0;
+        for (int h = 0; h < SB_DISC && SB_CONT + 2 * h + 1 < width; h++) {
+            const unsigned char v = h < s.n_disc ? 1 : 0;
+            m[SB_CONT + 2 * h] = v;
+            m[SB_CONT + 2 * h + 1] = v;
+        }
+    }
+    if (cudaMemcpy(mask, host.data(), host.size(), cudaMemcpyHostToDevice) != cudaSuccess)
+        set_err("puf_mask_init: copy failed");
+}
+
+int sb_device_status(void) {
+    if (!g_eng) return 0;
+    int st = 0;
+    cudaStreamSynchronize(g_eng->stream);
+    cudaMemcpy(&st, g_eng->ctx.status, sizeof(int), cudaMemcpyDeviceToHost);
+    return st;
+}
+
+void sb_shape(int* out) {
+    memset(out, 0, sizeof(int) * 8);
+    if (!g_eng) return;
+    Engine& E = *g_eng;
+    out[0] = E.n_env;
+    out[1] = (int)E.sd.size();
+    out[2] = (int)E.gd.size();
+    for (auto& s : E.hs) {
+        out[3] = std::max(out[3], s.obs_len());
+        out[4] = std::max(out[4], s.n_cont);
+        out[5] = std::max(out[5], s.n_disc);
+    }
+    out[6] = (int)E.slabs.size();
+    out[7] = 4;
+}
+
+void sb_env_info(int* obs_len, int* scenario) {
+    if (!g_eng) return;
+    for (int env = 0; env < g_eng->n_env; env++) {
+        const int s = g_eng->ei[env].scn;
+        if (obs_len) obs_len[env] = g_eng->hs[s].obs_len();
+        if (scenario) scenario[env] = s;
+    }
+}
+
+int sb_get_temp(int env, double* out, int n_cvs) {
+    if (!g_eng || env < 0 || env >= g_eng->n_env) return -1;
+    Engine& E = *g_eng;
+    const GroupDev& g = E.gd[E.ei[env].group];
+    const HostGroup& h = E.hg[E.ei[env].group];
+    if (n_cvs != g.ncv) return -1;
+    std::vector<double> tmp(g.ncv);
+    cudaStreamSynchronize(E.stream);
+    if (cudaMemcpy(tmp.data(), g.T + (size_t)E.ei[env].local * g.ncv, g.ncv * sizeof(double),
+                   cudaMemcpyDeviceToHost) != cudaSuccess)
+        return -1;
+    for (int p = 0; p < g.ncv; p++) out[p] = tmp[h.pos_of_cell[p]];
+    return 0;
+}
+
+int sb_get_mass(int env, double* out, int n_solved) {
+    if (!g_eng || env < 0 || env >= g_eng->n_env) return -1;
+    Engine& E = *g_eng;
+    const GroupDev& g = E.gd[E.ei[env].group];
+    const HostGroup& h = E.hg[E.ei[env].group];
+    if (n_solved != g.n) return -1;
+    std::vector<double> tmp(g.n);
+    cudaStreamSynchronize(E.stream);
+    if (cudaMemcpy(tmp.data(), g.M + (size_t)E.ei[env].local * g.n, g.n * sizeof(double),
+                   cudaMemcpyDeviceToHost) != cudaSuccess)
+        return -1;
+    for (int t = 0; t < g.n; t++) out[t] = tmp[h.row_of_solved[t]];
+    return 0;
+}
+
+int sb_get_reward_f64(double* reward, double* parts) {
+    if (!g_eng) return -1;
+    Engine& E = *g_eng;
+    cudaStreamSynchronize(E.stream);
+    if (reward && cudaMemcpy(reward, E.ctx.rew_f64, sizeof(double) * E.n_env, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return -1;
+    if (parts && cudaMemcpy(parts, E.ctx.parts_out, sizeof(double) * kParts * E.n_env, cudaMemcpyDeviceToHost) !=
+                     cudaSuccess)
+        return -1;
+    return 0;
+}
+
+int sb_kernels_per_step(void) { return 4; }
+
+int sb_solve_schedule(const char* blob_path, int sweep, uint8_t* out, size_t cap, size_t* used, uint32_t* nchunks) {
+    sbb::Reader r;
+    std::string e = r.open(blob_path ? blob_path : "");
+    if (!e.empty()) { set_err("%s", e.c_str()); return -1; }
+    HostGroup g;
+    e = build_group(r, g);
+    if (!e.empty()) { set_err("%s", e.c_str()); return -1; }
+    const HostSweep& s = sweep == 0 ? g.fwd : g.bwd;
+    if (used) *used = s.bytes.size();
+    if (nchunks) *nchunks = (uint32_t)s.chunk_bytes.size();
+    if (!out || cap < s.bytes.size()) return 1;
+    memcpy(out, s.bytes.data(), s.bytes.size());
+    return 0;
+}
+
+}  // extern "C"

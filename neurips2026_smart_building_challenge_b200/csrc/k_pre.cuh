@@ -1,0 +1,321 @@
+// Pre-solve stage of one env step: action decode, actuator routing, zone
+// sensing, thermostats, VAV/AHU air flows, reheat, and the per-zone applied
+// heat the forcing needs. One CTA per env; order-dependent sums run on one
+// thread in the reference's order, independent per-VAV work runs in parallel.
+//
+// Reference: complete_port/pufferlib_cpu_env.h:218-234 (clamp + decode),
+// complete_port/csim/sb_sim.c:220-244 (apply), :246-355 (device models,
+// thermostat), :357-457 (sb_sim_step_pre).
+#pragma once
+#include "dev_util.cuh"
+
+namespace sbenv {
+
+constexpr double RHO_AIR = 1.2;
+constexpr double CP_AIR = 1006.0;
+constexpr double RHO_W = 1000.0;
+constexpr double CP_W = 4180.0;
+constexpr double GRAV = 9.8;
+constexpr double PA_PER_BAR = 100000.0;
+enum { M_OFF = 0, M_HEAT = 1, M_COOL = 2, M_PASSIVE = 3 };
+
+struct EnvView {   // one env's state blocks
+    double* D;
+    int32_t* I;
+    const StateLayout* L;
+    __device__ double& d(int off, int i = 0) const { return D[off + i]; }
+    __device__ int32_t& iv(int off, int i = 0) const { return I[off + i]; }
+};
+
+__device__ __forceinline__ double ahu_static_p(const EnvView& v, const ScnDev& s, int a) {
+    if (v.iv(v.L->ahu_run, a) != 1) return 0.0;
+    const double sp = v.d(v.L->ahu_fan, a), mn = s.ahu_c[a * 9 + 2];
+    return sp > mn ? sp : mn;
+}
+__device__ __forceinline__ double vav_unrestricted(const EnvView& v, const ScnDev& s, int vv) {
+    const double* vc = &s.vav_c[vv * 9];
+    const double stat = ahu_static_p(v, s, s.v_ahu[vv]);
+    const double d = dmul(dmul(v.d(v.L->v_damp, vv), vc[0]), sqrt(ddiv(stat, vc[4])));
+    return d > 0.00001 ? d : 0.00001;
+}
+__device__ __forceinline__ double pump_dp(const EnvView& v) {
+    if (v.iv(v.L->pump_run) != 1) return 0.0;
+    return ddiv(dmul(GRAV * RHO_W, v.d(v.L->pump_head)), PA_PER_BAR);
+}
+__device__ __forceinline__ double water_flow(const EnvView& v, const ScnDev& s) {
+    const double ff = v.d(v.L->ff_sum);
+    const double den = dadd(1.0, dmul(dmul(ff, ff), s.header_res));
+    return ddiv(dmul(ff, sqrt(ddiv(pump_dp(v), den))), 3600.0);
+}
+// reheat_energy (sb_sim.c:289-314); vd = vav_flow_demand of this VAV
+__device__ inline double reheat_energy(const EnvView& v, const ScnDev& s, int vv, double sat, double iwt,
+                                       double vd) {
+    const double air_cap = dmul(CP_AIR * RHO_AIR, vd);
+    double eff;
+    if (air_cap <= 0.0) {
+        eff = 0.0;
+    } else {
+        const double ffs = v.d(v.L->ff_sum);
+        double wf = 0.0;
+        if (ffs != 0.0) wf = dmul(water_flow(v, s), ddiv(dmul(v.d(v.L->v_reh, vv), s.vav_c[vv * 9 + 1]), ffs));
+        eff = ddiv(dmul(CP_W * RHO_W, wf), air_cap);
+        if (eff > 1.0) eff = 1.0;
+        const double gap = dsub(iwt, sat);
+        if (gap > 0.0) {
+            const double head = dsub(s.vav_c[vv * 9 + 3], sat);
+            if (head <= 0.0) eff = 0.0;
+            else {
+                const double hr = ddiv(head, gap);
+                eff = eff < hr ? eff : hr;
+            }
+        }
+    }
+    return dmul(dmul(dmul(dmul(eff, CP_AIR), RHO_AIR), vd), dsub(iwt, sat));
+}
+
+// Field-averaged zone temperatures (sb_sim.c:149-160) from an extended-order field.
+__device__ inline void zone_means(const GroupDev& g, const ScnDev& s, const double* T, double* zavg) {
+    for (int z = threadIdx.x; z < s.nz; z += blockDim.x) {
+        const int rm = s.proom[z];
+        const int a = g.room_off[rm], b = g.room_off[rm + 1];
+        double sum = 0.0;
+        for (int t = a; t < b; t++) sum = dadd(sum, T[g.room_pos[t]]);
+        zavg[z] = ddiv(sum, (double)(b - a));
+    }
+}
+
+// VAV area + sensing (sb_sim.c:163-175), one thread per VAV.
+__device__ inline void vav_sensing(const ScnDev& s, const double* zavg, double* area_out, double* sense_out) {
+    for (int v = threadIdx.x; v < s.nv; v += blockDim.x) {
+        double area = 0.0, wt = 0.0;
+        for (int t = s.vz_off[v]; t < s.vz_off[v + 1]; t++) {
+            const int z = s.vz_idx[t];
+            area = dadd(area, s.zarea[z]);
+            wt = dadd(wt, dmul(zavg[z], s.zarea[z]));
+        }
+        area_out[v] = area;
+        sense_out[v] = area > 0.0 ? ddiv(wt, area) : 0.0;
+    }
+}
+
+__device__ __forceinline__ void mode_default(int& mode, double zt, double hsp, double csp) {
+    const double mid = dadd(dmul(0.5, dsub(csp, hsp)), hsp);
+    if (zt < hsp) mode = M_HEAT;
+    else if (zt > csp) mode = M_COOL;
+    else if (zt < mid && mode == M_HEAT) mode = M_HEAT;
+    else if (zt > mid && mode == M_COOL) mode = M_COOL;
+    else mode = M_OFF;
+}
+
+__global__ void __launch_bounds__(128) k_pre(const StepCtx* __restrict__ ctx) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int env = blockIdx.x;
+    const EnvIndex ei = ctx->envs[env];
+    const GroupDev& g = ctx->groups[ei.group];
+    const ScnDev& s = ctx->scns[ei.scn];
+    const StateLayout& L = ctx->lay;
+    EnvView v{ctx->Dst + (size_t)env * L.nd, ctx->Ist + (size_t)env * L.ni, &ctx->lay};
+    const int tid = threadIdx.x;
+    const int na = s.na, nv = s.nv, nz = s.nz, k = s.k;
+
+    double* T = reinterpret_cast<double*>(smem);      // [ncv]
+    double* zavg = T + g.ncv;                         // [nz]
+    double* zq = zavg + nz;                           // [nz]
+    double* unr = zq + nz;                            // [nv]
+    double* sv = unr + nv;                            // [na] supply air temperature
+    double* demand = sv + na;                         // [na]
+    double* rw = demand + na;                         // [k]
+    double* fdv = rw + k;                             // [k]
+
+    const int kk = v.iv(L.step);
+    const double ambient = s.amb[kk];
+    const int comfort = s.s_comf[kk] != 0.0;
+
+    // ---- decode + apply (pufferlib_cpu_env.h:218-234, sb_sim.c:557-576, :220-244) ----
+    // Actuator targets are unique per blob (checked on the host), so actions apply in parallel.
+    const float* act = ctx->actions + (size_t)env * kAct;
+    for (int i = tid; i < s.nact; i += blockDim.x) {
+        const uint8_t dsc = s.a_disc[i];
+        const int slot = s.a_slot[i];   // position in the packed continuous / discrete block
+        double val;
+        if (dsc) {
+            const double dv = (double)act[kCont + slot];
+            const double merged = dv == 1.0 ? 1.0 : -1.0;
+            val = dadd(dmul(ddiv(dsub(merged, s.a_mnr[i]), dsub(s.a_mxr[i], s.a_mnr[i])),
+                            dsub(s.a_mx[i], s.a_mn[i])), s.a_mn[i]);
+        } else {
+            double a = (double)act[slot];
+            a = a > 1.0 ? 1.0 : (a < -1.0 ? -1.0 : a);
+            const float m = (float)a;
+            const float span_in = (float)dsub(s.a_mxr[i], s.a_mnr[i]);
+            const float span_out = (float)dsub(s.a_mx[i], s.a_mn[i]);
+            const float r = __fadd_rn(__fmul_rn(__fdiv_rn(__fsub_rn(m, (float)s.a_mnr[i]), span_in), span_out),
+                                      (float)s.a_mn[i]);
+            val = (double)r;
+        }
+        const int idx = s.a_idx[i], ac = s.a_act[i];
+        if (s.a_kind[i] == 0) {
+            if (ac == 0) v.d(L.ahu_sat, idx) = val;
+            else if (ac == 1) v.d(L.ahu_fan, idx) = val;
+            else if (ac == 2) {
+                const double hi = s.ahu_c[idx * 9 + 3];
+                v.d(L.ahu_rec, idx) = val < 0.0 ? 0.0 : (val > hi ? hi : val);
+            } else v.iv(L.ahu_run, idx) = val == 1.0 ? 1 : 0;
+        } else if (s.a_kind[i] == 1) {
+            const double c01 = val < 0.0 ? 0.0 : (val > 1.0 ? 1.0 : val);
+            if (ac == 0) { v.d(L.v_dcmd, idx) = c01; v.iv(L.v_dset, idx) = 1; }
+            else { v.d(L.v_rcmd, idx) = c01; v.iv(L.v_rset, idx) = 1; }
+        } else {
+            if (ac == 0) v.d(L.b_sp) = val;
+            else if (ac == 1) v.d(L.pump_head) = ddiv(val, ddiv(GRAV * RHO_W, PA_PER_BAR));
+            else { const int on = val == 1.0 ? 1 : 0; v.iv(L.hws_run) = on; v.iv(L.pump_run) = on; }
+        }
+    }
+    // ---- field into shared memory, zone means ----
+    const double* Tg = g.T + (size_t)(env - g.env0) * g.ncv;
+    for (int i = tid; i < g.ncv; i += blockDim.x) T[i] = Tg[i];
+    __syncthreads();
+    if (tid == 0) v.iv(L.hws_req) = nv;
+    zone_means(g, s, T, zavg);
+    __syncthreads();
+    // ---- VAV sensing, thermostat, damper/reheat (sb_sim.c:368-384, :316-355) ----
+    for (int vv = tid; vv < nv; vv += blockDim.x) {
+        double area = 0.0, wt = 0.0;
+        for (int t = s.vz_off[vv]; t < s.vz_off[vv + 1]; t++) {
+            const int z = s.vz_idx[t];
+            area = dadd(area, s.zarea[z]);
+            wt = dadd(wt, dmul(zavg[z], s.zarea[z]));
+        }
+        v.d(L.v_area, vv) = area;
+        if (area <= 0.0) { v.d(L.v_sense, vv) = 0.0; continue; }
+        const double sensing = ddiv(wt, area);
+        v.d(L.v_sense, vv) = sensing;
+        const double* c = &s.vav_c[vv * 9];
+        const double hsp = s.s_heat[kk], csp = s.s_cool[kk];
+        v.d(L.v_hsp, vv) = hsp;
+        v.d(L.v_csp, vv) = csp;
+        int mode = v.iv(L.v_mode, vv);
+        if (comfort) mode_default(mode, sensing, hsp, csp);
+        else if (v.iv(L.v_prev, vv) && s.s_comf[kk - 1] != 0.0) mode = M_PASSIVE;
+        else if (mode == M_PASSIVE && sensing > hsp && sensing < csp) mode = M_PASSIVE;
+        else mode_default(mode, sensing, hsp, csp);
+        v.iv(L.v_mode, vv) = mode;
+        v.iv(L.v_prev, vv) = 1;
+        double damper, reheat;
+        if (mode == M_HEAT) { damper = 1.0; reheat = 1.0; }
+        else if (mode == M_COOL) { damper = 1.0; reheat = 0.0; }
+        else { damper = c[2]; reheat = 0.0; }
+        if (v.iv(L.v_dset, vv)) damper = v.d(L.v_dcmd, vv);
+        if (v.iv(L.v_rset, vv)) reheat = v.d(L.v_rcmd, vv);
+        v.d(L.v_damp, vv) = damper > c[2] ? damper : c[2];
+        v.d(L.v_reh, vv) = reheat;
+    }
+    __syncthreads();
+    // ---- ordered accumulations (sb_sim.c:367-392) ----
+    if (tid == 0) {
+        double ws[kMaxAhu], at[kMaxAhu];
+        for (int a = 0; a < na; a++) { ws[a] = 0.0; at[a] = 0.0; }
+        for (int vv = 0; vv < nv; vv++) {
+            const double area = v.d(L.v_area, vv);
+            if (area <= 0.0) continue;
+            const int a = s.v_ahu[vv];
+            ws[a] = dadd(ws[a], dmul(v.d(L.v_sense, vv), area));
+            at[a] = dadd(at[a], area);
+        }
+        double tmean = 0.0;
+        if (s.tmean_needed) {
+            for (int p = 0; p < g.ncv; p++) tmean = dadd(tmean, T[g.pos_of_cell[p]]);
+            tmean = ddiv(tmean, (double)g.ncv);
+        }
+        for (int a = 0; a < na; a++) {
+            const double recirc = at[a] > 0.0 ? ddiv(ws[a], at[a]) : tmean;
+            const double rec = v.d(L.ahu_rec, a);
+            const double mixed = dadd(dmul(rec, recirc), dmul(dsub(1.0, rec), ambient));
+            sv[a] = (mixed > v.d(L.ahu_sat, a) && v.iv(L.ahu_run, a) == 1) ? v.d(L.ahu_sat, a) : mixed;
+            v.d(L.ahu_flow, a) = 0.0;
+            v.iv(L.ahu_creq, a) = 0;
+            demand[a] = 0.0;
+        }
+        double ff = 0.0;
+        for (int vv = 0; vv < nv; vv++) ff = dadd(ff, dmul(v.d(L.v_reh, vv), s.vav_c[vv * 9 + 1]));
+        v.d(L.ff_sum) = ff;
+    }
+    __syncthreads();
+    for (int vv = tid; vv < nv; vv += blockDim.x) unr[vv] = vav_unrestricted(v, s, vv);
+    __syncthreads();
+    if (tid == 0)
+        for (int vv = 0; vv < nv; vv++) demand[s.v_ahu[vv]] = dadd(demand[s.v_ahu[vv]], unr[vv]);
+    __syncthreads();
+    for (int vv = tid; vv < nv; vv += blockDim.x) {
+        const int a = s.v_ahu[vv];
+        const double d = demand[a];
+        if (d > 0.0) {
+            const double r = ddiv(s.ahu_c[a * 9 + 1], d);
+            v.d(L.v_ratio, vv) = r < 1.0 ? r : 1.0;
+        } else {
+            v.d(L.v_ratio, vv) = 1.0;
+        }
+    }
+    for (int z = tid; z < nz; z += blockDim.x) zq[z] = 0.0;
+    __syncthreads();
+    // ---- coupled columns (sb_sim.c:408-436): per-column values in parallel ----
+    const double b_cur = v.d(L.b_cur);
+    for (int col = tid; col < k; col += blockDim.x) {
+        const int vv = s.coupled[col];
+        if (v.d(L.v_area, vv) <= 0.0) {
+            v.d(L.ag, col) = 0.0;
+            v.d(L.aT, col) = 0.0;
+            rw[col] = 0.0;
+            fdv[col] = 0.0;
+            continue;
+        }
+        const double sat = sv[s.v_ahu[vv]];
+        v.d(L.aT, col) = sat;
+        v.d(L.coil, col) = sat;
+        const double vd = dmul(unr[vv], v.d(L.v_ratio, vv));
+        rw[col] = reheat_energy(v, s, vv, sat, b_cur, vd);
+        fdv[col] = vd;
+        const bool flows = v.d(L.v_damp, vv) > 0.0 && s.vav_c[vv * 9] > 0.0;
+        v.d(L.ag, col) = flows ? dmul(dmul(vd, RHO_AIR), CP_AIR) : 0.0;
+    }
+    __syncthreads();
+    // ... and their order-dependent sums on one thread
+    if (tid == 0) {
+        double rsum = 0.0;
+        for (int col = 0; col < k; col++) {
+            const int vv = s.coupled[col];
+            const double area = v.d(L.v_area, vv);
+            if (area <= 0.0) continue;
+            const int a = s.v_ahu[vv];
+            rsum = dadd(rsum, rw[col]);
+            if (v.d(L.v_damp, vv) > 0.0 && s.vav_c[vv * 9] > 0.0)
+                for (int t = s.vz_off[vv]; t < s.vz_off[vv + 1]; t++) {
+                    const int z = s.vz_idx[t];
+                    zq[z] = dadd(zq[z], ddiv(dmul(rw[col], s.zarea[z]), area));
+                }
+            const double fd = fdv[col];
+            if (fd > 0.0) {
+                double f = dadd(v.d(L.ahu_flow, a), fd);
+                const double mf = s.ahu_c[a * 9 + 1];
+                if (f > mf) f = mf;
+                v.d(L.ahu_flow, a) = f;
+                v.iv(L.ahu_creq, a) += 1;
+            }
+        }
+        v.d(L.reheat_w) = rsum;
+    }
+    __syncthreads();
+    // ---- internal + occupant gains, per-cell applied heat (sb_sim.c:438-455) ----
+    const double* Vin = v.D + L.V;
+    const double frac = comfort ? 1.0 : s.standby;
+    const double wpc = dmul(dmul(s.internal_w, s.cv_area), frac);
+    for (int z = tid; z < nz; z += blockDim.x) {
+        double q = zq[z];
+        const double cells = (double)s.room_ncell[z];
+        if (s.internal_w > 0.0) q = dadd(q, dmul(wpc, cells));
+        if (s.occ_w > 0.0) q = dadd(q, dmul(Vin[z], s.occ_w));
+        v.d(L.qdiv, z) = ddiv(q, cells);
+    }
+}
+
+}  // namespace sbenv

@@ -1,0 +1,176 @@
+// Device-side table and state descriptors shared by the host builder
+// (tables.cpp, env.cu) and the kernels (kernels.cuh).
+//
+// Terminology (the reference's domain):
+//   scenario  one SBB1 blob = one building x one weather/calendar;
+//   group     scenarios whose geometry and thermal factors are byte-identical,
+//             so they share one set of device solver tables;
+//   slab      the envs of one group that one solve CTA holds in shared memory;
+//   row order the row index space of the factored matrix B = Pr A Pc: solved
+//             cell t sits at row position i with t = inv(perm_r)[i]. The field
+//             of every env is kept in "extended row order": positions [0, n)
+//             are the solved cells in row order, [n, ncv) the unsolved cells.
+#pragma once
+#include <cstdint>
+
+namespace sbenv {
+
+constexpr int kObs = 1024;             // OBS_SIZE (complete_port/gpu/smart_buildings.cu:33)
+constexpr int kCont = 256;             // SB_CONT
+constexpr int kDisc = 16;              // SB_DISC
+constexpr int kAct = kCont + kDisc;    // NUM_ATNS
+constexpr int kMaskWidth = kCont + 2 * kDisc;
+constexpr int kParts = 8;              // per-step log terms (smart_buildings.cu:101-115)
+constexpr int kRingSlots = 6;          // solve schedule ring depth
+constexpr int kRingSlotBytes = 4096;   // one schedule chunk at most
+constexpr int kSolveThreads = 512;
+constexpr int kMaxK = 128;             // coupled VAVs (dense air-side system in shared memory)
+constexpr int kMaxAhu = 16;
+constexpr int kMaxConvRoom = 8192;     // cells of one convection room
+
+// Error codes written to the device status word (first error wins).
+enum : int {
+    kErrNone = 0,
+    kErrRingTimeout = 1,   // a schedule chunk never arrived (bounded mbarrier wait)
+    kErrBadChunk = 2,      // a schedule chunk header failed its consistency check
+    kErrConvOverflow = 3,  // convection swap list exceeded its buffer
+    kErrDenseSingular = 4  // reserved: the reference tolerates a zero pivot, so do we
+};
+
+// One solve-schedule chunk in global memory, 16-byte aligned:
+//   ChunkHeader | TaskRec[ntask] | double val[nval] | uint16_t col[nval] | pad
+struct ChunkHeader {
+    uint32_t ntask;
+    uint32_t nval;
+    uint32_t next_bytes;  // byte size of the chunk kRingSlots positions later (0 past the end)
+    uint32_t check;       // ntask ^ (nval << 12) ^ 0x5B5B0000, validated on the device
+};
+// row: row position; nterm: terms applied in this phase; flags bit0: the task
+// finalises a backward-sweep row (divide by the diagonal stored in val[off+nterm]).
+struct TaskRec {
+    uint16_t row;
+    uint8_t nterm_lo;
+    uint8_t flags_hi;   // bits 0-3: nterm high nibble (nterm < 4096); bit 7: finalise
+    uint32_t off;       // first term in this chunk's val/col arrays
+};
+
+struct Sweep {
+    const uint8_t* stream;  // chunks back to back
+    uint32_t nchunks;
+    uint32_t first_bytes[kRingSlots];
+};
+
+// Geometry + solver tables of one group and the state of its envs.
+struct GroupDev {
+    int n, ncv, k, nz, nv, na;
+    int stride;        // shared-memory vector stride (doubles) of one env in a slab
+    int slab_envs;     // envs per solve CTA
+    int n_env;         // envs in the group
+    int env0;          // first global env index
+    int sigma_identity;
+    // row-order coefficient tables
+    const double *cap, *dirx, *mc, *ret, *gain;
+    const int32_t* zone_of_row;   // -1: no applied heat on this cell
+    Sweep fwd, bwd;
+    // air side in row positions
+    const int32_t *sn_p, *sn_pos;   // sensed CSR, k rows
+    const double* sn_x;
+    const int32_t *ap_rp, *ap_col;  // applied by row position, coupled columns ascending
+    const double* ap_x;
+    const double* S;                // k x k sensed response
+    // rooms: cells of each room in extended positions
+    const int32_t *room_off, *room_pos;
+    const int32_t* cell_of_pos;     // extended position -> cell index (field mean order)
+    const int32_t* pos_of_cell;
+    // convection (room-local candidate lists in convection-cell numbering)
+    const int32_t *cv_off, *cv_pos, *cand_off, *cand_idx;
+    int conv_nrooms, conv_maxroom;
+    // per-env state
+    double* T;     // [n_env][ncv] extended row order
+    double* M;     // [n_env][n] interior mass, row order
+};
+
+// Per-scenario (blob) tables. Everything that may differ between weathers of
+// one building lives here.
+struct ScnDev {
+    int group;
+    int env0, n_env;           // global env range
+    int na, nv, nz, k, nact, n_cont, n_disc, n_dev, n_aux, max_steps;
+    int assign, ea, la, ed, ld, hour_m1, wd_m1;
+    int tmean_needed;          // some AHU serves no VAV area: the field mean is used
+    double p_arr, p_dep, dt, internal_w, standby, occ_w, cv_area, header_res, pump_eff;
+    double pump_head0, gas_carbon, conv_p;
+    int conv_dist;
+    double boiler[10];
+    double boiler_cond;        // log(r2/c6)/c8, evaluated once on the host
+    const double *amb, *s_comf, *s_heat, *s_cool, *aux;
+    const int64_t *o_hour, *r_hour, *r_month;
+    const uint8_t *o_wd, *r_wd;
+    const double *ahu_c, *vav_c, *zarea;
+    const int32_t *vz_off, *vz_idx, *v_ahu, *coupled, *zv_off, *zv_idx, *proom, *room_ncell;
+    const uint8_t *a_kind, *a_act, *a_disc;
+    const int32_t *a_idx, *a_slot;
+    const double *a_mn, *a_mx, *a_mnr, *a_mxr;
+    const uint8_t *f_kind, *f_id;
+    const int32_t* f_idx;
+    const double *f_mean, *f_var;
+    const double *rw, *e_wd, *e_we, *e_c, *g_p;
+    const double *temp_init, *mass_init;   // extended row order / row order
+    // random streams (per scenario): MT19937 raw state + position
+    uint32_t* conv_mt;   // 625 words: 624 state + position
+    uint32_t* occ_mt;    // [2][625] double-buffered by env generation parity
+    int* occ_state0;     // [2][nz*assign] occupant states, same buffering
+    int32_t* conv_pairs; // [2*ncv]: (dst, src) extended positions
+    int* conv_npairs;
+    int32_t* conv_scratch; // per-room permutation scratch / swap lists
+    int scn_index;
+};
+
+// Per-env HVAC state. Offsets into one env's double and int blocks.
+struct StateLayout {
+    int nd, ni;   // doubles / ints per env
+    int ahu_rec, ahu_sat, ahu_fan, ahu_flow;
+    int v_damp, v_reh, v_ratio, v_hsp, v_csp, v_dcmd, v_rcmd, v_sense, v_area;
+    int qdiv, ag, aT, coil, V;   // step transients / occupancy
+    int ff_sum, pump_head, b_sp, b_ret, b_cur, b_step, reheat_w;
+    int ahu_run, ahu_creq, v_mode, v_prev, v_dset, v_rset;
+    int hws_req, hws_run, pump_run, step, gen, active;
+};
+
+struct EnvIndex {   // global env -> its group and scenario
+    int group, scn, local;   // local: index inside the group
+    int writer;              // 1: this env writes its scenario's next occupancy stream
+};
+
+// Everything one step launch needs; copied to device memory once.
+struct StepCtx {
+    const GroupDev* groups;
+    const ScnDev* scns;
+    const EnvIndex* envs;
+    int n_env, n_groups, n_scns;
+    StateLayout lay;
+    double* Dst;          // [n_env][lay.nd]
+    int32_t* Ist;         // [n_env][lay.ni]
+    // framework buffers (device memory owned by the caller)
+    const float* actions; // [n_env][kAct]
+    float* obs;           // [n_env][kObs]
+    float* rewards;       // [n_env]
+    float* terminals;     // [n_env]
+    float reward_scale;
+    void* env_records;    // Env[n_env] (managed memory, layout in include/sbenv.h)
+    // episode statistics
+    double* rew_f64;      // [n_env] last step's reward in double
+    double* parts_out;    // [n_env][kParts] last step's log terms
+    double* epret_d;      // [n_env] running episode return in double
+    double* live;         // [2 + kParts] step-level sums: count, reward, parts
+    double* live_scn;     // [n_scns][4]: reward, mean deviation, count, reward^2
+    double* ep_scn;       // [n_scns][2]: completed-episode mean rewards, count
+    int* status;          // device error word
+    // per-scenario random-stream results of the current step
+    const double* V_step;   // [n_scns][nz_max]
+    const double* V_prime;
+    const double* V_zero;
+    int nz_max;
+};
+
+}  // namespace sbenv

@@ -781,8 +781,9 @@ extern "C" int sbgen_preset(int config, int index, SbGenParams* o) {
         if (index < 0 || index >= 30) return -1;
         static const int rooms[6] = {41, 49, 57, 65, 73, 81};
         static const int ahus[6] = {1, 2, 2, 3, 3, 4};
-        static const int gr[6] = {64, 64, 64, 72, 72, 80};
-        static const int gc[6] = {48, 48, 56, 56, 64, 64};
+        // every layout shares configuration 1's 64x48 grid; the room count sets the partition
+        static const int gr[6] = {64, 64, 64, 64, 64, 64};
+        static const int gc[6] = {48, 48, 48, 48, 48, 48};
         static const double tmean[5] = {-5.0, 5.0, 15.0, 25.0, 32.0};
         static const double tamp[5] = {4.0, 5.5, 7.0, 8.5, 10.0};
         const int L = index / 5, c = index % 5;
