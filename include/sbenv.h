@@ -144,6 +144,10 @@ int sb_get_mass(int env, double* out, int n_solved);
 int sb_get_reward_f64(double* reward, double* parts);
 /* Number of hot-path kernel launches one puf_step enqueues. */
 int sb_kernels_per_step(void);
+/* Inspection: one env's last pre-stage results, out = [air conductance k][supply
+ * air temperature k][applied heat per zone cell nz][flow factor sum, reheat W,
+ * boiler temperature, boiler return, pump head]. Returns the count or -1. */
+int sb_debug_state(int env, double* out, int cap);
 /* Host-only: the device solve schedule of a blob's factor (sweep 0 = L, 1 = U)
  * as the byte stream the solve kernel streams into shared memory. Returns 0, 1
  * if cap is too small (*used then holds the size), -1 on error. */

@@ -38,7 +38,7 @@ ENV_SYMBOLS = ["sb_dict_new", "sb_dict_free", "dict_find", "dict_set", "dict_set
                "puf_bind_stream", "puf_init", "puf_reset", "puf_step", "puf_render", "puf_close", "puf_log",
                "puf_live_log", "puf_mask_init", "sb_last_error", "sb_device_status", "sb_shape",
                "sb_env_info", "sb_get_temp", "sb_get_mass", "sb_get_reward_f64", "sb_kernels_per_step",
-               "sb_solve_schedule"]
+               "sb_solve_schedule", "sb_debug_state"]
 GEN_SYMBOLS = ["sbgen_preset", "sbgen_write", "sbgen_factor_stats"]
 
 
@@ -113,6 +113,7 @@ def env_lib() -> ctypes.CDLL:
         lib.sb_get_temp.argtypes = [ctypes.c_int, dp, ctypes.c_int]
         lib.sb_get_mass.argtypes = [ctypes.c_int, dp, ctypes.c_int]
         lib.sb_get_reward_f64.argtypes = [dp, dp]
+        lib.sb_debug_state.argtypes = [ctypes.c_int, dp, ctypes.c_int]
         lib._sb_typed = True
     return lib
 

@@ -172,8 +172,12 @@ __device__ __forceinline__ uint32_t mt_bounded(WarpMt& m, uint32_t hi) {
     return v;
 }
 
-// Stores the stream back: raw words of the current block + position.
-__device__ inline void mt_store(const WarpMt& m, uint32_t* g) {
+// Stores the stream back: raw words of the current block + position. A
+// warp-parallel scan may have read ahead into the next block (position up to
+// 1247); the stored position must index the block the state words describe,
+// so such a stream is rolled forward first.
+__device__ inline void mt_store(WarpMt& m, uint32_t* g) {
+    if (m.pos > 624) mt_roll(m);
     const int lane = threadIdx.x & 31;
     for (int i = lane; i < 624; i += 32) g[i] = m.st[i];
     if (lane == 0) g[624] = (uint32_t)m.pos;

@@ -742,6 +742,27 @@ int sb_get_reward_f64(double* reward, double* parts) {
 
 int sb_kernels_per_step(void) { return 4; }
 
+int sb_debug_state(int env, double* out, int cap) {
+    if (!g_eng || env < 0 || env >= g_eng->n_env) return -1;
+    Engine& E = *g_eng;
+    const StateLayout& L = E.ctx.lay;
+    const HostScn& s = E.hs[E.ei[env].scn];
+    const int need = 2 * s.k + s.nz + 5;
+    if (cap < need) return -1;
+    std::vector<double> D(L.nd);
+    cudaStreamSynchronize(E.stream);
+    if (cudaMemcpy(D.data(), E.ctx.Dst + (size_t)env * L.nd, L.nd * sizeof(double), cudaMemcpyDeviceToHost) !=
+        cudaSuccess)
+        return -1;
+    int o = 0;
+    for (int i = 0; i < s.k; i++) out[o++] = D[L.ag + i];
+    for (int i = 0; i < s.k; i++) out[o++] = D[L.aT + i];
+    for (int z = 0; z < s.nz; z++) out[o++] = D[L.qdiv + z];
+    out[o++] = D[L.ff_sum]; out[o++] = D[L.reheat_w]; out[o++] = D[L.b_cur]; out[o++] = D[L.b_ret];
+    out[o++] = D[L.pump_head];
+    return o;
+}
+
 int sb_solve_schedule(const char* blob_path, int sweep, uint8_t* out, size_t cap, size_t* used, uint32_t* nchunks) {
     sbb::Reader r;
     std::string e = r.open(blob_path ? blob_path : "");

@@ -160,3 +160,5 @@ void sbo_reseed(SboEnv* e) {
     sb_rng_seed(&e->occ.rng, (uint32_t)sb_i64_1(&e->blob, "occ_seed", 17321));
     sb_rng_seed(&e->conv.rng, e->conv.seed);
 }
+
+int sbo_debug(const SboEnv* e, double* out) { (void)e; (void)out; return -1; }

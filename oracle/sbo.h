@@ -50,6 +50,9 @@ int sbo_step_index(const SboEnv* e);               /* steps in the current episo
 /* Re-seeds the occupancy and convection generators from the blob (tests that
  * compare two passes of one env need identical random streams). */
 void sbo_reseed(SboEnv* e);
+/* Inspection (restatement only): out = [air_g k][air_T k][per-cell zone heat nz]
+ * [flow factor sum, reheat W, boiler T, boiler return, pump head] of the last step. */
+int sbo_debug(const SboEnv* e, double* out);
 
 #ifdef __cplusplus
 }

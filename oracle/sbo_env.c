@@ -84,3 +84,15 @@ void sbo_reseed(SboEnv* e) {
     sbo_mt_seed(&e->st.orng, e->scn.occ_seed);
     sbo_mt_seed(&e->st.crng, e->scn.conv_seed);
 }
+
+int sbo_debug(const SboEnv* e, double* out) {
+    const SboScn* s = &e->scn;
+    const SboState* st = &e->st;
+    int o = 0;
+    for (int i = 0; i < s->k; i++) out[o++] = st->ag[i];
+    for (int i = 0; i < s->k; i++) out[o++] = st->aT[i];
+    for (int z = 0; z < s->nz; z++) out[o++] = st->qpre[z];
+    out[o++] = st->ff_sum; out[o++] = st->reheat_w; out[o++] = st->b_cur; out[o++] = st->b_ret;
+    out[o++] = st->pump_head;
+    return o;
+}

@@ -107,6 +107,7 @@ typedef struct {
     /* env wrapper */
     int step;
     double parts[12];
+    double* qpre;   /* applied heat per zone cell after the pre stage (inspection) */
     double native[272];
 } SboState;
 

@@ -223,6 +223,7 @@ int sbo_state_alloc(SboState* e, const SboScn* s) {
     DALLOC(e->coil, k); DALLOC(e->zfsp, nz); DALLOC(e->zfact, nz);
     IALLOC(e->ostate, nz * s->assign); DALLOC(e->V, nz);
     IALLOC(e->cl, s->conv_maxroom); IALLOC(e->cr, s->conv_maxroom);
+    DALLOC(e->qpre, nz);
     memcpy(e->temp, s->temp_init, sizeof(double) * (size_t)s->ncv);
     memcpy(e->mass, s->mass_init, sizeof(double) * (size_t)n);
     e->pump_head = s->pump_head0;   /* set once at init, never by reset (sb_sim.c:71-75) */
@@ -237,7 +238,7 @@ void sbo_state_free(SboState* e) {
                     e->ahu_at, e->ahu_sv, e->demand, e->v_damp, e->v_reh, e->v_ratio, e->v_hsp, e->v_csp,
                     e->v_dcmd, e->v_rcmd, e->v_sense, e->v_area, e->v_mode, e->v_prev, e->v_dset, e->v_rset,
                     e->zavg, e->zq, e->smean, e->ag, e->aT, e->coil, e->zfsp, e->zfact, e->ostate, e->V,
-                    e->cl, e->cr};
+                    e->cl, e->cr, e->qpre};
     for (size_t i = 0; i < sizeof(ptrs) / sizeof(ptrs[0]); i++) free(ptrs[i]);
     memset(e, 0, sizeof(*e));
 }
@@ -507,6 +508,7 @@ static void step_pre(SboState* e, const SboScn* s) {
         const int rm = s->proom[z];
         const int a = s->room_off[rm], b = s->room_off[rm + 1];
         const double q = e->zq[z] / (double)(b - a);
+        e->qpre[z] = q;
         for (int t = a; t < b; t++) e->inq[s->room_cells[2 * t] * s->nc + s->room_cells[2 * t + 1]] = q;
     }
 }

@@ -56,19 +56,51 @@ def _run_parity(blob_dir, n, steps, max_steps=0, seed=0, temp_every=10, groups=0
             rd, parts = env.reward_f64()
             for e in range(n):
                 o, r, t, r64, p12, log8 = orc[e].step(a[e])
-                where = f"step {s} env {e}"
-                np.testing.assert_array_equal(obs[e].view(np.uint32), o.view(np.uint32), err_msg=f"obs {where}")
-                assert rew[e] == np.float32(r), f"reward f32 {where}: {rew[e]} vs {r}"
-                assert rd[e] == r64, f"reward f64 {where}: {rd[e]!r} vs {r64!r}"
-                assert term[e] == t, f"terminal {where}"
-                np.testing.assert_array_equal(parts[e], log8, err_msg=f"log terms {where}")
-                if s % temp_every == 0 or s == steps - 1:
-                    np.testing.assert_array_equal(env.temp(e, orc[e].ncv), orc[e].temp(), err_msg=f"T {where}")
-                    np.testing.assert_array_equal(env.mass(e, orc[e].n), orc[e].mass(), err_msg=f"M {where}")
+                where = f"step {s} env {e} scenario {int(env.scenario[e])}"
+                bad = []
+                if not np.array_equal(obs[e].view(np.uint32), o.view(np.uint32)):
+                    bad.append(f"obs fields {np.nonzero(obs[e] != o)[0][:8].tolist()}")
+                if rew[e] != np.float32(r) or rd[e] != r64:
+                    bad.append(f"reward {rd[e]!r} vs {r64!r}")
+                if term[e] != t:
+                    bad.append("terminal")
+                if not np.array_equal(parts[e], log8):
+                    bad.append(f"log terms {np.nonzero(parts[e] != log8)[0].tolist()} {parts[e]} vs {log8}")
+                if bad or s % temp_every == 0 or s == steps - 1:
+                    dT = env.temp(e, orc[e].ncv) - orc[e].temp()
+                    dM = env.mass(e, orc[e].n) - orc[e].mass()
+                    if dT.any():
+                        bad.append(f"T differs at {np.count_nonzero(dT)} cells, max {np.abs(dT).max():.3e}")
+                    if dM.any():
+                        bad.append(f"M differs at {np.count_nonzero(dM)} cells, max {np.abs(dM).max():.3e}")
+                if bad:
+                    bad.append(_pre_stage_diff(env, orc[e], e))
+                assert not bad, f"{where}: " + "; ".join(bad)
         assert env.status() == 0
         return env
     finally:
         env.close()
+
+
+def _pre_stage_diff(env, orc, e):
+    """Which pre-stage quantity differs (air conductances, supply temperatures,
+    per-zone cell heat, boiler/pump scalars) -- localises a field mismatch."""
+    import ctypes
+
+    g, o = np.zeros(1024), np.zeros(1024)
+    ng = env.lib.sb_debug_state(e, g.ctypes.data_as(ctypes.POINTER(ctypes.c_double)), 1024)
+    orc.l.sbo_debug.restype = ctypes.c_int
+    no = orc.l.sbo_debug(orc.h, o.ctypes.data_as(ctypes.c_void_p))
+    if ng != no or ng < 0:
+        return f"pre-stage export sizes {ng} vs {no}"
+    k, nz = orc.k, orc.nz
+    out = []
+    for name, a, b in [("air_g", 0, k), ("air_T", k, 2 * k), ("zone q", 2 * k, 2 * k + nz),
+                       ("scalars", 2 * k + nz, 2 * k + nz + 5)]:
+        d = np.nonzero(g[a:b] != o[a:b])[0]
+        if len(d):
+            out.append(f"{name} differs at {d[:6].tolist()}: {g[a:b][d[:3]].tolist()} vs {o[a:b][d[:3]].tolist()}")
+    return "pre-stage: " + ("; ".join(out) if out else "identical")
 
 
 def _scenario_paths(env, blob_dir):
