@@ -144,6 +144,13 @@ int sb_get_mass(int env, double* out, int n_solved);
 int sb_get_reward_f64(double* reward, double* parts);
 /* Number of hot-path kernel launches one puf_step enqueues. */
 int sb_kernels_per_step(void);
+/* Measurement: runs one step with CUDA events around each kernel on the bound
+ * stream (not for graph capture). ms[4] = {k_rng, k_pre, k_solve, k_post}. */
+int sb_step_timed(float* ms);
+/* Algorithmic bytes one solve launch must move for the loaded batch: per env the
+ * field and interior mass read and written plus the per-zone heat and air-side
+ * vectors; per solver group the factor and coupling tables once. */
+int sb_solve_bytes(double* per_launch);
 /* Inspection: one env's last pre-stage results, out = [air conductance k][supply
  * air temperature k][applied heat per zone cell nz][flow factor sum, reheat W,
  * boiler temperature, boiler return, pump head]. Returns the count or -1. */

@@ -38,7 +38,7 @@ ENV_SYMBOLS = ["sb_dict_new", "sb_dict_free", "dict_find", "dict_set", "dict_set
                "puf_bind_stream", "puf_init", "puf_reset", "puf_step", "puf_render", "puf_close", "puf_log",
                "puf_live_log", "puf_mask_init", "sb_last_error", "sb_device_status", "sb_shape",
                "sb_env_info", "sb_get_temp", "sb_get_mass", "sb_get_reward_f64", "sb_kernels_per_step",
-               "sb_solve_schedule", "sb_debug_state"]
+               "sb_solve_schedule", "sb_debug_state", "sb_step_timed", "sb_solve_bytes"]
 GEN_SYMBOLS = ["sbgen_preset", "sbgen_write", "sbgen_factor_stats"]
 
 
@@ -114,6 +114,8 @@ def env_lib() -> ctypes.CDLL:
         lib.sb_get_mass.argtypes = [ctypes.c_int, dp, ctypes.c_int]
         lib.sb_get_reward_f64.argtypes = [dp, dp]
         lib.sb_debug_state.argtypes = [ctypes.c_int, dp, ctypes.c_int]
+        lib.sb_step_timed.argtypes = [ctypes.POINTER(ctypes.c_float)]
+        lib.sb_solve_bytes.argtypes = [dp]
         lib._sb_typed = True
     return lib
 
@@ -298,6 +300,19 @@ class SmartBuildingsVec:
 
     def status(self) -> int:
         return int(self.lib.sb_device_status())
+
+    def step_timed(self) -> dict:
+        """One step with CUDA events around each kernel (diagnostic; not capturable)."""
+        ms = (ctypes.c_float * 4)()
+        if self.lib.sb_step_timed(ms) != 0:
+            raise RuntimeError("sb_step_timed failed")
+        return dict(zip(["k_rng", "k_pre", "k_solve", "k_post"], list(ms)))
+
+    def solve_bytes(self) -> float:
+        b = ctypes.c_double()
+        if self.lib.sb_solve_bytes(ctypes.byref(b)) != 0:
+            raise RuntimeError("sb_solve_bytes failed")
+        return b.value
 
     def _check(self) -> None:
         err = self.lib.sb_last_error().decode()

@@ -742,6 +742,56 @@ int sb_get_reward_f64(double* reward, double* parts) {
 
 int sb_kernels_per_step(void) { return 4; }
 
+int sb_step_timed(float* ms) {
+    if (!g_eng || !g_eng->ready || !ms) return -1;
+    Engine& E = *g_eng;
+    cudaEvent_t ev[6];
+    for (auto& e : ev)
+        if (cudaEventCreate(&e) != cudaSuccess) return -1;
+    // k_rng timed on its own stream; the main-stream kernels one after another
+    cudaEventRecord(E.ev_fork, E.stream);
+    cudaStreamWaitEvent(E.side, E.ev_fork, 0);
+    cudaEventRecord(ev[4], E.side);
+    k_rng<<<(unsigned)E.sd.size(), 32, E.smem_rng, E.side>>>(E.d_ctx, E.d_scn_step, E.d_rng_out, 0);
+    cudaEventRecord(ev[5], E.side);
+    cudaEventRecord(E.ev_join, E.side);
+    cudaEventRecord(ev[0], E.stream);
+    k_pre<<<(unsigned)E.n_env, 128, E.smem_pre, E.stream>>>(E.d_ctx);
+    cudaEventRecord(ev[1], E.stream);
+    k_solve<<<(unsigned)E.slabs.size(), kSolveThreads, E.smem_solve, E.stream>>>(E.d_ctx, E.d_slabs);
+    cudaEventRecord(ev[2], E.stream);
+    cudaStreamWaitEvent(E.stream, E.ev_join, 0);
+    k_post<<<(unsigned)E.n_env, 128, E.smem_post, E.stream>>>(E.d_ctx);
+    cudaEventRecord(ev[3], E.stream);
+    const bool ok = cudaEventSynchronize(ev[3]) == cudaSuccess && cudaEventSynchronize(ev[5]) == cudaSuccess;
+    if (ok) {
+        cudaEventElapsedTime(&ms[0], ev[4], ev[5]);   // k_rng
+        cudaEventElapsedTime(&ms[1], ev[0], ev[1]);   // k_pre
+        cudaEventElapsedTime(&ms[2], ev[1], ev[2]);   // k_solve
+        cudaEventElapsedTime(&ms[3], ev[2], ev[3]);   // k_post (includes any wait on k_rng)
+    }
+    for (auto& e : ev) cudaEventDestroy(e);
+    return ok ? 0 : -1;
+}
+
+int sb_solve_bytes(double* per_launch) {
+    // Algorithmic bytes of one solve launch: per env, read+write of the field
+    // and the interior mass, the per-zone heat and air-side vectors, plus the
+    // factor / coupling tables shared by the envs of its group.
+    if (!g_eng || !per_launch) return -1;
+    Engine& E = *g_eng;
+    double total = 0.0;
+    for (size_t c = 0; c < E.gd.size(); c++) {
+        const HostGroup& h = E.hg[c];
+        const double per_env = 8.0 * (2.0 * h.ncv + 2.0 * h.n) + 8.0 * (h.nz + 3.0 * h.k);
+        const double shared = 12.0 * (double)(h.nnzL + h.nnzU) + 12.0 * (double)(h.ap_x.size() + h.sn_x.size()) +
+                              8.0 * (double)h.k * h.k;
+        total += per_env * E.gd[c].n_env + shared;
+    }
+    *per_launch = total;
+    return 0;
+}
+
 int sb_debug_state(int env, double* out, int cap) {
     if (!g_eng || env < 0 || env >= g_eng->n_env) return -1;
     Engine& E = *g_eng;

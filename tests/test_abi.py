@@ -1,0 +1,99 @@
+"""The C-ABI libraries load and export every symbol their headers declare; the
+host-only parts of the ABI (dictionary, error reporting) work without a GPU."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _declared(header: Path) -> list[str]:
+    text = re.sub(r"/\*.*?\*/", "", header.read_text(), flags=re.S)
+    names = re.findall(r"^[A-Za-z_][\w\s\*]*?\b(\w+)\s*\([^;{]*\)\s*;", text, flags=re.M)
+    return sorted(set(n for n in names if n not in ("if", "for", "while")))
+
+
+def test_env_library_exports_header(built):
+    import neurips2026_smart_building_challenge_b200 as pkg
+
+    lib = ctypes.CDLL(str(pkg.PKG / "libsbenv.so"))
+    declared = _declared(ROOT / "include" / "sbenv.h")
+    assert "puf_vec_create" in declared and "puf_step" in declared
+    for sym in declared:
+        assert hasattr(lib, sym), sym
+    assert sorted(declared) == sorted(pkg.ENV_SYMBOLS)
+
+
+def test_gen_library_exports_header(built):
+    import neurips2026_smart_building_challenge_b200 as pkg
+
+    lib = ctypes.CDLL(str(pkg.PKG / "libsbgen.so"))
+    declared = _declared(ROOT / "include" / "sbgen.h")
+    assert sorted(declared) == sorted(pkg.GEN_SYMBOLS)
+    for sym in declared:
+        assert hasattr(lib, sym), sym
+
+
+def test_dict_roundtrip(built):
+    import neurips2026_smart_building_challenge_b200 as pkg
+
+    lib = pkg.env_lib()
+    d = lib.sb_dict_new(2)
+    try:
+        for i in range(40):
+            lib.dict_set(d, f"k{i}".encode(), float(i))
+        lib.dict_set_str(d, b"blob", b"/x/y.sbb")
+        lib.dict_set(d, b"k3", 33.0)
+        assert lib.dict_find(d, b"k3").contents.value == 33.0
+        assert lib.dict_find(d, b"blob").contents.str == b"/x/y.sbb"
+        assert not lib.dict_find(d, b"missing")
+        assert pkg._dict_to_py(d)["k39"] == 39.0
+    finally:
+        lib.sb_dict_free(d)
+
+
+def test_puf_log_writes_every_field(built):
+    import neurips2026_smart_building_challenge_b200 as pkg
+
+    lib = pkg.env_lib()
+    log = pkg.Log(*[float(i) for i in range(len(pkg.LOG_FIELDS))])
+    d = lib.sb_dict_new(4)
+    try:
+        lib.puf_log(ctypes.byref(log), d)
+        out = pkg._dict_to_py(d)
+    finally:
+        lib.sb_dict_free(d)
+    assert list(out) == pkg.LOG_FIELDS
+    assert [out[f] for f in pkg.LOG_FIELDS] == [float(i) for i in range(len(pkg.LOG_FIELDS))]
+
+
+def test_create_errors_are_reported(built, tmp_path):
+    """No scenario / a corrupt blob: puf_vec_create returns NULL with a reason (never aborts)."""
+    import neurips2026_smart_building_challenge_b200 as pkg
+
+    lib = pkg.env_lib()
+    buf = (ctypes.c_float * 4096)()
+    p = ctypes.cast(buf, ctypes.c_void_p)
+    d = lib.sb_dict_new(4)
+    try:
+        assert not lib.puf_vec_create(4, d, p, p, p, p)
+        assert b"no scenario" in lib.sb_last_error()
+        bad = tmp_path / "bad.sbb"
+        bad.write_bytes(b"SBB1" + b"\x01\0\0\0" + b"\xff" * 60)
+        lib.dict_set_str(d, b"blob", str(bad).encode())
+        assert not lib.puf_vec_create(4, d, p, p, p, p)
+        assert lib.sb_last_error()
+    finally:
+        lib.sb_dict_free(d)
+
+
+def test_env_requires_gpu_without_fallback(built):
+    torch = pytest.importorskip("torch")
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    import neurips2026_smart_building_challenge_b200 as pkg
+
+    with pytest.raises(RuntimeError):
+        pkg.SmartBuildingsVec(2, blob="/nonexistent.sbb")
