@@ -57,6 +57,16 @@ __device__ __forceinline__ void fence_proxy_async() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Row ready flags of the solve sweeps (shared memory, CTA scope).
+__device__ __forceinline__ uint32_t ld_acquire_u8(const uint8_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.cta.shared::cta.u8 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_u8(uint8_t* p, uint32_t v) {
+    asm volatile("st.release.cta.shared::cta.u8 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ void set_error(int* status, int code) {
     if (status) atomicCAS(status, 0, code);
 }

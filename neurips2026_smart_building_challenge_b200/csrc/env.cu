@@ -216,6 +216,8 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     for (int i = 0; i < G; i++) scnt[i] = n / G + (i < n % G ? 1 : 0);
     const bool merge = kw_num(kw, "merge_weathers", 1.0) != 0.0;
     const int max_steps_kw = (int)kw_num(kw, "max_steps", 0.0);
+    // optional cap on the envs one solve CTA holds (1..8; default: as many as fit)
+    const int slab_cap = std::max(1, std::min(kGroupLanes, (int)kw_num(kw, "slab_envs", (double)kGroupLanes)));
     for (int i = 0; i < G; i++) {
         auto r = std::make_unique<sbb::Reader>();
         std::string e = r->open(paths[i]);
@@ -272,29 +274,30 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
         cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
         smem_cap = (size_t)optin;
     }
-    const size_t solve_fixed = (size_t)kRingSlots * kRingSlotBytes + 256;
     for (int c = 0; c < NG; c++) {
         HostGroup& h = E.hg[c];
         GroupDev& gd = E.gd[c];
         gd.n = h.n; gd.ncv = h.ncv; gd.k = h.k; gd.nz = h.nz;
         gd.sigma_identity = 1;
-        gd.stride = ((h.n + 15) & ~15) + 2;
-        int B = 8;
-        while (B > 1 && (size_t)B * gd.stride * 8 + solve_fixed + 1024 > smem_cap) B /= 2;
-        if ((size_t)B * gd.stride * 8 + solve_fixed + 1024 > smem_cap) {
+        gd.stride = ((h.n + 15) & ~15) + 2;   // >= n + 1: slot n is the zero column of padded terms
+        const size_t solve_fixed = solve_smem_fixed(h.n) + 512;   // + the kernel's static shared memory
+        int B = slab_cap;
+        while (B > 1 && (size_t)B * gd.stride * 8 + solve_fixed > smem_cap) B--;
+        if ((size_t)B * gd.stride * 8 + solve_fixed > smem_cap) {
             set_err("group %d: one env's field (%d cells) exceeds shared memory", c, h.n);
             return false;
         }
         gd.slab_envs = B;
-        E.smem_solve = std::max(E.smem_solve, (size_t)B * gd.stride * 8 + solve_fixed);
+        E.smem_solve = std::max(E.smem_solve, (size_t)B * gd.stride * 8 + solve_smem_fixed(h.n));
         gd.cap = E.arena.upload(h.cap, ok); gd.dirx = E.arena.upload(h.dirx, ok);
         gd.mc = E.arena.upload(h.mc, ok); gd.ret = E.arena.upload(h.ret, ok); gd.gain = E.arena.upload(h.gain, ok);
         gd.zone_of_row = E.arena.upload(h.zone_of_row, ok);
         auto put_sweep = [&](const HostSweep& hsw, Sweep& s) {
             s.stream = E.arena.upload(hsw.bytes, ok);
-            s.nchunks = (uint32_t)hsw.chunk_bytes.size();
-            for (int q = 0; q < kRingSlots; q++)
-                s.first_bytes[q] = q < (int)hsw.chunk_bytes.size() ? hsw.chunk_bytes[q] : 0;
+            for (int w = 0; w < kSweepWarps; w++) {
+                s.warp_off[w] = hsw.warp_off[w];
+                s.warp_stages[w] = hsw.warp_stages[w];
+            }
         };
         put_sweep(h.fwd, gd.fwd);
         put_sweep(h.bwd, gd.bwd);
@@ -813,18 +816,36 @@ int sb_debug_state(int env, double* out, int cap) {
     return o;
 }
 
-int sb_solve_schedule(const char* blob_path, int sweep, uint8_t* out, size_t cap, size_t* used, uint32_t* nchunks) {
+static std::string schedule_of(const char* blob_path, int sweep, HostGroup& g) {
     sbb::Reader r;
     std::string e = r.open(blob_path ? blob_path : "");
-    if (!e.empty()) { set_err("%s", e.c_str()); return -1; }
+    if (e.empty()) e = build_group(r, g);
+    if (e.empty() && sweep != 0 && sweep != 1) e = "sweep must be 0 (L) or 1 (U)";
+    return e;
+}
+
+int sb_solve_schedule(const char* blob_path, int sweep, uint8_t* out, size_t cap, size_t* used,
+                      uint32_t* warp_stages) {
     HostGroup g;
-    e = build_group(r, g);
+    const std::string e = schedule_of(blob_path, sweep, g);
     if (!e.empty()) { set_err("%s", e.c_str()); return -1; }
     const HostSweep& s = sweep == 0 ? g.fwd : g.bwd;
     if (used) *used = s.bytes.size();
-    if (nchunks) *nchunks = (uint32_t)s.chunk_bytes.size();
+    if (warp_stages)
+        for (int w = 0; w < kSweepWarps; w++) warp_stages[w] = s.warp_stages[w];
     if (!out || cap < s.bytes.size()) return 1;
     memcpy(out, s.bytes.data(), s.bytes.size());
+    return 0;
+}
+
+int sb_sweep_stats(const char* blob_path, int sweep, double* out) {
+    HostGroup g;
+    const std::string e = schedule_of(blob_path, sweep, g);
+    if (!e.empty() || !out) { set_err("%s", e.empty() ? "null output" : e.c_str()); return -1; }
+    const HostSweep& s = sweep == 0 ? g.fwd : g.bwd;
+    const double v[8] = {(double)s.terms,    (double)s.bundles,   (double)s.blocks, (double)s.pieces,
+                         (double)s.prewaits, (double)s.publishes, s.sim_cycles,     (double)s.bytes.size()};
+    for (int i = 0; i < 8; i++) out[i] = v[i];
     return 0;
 }
 

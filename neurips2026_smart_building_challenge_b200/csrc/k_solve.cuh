@@ -7,8 +7,10 @@
 // below/above it; here every row pulls its terms in the same column order, so
 // each row receives exactly the same sequence of subtractions and the result
 // is bit-identical. The pull schedule is precomputed on the host
-// (tables.cpp): phases of a level schedule, each phase a list of (row, run of
-// terms) tasks, streamed into a shared-memory ring with cp.async.bulk.
+// (sweep_sched.cpp): every warp runs its own stream of bundles (four rows in
+// lock step, one lane per env), streamed into a per-warp shared-memory ring
+// with cp.async.bulk; before a bundle, the warp acquires the ready flags of
+// the other warps' rows it reads.
 #pragma once
 #include "dev_util.cuh"
 
@@ -21,93 +23,180 @@ struct SlabDesc {
     int pad;
 };
 
+constexpr uint32_t kSpinLimit = 1u << 22;
+
 struct SolveShared {
-    double* X;          // [B][stride]
-    uint8_t* ring;      // kRingSlots x kRingSlotBytes
-    uint64_t* bar;      // kRingSlots
-    int* flag;          // [0]: error seen in this CTA
-    uint32_t chunk_seq; // chunks consumed by this CTA so far (mbarrier parity)
+    double* X;            // [B][stride]
+    uint8_t* ring;        // [kSweepWarps][kRingBytes]
+    uint64_t* bar;        // [kSweepWarps][kStages]
+    uint8_t* ready;       // [n + 1] row ready flags (epoch of the sweep that finished the row)
+    volatile int* abort;  // first error of this CTA
 };
 
-// One sweep over the schedule stream. All threads of the CTA participate.
-__device__ inline void run_sweep(SolveShared& sh, const Sweep& sw, int B, int S, int nenv, int n,
-                                 int* status) {
-    const int tid = threadIdx.x;
-    const int grp = tid / B, lane_env = tid % B;
-    const int ngrp = blockDim.x / B;
-    const uint32_t nch = sw.nchunks;
-    uint32_t issue_off = 0;   // producer: byte offset of the next chunk to issue
-    if (tid == 0) {
+// Shared-memory bytes of a solve CTA besides the slab's field vectors.
+__host__ __device__ constexpr size_t solve_smem_fixed(int n) {
+    return (size_t)kSweepWarps * kRingBytes + (size_t)kSweepWarps * kStages * 8 + (((size_t)n + 1 + 15) & ~(size_t)15) +
+           256;
+}
+
+// One triangular sweep. Every warp runs its own bundle stream; all threads of
+// the CTA must call it. par: per-warp parity bits of the ring's mbarriers.
+__device__ inline void run_sweep(const SolveShared& sh, const Sweep& sw, int B, int S, int n, uint32_t epoch,
+                                 uint32_t& par) {
+    const unsigned full = 0xffffffffu;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int g = lane >> 3, e = lane & 7;
+    const uint8_t* src = sw.stream + (size_t)sw.warp_off[w] * kStageBytes;
+    const uint32_t nst = sw.warp_stages[w];
+    uint8_t* ring = sh.ring + (size_t)w * kRingBytes;
+    uint64_t* bar = sh.bar + w * kStages;
+    // lanes of envs beyond the slab's capacity read env 0's field and never
+    // store, so they touch no memory outside the field
+    const bool owns = e < B;
+    double* xe = sh.X + (size_t)(owns ? e : 0) * S;
+
+    uint32_t issued = nst < (uint32_t)kStages ? nst : (uint32_t)kStages;
+    uint32_t waited = 0, released = 0, p = 0, ro = 0;
+    if (lane == 0) {
         fence_proxy_async();
-        for (uint32_t c = 0; c < nch && c < (uint32_t)kRingSlots; c++) {
-            const uint32_t seq = sh.chunk_seq + c;
-            const int slot = seq % kRingSlots;
-            const uint32_t bytes = sw.first_bytes[c];
-            mbar_expect_tx(&sh.bar[slot], bytes);
-            bulk_g2s(sh.ring + (size_t)slot * kRingSlotBytes, sw.stream + issue_off, bytes, &sh.bar[slot]);
-            issue_off += bytes;
+        for (uint32_t k = 0; k < issued; k++) {
+            mbar_expect_tx(&bar[k], kStageBytes);
+            bulk_g2s(ring + k * kStageBytes, src + (size_t)k * kStageBytes, kStageBytes, &bar[k]);
         }
     }
-    for (uint32_t c = 0; c < nch; c++) {
-        const uint32_t seq = sh.chunk_seq + c;
-        const int slot = seq % kRingSlots;
-        const uint32_t parity = (seq / kRingSlots) & 1u;
-        if (!mbar_wait_bounded(&sh.bar[slot], parity)) sh.flag[0] = kErrRingTimeout;
-        const uint8_t* base = sh.ring + (size_t)slot * kRingSlotBytes;
-        const ChunkHeader hdr = *reinterpret_cast<const ChunkHeader*>(base);
-        const bool ok = hdr.check == (hdr.ntask ^ (hdr.nval << 12) ^ 0x5B5B0000u) &&
-                        16u + 10u * hdr.nval + 8u * hdr.ntask <= (uint32_t)kRingSlotBytes;
-        if (!ok) sh.flag[0] = kErrBadChunk;
-        if (ok && sh.flag[0] == 0) {
-            const TaskRec* tasks = reinterpret_cast<const TaskRec*>(base + 16);
-            const double* vals = reinterpret_cast<const double*>(base + 16 + 8 * hdr.ntask);
-            const uint16_t* cols = reinterpret_cast<const uint16_t*>(vals + hdr.nval);
-            double* xe = sh.X + (size_t)lane_env * S;
-            for (uint32_t t = grp; t < hdr.ntask; t += ngrp) {
-                const TaskRec r = tasks[t];
-                const int nterm = (int)r.nterm_lo | ((int)(r.flags_hi & 0x0F) << 8);
-                const uint32_t need = r.off + (uint32_t)nterm + ((r.flags_hi & 0x80) ? 1u : 0u);
-                if (lane_env >= nenv || r.row >= n || need > hdr.nval) continue;
-                double acc = xe[r.row];
-                const double* v = vals + r.off;
-                const uint16_t* cc = cols + r.off;
-                int q = 0;
-                for (; q + 4 <= nterm; q += 4) {
-                    const double p0 = dmul(v[q], xe[cc[q]]);
-                    const double p1 = dmul(v[q + 1], xe[cc[q + 1]]);
-                    const double p2 = dmul(v[q + 2], xe[cc[q + 2]]);
-                    const double p3 = dmul(v[q + 3], xe[cc[q + 3]]);
-                    acc = dsub(acc, p0);
-                    acc = dsub(acc, p1);
-                    acc = dsub(acc, p2);
-                    acc = dsub(acc, p3);
+    bool ok = true;
+    // wait until the stream's bytes [0, end) are in the ring
+    auto ensure = [&](uint32_t end) {
+        while (end > waited * kStageBytes) {
+            if (waited >= issued) { ok = false; break; }
+            const uint32_t slot = waited % kStages;
+            const uint32_t parity = ((par >> slot) & 1u) ^ ((waited / kStages) & 1u);
+            if (!mbar_wait_bounded(&bar[slot], parity)) { ok = false; break; }
+            waited++;
+        }
+    };
+    // refill the slots of stages the warp has read completely; only stages
+    // whose arrival was observed (a slot's mbarrier must not run two phases
+    // ahead of its waiter, or the parity wait would never succeed)
+    auto release = [&]() {
+        const uint32_t upto = min(p / kStageBytes, waited);
+        while (released < upto) {
+            const uint32_t k = released + kStages;
+            if (k < nst) {
+                __syncwarp();
+                if (lane == 0) {
+                    const uint32_t slot = k % kStages;
+                    fence_proxy_async();
+                    mbar_expect_tx(&bar[slot], kStageBytes);
+                    bulk_g2s(ring + slot * kStageBytes, src + (size_t)k * kStageBytes, kStageBytes, &bar[slot]);
                 }
-                for (; q < nterm; q++) acc = dsub(acc, dmul(v[q], xe[cc[q]]));
-                if (r.flags_hi & 0x80) acc = ddiv(acc, v[nterm]);
-                xe[r.row] = acc;
+                issued = k + 1;
+            }
+            released++;
+        }
+    };
+
+    for (;;) {
+        int ab = 0;
+        if (lane == 0) ab = *sh.abort;
+        ab = __shfl_sync(full, ab, 0);
+        ensure(p + sizeof(BundleHeader));
+        if (!__all_sync(full, ok) || ab) break;
+        const uint8_t* base = ring + ro;
+        const uint4 hv = *reinterpret_cast<const uint4*>(base);
+        const uint32_t flags = hv.z >> 16, nblk = hv.z & 0xFFFFu;
+        if (flags & kBundleEnd) break;
+        if (flags & kBundleSkip) {   // the next bundle starts at the ring's beginning
+            p += kRingBytes - ro;
+            ro = 0;
+            ensure(p);   // observe the skipped stages before their slots are refilled
+            release();
+            continue;
+        }
+        const uint32_t row = ((g < 2 ? hv.x : hv.y) >> (16 * (g & 1))) & 0xFFFFu;
+        const uint32_t fin = (hv.w >> (8 * g)) & 0xFFu;
+        const uint32_t npre = (flags >> 8) & 0xFu;
+        const uint32_t bsz = (uint32_t)bundle_bytes((int)npre, (flags & 0xF0u) != 0, (int)nblk);
+        const bool bad = row > (uint32_t)n || (fin != kFinNever && fin > nblk) || (flags & 0x3000u) ||
+                         npre > (uint32_t)kMaxPreItems || bsz > (uint32_t)kMaxBundleBytes ||
+                         ro + bsz > (uint32_t)kRingBytes;
+        if (__any_sync(full, bad)) { atomicCAS((int*)sh.abort, 0, kErrBadBundle); ok = false; break; }
+        ensure(p + bsz);
+        if (!__all_sync(full, ok)) break;
+        // pre-waits: eight rows per item, one per lane; the warp barrier after
+        // them orders every lane's later reads after all the acquires
+        if (lane < 8 * (int)npre) {
+            const uint32_t r = reinterpret_cast<const uint16_t*>(base + 16)[lane];
+            if (r > (uint32_t)n) {
+                atomicCAS((int*)sh.abort, 0, kErrBadBundle);
+                ok = false;
+            } else {
+                uint32_t spins = 0;
+                while (ld_acquire_u8(sh.ready + r) < epoch) {
+                    if (++spins >= kSpinLimit) {
+                        atomicCAS((int*)sh.abort, 0, kErrWaitTimeout);
+                        ok = false;
+                        break;
+                    }
+                    if ((spins & 1023u) == 0 && *sh.abort) { ok = false; break; }
+                }
             }
         }
-        const uint32_t next_bytes = hdr.next_bytes;
-        __syncthreads();
-        if (sh.flag[0] != 0) {
-            // error: drain the copies still in flight (bounded), then leave the sweep
-            if (tid == 0)
-                for (uint32_t d = c + 1; d < nch && d < c + kRingSlots; d++) {
-                    const uint32_t sq = sh.chunk_seq + d;
-                    mbar_wait_bounded(&sh.bar[sq % kRingSlots], (sq / kRingSlots) & 1u);
+        __syncwarp();
+        if (!__all_sync(full, ok)) break;
+        uint32_t off = 16 + 16 * npre;
+        const bool pub = (flags >> g) & 1u, div = (flags >> (4 + g)) & 1u;
+        double d = 1.0;
+        if (flags & 0xF0u) {
+            d = reinterpret_cast<const double*>(base + off)[g];
+            off += 32;
+        }
+        double acc = xe[row];
+        bool final_written = false;
+        auto finish = [&]() {
+            if (div) acc = ddiv(acc, d);
+            if (owns) xe[row] = acc;
+            final_written = true;
+            if (pub) {
+                __syncwarp(0xFFu << (8 * g));
+                if (e == 0) {
+                    __threadfence_block();
+                    st_release_u8(sh.ready + row, epoch);
                 }
-            __syncthreads();
-            break;
+            }
+        };
+        if (fin == 0) finish();
+        const uint8_t* bp = base + off;
+        for (uint32_t b = 0; b < nblk; b++, bp += kTermBlockBytes) {
+            const double2 v01 = *reinterpret_cast<const double2*>(bp + 32 * g);
+            const double2 v23 = *reinterpret_cast<const double2*>(bp + 32 * g + 16);
+            const uint2 cc = *reinterpret_cast<const uint2*>(bp + 128 + 8 * g);
+            const double x0 = xe[cc.x & 0xFFFFu], x1 = xe[cc.x >> 16];
+            const double x2 = xe[cc.y & 0xFFFFu], x3 = xe[cc.y >> 16];
+            acc = dsub(acc, dmul(v01.x, x0));
+            acc = dsub(acc, dmul(v01.y, x1));
+            acc = dsub(acc, dmul(v23.x, x2));
+            acc = dsub(acc, dmul(v23.y, x3));
+            if (fin == b + 1) finish();
         }
-        if (tid == 0 && c + kRingSlots < nch) {
-            fence_proxy_async();
-            mbar_expect_tx(&sh.bar[slot], next_bytes);
-            bulk_g2s(sh.ring + (size_t)slot * kRingSlotBytes, sw.stream + issue_off, next_bytes, &sh.bar[slot]);
-            issue_off += next_bytes;
-        }
+        if (!final_written && owns) xe[row] = acc;
+        __syncwarp();
+        p += bsz;
+        ro += bsz;
+        if (ro == (uint32_t)kRingBytes) ro = 0;
+        release();
     }
-    sh.chunk_seq += nch;
-    if (tid == 0 && sh.flag[0] != 0) set_error(status, sh.flag[0]);
+    if (!ok) atomicCAS((int*)sh.abort, 0, kErrRingTimeout);
+    // every issued stage completes before the ring is reused
+    for (; waited < issued; waited++) {
+        const uint32_t slot = waited % kStages;
+        mbar_wait_bounded(&bar[slot], ((par >> slot) & 1u) ^ ((waited / kStages) & 1u));
+    }
+    for (uint32_t s = 0; s < (uint32_t)kStages; s++) {
+        const uint32_t used = issued > s ? (issued - s + kStages - 1) / kStages : 0;
+        par ^= (used & 1u) << s;
+    }
+    __syncwarp();
 }
 
 // Dense k x k system M q = b per env with partial pivoting, the reference's
@@ -217,16 +306,24 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
     const int nenv = sd.nenv;
     const int tid = threadIdx.x;
 
+    // shared memory: field [B][S] | rings | mbarriers | ready flags | misc
     SolveShared sh;
     sh.X = reinterpret_cast<double*>(smem);
     sh.ring = smem + (size_t)B * S * sizeof(double);
-    sh.bar = reinterpret_cast<uint64_t*>(sh.ring + (size_t)kRingSlots * kRingSlotBytes);
-    sh.flag = reinterpret_cast<int*>(sh.bar + kRingSlots);
-    double* amb_e = reinterpret_cast<double*>(sh.flag + 4);   // [B]
-    int* active = reinterpret_cast<int*>(amb_e + 8);           // [B]
-    sh.chunk_seq = 0;
-    if (tid < kRingSlots) mbar_init(&sh.bar[tid], 1);
-    if (tid == 0) sh.flag[0] = 0;
+    sh.bar = reinterpret_cast<uint64_t*>(sh.ring + (size_t)kSweepWarps * kRingBytes);
+    sh.ready = reinterpret_cast<uint8_t*>(sh.bar + kSweepWarps * kStages);
+    int* misc = reinterpret_cast<int*>(sh.ready + ((n + 1 + 15) & ~15));
+    sh.abort = misc;
+    double* amb_e = reinterpret_cast<double*>(misc + 4);   // [8]
+    int* active = reinterpret_cast<int*>(amb_e + 8);        // [8]
+    if (tid < kSweepWarps * kStages) mbar_init(&sh.bar[tid], 1);
+    if (tid == 0) misc[0] = 0;
+    for (int i = tid; i <= n; i += blockDim.x) sh.ready[i] = i < n ? 0 : 0xFF;   // slot n: "no row"
+    // padding slots (the zero column of padded terms) and envs the slab does not fill
+    for (int e = 0; e < B; e++) {
+        const int from = e < nenv ? n : 0;
+        for (int i = from + tid; i < S; i += blockDim.x) sh.X[(size_t)e * S + i] = 0.0;
+    }
     if (tid < nenv) {
         const int env = sd.env0 + tid;
         const ScnDev& sc = ctx->scns[ctx->envs[env].scn];
@@ -242,6 +339,7 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
     }
     mbar_fence_init();
     __syncthreads();
+    uint32_t par = 0;   // ring mbarrier parities of this thread's warp
 
     // ---- forcing (sb_fdm.c:146-152), written in row order ----
     for (int idx = tid; idx < nenv * n; idx += blockDim.x) {
@@ -260,8 +358,14 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
     __syncthreads();
 
     // ---- first solve ----
-    run_sweep(sh, g.fwd, B, S, nenv, n, ctx->status);
-    run_sweep(sh, g.bwd, B, S, nenv, n, ctx->status);
+    run_sweep(sh, g.fwd, B, S, n, 1, par);
+    __syncthreads();
+    run_sweep(sh, g.bwd, B, S, n, 2, par);
+    __syncthreads();
+    if (*sh.abort) {   // uniform: read after the barrier
+        if (tid == 0) set_error(ctx->status, *sh.abort);
+        return;
+    }
 
     // ---- air side (sb_fdm.c:155-181) ----
     double* pw = reinterpret_cast<double*>(sh.ring);   // [B][k], ring is idle between sweeps
@@ -316,11 +420,13 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
             }
             __syncthreads();
         }
-        // r = applied q, pulled per row in ascending column order; zero q skipped
-        for (int idx = tid; idx < nenv * n; idx += blockDim.x) {
-            const int e = idx / n, i = idx % n;
+        // r = applied q, pulled per row in ascending column order; zero q skipped.
+        // The dense workspace overlapped the field: padding slots and unused
+        // envs are zeroed again (padded sweep terms read the zero slot).
+        for (int idx = tid; idx < B * S; idx += blockDim.x) {
+            const int e = idx / S, i = idx % S;
             double acc = 0.0;
-            if (active[e]) {
+            if (e < nenv && i < n && active[e]) {
                 for (int p = g.ap_rp[i]; p < g.ap_rp[i + 1]; p++) {
                     const double qj = pw[e * k + g.ap_col[p]];
                     if (qj == 0.0) continue;
@@ -330,8 +436,14 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
             sh.X[(size_t)e * S + i] = acc;
         }
         __syncthreads();
-        run_sweep(sh, g.fwd, B, S, nenv, n, ctx->status);
-        run_sweep(sh, g.bwd, B, S, nenv, n, ctx->status);
+        run_sweep(sh, g.fwd, B, S, n, 3, par);
+        __syncthreads();
+        run_sweep(sh, g.bwd, B, S, n, 4, par);
+        __syncthreads();
+        if (*sh.abort) {
+            if (tid == 0) set_error(ctx->status, *sh.abort);
+            return;
+        }
     }
 
     // ---- interior mass + field (sb_fdm.c:183-187) ----

@@ -1,5 +1,5 @@
 // Device-side table and state descriptors shared by the host builder
-// (tables.cpp, env.cu) and the kernels (kernels.cuh).
+// (tables.cpp, sweep_sched.cpp, env.cu) and the kernels (k_*.cuh).
 //
 // Terminology (the reference's domain):
 //   scenario  one SBB1 blob = one building x one weather/calendar;
@@ -13,6 +13,12 @@
 #pragma once
 #include <cstdint>
 
+#ifdef __CUDACC__
+#define SB_HD __host__ __device__
+#else
+#define SB_HD
+#endif
+
 namespace sbenv {
 
 constexpr int kObs = 1024;             // OBS_SIZE (complete_port/gpu/smart_buildings.cu:33)
@@ -21,8 +27,6 @@ constexpr int kDisc = 16;              // SB_DISC
 constexpr int kAct = kCont + kDisc;    // NUM_ATNS
 constexpr int kMaskWidth = kCont + 2 * kDisc;
 constexpr int kParts = 8;              // per-step log terms (smart_buildings.cu:101-115)
-constexpr int kRingSlots = 6;          // solve schedule ring depth
-constexpr int kRingSlotBytes = 4096;   // one schedule chunk at most
 constexpr int kSolveThreads = 512;
 constexpr int kMaxK = 128;             // coupled VAVs (dense air-side system in shared memory)
 constexpr int kMaxAhu = 16;
@@ -31,33 +35,66 @@ constexpr int kMaxConvRoom = 8192;     // cells of one convection room
 // Error codes written to the device status word (first error wins).
 enum : int {
     kErrNone = 0,
-    kErrRingTimeout = 1,   // a schedule chunk never arrived (bounded mbarrier wait)
-    kErrBadChunk = 2,      // a schedule chunk header failed its consistency check
+    kErrRingTimeout = 1,   // a schedule stage never arrived (bounded mbarrier wait)
+    kErrBadChunk = 2,      // reserved
     kErrConvOverflow = 3,  // convection swap list exceeded its buffer
-    kErrDenseSingular = 4  // reserved: the reference tolerates a zero pivot, so do we
+    kErrDenseSingular = 4, // reserved: the reference tolerates a zero pivot, so do we
+    kErrWaitTimeout = 5,   // a row's ready flag never arrived (bounded spin)
+    kErrBadBundle = 6      // a sweep bundle header failed its consistency check
 };
 
-// One solve-schedule chunk in global memory, 16-byte aligned:
-//   ChunkHeader | TaskRec[ntask] | double val[nval] | uint16_t col[nval] | pad
-struct ChunkHeader {
-    uint32_t ntask;
-    uint32_t nval;
-    uint32_t next_bytes;  // byte size of the chunk kRingSlots positions later (0 past the end)
-    uint32_t check;       // ntask ^ (nval << 12) ^ 0x5B5B0000, validated on the device
-};
-// row: row position; nterm: terms applied in this phase; flags bit0: the task
-// finalises a backward-sweep row (divide by the diagonal stored in val[off+nterm]).
-struct TaskRec {
-    uint16_t row;
-    uint8_t nterm_lo;
-    uint8_t flags_hi;   // bits 0-3: nterm high nibble (nterm < 4096); bit 7: finalise
-    uint32_t off;       // first term in this chunk's val/col arrays
-};
+// Solve schedule ("sweep program"), built on the host (sweep_sched.cpp).
+//
+// Each of the kSweepWarps warps of a solve CTA runs its own stream of bundles.
+// A bundle advances up to kBundleRows rows of the triangular factor in lock
+// step: lane group g (kGroupLanes lanes, one per env of the slab) owns row g.
+// Every term subtracts val * x[col] from the row's accumulator, in the order
+// the reference's column push would deliver it (bit-exact). Before a bundle
+// starts, the warp waits (acquire) for the ready flags of the rows listed in
+// it; the host lists rows whose completion implies every column the bundle
+// reads that this warp has not produced or waited for itself. A row that
+// another warp reads is published with a release store of the sweep's epoch.
+//
+// Stream layout (16-byte items; a bundle never wraps around the warp's ring):
+//   BundleHeader (16 B)
+//   npre x u16 row[8] (16 B each): rows to wait for (entry n = no row; its
+//        flag is always set)
+//   [double diag[4]] (32 B) when any divide bit is set (backward sweep)
+//   nblk x TermBlock (160 B): double val[4 groups][4 steps], u16 col[4][4]
+//   ... next bundle ...
+// A header with kBundleSkip continues the stream at the start of the ring; a
+// header with kBundleEnd ends it. Streams are padded to whole stages.
+constexpr int kSweepWarps = kSolveThreads / 32;
+constexpr int kGroupLanes = 8;           // envs per lane group (slab_envs <= 8)
+constexpr int kBundleRows = 4;           // lane groups per warp
+constexpr int kTermSteps = 4;            // terms per group per TermBlock
+constexpr int kTermBlockBytes = kBundleRows * kTermSteps * 10;   // 160
+constexpr int kStageBytes = 480;         // one bulk copy into a warp's ring
+constexpr int kStages = 4;               // ring depth per warp
+constexpr int kRingBytes = kStageBytes * kStages;
+constexpr int kMaxBundleBytes = 2 * kStageBytes;   // a bundle spans at most 3 stages
+constexpr int kMaxPreItems = 2;          // pre-wait items per bundle (8 rows each)
+constexpr uint16_t kBundleEnd = 0x8000;  // BundleHeader.flags: end of stream
+constexpr uint16_t kBundleSkip = 0x4000; // BundleHeader.flags: continue at ring offset 0
+constexpr uint8_t kFinNever = 0xFF;      // BundleHeader.fin: row continues in a later bundle
 
+struct BundleHeader {
+    uint16_t row[kBundleRows];   // row of each group; n = the always-zero padding slot
+    uint16_t nblk;               // TermBlocks that follow
+    uint16_t flags;              // bits 0-3 publish row g, 4-7 divide row g, 8-11 npre, 14 skip, 15 end
+    uint8_t fin[kBundleRows];    // row g is final after this many blocks (kFinNever: not here)
+};
+static_assert(sizeof(BundleHeader) == 16, "bundle header is one 16-byte item");
+
+SB_HD constexpr int bundle_bytes(int npre, bool divides, int nblk) {
+    return 16 + 16 * npre + (divides ? 32 : 0) + kTermBlockBytes * nblk;
+}
+
+// One triangular sweep: per-warp byte streams, each a whole number of stages.
 struct Sweep {
-    const uint8_t* stream;  // chunks back to back
-    uint32_t nchunks;
-    uint32_t first_bytes[kRingSlots];
+    const uint8_t* stream;                 // all warps' streams back to back
+    uint32_t warp_off[kSweepWarps];        // stage index where warp w's stream starts
+    uint32_t warp_stages[kSweepWarps];     // stages in warp w's stream
 };
 
 // Geometry + solver tables of one group and the state of its envs.

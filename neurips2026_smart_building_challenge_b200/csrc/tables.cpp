@@ -22,113 +22,6 @@ namespace {
 
 template <class T> std::vector<T> vec(const T* p, uint64_t n) { return p ? std::vector<T>(p, p + n) : std::vector<T>(); }
 
-// Pull form of one triangular sweep. terms[i]: (column, value) in the order the
-// reference's column push delivers them to row i. Rows are finished phase by
-// phase; a term of row i can run once its column's row finished in an earlier
-// phase, and a row's terms always run in order (consecutive terms whose
-// columns are ready in the same phase form one task).
-HostSweep build_sweep(int n, const std::vector<std::vector<std::pair<int, double>>>& terms, bool backward,
-                      const std::vector<double>& diag) {
-    HostSweep sw;
-    struct Task { int row, phase, t0, t1; bool fin; };
-    std::vector<int> fin(n, -1);
-    std::vector<Task> tasks;
-    for (int s = 0; s < n; s++) {
-        const int i = backward ? n - 1 - s : s;
-        const auto& tv = terms[i];
-        int ph = 0, start = 0;
-        if (tv.empty()) {
-            if (backward) { tasks.push_back({i, 0, 0, 0, true}); fin[i] = 0; }
-            continue;
-        }
-        for (int q = 0; q < (int)tv.size(); q++) {
-            const int ready = fin[tv[q].first] + 1;
-            if (ready > ph) {
-                if (q > start) tasks.push_back({i, ph, start, q, false});
-                ph = ready;
-                start = q;
-            }
-        }
-        tasks.push_back({i, ph, start, (int)tv.size(), backward});
-        fin[i] = ph;
-    }
-    int nphase = 0;
-    for (auto& t : tasks) nphase = std::max(nphase, t.phase + 1);
-    sw.phases = nphase;
-    std::vector<std::vector<int>> byphase(nphase);
-    for (int q = 0; q < (int)tasks.size(); q++) byphase[tasks[q].phase].push_back(q);
-    sw.tasks = (int64_t)tasks.size();
-
-    struct Part { int row, t0, t1; bool fin; };
-    std::vector<std::vector<Part>> chunks;
-    const int kMaxBody = kRingSlotBytes - 16;
-    auto part_bytes = [](const Part& p) { return 8 + 10 * (p.t1 - p.t0 + (p.fin ? 1 : 0)); };
-    for (int ph = 0; ph < nphase; ph++) {
-        auto& list = byphase[ph];
-        std::stable_sort(list.begin(), list.end(), [&](int a, int b) {
-            return (tasks[a].t1 - tasks[a].t0) > (tasks[b].t1 - tasks[b].t0);
-        });
-        std::vector<Part> cur;
-        int used = 0;
-        for (int q : list) {
-            const Task& t = tasks[q];
-            Part whole{t.row, t.t0, t.t1, t.fin};
-            if (part_bytes(whole) > kMaxBody) {
-                // a long run: its pieces go to consecutive chunks of this phase
-                if (!cur.empty()) { chunks.push_back(cur); cur.clear(); used = 0; }
-                const int per = (kMaxBody - 8) / 10 - 1;
-                for (int a = t.t0; a < t.t1; a += per) {
-                    const int b = std::min(t.t1, a + per);
-                    chunks.push_back({Part{t.row, a, b, t.fin && b == t.t1}});
-                }
-                continue;
-            }
-            if (used + part_bytes(whole) > kMaxBody) { chunks.push_back(cur); cur.clear(); used = 0; }
-            cur.push_back(whole);
-            used += part_bytes(whole);
-        }
-        if (!cur.empty()) chunks.push_back(cur);
-    }
-    // serialise
-    for (auto& ch : chunks) {
-        uint32_t ntask = (uint32_t)ch.size(), nval = 0;
-        for (auto& p : ch) nval += (uint32_t)(p.t1 - p.t0 + (p.fin ? 1 : 0));
-        uint32_t bytes = 16 + 8 * ntask + 10 * nval;
-        bytes = (bytes + 15) & ~15u;
-        std::vector<uint8_t> buf(bytes, 0);
-        ChunkHeader h{ntask, nval, 0, ntask ^ (nval << 12) ^ 0x5B5B0000u};
-        memcpy(buf.data(), &h, sizeof(h));
-        TaskRec* tr = reinterpret_cast<TaskRec*>(buf.data() + 16);
-        double* val = reinterpret_cast<double*>(buf.data() + 16 + 8 * ntask);
-        uint16_t* col = reinterpret_cast<uint16_t*>(val + nval);
-        uint32_t off = 0;
-        for (uint32_t q = 0; q < ntask; q++) {
-            const Part& p = ch[q];
-            const int nt = p.t1 - p.t0;
-            tr[q].row = (uint16_t)p.row;
-            tr[q].nterm_lo = (uint8_t)(nt & 0xFF);
-            tr[q].flags_hi = (uint8_t)(((nt >> 8) & 0x0F) | (p.fin ? 0x80 : 0));
-            tr[q].off = off;
-            for (int a = p.t0; a < p.t1; a++) {
-                val[off] = terms[p.row][a].second;
-                col[off] = (uint16_t)terms[p.row][a].first;
-                off++;
-            }
-            if (p.fin) { val[off] = diag[p.row]; col[off] = 0; off++; }
-            sw.terms += nt;
-        }
-        sw.chunk_bytes.push_back(bytes);
-        sw.bytes.insert(sw.bytes.end(), buf.begin(), buf.end());
-    }
-    size_t pos = 0;
-    for (size_t c = 0; c < sw.chunk_bytes.size(); c++) {
-        const uint32_t nb = c + kRingSlots < sw.chunk_bytes.size() ? sw.chunk_bytes[c + kRingSlots] : 0;
-        memcpy(&sw.bytes[pos + 8], &nb, 4);
-        pos += sw.chunk_bytes[c];
-    }
-    return sw;
-}
-
 struct Factor {
     int n;
     const int32_t *Lp, *Li, *Up, *Ui, *pr, *pcc;
@@ -324,8 +217,9 @@ std::string build_group(const sbb::Reader& b, HostGroup& g) {
     for (int i = 0; i < n; i++)
         for (size_t a = 0; a < ut[i].size(); a++)
             if (ut[i][a].first == i) return "U has a duplicate diagonal";
-    g.fwd = build_sweep(n, lt, false, udiag);
-    g.bwd = build_sweep(n, ut, true, udiag);
+    std::string se = build_sweep(n, lt, false, udiag, g.fwd);
+    if (se.empty()) se = build_sweep(n, ut, true, udiag, g.bwd);
+    if (!se.empty()) return se;
 
     // air side
     const int64_t* shp = b.i64("sensed_shape");

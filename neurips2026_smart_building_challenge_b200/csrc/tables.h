@@ -6,15 +6,9 @@
 
 #include "sbb.h"
 #include "sbenv_dev.h"
+#include "sweep_sched.h"
 
 namespace sbenv {
-
-struct HostSweep {
-    std::vector<uint8_t> bytes;
-    std::vector<uint32_t> chunk_bytes;
-    int phases = 0;
-    int64_t tasks = 0, terms = 0;
-};
 
 struct HostGroup {
     int n = 0, ncv = 0, k = 0, nz = 0, nv = 0, na = 0;

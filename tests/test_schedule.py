@@ -1,7 +1,10 @@
-"""The device solve schedule (host-built, streamed chunk by chunk into shared
-memory) replayed on the CPU: executing it with the kernel's semantics -- every
-task of a chunk reads the vector as it was when the chunk started -- must give
-bit for bit the reference's column-push replay (complete_port/csim/sb_lu.c:38-63)."""
+"""The solve kernel's sweep programs (built on the host by csrc/sweep_sched.cpp),
+executed on the CPU with the kernel's semantics under several interleavings of
+the 16 warps. Every row must receive exactly the reference's terms in the
+reference's order (the column push of complete_port/csim/sb_lu.c:38-63), no
+bundle may read a row that is not final yet (a bundle starts only when the
+rows it waits for are published), no interleaving may deadlock, and the solve
+must equal the column-push replay bit for bit."""
 import ctypes
 import struct
 
@@ -10,96 +13,171 @@ import pytest
 
 from sbb_read import Blob
 
+NW, STAGE, RING, MAX_BUNDLE = 16, 480, 1920, 960
+END, SKIP, FIN_NEVER = 0x8000, 0x4000, 0xFF
 
-def _schedule(lib, blob, sweep):
+
+def _programs(lib, blob, sweep):
     used = ctypes.c_size_t()
-    nch = ctypes.c_uint32()
+    stages = (ctypes.c_uint32 * NW)()
     lib.sb_solve_schedule.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t,
                                       ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_uint32)]
-    assert lib.sb_solve_schedule(str(blob).encode(), sweep, None, 0, ctypes.byref(used), ctypes.byref(nch)) == 1
+    assert lib.sb_solve_schedule(str(blob).encode(), sweep, None, 0, ctypes.byref(used), stages) == 1
     buf = (ctypes.c_uint8 * used.value)()
-    assert lib.sb_solve_schedule(str(blob).encode(), sweep, buf, used.value, ctypes.byref(used),
-                                 ctypes.byref(nch)) == 0
-    return bytes(buf), nch.value
-
-
-def _chunks(raw, nch):
-    pos, out, sizes = 0, [], []
-    for _ in range(nch):
-        ntask, nval, nxt, check = struct.unpack_from("<4I", raw, pos)
-        assert check == (ntask ^ (nval << 12) ^ 0x5B5B0000) & 0xFFFFFFFF
-        size = (16 + 8 * ntask + 10 * nval + 15) & ~15
-        assert size <= 4096
-        tasks = np.frombuffer(raw, dtype=np.dtype([("row", "<u2"), ("lo", "u1"), ("hi", "u1"), ("off", "<u4")]),
-                              count=ntask, offset=pos + 16)
-        vals = np.frombuffer(raw, dtype="<f8", count=nval, offset=pos + 16 + 8 * ntask)
-        cols = np.frombuffer(raw, dtype="<u2", count=nval, offset=pos + 16 + 8 * ntask + 8 * nval)
-        out.append((tasks, vals, cols, nxt))
-        sizes.append(size)
+    assert lib.sb_solve_schedule(str(blob).encode(), sweep, buf, used.value, ctypes.byref(used), stages) == 0
+    raw, out, pos = bytes(buf), [], 0
+    for w in range(NW):
+        size = stages[w] * STAGE
+        out.append(raw[pos:pos + size])
         pos += size
     assert pos == len(raw)
-    for c, (_, _, _, nxt) in enumerate(out):   # next_bytes = size of the chunk six later
-        assert nxt == (sizes[c + 6] if c + 6 < nch else 0)
     return out
 
 
-def _run(chunks, x, backward, n):
-    x = x.copy()
-    final = np.zeros(n, bool)
+def _parse(stream, n, backward):
+    """Bundles of one warp stream. A bundle never wraps around the 1920-byte
+    ring: a skip header moves the stream to the ring's start (zero bytes)."""
+    pos, bundles = 0, []
+    while True:
+        hdr = stream[pos:pos + 16]
+        assert len(hdr) == 16, "stream ends without an end marker"
+        rows = struct.unpack_from("<4H", hdr)
+        nblk, flags = struct.unpack_from("<HH", hdr, 8)
+        fin = list(hdr[12:16])
+        if flags & END:
+            pos += 16
+            break
+        if flags & SKIP:
+            ro = pos % RING
+            assert not any(stream[pos + 16:pos + RING - ro])
+            pos += RING - ro
+            continue
+        assert flags & 0x3000 == 0
+        assert all(r <= n for r in rows)
+        assert all(f == FIN_NEVER or f <= nblk for f in fin)
+        npre = (flags >> 8) & 0xF
+        size = 16 + 16 * npre + (32 if flags & 0xF0 else 0) + 160 * nblk
+        assert size <= MAX_BUNDLE and pos % RING + size <= RING, "bundle too large or wraps the ring"
+        off = pos + 16
+        pre = list(struct.unpack_from(f"<{8 * npre}H", stream, off)) if npre else []
+        off += 16 * npre
+        diag = [1.0] * 4
+        if flags & 0xF0:
+            diag = list(struct.unpack_from("<4d", stream, off))
+            off += 32
+        assert bool(flags & 0xF0) == (backward and any(f != FIN_NEVER for f in fin))
+        blocks = []
+        for _ in range(nblk):
+            vals = np.frombuffer(stream, "<f8", 16, off).reshape(4, 4)
+            cols = np.frombuffer(stream, "<u2", 16, off + 128).reshape(4, 4)
+            blocks.append((vals, cols))
+            off += 160
+        bundles.append(dict(rows=rows, flags=flags, fin=fin, pre=pre, diag=diag, blocks=blocks))
+        pos = off
+    assert not any(stream[pos:]), "bytes after the end marker"
+    assert len(stream) % STAGE == 0
+    return bundles
+
+
+class _Warp:
+    def __init__(self, bundles):
+        self.bundles, self.bi, self.b, self.acc, self.done = bundles, 0, -1, [0.0] * 4, [False] * 4
+
+    def finished(self):
+        return self.bi >= len(self.bundles)
+
+
+def _execute(programs, x, n, backward, pick, expect):
+    """Runs the warps' bundles block by block in the order pick() chooses."""
+    x = list(x) + [0.0]
+    final = [False] * (n + 1)
+    final[n] = True
     if not backward:
-        final[:] = True   # rows without L terms are final from the start; corrected below
-        has = np.zeros(n, bool)
-        for tasks, _, _, _ in chunks:
-            has[tasks["row"]] = True
-        final[has] = False
-    for tasks, vals, cols, _ in chunks:
-        snap = x.copy()
-        newv = {}
-        rows = [int(r) for r in tasks["row"]]
-        assert len(set(rows)) == len(rows), "a row appears twice in one chunk"
-        for t in tasks:
-            row, nt = int(t["row"]), int(t["lo"]) | ((int(t["hi"]) & 0x0F) << 8)
-            off, fin = int(t["off"]), bool(t["hi"] & 0x80)
-            acc = snap[row]
-            for q in range(nt):
-                c = int(cols[off + q])
-                assert final[c], "a term reads a row that is not final yet"
-                acc = acc - vals[off + q] * snap[c]
-            if fin:
-                acc = acc / vals[off + nt]
-            newv[row] = (acc, fin or not backward)
-        for row, (v, f) in newv.items():
-            x[row] = v
-        # forward rows become final after their last task; track via remaining terms
-        for t in tasks:
-            row = int(t["row"])
-            if backward and (t["hi"] & 0x80):
-                final[row] = True
-        if not backward:
-            for row in newv:
-                final[row] = _fwd_done(row)
-    return x
+        for i in range(n):
+            final[i] = not expect[i]
+    ready = [False] * n + [True]
+    got = [[] for _ in range(n)]
+    warps = [_Warp(_parse(p, n, backward)) for p in programs]
+
+    def finish(wp, B, g):
+        r = B["rows"][g]
+        acc = wp.acc[g]
+        if (B["flags"] >> (4 + g)) & 1:
+            acc = acc / B["diag"][g]
+        x[r], wp.acc[g], wp.done[g] = acc, acc, True
+        final[r] = True
+        if (B["flags"] >> g) & 1:
+            ready[r] = True
+
+    def step(wp):
+        """One unit of warp wp; False if it is blocked."""
+        B = wp.bundles[wp.bi]
+        if wp.b < 0:   # bundle start: pre-waits, accumulators
+            if not all(ready[r] for r in B["pre"]):
+                return False
+            for g in range(4):
+                wp.acc[g], wp.done[g] = x[B["rows"][g]], False
+                if B["fin"][g] == 0:
+                    finish(wp, B, g)
+            wp.b = 0
+        elif wp.b < len(B["blocks"]):
+            vals, cols = B["blocks"][wp.b]
+            for g in range(4):
+                r = B["rows"][g]
+                for s in range(4):
+                    c, v = int(cols[g, s]), float(vals[g, s])
+                    assert final[c], f"row {r} reads row {c} before it is final"
+                    wp.acc[g] = wp.acc[g] - v * x[c]
+                    if c != n:
+                        got[r].append((c, v))
+                    else:
+                        assert v == 0.0
+                if B["fin"][g] == wp.b + 1:
+                    finish(wp, B, g)
+            wp.b += 1
+        else:          # bundle end
+            for g in range(4):
+                if not wp.done[g]:
+                    x[B["rows"][g]] = wp.acc[g]
+            wp.bi, wp.b = wp.bi + 1, -1
+        return True
+
+    while True:
+        live = [w for w in warps if not w.finished()]
+        if not live:
+            break
+        order = pick(live)
+        assert any(step(w) for w in order), "deadlock: every unfinished warp waits"
+    for i in range(n):
+        assert got[i] == expect[i], f"row {i}: terms differ from the reference's push order"
+        assert final[i]
+    return np.array(x[:n])
 
 
-_FWD_LEFT = {}
-
-
-def _fwd_done(row):
-    _FWD_LEFT[row] -= 1
-    return _FWD_LEFT[row] == 0
+def _terms(M, backward):
+    """(column, value) per row in the order the reference's column push delivers them."""
+    Mc = M.tocsc()
+    n = Mc.shape[0]
+    out = [[] for _ in range(n)]
+    cols = range(n - 1, -1, -1) if backward else range(n)
+    for j in cols:
+        for p in range(Mc.indptr[j], Mc.indptr[j + 1]):
+            i = int(Mc.indices[p])
+            if i != j:
+                out[i].append((j, float(Mc.data[p])))
+    return out
 
 
 def _push_reference(L, U, b):
     n = len(b)
     w = b.copy().tolist()
-    Lc = L.tocsc()
+    Lc, Uc = L.tocsc(), U.tocsc()
     for j in range(n):
         yj = w[j]
         for p in range(Lc.indptr[j], Lc.indptr[j + 1]):
             i = Lc.indices[p]
             if i != j:
                 w[i] = w[i] - Lc.data[p] * yj
-    Uc = U.tocsc()
     diag = Uc.diagonal()
     for j in range(n - 1, -1, -1):
         zj = w[j] / diag[j]
@@ -111,6 +189,21 @@ def _push_reference(L, U, b):
     return np.array(w)
 
 
+def _pickers(seed):
+    rng = np.random.default_rng(seed)
+
+    def shuffled(live):
+        return [live[k] for k in rng.permutation(len(live))]
+
+    def greedy(live):      # one warp as far as it goes: reads race ahead of producers
+        return live
+
+    def laggard(live):     # the warp with the least progress first
+        return sorted(live, key=lambda w: (w.bi, w.b))
+
+    return [shuffled, greedy, laggard]
+
+
 @pytest.mark.parametrize("config,index", [(1, 0), (2, 23)])
 def test_schedule_replays_reference_solve(built, tmp_path, config, index):
     import neurips2026_smart_building_challenge_b200 as pkg
@@ -120,19 +213,34 @@ def test_schedule_replays_reference_solve(built, tmp_path, config, index):
     L, U = b.csc("lu_L"), b.csc("lu_U")
     n = L.shape[0]
     lib = pkg.env_lib()
-    fwd = _chunks(*_schedule(lib, blob, 0))
-    bwd = _chunks(*_schedule(lib, blob, 1))
-    # number of forward tasks per row (a row is final after its last one)
-    _FWD_LEFT.clear()
-    for tasks, _, _, _ in fwd:
-        for r in tasks["row"]:
-            _FWD_LEFT[int(r)] = _FWD_LEFT.get(int(r), 0) + 1
-    rng = np.random.default_rng(index)
-    rhs = rng.standard_normal(n) * 300.0
-    y = _run(fwd, rhs, False, n)
-    z = _run(bwd, y, True, n)
+    fwd, bwd = _programs(lib, blob, 0), _programs(lib, blob, 1)
+    tl, tu = _terms(L, False), _terms(U, True)
+    rhs = np.random.default_rng(index).standard_normal(n) * 300.0
     ref = _push_reference(L, U, rhs)
-    assert np.array_equal(z, ref)
-    # every off-diagonal term appears exactly once
-    assert sum(len(c[2]) for c in fwd) == L.nnz - n
-    assert sum(len(c[2]) for c in bwd) == U.nnz   # terms + one diagonal per row
+    for k, pick in enumerate(_pickers(index)):
+        y = _execute(fwd, rhs, n, False, pick, tl)
+        z = _execute(bwd, y, n, True, pick, tu)
+        assert np.array_equal(z, ref), f"interleaving {k}"
+
+
+def test_schedule_stats(built, tmp_path):
+    """The statistics export agrees with the streams."""
+    import neurips2026_smart_building_challenge_b200 as pkg
+
+    blob = pkg.write_scenario(tmp_path / "s.sbb", pkg.preset(1, 0, n_steps=10))
+    lib = pkg.env_lib()
+    lib.sb_sweep_stats.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(ctypes.c_double)]
+    L = Blob(blob).csc("lu_L")
+    n = L.shape[0]
+    for sweep in (0, 1):
+        st = (ctypes.c_double * 8)()
+        assert lib.sb_sweep_stats(str(blob).encode(), sweep, st) == 0
+        progs = _programs(lib, blob, sweep)
+        bundles = [B for p in progs for B in _parse(p, n, sweep == 1)]
+        assert st[0] == L.nnz - n
+        assert st[1] == len(bundles)
+        assert st[2] == sum(len(B["blocks"]) for B in bundles)
+        assert st[3] == sum(int(r != n) for B in bundles for r in B["rows"])
+        assert st[4] <= sum(len(B["pre"]) for B in bundles)
+        assert st[7] == sum(len(p) for p in progs)
+    assert lib.sb_sweep_stats(str(blob).encode(), 2, st) == -1
