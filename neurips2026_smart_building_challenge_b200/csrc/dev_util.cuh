@@ -57,6 +57,10 @@ __device__ __forceinline__ void fence_proxy_async() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// An int carried in the low word of a double (scratch exchange through shared memory).
+__device__ __forceinline__ double int_in_double(int v) { return __hiloint2double(0, v); }
+__device__ __forceinline__ int int_from_double(double d) { return __double2loint(d); }
+
 // Row ready flags of the solve sweeps (shared memory, CTA scope).
 __device__ __forceinline__ uint32_t ld_acquire_u8(const uint8_t* p) {
     uint32_t v;

@@ -274,21 +274,81 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
         cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
         smem_cap = (size_t)optin;
     }
+    // slab width: the narrowest that still puts every slab on its own SM in one
+    // wave (a narrower slab leaves a deeper schedule ring), else the widest
+    // that fits; ring depth: what the slab leaves of shared memory
+    int n_sm = 0;
+    {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+    }
+    // bmin: the narrowest slab whose free memory between the sweeps holds the
+    // air-side dense system
+    std::vector<int> bmax(NG), bmin(NG);
+    for (int c = 0; c < NG; c++) {
+        const HostGroup& h = E.hg[c];
+        bmax[c] = bmin[c] = 0;
+        for (int b = slab_cap; b >= 1 && !bmax[c]; b--)
+            if (solve_ring_stages(h.n, b, smem_cap) > 0) bmax[c] = b;
+        for (int b = 1; b <= bmax[c] && !bmin[c]; b++)
+            if (h.k == 0 || dense_teams(h.n, h.k, b, solve_ring_stages(h.n, b, smem_cap)) >= 1) bmin[c] = b;
+        if (!bmax[c]) {
+            set_err("group %d: one env's field (%d cells) exceeds shared memory", c, h.n);
+            return false;
+        }
+        if (!bmin[c]) {
+            set_err("group %d: the %d x %d air-side system does not fit in shared memory", c, h.k, h.k);
+            return false;
+        }
+    }
+    auto width = [&](int c, int b) { return std::max(bmin[c], std::min(b, bmax[c])); };
+    int bwave = slab_cap;
+    for (int b = 1; b <= slab_cap; b++) {
+        long slabs = 0;
+        for (int c = 0; c < NG; c++) slabs += (E.gd[c].n_env + width(c, b) - 1) / width(c, b);
+        if (slabs <= n_sm) { bwave = b; break; }
+    }
+    // then narrow the slabs of the group with the most dense-solve work (rounds
+    // of team solves x k^2) while the slabs still fit in one wave: slabs run
+    // side by side, so the slowest one sets the step time
+    std::vector<int> bsel(NG);
+    long slabs_now = 0;
+    for (int c = 0; c < NG; c++) {
+        bsel[c] = width(c, bwave);
+        slabs_now += (E.gd[c].n_env + bsel[c] - 1) / bsel[c];
+    }
+    auto rounds = [&](int c, int b) {
+        const HostGroup& h = E.hg[c];
+        if (h.k == 0) return 0;
+        const int t = dense_teams(h.n, h.k, b, solve_ring_stages(h.n, b, smem_cap));
+        return (b + t - 1) / t;
+    };
+    auto dense_cost = [&](int c, int b) { return (double)rounds(c, b) * E.hg[c].k * E.hg[c].k; };
+    for (int it = 0; it < 64; it++) {
+        int worst = 0;
+        for (int c = 1; c < NG; c++)
+            if (dense_cost(c, bsel[c]) > dense_cost(worst, bsel[worst])) worst = c;
+        int nb = bsel[worst] - 1;
+        while (nb >= bmin[worst] && rounds(worst, nb) >= rounds(worst, bsel[worst])) nb--;
+        if (nb < bmin[worst] || dense_cost(worst, bsel[worst]) == 0.0) break;
+        const long delta = (long)(E.gd[worst].n_env + nb - 1) / nb - (E.gd[worst].n_env + bsel[worst] - 1) / bsel[worst];
+        if (slabs_now + delta > n_sm) break;
+        slabs_now += delta;
+        bsel[worst] = nb;
+    }
     for (int c = 0; c < NG; c++) {
         HostGroup& h = E.hg[c];
         GroupDev& gd = E.gd[c];
         gd.n = h.n; gd.ncv = h.ncv; gd.k = h.k; gd.nz = h.nz;
         gd.sigma_identity = 1;
-        gd.stride = ((h.n + 15) & ~15) + 2;   // >= n + 1: slot n is the zero column of padded terms
-        const size_t solve_fixed = solve_smem_fixed(h.n) + 512;   // + the kernel's static shared memory
-        int B = slab_cap;
-        while (B > 1 && (size_t)B * gd.stride * 8 + solve_fixed > smem_cap) B--;
-        if ((size_t)B * gd.stride * 8 + solve_fixed > smem_cap) {
-            set_err("group %d: one env's field (%d cells) exceeds shared memory", c, h.n);
-            return false;
-        }
+        gd.stride = slab_stride(h.n);
+        const int B = bsel[c];
+        const int rs = solve_ring_stages(h.n, B, smem_cap);
         gd.slab_envs = B;
-        E.smem_solve = std::max(E.smem_solve, (size_t)B * gd.stride * 8 + solve_smem_fixed(h.n));
+        E.smem_solve = std::max(E.smem_solve, solve_smem_bytes(h.n, B, rs));
+        std::string se = build_sweeps(h, rs);
+        if (!se.empty()) { set_err("group %d: %s", c, se.c_str()); return false; }
         gd.cap = E.arena.upload(h.cap, ok); gd.dirx = E.arena.upload(h.dirx, ok);
         gd.mc = E.arena.upload(h.mc, ok); gd.ret = E.arena.upload(h.ret, ok); gd.gain = E.arena.upload(h.gain, ok);
         gd.zone_of_row = E.arena.upload(h.zone_of_row, ok);
@@ -298,6 +358,7 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
                 s.warp_off[w] = hsw.warp_off[w];
                 s.warp_stages[w] = hsw.warp_stages[w];
             }
+            s.ring_stages = (uint32_t)hsw.ring_stages;
         };
         put_sweep(h.fwd, gd.fwd);
         put_sweep(h.bwd, gd.bwd);
@@ -816,18 +877,22 @@ int sb_debug_state(int env, double* out, int cap) {
     return o;
 }
 
-static std::string schedule_of(const char* blob_path, int sweep, HostGroup& g) {
+static std::string schedule_of(const char* blob_path, int sweep, int ring_stages, HostGroup& g) {
     sbb::Reader r;
     std::string e = r.open(blob_path ? blob_path : "");
     if (e.empty()) e = build_group(r, g);
     if (e.empty() && sweep != 0 && sweep != 1) e = "sweep must be 0 (L) or 1 (U)";
+    if (e.empty() && ring_stages == 0) {   // the depth a full slab leaves on a B200 (227 KiB per block)
+        for (int b = kGroupLanes; b >= 1 && !ring_stages; b--) ring_stages = solve_ring_stages(g.n, b, 232448);
+    }
+    if (e.empty()) e = build_sweeps(g, ring_stages);
     return e;
 }
 
-int sb_solve_schedule(const char* blob_path, int sweep, uint8_t* out, size_t cap, size_t* used,
+int sb_solve_schedule(const char* blob_path, int sweep, int ring_stages, uint8_t* out, size_t cap, size_t* used,
                       uint32_t* warp_stages) {
     HostGroup g;
-    const std::string e = schedule_of(blob_path, sweep, g);
+    const std::string e = schedule_of(blob_path, sweep, ring_stages, g);
     if (!e.empty()) { set_err("%s", e.c_str()); return -1; }
     const HostSweep& s = sweep == 0 ? g.fwd : g.bwd;
     if (used) *used = s.bytes.size();
@@ -838,9 +903,9 @@ int sb_solve_schedule(const char* blob_path, int sweep, uint8_t* out, size_t cap
     return 0;
 }
 
-int sb_sweep_stats(const char* blob_path, int sweep, double* out) {
+int sb_sweep_stats(const char* blob_path, int sweep, int ring_stages, double* out) {
     HostGroup g;
-    const std::string e = schedule_of(blob_path, sweep, g);
+    const std::string e = schedule_of(blob_path, sweep, ring_stages, g);
     if (!e.empty() || !out) { set_err("%s", e.empty() ? "null output" : e.c_str()); return -1; }
     const HostSweep& s = sweep == 0 ? g.fwd : g.bwd;
     const double v[8] = {(double)s.terms,    (double)s.bundles,   (double)s.blocks, (double)s.pieces,

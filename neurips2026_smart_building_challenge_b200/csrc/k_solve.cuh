@@ -9,8 +9,8 @@
 // is bit-identical. The pull schedule is precomputed on the host
 // (sweep_sched.cpp): every warp runs its own stream of bundles (four rows in
 // lock step, one lane per env), streamed into a per-warp shared-memory ring
-// with cp.async.bulk; before a bundle, the warp acquires the ready flags of
-// the other warps' rows it reads.
+// with cp.async; before a bundle, the warp acquires the ready flags of the
+// other warps' rows it reads.
 #pragma once
 #include "dev_util.cuh"
 
@@ -27,72 +27,75 @@ constexpr uint32_t kSpinLimit = 1u << 22;
 
 struct SolveShared {
     double* X;            // [B][stride]
-    uint8_t* ring;        // [kSweepWarps][kRingBytes]
-    uint64_t* bar;        // [kSweepWarps][kStages]
+    uint8_t* ring;        // [kSweepWarps][ring_stages][kStageBytes]
     uint8_t* ready;       // [n + 1] row ready flags (epoch of the sweep that finished the row)
     volatile int* abort;  // first error of this CTA
 };
 
-// Shared-memory bytes of a solve CTA besides the slab's field vectors.
-__host__ __device__ constexpr size_t solve_smem_fixed(int n) {
-    return (size_t)kSweepWarps * kRingBytes + (size_t)kSweepWarps * kStages * 8 + (((size_t)n + 1 + 15) & ~(size_t)15) +
-           256;
+// cp.async: 16 bytes global -> shared per lane; one commit group per stage
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// waits until at most `pending` of this thread's newest groups are in flight
+__device__ __forceinline__ void cp_async_wait(uint32_t pending) {
+    switch (pending) {
+        case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
+        case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
+        case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
+        case 3: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
+        case 4: asm volatile("cp.async.wait_group 4;" ::: "memory"); break;
+        case 5: asm volatile("cp.async.wait_group 5;" ::: "memory"); break;
+        case 6: asm volatile("cp.async.wait_group 6;" ::: "memory"); break;
+        default: asm volatile("cp.async.wait_group 7;" ::: "memory"); break;
+    }
 }
 
-// One triangular sweep. Every warp runs its own bundle stream; all threads of
-// the CTA must call it. par: per-warp parity bits of the ring's mbarriers.
-__device__ inline void run_sweep(const SolveShared& sh, const Sweep& sw, int B, int S, int n, uint32_t epoch,
-                                 uint32_t& par) {
+// One triangular sweep. Every warp runs its own bundle stream, copied stage
+// by stage into its ring (each lane copies 16 bytes of a stage); all threads
+// of the CTA must call it.
+__device__ inline void run_sweep(const SolveShared& sh, const Sweep& sw, int B, int S, int n, uint32_t epoch) {
     const unsigned full = 0xffffffffu;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int g = lane >> 3, e = lane & 7;
-    const uint8_t* src = sw.stream + (size_t)sw.warp_off[w] * kStageBytes;
+    const uint32_t R = sw.ring_stages, ring_bytes = R * kStageBytes;
+    const uint8_t* src = sw.stream + (size_t)sw.warp_off[w] * kStageBytes + 16 * lane;
     const uint32_t nst = sw.warp_stages[w];
-    uint8_t* ring = sh.ring + (size_t)w * kRingBytes;
-    uint64_t* bar = sh.bar + w * kStages;
+    uint8_t* ring = sh.ring + (size_t)w * ring_bytes;
     // lanes of envs beyond the slab's capacity read env 0's field and never
     // store, so they touch no memory outside the field
     const bool owns = e < B;
     double* xe = sh.X + (size_t)(owns ? e : 0) * S;
 
-    uint32_t issued = nst < (uint32_t)kStages ? nst : (uint32_t)kStages;
-    uint32_t waited = 0, released = 0, p = 0, ro = 0;
-    if (lane == 0) {
-        fence_proxy_async();
-        for (uint32_t k = 0; k < issued; k++) {
-            mbar_expect_tx(&bar[k], kStageBytes);
-            bulk_g2s(ring + k * kStageBytes, src + (size_t)k * kStageBytes, kStageBytes, &bar[k]);
-        }
+    uint32_t issued = 0, waited = 0, released = 0, p = 0, ro = 0;
+    for (; issued < nst && issued < R; issued++) {
+        cp_async16(ring + issued * kStageBytes + 16 * lane, src + (size_t)issued * kStageBytes);
+        cp_async_commit();
     }
     bool ok = true;
     // wait until the stream's bytes [0, end) are in the ring
     auto ensure = [&](uint32_t end) {
-        while (end > waited * kStageBytes) {
-            if (waited >= issued) { ok = false; break; }
-            const uint32_t slot = waited % kStages;
-            const uint32_t parity = ((par >> slot) & 1u) ^ ((waited / kStages) & 1u);
-            if (!mbar_wait_bounded(&bar[slot], parity)) { ok = false; break; }
-            waited++;
+        if (end > waited * kStageBytes) {
+            const uint32_t need = (end + kStageBytes - 1) / kStageBytes;   // stages [0, need)
+            if (need > issued) { ok = false; return; }
+            cp_async_wait(issued - need);
+            __syncwarp();
+            waited = need;
         }
     };
-    // refill the slots of stages the warp has read completely; only stages
-    // whose arrival was observed (a slot's mbarrier must not run two phases
-    // ahead of its waiter, or the parity wait would never succeed)
+    // refill the slots of stages the warp has read completely
     auto release = [&]() {
         const uint32_t upto = min(p / kStageBytes, waited);
-        while (released < upto) {
-            const uint32_t k = released + kStages;
-            if (k < nst) {
-                __syncwarp();
-                if (lane == 0) {
-                    const uint32_t slot = k % kStages;
-                    fence_proxy_async();
-                    mbar_expect_tx(&bar[slot], kStageBytes);
-                    bulk_g2s(ring + slot * kStageBytes, src + (size_t)k * kStageBytes, kStageBytes, &bar[slot]);
+        if (released < upto) {
+            __syncwarp();   // every lane's reads of those slots are done
+            for (; released < upto; released++) {
+                const uint32_t k = released + R;
+                if (k < nst) {
+                    cp_async16(ring + (k % R) * kStageBytes + 16 * lane, src + (size_t)k * kStageBytes);
+                    cp_async_commit();
+                    issued = k + 1;
                 }
-                issued = k + 1;
             }
-            released++;
         }
     };
 
@@ -107,9 +110,9 @@ __device__ inline void run_sweep(const SolveShared& sh, const Sweep& sw, int B, 
         const uint32_t flags = hv.z >> 16, nblk = hv.z & 0xFFFFu;
         if (flags & kBundleEnd) break;
         if (flags & kBundleSkip) {   // the next bundle starts at the ring's beginning
-            p += kRingBytes - ro;
+            p += ring_bytes - ro;
             ro = 0;
-            ensure(p);   // observe the skipped stages before their slots are refilled
+            ensure(p);
             release();
             continue;
         }
@@ -118,8 +121,7 @@ __device__ inline void run_sweep(const SolveShared& sh, const Sweep& sw, int B, 
         const uint32_t npre = (flags >> 8) & 0xFu;
         const uint32_t bsz = (uint32_t)bundle_bytes((int)npre, (flags & 0xF0u) != 0, (int)nblk);
         const bool bad = row > (uint32_t)n || (fin != kFinNever && fin > nblk) || (flags & 0x3000u) ||
-                         npre > (uint32_t)kMaxPreItems || bsz > (uint32_t)kMaxBundleBytes ||
-                         ro + bsz > (uint32_t)kRingBytes;
+                         npre > (uint32_t)kMaxPreItems || bsz > (uint32_t)kMaxBundleBytes || ro + bsz > ring_bytes;
         if (__any_sync(full, bad)) { atomicCAS((int*)sh.abort, 0, kErrBadBundle); ok = false; break; }
         ensure(p + bsz);
         if (!__all_sync(full, ok)) break;
@@ -183,117 +185,130 @@ __device__ inline void run_sweep(const SolveShared& sh, const Sweep& sw, int B, 
         __syncwarp();
         p += bsz;
         ro += bsz;
-        if (ro == (uint32_t)kRingBytes) ro = 0;
+        if (ro == ring_bytes) ro = 0;
         release();
     }
     if (!ok) atomicCAS((int*)sh.abort, 0, kErrRingTimeout);
-    // every issued stage completes before the ring is reused
-    for (; waited < issued; waited++) {
-        const uint32_t slot = waited % kStages;
-        mbar_wait_bounded(&bar[slot], ((par >> slot) & 1u) ^ ((waited / kStages) & 1u));
-    }
-    for (uint32_t s = 0; s < (uint32_t)kStages; s++) {
-        const uint32_t used = issued > s ? (issued - s + kStages - 1) / kStages : 0;
-        par ^= (used & 1u) << s;
-    }
+    // no copy may land after the sweep: the ring memory is reused
+    cp_async_wait(0);
     __syncwarp();
 }
 
-// Dense k x k system M q = b per env with partial pivoting, the reference's
-// elimination order (complete_port/csim/sb_fdm.c:9-38): first maximal |pivot|,
-// rows with a zero multiplier untouched, a zero pivot column ends the solve.
-// cap envs are processed at once; M rows have stride k+1 (conflict-free columns).
-__device__ inline void dense_solve_chunk(double* base, int k, int cap, const int* live) {
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int ld = k + 1;
-    const size_t per_env = (size_t)k * ld + 3 * (size_t)k + 2;
-    __shared__ int stop_col[16];
-    if (tid < 16) stop_col[tid] = 0;
-    __syncthreads();
+// Dense k x k system M q = b of one env, solved by a team of warps with the
+// reference's elimination (complete_port/csim/sb_fdm.c:9-38): partial
+// pivoting on the first strictly largest |M[r][c]| below the diagonal (the
+// diagonal wins ties, a NaN never wins), rows whose multiplier is 0 left
+// untouched, a zero pivot column ends the solve with b as eliminated so far,
+// then back substitution subtracting the products in ascending column order.
+// Every element receives the reference's operations in the reference's order.
+//
+// Thread p of the team owns matrix row p for the whole solve. Row exchanges
+// are virtual: each thread tracks the position its row currently holds in the
+// reference's (physically swapped) matrix, so a swap moves no data.
+//   M    column-major, k rows: element (r, j) at M[j * k + r]; column k is b
+//   red  [2][team warps][2] doubles of scratch for the pivot reduction
+//   z    [k] solution by position, then [1] diagonal scratch
+__host__ __device__ constexpr size_t dense_env_doubles(int k) { return (size_t)k * (k + 1) + 16 + 2 * (size_t)k; }
+
+__device__ inline void team_sync(int bar, int T) {
+    asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(T) : "memory");
+}
+
+__device__ inline void dense_team(double* M, int k, int ttid, int T, int bar) {
+    const int lane = ttid & 31, tw = ttid >> 5, W = T >> 5;
+    double* red = M + (size_t)k * (k + 1);   // [2][W][2]
+    double* z = red + 16;                     // [k]
+    double* dg = z + k;                       // [k]: diagonal candidate per step parity slot
+    const bool has_row = ttid < k;
+    const int p = has_row ? ttid : 0;
+    int mypos = ttid;
+    bool stopped = false;
     for (int c = 0; c < k; c++) {
-        // (1) pivot search, row swap and multipliers: one warp per env
-        for (int e = warp; e < cap; e += blockDim.x >> 5) {
-            if (!live[e] || stop_col[e]) continue;
-            double* M = base + e * per_env;
-            double* b = M + (size_t)k * ld;
-            double* f = b + k;
-            const double diag = fabs(M[(size_t)c * ld + c]);
-            double best = -1.0;
-            int bidx = 1 << 30;
-            for (int r = c + 1 + lane; r < k; r += 32) {
-                const double v = fabs(M[(size_t)r * ld + c]);
-                if (v > best) { best = v; bidx = r; }   // NaN never wins (as in the scan)
-            }
-            for (int o = 16; o > 0; o >>= 1) {
-                const double ob = __shfl_xor_sync(0xffffffffu, best, o);
-                const int oi = __shfl_xor_sync(0xffffffffu, bidx, o);
-                if (ob > best || (ob == best && oi < bidx)) { best = ob; bidx = oi; }
-            }
-            // sequential scan semantics: the diagonal is the initial best; a later
-            // row replaces it only if strictly larger (a NaN diagonal is never replaced)
-            int piv = c;
-            double pbest = diag;
-            if (bidx < k && best > diag) { piv = bidx; pbest = best; }
-            if (pbest == 0.0) {
-                if (lane == 0) stop_col[e] = 1;
-                __syncwarp();
-                continue;
-            }
-            if (piv != c) {
-                for (int j = c + lane; j < k; j += 32) {
-                    const double t = M[(size_t)c * ld + j];
-                    M[(size_t)c * ld + j] = M[(size_t)piv * ld + j];
-                    M[(size_t)piv * ld + j] = t;
-                }
-                if (lane == 0) { const double t = b[c]; b[c] = b[piv]; b[piv] = t; }
-            }
-            __syncwarp();
-            const double d = M[(size_t)c * ld + c];
-            for (int r = c + 1 + lane; r < k; r += 32) f[r] = ddiv(M[(size_t)r * ld + c], d);
-            __syncwarp();
-        }
-        __syncthreads();
-        // (2) rank-1 update of the trailing rows (columns c+1..k-1) and of b
-        const int rows = k - c - 1;
-        if (rows > 0) {
-            const int cols = k - c;   // column slot 0 updates b, slots 1.. the matrix
-            const int per = rows * cols;
-            for (int idx = tid; idx < cap * per; idx += blockDim.x) {
-                const int e = idx / per, rem = idx % per;
-                if (!live[e] || stop_col[e]) continue;
-                const int r = c + 1 + rem / cols, jj = rem % cols;
-                double* M = base + e * per_env;
-                double* b = M + (size_t)k * ld;
-                const double fr = b[k + r];
-                if (fr == 0.0) continue;
-                if (jj == 0) b[r] = dsub(b[r], dmul(fr, b[c]));
-                else {
-                    const int j = c + jj;
-                    M[(size_t)r * ld + j] = dsub(M[(size_t)r * ld + j], dmul(fr, M[(size_t)c * ld + j]));
-                }
+        // candidates below the diagonal: larger |value| wins, the lower position on
+        // ties (key: position << 8 | row); a NaN never compares greater, so never wins
+        double ba = -1.0;
+        int key = 0x7FFFFFFF;
+        if (has_row && mypos >= c) {
+            const double v = M[(size_t)c * k + p];
+            if (mypos == c) {
+                dg[c & 1] = (double)p;   // the diagonal row: read by everyone after the barrier
+            } else if (fabs(v) > -1.0) {
+                ba = fabs(v);
+                key = (mypos << 8) | p;
             }
         }
-        __syncthreads();
-    }
-    // (3) back substitution, one warp per env: products in parallel, the
-    // subtraction chain in the reference's ascending-column order on lane 0
-    for (int e = warp; e < cap; e += blockDim.x >> 5) {
-        if (!live[e] || stop_col[e]) continue;
-        double* M = base + e * per_env;
-        double* b = M + (size_t)k * ld;
-        double* prod = b + 2 * k;
-        for (int r = k - 1; r >= 0; r--) {
-            for (int j = r + 1 + lane; j < k; j += 32) prod[j] = dmul(M[(size_t)r * ld + j], b[j]);
-            __syncwarp();
-            if (lane == 0) {
-                double s = b[r];
-                for (int j = r + 1; j < k; j++) s = dsub(s, prod[j]);
-                b[r] = ddiv(s, M[(size_t)r * ld + r]);
+        for (int o = 16; o > 0; o >>= 1) {
+            const double oa = __shfl_xor_sync(0xffffffffu, ba, o);
+            const int ok = __shfl_xor_sync(0xffffffffu, key, o);
+            if (oa > ba || (oa == ba && ok < key)) { ba = oa; key = ok; }
+        }
+        double* rb = red + (size_t)(c & 1) * W * 2;
+        if (lane == 0) {
+            rb[2 * tw] = ba;
+            rb[2 * tw + 1] = int_in_double(key);
+        }
+        team_sync(bar, T);
+        for (int q = 0; q < W; q++) {
+            const double oa = rb[2 * q];
+            const int ok = int_from_double(rb[2 * q + 1]);
+            if (oa > ba || (oa == ba && ok < key)) { ba = oa; key = ok; }
+        }
+        // the reference: best = |diagonal|, replaced by a later row only if strictly larger
+        const int drow = (int)dg[c & 1];
+        const double dv = M[(size_t)c * k + drow];
+        int piv = c, prow = drow;
+        double pbest = fabs(dv);
+        if (key != 0x7FFFFFFF && ba > pbest) { piv = key >> 8; prow = key & 0xFF; pbest = ba; }
+        if (pbest == 0.0) { stopped = true; break; }
+        const double d = M[(size_t)c * k + prow];
+        if (mypos == c) mypos = piv;
+        else if (mypos == piv) mypos = c;
+        // eliminate below the pivot, eight columns at a time (all loads first)
+        if (has_row && mypos > c) {
+            const double fr = ddiv(M[(size_t)c * k + p], d);
+            if (fr != 0.0) {
+                int j = c + 1;
+                for (; j + 8 <= k + 1; j += 8) {
+                    double a[8], q[8];
+#pragma unroll
+                    for (int u = 0; u < 8; u++) {
+                        a[u] = M[(size_t)(j + u) * k + p];
+                        q[u] = M[(size_t)(j + u) * k + prow];
+                    }
+#pragma unroll
+                    for (int u = 0; u < 8; u++) M[(size_t)(j + u) * k + p] = dsub(a[u], dmul(fr, q[u]));
+                }
+                for (; j <= k; j++) M[(size_t)j * k + p] = dsub(M[(size_t)j * k + p], dmul(fr, M[(size_t)j * k + prow]));
             }
-            __syncwarp();
         }
     }
-    __syncthreads();
+    // back substitution position by position (columns are not permuted): every
+    // pending row forms its product with the newest z in place, the owner of
+    // the position subtracts its products in ascending column order
+    if (!stopped) {
+        for (int pos = k - 1; pos >= 0; pos--) {
+            if (has_row && mypos <= pos && pos + 1 < k)
+                M[(size_t)(pos + 1) * k + p] = dmul(M[(size_t)(pos + 1) * k + p], z[pos + 1]);
+            if (has_row && mypos == pos) {
+                double s = M[(size_t)k * k + p];
+                int j = pos + 1;
+                for (; j + 8 <= k; j += 8) {
+                    double q[8];
+#pragma unroll
+                    for (int u = 0; u < 8; u++) q[u] = M[(size_t)(j + u) * k + p];
+#pragma unroll
+                    for (int u = 0; u < 8; u++) s = dsub(s, q[u]);
+                }
+                for (; j < k; j++) s = dsub(s, M[(size_t)j * k + p]);
+                z[pos] = ddiv(s, M[(size_t)pos * k + p]);
+            }
+            team_sync(bar, T);
+        }
+    } else {
+        // the reference leaves b as eliminated so far (in swapped order)
+        if (has_row) z[mypos] = M[(size_t)k * k + p];
+    }
+    team_sync(bar, T);
 }
 
 __global__ void __launch_bounds__(kSolveThreads, 1)
@@ -306,17 +321,16 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
     const int nenv = sd.nenv;
     const int tid = threadIdx.x;
 
-    // shared memory: field [B][S] | rings | mbarriers | ready flags | misc
+    // shared memory: field [B][S] | rings | ready flags | misc (solve_smem_bytes)
+    const int R = (int)g.fwd.ring_stages;
     SolveShared sh;
     sh.X = reinterpret_cast<double*>(smem);
     sh.ring = smem + (size_t)B * S * sizeof(double);
-    sh.bar = reinterpret_cast<uint64_t*>(sh.ring + (size_t)kSweepWarps * kRingBytes);
-    sh.ready = reinterpret_cast<uint8_t*>(sh.bar + kSweepWarps * kStages);
+    sh.ready = sh.ring + (size_t)kSweepWarps * R * kStageBytes;
     int* misc = reinterpret_cast<int*>(sh.ready + ((n + 1 + 15) & ~15));
     sh.abort = misc;
     double* amb_e = reinterpret_cast<double*>(misc + 4);   // [8]
     int* active = reinterpret_cast<int*>(amb_e + 8);        // [8]
-    if (tid < kSweepWarps * kStages) mbar_init(&sh.bar[tid], 1);
     if (tid == 0) misc[0] = 0;
     for (int i = tid; i <= n; i += blockDim.x) sh.ready[i] = i < n ? 0 : 0xFF;   // slot n: "no row"
     // padding slots (the zero column of padded terms) and envs the slab does not fill
@@ -337,9 +351,7 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
     } else if (tid < 8) {
         active[tid] = 0;
     }
-    mbar_fence_init();
     __syncthreads();
-    uint32_t par = 0;   // ring mbarrier parities of this thread's warp
 
     // ---- forcing (sb_fdm.c:146-152), written in row order ----
     for (int idx = tid; idx < nenv * n; idx += blockDim.x) {
@@ -358,9 +370,9 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
     __syncthreads();
 
     // ---- first solve ----
-    run_sweep(sh, g.fwd, B, S, n, 1, par);
+    run_sweep(sh, g.fwd, B, S, n, 1);
     __syncthreads();
-    run_sweep(sh, g.bwd, B, S, n, 2, par);
+    run_sweep(sh, g.bwd, B, S, n, 2);
     __syncthreads();
     if (*sh.abort) {   // uniform: read after the barrier
         if (tid == 0) set_error(ctx->status, *sh.abort);
@@ -368,7 +380,11 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
     }
 
     // ---- air side (sb_fdm.c:155-181) ----
-    double* pw = reinterpret_cast<double*>(sh.ring);   // [B][k], ring is idle between sweeps
+    // between the sweeps the fields and the rings are free: the dense
+    // workspace starts at the fields, the air-side vector pw sits at the end
+    // of the rings (dense_workspace_doubles() is checked on the host)
+    const size_t free_doubles = ((size_t)B * S * 8 + (size_t)kSweepWarps * R * kStageBytes) / 8;
+    double* pw = sh.X + free_doubles - (size_t)B * k;   // [B][k]
     int any_active = 0;
     for (int e = 0; e < nenv; e++) any_active |= active[e];
     if (k > 0 && any_active) {
@@ -390,33 +406,29 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
     }
     __syncthreads();
     if (k > 0 && any_active) {
-        const int ld = k + 1;
-        const size_t per_env = (size_t)k * ld + 3 * (size_t)k + 2;
-        const int cap_all = (int)(((size_t)B * S) / per_env);
-        const int cap = cap_all < 1 ? 1 : (cap_all > 16 ? 16 : cap_all);
-        double* base = sh.X;
-        __shared__ int live[16];
+        // one team of warps per env (thread p owns row p), as many envs at once
+        // as the free memory holds (at most 15: named barriers 1..15)
+        const size_t per_env = dense_env_doubles(k);
+        const int wpt = (k + 31) >> 5;                 // warps per team
+        const int cap = dense_teams(n, k, B, R);       // >= 1 (host check)
         for (int e0 = 0; e0 < nenv; e0 += cap) {
             const int ce = (nenv - e0) < cap ? (nenv - e0) : cap;
-            if (tid < 16) live[tid] = (tid < ce) ? active[e0 + tid] : 0;
-            __syncthreads();
-            const int per = k * k;
+            const int per = k * (k + 1);
             for (int idx = tid; idx < ce * per; idx += blockDim.x) {
-                const int e = idx / per, rem = idx % per, i = rem / k, j = rem % k;
-                if (!live[e]) continue;
+                const int e = idx / per, rem = idx % per, j = rem / k, i = rem % k;   // column-major
+                if (!active[e0 + e]) continue;
                 const double* D = ctx->Dst + (size_t)(sd.env0 + e0 + e) * L.nd;
-                double* M = base + e * per_env;
-                M[(size_t)i * ld + j] = dadd(i == j ? 1.0 : 0.0, dmul(D[L.ag + i], g.S[(size_t)i * k + j]));
-            }
-            for (int idx = tid; idx < ce * k; idx += blockDim.x) {
-                const int e = idx / k, i = idx % k;
-                if (live[e]) base[e * per_env + (size_t)k * ld + i] = pw[(e0 + e) * k + i];
+                sh.X[e * per_env + (size_t)j * k + i] =
+                    j < k ? dadd(i == j ? 1.0 : 0.0, dmul(D[L.ag + i], g.S[(size_t)i * k + j])) : pw[(e0 + e) * k + i];
             }
             __syncthreads();
-            dense_solve_chunk(base, k, ce, live);
+            const int team = (tid >> 5) / wpt;
+            if (team < ce && active[e0 + team])
+                dense_team(sh.X + team * per_env, k, tid - team * wpt * 32, wpt * 32, 1 + team);
+            __syncthreads();
             for (int idx = tid; idx < ce * k; idx += blockDim.x) {
                 const int e = idx / k, i = idx % k;
-                if (live[e]) pw[(e0 + e) * k + i] = base[e * per_env + (size_t)k * ld + i];
+                if (active[e0 + e]) pw[(e0 + e) * k + i] = sh.X[e * per_env + (size_t)k * (k + 1) + 16 + i];
             }
             __syncthreads();
         }
@@ -436,9 +448,9 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
             sh.X[(size_t)e * S + i] = acc;
         }
         __syncthreads();
-        run_sweep(sh, g.fwd, B, S, n, 3, par);
+        run_sweep(sh, g.fwd, B, S, n, 3);
         __syncthreads();
-        run_sweep(sh, g.bwd, B, S, n, 4, par);
+        run_sweep(sh, g.bwd, B, S, n, 4);
         __syncthreads();
         if (*sh.abort) {
             if (tid == 0) set_error(ctx->status, *sh.abort);

@@ -55,7 +55,8 @@ enum : int {
 // reads that this warp has not produced or waited for itself. A row that
 // another warp reads is published with a release store of the sweep's epoch.
 //
-// Stream layout (16-byte items; a bundle never wraps around the warp's ring):
+// Stream layout (16-byte items; a bundle never wraps around the warp's ring of
+// ring_stages x kStageBytes bytes):
 //   BundleHeader (16 B)
 //   npre x u16 row[8] (16 B each): rows to wait for (entry n = no row; its
 //        flag is always set)
@@ -69,10 +70,10 @@ constexpr int kGroupLanes = 8;           // envs per lane group (slab_envs <= 8)
 constexpr int kBundleRows = 4;           // lane groups per warp
 constexpr int kTermSteps = 4;            // terms per group per TermBlock
 constexpr int kTermBlockBytes = kBundleRows * kTermSteps * 10;   // 160
-constexpr int kStageBytes = 480;         // one bulk copy into a warp's ring
-constexpr int kStages = 4;               // ring depth per warp
-constexpr int kRingBytes = kStageBytes * kStages;
-constexpr int kMaxBundleBytes = 2 * kStageBytes;   // a bundle spans at most 3 stages
+constexpr int kStageBytes = 512;         // one copy into a warp's ring: 16 bytes per lane
+constexpr int kStagesMin = 4;            // ring depth per warp (stages), chosen per group
+constexpr int kStagesMax = 8;
+constexpr int kMaxBundleBytes = 960;     // a bundle spans at most 3 stages
 constexpr int kMaxPreItems = 2;          // pre-wait items per bundle (8 rows each)
 constexpr uint16_t kBundleEnd = 0x8000;  // BundleHeader.flags: end of stream
 constexpr uint16_t kBundleSkip = 0x4000; // BundleHeader.flags: continue at ring offset 0
@@ -90,11 +91,35 @@ SB_HD constexpr int bundle_bytes(int npre, bool divides, int nblk) {
     return 16 + 16 * npre + (divides ? 32 : 0) + kTermBlockBytes * nblk;
 }
 
+// Shared memory of a solve CTA: the slab's fields [B][stride] | the warps'
+// rings [kSweepWarps][ring_stages][kStageBytes] | ready flags [n + 1] | misc.
+SB_HD constexpr int slab_stride(int n) { return ((n + 15) & ~15) + 2; }   // >= n + 1: slot n is zero
+// Doubles free between the sweeps (fields and rings): the air-side dense
+// systems and pw [B][k] live there.
+SB_HD constexpr size_t dense_free_doubles(int n, int B, int ring_stages) {
+    return ((size_t)B * slab_stride(n) * 8 + (size_t)kSweepWarps * ring_stages * kStageBytes) / 8;
+}
+// Envs whose dense systems the solve kernel holds at once: one team of
+// ceil(k/32) warps each, within the free memory, at most 15 (named barriers).
+SB_HD constexpr int dense_teams(int n, int k, int B, int ring_stages) {
+    const size_t per_env = (size_t)k * (k + 1) + 16 + 2 * (size_t)k;
+    const size_t fr = dense_free_doubles(n, B, ring_stages);
+    const int by_mem = fr > (size_t)B * k ? (int)((fr - (size_t)B * k) / per_env) : 0;
+    const int by_warps = kSolveThreads / 32 / ((k + 31) / 32);
+    const int c = by_mem < by_warps ? by_mem : by_warps;
+    return c > 15 ? 15 : c;
+}
+SB_HD constexpr size_t solve_smem_bytes(int n, int B, int ring_stages) {
+    return (size_t)B * slab_stride(n) * 8 + (size_t)kSweepWarps * ring_stages * kStageBytes +
+           (((size_t)n + 1 + 15) & ~(size_t)15) + 256;
+}
+
 // One triangular sweep: per-warp byte streams, each a whole number of stages.
 struct Sweep {
     const uint8_t* stream;                 // all warps' streams back to back
     uint32_t warp_off[kSweepWarps];        // stage index where warp w's stream starts
     uint32_t warp_stages[kSweepWarps];     // stages in warp w's stream
+    uint32_t ring_stages;                  // ring depth the streams were laid out for
 };
 
 // Geometry + solver tables of one group and the state of its envs.

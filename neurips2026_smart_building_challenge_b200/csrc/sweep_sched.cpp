@@ -60,9 +60,12 @@ inline void orr(uint64_t* d, const uint64_t* s, int w) {
 }  // namespace
 
 std::string build_sweep(int n, const std::vector<std::vector<std::pair<int, double>>>& terms, bool backward,
-                        const std::vector<double>& diag, HostSweep& out) {
+                        const std::vector<double>& diag, int ring_stages, HostSweep& out) {
     out = HostSweep();
     if (n <= 0 || n >= 0xFFFF) return "factor too large for the sweep format";
+    if (ring_stages < kStagesMin || ring_stages > kStagesMax) return "unsupported ring depth";
+    out.ring_stages = ring_stages;
+    const size_t ring_bytes = (size_t)ring_stages * kStageBytes;
     const int W = kSweepWarps;
     std::vector<int> nt(n);
     std::vector<char> need(n);
@@ -315,14 +318,14 @@ std::string build_sweep(int n, const std::vector<std::vector<std::pair<int, doub
             h.flags |= (uint16_t)(npre << 8);
             const size_t bytes = (size_t)bundle_bytes(npre, (h.flags & 0xF0) != 0, B.nblk);
             if (bytes > (size_t)kMaxBundleBytes) return "sweep bundle too large";
-            const size_t ro = stream.size() % kRingBytes;
-            if (ro + bytes > (size_t)kRingBytes) {   // continue at the start of the ring
+            const size_t ro = stream.size() % ring_bytes;
+            if (ro + bytes > ring_bytes) {   // continue at the start of the ring
                 BundleHeader skip;
                 memset(&skip, 0, sizeof(skip));
                 skip.flags = kBundleSkip;
                 for (int g = 0; g < kBundleRows; g++) skip.fin[g] = kFinNever;
                 put(&skip, sizeof(skip));
-                stream.resize(stream.size() + (kRingBytes - ro - sizeof(skip)), 0);
+                stream.resize(stream.size() + (ring_bytes - ro - sizeof(skip)), 0);
             }
             put(&h, sizeof(h));
             for (int it = 0; it < npre; it++) {

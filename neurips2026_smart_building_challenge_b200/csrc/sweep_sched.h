@@ -13,6 +13,7 @@ struct HostSweep {
     std::vector<uint8_t> bytes;             // all warps' streams back to back
     uint32_t warp_off[kSweepWarps] = {};    // stage index where warp w's stream starts
     uint32_t warp_stages[kSweepWarps] = {}; // stages in warp w's stream
+    int ring_stages = 0;                    // ring depth the streams were laid out for
     // statistics of the schedule
     int64_t terms = 0, bundles = 0, blocks = 0, prewaits = 0, publishes = 0, pieces = 0;
     double sim_cycles = 0;                  // modelled length of the sweep (cycles of one warp)
@@ -23,9 +24,10 @@ struct HostSweep {
 //             reference's column push subtracts them from row i;
 //   backward  U sweep: every row is finished by a division by diag[i]
 //             (rows without terms too); forward rows without terms are final
-//             from the start and get no work.
+//             from the start and get no work;
+//   ring_stages  depth of the kernel's per-warp ring (a bundle never wraps it).
 // Returns "" or an error.
 std::string build_sweep(int n, const std::vector<std::vector<std::pair<int, double>>>& terms, bool backward,
-                        const std::vector<double>& diag, HostSweep& out);
+                        const std::vector<double>& diag, int ring_stages, HostSweep& out);
 
 }  // namespace sbenv

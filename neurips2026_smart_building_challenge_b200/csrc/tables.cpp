@@ -204,8 +204,12 @@ std::string build_group(const sbb::Reader& b, HostGroup& g) {
     for (int i = 0; i < n; i++) g.zone_of_row[i] = cell_zone[solved[F.ir[i]]];
 
     // sweeps: L rows pull columns ascending, U rows pull columns descending
-    std::vector<std::vector<std::pair<int, double>>> lt(n), ut(n);
-    std::vector<double> udiag(n);
+    std::vector<std::vector<std::pair<int, double>>>& lt = g.lt;
+    std::vector<std::vector<std::pair<int, double>>>& ut = g.ut;
+    std::vector<double>& udiag = g.udiag;
+    lt.assign(n, {});
+    ut.assign(n, {});
+    udiag.assign(n, 0.0);
     for (int j = 0; j < n; j++)
         for (int q = F.Lp[j]; q < F.Lp[j + 1]; q++)
             if (q != F.Ldg[j]) lt[F.Li[q]].push_back({j, F.Lx[q]});
@@ -217,9 +221,7 @@ std::string build_group(const sbb::Reader& b, HostGroup& g) {
     for (int i = 0; i < n; i++)
         for (size_t a = 0; a < ut[i].size(); a++)
             if (ut[i][a].first == i) return "U has a duplicate diagonal";
-    std::string se = build_sweep(n, lt, false, udiag, g.fwd);
-    if (se.empty()) se = build_sweep(n, ut, true, udiag, g.bwd);
-    if (!se.empty()) return se;
+    if (n >= 0xFFFF) return "more than 65534 solved cells";
 
     // air side
     const int64_t* shp = b.i64("sensed_shape");
@@ -474,6 +476,19 @@ std::string build_scenario(const sbb::Reader& b, const HostGroup& g, int max_ste
     for (int t = 0; t < n; t++) s.mass_init[g.row_of_solved[t]] = mi[t];
     (void)solved;
     return "";
+}
+
+int solve_ring_stages(int n, int B, size_t smem_cap) {
+    const size_t kStatic = 512;   // the solve kernel's static shared memory, with margin
+    for (int r = kStagesMax; r >= kStagesMin; r--)
+        if (solve_smem_bytes(n, B, r) + kStatic <= smem_cap) return r;
+    return 0;
+}
+
+std::string build_sweeps(HostGroup& g, int ring_stages) {
+    std::string e = build_sweep(g.n, g.lt, false, g.udiag, ring_stages, g.fwd);
+    if (e.empty()) e = build_sweep(g.n, g.ut, true, g.udiag, ring_stages, g.bwd);
+    return e;
 }
 
 }  // namespace sbenv

@@ -15,7 +15,9 @@ struct HostGroup {
     int64_t nnzL = 0, nnzU = 0;
     std::vector<double> cap, dirx, mc, ret, gain;   // row order
     std::vector<int32_t> zone_of_row;
-    HostSweep fwd, bwd;
+    HostSweep fwd, bwd;                   // built by build_sweeps once the ring depth is known
+    std::vector<std::vector<std::pair<int, double>>> lt, ut;   // sweep terms in push order
+    std::vector<double> udiag;
     std::vector<int32_t> sn_p, sn_pos, ap_rp, ap_col;
     std::vector<double> sn_x, ap_x, S;
     std::vector<int32_t> room_off, room_pos, cell_of_pos, pos_of_cell;
@@ -51,6 +53,11 @@ struct HostScn {
 
 // Builds the solver/geometry tables of a group from its first blob.
 std::string build_group(const sbb::Reader& b, HostGroup& g);
+// Deepest per-warp ring (stages, at most kStagesMax) that a slab of B envs of an
+// n-cell field leaves room for within smem_cap bytes; 0 if not even kStagesMin.
+int solve_ring_stages(int n, int B, size_t smem_cap);
+// Builds the group's L and U sweep programs for a per-warp ring of ring_stages.
+std::string build_sweeps(HostGroup& g, int ring_stages);
 // Builds the per-scenario tables (needs the group's position maps).
 std::string build_scenario(const sbb::Reader& b, const HostGroup& g, int max_steps_kw, HostScn& s);
 // True when b can share a's group: every geometry / solver section identical.

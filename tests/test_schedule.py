@@ -13,18 +13,19 @@ import pytest
 
 from sbb_read import Blob
 
-NW, STAGE, RING, MAX_BUNDLE = 16, 480, 1920, 960
+NW, STAGE, MAX_BUNDLE = 16, 512, 960
 END, SKIP, FIN_NEVER = 0x8000, 0x4000, 0xFF
 
 
-def _programs(lib, blob, sweep):
+def _programs(lib, blob, sweep, ring_stages):
     used = ctypes.c_size_t()
     stages = (ctypes.c_uint32 * NW)()
-    lib.sb_solve_schedule.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t,
+    lib.sb_solve_schedule.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t,
                                       ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_uint32)]
-    assert lib.sb_solve_schedule(str(blob).encode(), sweep, None, 0, ctypes.byref(used), stages) == 1
+    b = str(blob).encode()
+    assert lib.sb_solve_schedule(b, sweep, ring_stages, None, 0, ctypes.byref(used), stages) == 1
     buf = (ctypes.c_uint8 * used.value)()
-    assert lib.sb_solve_schedule(str(blob).encode(), sweep, buf, used.value, ctypes.byref(used), stages) == 0
+    assert lib.sb_solve_schedule(b, sweep, ring_stages, buf, used.value, ctypes.byref(used), stages) == 0
     raw, out, pos = bytes(buf), [], 0
     for w in range(NW):
         size = stages[w] * STAGE
@@ -34,9 +35,11 @@ def _programs(lib, blob, sweep):
     return out
 
 
-def _parse(stream, n, backward):
-    """Bundles of one warp stream. A bundle never wraps around the 1920-byte
-    ring: a skip header moves the stream to the ring's start (zero bytes)."""
+def _parse(stream, n, backward, ring_stages):
+    """Bundles of one warp stream. A bundle never wraps around the warp's ring
+    (ring_stages x 512 bytes): a skip header moves the stream to the ring's
+    start (zero bytes)."""
+    RING = ring_stages * STAGE
     pos, bundles = 0, []
     while True:
         hdr = stream[pos:pos + 16]
@@ -87,7 +90,7 @@ class _Warp:
         return self.bi >= len(self.bundles)
 
 
-def _execute(programs, x, n, backward, pick, expect):
+def _execute(programs, x, n, backward, pick, expect, ring_stages):
     """Runs the warps' bundles block by block in the order pick() chooses."""
     x = list(x) + [0.0]
     final = [False] * (n + 1)
@@ -97,7 +100,7 @@ def _execute(programs, x, n, backward, pick, expect):
             final[i] = not expect[i]
     ready = [False] * n + [True]
     got = [[] for _ in range(n)]
-    warps = [_Warp(_parse(p, n, backward)) for p in programs]
+    warps = [_Warp(_parse(p, n, backward, ring_stages)) for p in programs]
 
     def finish(wp, B, g):
         r = B["rows"][g]
@@ -204,8 +207,8 @@ def _pickers(seed):
     return [shuffled, greedy, laggard]
 
 
-@pytest.mark.parametrize("config,index", [(1, 0), (2, 23)])
-def test_schedule_replays_reference_solve(built, tmp_path, config, index):
+@pytest.mark.parametrize("config,index,ring", [(1, 0, 4), (2, 23, 6), (2, 5, 8)])
+def test_schedule_replays_reference_solve(built, tmp_path, config, index, ring):
     import neurips2026_smart_building_challenge_b200 as pkg
 
     blob = pkg.write_scenario(tmp_path / "s.sbb", pkg.preset(config, index, n_steps=10))
@@ -213,34 +216,37 @@ def test_schedule_replays_reference_solve(built, tmp_path, config, index):
     L, U = b.csc("lu_L"), b.csc("lu_U")
     n = L.shape[0]
     lib = pkg.env_lib()
-    fwd, bwd = _programs(lib, blob, 0), _programs(lib, blob, 1)
+    fwd, bwd = _programs(lib, blob, 0, ring), _programs(lib, blob, 1, ring)
     tl, tu = _terms(L, False), _terms(U, True)
     rhs = np.random.default_rng(index).standard_normal(n) * 300.0
     ref = _push_reference(L, U, rhs)
     for k, pick in enumerate(_pickers(index)):
-        y = _execute(fwd, rhs, n, False, pick, tl)
-        z = _execute(bwd, y, n, True, pick, tu)
+        y = _execute(fwd, rhs, n, False, pick, tl, ring)
+        z = _execute(bwd, y, n, True, pick, tu, ring)
         assert np.array_equal(z, ref), f"interleaving {k}"
 
 
 def test_schedule_stats(built, tmp_path):
-    """The statistics export agrees with the streams."""
+    """The statistics export agrees with the streams; bad arguments are errors."""
     import neurips2026_smart_building_challenge_b200 as pkg
 
     blob = pkg.write_scenario(tmp_path / "s.sbb", pkg.preset(1, 0, n_steps=10))
     lib = pkg.env_lib()
-    lib.sb_sweep_stats.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(ctypes.c_double)]
+    lib.sb_sweep_stats.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_double)]
     L = Blob(blob).csc("lu_L")
     n = L.shape[0]
+    st = (ctypes.c_double * 8)()
     for sweep in (0, 1):
-        st = (ctypes.c_double * 8)()
-        assert lib.sb_sweep_stats(str(blob).encode(), sweep, st) == 0
-        progs = _programs(lib, blob, sweep)
-        bundles = [B for p in progs for B in _parse(p, n, sweep == 1)]
+        assert lib.sb_sweep_stats(str(blob).encode(), sweep, 5, st) == 0
+        progs = _programs(lib, blob, sweep, 5)
+        bundles = [B for p in progs for B in _parse(p, n, sweep == 1, 5)]
         assert st[0] == L.nnz - n
         assert st[1] == len(bundles)
         assert st[2] == sum(len(B["blocks"]) for B in bundles)
         assert st[3] == sum(int(r != n) for B in bundles for r in B["rows"])
         assert st[4] <= sum(len(B["pre"]) for B in bundles)
         assert st[7] == sum(len(p) for p in progs)
-    assert lib.sb_sweep_stats(str(blob).encode(), 2, st) == -1
+    assert lib.sb_sweep_stats(str(blob).encode(), 0, 0, st) == 0          # default depth
+    assert lib.sb_sweep_stats(str(blob).encode(), 2, 5, st) == -1         # no such sweep
+    assert lib.sb_sweep_stats(str(blob).encode(), 0, 3, st) == -1         # ring too shallow
+    assert b"ring" in lib.sb_last_error()
