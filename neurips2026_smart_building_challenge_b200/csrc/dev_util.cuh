@@ -83,7 +83,8 @@ __device__ __forceinline__ void set_error(int* status, int code) {
 // words, and the 624-word regeneration is shared across the lanes.
 // ---------------------------------------------------------------------------
 struct WarpMt {
-    uint32_t* st;   // 624 raw state words (shared memory)
+    uint32_t* st;   // 624 raw state words of the current block (shared memory)
+    uint32_t* nx;   // 624 raw state words of the next block
     uint32_t* tw;   // 2 x 624 tempered words: current block, next block
     int pos;        // absolute index into tw (0..1247); words < 624 are the current block
 };
@@ -96,72 +97,105 @@ __device__ __forceinline__ uint32_t mt_temper(uint32_t y) {
     return y;
 }
 
-// In-place regeneration of the 624-word state. Processing 32-word chunks in
-// increasing index order, reading each chunk before writing it, reproduces the
-// sequential recurrence: s[i] uses the old s[i+1] and the new s[i-227].
-__device__ inline void mt_twist_warp(uint32_t* st) {
-    const int lane = threadIdx.x & 31;
-    for (int base = 0; base < 624; base += 32) {
-        const int i = base + lane;
-        uint32_t nv = 0;
-        if (i < 624) {
-            const uint32_t x = (st[i] & 0x80000000u) | (st[(i + 1) % 624] & 0x7fffffffu);
-            uint32_t xa = x >> 1;
-            if (x & 1u) xa ^= 0x9908b0dfu;
-            nv = st[(i + 397) % 624] ^ xa;
-        }
-        __syncwarp();
-        if (i < 624) st[i] = nv;
-        __syncwarp();
-    }
+__device__ __forceinline__ uint32_t mt_mix(uint32_t si, uint32_t si1, uint32_t sm) {
+    const uint32_t x = (si & 0x80000000u) | (si1 & 0x7fffffffu);
+    return sm ^ (x >> 1) ^ ((x & 1u) ? 0x9908b0dfu : 0u);
 }
 
-__device__ inline void mt_fill_block(uint32_t* st, uint32_t* dst) {
-    mt_twist_warp(st);
-    for (int i = threadIdx.x & 31; i < 624; i += 32) dst[i] = mt_temper(st[i]);
+// In-place regeneration of the 624-word state. The sequential recurrence
+// new[i] = f(old[i], old[i+1], new-or-old[i+397 mod 624]) reads only old words
+// for i < 227, words of the first range for 227 <= i < 454 and of the second
+// for i >= 454 (with new[0] for i = 623): three ranges, each computed by the
+// whole warp from values read before any of it is written.
+__device__ inline void mt_twist_warp(uint32_t* st) {
+    const int lane = threadIdx.x & 31;
+    uint32_t v[8];
+    // [0, 227): st[i + 397] is still old
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+        const int i = lane + 32 * q;
+        v[q] = i < 227 ? mt_mix(st[i], st[i + 1], st[i + 397]) : 0u;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+        const int i = lane + 32 * q;
+        if (i < 227) st[i] = v[q];
+    }
+    __syncwarp();
+    // [227, 454): st[i - 227] is new
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+        const int i = 227 + lane + 32 * q;
+        v[q] = i < 454 ? mt_mix(st[i], st[i + 1], st[i - 227]) : 0u;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+        const int i = 227 + lane + 32 * q;
+        if (i < 454) st[i] = v[q];
+    }
+    __syncwarp();
+    // [454, 624): st[i - 227] is new, and so is st[0] for i = 623
+#pragma unroll
+    for (int q = 0; q < 6; q++) {
+        const int i = 454 + lane + 32 * q;
+        v[q] = i < 624 ? mt_mix(st[i], st[(i + 1) % 624], st[i - 227]) : 0u;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < 6; q++) {
+        const int i = 454 + lane + 32 * q;
+        if (i < 624) st[i] = v[q];
+    }
     __syncwarp();
 }
 
-// Loads a stream (624 raw words + position) and prepares the current and next
-// tempered blocks. A stream whose position is 624 (fresh seed or block fully
-// used) starts with a regeneration, as the sequential generator would.
-__device__ inline void mt_load(WarpMt& m, const uint32_t* g, uint32_t* st, uint32_t* tw) {
+// Tempered current block from st, raw and tempered next block from a copy.
+__device__ inline void mt_prepare_blocks(WarpMt& m) {
+    const int lane = threadIdx.x & 31;
+    for (int i = lane; i < 624; i += 32) {
+        m.tw[i] = mt_temper(m.st[i]);
+        m.nx[i] = m.st[i];
+    }
+    __syncwarp();
+    mt_twist_warp(m.nx);
+    for (int i = lane; i < 624; i += 32) m.tw[624 + i] = mt_temper(m.nx[i]);
+    __syncwarp();
+}
+
+// Loads a stream (624 raw words + position). A stream whose position is 624
+// (fresh seed or block fully used) starts with a regeneration, as the
+// sequential generator would.
+__device__ inline void mt_load(WarpMt& m, const uint32_t* g, uint32_t* st, uint32_t* nx, uint32_t* tw) {
     const int lane = threadIdx.x & 31;
     m.st = st;
+    m.nx = nx;
     m.tw = tw;
     for (int i = lane; i < 624; i += 32) st[i] = g[i];
     const int p = (int)g[624];
     __syncwarp();
     if (p >= 624) {
-        mt_fill_block(st, tw);
+        mt_twist_warp(st);
         m.pos = 0;
     } else {
-        // the raw state is the twisted block the position indexes into
-        for (int i = lane; i < 624; i += 32) tw[i] = mt_temper(st[i]);
-        __syncwarp();
-        m.pos = p;
+        m.pos = p;   // the raw state is the twisted block the position indexes into
     }
-    // next block from a copy of the state (the stored state stays the current block)
-    for (int i = lane; i < 624; i += 32) tw[624 + i] = st[i];
-    __syncwarp();
-    mt_twist_warp(tw + 624);
-    for (int i = lane; i < 624; i += 32) tw[624 + i] = mt_temper(tw[624 + i]);
-    __syncwarp();
+    mt_prepare_blocks(m);
 }
 
 // Advances to the next block once the current one is used up: the next block
-// becomes current, and its raw state (st twisted once more) is kept in st.
+// becomes current (raw and tempered), and one regeneration makes the new next.
 __device__ inline void mt_roll(WarpMt& m) {
     if (m.pos < 624) return;
     const int lane = threadIdx.x & 31;
-    mt_twist_warp(m.st);   // st now holds the raw words of the block that becomes current
-    for (int i = lane; i < 624; i += 32) m.tw[i] = m.tw[624 + i];
+    for (int i = lane; i < 624; i += 32) {
+        m.st[i] = m.nx[i];
+        m.tw[i] = m.tw[624 + i];
+    }
     __syncwarp();
-    // new next block: twist a scratch copy of st (scratch = next-block area)
-    for (int i = lane; i < 624; i += 32) m.tw[624 + i] = m.st[i];
-    __syncwarp();
-    mt_twist_warp(m.tw + 624);
-    for (int i = lane; i < 624; i += 32) m.tw[624 + i] = mt_temper(m.tw[624 + i]);
+    mt_twist_warp(m.nx);
+    for (int i = lane; i < 624; i += 32) m.tw[624 + i] = mt_temper(m.nx[i]);
     __syncwarp();
     m.pos -= 624;
 }

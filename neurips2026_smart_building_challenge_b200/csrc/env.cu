@@ -378,7 +378,7 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
         E.max_ncv = std::max(E.max_ncv, h.ncv);
         E.smem_pre = std::max(E.smem_pre, sizeof(double) * (size_t)(h.ncv + 2 * nz_max + nv_max + 2 * na_max + 2 * k_max));
         E.smem_post = std::max(E.smem_post, sizeof(double) * (size_t)(2 * h.ncv + 3 * nz_max + 2 * nv_max));
-        const size_t rng_b = 4 * (size_t)(624 + 1248) + 4 * (size_t)(h.cv_off.back() + 2 * h.conv_maxroom);
+        const size_t rng_b = 4 * (size_t)(624 + 624 + 1248) + 4 * (4 * (size_t)h.cv_off.back() + 1 + h.cv_off.size());
         E.smem_rng = std::max(E.smem_rng, rng_b);
     }
     // ---- scenario tables + random streams ----
@@ -435,7 +435,7 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
         s.conv_npairs = E.arena.zeros<int>(1, ok);
         s.conv_scratch = nullptr;
     }
-    for (int i = 0; i < G; i++) E.smem_rng = std::max(E.smem_rng, 4 * (size_t)(624 + 1248) + 4 * (size_t)E.hs[i].nz * E.hs[i].assign);
+    for (int i = 0; i < G; i++) E.smem_rng = std::max(E.smem_rng, 4 * (size_t)(624 + 624 + 1248) + 4 * (size_t)E.hs[i].nz * E.hs[i].assign);
     // ---- env index ----
     E.ei.resize(n);
     for (int i = 0; i < G; i++)

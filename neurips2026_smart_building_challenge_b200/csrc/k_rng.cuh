@@ -56,11 +56,17 @@ __global__ void __launch_bounds__(32) k_rng(const StepCtx* __restrict__ ctx, int
     const ScnDev& s = ctx->scns[si];
     const GroupDev& g = ctx->groups[s.group];
     const int lane = threadIdx.x & 31;
+    // shared memory: MT state 624 | next state 624 | tempered blocks 1248 |
+    // perm, cand_off, pick cells, pick candidates (conv cells each) | room pick offsets
+    const int ncells = g.cv_off[g.conv_nrooms];
     uint32_t* st = reinterpret_cast<uint32_t*>(smem);   // 624
-    uint32_t* tw = st + 624;                             // 1248
-    int* perm = reinterpret_cast<int*>(tw + 1248);       // conv cells
-    int* left = perm + g.cv_off[g.conv_nrooms];          // conv_maxroom
-    int* right = left + g.conv_maxroom;                  // conv_maxroom
+    uint32_t* nx = st + 624;                             // 624
+    uint32_t* tw = nx + 624;                             // 1248
+    int* perm = reinterpret_cast<int*>(tw + 1248);       // [ncells]
+    int* coff = perm + ncells;                           // [ncells + 1]: candidate list offsets
+    int* left = coff + ncells + 1;                       // [ncells]: picked cells, all rooms
+    int* right = left + ncells;                          // [ncells]: their candidate list entries
+    int* roff = right + ncells;                          // [rooms + 1]: picks per room
     RngOut out = outs[si];
     WarpMt m;
 
@@ -70,13 +76,15 @@ __global__ void __launch_bounds__(32) k_rng(const StepCtx* __restrict__ ctx, int
         // ---------------- convection ----------------
         int npairs = 0;
         if (!(s.conv_p == 0.0 || s.conv_dist == 0)) {
-            mt_load(m, s.conv_mt, st, tw);
-            const int ncells = g.cv_off[g.conv_nrooms];
+            for (int x = lane; x <= ncells; x += 32) coff[x] = g.cand_off[x];
             for (int x = lane; x < ncells; x += 32) perm[x] = x;
-            __syncwarp();
+            mt_load(m, s.conv_mt, st, nx, tw);   // its warp barriers order the loads above
+            int total = 0;
             for (int rm = 0; rm < g.conv_nrooms; rm++) {
                 const int base = g.cv_off[rm], cells = g.cv_off[rm + 1] - base;
-                if (cells <= 0) continue;
+                if (lane == 0) roff[rm] = total;
+                int* L = left + total;
+                int* Rr = right + total;
                 int mcount = 0, j = 0;
                 while (j < cells) {
                     mt_roll(m);
@@ -100,12 +108,12 @@ __global__ void __launch_bounds__(32) k_rng(const StepCtx* __restrict__ ctx, int
                     m.pos += 2 * (f + 1);
                     const int gcell = base + j + f;
                     j += f + 1;
-                    const int c0 = g.cand_off[gcell], c1 = g.cand_off[gcell + 1];
+                    const int c0 = coff[gcell], c1 = coff[gcell + 1];
                     if (c1 <= c0) continue;
                     const uint32_t pick_i = mt_bounded(m, (uint32_t)(c1 - c0 - 1));
                     if (lane == 0) {
-                        left[mcount] = gcell;
-                        right[mcount] = g.cand_idx[c0 + (int)pick_i];
+                        L[mcount] = gcell;
+                        Rr[mcount] = c0 + (int)pick_i;   // resolved to a cell after all rooms
                     }
                     mcount++;
                 }
@@ -113,20 +121,25 @@ __global__ void __launch_bounds__(32) k_rng(const StepCtx* __restrict__ ctx, int
                 for (int q = mcount - 1; q > 0; q--) {
                     const int u = (int)mt_bounded(m, (uint32_t)q);
                     if (lane == 0) {
-                        int x = left[q]; left[q] = left[u]; left[u] = x;
-                        x = right[q]; right[q] = right[u]; right[u] = x;
+                        int x = L[q]; L[q] = L[u]; L[u] = x;
+                        x = Rr[q]; Rr[q] = Rr[u]; Rr[u] = x;
                     }
                     __syncwarp();
                 }
-                // compose the swaps: perm[x] = source of the value that ends at x
-                if (lane == 0)
-                    for (int q = 0; q < mcount; q++) {
-                        const int ia = left[q], ib = right[q];
-                        const int x = perm[ia]; perm[ia] = perm[ib]; perm[ib] = x;
-                    }
-                __syncwarp();
+                total += mcount;
             }
+            if (lane == 0) roff[g.conv_nrooms] = total;
             mt_store(m, s.conv_mt);
+            // candidate cells of all picks at once, then the swaps of every room
+            // composed in order (rooms are disjoint: one lane per room)
+            for (int q = lane; q < total; q += 32) right[q] = g.cand_idx[right[q]];
+            __syncwarp();
+            for (int rm = lane; rm < g.conv_nrooms; rm += 32)
+                for (int q = roff[rm]; q < roff[rm + 1]; q++) {
+                    const int ia = left[q], ib = right[q];
+                    const int x = perm[ia]; perm[ia] = perm[ib]; perm[ib] = x;
+                }
+            __syncwarp();
             // emit the moved cells, compacted in ascending order
             for (int x0 = 0; x0 < ncells; x0 += 32) {
                 const int x = x0 + lane;
@@ -143,10 +156,10 @@ __global__ void __launch_bounds__(32) k_rng(const StepCtx* __restrict__ ctx, int
         if (lane == 0) *s.conv_npairs = npairs;
     }
     // ---------------- occupancy ----------------
-    int* occ_st = reinterpret_cast<int*>(smem + (size_t)(624 + 1248) * 4);   // reuse: conv is done
+    int* occ_st = reinterpret_cast<int*>(smem + (size_t)(624 + 624 + 1248) * 4);   // reuse: conv is done
     for (int x = lane; x < s.nz * s.assign; x += 32) occ_st[x] = s.occ_state0[x];
     __syncwarp();
-    mt_load(m, s.occ_mt, st, tw);
+    mt_load(m, s.occ_mt, st, nx, tw);
     if (!reset_only) {
         const int tn = t + 1;
         occ_advance(m, s, occ_st, (int)s.o_hour[tn], (int)s.o_wd[tn], out.V_step);
