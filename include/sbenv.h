@@ -157,12 +157,14 @@ int sb_solve_bytes(double* per_launch);
 int sb_debug_state(int env, double* out, int cap);
 /* Host-only: the solve kernel's program for one sweep of a blob's factor
  * (sweep 0 = L, 1 = U), laid out for per-warp rings of ring_stages 512-byte
- * stages (4..8; 0 = the depth a full slab leaves on a B200): the 16 warps'
- * bundle streams back to back; warp_stages[16] receives each stream's stage
- * count. Returns 0, 1 if cap is too small (*used then holds the size), -1 on
+ * stages (4..8; 0 = the depth a full slab leaves on a B200): the
+ * sb_sweep_warps() warps' programs back to back; warp_stages[] receives each
+ * program's stage count. Returns 0, 1 if cap is too small (*used then holds the size), -1 on
  * error. No counterpart in the reference (its CPU core has no schedule). */
 int sb_solve_schedule(const char* blob_path, int sweep, int ring_stages, uint8_t* out, size_t cap, size_t* used,
                       uint32_t* warp_stages);
+/* Warps of a solve CTA that run sweep programs (streams per sweep). */
+int sb_sweep_warps(void);
 /* Host-only: statistics of that program, out[8] = {terms, bundles, term blocks,
  * row pieces, pre-waits, published rows, modelled cycles, stream bytes}. */
 int sb_sweep_stats(const char* blob_path, int sweep, int ring_stages, double* out);

@@ -903,6 +903,8 @@ int sb_solve_schedule(const char* blob_path, int sweep, int ring_stages, uint8_t
     return 0;
 }
 
+int sb_sweep_warps(void) { return kSweepWarps; }
+
 int sb_sweep_stats(const char* blob_path, int sweep, int ring_stages, double* out) {
     HostGroup g;
     const std::string e = schedule_of(blob_path, sweep, ring_stages, g);

@@ -7,10 +7,10 @@
 // below/above it; here every row pulls its terms in the same column order, so
 // each row receives exactly the same sequence of subtractions and the result
 // is bit-identical. The pull schedule is precomputed on the host
-// (sweep_sched.cpp): every warp runs its own stream of bundles (four rows in
-// lock step, one lane per env), streamed into a per-warp shared-memory ring
-// with cp.async; before a bundle, the warp acquires the ready flags of the
-// other warps' rows it reads.
+// (sweep_sched.cpp): every warp runs its own program, streamed into a per-warp
+// shared-memory ring with cp.async; its four lane groups (one lane per env)
+// each work through their own rows, and control records acquire the ready
+// flags of other warps' rows before rows that read them start.
 #pragma once
 #include "dev_util.cuh"
 
@@ -23,7 +23,7 @@ struct SlabDesc {
     int pad;
 };
 
-constexpr uint32_t kSpinLimit = 1u << 22;
+constexpr uint32_t kSpinLimit = 1u << 22;   // polls of one ready flag (at most ~1 s with the sleeps)
 
 struct SolveShared {
     double* X;            // [B][stride]
@@ -51,144 +51,125 @@ __device__ __forceinline__ void cp_async_wait(uint32_t pending) {
     }
 }
 
-// One triangular sweep. Every warp runs its own bundle stream, copied stage
-// by stage into its ring (each lane copies 16 bytes of a stage); all threads
-// of the CTA must call it.
+// One triangular sweep. Every warp runs its own program, copied stage by
+// stage (three records each) into its ring, 16 bytes per lane; all threads of
+// the CTA must call it.
 __device__ inline void run_sweep(const SolveShared& sh, const Sweep& sw, int B, int S, int n, uint32_t epoch) {
     const unsigned full = 0xffffffffu;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int g = lane >> 3, e = lane & 7;
-    const uint32_t R = sw.ring_stages, ring_bytes = R * kStageBytes;
-    const uint8_t* src = sw.stream + (size_t)sw.warp_off[w] * kStageBytes + 16 * lane;
+    const uint32_t R = sw.ring_stages;
     const uint32_t nst = sw.warp_stages[w];
-    uint8_t* ring = sh.ring + (size_t)w * ring_bytes;
+    const bool copier = lane < kStageBytes / 16;
+    const uint8_t* src = sw.stream + (size_t)sw.warp_off[w] * kStageBytes + 16 * lane;
+    uint8_t* ring = sh.ring + (size_t)w * R * kStageBytes;
     // lanes of envs beyond the slab's capacity read env 0's field and never
     // store, so they touch no memory outside the field
     const bool owns = e < B;
     double* xe = sh.X + (size_t)(owns ? e : 0) * S;
 
-    uint32_t issued = 0, waited = 0, released = 0, p = 0, ro = 0;
+    uint32_t issued = 0;
     for (; issued < nst && issued < R; issued++) {
-        cp_async16(ring + issued * kStageBytes + 16 * lane, src + (size_t)issued * kStageBytes);
+        if (copier) cp_async16(ring + issued * kStageBytes + 16 * lane, src + (size_t)issued * kStageBytes);
         cp_async_commit();
     }
-    bool ok = true;
-    // wait until the stream's bytes [0, end) are in the ring
-    auto ensure = [&](uint32_t end) {
-        if (end > waited * kStageBytes) {
-            const uint32_t need = (end + kStageBytes - 1) / kStageBytes;   // stages [0, need)
-            if (need > issued) { ok = false; return; }
-            cp_async_wait(issued - need);
-            __syncwarp();
-            waited = need;
-        }
-    };
-    // refill the slots of stages the warp has read completely
-    auto release = [&]() {
-        const uint32_t upto = min(p / kStageBytes, waited);
-        if (released < upto) {
-            __syncwarp();   // every lane's reads of those slots are done
-            for (; released < upto; released++) {
-                const uint32_t k = released + R;
-                if (k < nst) {
-                    cp_async16(ring + (k % R) * kStageBytes + 16 * lane, src + (size_t)k * kStageBytes);
-                    cp_async_commit();
-                    issued = k + 1;
-                }
-            }
-        }
-    };
-
-    for (;;) {
+    bool ok = true, end = false, next_ctrl = true;
+    uint32_t row = (uint32_t)n;   // this group's row (n: idle)
+    double acc = 0.0;
+    for (uint32_t s = 0; s < nst && !end; s++) {
         int ab = 0;
         if (lane == 0) ab = *sh.abort;
         ab = __shfl_sync(full, ab, 0);
-        ensure(p + sizeof(BundleHeader));
         if (!__all_sync(full, ok) || ab) break;
-        const uint8_t* base = ring + ro;
-        const uint4 hv = *reinterpret_cast<const uint4*>(base);
-        const uint32_t flags = hv.z >> 16, nblk = hv.z & 0xFFFFu;
-        if (flags & kBundleEnd) break;
-        if (flags & kBundleSkip) {   // the next bundle starts at the ring's beginning
-            p += ring_bytes - ro;
-            ro = 0;
-            ensure(p);
-            release();
-            continue;
-        }
-        const uint32_t row = ((g < 2 ? hv.x : hv.y) >> (16 * (g & 1))) & 0xFFFFu;
-        const uint32_t fin = (hv.w >> (8 * g)) & 0xFFu;
-        const uint32_t npre = (flags >> 8) & 0xFu;
-        const uint32_t bsz = (uint32_t)bundle_bytes((int)npre, (flags & 0xF0u) != 0, (int)nblk);
-        const bool bad = row > (uint32_t)n || (fin != kFinNever && fin > nblk) || (flags & 0x3000u) ||
-                         npre > (uint32_t)kMaxPreItems || bsz > (uint32_t)kMaxBundleBytes || ro + bsz > ring_bytes;
-        if (__any_sync(full, bad)) { atomicCAS((int*)sh.abort, 0, kErrBadBundle); ok = false; break; }
-        ensure(p + bsz);
-        if (!__all_sync(full, ok)) break;
-        // pre-waits: eight rows per item, one per lane; the warp barrier after
-        // them orders every lane's later reads after all the acquires
-        if (lane < 8 * (int)npre) {
-            const uint32_t r = reinterpret_cast<const uint16_t*>(base + 16)[lane];
-            if (r > (uint32_t)n) {
+        cp_async_wait(issued - 1 - s);
+        __syncwarp();
+        const uint8_t* stage = ring + (s % R) * kStageBytes;
+        for (int q = 0; q < kRecordsPerStage && !end; q++) {
+            const uint8_t* rec = stage + q * kRecordBytes;
+            if (!next_ctrl) {
+                // term record: four terms of this group's row
+                const double2 v01 = *reinterpret_cast<const double2*>(rec + 32 * g);
+                const double2 v23 = *reinterpret_cast<const double2*>(rec + 32 * g + 16);
+                const uint2 cc = *reinterpret_cast<const uint2*>(rec + 128 + 8 * g);
+                next_ctrl = (cc.x & kNextIsCtrl) != 0;
+                const double x0 = xe[cc.x & kColMask], x1 = xe[cc.x >> 16];
+                const double x2 = xe[cc.y & 0xFFFFu], x3 = xe[cc.y >> 16];
+                acc = dsub(acc, dmul(v01.x, x0));
+                acc = dsub(acc, dmul(v01.y, x1));
+                acc = dsub(acc, dmul(v23.x, x2));
+                acc = dsub(acc, dmul(v23.y, x3));
+                continue;
+            }
+            // control record: end segments, wait, start rows
+            const ControlRecord* c = reinterpret_cast<const ControlRecord*>(rec);
+            const uint32_t gf = c->gflags[g];
+            const uint32_t nw = c->nwait, newrow = c->row[g];
+            if (__any_sync(full, newrow > (uint32_t)n || nw > (uint32_t)kCtrlWaits)) {
                 atomicCAS((int*)sh.abort, 0, kErrBadBundle);
                 ok = false;
-            } else {
-                uint32_t spins = 0;
+                break;
+            }
+            if ((gf & kGSwitch) && row < (uint32_t)n) {
+                if (gf & kGFinal) {
+                    if (gf & kGDivide) acc = ddiv(acc, c->diag[g]);
+                    if (owns) xe[row] = acc;
+                    if (gf & kGPublish) {
+                        __syncwarp(0xFFu << (8 * g));
+                        if (e == 0) {
+                            __threadfence_block();
+                            st_release_u8(sh.ready + row, epoch);
+                        }
+                    }
+                } else if (owns) {
+                    xe[row] = acc;   // the row continues in a later segment
+                }
+            }
+            __syncwarp();
+            // waits: one row per lane; the warp barrier after them orders every
+            // lane's later reads after all the acquires
+            for (uint32_t i = lane; i < nw; i += 32) {
+                const uint32_t r = c->wait[i];
+                if (r > (uint32_t)n) {
+                    atomicCAS((int*)sh.abort, 0, kErrBadBundle);
+                    ok = false;
+                    break;
+                }
+                // a few quick polls, then sleeps that leave the issue slots to
+                // the warps doing work (bounded: kSpinLimit polls in all)
+                uint32_t spins = 0, nap = 32;
                 while (ld_acquire_u8(sh.ready + r) < epoch) {
                     if (++spins >= kSpinLimit) {
                         atomicCAS((int*)sh.abort, 0, kErrWaitTimeout);
                         ok = false;
                         break;
                     }
-                    if ((spins & 1023u) == 0 && *sh.abort) { ok = false; break; }
+                    if ((spins & 255u) == 0 && *sh.abort) { ok = false; break; }
+                    if (spins > 4) {
+                        __nanosleep(nap);
+                        nap = nap < 256 ? 2 * nap : 256;
+                    }
                 }
+                if (!ok) break;
             }
+            __syncwarp();
+            if (!__all_sync(full, ok)) break;
+            if (gf & kGSwitch) {
+                row = newrow;
+                acc = row < (uint32_t)n ? xe[row] : 0.0;
+            }
+            next_ctrl = (c->flags & kCtrlNext) != 0;
+            end = (c->flags & kCtrlEnd) != 0;
         }
-        __syncwarp();
         if (!__all_sync(full, ok)) break;
-        uint32_t off = 16 + 16 * npre;
-        const bool pub = (flags >> g) & 1u, div = (flags >> (4 + g)) & 1u;
-        double d = 1.0;
-        if (flags & 0xF0u) {
-            d = reinterpret_cast<const double*>(base + off)[g];
-            off += 32;
-        }
-        double acc = xe[row];
-        bool final_written = false;
-        auto finish = [&]() {
-            if (div) acc = ddiv(acc, d);
-            if (owns) xe[row] = acc;
-            final_written = true;
-            if (pub) {
-                __syncwarp(0xFFu << (8 * g));
-                if (e == 0) {
-                    __threadfence_block();
-                    st_release_u8(sh.ready + row, epoch);
-                }
-            }
-        };
-        if (fin == 0) finish();
-        const uint8_t* bp = base + off;
-        for (uint32_t b = 0; b < nblk; b++, bp += kTermBlockBytes) {
-            const double2 v01 = *reinterpret_cast<const double2*>(bp + 32 * g);
-            const double2 v23 = *reinterpret_cast<const double2*>(bp + 32 * g + 16);
-            const uint2 cc = *reinterpret_cast<const uint2*>(bp + 128 + 8 * g);
-            const double x0 = xe[cc.x & 0xFFFFu], x1 = xe[cc.x >> 16];
-            const double x2 = xe[cc.y & 0xFFFFu], x3 = xe[cc.y >> 16];
-            acc = dsub(acc, dmul(v01.x, x0));
-            acc = dsub(acc, dmul(v01.y, x1));
-            acc = dsub(acc, dmul(v23.x, x2));
-            acc = dsub(acc, dmul(v23.y, x3));
-            if (fin == b + 1) finish();
-        }
-        if (!final_written && owns) xe[row] = acc;
+        // refill the slot of stage s with stage s + R
         __syncwarp();
-        p += bsz;
-        ro += bsz;
-        if (ro == ring_bytes) ro = 0;
-        release();
+        if (!end && s + R < nst) {
+            if (copier) cp_async16(ring + (s % R) * kStageBytes + 16 * lane, src + (size_t)(s + R) * kStageBytes);
+            cp_async_commit();
+            issued = s + R + 1;
+        }
     }
-    if (!ok) atomicCAS((int*)sh.abort, 0, kErrRingTimeout);
+    if (!ok || !end) atomicCAS((int*)sh.abort, 0, kErrBadBundle);
     // no copy may land after the sweep: the ring memory is reused
     cp_async_wait(0);
     __syncwarp();
@@ -353,26 +334,35 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
     }
     __syncthreads();
 
-    // ---- forcing (sb_fdm.c:146-152), written in row order ----
-    for (int idx = tid; idx < nenv * n; idx += blockDim.x) {
-        const int e = idx / n, i = idx % n;
-        const int env = sd.env0 + e, local = env - g.env0;
-        const double* D = ctx->Dst + (size_t)env * L.nd;
+    // ---- forcing (sb_fdm.c:146-152), written in row order: one thread per
+    // row for all envs of the slab, the row's coefficients loaded once ----
+    const int local0 = sd.env0 - g.env0;
+    for (int i = tid; i < n; i += blockDim.x) {
+        const double cap = g.cap[i], dirx = g.dirx[i], mc = g.mc[i];
         const int z = g.zone_of_row[i];
-        const double q = z >= 0 ? D[L.qdiv + z] : 0.0;
-        const double Ti = g.T[(size_t)local * ncv + i];
-        const double Mi = g.M[(size_t)local * n + i];
-        double b = dadd(dmul(g.cap[i], Ti), q);
-        b = dadd(b, dmul(amb_e[e], g.dirx[i]));
-        b = dadd(b, dmul(g.mc[i], Mi));
-        sh.X[(size_t)e * S + i] = b;
+        double Ti[kGroupLanes], Mi[kGroupLanes], qi[kGroupLanes];
+#pragma unroll
+        for (int e = 0; e < kGroupLanes; e++) {
+            if (e >= nenv) break;
+            Ti[e] = g.T[(size_t)(local0 + e) * ncv + i];
+            Mi[e] = g.M[(size_t)(local0 + e) * n + i];
+            qi[e] = z >= 0 ? ctx->Dst[(size_t)(sd.env0 + e) * L.nd + L.qdiv + z] : 0.0;
+        }
+#pragma unroll
+        for (int e = 0; e < kGroupLanes; e++) {
+            if (e >= nenv) break;
+            double b = dadd(dmul(cap, Ti[e]), qi[e]);
+            b = dadd(b, dmul(amb_e[e], dirx));
+            b = dadd(b, dmul(mc, Mi[e]));
+            sh.X[(size_t)e * S + i] = b;
+        }
     }
     __syncthreads();
 
     // ---- first solve ----
-    run_sweep(sh, g.fwd, B, S, n, 1);
+    if (tid < kSweepWarps * 32) run_sweep(sh, g.fwd, B, S, n, 1);
     __syncthreads();
-    run_sweep(sh, g.bwd, B, S, n, 2);
+    if (tid < kSweepWarps * 32) run_sweep(sh, g.bwd, B, S, n, 2);
     __syncthreads();
     if (*sh.abort) {   // uniform: read after the barrier
         if (tid == 0) set_error(ctx->status, *sh.abort);
@@ -388,21 +378,43 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
     int any_active = 0;
     for (int e = 0; e < nenv; e++) any_active |= active[e];
     if (k > 0 && any_active) {
-        for (int idx = tid; idx < nenv * k; idx += blockDim.x) {
-            const int e = idx / k, i = idx % k;
-            if (!active[e]) continue;
-            const double* xe = sh.X + (size_t)e * S;
-            double acc = 0.0;
-            for (int p = g.sn_p[i]; p < g.sn_p[i + 1]; p++) acc = dadd(acc, dmul(g.sn_x[p], xe[g.sn_pos[p]]));
-            const double* D = ctx->Dst + (size_t)(sd.env0 + e) * L.nd;
-            pw[e * k + i] = dmul(D[L.ag + i], dsub(D[L.aT + i], acc));
+        // sensed temperature of each coupled VAV: one thread per VAV for all
+        // envs, its terms fetched eight at a time, summed in order per env
+        for (int i = tid; i < k; i += blockDim.x) {
+            double acc[kGroupLanes];
+#pragma unroll
+            for (int e = 0; e < kGroupLanes; e++) acc[e] = 0.0;
+            const int p0 = g.sn_p[i], p1 = g.sn_p[i + 1];
+            for (int p = p0; p < p1; p += 8) {
+                double xv[8];
+                int pos[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    xv[u] = p + u < p1 ? g.sn_x[p + u] : 0.0;
+                    pos[u] = p + u < p1 ? g.sn_pos[p + u] : 0;
+                }
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    if (p + u >= p1) break;
+#pragma unroll
+                    for (int e = 0; e < kGroupLanes; e++)
+                        if (e < nenv) acc[e] = dadd(acc[e], dmul(xv[u], sh.X[(size_t)e * S + pos[u]]));
+                }
+            }
+#pragma unroll
+            for (int e = 0; e < kGroupLanes; e++) {
+                if (e >= nenv) break;
+                if (!active[e]) continue;
+                const double* D = ctx->Dst + (size_t)(sd.env0 + e) * L.nd;
+                pw[e * k + i] = dmul(D[L.ag + i], dsub(D[L.aT + i], acc[e]));
+            }
         }
     }
     // y -> the field array (row positions); the second solve adds to it
-    for (int idx = tid; idx < nenv * n; idx += blockDim.x) {
-        const int e = idx / n, i = idx % n;
-        const int local = sd.env0 + e - g.env0;
-        g.T[(size_t)local * ncv + i] = sh.X[(size_t)e * S + i];
+    for (int i = tid; i < n; i += blockDim.x) {
+#pragma unroll
+        for (int e = 0; e < kGroupLanes; e++)
+            if (e < nenv) g.T[(size_t)(local0 + e) * ncv + i] = sh.X[(size_t)e * S + i];
     }
     __syncthreads();
     if (k > 0 && any_active) {
@@ -432,25 +444,35 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
             }
             __syncthreads();
         }
-        // r = applied q, pulled per row in ascending column order; zero q skipped.
-        // The dense workspace overlapped the field: padding slots and unused
-        // envs are zeroed again (padded sweep terms read the zero slot).
-        for (int idx = tid; idx < B * S; idx += blockDim.x) {
-            const int e = idx / S, i = idx % S;
-            double acc = 0.0;
-            if (e < nenv && i < n && active[e]) {
-                for (int p = g.ap_rp[i]; p < g.ap_rp[i + 1]; p++) {
-                    const double qj = pw[e * k + g.ap_col[p]];
-                    if (qj == 0.0) continue;
-                    acc = dadd(acc, dmul(g.ap_x[p], qj));
+        // r = applied q, pulled per row in ascending column order; zero q
+        // skipped; one thread per row for all envs. The dense workspace
+        // overlapped the field: padding slots and unused envs are zeroed again
+        // (padded sweep terms read the zero slot).
+        for (int i = tid; i < n; i += blockDim.x) {
+            double acc[kGroupLanes];
+#pragma unroll
+            for (int e = 0; e < kGroupLanes; e++) acc[e] = 0.0;
+            const int p0 = g.ap_rp[i], p1 = g.ap_rp[i + 1];
+            for (int p = p0; p < p1; p++) {
+                const int col = g.ap_col[p];
+                const double xv = g.ap_x[p];
+#pragma unroll
+                for (int e = 0; e < kGroupLanes; e++) {
+                    if (e >= nenv) break;
+                    const double qj = pw[e * k + col];
+                    if (active[e] && qj != 0.0) acc[e] = dadd(acc[e], dmul(xv, qj));
                 }
             }
-            sh.X[(size_t)e * S + i] = acc;
+#pragma unroll
+            for (int e = 0; e < kGroupLanes; e++)
+                if (e < B) sh.X[(size_t)e * S + i] = e < nenv && active[e] ? acc[e] : 0.0;
         }
+        for (int idx = tid; idx < B * (S - n); idx += blockDim.x)
+            sh.X[(size_t)(idx / (S - n)) * S + n + idx % (S - n)] = 0.0;
         __syncthreads();
-        run_sweep(sh, g.fwd, B, S, n, 3);
+        if (tid < kSweepWarps * 32) run_sweep(sh, g.fwd, B, S, n, 3);
         __syncthreads();
-        run_sweep(sh, g.bwd, B, S, n, 4);
+        if (tid < kSweepWarps * 32) run_sweep(sh, g.bwd, B, S, n, 4);
         __syncthreads();
         if (*sh.abort) {
             if (tid == 0) set_error(ctx->status, *sh.abort);
@@ -458,15 +480,24 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
         }
     }
 
-    // ---- interior mass + field (sb_fdm.c:183-187) ----
-    for (int idx = tid; idx < nenv * n; idx += blockDim.x) {
-        const int e = idx / n, i = idx % n;
-        const int local = sd.env0 + e - g.env0;
-        double y = g.T[(size_t)local * ncv + i];
-        if (k > 0 && active[e]) y = dadd(y, sh.X[(size_t)e * S + i]);
-        const double m = g.M[(size_t)local * n + i];
-        g.M[(size_t)local * n + i] = dadd(dmul(m, g.ret[i]), dmul(g.gain[i], y));
-        g.T[(size_t)local * ncv + i] = y;
+    // ---- interior mass + field (sb_fdm.c:183-187): one thread per row ----
+    for (int i = tid; i < n; i += blockDim.x) {
+        const double ret = g.ret[i], gain = g.gain[i];
+        double y[kGroupLanes], m[kGroupLanes];
+#pragma unroll
+        for (int e = 0; e < kGroupLanes; e++) {
+            if (e >= nenv) break;
+            y[e] = g.T[(size_t)(local0 + e) * ncv + i];
+            m[e] = g.M[(size_t)(local0 + e) * n + i];
+        }
+#pragma unroll
+        for (int e = 0; e < kGroupLanes; e++) {
+            if (e >= nenv) break;
+            double ye = y[e];
+            if (k > 0 && active[e]) ye = dadd(ye, sh.X[(size_t)e * S + i]);
+            g.M[(size_t)(local0 + e) * n + i] = dadd(dmul(m[e], ret), dmul(gain, ye));
+            g.T[(size_t)(local0 + e) * ncv + i] = ye;
+        }
     }
     for (int idx = tid; idx < nenv * (ncv - n); idx += blockDim.x) {
         const int e = idx / (ncv - n), i = n + idx % (ncv - n);

@@ -45,51 +45,54 @@ enum : int {
 
 // Solve schedule ("sweep program"), built on the host (sweep_sched.cpp).
 //
-// Each of the kSweepWarps warps of a solve CTA runs its own stream of bundles.
-// A bundle advances up to kBundleRows rows of the triangular factor in lock
-// step: lane group g (kGroupLanes lanes, one per env of the slab) owns row g.
-// Every term subtracts val * x[col] from the row's accumulator, in the order
-// the reference's column push would deliver it (bit-exact). Before a bundle
-// starts, the warp waits (acquire) for the ready flags of the rows listed in
-// it; the host lists rows whose completion implies every column the bundle
-// reads that this warp has not produced or waited for itself. A row that
-// another warp reads is published with a release store of the sweep's epoch.
+// Each of the kSweepWarps warps of a solve CTA runs its own program. The warp
+// is four lane groups (kGroupLanes lanes each, one per env of the slab); each
+// group works through its own sequence of rows, and the groups advance in
+// lock step, four terms per group per term record. Every term subtracts
+// val * x[col] from the group's accumulator, in the order the reference's
+// column push would deliver it (bit-exact). Control records switch groups to
+// new rows: they finish the ending rows (backward sweep: divide by the
+// diagonal; publish with a release store of the sweep's epoch where another
+// warp reads them), then wait (acquire) for the rows of other warps that the
+// new rows read, then load the new rows' accumulators.
 //
-// Stream layout (16-byte items; a bundle never wraps around the warp's ring of
-// ring_stages x kStageBytes bytes):
-//   BundleHeader (16 B)
-//   npre x u16 row[8] (16 B each): rows to wait for (entry n = no row; its
-//        flag is always set)
-//   [double diag[4]] (32 B) when any divide bit is set (backward sweep)
-//   nblk x TermBlock (160 B): double val[4 groups][4 steps], u16 col[4][4]
-//   ... next bundle ...
-// A header with kBundleSkip continues the stream at the start of the ring; a
-// header with kBundleEnd ends it. Streams are padded to whole stages.
-constexpr int kSweepWarps = kSolveThreads / 32;
+// A program is a sequence of kRecordBytes records, three to a ring stage;
+// it starts with a control record, and a control record with kCtrlEnd ends it.
+constexpr int kSweepWarps = kSolveThreads / 32;   // warps that run sweep programs
 constexpr int kGroupLanes = 8;           // envs per lane group (slab_envs <= 8)
 constexpr int kBundleRows = 4;           // lane groups per warp
-constexpr int kTermSteps = 4;            // terms per group per TermBlock
-constexpr int kTermBlockBytes = kBundleRows * kTermSteps * 10;   // 160
-constexpr int kStageBytes = 512;         // one copy into a warp's ring: 16 bytes per lane
+constexpr int kTermSteps = 4;            // terms per group per term record
+constexpr int kRecordBytes = 160;
+constexpr int kRecordsPerStage = 3;
+constexpr int kStageBytes = kRecordBytes * kRecordsPerStage;   // one copy into a warp's ring
 constexpr int kStagesMin = 4;            // ring depth per warp (stages), chosen per group
 constexpr int kStagesMax = 8;
-constexpr int kMaxBundleBytes = 960;     // a bundle spans at most 3 stages
-constexpr int kMaxPreItems = 2;          // pre-wait items per bundle (8 rows each)
-constexpr uint16_t kBundleEnd = 0x8000;  // BundleHeader.flags: end of stream
-constexpr uint16_t kBundleSkip = 0x4000; // BundleHeader.flags: continue at ring offset 0
-constexpr uint8_t kFinNever = 0xFF;      // BundleHeader.fin: row continues in a later bundle
+constexpr int kCtrlWaits = 56;           // wait rows per control record
+constexpr uint16_t kNextIsCtrl = 0x8000; // TermRecord.col[g][0]: a control record follows
+constexpr uint16_t kColMask = 0x7FFF;
+// ControlRecord.gflags bits
+constexpr uint8_t kGSwitch = 1;          // the group ends its segment and starts row[g]
+constexpr uint8_t kGFinal = 2;           // the ending segment completes its row
+constexpr uint8_t kGDivide = 4;          // ... and divides it by diag[g] (backward sweep)
+constexpr uint8_t kGPublish = 8;         // ... and publishes it
+// ControlRecord.flags bits
+constexpr uint8_t kCtrlNext = 1;         // the next record is a control record too
+constexpr uint8_t kCtrlEnd = 2;          // the program ends after this record
 
-struct BundleHeader {
-    uint16_t row[kBundleRows];   // row of each group; n = the always-zero padding slot
-    uint16_t nblk;               // TermBlocks that follow
-    uint16_t flags;              // bits 0-3 publish row g, 4-7 divide row g, 8-11 npre, 14 skip, 15 end
-    uint8_t fin[kBundleRows];    // row g is final after this many blocks (kFinNever: not here)
+struct TermRecord {
+    double val[kBundleRows][kTermSteps];
+    uint16_t col[kBundleRows][kTermSteps];   // column; n = the always-zero padding slot
 };
-static_assert(sizeof(BundleHeader) == 16, "bundle header is one 16-byte item");
-
-SB_HD constexpr int bundle_bytes(int npre, bool divides, int nblk) {
-    return 16 + 16 * npre + (divides ? 32 : 0) + kTermBlockBytes * nblk;
-}
+struct ControlRecord {
+    uint16_t row[kBundleRows];   // new row of a switching group (n: the group idles)
+    uint8_t gflags[kBundleRows];
+    uint8_t nwait;
+    uint8_t flags;
+    uint16_t pad;
+    double diag[kBundleRows];
+    uint16_t wait[kCtrlWaits];   // rows to acquire before the new rows start
+};
+static_assert(sizeof(TermRecord) == kRecordBytes && sizeof(ControlRecord) == kRecordBytes, "record size");
 
 // Shared memory of a solve CTA: the slab's fields [B][stride] | the warps'
 // rings [kSweepWarps][ring_stages][kStageBytes] | ready flags [n + 1] | misc.

@@ -1,20 +1,23 @@
 // Sweep programs for the solve kernel: a static list schedule of the
-// triangular factor's rows over the warps of one solve CTA.
+// triangular factor's rows over the warps (and their four lane groups) of one
+// solve CTA.
 //
 // The reference solves L y = b, U z = y by column push
 // (complete_port/csim/sb_lu.c:38-63): column j, once final, is subtracted from
 // every row below (L) or above (U) it. Here every row pulls its terms itself,
 // in exactly the order the push would deliver them, so the rounding sequence
-// of each row is unchanged. Rows are spread over the warps by simulating the
-// sweep with a simple cost model; the model decides only speed, never
-// results: a bundle reads another warp's row only after waiting for the ready
-// flag of that row or of a row whose completion implies it.
+// of each row is unchanged. Rows are spread over the warps and lane groups by
+// simulating the sweep with a simple cost model; the model decides only
+// speed, never results. A lane group starts a run of a row's terms ("segment")
+// only at a control record, and only with terms whose columns are final by
+// then: rows finished earlier by this warp, or rows of other warps covered by
+// the record's waits (a wait for a row also covers every row it depends on).
 //
-// Deadlock freedom: a bundle waits only for rows whose final piece lies in a
-// bundle created earlier in the simulation (smaller sequence number), and
-// every warp runs its bundles in creation order. The unfinished bundle with
-// the smallest sequence number therefore always has its inputs done and its
-// warp at it.
+// Deadlock freedom: a control record waits only for rows finished at control
+// records created earlier in the simulation (smaller sequence number), and
+// every warp runs its records in creation order. The unfinished control
+// record with the smallest sequence number therefore always finds its waits
+// satisfied and its warp at it; term records never wait.
 #include "sweep_sched.h"
 
 #include <algorithm>
@@ -27,29 +30,13 @@ namespace sbenv {
 namespace {
 
 // Cost model of one warp, in cycles. Only used to order the work.
-constexpr double kC0 = 120;    // bundle start: stage waits, header, pre-waits, row loads
-constexpr double kCBlk = 60;   // one TermBlock (four terms of four rows)
-constexpr double kCEnd = 30;   // bundle end: stores, warp barrier
-constexpr double kC2 = 80;     // release store until another warp's acquire sees it
-constexpr double kCPub = 30;   // publishing a row
-constexpr double kSlack = 150; // a row may be picked this long before its next input is ready
-constexpr int kPartnerPool = 16;   // bundle partners are chosen among this many top rows
-constexpr int kMaxPre = 8 * kMaxPreItems;
-constexpr int kMaxBlk = (kMaxBundleBytes - bundle_bytes(kMaxPreItems, true, 0)) / kTermBlockBytes;
+constexpr double kCCtrl = 100;  // a control record: finishes, waits, new rows
+constexpr double kCBlk = 40;    // a term record
+constexpr double kC2 = 80;      // release store until another warp's acquire sees it
+constexpr double kSlack = 150;  // a row may be picked this long before its next input is ready
+constexpr int kMinSeg = 8;       // shortest segment worth a control record (unless the row ends sooner)
+constexpr double kCritical = 0.85;   // rows within this fraction of the top priority start at any length
 constexpr int kUnsched = std::numeric_limits<int>::max();
-static_assert(kMaxBlk >= 1, "a bundle must hold one term block");
-
-struct Piece {
-    int row = -1, q0 = 0, q1 = 0;
-    bool fin = false;
-    int fin_blk = kFinNever;
-};
-
-struct Bundle {
-    int nblk = 0;
-    Piece p[kBundleRows];
-    std::vector<int> pre;   // rows the warp waits for before the bundle
-};
 
 inline bool test(const uint64_t* s, int i) { return (s[i >> 6] >> (i & 63)) & 1u; }
 inline void set(uint64_t* s, int i) { s[i >> 6] |= uint64_t(1) << (i & 63); }
@@ -57,15 +44,29 @@ inline void orr(uint64_t* d, const uint64_t* s, int w) {
     for (int k = 0; k < w; k++) d[k] |= s[k];
 }
 
+struct Group {
+    int row = -1;     // -1: idle
+    int q = 0, qend = 0;
+};
+
+struct WarpProg {
+    double T = 0;
+    Group g[kBundleRows];
+    std::vector<uint8_t> rec;   // records, kRecordBytes each
+    int last = -1;              // index of the last record
+    bool last_ctrl = false;
+    bool ended = false;
+    bool idle = false;          // found nothing to do at T in the current state
+};
+
 }  // namespace
 
 std::string build_sweep(int n, const std::vector<std::vector<std::pair<int, double>>>& terms, bool backward,
                         const std::vector<double>& diag, int ring_stages, HostSweep& out) {
     out = HostSweep();
-    if (n <= 0 || n >= 0xFFFF) return "factor too large for the sweep format";
+    if (n <= 0 || n >= (int)kColMask) return "factor too large for the sweep format";
     if (ring_stages < kStagesMin || ring_stages > kStagesMax) return "unsupported ring depth";
     out.ring_stages = ring_stages;
-    const size_t ring_bytes = (size_t)ring_stages * kStageBytes;
     const int W = kSweepWarps;
     std::vector<int> nt(n);
     std::vector<char> need(n);
@@ -89,7 +90,7 @@ std::string build_sweep(int n, const std::vector<std::vector<std::pair<int, doub
         const int i = backward ? s : n - 1 - s;   // dependents first
         double best = 0.0;
         for (int d : dependents[i]) best = std::max(best, prio[d]);
-        prio[i] = best + kC2 + kC0 + kCBlk * std::ceil(nt[i] / (double)kTermSteps);
+        prio[i] = best + kC2 + kCCtrl + kCBlk * std::ceil(nt[i] / (double)kTermSteps);
     }
 
     // closure[i]: rows that are final whenever row i is (i and, recursively,
@@ -152,6 +153,7 @@ std::string build_sweep(int n, const std::vector<std::vector<std::pair<int, doub
     // ---- list-scheduling simulation ----
     std::vector<double> done(n, std::numeric_limits<double>::infinity());
     std::vector<int> fseq(n, kUnsched), owner(n, -1), prog(n, 0);
+    std::vector<char> in_use(n, 0), waited(n, 0);
     std::vector<int> open;
     std::vector<uint64_t> K((size_t)W * WD, 0);   // per warp: rows it knows final
     for (int w = 0; w < W; w++) set(K.data() + (size_t)w * WD, n);
@@ -163,28 +165,78 @@ std::string build_sweep(int n, const std::vector<std::vector<std::pair<int, doub
             for (int w = 0; w < W; w++) set(K.data() + (size_t)w * WD, i);
         }
     }
-    std::vector<double> free_t(W, 0.0);
-    std::vector<std::vector<Bundle>> wb(W);
+    std::vector<WarpProg> wp(W);
     std::vector<int> cand;
     std::vector<uint64_t> Kb(WD);
-    std::vector<char> waited(n, 0);
     int seq = 0;
     int64_t guard = 0;
-    // idle[w]: w found no work at free_t[w] in the current state (reset whenever
-    // a bundle is created); among warps free at the same time, busy ones go first
-    std::vector<char> idle(W, 0);
-    while (remaining > 0) {
-        if (++guard > 64LL * n + 100000) return "sweep schedule did not converge";
-        int w = 0;
-        for (int q = 1; q < W; q++)
-            if (free_t[q] < free_t[w] || (free_t[q] == free_t[w] && idle[w] && !idle[q])) w = q;
-        const double t = free_t[w];
+
+    auto new_record = [&](WarpProg& P, bool ctrl) -> uint8_t* {
+        if (P.last >= 0) {   // tell the previous record what follows
+            uint8_t* prev = P.rec.data() + (size_t)P.last * kRecordBytes;
+            if (ctrl) {
+                if (P.last_ctrl) reinterpret_cast<ControlRecord*>(prev)->flags |= kCtrlNext;
+                else
+                    for (int g = 0; g < kBundleRows; g++) reinterpret_cast<TermRecord*>(prev)->col[g][0] |= kNextIsCtrl;
+            }
+        }
+        P.rec.resize(P.rec.size() + kRecordBytes, 0);
+        P.last++;
+        P.last_ctrl = ctrl;
+        return P.rec.data() + (size_t)P.last * kRecordBytes;
+    };
+    auto may_take = [&](int w, int r) {
+        return (owner[r] == -1 || owner[r] == w) && (home[r] == -1 || home[r] == w) && !in_use[r];
+    };
+
+    while (true) {
+        if (++guard > 256LL * n + 100000) return "sweep schedule did not converge";
+        // the warp with the earliest time (busy before idle on ties); done when all ended
+        int w = -1;
+        for (int q = 0; q < W; q++) {
+            if (wp[q].ended) continue;
+            if (w < 0 || wp[q].T < wp[w].T || (wp[q].T == wp[w].T && wp[w].idle && !wp[q].idle)) w = q;
+        }
+        if (w < 0) break;
+        WarpProg& P = wp[w];
+        const double t = P.T;
         uint64_t* Kw = K.data() + (size_t)w * WD;
+
+        // (a) segments that ended: rows final or paused
+        ControlRecord cr;
+        memset(&cr, 0, sizeof(cr));
+        for (int g = 0; g < kBundleRows; g++) cr.row[g] = (uint16_t)n;
+        bool any = false;
+        for (int g = 0; g < kBundleRows; g++) {
+            Group& G = P.g[g];
+            if (G.row < 0 || G.q < G.qend) continue;
+            const int r = G.row;
+            prog[r] = G.q;
+            in_use[r] = 0;
+            cr.gflags[g] = kGSwitch;
+            if (G.q == nt[r]) {
+                cr.gflags[g] |= kGFinal;
+                if (backward) {
+                    cr.gflags[g] |= kGDivide;
+                    cr.diag[g] = diag[r];
+                }
+                done[r] = t + kCCtrl;
+                fseq[r] = seq;
+                set(Kw, r);
+                remaining--;
+            }
+            G.row = -1;
+            any = true;
+        }
+        if (any)
+            open.erase(std::remove_if(open.begin(), open.end(), [&](int r) { return fseq[r] != kUnsched; }),
+                       open.end());
+
+        // (b) new segments for the free groups, most urgent rows first
         cand.clear();
         double next_event = std::numeric_limits<double>::infinity();
         for (int r : open) {
-            if (owner[r] != -1 && owner[r] != w) continue;
-            if (home[r] != -1 && home[r] != w) continue;
+            if (!may_take(w, r)) continue;
             if (prog[r] < nt[r]) {
                 const int c = terms[r][prog[r]].first;
                 if (!test(Kw, c)) {
@@ -194,182 +246,159 @@ std::string build_sweep(int n, const std::vector<std::vector<std::pair<int, doub
             }
             cand.push_back(r);
         }
-        if (cand.empty()) {
-            bool other_now = false;
-            for (int q = 0; q < W; q++) {
-                if (q != w && free_t[q] > t) next_event = std::min(next_event, free_t[q]);
-                other_now |= (q != w && free_t[q] == t && !idle[q]);
-            }
-            if (other_now) { idle[w] = 1; continue; }
-            if (!std::isfinite(next_event)) return "sweep schedule deadlocked";
-            free_t[w] = next_event;
-            idle[w] = 0;
-            continue;
-        }
-        std::fill(idle.begin(), idle.end(), 0);
-        // the most urgent row, then partners of similar remaining length among
-        // the next most urgent ones (lock-step rows pad to the longest)
-        const int pool_n = std::min<int>(kPartnerPool, (int)cand.size());
-        std::partial_sort(cand.begin(), cand.begin() + pool_n, cand.end(), [&](int a, int b) {
+        std::sort(cand.begin(), cand.end(), [&](int a, int b) {
             if (prio[a] != prio[b]) return prio[a] > prio[b];
             return backward ? a > b : a < b;
         });
-        const int take = std::min<int>(kBundleRows, pool_n);
-        {
-            const int len0 = std::min(nt[cand[0]] - prog[cand[0]], kMaxBlk * kTermSteps);
-            std::stable_sort(cand.begin() + 1, cand.begin() + pool_n, [&](int a, int b) {
-                const int la = std::min(nt[a] - prog[a], kMaxBlk * kTermSteps);
-                const int lb = std::min(nt[b] - prog[b], kMaxBlk * kTermSteps);
-                return std::abs(la - len0) < std::abs(lb - len0);
-            });
-        }
-        // the bundle starts once the first inputs of its rows are ready
-        double T0 = t;
-        for (int g = 0; g < take; g++) {
-            const int r = cand[g];
-            if (prog[r] < nt[r]) {
-                const int c = terms[r][prog[r]].first;
-                if (!test(Kw, c)) T0 = std::max(T0, done[c] + kC2);
-            }
-        }
-        // every group takes the terms whose inputs are ready at T0: known to the
-        // warp, or covered by a pre-wait (the highest row above the input that is
-        // also ready, so that one flag covers as much as possible)
-        Bundle B;
+        double top_prio = 0.0;
+        for (int r : open) top_prio = std::max(top_prio, prio[r]);
         std::copy(Kw, Kw + WD, Kb.begin());
-        int steps_max = 0, ng = 0;
-        for (int g = 0; g < take; g++) {
-            const int r = cand[g];
-            int q = prog[r];
-            int steps = 0;
-            while (q < nt[r] && steps < kMaxBlk * kTermSteps) {
-                const int c = terms[r][q].first;
-                if (!test(Kb.data(), c)) {
-                    if (!(fseq[c] < seq && done[c] + kC2 <= T0) || (int)B.pre.size() >= kMaxPre) break;
-                    int top = c;
-                    while (parent[top] >= 0 && fseq[parent[top]] < seq && done[parent[top]] + kC2 <= T0)
-                        top = parent[top];
-                    B.pre.push_back(top);
-                    orr(Kb.data(), clo.data() + (size_t)top * WD, WD);
+        std::vector<int> waits;
+        double ready = t;
+        size_t ci = 0;
+        for (int g = 0; g < kBundleRows && ci < cand.size(); g++) {
+            if (P.g[g].row >= 0) continue;
+            while (ci < cand.size()) {
+                const int r = cand[ci++];
+                int q = prog[r];
+                double rdy = ready;
+                std::vector<int> wnew;
+                while (q < nt[r]) {
+                    const int c = terms[r][q].first;
+                    if (!test(Kb.data(), c)) {
+                        if (!(fseq[c] < seq && done[c] + kC2 <= t + kSlack) ||
+                            (int)(waits.size() + wnew.size()) >= kCtrlWaits)
+                            break;
+                        int top = c;
+                        while (parent[top] >= 0 && fseq[parent[top]] < seq && done[parent[top]] + kC2 <= t + kSlack)
+                            top = parent[top];
+                        wnew.push_back(top);
+                        rdy = std::max(rdy, done[top] + kC2);
+                        orr(Kb.data(), clo.data() + (size_t)top * WD, WD);
+                    }
+                    q++;
                 }
-                q++;
-                steps++;
+                if (q == prog[r] && q < nt[r]) continue;   // not a single term ready after all
+                if (q < nt[r] && q - prog[r] < kMinSeg && prio[r] < kCritical * top_prio) {
+                    // too short a run for an off-critical row: its waits are not kept
+                    std::copy(Kw, Kw + WD, Kb.begin());
+                    for (int x : waits) orr(Kb.data(), clo.data() + (size_t)x * WD, WD);
+                    continue;
+                }
+                for (int x : wnew) waits.push_back(x);
+                ready = rdy;
+                P.g[g] = Group{r, prog[r], q};
+                in_use[r] = 1;
+                owner[r] = w;
+                cr.gflags[g] |= kGSwitch;
+                cr.row[g] = (uint16_t)r;
+                any = true;
+                out.pieces++;
+                break;
             }
-            const bool fin = q == nt[r];
-            if (steps == 0 && !fin) continue;   // nothing ready for this row after all
-            Piece& p = B.p[ng++];
-            p.row = r;
-            p.q0 = prog[r];
-            p.q1 = q;
-            p.fin = fin;
-            p.fin_blk = fin ? (steps + kTermSteps - 1) / kTermSteps : kFinNever;
-            steps_max = std::max(steps_max, steps);
         }
-        B.nblk = (steps_max + kTermSteps - 1) / kTermSteps;
-        for (int top : B.pre) waited[top] = 1;
-        std::copy(Kb.begin(), Kb.end(), Kw);
-        const double tstart = T0 + kC0;
-        for (int g = 0; g < ng; g++) {
-            Piece& p = B.p[g];
-            owner[p.row] = w;
-            prog[p.row] = p.q1;
-            out.pieces++;
-            if (p.fin) {
-                done[p.row] = tstart + p.fin_blk * kCBlk + kCPub;
-                fseq[p.row] = seq;
-                set(Kw, p.row);
-                remaining--;
+        if (any || !waits.empty()) {
+            cr.nwait = (uint8_t)waits.size();
+            for (size_t i = 0; i < waits.size(); i++) {
+                cr.wait[i] = (uint16_t)waits[i];
+                waited[waits[i]] = 1;
             }
+            out.prewaits += (int64_t)waits.size();
+            std::copy(Kb.begin(), Kb.end(), Kw);
+            memcpy(new_record(P, true), &cr, sizeof(cr));
+            P.T = std::max(t, ready) + kCCtrl;
+            out.sim_cycles = std::max(out.sim_cycles, P.T);
+            seq++;
+            for (auto& x : wp) x.idle = false;
         }
-        out.prewaits += (int64_t)B.pre.size();
-        open.erase(std::remove_if(open.begin(), open.end(), [&](int r) { return fseq[r] != kUnsched; }),
-                   open.end());
-        free_t[w] = tstart + B.nblk * kCBlk + kCEnd;
-        out.sim_cycles = std::max(out.sim_cycles, free_t[w]);
-        wb[w].push_back(std::move(B));
-        seq++;
-    }
-
-    // ---- serialise ----
-    std::vector<uint8_t> stream;
-    auto put = [&](const void* src, size_t sz) {
-        const size_t at = stream.size();
-        stream.resize(at + sz);
-        memcpy(stream.data() + at, src, sz);
-    };
-    for (int w = 0; w < W; w++) {
-        stream.clear();
-        for (const Bundle& B : wb[w]) {
-            BundleHeader h;
-            memset(&h, 0, sizeof(h));
-            h.nblk = (uint16_t)B.nblk;
-            double dg[kBundleRows] = {1.0, 1.0, 1.0, 1.0};
-            const int npre = ((int)B.pre.size() + 7) / 8;
-            for (int g = 0; g < kBundleRows; g++) {
-                const Piece& p = B.p[g];
-                h.row[g] = (uint16_t)(p.row < 0 ? n : p.row);
-                h.fin[g] = p.row >= 0 && p.fin ? (uint8_t)p.fin_blk : kFinNever;
-                if (p.row >= 0 && p.fin && waited[p.row]) { h.flags |= (uint16_t)(1u << g); out.publishes++; }
-                if (p.row >= 0 && p.fin && backward) {
-                    h.flags |= (uint16_t)(1u << (4 + g));
-                    dg[g] = diag[p.row];
-                }
+        // (c) run term records until the first active segment ends
+        int nb = std::numeric_limits<int>::max();
+        bool active = false;
+        for (int g = 0; g < kBundleRows; g++)
+            if (P.g[g].row >= 0) {
+                active = true;
+                nb = std::min(nb, (P.g[g].qend - P.g[g].q + kTermSteps - 1) / kTermSteps);
             }
-            h.flags |= (uint16_t)(npre << 8);
-            const size_t bytes = (size_t)bundle_bytes(npre, (h.flags & 0xF0) != 0, B.nblk);
-            if (bytes > (size_t)kMaxBundleBytes) return "sweep bundle too large";
-            const size_t ro = stream.size() % ring_bytes;
-            if (ro + bytes > ring_bytes) {   // continue at the start of the ring
-                BundleHeader skip;
-                memset(&skip, 0, sizeof(skip));
-                skip.flags = kBundleSkip;
-                for (int g = 0; g < kBundleRows; g++) skip.fin[g] = kFinNever;
-                put(&skip, sizeof(skip));
-                stream.resize(stream.size() + (ring_bytes - ro - sizeof(skip)), 0);
-            }
-            put(&h, sizeof(h));
-            for (int it = 0; it < npre; it++) {
-                uint16_t rows8[8];
-                for (int k = 0; k < 8; k++) {
-                    const size_t at = (size_t)it * 8 + k;
-                    rows8[k] = (uint16_t)(at < B.pre.size() ? B.pre[at] : n);
-                }
-                put(rows8, sizeof(rows8));
-            }
-            if (h.flags & 0xF0) put(dg, sizeof(dg));
-            for (int b = 0; b < B.nblk; b++) {
-                double val[kBundleRows][kTermSteps];
-                uint16_t col[kBundleRows][kTermSteps];
+        if (active) {
+            for (int b = 0; b < nb; b++) {
+                TermRecord tr;
                 for (int g = 0; g < kBundleRows; g++)
                     for (int s = 0; s < kTermSteps; s++) {
-                        const Piece& p = B.p[g];
-                        const int a = b * kTermSteps + s;
-                        if (p.row >= 0 && a < p.q1 - p.q0) {
-                            const auto& tm = terms[p.row][p.q0 + a];
-                            val[g][s] = tm.second;
-                            col[g][s] = (uint16_t)tm.first;
+                        Group& G = P.g[g];
+                        if (G.row >= 0 && G.q < G.qend) {
+                            const auto& tm = terms[G.row][G.q++];
+                            tr.val[g][s] = tm.second;
+                            tr.col[g][s] = (uint16_t)tm.first;
                         } else {   // padding: 0 * x[n] (the zero slot) leaves the row unchanged
-                            val[g][s] = 0.0;
-                            col[g][s] = (uint16_t)n;
+                            tr.val[g][s] = 0.0;
+                            tr.col[g][s] = (uint16_t)n;
                         }
                     }
-                uint8_t blk[kTermBlockBytes];
-                memcpy(blk, val, sizeof(val));
-                memcpy(blk + sizeof(val), col, sizeof(col));
-                put(blk, sizeof(blk));
+                memcpy(new_record(P, false), &tr, sizeof(tr));
                 out.blocks++;
             }
-            out.bundles++;
+            P.T += nb * kCBlk;
+            out.sim_cycles = std::max(out.sim_cycles, P.T);
+            continue;
         }
-        BundleHeader end;
-        memset(&end, 0, sizeof(end));
-        end.flags = kBundleEnd;
-        for (int g = 0; g < kBundleRows; g++) end.fin[g] = kFinNever;
-        put(&end, sizeof(end));
-        stream.resize((stream.size() + kStageBytes - 1) / kStageBytes * kStageBytes, 0);
+        // (d) nothing running: end, or wait for the next event
+        bool future = false;
+        for (int r : open)
+            if ((owner[r] == -1 || owner[r] == w) && (home[r] == -1 || home[r] == w)) { future = true; break; }
+        if (!future) {
+            ControlRecord end;
+            memset(&end, 0, sizeof(end));
+            for (int g = 0; g < kBundleRows; g++) end.row[g] = (uint16_t)n;
+            end.flags = kCtrlEnd;
+            memcpy(new_record(P, true), &end, sizeof(end));
+            P.ended = true;
+            continue;
+        }
+        bool other_now = false;
+        for (int q = 0; q < W; q++) {
+            if (q == w || wp[q].ended) continue;
+            if (wp[q].T > t) next_event = std::min(next_event, wp[q].T);
+            other_now |= (wp[q].T == t && !wp[q].idle);
+        }
+        if (any) continue;   // the control record moved time on
+        if (other_now) { P.idle = true; continue; }
+        if (!std::isfinite(next_event)) return "sweep schedule deadlocked";
+        P.T = next_event;
+        P.idle = false;
+    }
+    if (remaining != 0) return "sweep schedule left rows unfinished";
+
+    // ---- serialise; a row another warp waits for is published where it
+    // finishes (a control record finishes the row its group was given before) ----
+    for (int w = 0; w < W; w++) {
+        WarpProg& P = wp[w];
+        // the row a group finishes at a control record is the row it was given earlier
+        int cur[kBundleRows];
+        for (int g = 0; g < kBundleRows; g++) cur[g] = -1;
+        bool ctrl = true;
+        for (int i = 0; i <= P.last; i++) {
+            uint8_t* r = P.rec.data() + (size_t)i * kRecordBytes;
+            out.bundles += ctrl ? 1 : 0;
+            if (ctrl) {
+                ControlRecord* c = reinterpret_cast<ControlRecord*>(r);
+                for (int g = 0; g < kBundleRows; g++) {
+                    if (!(c->gflags[g] & kGSwitch)) continue;
+                    if ((c->gflags[g] & kGFinal) && cur[g] >= 0 && waited[cur[g]]) {
+                        c->gflags[g] |= kGPublish;
+                        out.publishes++;
+                    }
+                    cur[g] = c->row[g] < n ? c->row[g] : -1;
+                }
+                ctrl = (c->flags & kCtrlNext) != 0;
+            } else {
+                ctrl = (reinterpret_cast<TermRecord*>(r)->col[0][0] & kNextIsCtrl) != 0;
+            }
+        }
+        const size_t stages = (P.rec.size() + kStageBytes - 1) / kStageBytes;
+        P.rec.resize(stages * kStageBytes, 0);
         out.warp_off[w] = (uint32_t)(out.bytes.size() / kStageBytes);
-        out.warp_stages[w] = (uint32_t)(stream.size() / kStageBytes);
-        out.bytes.insert(out.bytes.end(), stream.begin(), stream.end());
+        out.warp_stages[w] = (uint32_t)stages;
+        out.bytes.insert(out.bytes.end(), P.rec.begin(), P.rec.end());
     }
     return "";
 }

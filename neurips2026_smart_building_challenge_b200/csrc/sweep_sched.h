@@ -14,7 +14,8 @@ struct HostSweep {
     uint32_t warp_off[kSweepWarps] = {};    // stage index where warp w's stream starts
     uint32_t warp_stages[kSweepWarps] = {}; // stages in warp w's stream
     int ring_stages = 0;                    // ring depth the streams were laid out for
-    // statistics of the schedule
+    // statistics of the schedule: terms, control records (bundles), term
+    // records (blocks), waits, published rows, row segments (pieces)
     int64_t terms = 0, bundles = 0, blocks = 0, prewaits = 0, publishes = 0, pieces = 0;
     double sim_cycles = 0;                  // modelled length of the sweep (cycles of one warp)
 };

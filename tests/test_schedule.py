@@ -13,13 +13,16 @@ import pytest
 
 from sbb_read import Blob
 
-NW, STAGE, MAX_BUNDLE = 16, 512, 960
-END, SKIP, FIN_NEVER = 0x8000, 0x4000, 0xFF
+REC, STAGE = 160, 480
+NEXT_CTRL, COL_MASK = 0x8000, 0x7FFF
+G_SWITCH, G_FINAL, G_DIVIDE, G_PUBLISH = 1, 2, 4, 8
+C_NEXT, C_END = 1, 2
 
 
 def _programs(lib, blob, sweep, ring_stages):
+    NW = lib.sb_sweep_warps()
     used = ctypes.c_size_t()
-    stages = (ctypes.c_uint32 * NW)()
+    stages = (ctypes.c_uint32 * 32)()
     lib.sb_solve_schedule.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t,
                                       ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_uint32)]
     b = str(blob).encode()
@@ -35,63 +38,55 @@ def _programs(lib, blob, sweep, ring_stages):
     return out
 
 
-def _parse(stream, n, backward, ring_stages):
-    """Bundles of one warp stream. A bundle never wraps around the warp's ring
-    (ring_stages x 512 bytes): a skip header moves the stream to the ring's
-    start (zero bytes)."""
-    RING = ring_stages * STAGE
-    pos, bundles = 0, []
-    while True:
-        hdr = stream[pos:pos + 16]
-        assert len(hdr) == 16, "stream ends without an end marker"
-        rows = struct.unpack_from("<4H", hdr)
-        nblk, flags = struct.unpack_from("<HH", hdr, 8)
-        fin = list(hdr[12:16])
-        if flags & END:
-            pos += 16
-            break
-        if flags & SKIP:
-            ro = pos % RING
-            assert not any(stream[pos + 16:pos + RING - ro])
-            pos += RING - ro
-            continue
-        assert flags & 0x3000 == 0
-        assert all(r <= n for r in rows)
-        assert all(f == FIN_NEVER or f <= nblk for f in fin)
-        npre = (flags >> 8) & 0xF
-        size = 16 + 16 * npre + (32 if flags & 0xF0 else 0) + 160 * nblk
-        assert size <= MAX_BUNDLE and pos % RING + size <= RING, "bundle too large or wraps the ring"
-        off = pos + 16
-        pre = list(struct.unpack_from(f"<{8 * npre}H", stream, off)) if npre else []
-        off += 16 * npre
-        diag = [1.0] * 4
-        if flags & 0xF0:
-            diag = list(struct.unpack_from("<4d", stream, off))
-            off += 32
-        assert bool(flags & 0xF0) == (backward and any(f != FIN_NEVER for f in fin))
-        blocks = []
-        for _ in range(nblk):
-            vals = np.frombuffer(stream, "<f8", 16, off).reshape(4, 4)
-            cols = np.frombuffer(stream, "<u2", 16, off + 128).reshape(4, 4)
-            blocks.append((vals, cols))
-            off += 160
-        bundles.append(dict(rows=rows, flags=flags, fin=fin, pre=pre, diag=diag, blocks=blocks))
-        pos = off
-    assert not any(stream[pos:]), "bytes after the end marker"
+def _parse(stream, n, backward):
+    """Records of one warp program: ("ctrl", rows, gflags, waits, diag) or
+    ("term", vals[4][4], cols[4][4]); it starts with a control record and ends
+    with one carrying the end flag, padded with zero bytes to whole stages."""
     assert len(stream) % STAGE == 0
-    return bundles
+    recs, pos, ctrl = [], 0, True
+    while True:
+        assert pos + REC <= len(stream), "program without an end record"
+        if ctrl:
+            rows = struct.unpack_from("<4H", stream, pos)
+            gflags = list(stream[pos + 8:pos + 12])
+            nwait, flags = stream[pos + 12], stream[pos + 13]
+            diag = struct.unpack_from("<4d", stream, pos + 16)
+            waits = list(struct.unpack_from(f"<{nwait}H", stream, pos + 48)) if nwait else []
+            assert nwait <= 56 and all(r <= n for r in rows) and all(r <= n for r in waits)
+            for g in range(4):
+                if gflags[g] & (G_DIVIDE | G_PUBLISH):
+                    assert gflags[g] & G_FINAL
+                assert bool(gflags[g] & G_DIVIDE) == (backward and bool(gflags[g] & G_FINAL))
+            recs.append(("ctrl", rows, gflags, waits, diag))
+            pos += REC
+            if flags & C_END:
+                break
+            ctrl = bool(flags & C_NEXT)
+        else:
+            vals = np.frombuffer(stream, "<f8", 16, pos).reshape(4, 4)
+            cols = np.frombuffer(stream, "<u2", 16, pos + 128).reshape(4, 4).astype(np.int64)
+            nxt = [bool(cols[g, 0] & NEXT_CTRL) for g in range(4)]
+            assert all(x == nxt[0] for x in nxt), "the control flag differs between groups"
+            cols = cols & COL_MASK
+            cols[:, 1:] = np.frombuffer(stream, "<u2", 16, pos + 128).reshape(4, 4)[:, 1:]
+            recs.append(("term", vals, cols))
+            pos += REC
+            ctrl = nxt[0]
+    assert not any(stream[pos:]), "bytes after the end record"
+    return recs
 
 
 class _Warp:
-    def __init__(self, bundles):
-        self.bundles, self.bi, self.b, self.acc, self.done = bundles, 0, -1, [0.0] * 4, [False] * 4
+    def __init__(self, recs):
+        self.recs, self.i, self.phase = recs, 0, 0
+        self.row, self.acc = [None] * 4, [0.0] * 4
 
     def finished(self):
-        return self.bi >= len(self.bundles)
+        return self.i >= len(self.recs)
 
 
-def _execute(programs, x, n, backward, pick, expect, ring_stages):
-    """Runs the warps' bundles block by block in the order pick() chooses."""
+def _execute(programs, x, n, backward, pick, expect):
+    """Runs the warps' records one at a time in the order pick() chooses."""
     x = list(x) + [0.0]
     final = [False] * (n + 1)
     final[n] = True
@@ -100,57 +95,59 @@ def _execute(programs, x, n, backward, pick, expect, ring_stages):
             final[i] = not expect[i]
     ready = [False] * n + [True]
     got = [[] for _ in range(n)]
-    warps = [_Warp(_parse(p, n, backward, ring_stages)) for p in programs]
-
-    def finish(wp, B, g):
-        r = B["rows"][g]
-        acc = wp.acc[g]
-        if (B["flags"] >> (4 + g)) & 1:
-            acc = acc / B["diag"][g]
-        x[r], wp.acc[g], wp.done[g] = acc, acc, True
-        final[r] = True
-        if (B["flags"] >> g) & 1:
-            ready[r] = True
+    warps = [_Warp(_parse(p, n, backward)) for p in programs]
 
     def step(wp):
         """One unit of warp wp; False if it is blocked."""
-        B = wp.bundles[wp.bi]
-        if wp.b < 0:   # bundle start: pre-waits, accumulators
-            if not all(ready[r] for r in B["pre"]):
-                return False
+        rec = wp.recs[wp.i]
+        if rec[0] == "term":
+            _, vals, cols = rec
             for g in range(4):
-                wp.acc[g], wp.done[g] = x[B["rows"][g]], False
-                if B["fin"][g] == 0:
-                    finish(wp, B, g)
-            wp.b = 0
-        elif wp.b < len(B["blocks"]):
-            vals, cols = B["blocks"][wp.b]
-            for g in range(4):
-                r = B["rows"][g]
+                r = wp.row[g]
                 for s in range(4):
                     c, v = int(cols[g, s]), float(vals[g, s])
                     assert final[c], f"row {r} reads row {c} before it is final"
                     wp.acc[g] = wp.acc[g] - v * x[c]
                     if c != n:
+                        assert r is not None, "an idle group has a term"
                         got[r].append((c, v))
                     else:
                         assert v == 0.0
-                if B["fin"][g] == wp.b + 1:
-                    finish(wp, B, g)
-            wp.b += 1
-        else:          # bundle end
+            wp.i += 1
+            return True
+        _, rows, gflags, waits, diag = rec
+        if wp.phase == 0:   # end segments (finish, pause), then the warp barrier
             for g in range(4):
-                if not wp.done[g]:
-                    x[B["rows"][g]] = wp.acc[g]
-            wp.bi, wp.b = wp.bi + 1, -1
+                if not gflags[g] & G_SWITCH or wp.row[g] is None:
+                    continue
+                r, acc = wp.row[g], wp.acc[g]
+                if gflags[g] & G_FINAL:
+                    if gflags[g] & G_DIVIDE:
+                        acc = acc / diag[g]
+                    final[r] = True
+                    if gflags[g] & G_PUBLISH:
+                        ready[r] = True
+                x[r] = acc
+                wp.row[g] = None
+            wp.phase = 1
+        if not all(ready[r] for r in waits):
+            return False
+        for g in range(4):
+            if gflags[g] & G_SWITCH:
+                r = rows[g]
+                wp.row[g] = None if r == n else r
+                wp.acc[g] = x[r] if r != n else 0.0
+        wp.phase = 0
+        wp.i += 1
         return True
 
     while True:
         live = [w for w in warps if not w.finished()]
         if not live:
             break
-        order = pick(live)
-        assert any(step(w) for w in order), "deadlock: every unfinished warp waits"
+        assert any(step(w) for w in pick(live)), "deadlock: every unfinished warp waits"
+    for w in warps:
+        assert all(r is None for r in w.row), "a program ends with a row in progress"
     for i in range(n):
         assert got[i] == expect[i], f"row {i}: terms differ from the reference's push order"
         assert final[i]
@@ -202,7 +199,7 @@ def _pickers(seed):
         return live
 
     def laggard(live):     # the warp with the least progress first
-        return sorted(live, key=lambda w: (w.bi, w.b))
+        return sorted(live, key=lambda w: w.i)
 
     return [shuffled, greedy, laggard]
 
@@ -221,13 +218,13 @@ def test_schedule_replays_reference_solve(built, tmp_path, config, index, ring):
     rhs = np.random.default_rng(index).standard_normal(n) * 300.0
     ref = _push_reference(L, U, rhs)
     for k, pick in enumerate(_pickers(index)):
-        y = _execute(fwd, rhs, n, False, pick, tl, ring)
-        z = _execute(bwd, y, n, True, pick, tu, ring)
+        y = _execute(fwd, rhs, n, False, pick, tl)
+        z = _execute(bwd, y, n, True, pick, tu)
         assert np.array_equal(z, ref), f"interleaving {k}"
 
 
 def test_schedule_stats(built, tmp_path):
-    """The statistics export agrees with the streams; bad arguments are errors."""
+    """The statistics export agrees with the programs; bad arguments are errors."""
     import neurips2026_smart_building_challenge_b200 as pkg
 
     blob = pkg.write_scenario(tmp_path / "s.sbb", pkg.preset(1, 0, n_steps=10))
@@ -239,12 +236,14 @@ def test_schedule_stats(built, tmp_path):
     for sweep in (0, 1):
         assert lib.sb_sweep_stats(str(blob).encode(), sweep, 5, st) == 0
         progs = _programs(lib, blob, sweep, 5)
-        bundles = [B for p in progs for B in _parse(p, n, sweep == 1, 5)]
+        recs = [r for p in progs for r in _parse(p, n, sweep == 1)]
+        ctrl = [r for r in recs if r[0] == "ctrl"]
         assert st[0] == L.nnz - n
-        assert st[1] == len(bundles)
-        assert st[2] == sum(len(B["blocks"]) for B in bundles)
-        assert st[3] == sum(int(r != n) for B in bundles for r in B["rows"])
-        assert st[4] <= sum(len(B["pre"]) for B in bundles)
+        assert st[1] == len(ctrl)
+        assert st[2] == len(recs) - len(ctrl)
+        assert st[3] == sum(int(r[2][g] & G_SWITCH and r[1][g] != n) for r in ctrl for g in range(4))
+        assert st[4] == sum(len(r[3]) for r in ctrl)
+        assert st[5] == sum(int(bool(r[2][g] & G_PUBLISH)) for r in ctrl for g in range(4))
         assert st[7] == sum(len(p) for p in progs)
     assert lib.sb_sweep_stats(str(blob).encode(), 0, 0, st) == 0          # default depth
     assert lib.sb_sweep_stats(str(blob).encode(), 2, 5, st) == -1         # no such sweep
