@@ -3,11 +3,14 @@
 // Reference interface: complete_port/gpu/smart_buildings.cu:2497-3323
 // (puf_vec_create, puf_bind_stream, puf_init, puf_reset, puf_step, puf_close,
 // puf_log, puf_live_log, puf_mask_init). One step enqueues, on the bound
-// stream and one forked side stream:
-//   k_rng   (side)  per-scenario convection permutation + occupancy chains
+// stream and two streams forked from it:
 //   k_pre   (main)  decode, actuators, zone sensing, VAV/AHU/boiler pre-step
-//   k_solve (main)  fused thermal solve over slabs of envs in shared memory
-//   k_post  (main, after joining the side stream) convection apply, boiler,
+//   k_solve (side, after k_pre) fused thermal solve over slabs of envs in
+//           shared memory, one slab per SM
+//   k_rng   (side, a programmatic dependent of k_solve) per-scenario
+//           convection permutation + occupancy chains: it starts once every
+//           slab is resident and runs on the SMs the slabs leave free
+//   k_post  (main, after the side stream) convection apply, boiler,
 //           observation, reward, episode log, in-step restart
 // No host synchronisation, allocation or attribute change happens inside
 // puf_step, so a caller can capture it in a CUDA graph.
@@ -100,19 +103,21 @@ struct Engine {
     int* d_scn_step = nullptr;
     RngOut* d_rng_out = nullptr;
     Env* envs = nullptr;          // managed
-    cudaStream_t stream = nullptr, own_stream = nullptr, side = nullptr;
-    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    cudaStream_t stream = nullptr, own_stream = nullptr, side = nullptr, hi = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr, ev_solve = nullptr;
     size_t smem_solve = 0, smem_pre = 0, smem_post = 0, smem_rng = 0;
     int max_ncv = 0;
     bool ready = false;
     ~Engine() { destroy(); }
     void destroy() {
         if (side) cudaStreamDestroy(side);
+        if (hi) cudaStreamDestroy(hi);
         if (own_stream) cudaStreamDestroy(own_stream);
         if (ev_fork) cudaEventDestroy(ev_fork);
         if (ev_join) cudaEventDestroy(ev_join);
-        side = own_stream = nullptr;
-        ev_fork = ev_join = nullptr;
+        if (ev_solve) cudaEventDestroy(ev_solve);
+        side = hi = own_stream = nullptr;
+        ev_fork = ev_join = ev_solve = nullptr;
         if (envs) cudaFree(envs);
         envs = nullptr;
         arena.release();
@@ -178,16 +183,34 @@ StateLayout make_layout(int na, int nv, int nz, int k) {
     return L;
 }
 
+// k_rng as a programmatic dependent of k_solve on the same stream: every
+// solve CTA signals at its start, so the random streams begin once all slabs
+// are resident and take the SMs the slab count leaves free. k_rng reads
+// nothing k_solve writes; it ends by waiting for k_solve's completion, so the
+// side stream's work is complete when k_rng is.
+cudaError_t launch_rng_after_solve(Engine& E, cudaStream_t st, int reset_only) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)E.sd.size());
+    cfg.blockDim = dim3(32);
+    cfg.dynamicSmemBytes = E.smem_rng;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k_rng, (const StepCtx*)E.d_ctx, E.d_scn_step, E.d_rng_out, reset_only);
+}
+
 bool launch_step(Engine& E) {
-    CK(cudaEventRecord(E.ev_fork, E.stream));
-    CK(cudaStreamWaitEvent(E.side, E.ev_fork, 0));
-    k_rng<<<(unsigned)E.sd.size(), 32, E.smem_rng, E.side>>>(E.d_ctx, E.d_scn_step, E.d_rng_out, 0);
-    CK(cudaGetLastError());
-    CK(cudaEventRecord(E.ev_join, E.side));
     k_pre<<<(unsigned)E.n_env, 128, E.smem_pre, E.stream>>>(E.d_ctx);
     CK(cudaGetLastError());
-    k_solve<<<(unsigned)E.slabs.size(), kSolveThreads, E.smem_solve, E.stream>>>(E.d_ctx, E.d_slabs);
+    CK(cudaEventRecord(E.ev_fork, E.stream));
+    CK(cudaStreamWaitEvent(E.hi, E.ev_fork, 0));
+    k_solve<<<(unsigned)E.slabs.size(), kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
     CK(cudaGetLastError());
+    CK(launch_rng_after_solve(E, E.hi, 0));
+    CK(cudaEventRecord(E.ev_join, E.hi));
     CK(cudaStreamWaitEvent(E.stream, E.ev_join, 0));
     k_post<<<(unsigned)E.n_env, 128, E.smem_post, E.stream>>>(E.d_ctx);
     CK(cudaGetLastError());
@@ -303,11 +326,23 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
         }
     }
     auto width = [&](int c, int b) { return std::max(bmin[c], std::min(b, bmax[c])); };
+    // SMs left to the random-stream blocks, which run beside the solve (each
+    // needs the shared memory of one scenario's convection tables)
+    long sm_budget = n_sm;
+    {
+        size_t rng_b = 0;
+        for (int c = 0; c < NG; c++)
+            rng_b = std::max(rng_b, 4 * (size_t)(624 + 624 + 1248) +
+                                        4 * (4 * (size_t)E.hg[c].cv_off.back() + 1 + E.hg[c].cv_off.size()));
+        const long per_sm = std::max<long>(1, std::min<long>(32, (long)(233472 / (rng_b + 1024))));
+        const long reserve = std::min<long>(n_sm / 4, (G + per_sm - 1) / per_sm);
+        sm_budget = n_sm - reserve;
+    }
     int bwave = slab_cap;
     for (int b = 1; b <= slab_cap; b++) {
         long slabs = 0;
         for (int c = 0; c < NG; c++) slabs += (E.gd[c].n_env + width(c, b) - 1) / width(c, b);
-        if (slabs <= n_sm) { bwave = b; break; }
+        if (slabs <= sm_budget) { bwave = b; break; }
     }
     // then narrow the slabs of the group with the most dense-solve work (rounds
     // of team solves x k^2) while the slabs still fit in one wave: slabs run
@@ -333,7 +368,7 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
         while (nb >= bmin[worst] && rounds(worst, nb) >= rounds(worst, bsel[worst])) nb--;
         if (nb < bmin[worst] || dense_cost(worst, bsel[worst]) == 0.0) break;
         const long delta = (long)(E.gd[worst].n_env + nb - 1) / nb - (E.gd[worst].n_env + bsel[worst] - 1) / bsel[worst];
-        if (slabs_now + delta > n_sm) break;
+        if (slabs_now + delta > sm_budget) break;
         slabs_now += delta;
         bsel[worst] = nb;
     }
@@ -376,7 +411,8 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
         gd.M = E.arena.zeros<double>((size_t)gd.n_env * h.n, ok);
         for (int e0 = 0; e0 < gd.n_env; e0 += B) E.slabs.push_back({c, gd.env0 + e0, std::min(B, gd.n_env - e0), 0});
         E.max_ncv = std::max(E.max_ncv, h.ncv);
-        E.smem_pre = std::max(E.smem_pre, sizeof(double) * (size_t)(h.ncv + 2 * nz_max + nv_max + 2 * na_max + 2 * k_max));
+        E.smem_pre = std::max(E.smem_pre, sizeof(double) * (size_t)(L.nd + 2 * nz_max + nv_max + 2 * na_max + 2 * k_max) +
+                                              sizeof(int32_t) * (size_t)L.ni);
         E.smem_post = std::max(E.smem_post, sizeof(double) * (size_t)(2 * h.ncv + 3 * nz_max + 2 * nv_max));
         const size_t rng_b = 4 * (size_t)(624 + 624 + 1248) + 4 * (4 * (size_t)h.cv_off.back() + 1 + h.cv_off.size());
         E.smem_rng = std::max(E.smem_rng, rng_b);
@@ -510,8 +546,14 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     CK(cudaFuncSetAttribute(k_rng, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_rng));
     CK(cudaStreamCreateWithFlags(&E.own_stream, cudaStreamNonBlocking));
     CK(cudaStreamCreateWithFlags(&E.side, cudaStreamNonBlocking));
+    {
+        int least = 0, greatest = 0;
+        CK(cudaDeviceGetStreamPriorityRange(&least, &greatest));
+        CK(cudaStreamCreateWithPriority(&E.hi, cudaStreamNonBlocking, greatest));
+    }
     CK(cudaEventCreateWithFlags(&E.ev_fork, cudaEventDisableTiming));
     CK(cudaEventCreateWithFlags(&E.ev_join, cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&E.ev_solve, cudaEventDisableTiming));
     if (!E.stream) E.stream = E.own_stream;
     CK(cudaDeviceSynchronize());
     E.ready = true;
@@ -809,30 +851,29 @@ int sb_kernels_per_step(void) { return 4; }
 int sb_step_timed(float* ms) {
     if (!g_eng || !g_eng->ready || !ms) return -1;
     Engine& E = *g_eng;
-    cudaEvent_t ev[6];
+    cudaEvent_t ev[7];
     for (auto& e : ev)
         if (cudaEventCreate(&e) != cudaSuccess) return -1;
-    // k_rng timed on its own stream; the main-stream kernels one after another
-    cudaEventRecord(E.ev_fork, E.stream);
-    cudaStreamWaitEvent(E.side, E.ev_fork, 0);
-    cudaEventRecord(ev[4], E.side);
-    k_rng<<<(unsigned)E.sd.size(), 32, E.smem_rng, E.side>>>(E.d_ctx, E.d_scn_step, E.d_rng_out, 0);
-    cudaEventRecord(ev[5], E.side);
-    cudaEventRecord(E.ev_join, E.side);
+    // the step of launch_step with events around each kernel (k_solve and
+    // k_rng share their stream: ev[2] closes both, k_rng is timed alone below)
     cudaEventRecord(ev[0], E.stream);
     k_pre<<<(unsigned)E.n_env, 128, E.smem_pre, E.stream>>>(E.d_ctx);
     cudaEventRecord(ev[1], E.stream);
-    k_solve<<<(unsigned)E.slabs.size(), kSolveThreads, E.smem_solve, E.stream>>>(E.d_ctx, E.d_slabs);
-    cudaEventRecord(ev[2], E.stream);
-    cudaStreamWaitEvent(E.stream, E.ev_join, 0);
+    cudaEventRecord(E.ev_fork, E.stream);
+    cudaStreamWaitEvent(E.hi, E.ev_fork, 0);
+    k_solve<<<(unsigned)E.slabs.size(), kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
+    launch_rng_after_solve(E, E.hi, 0);
+    cudaEventRecord(ev[2], E.hi);
+    cudaStreamWaitEvent(E.stream, ev[2], 0);
+    cudaEventRecord(ev[6], E.stream);
     k_post<<<(unsigned)E.n_env, 128, E.smem_post, E.stream>>>(E.d_ctx);
     cudaEventRecord(ev[3], E.stream);
-    const bool ok = cudaEventSynchronize(ev[3]) == cudaSuccess && cudaEventSynchronize(ev[5]) == cudaSuccess;
+    const bool ok = cudaEventSynchronize(ev[3]) == cudaSuccess;
     if (ok) {
-        cudaEventElapsedTime(&ms[0], ev[4], ev[5]);   // k_rng
+        ms[0] = -1.0f;                                 // k_rng runs beside k_solve, inside ms[2]
         cudaEventElapsedTime(&ms[1], ev[0], ev[1]);   // k_pre
-        cudaEventElapsedTime(&ms[2], ev[1], ev[2]);   // k_solve
-        cudaEventElapsedTime(&ms[3], ev[2], ev[3]);   // k_post (includes any wait on k_rng)
+        cudaEventElapsedTime(&ms[2], ev[1], ev[2]);   // k_solve (with k_rng beside it)
+        cudaEventElapsedTime(&ms[3], ev[6], ev[3]);   // k_post
     }
     for (auto& e : ev) cudaEventDestroy(e);
     return ok ? 0 : -1;

@@ -73,13 +73,22 @@ __device__ inline double reheat_energy(const EnvView& v, const ScnDev& s, int vv
     return dmul(dmul(dmul(dmul(eff, CP_AIR), RHO_AIR), vd), dsub(iwt, sat));
 }
 
-// Field-averaged zone temperatures (sb_sim.c:149-160) from an extended-order field.
+// Field-averaged zone temperatures (sb_sim.c:149-160) from an extended-order
+// field in global memory: one thread per zone, cells fetched eight at a time,
+// summed in the reference's order.
 __device__ inline void zone_means(const GroupDev& g, const ScnDev& s, const double* T, double* zavg) {
     for (int z = threadIdx.x; z < s.nz; z += blockDim.x) {
         const int rm = s.proom[z];
         const int a = g.room_off[rm], b = g.room_off[rm + 1];
         double sum = 0.0;
-        for (int t = a; t < b; t++) sum = dadd(sum, T[g.room_pos[t]]);
+        for (int t = a; t < b; t += 8) {
+            double tv[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) tv[u] = t + u < b ? T[g.room_pos[t + u]] : 0.0;
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+                if (t + u < b) sum = dadd(sum, tv[u]);
+        }
         zavg[z] = ddiv(sum, (double)(b - a));
     }
 }
@@ -114,12 +123,18 @@ __global__ void __launch_bounds__(128) k_pre(const StepCtx* __restrict__ ctx) {
     const GroupDev& g = ctx->groups[ei.group];
     const ScnDev& s = ctx->scns[ei.scn];
     const StateLayout& L = ctx->lay;
-    EnvView v{ctx->Dst + (size_t)env * L.nd, ctx->Ist + (size_t)env * L.ni, &ctx->lay};
     const int tid = threadIdx.x;
     const int na = s.na, nv = s.nv, nz = s.nz, k = s.k;
-
-    double* T = reinterpret_cast<double*>(smem);      // [ncv]
-    double* zavg = T + g.ncv;                         // [nz]
+    // the env's state blocks are worked on in shared memory (the ordered loops
+    // below read and update them element by element) and written back at the end
+    double* Dg = ctx->Dst + (size_t)env * L.nd;
+    int32_t* Ig = ctx->Ist + (size_t)env * L.ni;
+    double* Ds = reinterpret_cast<double*>(smem);          // [nd]
+    int32_t* Is = reinterpret_cast<int32_t*>(Ds + L.nd);   // [ni]
+    for (int i = tid; i < L.nd; i += blockDim.x) Ds[i] = Dg[i];
+    for (int i = tid; i < L.ni; i += blockDim.x) Is[i] = Ig[i];
+    EnvView v{Ds, Is, &ctx->lay};
+    double* zavg = reinterpret_cast<double*>(Is + L.ni);   // [nz] (ni is a multiple of 4)
     double* zq = zavg + nz;                           // [nz]
     double* unr = zq + nz;                            // [nv]
     double* sv = unr + nv;                            // [na] supply air temperature
@@ -127,6 +142,7 @@ __global__ void __launch_bounds__(128) k_pre(const StepCtx* __restrict__ ctx) {
     double* rw = demand + na;                         // [k]
     double* fdv = rw + k;                             // [k]
 
+    __syncthreads();
     const int kk = v.iv(L.step);
     const double ambient = s.amb[kk];
     const int comfort = s.s_comf[kk] != 0.0;
@@ -171,12 +187,11 @@ __global__ void __launch_bounds__(128) k_pre(const StepCtx* __restrict__ ctx) {
             else { const int on = val == 1.0 ? 1 : 0; v.iv(L.hws_run) = on; v.iv(L.pump_run) = on; }
         }
     }
-    // ---- field into shared memory, zone means ----
+    // ---- zone means from the field ----
     const double* Tg = g.T + (size_t)(env - g.env0) * g.ncv;
-    for (int i = tid; i < g.ncv; i += blockDim.x) T[i] = Tg[i];
     __syncthreads();
     if (tid == 0) v.iv(L.hws_req) = nv;
-    zone_means(g, s, T, zavg);
+    zone_means(g, s, Tg, zavg);
     __syncthreads();
     // ---- VAV sensing, thermostat, damper/reheat (sb_sim.c:368-384, :316-355) ----
     for (int vv = tid; vv < nv; vv += blockDim.x) {
@@ -224,7 +239,7 @@ __global__ void __launch_bounds__(128) k_pre(const StepCtx* __restrict__ ctx) {
         }
         double tmean = 0.0;
         if (s.tmean_needed) {
-            for (int p = 0; p < g.ncv; p++) tmean = dadd(tmean, T[g.pos_of_cell[p]]);
+            for (int p = 0; p < g.ncv; p++) tmean = dadd(tmean, Tg[g.pos_of_cell[p]]);
             tmean = ddiv(tmean, (double)g.ncv);
         }
         for (int a = 0; a < na; a++) {
@@ -316,6 +331,9 @@ __global__ void __launch_bounds__(128) k_pre(const StepCtx* __restrict__ ctx) {
         if (s.occ_w > 0.0) q = dadd(q, dmul(Vin[z], s.occ_w));
         v.d(L.qdiv, z) = ddiv(q, cells);
     }
+    __syncthreads();
+    for (int i = tid; i < L.nd; i += blockDim.x) Dg[i] = Ds[i];
+    for (int i = tid; i < L.ni; i += blockDim.x) Ig[i] = Is[i];
 }
 
 }  // namespace sbenv

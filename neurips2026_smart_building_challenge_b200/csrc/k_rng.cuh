@@ -171,6 +171,8 @@ __global__ void __launch_bounds__(32) k_rng(const StepCtx* __restrict__ ctx, int
     mt_store(m, s.occ_mt);
     for (int x = lane; x < s.nz * s.assign; x += 32) s.occ_state0[x] = occ_st[x];
     if (lane == 0) scn_step[si] = restart ? 0 : t + 1;
+    // launched as a programmatic dependent of the solve: complete only after it
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 }  // namespace sbenv

@@ -295,6 +295,8 @@ __device__ inline void dense_team(double* M, int k, int ttid, int T, int bar) {
 __global__ void __launch_bounds__(kSolveThreads, 1)
 k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
     extern __shared__ __align__(128) uint8_t smem[];
+    // a programmatic dependent (the random streams) may start once every CTA is resident
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const SlabDesc sd = slabs[blockIdx.x];
     const GroupDev& g = ctx->groups[sd.group];
     const StateLayout& L = ctx->lay;
