@@ -100,31 +100,29 @@ __device__ inline void run_sweep(const SolveShared& sh, const Sweep& sw, int B, 
                 acc = dsub(acc, dmul(v23.y, x3));
                 continue;
             }
-            // control record: end segments, wait, start rows
+            // control record: end segments, wait, start rows (warp-uniform
+            // control flow; per-group choices are predicates)
             const ControlRecord* c = reinterpret_cast<const ControlRecord*>(rec);
             const uint32_t gf = c->gflags[g];
             const uint32_t nw = c->nwait, newrow = c->row[g];
+            const uint32_t cflags = c->flags;
             if (__any_sync(full, newrow > (uint32_t)n || nw > (uint32_t)kCtrlWaits)) {
                 atomicCAS((int*)sh.abort, 0, kErrBadBundle);
                 ok = false;
                 break;
             }
-            if ((gf & kGSwitch) && row < (uint32_t)n) {
-                if (gf & kGFinal) {
-                    if (gf & kGDivide) acc = ddiv(acc, c->diag[g]);
-                    if (owns) xe[row] = acc;
-                    if (gf & kGPublish) {
-                        __syncwarp(0xFFu << (8 * g));
-                        if (e == 0) {
-                            __threadfence_block();
-                            st_release_u8(sh.ready + row, epoch);
-                        }
-                    }
-                } else if (owns) {
-                    xe[row] = acc;   // the row continues in a later segment
-                }
+            const bool ending = (gf & kGSwitch) && row < (uint32_t)n;
+            if (__any_sync(full, ending && (gf & kGDivide))) {
+                const double q = ddiv(acc, c->diag[g]);
+                if (ending && (gf & kGDivide)) acc = q;
             }
+            if (ending && owns) xe[row] = acc;   // final value, or the partial sum of a paused row
+            const bool pub = ending && (gf & kGPublish);
             __syncwarp();
+            if (__any_sync(full, pub) && pub && e == 0) {
+                __threadfence_block();
+                st_release_u8(sh.ready + row, epoch);
+            }
             // waits: one row per lane; the warp barrier after them orders every
             // lane's later reads after all the acquires
             for (uint32_t i = lane; i < nw; i += 32) {
@@ -153,12 +151,12 @@ __device__ inline void run_sweep(const SolveShared& sh, const Sweep& sw, int B, 
             }
             __syncwarp();
             if (!__all_sync(full, ok)) break;
-            if (gf & kGSwitch) {
-                row = newrow;
-                acc = row < (uint32_t)n ? xe[row] : 0.0;
-            }
-            next_ctrl = (c->flags & kCtrlNext) != 0;
-            end = (c->flags & kCtrlEnd) != 0;
+            // new rows: slot n (idle) reads the zero column
+            if (gf & kGSwitch) row = newrow;
+            const double a0 = xe[row];
+            acc = (gf & kGSwitch) ? a0 : acc;
+            next_ctrl = (cflags & kCtrlNext) != 0;
+            end = (cflags & kCtrlEnd) != 0;
         }
         if (!__all_sync(full, ok)) break;
         // refill the slot of stage s with stage s + R

@@ -34,8 +34,8 @@ constexpr double kCCtrl = 100;  // a control record: finishes, waits, new rows
 constexpr double kCBlk = 40;    // a term record
 constexpr double kC2 = 80;      // release store until another warp's acquire sees it
 constexpr double kSlack = 150;  // a row may be picked this long before its next input is ready
-constexpr int kMinSeg = 8;       // shortest segment worth a control record (unless the row ends sooner)
-constexpr double kCritical = 0.85;   // rows within this fraction of the top priority start at any length
+constexpr int kMinSeg = 16;      // shortest segment worth a control record (unless the row ends sooner)
+constexpr double kCritical = 0.9;    // rows within this fraction of the top priority start at any length
 constexpr int kUnsched = std::numeric_limits<int>::max();
 
 inline bool test(const uint64_t* s, int i) { return (s[i >> 6] >> (i & 63)) & 1u; }
