@@ -166,8 +166,9 @@ int sb_solve_schedule(const char* blob_path, int sweep, int ring_stages, uint8_t
                       uint32_t* warp_stages);
 /* Warps of a solve CTA that run sweep programs (streams per sweep). */
 int sb_sweep_warps(void);
-/* Host-only: statistics of that program, out[8] = {terms, bundles, term blocks,
- * row pieces, pre-waits, published rows, modelled cycles, stream bytes}. */
+/* Host-only: statistics of that program, out[10] = {terms, control records,
+ * term records, row segments, waits, published rows and partial sums,
+ * modelled cycles, stream bytes, dense block records, rows they finish}. */
 int sb_sweep_stats(const char* blob_path, int sweep, int ring_stages, double* out);
 
 #ifdef __cplusplus

@@ -469,7 +469,6 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
         const HostGroup& hgp = E.hg[scn_group[i]];
         s.conv_pairs = E.arena.zeros<int32_t>(2 * (size_t)hgp.ncv + 2, ok);
         s.conv_npairs = E.arena.zeros<int>(1, ok);
-        s.conv_scratch = nullptr;
     }
     for (int i = 0; i < G; i++) E.smem_rng = std::max(E.smem_rng, 4 * (size_t)(624 + 624 + 1248) + 4 * (size_t)E.hs[i].nz * E.hs[i].assign);
     // ---- env index ----
@@ -951,9 +950,10 @@ int sb_sweep_stats(const char* blob_path, int sweep, int ring_stages, double* ou
     const std::string e = schedule_of(blob_path, sweep, ring_stages, g);
     if (!e.empty() || !out) { set_err("%s", e.empty() ? "null output" : e.c_str()); return -1; }
     const HostSweep& s = sweep == 0 ? g.fwd : g.bwd;
-    const double v[8] = {(double)s.terms,    (double)s.bundles,   (double)s.blocks, (double)s.pieces,
-                         (double)s.prewaits, (double)s.publishes, s.sim_cycles,     (double)s.bytes.size()};
-    for (int i = 0; i < 8; i++) out[i] = v[i];
+    const double v[10] = {(double)s.terms,    (double)s.bundles,   (double)s.blocks, (double)s.pieces,
+                          (double)s.prewaits, (double)s.publishes, s.sim_cycles,     (double)s.bytes.size(),
+                          (double)s.dense_blocks, (double)s.block_rows};
+    for (int i = 0; i < 10; i++) out[i] = v[i];
     return 0;
 }
 

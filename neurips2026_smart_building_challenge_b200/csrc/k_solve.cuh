@@ -8,7 +8,7 @@
 // each row receives exactly the same sequence of subtractions and the result
 // is bit-identical. The pull schedule is precomputed on the host
 // (sweep_sched.cpp): every warp runs its own program, streamed into a per-warp
-// shared-memory ring with cp.async; its four lane groups (one lane per env)
+// shared-memory ring by bulk copies; its four lane groups (one lane per env)
 // each work through their own rows, and control records acquire the ready
 // flags of other warps' rows before rows that read them start.
 #pragma once
@@ -23,154 +23,311 @@ struct SlabDesc {
     int pad;
 };
 
-constexpr uint32_t kSpinLimit = 1u << 22;   // polls of one ready flag (at most ~1 s with the sleeps)
+constexpr uint32_t kSpinLimit = 1u << 22;   // polls of one ready flag before the wait gives up
 
 struct SolveShared {
     double* X;            // [B][stride]
     uint8_t* ring;        // [kSweepWarps][ring_stages][kStageBytes]
-    uint8_t* ready;       // [n + 1] row ready flags (epoch of the sweep that finished the row)
+    uint8_t* ready;       // [n + 1] row ready flags: 2 epoch final, 2 epoch - 1 outside terms applied
+    uint64_t* bars;       // [kSweepWarps][kStagesMax] completion barriers of the ring stages
     volatile int* abort;  // first error of this CTA
 };
 
-// cp.async: 16 bytes global -> shared per lane; one commit group per stage
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-// waits until at most `pending` of this thread's newest groups are in flight
-__device__ __forceinline__ void cp_async_wait(uint32_t pending) {
-    switch (pending) {
-        case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
-        case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
-        case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
-        case 3: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
-        case 4: asm volatile("cp.async.wait_group 4;" ::: "memory"); break;
-        case 5: asm volatile("cp.async.wait_group 5;" ::: "memory"); break;
-        case 6: asm volatile("cp.async.wait_group 6;" ::: "memory"); break;
-        default: asm volatile("cp.async.wait_group 7;" ::: "memory"); break;
+// Waits (acquire) until every listed row's ready flag reaches its target:
+// `fin` for a final row, fin - 1 for an entry with kWaitPartial. One row per
+// lane; bounded, and left early once another warp has reported an error.
+// Warp-uniform result: false if some lane gave up.
+__device__ inline bool wait_rows(const SolveShared& sh, const uint16_t* list, uint32_t nw, uint32_t n, uint32_t fin) {
+    const int lane = threadIdx.x & 31;
+    bool ok = true;
+    for (uint32_t i = lane; i < nw && ok; i += 32) {
+        const uint32_t w = list[i];
+        const uint32_t r = min(w & (uint32_t)kColMask, n);   // slot n is always ready
+        const uint32_t need = (w & kWaitPartial) ? fin - 1 : fin;
+        uint32_t spins = 0;
+        while (ld_acquire_u8(sh.ready + r) < need) {
+            if (++spins >= kSpinLimit) {
+                atomicCAS((int*)sh.abort, 0, kErrWaitTimeout);
+                ok = false;
+                break;
+            }
+            if ((spins & 1023u) == 0 && *sh.abort) { ok = false; break; }
+            if (spins > 16) __nanosleep(32);
+        }
     }
+    return __all_sync(0xffffffffu, ok);
 }
 
-// One triangular sweep. Every warp runs its own program, copied stage by
-// stage (three records each) into its ring, 16 bytes per lane; all threads of
-// the CTA must call it.
-__device__ inline void run_sweep(const SolveShared& sh, const Sweep& sw, int B, int S, int n, uint32_t epoch) {
+// The stage ring of one warp: its program is copied stage by stage (three
+// records) into ring_stages slots by bulk copies that lane 0 issues, each
+// completing on its slot's mbarrier. Stages are consumed in order; a slot is
+// refilled with the stage ring_stages further on once its stage is consumed.
+struct StageRing {
+    uint8_t* ring;
+    uint64_t* bar;
+    const uint8_t* src;
+    uint32_t R, nst;
+    uint32_t head = 0, hslot = 0;               // first stage not consumed, its slot
+    uint32_t landed = 0, lslot = 0, lpar = 0;   // stages < landed have arrived; slot and phase of `landed`
+
+    __device__ void issue(uint32_t st, uint32_t slot) const {   // lane 0; the slot's earlier reads are complete
+        mbar_expect_tx(bar + slot, kStageBytes);
+        bulk_g2s(ring + (size_t)slot * kStageBytes, src + (size_t)st * kStageBytes, kStageBytes, bar + slot);
+    }
+    __device__ void start(int lane) {
+        if (lane == 0) {
+            for (uint32_t s = 0; s < R; s++) mbar_init(bar + s, 1);
+            mbar_fence_init();
+            for (uint32_t s = 0; s < R && s < nst; s++) issue(s, s);
+        }
+        __syncwarp();
+    }
+    // stage t has arrived (t < head + R); warp-uniform, false on timeout
+    __device__ bool land(uint32_t t) {
+        if (landed > t) return true;
+        bool ok = true;
+        while (landed <= t && ok) {
+            ok = mbar_wait_bounded(bar + lslot, lpar);
+            landed++;
+            if (++lslot == R) { lslot = 0; lpar ^= 1u; }
+        }
+        return __all_sync(0xffffffffu, ok);
+    }
+    // stages < t are consumed: their slots are refilled
+    __device__ void consume(uint32_t t, int lane) {
+        if (head >= t) return;
+        __syncwarp();   // every lane is done reading the slots
+        for (; head < t; head++) {
+            if (lane == 0 && head + R < nst) issue(head + R, hslot);
+            if (++hslot == R) hslot = 0;
+        }
+    }
+    // no copy may land after the sweep (the ring memory is reused): wait for
+    // the stages in flight, then retire the barriers
+    __device__ bool finish(int lane) {
+        const uint32_t end = min(head + R, nst);
+        const bool ok = end == 0 || land(end - 1);
+        __syncwarp();
+        if (lane == 0)
+            for (uint32_t s = 0; s < R; s++) mbar_inval(bar + s);
+        __syncwarp();
+        return ok;
+    }
+};
+
+// One dense block record (format in sbenv_dev.h), the cursor at its header
+// (stage rg.head, record hq). Lane group g holds the block's rows i = g mod 4,
+// one lane per env, their partial sums in registers: slot u is the group's
+// row c0 + g + 4u of the current round c0, and after every round the slots
+// shift down by one. Inside a round the four rows finish in turn (x_k from
+// group k to all lanes by a shuffle); the later rows then take the round's
+// four values from one 32-byte run of terms each. Returns the record index
+// after the block's values, or 0xFFFFFFFF on an error (reported in sh.abort).
+constexpr int kBlockSlots = kMaxBlockRows / kBundleRows;
+
+__device__ inline uint32_t run_block(const SolveShared& sh, StageRing& rg, uint32_t hq, double* __restrict__ xe,
+                                     bool owns, uint32_t n, uint32_t fin) {
     const unsigned full = 0xffffffffu;
+    const int lane = threadIdx.x & 31, e = lane & 7;
+    const uint32_t g = (uint32_t)lane >> 3;
+    const BlockRecord* b = reinterpret_cast<const BlockRecord*>(rg.ring + (size_t)rg.hslot * kStageBytes + hq * kRecordBytes);
+    const uint32_t first = b->first, size = b->size, bw = b->backward, nw = b->nwait, nrec = b->nrec;
+    const uint64_t pubm = b->publish;
+    const uint32_t lastrow = bw ? first - (size - 1) : first + (size - 1);
+    const uint32_t hidx = rg.head * kRecordsPerStage + hq;
+    if (size == 0 || size > (uint32_t)block_rows_for_ring((int)rg.R) || first >= n || lastrow >= n ||
+        nrec * (uint32_t)kRecordBytes < (uint32_t)block_values((int)size) * 8u ||
+        (hidx + 1 + nrec) / kRecordsPerStage >= rg.nst) {
+        atomicCAS((int*)sh.abort, 0, kErrBadBundle);
+        return 0xFFFFFFFFu;
+    }
+    if (nw && !wait_rows(sh, b->wait, min(nw, (uint32_t)kCtrlWaits), n, fin)) return 0xFFFFFFFFu;
+    const int dir = bw ? -1 : 1;
+    const uint32_t RB = rg.R * kStageBytes;
+    const uint8_t* __restrict__ ring = rg.ring;
+    double acc[kBlockSlots];
+#pragma unroll
+    for (int u = 0; u < kBlockSlots; u++) {
+        const uint32_t i = g + 4 * u;
+        acc[u] = i < size ? xe[(int)first + dir * (int)i] : 0.0;
+    }
+    // value cursor: stage vst (slot vslot), byte vb within it; rounds keep it 16-byte aligned
+    uint32_t vst = rg.head, vslot = rg.hslot, vb = (hq + 1) * kRecordBytes;
+    if (vb == kStageBytes) {
+        vst++; vb = 0;
+        if (++vslot == rg.R) vslot = 0;
+    }
+    rg.consume(vst, lane);   // the header's stage, if the values start after it
+    // this group's in-round terms (k < g at triangle index g(g-1)/2 + k) and diagonal
+    const uint32_t tri0 = g * (g - 1) / 2;
+    for (uint32_t c0 = 0; c0 < size; c0 += 4) {
+        const uint32_t after = size > c0 + 4 ? size - c0 - 4 : 0;   // rows after the round
+        const uint32_t rbytes = (kRoundHead + 4 * after) * 8;
+        if (!rg.land(vst + (vb + rbytes - 1) / kStageBytes)) {
+            atomicCAS((int*)sh.abort, 0, kErrRingTimeout);
+            return 0xFFFFFFFFu;
+        }
+        const uint32_t base = vslot * kStageBytes + vb;   // ring offset of the round
+        auto val = [&](uint32_t off) {
+            uint32_t a = base + off;
+            if (a >= RB) a -= RB;
+            return *reinterpret_cast<const double*>(ring + a);
+        };
+        const double dg = bw ? val(8 * g) : 1.0;
+        const double t0 = val(32 + 8 * min(tri0 + 0, 5u));
+        const double t1 = val(32 + 8 * min(tri0 + 1, 5u));
+        const double t2 = val(32 + 8 * min(tri0 + 2, 5u));
+        // the four rows in turn: group k's row is final at stage k
+        double a = acc[0];
+        const double x0 = __shfl_sync(full, bw ? ddiv(a, dg) : a, e);
+        if (g > 0) a = dsub(a, dmul(t0, x0));
+        const double x1 = __shfl_sync(full, bw ? ddiv(a, dg) : a, 8 | e);
+        if (g > 1) a = dsub(a, dmul(t1, x1));
+        const double x2 = __shfl_sync(full, bw ? ddiv(a, dg) : a, 16 | e);
+        if (g > 2) a = dsub(a, dmul(t2, x2));
+        const double x3 = __shfl_sync(full, bw ? ddiv(a, dg) : a, 24 | e);
+        // the round's rows are final: store, publish those other warps read
+        const bool mine = c0 + g < size;
+        const int row = (int)first + dir * (int)(c0 + g);
+        const double xm = g == 0 ? x0 : g == 1 ? x1 : g == 2 ? x2 : x3;
+        if (mine && owns) xe[row] = xm;
+        const uint32_t pr = (uint32_t)(pubm >> c0) & 0xFu;
+        if (pr) {
+            __syncwarp();
+            if (mine && e == 0 && ((pr >> g) & 1u)) {
+                __threadfence_block();
+                st_release_u8(sh.ready + row, fin);
+            }
+        }
+        // later rows: four terms each, in column order; chunks of four slots
+        // while some group still has rows there
+        const uint32_t live = (after + 3) / 4;   // slots 1..live
+#pragma unroll
+        for (int c = 1; c < kBlockSlots; c += 4) {
+            if ((uint32_t)c > live) break;   // warp-uniform
+#pragma unroll
+            for (int u = c; u < c + 4 && u < kBlockSlots; u++) {
+                const bool use = c0 + g + 4 * u < size;
+                uint32_t o = base + kRoundHead * 8 + 32 * (g + 4 * (u - 1));
+                if (o >= RB) o -= RB;
+                if (!use) o = base;
+                uint32_t o2 = o + 16;   // the run may wrap around the ring end
+                if (o2 >= RB) o2 -= RB;
+                const double2 v01 = *reinterpret_cast<const double2*>(ring + o);
+                const double2 v23 = *reinterpret_cast<const double2*>(ring + o2);
+                double r = acc[u];
+                r = dsub(r, dmul(v01.x, x0));
+                r = dsub(r, dmul(v01.y, x1));
+                r = dsub(r, dmul(v23.x, x2));
+                r = dsub(r, dmul(v23.y, x3));
+                acc[u] = use ? r : acc[u];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u + 1 < kBlockSlots; u++) acc[u] = acc[u + 1];
+        vb += rbytes;
+        while (vb >= kStageBytes) {
+            vb -= kStageBytes;
+            vst++;
+            if (++vslot == rg.R) vslot = 0;
+        }
+        rg.consume(vst, lane);
+    }
+    return hidx + 1 + nrec;
+}
+
+// One triangular sweep. Every warp runs its own program from its stage ring;
+// all threads of the CTA must call it. Term records: four terms per lane
+// group. Control records: finish ending rows (divide, store, publish), wait
+// for other warps' rows, load the new rows. Block records: run_block.
+// Every branch on a record's contents is warp-uniform (record-level flags),
+// so the warp never needs a vote on the hot path.
+__device__ inline void run_sweep(const SolveShared& sh, const Sweep& sw, int B, int S, int n, uint32_t epoch) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int g = lane >> 3, e = lane & 7;
-    const uint32_t R = sw.ring_stages;
-    const uint32_t nst = sw.warp_stages[w];
-    const bool copier = lane < kStageBytes / 16;
-    const uint8_t* src = sw.stream + (size_t)sw.warp_off[w] * kStageBytes + 16 * lane;
-    uint8_t* ring = sh.ring + (size_t)w * R * kStageBytes;
+    const uint32_t fin = 2 * epoch, un = (uint32_t)n;
+    StageRing rg;
+    rg.R = sw.ring_stages;
+    rg.nst = sw.warp_stages[w];
+    rg.src = sw.stream + (size_t)sw.warp_off[w] * kStageBytes;
+    rg.ring = sh.ring + (size_t)w * rg.R * kStageBytes;
+    rg.bar = sh.bars + (size_t)w * kStagesMax;
     // lanes of envs beyond the slab's capacity read env 0's field and never
     // store, so they touch no memory outside the field
     const bool owns = e < B;
     double* xe = sh.X + (size_t)(owns ? e : 0) * S;
 
-    uint32_t issued = 0;
-    for (; issued < nst && issued < R; issued++) {
-        if (copier) cp_async16(ring + issued * kStageBytes + 16 * lane, src + (size_t)issued * kStageBytes);
-        cp_async_commit();
-    }
-    bool ok = true, end = false, next_ctrl = true;
-    uint32_t row = (uint32_t)n;   // this group's row (n: idle)
+    rg.start(lane);
+    int err = rg.nst == 0 ? kErrBadBundle : (rg.land(0) ? kErrNone : kErrRingTimeout);
+    const uint8_t* rp = rg.ring;
+    uint32_t q = 0;
+    bool ctrl = true;
+    uint32_t row = un;   // this group's row (n: idle, reads the zero slot)
     double acc = 0.0;
-    for (uint32_t s = 0; s < nst && !end; s++) {
-        int ab = 0;
-        if (lane == 0) ab = *sh.abort;
-        ab = __shfl_sync(full, ab, 0);
-        if (!__all_sync(full, ok) || ab) break;
-        cp_async_wait(issued - 1 - s);
-        __syncwarp();
-        const uint8_t* stage = ring + (s % R) * kStageBytes;
-        for (int q = 0; q < kRecordsPerStage && !end; q++) {
-            const uint8_t* rec = stage + q * kRecordBytes;
-            if (!next_ctrl) {
-                // term record: four terms of this group's row
-                const double2 v01 = *reinterpret_cast<const double2*>(rec + 32 * g);
-                const double2 v23 = *reinterpret_cast<const double2*>(rec + 32 * g + 16);
-                const uint2 cc = *reinterpret_cast<const uint2*>(rec + 128 + 8 * g);
-                next_ctrl = (cc.x & kNextIsCtrl) != 0;
-                const double x0 = xe[cc.x & kColMask], x1 = xe[cc.x >> 16];
-                const double x2 = xe[cc.y & 0xFFFFu], x3 = xe[cc.y >> 16];
-                acc = dsub(acc, dmul(v01.x, x0));
-                acc = dsub(acc, dmul(v01.y, x1));
-                acc = dsub(acc, dmul(v23.x, x2));
-                acc = dsub(acc, dmul(v23.y, x3));
+    while (err == kErrNone) {
+        if (!ctrl) {
+            // term record: four terms of this group's row
+            const double2 v01 = *reinterpret_cast<const double2*>(rp + 32 * g);
+            const double2 v23 = *reinterpret_cast<const double2*>(rp + 32 * g + 16);
+            const uint2 cc = *reinterpret_cast<const uint2*>(rp + 128 + 8 * g);
+            ctrl = (cc.x & kNextIsCtrl) != 0;
+            const double x0 = xe[cc.x & kColMask], x1 = xe[cc.x >> 16];
+            const double x2 = xe[cc.y & 0xFFFFu], x3 = xe[cc.y >> 16];
+            acc = dsub(acc, dmul(v01.x, x0));
+            acc = dsub(acc, dmul(v01.y, x1));
+            acc = dsub(acc, dmul(v23.x, x2));
+            acc = dsub(acc, dmul(v23.y, x3));
+        } else {
+            const ControlRecord* c = reinterpret_cast<const ControlRecord*>(rp);
+            const uint32_t cf = c->flags;
+            if (cf & kCtrlBlock) {
+                const uint32_t next = run_block(sh, rg, q, xe, owns, un, fin);
+                if (next == 0xFFFFFFFFu) { err = kErrBadBundle; break; }
+                rg.consume(next / kRecordsPerStage, lane);
+                if (!rg.land(rg.head)) { err = kErrRingTimeout; break; }
+                q = next % kRecordsPerStage;
+                rp = rg.ring + (size_t)rg.hslot * kStageBytes + q * kRecordBytes;
+                ctrl = true;   // a block is followed by a control or block record
                 continue;
             }
-            // control record: end segments, wait, start rows (warp-uniform
-            // control flow; per-group choices are predicates)
-            const ControlRecord* c = reinterpret_cast<const ControlRecord*>(rec);
             const uint32_t gf = c->gflags[g];
-            const uint32_t nw = c->nwait, newrow = c->row[g];
-            const uint32_t cflags = c->flags;
-            if (__any_sync(full, newrow > (uint32_t)n || nw > (uint32_t)kCtrlWaits)) {
-                atomicCAS((int*)sh.abort, 0, kErrBadBundle);
-                ok = false;
-                break;
+            const uint32_t newrow = min((uint32_t)c->row[g], un);
+            const uint32_t nw = c->nwait;
+            const bool ending = (gf & kGSwitch) && row < un;
+            if (cf & kCtrlDivide) {
+                const double dq = ddiv(acc, c->diag[g]);
+                if (gf & kGDivide) acc = dq;
             }
-            const bool ending = (gf & kGSwitch) && row < (uint32_t)n;
-            if (__any_sync(full, ending && (gf & kGDivide))) {
-                const double q = ddiv(acc, c->diag[g]);
-                if (ending && (gf & kGDivide)) acc = q;
-            }
-            if (ending && owns) xe[row] = acc;   // final value, or the partial sum of a paused row
-            const bool pub = ending && (gf & kGPublish);
-            __syncwarp();
-            if (__any_sync(full, pub) && pub && e == 0) {
-                __threadfence_block();
-                st_release_u8(sh.ready + row, epoch);
-            }
-            // waits: one row per lane; the warp barrier after them orders every
-            // lane's later reads after all the acquires
-            for (uint32_t i = lane; i < nw; i += 32) {
-                const uint32_t r = c->wait[i];
-                if (r > (uint32_t)n) {
-                    atomicCAS((int*)sh.abort, 0, kErrBadBundle);
-                    ok = false;
-                    break;
+            if (ending && owns) xe[row] = acc;   // final value, partial sum, or paused row
+            if (cf & kCtrlPublish) {
+                __syncwarp();
+                if (ending && e == 0 && (gf & (kGPublish | kGPartial))) {
+                    __threadfence_block();
+                    st_release_u8(sh.ready + row, (gf & kGPublish) ? fin : fin - 1);
                 }
-                // a few quick polls, then sleeps that leave the issue slots to
-                // the warps doing work (bounded: kSpinLimit polls in all)
-                uint32_t spins = 0, nap = 32;
-                while (ld_acquire_u8(sh.ready + r) < epoch) {
-                    if (++spins >= kSpinLimit) {
-                        atomicCAS((int*)sh.abort, 0, kErrWaitTimeout);
-                        ok = false;
-                        break;
-                    }
-                    if ((spins & 255u) == 0 && *sh.abort) { ok = false; break; }
-                    if (spins > 4) {
-                        __nanosleep(nap);
-                        nap = nap < 256 ? 2 * nap : 256;
-                    }
-                }
-                if (!ok) break;
             }
-            __syncwarp();
-            if (!__all_sync(full, ok)) break;
-            // new rows: slot n (idle) reads the zero column
-            if (gf & kGSwitch) row = newrow;
-            const double a0 = xe[row];
-            acc = (gf & kGSwitch) ? a0 : acc;
-            next_ctrl = (cflags & kCtrlNext) != 0;
-            end = (cflags & kCtrlEnd) != 0;
+            if (nw && !wait_rows(sh, c->wait, min(nw, (uint32_t)kCtrlWaits), un, fin)) { err = kErrWaitTimeout; break; }
+            __syncwarp();   // stores of every group before any group's new loads
+            if (gf & kGSwitch) {
+                row = newrow;
+                acc = xe[row];
+            }
+            if (cf & kCtrlEnd) break;
+            ctrl = (cf & kCtrlNext) != 0;
         }
-        if (!__all_sync(full, ok)) break;
-        // refill the slot of stage s with stage s + R
-        __syncwarp();
-        if (!end && s + R < nst) {
-            if (copier) cp_async16(ring + (s % R) * kStageBytes + 16 * lane, src + (size_t)(s + R) * kStageBytes);
-            cp_async_commit();
-            issued = s + R + 1;
+        // next record
+        if (++q == kRecordsPerStage) {
+            rg.consume(rg.head + 1, lane);
+            if (rg.head >= rg.nst) { err = kErrBadBundle; break; }
+            if (!rg.land(rg.head)) { err = kErrRingTimeout; break; }
+            q = 0;
+            rp = rg.ring + (size_t)rg.hslot * kStageBytes;
+        } else {
+            rp += kRecordBytes;
         }
     }
-    if (!ok || !end) atomicCAS((int*)sh.abort, 0, kErrBadBundle);
-    // no copy may land after the sweep: the ring memory is reused
-    cp_async_wait(0);
-    __syncwarp();
+    if (err != kErrNone) atomicCAS((int*)sh.abort, 0, err);
+    if (!rg.finish(lane)) atomicCAS((int*)sh.abort, 0, kErrRingTimeout);
 }
 
 // Dense k x k system M q = b of one env, solved by a team of warps with the
@@ -308,7 +465,8 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
     sh.X = reinterpret_cast<double*>(smem);
     sh.ring = smem + (size_t)B * S * sizeof(double);
     sh.ready = sh.ring + (size_t)kSweepWarps * R * kStageBytes;
-    int* misc = reinterpret_cast<int*>(sh.ready + ((n + 1 + 15) & ~15));
+    sh.bars = reinterpret_cast<uint64_t*>(sh.ready + ((n + 1 + 15) & ~15));
+    int* misc = reinterpret_cast<int*>(sh.bars + kSweepWarps * kStagesMax);
     sh.abort = misc;
     double* amb_e = reinterpret_cast<double*>(misc + 4);   // [8]
     int* active = reinterpret_cast<int*>(amb_e + 8);        // [8]

@@ -56,6 +56,23 @@ enum : int {
 // warp reads them), then wait (acquire) for the rows of other warps that the
 // new rows read, then load the new rows' accumulators.
 //
+// A block record solves a dense block of up to kMaxBlockRows consecutive rows
+// (in sweep order) whose terms among themselves form a full triangle (the
+// separators of the nested-dissection order): the whole warp works on it,
+// lane group q holding the block's rows i = q mod 4, one lane per env. The
+// block is solved in rounds of four rows c0..c0+3: the four rows finish one
+// after another inside the round (each hands its value to the others by a
+// shuffle), then every later row of the block subtracts the four values in
+// column order, so each row receives its in-block terms in the push order.
+// The rows' terms from outside the block are applied before, as ordinary
+// segments; the end of such a segment publishes a "partial" flag where
+// another warp runs the block. Ready flags: a finished row holds 2 epoch, a
+// row whose outside terms are applied 2 epoch - 1. The block's values follow
+// the block record, round after round: 4 diagonals (U; zero in L), the 6
+// in-round terms (c0+1,c0) (c0+2,c0) (c0+2,c0+1) (c0+3,c0) (c0+3,c0+1)
+// (c0+3,c0+2), 2 zeros, then for every row i >= c0+4 of the block its four
+// terms (i,c0..c0+3); the last record is padded with zeros.
+//
 // A program is a sequence of kRecordBytes records, three to a ring stage;
 // it starts with a control record, and a control record with kCtrlEnd ends it.
 constexpr int kSweepWarps = kSolveThreads / 32;   // warps that run sweep programs
@@ -68,6 +85,8 @@ constexpr int kStageBytes = kRecordBytes * kRecordsPerStage;   // one copy into 
 constexpr int kStagesMin = 4;            // ring depth per warp (stages), chosen per group
 constexpr int kStagesMax = 8;
 constexpr int kCtrlWaits = 56;           // wait rows per control record
+constexpr int kMaxBlockRows = 48;        // rows of a dense block record (12 register slots per lane group)
+constexpr uint16_t kWaitPartial = 0x8000; // wait entry: the row's outside terms only
 constexpr uint16_t kNextIsCtrl = 0x8000; // TermRecord.col[g][0]: a control record follows
 constexpr uint16_t kColMask = 0x7FFF;
 // ControlRecord.gflags bits
@@ -75,9 +94,13 @@ constexpr uint8_t kGSwitch = 1;          // the group ends its segment and start
 constexpr uint8_t kGFinal = 2;           // the ending segment completes its row
 constexpr uint8_t kGDivide = 4;          // ... and divides it by diag[g] (backward sweep)
 constexpr uint8_t kGPublish = 8;         // ... and publishes it
-// ControlRecord.flags bits
-constexpr uint8_t kCtrlNext = 1;         // the next record is a control record too
+constexpr uint8_t kGPartial = 16;        // the ending segment completes the row's outside terms: publish them
+// ControlRecord.flags bits (warp-uniform summaries of the record)
+constexpr uint8_t kCtrlNext = 1;         // the next record is a control or block record
 constexpr uint8_t kCtrlEnd = 2;          // the program ends after this record
+constexpr uint8_t kCtrlBlock = 4;        // a BlockRecord (its values follow it)
+constexpr uint8_t kCtrlDivide = 8;       // some group has kGDivide
+constexpr uint8_t kCtrlPublish = 16;     // some group has kGPublish or kGPartial
 
 struct TermRecord {
     double val[kBundleRows][kTermSteps];
@@ -92,10 +115,39 @@ struct ControlRecord {
     double diag[kBundleRows];
     uint16_t wait[kCtrlWaits];   // rows to acquire before the new rows start
 };
-static_assert(sizeof(TermRecord) == kRecordBytes && sizeof(ControlRecord) == kRecordBytes, "record size");
+struct BlockRecord {
+    uint16_t first;              // the block's first row
+    uint16_t size;               // rows (2..kMaxBlockRows)
+    uint8_t backward;            // 0: rows first, first+1, ..; 1: first, first-1, .. (divides)
+    uint8_t pad0[7];
+    uint8_t nwait;               // at ControlRecord.nwait's offset
+    uint8_t flags;               // at ControlRecord.flags' offset: kCtrlBlock | kCtrlNext | kCtrlEnd
+    uint16_t nrec;               // value records that follow
+    uint64_t publish;            // bit i: publish row i when it is final
+    uint8_t pad1[24];
+    uint16_t wait[kCtrlWaits];   // rows to acquire first (kWaitPartial: outside terms only)
+};
+static_assert(sizeof(TermRecord) == kRecordBytes && sizeof(ControlRecord) == kRecordBytes &&
+                  sizeof(BlockRecord) == kRecordBytes, "record size");
+constexpr int kRoundHead = 12;           // doubles of a block round before its rows' terms
+// Doubles of a block's values (all rounds).
+SB_HD constexpr int block_values(int size) {
+    int v = 0;
+    for (int c0 = 0; c0 < size; c0 += 4) v += kRoundHead + 4 * (size - c0 - 4 > 0 ? size - c0 - 4 : 0);
+    return v;
+}
+// Largest block whose first round (the longest) fits a ring of ring_stages
+// stages from any starting byte of a stage.
+SB_HD constexpr int block_rows_for_ring(int ring_stages) {
+    const int room = (ring_stages * kStageBytes - (kStageBytes - 8)) / 8 - kRoundHead;   // doubles for the rows' terms
+    const int rows = 4 + room / 4;
+    return rows < kMaxBlockRows ? rows : kMaxBlockRows;
+}
+
 
 // Shared memory of a solve CTA: the slab's fields [B][stride] | the warps'
-// rings [kSweepWarps][ring_stages][kStageBytes] | ready flags [n + 1] | misc.
+// rings [kSweepWarps][ring_stages][kStageBytes] | ready flags [n + 1] |
+// ring stage barriers [kSweepWarps][kStagesMax] | misc.
 SB_HD constexpr int slab_stride(int n) { return ((n + 15) & ~15) + 2; }   // >= n + 1: slot n is zero
 // Doubles free between the sweeps (fields and rings): the air-side dense
 // systems and pw [B][k] live there.
@@ -114,7 +166,7 @@ SB_HD constexpr int dense_teams(int n, int k, int B, int ring_stages) {
 }
 SB_HD constexpr size_t solve_smem_bytes(int n, int B, int ring_stages) {
     return (size_t)B * slab_stride(n) * 8 + (size_t)kSweepWarps * ring_stages * kStageBytes +
-           (((size_t)n + 1 + 15) & ~(size_t)15) + 256;
+           (((size_t)n + 1 + 15) & ~(size_t)15) + (size_t)kSweepWarps * kStagesMax * 8 + 256;
 }
 
 // One triangular sweep: per-warp byte streams, each a whole number of stages.
@@ -187,7 +239,6 @@ struct ScnDev {
     int* occ_state0;     // [2][nz*assign] occupant states, same buffering
     int32_t* conv_pairs; // [2*ncv]: (dst, src) extended positions
     int* conv_npairs;
-    int32_t* conv_scratch; // per-room permutation scratch / swap lists
     int scn_index;
 };
 

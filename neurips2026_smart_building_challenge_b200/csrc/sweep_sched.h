@@ -15,8 +15,10 @@ struct HostSweep {
     uint32_t warp_stages[kSweepWarps] = {}; // stages in warp w's stream
     int ring_stages = 0;                    // ring depth the streams were laid out for
     // statistics of the schedule: terms, control records (bundles), term
-    // records (blocks), waits, published rows, row segments (pieces)
+    // records (blocks), waits, published rows and partial sums, row segments
+    // (pieces), dense block records and the rows they finish
     int64_t terms = 0, bundles = 0, blocks = 0, prewaits = 0, publishes = 0, pieces = 0;
+    int64_t dense_blocks = 0, block_rows = 0;
     double sim_cycles = 0;                  // modelled length of the sweep (cycles of one warp)
 };
 

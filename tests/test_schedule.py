@@ -2,9 +2,10 @@
 executed on the CPU with the kernel's semantics under several interleavings of
 the 16 warps. Every row must receive exactly the reference's terms in the
 reference's order (the column push of complete_port/csim/sb_lu.c:38-63), no
-bundle may read a row that is not final yet (a bundle starts only when the
-rows it waits for are published), no interleaving may deadlock, and the solve
-must equal the column-push replay bit for bit."""
+record may read a row that is not final yet (a record starts only when the
+rows it waits for are published), a dense block must find its rows' outside
+terms applied and acquired, no interleaving may deadlock, and the solve must
+equal the column-push replay bit for bit."""
 import ctypes
 import struct
 
@@ -15,8 +16,9 @@ from sbb_read import Blob
 
 REC, STAGE = 160, 480
 NEXT_CTRL, COL_MASK = 0x8000, 0x7FFF
-G_SWITCH, G_FINAL, G_DIVIDE, G_PUBLISH = 1, 2, 4, 8
-C_NEXT, C_END = 1, 2
+G_SWITCH, G_FINAL, G_DIVIDE, G_PUBLISH, G_PARTIAL = 1, 2, 4, 8, 16
+C_NEXT, C_END, C_BLOCK, C_DIVIDE, C_PUBLISH = 1, 2, 4, 8, 16
+W_PARTIAL = 0x8000
 
 
 def _programs(lib, blob, sweep, ring_stages):
@@ -38,25 +40,76 @@ def _programs(lib, blob, sweep, ring_stages):
     return out
 
 
+def _block_terms(vals, size, backward):
+    """(diag[j], v[i][j]) of a block from its round layout: per round of rows
+    c0..c0+3, 4 diagonals, the 6 in-round terms, 2 zeros, then four terms per
+    later row."""
+    diag, v, p = [1.0] * size, {}, 0
+    for c0 in range(0, size, 4):
+        for k in range(4):
+            if c0 + k < size:
+                diag[c0 + k] = float(vals[p + k]) if backward else 1.0
+            else:
+                assert vals[p + k] == 0.0
+            if not backward:
+                assert vals[p + k] == 0.0
+        t = p + 4
+        for r in range(1, 4):
+            for k in range(r):
+                if c0 + r < size:
+                    v[(c0 + r, c0 + k)] = float(vals[t])
+                else:
+                    assert vals[t] == 0.0
+                t += 1
+        assert vals[p + 10] == 0.0 and vals[p + 11] == 0.0
+        p += 12
+        for i in range(c0 + 4, size):
+            for k in range(4):
+                v[(i, c0 + k)] = float(vals[p])
+                p += 1
+    assert p == len(vals)
+    return diag, v
+
+
 def _parse(stream, n, backward):
-    """Records of one warp program: ("ctrl", rows, gflags, waits, diag) or
-    ("term", vals[4][4], cols[4][4]); it starts with a control record and ends
-    with one carrying the end flag, padded with zero bytes to whole stages."""
+    """Records of one warp program: ("ctrl", rows, gflags, waits, diag),
+    ("term", vals[4][4], cols[4][4]) or ("block", rows, waits, publish, vals);
+    it starts with a control record and ends with one carrying the end flag,
+    padded with zero bytes to whole stages."""
     assert len(stream) % STAGE == 0
     recs, pos, ctrl = [], 0, True
     while True:
         assert pos + REC <= len(stream), "program without an end record"
         if ctrl:
+            nwait, flags = stream[pos + 12], stream[pos + 13]
+            waits = list(struct.unpack_from(f"<{nwait}H", stream, pos + 48)) if nwait else []
+            assert nwait <= 56 and all((r & ~W_PARTIAL) <= n for r in waits)
+            if flags & C_BLOCK:
+                first, size, bw = struct.unpack_from("<HHB", stream, pos)
+                nrec = struct.unpack_from("<H", stream, pos + 14)[0]
+                publish = struct.unpack_from("<Q", stream, pos + 16)[0]
+                assert bw == int(backward) and 1 <= size <= 48 and not flags & C_END
+                rows = [first - j if backward else first + j for j in range(size)]
+                assert all(0 <= r < n for r in rows) and publish >> size == 0
+                nv = sum(12 + 4 * max(0, size - c0 - 4) for c0 in range(0, size, 4))
+                assert nrec == (nv * 8 + REC - 1) // REC
+                vals = np.frombuffer(stream, "<f8", nv, pos + REC)
+                assert not any(stream[pos + REC + 8 * nv:pos + REC * (1 + nrec)]), "block padding not zero"
+                recs.append(("block", rows, waits, publish, _block_terms(vals, size, backward)))
+                pos += REC * (1 + nrec)
+                assert flags & C_NEXT, "a block is followed by a control or block record"
+                continue
             rows = struct.unpack_from("<4H", stream, pos)
             gflags = list(stream[pos + 8:pos + 12])
-            nwait, flags = stream[pos + 12], stream[pos + 13]
             diag = struct.unpack_from("<4d", stream, pos + 16)
-            waits = list(struct.unpack_from(f"<{nwait}H", stream, pos + 48)) if nwait else []
-            assert nwait <= 56 and all(r <= n for r in rows) and all(r <= n for r in waits)
+            assert all(r <= n for r in rows)
             for g in range(4):
                 if gflags[g] & (G_DIVIDE | G_PUBLISH):
                     assert gflags[g] & G_FINAL
+                assert not (gflags[g] & G_PARTIAL and gflags[g] & G_FINAL)
                 assert bool(gflags[g] & G_DIVIDE) == (backward and bool(gflags[g] & G_FINAL))
+            assert bool(flags & C_DIVIDE) == any(f & G_DIVIDE for f in gflags)
+            assert bool(flags & C_PUBLISH) == any(f & (G_PUBLISH | G_PARTIAL) for f in gflags)
             recs.append(("ctrl", rows, gflags, waits, diag))
             pos += REC
             if flags & C_END:
@@ -77,8 +130,8 @@ def _parse(stream, n, backward):
 
 
 class _Warp:
-    def __init__(self, recs):
-        self.recs, self.i, self.phase = recs, 0, 0
+    def __init__(self, k, recs):
+        self.k, self.recs, self.i, self.phase = k, recs, 0, 0
         self.row, self.acc = [None] * 4, [0.0] * 4
 
     def finished(self):
@@ -86,16 +139,23 @@ class _Warp:
 
 
 def _execute(programs, x, n, backward, pick, expect):
-    """Runs the warps' records one at a time in the order pick() chooses."""
+    """Runs the warps' records (a dense block one step at a time) in the order
+    pick() chooses."""
     x = list(x) + [0.0]
     final = [False] * (n + 1)
     final[n] = True
     if not backward:
         for i in range(n):
             final[i] = not expect[i]
-    ready = [False] * n + [True]
+    ready = [False] * n + [True]        # final flag published
+    partial = [False] * n + [True]      # outside-terms flag published
+    writer = [None] * (n + 1)           # warp that last stored the row
+    acquired = [set() for _ in programs]   # rows whose partial flag a warp has acquired
     got = [[] for _ in range(n)]
-    warps = [_Warp(_parse(p, n, backward)) for p in programs]
+    warps = [_Warp(k, _parse(p, n, backward)) for k, p in enumerate(programs)]
+
+    def waits_met(waits):
+        return all(partial[r & ~W_PARTIAL] or ready[r & ~W_PARTIAL] if r & W_PARTIAL else ready[r] for r in waits)
 
     def step(wp):
         """One unit of warp wp; False if it is blocked."""
@@ -115,6 +175,41 @@ def _execute(programs, x, n, backward, pick, expect):
                         assert v == 0.0
             wp.i += 1
             return True
+        if rec[0] == "block":
+            _, rows, waits, publish, vals = rec
+            if wp.phase == 0:
+                assert all(r is None for r in wp.row), "a block starts with a group busy"
+                if not waits_met(waits):
+                    return False
+                for r in waits:
+                    if r & W_PARTIAL:
+                        acquired[wp.k].add(r & ~W_PARTIAL)
+                size = len(rows)
+                for i, r in enumerate(rows):   # outside terms applied, stored and visible
+                    assert len(got[r]) == len(expect[r]) - i, f"block row {r} misses outside terms"
+                    assert writer[r] in (None, wp.k) or r in acquired[wp.k], f"block row {r} not acquired"
+                wp.phase = 1
+            j = wp.phase - 1
+            diag, terms = vals
+            size = len(rows)
+            rj = rows[j]
+            a = x[rj]
+            if backward:
+                a = a / diag[j]
+            x[rj] = a
+            writer[rj] = wp.k
+            final[rj] = True
+            if publish >> j & 1:
+                ready[rj] = True
+            for i in range(j + 1, size):
+                v = terms[(i, j)]
+                x[rows[i]] = x[rows[i]] - v * a
+                got[rows[i]].append((rj, v))
+            wp.phase += 1
+            if wp.phase > size:
+                wp.phase = 0
+                wp.i += 1
+            return True
         _, rows, gflags, waits, diag = rec
         if wp.phase == 0:   # end segments (finish, pause), then the warp barrier
             for g in range(4):
@@ -127,11 +222,17 @@ def _execute(programs, x, n, backward, pick, expect):
                     final[r] = True
                     if gflags[g] & G_PUBLISH:
                         ready[r] = True
+                if gflags[g] & G_PARTIAL:
+                    partial[r] = True
                 x[r] = acc
+                writer[r] = wp.k
                 wp.row[g] = None
             wp.phase = 1
-        if not all(ready[r] for r in waits):
+        if not waits_met(waits):
             return False
+        for r in waits:
+            if r & W_PARTIAL:
+                acquired[wp.k].add(r & ~W_PARTIAL)
         for g in range(4):
             if gflags[g] & G_SWITCH:
                 r = rows[g]
@@ -232,19 +333,23 @@ def test_schedule_stats(built, tmp_path):
     lib.sb_sweep_stats.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_double)]
     L = Blob(blob).csc("lu_L")
     n = L.shape[0]
-    st = (ctypes.c_double * 8)()
+    st = (ctypes.c_double * 10)()
     for sweep in (0, 1):
         assert lib.sb_sweep_stats(str(blob).encode(), sweep, 5, st) == 0
         progs = _programs(lib, blob, sweep, 5)
         recs = [r for p in progs for r in _parse(p, n, sweep == 1)]
         ctrl = [r for r in recs if r[0] == "ctrl"]
+        blocks = [r for r in recs if r[0] == "block"]
         assert st[0] == L.nnz - n
         assert st[1] == len(ctrl)
-        assert st[2] == len(recs) - len(ctrl)
+        assert st[2] == len(recs) - len(ctrl) - len(blocks)
         assert st[3] == sum(int(r[2][g] & G_SWITCH and r[1][g] != n) for r in ctrl for g in range(4))
-        assert st[4] == sum(len(r[3]) for r in ctrl)
-        assert st[5] == sum(int(bool(r[2][g] & G_PUBLISH)) for r in ctrl for g in range(4))
+        assert st[4] == sum(len(r[3]) for r in ctrl) + sum(len(r[2]) for r in blocks)
+        assert st[5] == (sum(int(bool(r[2][g] & (G_PUBLISH | G_PARTIAL))) for r in ctrl for g in range(4)) +
+                         sum(bin(r[3]).count("1") for r in blocks))
         assert st[7] == sum(len(p) for p in progs)
+        assert st[8] == len(blocks) > 0
+        assert st[9] == sum(len(r[1]) for r in blocks)
     assert lib.sb_sweep_stats(str(blob).encode(), 0, 0, st) == 0          # default depth
     assert lib.sb_sweep_stats(str(blob).encode(), 2, 5, st) == -1         # no such sweep
     assert lib.sb_sweep_stats(str(blob).encode(), 0, 3, st) == -1         # ring too shallow
