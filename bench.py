@@ -266,12 +266,12 @@ def run_ours(args) -> None:
     status = env.status()
 
     # per-kernel durations (diagnostic steps after the timed region)
-    kt = {"k_rng": [], "k_pre": [], "k_solve": [], "k_post": []}
+    kt = {}
     for i in range(5):
         one_step(i)
         env.synchronize()
         for k, v in env.step_timed().items():
-            kt[k].append(v)
+            kt.setdefault(k, []).append(v)
     k_ms = {k: float(np.mean(v)) for k, v in kt.items()}
     bytes_launch = env.solve_bytes()
     peaks = {}

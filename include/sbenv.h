@@ -145,8 +145,9 @@ int sb_get_reward_f64(double* reward, double* parts);
 /* Number of hot-path kernel launches one puf_step enqueues. */
 int sb_kernels_per_step(void);
 /* Measurement: runs one step with CUDA events around each kernel on the bound
- * streams (not for graph capture). ms[4] = {k_rng, k_pre, k_solve, k_post}; k_rng
- * runs beside k_solve, inside its interval, and reports -1. */
+ * streams (not for graph capture). ms[7] = {k_rng, k_pre, solve, k_post, solve
+ * phase 0, k_dense, solve phase 1}; solve = phase 0 + k_dense + phase 1; k_rng
+ * runs beside phase 0, inside its interval, and reports -1. */
 int sb_step_timed(float* ms);
 /* Algorithmic bytes one solve launch must move for the loaded batch: per env the
  * field and interior mass read and written plus the per-zone heat and air-side

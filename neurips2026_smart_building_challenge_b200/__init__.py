@@ -303,10 +303,11 @@ class SmartBuildingsVec:
 
     def step_timed(self) -> dict:
         """One step with CUDA events around each kernel (diagnostic; not capturable)."""
-        ms = (ctypes.c_float * 4)()
+        ms = (ctypes.c_float * 7)()
         if self.lib.sb_step_timed(ms) != 0:
             raise RuntimeError("sb_step_timed failed")
-        return dict(zip(["k_rng", "k_pre", "k_solve", "k_post"], list(ms)))
+        return dict(zip(["k_rng", "k_pre", "k_solve", "k_post", "k_solve_phase0", "k_dense", "k_solve_phase1"],
+                        list(ms)))
 
     def solve_bytes(self) -> float:
         b = ctypes.c_double()

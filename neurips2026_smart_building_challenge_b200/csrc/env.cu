@@ -4,14 +4,16 @@
 // (puf_vec_create, puf_bind_stream, puf_init, puf_reset, puf_step, puf_close,
 // puf_log, puf_live_log, puf_mask_init). One step enqueues, on the bound
 // stream and two streams forked from it:
-//   k_pre   (main)  decode, actuators, zone sensing, VAV/AHU/boiler pre-step
-//   k_solve (side, after k_pre) fused thermal solve over slabs of envs in
-//           shared memory, one slab per SM
-//   k_rng   (side, a programmatic dependent of k_solve) per-scenario
-//           convection permutation + occupancy chains: it starts once every
-//           slab is resident and runs on the SMs the slabs leave free
-//   k_post  (main, after the side stream) convection apply, boiler,
-//           observation, reward, episode log, in-step restart
+//   k_pre      (main)  decode, actuators, zone sensing, VAV/AHU/boiler pre-step
+//   k_solve<0> (side, after k_pre) forcing and first L/U solve over slabs of
+//              envs in shared memory, one slab per SM; air-side right side
+//   k_rng      (side, a programmatic dependent of k_solve<0>) per-scenario
+//              convection permutation + occupancy chains: it starts once every
+//              slab is resident and runs on the SMs the slabs leave free
+//   k_dense    (side) the air-side dense solve of every env, one CTA each
+//   k_solve<1> (side) applied heat, second L/U solve, interior mass, field
+//   k_post     (main, after the side stream) convection apply, boiler,
+//              observation, reward, episode log, in-step restart
 // No host synchronisation, allocation or attribute change happens inside
 // puf_step, so a caller can capture it in a CUDA graph.
 #include <cuda_runtime.h>
@@ -105,7 +107,7 @@ struct Engine {
     Env* envs = nullptr;          // managed
     cudaStream_t stream = nullptr, own_stream = nullptr, side = nullptr, hi = nullptr;
     cudaEvent_t ev_fork = nullptr, ev_join = nullptr, ev_solve = nullptr;
-    size_t smem_solve = 0, smem_pre = 0, smem_post = 0, smem_rng = 0;
+    size_t smem_solve = 0, smem_pre = 0, smem_post = 0, smem_rng = 0, smem_dense = 0;
     int max_ncv = 0;
     bool ready = false;
     ~Engine() { destroy(); }
@@ -202,14 +204,26 @@ cudaError_t launch_rng_after_solve(Engine& E, cudaStream_t st, int reset_only) {
     return cudaLaunchKernelEx(&cfg, k_rng, (const StepCtx*)E.d_ctx, E.d_scn_step, E.d_rng_out, reset_only);
 }
 
+// The solve on the high-priority stream: phase 0 (first L/U solve), the
+// random streams as its programmatic dependent, the dense air-side solves,
+// phase 1 (second L/U solve, mass, field).
+cudaError_t launch_solve(Engine& E) {
+    const unsigned slabs = (unsigned)E.slabs.size();
+    k_solve<0><<<slabs, kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = launch_rng_after_solve(E, E.hi, 0);
+    if (e != cudaSuccess) return e;
+    k_dense<<<(unsigned)E.n_env, kMaxK, E.smem_dense, E.hi>>>(E.d_ctx);
+    k_solve<1><<<slabs, kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
+    return cudaGetLastError();
+}
+
 bool launch_step(Engine& E) {
     k_pre<<<(unsigned)E.n_env, 128, E.smem_pre, E.stream>>>(E.d_ctx);
     CK(cudaGetLastError());
     CK(cudaEventRecord(E.ev_fork, E.stream));
     CK(cudaStreamWaitEvent(E.hi, E.ev_fork, 0));
-    k_solve<<<(unsigned)E.slabs.size(), kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
-    CK(cudaGetLastError());
-    CK(launch_rng_after_solve(E, E.hi, 0));
+    CK(launch_solve(E));
     CK(cudaEventRecord(E.ev_join, E.hi));
     CK(cudaStreamWaitEvent(E.stream, E.ev_join, 0));
     k_post<<<(unsigned)E.n_env, 128, E.smem_post, E.stream>>>(E.d_ctx);
@@ -306,26 +320,22 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
     }
-    // bmin: the narrowest slab whose free memory between the sweeps holds the
-    // air-side dense system
-    std::vector<int> bmax(NG), bmin(NG);
+    std::vector<int> bmax(NG);
     for (int c = 0; c < NG; c++) {
         const HostGroup& h = E.hg[c];
-        bmax[c] = bmin[c] = 0;
+        bmax[c] = 0;
         for (int b = slab_cap; b >= 1 && !bmax[c]; b--)
             if (solve_ring_stages(h.n, b, smem_cap) > 0) bmax[c] = b;
-        for (int b = 1; b <= bmax[c] && !bmin[c]; b++)
-            if (h.k == 0 || dense_teams(h.n, h.k, b, solve_ring_stages(h.n, b, smem_cap)) >= 1) bmin[c] = b;
         if (!bmax[c]) {
             set_err("group %d: one env's field (%d cells) exceeds shared memory", c, h.n);
             return false;
         }
-        if (!bmin[c]) {
-            set_err("group %d: the %d x %d air-side system does not fit in shared memory", c, h.k, h.k);
+        if (h.k > kMaxK) {
+            set_err("group %d: %d coupled VAVs (at most %d)", c, h.k, kMaxK);
             return false;
         }
     }
-    auto width = [&](int c, int b) { return std::max(bmin[c], std::min(b, bmax[c])); };
+    auto width = [&](int c, int b) { return std::min(b, bmax[c]); };
     // SMs left to the random-stream blocks, which run beside the solve (each
     // needs the shared memory of one scenario's convection tables)
     long sm_budget = n_sm;
@@ -344,34 +354,8 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
         for (int c = 0; c < NG; c++) slabs += (E.gd[c].n_env + width(c, b) - 1) / width(c, b);
         if (slabs <= sm_budget) { bwave = b; break; }
     }
-    // then narrow the slabs of the group with the most dense-solve work (rounds
-    // of team solves x k^2) while the slabs still fit in one wave: slabs run
-    // side by side, so the slowest one sets the step time
     std::vector<int> bsel(NG);
-    long slabs_now = 0;
-    for (int c = 0; c < NG; c++) {
-        bsel[c] = width(c, bwave);
-        slabs_now += (E.gd[c].n_env + bsel[c] - 1) / bsel[c];
-    }
-    auto rounds = [&](int c, int b) {
-        const HostGroup& h = E.hg[c];
-        if (h.k == 0) return 0;
-        const int t = dense_teams(h.n, h.k, b, solve_ring_stages(h.n, b, smem_cap));
-        return (b + t - 1) / t;
-    };
-    auto dense_cost = [&](int c, int b) { return (double)rounds(c, b) * E.hg[c].k * E.hg[c].k; };
-    for (int it = 0; it < 64; it++) {
-        int worst = 0;
-        for (int c = 1; c < NG; c++)
-            if (dense_cost(c, bsel[c]) > dense_cost(worst, bsel[worst])) worst = c;
-        int nb = bsel[worst] - 1;
-        while (nb >= bmin[worst] && rounds(worst, nb) >= rounds(worst, bsel[worst])) nb--;
-        if (nb < bmin[worst] || dense_cost(worst, bsel[worst]) == 0.0) break;
-        const long delta = (long)(E.gd[worst].n_env + nb - 1) / nb - (E.gd[worst].n_env + bsel[worst] - 1) / bsel[worst];
-        if (slabs_now + delta > sm_budget) break;
-        slabs_now += delta;
-        bsel[worst] = nb;
-    }
+    for (int c = 0; c < NG; c++) bsel[c] = width(c, bwave);
     for (int c = 0; c < NG; c++) {
         HostGroup& h = E.hg[c];
         GroupDev& gd = E.gd[c];
@@ -503,6 +487,18 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     C.ep_scn = E.arena.zeros<double>((size_t)G * 2, ok);
     C.status = E.arena.zeros<int>(1, ok);
     C.nz_max = nz_max;
+    // air side: right side / solution per env; k_dense runs the heaviest envs first
+    C.k_max = std::max(k_max, 1);
+    C.airq = E.arena.zeros<double>((size_t)n * C.k_max, ok);
+    {
+        std::vector<int> order(n);
+        for (int env = 0; env < n; env++) order[env] = env;
+        std::stable_sort(order.begin(), order.end(), [&](int a, int b) {
+            return E.hs[E.ei[a].scn].k > E.hs[E.ei[b].scn].k;
+        });
+        C.dense_order = E.arena.upload(order, ok);
+    }
+    E.smem_dense = std::max<size_t>(16, dense_env_doubles(k_max) * sizeof(double));
     double* vbuf = E.arena.zeros<double>((size_t)3 * G * nz_max, ok);
     C.V_step = vbuf;
     C.V_prime = vbuf + (size_t)G * nz_max;
@@ -538,7 +534,10 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     if (!ok) return false;
     // ---- launch configuration (once; never inside a step) ----
     if (E.smem_solve > smem_cap) { set_err("solve kernel needs %zu B of shared memory", E.smem_solve); return false; }
-    CK(cudaFuncSetAttribute(k_solve, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_solve));
+    if (E.smem_dense > smem_cap) { set_err("dense kernel needs %zu B of shared memory", E.smem_dense); return false; }
+    CK(cudaFuncSetAttribute(k_solve<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_solve));
+    CK(cudaFuncSetAttribute(k_solve<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_solve));
+    CK(cudaFuncSetAttribute(k_dense, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_dense));
     CK(cudaFuncSetAttribute(k_pre, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_pre));
     CK(cudaFuncSetAttribute(k_post, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_post));
     CK(cudaFuncSetAttribute(k_reset, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_post));
@@ -791,7 +790,7 @@ void sb_shape(int* out) {
         out[5] = std::max(out[5], s.n_disc);
     }
     out[6] = (int)E.slabs.size();
-    out[7] = 4;
+    out[7] = 6;
 }
 
 void sb_env_info(int* obs_len, int* scenario) {
@@ -845,23 +844,28 @@ int sb_get_reward_f64(double* reward, double* parts) {
     return 0;
 }
 
-int sb_kernels_per_step(void) { return 4; }
+int sb_kernels_per_step(void) { return 6; }
 
 int sb_step_timed(float* ms) {
     if (!g_eng || !g_eng->ready || !ms) return -1;
     Engine& E = *g_eng;
-    cudaEvent_t ev[7];
+    cudaEvent_t ev[9];
     for (auto& e : ev)
         if (cudaEventCreate(&e) != cudaSuccess) return -1;
-    // the step of launch_step with events around each kernel (k_solve and
-    // k_rng share their stream: ev[2] closes both, k_rng is timed alone below)
+    // the step of launch_step with events around each kernel (k_solve phase 0
+    // and k_rng share their stream: ev[4] closes both)
     cudaEventRecord(ev[0], E.stream);
     k_pre<<<(unsigned)E.n_env, 128, E.smem_pre, E.stream>>>(E.d_ctx);
     cudaEventRecord(ev[1], E.stream);
     cudaEventRecord(E.ev_fork, E.stream);
     cudaStreamWaitEvent(E.hi, E.ev_fork, 0);
-    k_solve<<<(unsigned)E.slabs.size(), kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
+    const unsigned slabs = (unsigned)E.slabs.size();
+    k_solve<0><<<slabs, kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
     launch_rng_after_solve(E, E.hi, 0);
+    cudaEventRecord(ev[4], E.hi);
+    k_dense<<<(unsigned)E.n_env, kMaxK, E.smem_dense, E.hi>>>(E.d_ctx);
+    cudaEventRecord(ev[5], E.hi);
+    k_solve<1><<<slabs, kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
     cudaEventRecord(ev[2], E.hi);
     cudaStreamWaitEvent(E.stream, ev[2], 0);
     cudaEventRecord(ev[6], E.stream);
@@ -869,10 +873,13 @@ int sb_step_timed(float* ms) {
     cudaEventRecord(ev[3], E.stream);
     const bool ok = cudaEventSynchronize(ev[3]) == cudaSuccess;
     if (ok) {
-        ms[0] = -1.0f;                                 // k_rng runs beside k_solve, inside ms[2]
+        ms[0] = -1.0f;                                 // k_rng runs beside k_solve phase 0, inside ms[4]
         cudaEventElapsedTime(&ms[1], ev[0], ev[1]);   // k_pre
-        cudaEventElapsedTime(&ms[2], ev[1], ev[2]);   // k_solve (with k_rng beside it)
+        cudaEventElapsedTime(&ms[2], ev[1], ev[2]);   // the solve: phase 0, k_dense, phase 1
         cudaEventElapsedTime(&ms[3], ev[6], ev[3]);   // k_post
+        cudaEventElapsedTime(&ms[4], ev[1], ev[4]);   // phase 0 (with k_rng beside it)
+        cudaEventElapsedTime(&ms[5], ev[4], ev[5]);   // k_dense
+        cudaEventElapsedTime(&ms[6], ev[5], ev[2]);   // phase 1
     }
     for (auto& e : ev) cudaEventDestroy(e);
     return ok ? 0 : -1;

@@ -93,14 +93,18 @@ struct StageRing {
         }
         return __all_sync(0xffffffffu, ok);
     }
-    // stages < t are consumed: their slots are refilled
-    __device__ void consume(uint32_t t, int lane) {
-        if (head >= t) return;
+    // stages < t (t <= head + R) are consumed: their slots are refilled. A
+    // slot is refilled only after its copy has arrived, also for stages that
+    // were skipped unread. Warp-uniform, false on timeout.
+    __device__ bool consume(uint32_t t, int lane) {
+        if (head >= t) return true;
+        if (!land(t - 1)) return false;
         __syncwarp();   // every lane is done reading the slots
         for (; head < t; head++) {
             if (lane == 0 && head + R < nst) issue(head + R, hslot);
             if (++hslot == R) hslot = 0;
         }
+        return true;
     }
     // no copy may land after the sweep (the ring memory is reused): wait for
     // the stages in flight, then retire the barriers
@@ -117,14 +121,12 @@ struct StageRing {
 
 // One dense block record (format in sbenv_dev.h), the cursor at its header
 // (stage rg.head, record hq). Lane group g holds the block's rows i = g mod 4,
-// one lane per env, their partial sums in registers: slot u is the group's
-// row c0 + g + 4u of the current round c0, and after every round the slots
-// shift down by one. Inside a round the four rows finish in turn (x_k from
-// group k to all lanes by a shuffle); the later rows then take the round's
-// four values from one 32-byte run of terms each. Returns the record index
-// after the block's values, or 0xFFFFFFFF on an error (reported in sh.abort).
-constexpr int kBlockSlots = kMaxBlockRows / kBundleRows;
-
+// one lane per env. Round c0: group g's row c0 + g loads its partial sum,
+// pulls its terms from rows 0..c0-1 (final values in shared memory), then the
+// round's four rows finish in turn, x_k from group k to all lanes by a
+// shuffle. A round lies contiguous in the ring, so its values are read at
+// fixed offsets from one pointer. Returns the record index after the block's
+// values, or 0xFFFFFFFF on an error (reported in sh.abort).
 __device__ inline uint32_t run_block(const SolveShared& sh, StageRing& rg, uint32_t hq, double* __restrict__ xe,
                                      bool owns, uint32_t n, uint32_t fin) {
     const unsigned full = 0xffffffffu;
@@ -135,7 +137,8 @@ __device__ inline uint32_t run_block(const SolveShared& sh, StageRing& rg, uint3
     const uint64_t pubm = b->publish;
     const uint32_t lastrow = bw ? first - (size - 1) : first + (size - 1);
     const uint32_t hidx = rg.head * kRecordsPerStage + hq;
-    if (size == 0 || size > (uint32_t)block_rows_for_ring((int)rg.R) || first >= n || lastrow >= n ||
+    const uint32_t vend = (hidx + 1 + nrec) * kRecordBytes;   // stream byte after the values
+    if (size == 0 || size > (uint32_t)kMaxBlockRows || bw > 1 || first >= n || lastrow >= n ||
         nrec * (uint32_t)kRecordBytes < (uint32_t)block_values((int)size) * 8u ||
         (hidx + 1 + nrec) / kRecordsPerStage >= rg.nst) {
         atomicCAS((int*)sh.abort, 0, kErrBadBundle);
@@ -144,41 +147,49 @@ __device__ inline uint32_t run_block(const SolveShared& sh, StageRing& rg, uint3
     if (nw && !wait_rows(sh, b->wait, min(nw, (uint32_t)kCtrlWaits), n, fin)) return 0xFFFFFFFFu;
     const int dir = bw ? -1 : 1;
     const uint32_t RB = rg.R * kStageBytes;
-    const uint8_t* __restrict__ ring = rg.ring;
-    double acc[kBlockSlots];
-#pragma unroll
-    for (int u = 0; u < kBlockSlots; u++) {
-        const uint32_t i = g + 4 * u;
-        acc[u] = i < size ? xe[(int)first + dir * (int)i] : 0.0;
-    }
-    // value cursor: stage vst (slot vslot), byte vb within it; rounds keep it 16-byte aligned
-    uint32_t vst = rg.head, vslot = rg.hslot, vb = (hq + 1) * kRecordBytes;
-    if (vb == kStageBytes) {
-        vst++; vb = 0;
-        if (++vslot == rg.R) vslot = 0;
-    }
-    rg.consume(vst, lane);   // the header's stage, if the values start after it
-    // this group's in-round terms (k < g at triangle index g(g-1)/2 + k) and diagonal
+    const double* __restrict__ xb = xe + (int)first;   // block row j at xb[dir * j]
+    // value cursor: stream byte vo, its ring offset vr
+    uint32_t vo = (hidx + 1) * kRecordBytes;
+    uint32_t vr = rg.hslot * kStageBytes + (hq + 1) * kRecordBytes;
+    if (vr >= RB) vr -= RB;
+    // this group's in-round terms (k < g at triangle index g(g-1)/2 + k)
     const uint32_t tri0 = g * (g - 1) / 2;
+    const uint32_t o0 = 32 + 8 * min(tri0 + 0, 5u), o1 = 32 + 8 * min(tri0 + 1, 5u), o2 = 32 + 8 * min(tri0 + 2, 5u);
     for (uint32_t c0 = 0; c0 < size; c0 += 4) {
-        const uint32_t after = size > c0 + 4 ? size - c0 - 4 : 0;   // rows after the round
-        const uint32_t rbytes = (kRoundHead + 4 * after) * 8;
-        if (!rg.land(vst + (vb + rbytes - 1) / kStageBytes)) {
+        const uint32_t rbytes = (kRoundHead + 4 * c0) * 8;
+        if (vr + rbytes > RB) {   // the round starts at the ring's start
+            vo += RB - vr;
+            vr = 0;
+        }
+        if (vo + rbytes > vend) {
+            atomicCAS((int*)sh.abort, 0, kErrBadBundle);
+            return 0xFFFFFFFFu;
+        }
+        if (!rg.consume(vo / kStageBytes, lane) || !rg.land((vo + rbytes - 1) / kStageBytes)) {
             atomicCAS((int*)sh.abort, 0, kErrRingTimeout);
             return 0xFFFFFFFFu;
         }
-        const uint32_t base = vslot * kStageBytes + vb;   // ring offset of the round
-        auto val = [&](uint32_t off) {
-            uint32_t a = base + off;
-            if (a >= RB) a -= RB;
-            return *reinterpret_cast<const double*>(ring + a);
-        };
-        const double dg = bw ? val(8 * g) : 1.0;
-        const double t0 = val(32 + 8 * min(tri0 + 0, 5u));
-        const double t1 = val(32 + 8 * min(tri0 + 1, 5u));
-        const double t2 = val(32 + 8 * min(tri0 + 2, 5u));
+        const uint8_t* __restrict__ rp = rg.ring + vr;
+        const bool mine = c0 + g < size;
+        const int row = (int)first + dir * (int)(c0 + g);
+        // the row's partial sum, then its terms from the earlier rounds in order
+        double a = xe[mine ? row : (int)first];
+        const uint8_t* __restrict__ tv = rp + kRoundHead * 8 + 8 * c0 * g;
+        for (uint32_t j = 0; j < c0; j += 4) {
+            const double2 v01 = *reinterpret_cast<const double2*>(tv + 8 * j);
+            const double2 v23 = *reinterpret_cast<const double2*>(tv + 8 * j + 16);
+            const double x0 = xb[dir * (int)j], x1 = xb[dir * (int)(j + 1)];
+            const double x2 = xb[dir * (int)(j + 2)], x3 = xb[dir * (int)(j + 3)];
+            a = dsub(a, dmul(v01.x, x0));
+            a = dsub(a, dmul(v01.y, x1));
+            a = dsub(a, dmul(v23.x, x2));
+            a = dsub(a, dmul(v23.y, x3));
+        }
+        const double dg = bw ? *reinterpret_cast<const double*>(rp + 8 * g) : 1.0;
+        const double t0 = *reinterpret_cast<const double*>(rp + o0);
+        const double t1 = *reinterpret_cast<const double*>(rp + o1);
+        const double t2 = *reinterpret_cast<const double*>(rp + o2);
         // the four rows in turn: group k's row is final at stage k
-        double a = acc[0];
         const double x0 = __shfl_sync(full, bw ? ddiv(a, dg) : a, e);
         if (g > 0) a = dsub(a, dmul(t0, x0));
         const double x1 = __shfl_sync(full, bw ? ddiv(a, dg) : a, 8 | e);
@@ -186,52 +197,19 @@ __device__ inline uint32_t run_block(const SolveShared& sh, StageRing& rg, uint3
         const double x2 = __shfl_sync(full, bw ? ddiv(a, dg) : a, 16 | e);
         if (g > 2) a = dsub(a, dmul(t2, x2));
         const double x3 = __shfl_sync(full, bw ? ddiv(a, dg) : a, 24 | e);
-        // the round's rows are final: store, publish those other warps read
-        const bool mine = c0 + g < size;
-        const int row = (int)first + dir * (int)(c0 + g);
+        // the round's rows are final: store (later rounds read them), publish
+        // those other warps read
         const double xm = g == 0 ? x0 : g == 1 ? x1 : g == 2 ? x2 : x3;
         if (mine && owns) xe[row] = xm;
-        const uint32_t pr = (uint32_t)(pubm >> c0) & 0xFu;
-        if (pr) {
-            __syncwarp();
-            if (mine && e == 0 && ((pr >> g) & 1u)) {
-                __threadfence_block();
-                st_release_u8(sh.ready + row, fin);
-            }
+        __syncwarp();
+        const uint32_t pb = (uint32_t)(pubm >> c0) & 0xFu;
+        if (pb && mine && e == 0 && ((pb >> g) & 1u)) {
+            __threadfence_block();
+            st_release_u8(sh.ready + row, fin);
         }
-        // later rows: four terms each, in column order; chunks of four slots
-        // while some group still has rows there
-        const uint32_t live = (after + 3) / 4;   // slots 1..live
-#pragma unroll
-        for (int c = 1; c < kBlockSlots; c += 4) {
-            if ((uint32_t)c > live) break;   // warp-uniform
-#pragma unroll
-            for (int u = c; u < c + 4 && u < kBlockSlots; u++) {
-                const bool use = c0 + g + 4 * u < size;
-                uint32_t o = base + kRoundHead * 8 + 32 * (g + 4 * (u - 1));
-                if (o >= RB) o -= RB;
-                if (!use) o = base;
-                uint32_t o2 = o + 16;   // the run may wrap around the ring end
-                if (o2 >= RB) o2 -= RB;
-                const double2 v01 = *reinterpret_cast<const double2*>(ring + o);
-                const double2 v23 = *reinterpret_cast<const double2*>(ring + o2);
-                double r = acc[u];
-                r = dsub(r, dmul(v01.x, x0));
-                r = dsub(r, dmul(v01.y, x1));
-                r = dsub(r, dmul(v23.x, x2));
-                r = dsub(r, dmul(v23.y, x3));
-                acc[u] = use ? r : acc[u];
-            }
-        }
-#pragma unroll
-        for (int u = 0; u + 1 < kBlockSlots; u++) acc[u] = acc[u + 1];
-        vb += rbytes;
-        while (vb >= kStageBytes) {
-            vb -= kStageBytes;
-            vst++;
-            if (++vslot == rg.R) vslot = 0;
-        }
-        rg.consume(vst, lane);
+        vo += rbytes;
+        vr += rbytes;
+        if (vr == RB) vr = 0;
     }
     return hidx + 1 + nrec;
 }
@@ -283,8 +261,7 @@ __device__ inline void run_sweep(const SolveShared& sh, const Sweep& sw, int B, 
             if (cf & kCtrlBlock) {
                 const uint32_t next = run_block(sh, rg, q, xe, owns, un, fin);
                 if (next == 0xFFFFFFFFu) { err = kErrBadBundle; break; }
-                rg.consume(next / kRecordsPerStage, lane);
-                if (!rg.land(rg.head)) { err = kErrRingTimeout; break; }
+                if (!rg.consume(next / kRecordsPerStage, lane) || !rg.land(rg.head)) { err = kErrRingTimeout; break; }
                 q = next % kRecordsPerStage;
                 rp = rg.ring + (size_t)rg.hslot * kStageBytes + q * kRecordBytes;
                 ctrl = true;   // a block is followed by a control or block record
@@ -317,7 +294,7 @@ __device__ inline void run_sweep(const SolveShared& sh, const Sweep& sw, int B, 
         }
         // next record
         if (++q == kRecordsPerStage) {
-            rg.consume(rg.head + 1, lane);
+            if (!rg.consume(rg.head + 1, lane)) { err = kErrRingTimeout; break; }
             if (rg.head >= rg.nst) { err = kErrBadBundle; break; }
             if (!rg.land(rg.head)) { err = kErrRingTimeout; break; }
             q = 0;
@@ -447,6 +424,38 @@ __device__ inline void dense_team(double* M, int k, int ttid, int T, int bar) {
     team_sync(bar, T);
 }
 
+// Air-side dense solve of every env, one CTA per env (heaviest groups first):
+// M = I + diag(g) S (sb_fdm.c:160-170) in shared memory, column-major with
+// the right side ctx->airq as column k, solved by dense_team; the solution
+// replaces the right side in ctx->airq. Envs whose VAV gains are all zero
+// (or whose building couples no VAV) have no air side and return at once.
+__global__ void __launch_bounds__(kMaxK) k_dense(const StepCtx* __restrict__ ctx) {
+    extern __shared__ __align__(16) double dsm[];
+    const int env = ctx->dense_order[blockIdx.x];
+    const ScnDev& sc = ctx->scns[ctx->envs[env].scn];
+    const GroupDev& g = ctx->groups[sc.group];
+    const StateLayout& L = ctx->lay;
+    const int k = g.k, tid = threadIdx.x;
+    if (k == 0) return;
+    const double* D = ctx->Dst + (size_t)env * L.nd;
+    if (!__syncthreads_or(tid < k && D[L.ag + tid] != 0.0)) return;
+    double* q = ctx->airq + (size_t)env * ctx->k_max;
+    const int per = k * (k + 1);
+    for (int idx = tid; idx < per; idx += blockDim.x) {
+        const int j = idx / k, i = idx % k;
+        dsm[idx] = j < k ? dadd(i == j ? 1.0 : 0.0, dmul(D[L.ag + i], g.S[(size_t)i * k + j])) : q[i];
+    }
+    __syncthreads();
+    const int T = ((k + 31) >> 5) * 32;
+    if (tid < T) dense_team(dsm, k, tid, T, 1);
+    __syncthreads();
+    for (int i = tid; i < k; i += blockDim.x) q[i] = dsm[per + 16 + i];
+}
+
+// Phase 0: forcing, first L/U solve, sensed air-side right side (to
+// ctx->airq), y to the field. Phase 1 (after k_dense): applied heat of the
+// dense solution, second L/U solve, interior mass and field.
+template <int Phase>
 __global__ void __launch_bounds__(kSolveThreads, 1)
 k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -492,120 +501,92 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
     }
     __syncthreads();
 
-    // ---- forcing (sb_fdm.c:146-152), written in row order: one thread per
-    // row for all envs of the slab, the row's coefficients loaded once ----
-    const int local0 = sd.env0 - g.env0;
-    for (int i = tid; i < n; i += blockDim.x) {
-        const double cap = g.cap[i], dirx = g.dirx[i], mc = g.mc[i];
-        const int z = g.zone_of_row[i];
-        double Ti[kGroupLanes], Mi[kGroupLanes], qi[kGroupLanes];
-#pragma unroll
-        for (int e = 0; e < kGroupLanes; e++) {
-            if (e >= nenv) break;
-            Ti[e] = g.T[(size_t)(local0 + e) * ncv + i];
-            Mi[e] = g.M[(size_t)(local0 + e) * n + i];
-            qi[e] = z >= 0 ? ctx->Dst[(size_t)(sd.env0 + e) * L.nd + L.qdiv + z] : 0.0;
-        }
-#pragma unroll
-        for (int e = 0; e < kGroupLanes; e++) {
-            if (e >= nenv) break;
-            double b = dadd(dmul(cap, Ti[e]), qi[e]);
-            b = dadd(b, dmul(amb_e[e], dirx));
-            b = dadd(b, dmul(mc, Mi[e]));
-            sh.X[(size_t)e * S + i] = b;
-        }
-    }
-    __syncthreads();
-
-    // ---- first solve ----
-    if (tid < kSweepWarps * 32) run_sweep(sh, g.fwd, B, S, n, 1);
-    __syncthreads();
-    if (tid < kSweepWarps * 32) run_sweep(sh, g.bwd, B, S, n, 2);
-    __syncthreads();
-    if (*sh.abort) {   // uniform: read after the barrier
-        if (tid == 0) set_error(ctx->status, *sh.abort);
-        return;
-    }
-
-    // ---- air side (sb_fdm.c:155-181) ----
-    // between the sweeps the fields and the rings are free: the dense
-    // workspace starts at the fields, the air-side vector pw sits at the end
-    // of the rings (dense_workspace_doubles() is checked on the host)
-    const size_t free_doubles = ((size_t)B * S * 8 + (size_t)kSweepWarps * R * kStageBytes) / 8;
-    double* pw = sh.X + free_doubles - (size_t)B * k;   // [B][k]
     int any_active = 0;
     for (int e = 0; e < nenv; e++) any_active |= active[e];
-    if (k > 0 && any_active) {
-        // sensed temperature of each coupled VAV: one thread per VAV for all
-        // envs, its terms fetched eight at a time, summed in order per env
-        for (int i = tid; i < k; i += blockDim.x) {
-            double acc[kGroupLanes];
+    if (Phase == 0) {
+        // ---- forcing (sb_fdm.c:146-152), written in row order: one thread per
+        // row for all envs of the slab, the row's coefficients loaded once ----
+        const int local0 = sd.env0 - g.env0;
+        for (int i = tid; i < n; i += blockDim.x) {
+            const double cap = g.cap[i], dirx = g.dirx[i], mc = g.mc[i];
+            const int z = g.zone_of_row[i];
+            double Ti[kGroupLanes], Mi[kGroupLanes], qi[kGroupLanes];
 #pragma unroll
-            for (int e = 0; e < kGroupLanes; e++) acc[e] = 0.0;
-            const int p0 = g.sn_p[i], p1 = g.sn_p[i + 1];
-            for (int p = p0; p < p1; p += 8) {
-                double xv[8];
-                int pos[8];
-#pragma unroll
-                for (int u = 0; u < 8; u++) {
-                    xv[u] = p + u < p1 ? g.sn_x[p + u] : 0.0;
-                    pos[u] = p + u < p1 ? g.sn_pos[p + u] : 0;
-                }
-#pragma unroll
-                for (int u = 0; u < 8; u++) {
-                    if (p + u >= p1) break;
-#pragma unroll
-                    for (int e = 0; e < kGroupLanes; e++)
-                        if (e < nenv) acc[e] = dadd(acc[e], dmul(xv[u], sh.X[(size_t)e * S + pos[u]]));
-                }
+            for (int e = 0; e < kGroupLanes; e++) {
+                if (e >= nenv) break;
+                Ti[e] = g.T[(size_t)(local0 + e) * ncv + i];
+                Mi[e] = g.M[(size_t)(local0 + e) * n + i];
+                qi[e] = z >= 0 ? ctx->Dst[(size_t)(sd.env0 + e) * L.nd + L.qdiv + z] : 0.0;
             }
 #pragma unroll
             for (int e = 0; e < kGroupLanes; e++) {
                 if (e >= nenv) break;
-                if (!active[e]) continue;
-                const double* D = ctx->Dst + (size_t)(sd.env0 + e) * L.nd;
-                pw[e * k + i] = dmul(D[L.ag + i], dsub(D[L.aT + i], acc[e]));
+                double b = dadd(dmul(cap, Ti[e]), qi[e]);
+                b = dadd(b, dmul(amb_e[e], dirx));
+                b = dadd(b, dmul(mc, Mi[e]));
+                sh.X[(size_t)e * S + i] = b;
             }
         }
-    }
-    // y -> the field array (row positions); the second solve adds to it
-    for (int i = tid; i < n; i += blockDim.x) {
+        __syncthreads();
+
+        // ---- first solve ----
+        if (tid < kSweepWarps * 32) run_sweep(sh, g.fwd, B, S, n, 1);
+        __syncthreads();
+        if (tid < kSweepWarps * 32) run_sweep(sh, g.bwd, B, S, n, 2);
+        __syncthreads();
+        if (*sh.abort) {   // uniform: read after the barrier
+            if (tid == 0) set_error(ctx->status, *sh.abort);
+            return;
+        }
+
+        // ---- air side (sb_fdm.c:155-181): the sensed right side to ctx->airq ----
+        if (k > 0 && any_active) {
+            // sensed temperature of each coupled VAV: one thread per VAV for all
+            // envs, its terms fetched eight at a time, summed in order per env
+            for (int i = tid; i < k; i += blockDim.x) {
+                double acc[kGroupLanes];
 #pragma unroll
-        for (int e = 0; e < kGroupLanes; e++)
-            if (e < nenv) g.T[(size_t)(local0 + e) * ncv + i] = sh.X[(size_t)e * S + i];
-    }
-    __syncthreads();
-    if (k > 0 && any_active) {
-        // one team of warps per env (thread p owns row p), as many envs at once
-        // as the free memory holds (at most 15: named barriers 1..15)
-        const size_t per_env = dense_env_doubles(k);
-        const int wpt = (k + 31) >> 5;                 // warps per team
-        const int cap = dense_teams(n, k, B, R);       // >= 1 (host check)
-        for (int e0 = 0; e0 < nenv; e0 += cap) {
-            const int ce = (nenv - e0) < cap ? (nenv - e0) : cap;
-            const int per = k * (k + 1);
-            for (int idx = tid; idx < ce * per; idx += blockDim.x) {
-                const int e = idx / per, rem = idx % per, j = rem / k, i = rem % k;   // column-major
-                if (!active[e0 + e]) continue;
-                const double* D = ctx->Dst + (size_t)(sd.env0 + e0 + e) * L.nd;
-                sh.X[e * per_env + (size_t)j * k + i] =
-                    j < k ? dadd(i == j ? 1.0 : 0.0, dmul(D[L.ag + i], g.S[(size_t)i * k + j])) : pw[(e0 + e) * k + i];
+                for (int e = 0; e < kGroupLanes; e++) acc[e] = 0.0;
+                const int p0 = g.sn_p[i], p1 = g.sn_p[i + 1];
+                for (int p = p0; p < p1; p += 8) {
+                    double xv[8];
+                    int pos[8];
+#pragma unroll
+                    for (int u = 0; u < 8; u++) {
+                        xv[u] = p + u < p1 ? g.sn_x[p + u] : 0.0;
+                        pos[u] = p + u < p1 ? g.sn_pos[p + u] : 0;
+                    }
+#pragma unroll
+                    for (int u = 0; u < 8; u++) {
+                        if (p + u >= p1) break;
+#pragma unroll
+                        for (int e = 0; e < kGroupLanes; e++)
+                            if (e < nenv) acc[e] = dadd(acc[e], dmul(xv[u], sh.X[(size_t)e * S + pos[u]]));
+                    }
+                }
+#pragma unroll
+                for (int e = 0; e < kGroupLanes; e++) {
+                    if (e >= nenv) break;
+                    if (!active[e]) continue;
+                    const double* D = ctx->Dst + (size_t)(sd.env0 + e) * L.nd;
+                    ctx->airq[(size_t)(sd.env0 + e) * ctx->k_max + i] = dmul(D[L.ag + i], dsub(D[L.aT + i], acc[e]));
+                }
             }
-            __syncthreads();
-            const int team = (tid >> 5) / wpt;
-            if (team < ce && active[e0 + team])
-                dense_team(sh.X + team * per_env, k, tid - team * wpt * 32, wpt * 32, 1 + team);
-            __syncthreads();
-            for (int idx = tid; idx < ce * k; idx += blockDim.x) {
-                const int e = idx / k, i = idx % k;
-                if (active[e0 + e]) pw[(e0 + e) * k + i] = sh.X[e * per_env + (size_t)k * (k + 1) + 16 + i];
-            }
-            __syncthreads();
         }
-        // r = applied q, pulled per row in ascending column order; zero q
-        // skipped; one thread per row for all envs. The dense workspace
-        // overlapped the field: padding slots and unused envs are zeroed again
-        // (padded sweep terms read the zero slot).
+        // y -> the field array (row positions); the second solve adds to it
+        for (int i = tid; i < n; i += blockDim.x) {
+#pragma unroll
+            for (int e = 0; e < kGroupLanes; e++)
+                if (e < nenv) g.T[(size_t)(local0 + e) * ncv + i] = sh.X[(size_t)e * S + i];
+        }
+        return;
+    }   // Phase 0
+
+    // ---- second solve: r = applied q (k_dense's solution), pulled per row in
+    // ascending column order, zero q skipped; one thread per row for all envs ----
+    const int local0 = sd.env0 - g.env0;
+    if (k > 0 && any_active) {
+        const double* q = ctx->airq;
         for (int i = tid; i < n; i += blockDim.x) {
             double acc[kGroupLanes];
 #pragma unroll
@@ -617,7 +598,7 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
 #pragma unroll
                 for (int e = 0; e < kGroupLanes; e++) {
                     if (e >= nenv) break;
-                    const double qj = pw[e * k + col];
+                    const double qj = q[(size_t)(sd.env0 + e) * ctx->k_max + col];
                     if (active[e] && qj != 0.0) acc[e] = dadd(acc[e], dmul(xv, qj));
                 }
             }
@@ -625,12 +606,10 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
             for (int e = 0; e < kGroupLanes; e++)
                 if (e < B) sh.X[(size_t)e * S + i] = e < nenv && active[e] ? acc[e] : 0.0;
         }
-        for (int idx = tid; idx < B * (S - n); idx += blockDim.x)
-            sh.X[(size_t)(idx / (S - n)) * S + n + idx % (S - n)] = 0.0;
         __syncthreads();
-        if (tid < kSweepWarps * 32) run_sweep(sh, g.fwd, B, S, n, 3);
+        if (tid < kSweepWarps * 32) run_sweep(sh, g.fwd, B, S, n, 1);
         __syncthreads();
-        if (tid < kSweepWarps * 32) run_sweep(sh, g.bwd, B, S, n, 4);
+        if (tid < kSweepWarps * 32) run_sweep(sh, g.bwd, B, S, n, 2);
         __syncthreads();
         if (*sh.abort) {
             if (tid == 0) set_error(ctx->status, *sh.abort);

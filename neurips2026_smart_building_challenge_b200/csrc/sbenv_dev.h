@@ -60,18 +60,22 @@ enum : int {
 // (in sweep order) whose terms among themselves form a full triangle (the
 // separators of the nested-dissection order): the whole warp works on it,
 // lane group q holding the block's rows i = q mod 4, one lane per env. The
-// block is solved in rounds of four rows c0..c0+3: the four rows finish one
-// after another inside the round (each hands its value to the others by a
-// shuffle), then every later row of the block subtracts the four values in
-// column order, so each row receives its in-block terms in the push order.
-// The rows' terms from outside the block are applied before, as ordinary
-// segments; the end of such a segment publishes a "partial" flag where
-// another warp runs the block. Ready flags: a finished row holds 2 epoch, a
-// row whose outside terms are applied 2 epoch - 1. The block's values follow
-// the block record, round after round: 4 diagonals (U; zero in L), the 6
-// in-round terms (c0+1,c0) (c0+2,c0) (c0+2,c0+1) (c0+3,c0) (c0+3,c0+1)
-// (c0+3,c0+2), 2 zeros, then for every row i >= c0+4 of the block its four
-// terms (i,c0..c0+3); the last record is padded with zeros.
+// block is solved in rounds of four rows c0..c0+3 (left-looking): each of
+// the round's rows first pulls its terms from the rows of the earlier rounds
+// (final in shared memory), then the four rows finish one after another
+// inside the round, each handing its value to the others by a shuffle; so
+// every row receives its in-block terms in the push order. The rows' terms
+// from outside the block are applied before, as ordinary segments; the end of
+// such a segment publishes a "partial" flag where another warp runs the
+// block. Ready flags: a finished row holds 2 epoch, a row whose outside terms
+// are applied 2 epoch - 1. The block's values follow the block record, round
+// after round: 4 diagonals (U; zero in L), the 6 in-round terms (c0+1,c0)
+// (c0+2,c0) (c0+2,c0+1) (c0+3,c0) (c0+3,c0+1) (c0+3,c0+2), 2 zeros, then for
+// each row c0+q (q = 0..3) its terms (c0+q, 0..c0-1) (zeros for rows past the
+// block). A round never wraps around the end of the kernel's ring
+// (ring_stages * kStageBytes bytes of the warp's stream map onto the ring):
+// one that would is moved to the next ring start, zeros before it. The last
+// record is padded with zeros.
 //
 // A program is a sequence of kRecordBytes records, three to a ring stage;
 // it starts with a control record, and a control record with kCtrlEnd ends it.
@@ -130,18 +134,12 @@ struct BlockRecord {
 static_assert(sizeof(TermRecord) == kRecordBytes && sizeof(ControlRecord) == kRecordBytes &&
                   sizeof(BlockRecord) == kRecordBytes, "record size");
 constexpr int kRoundHead = 12;           // doubles of a block round before its rows' terms
-// Doubles of a block's values (all rounds).
+static_assert((kRoundHead + 4 * ((kMaxBlockRows - 1) / 4 * 4)) * 8 <= kStagesMin * kStageBytes, "a round fits the ring");
+// Doubles of a block's values (all rounds, without ring padding).
 SB_HD constexpr int block_values(int size) {
     int v = 0;
-    for (int c0 = 0; c0 < size; c0 += 4) v += kRoundHead + 4 * (size - c0 - 4 > 0 ? size - c0 - 4 : 0);
+    for (int c0 = 0; c0 < size; c0 += 4) v += kRoundHead + 4 * c0;
     return v;
-}
-// Largest block whose first round (the longest) fits a ring of ring_stages
-// stages from any starting byte of a stage.
-SB_HD constexpr int block_rows_for_ring(int ring_stages) {
-    const int room = (ring_stages * kStageBytes - (kStageBytes - 8)) / 8 - kRoundHead;   // doubles for the rows' terms
-    const int rows = 4 + room / 4;
-    return rows < kMaxBlockRows ? rows : kMaxBlockRows;
 }
 
 
@@ -287,6 +285,11 @@ struct StepCtx {
     const double* V_prime;
     const double* V_zero;
     int nz_max;
+    // air side: per env the dense system's right side (k_solve phase 0), then
+    // its solution (k_dense), read by k_solve phase 1
+    double* airq;           // [n_env][k_max]
+    int k_max;
+    const int* dense_order; // [n_env] envs by descending k (k_dense's CTA order)
 };
 
 }  // namespace sbenv

@@ -15,8 +15,9 @@
 //
 // Dense blocks (runs of consecutive rows, in sweep order, whose terms among
 // themselves form a full triangle: the separators of the nested-dissection
-// order) are finished by one warp in a block record, four rows per round;
-// their rows' other ("outside") terms run before as ordinary segments.
+// order) are finished by one warp in a block record, four rows per round
+// (each pulls its terms from the earlier rounds, then the four finish in
+// turn); their rows' other ("outside") terms run before as ordinary segments.
 //
 // Deadlock freedom: a record waits only for rows (or rows' outside terms)
 // finished at records created earlier in the simulation (smaller sequence
@@ -40,7 +41,7 @@ constexpr double kCCtrl = 350;    // a control record: finish rows, waits, start
 constexpr double kCBlk = 150;     // a term record
 constexpr double kC2 = 400;       // release store until the waiting warp has seen it
 constexpr double kCBRound = 300;  // one round (four rows) of a block record ...
-constexpr double kCBRow = 30;     // ... plus this per later row of a lane group
+constexpr double kCBRow = 10;     // ... plus this per row of the earlier rounds
 constexpr double kSlack = 150;    // a row may be picked this long before its next input is ready
 constexpr int kMinSeg = 16;       // shortest segment worth a control record (unless the row ends sooner)
 constexpr double kCritical = 0.9; // rows within this fraction of the top priority start at any length
@@ -55,7 +56,7 @@ inline void orr(uint64_t* d, const uint64_t* s, int w) {
 }
 
 // modelled length of the round of a block of s rows that starts at row c0
-inline double block_round(int s, int c0) { return kCBRound + kCBRow * std::ceil(std::max(0, s - c0 - 4) / 4.0); }
+inline double block_round(int s, int c0) { (void)s; return kCBRound + kCBRow * c0; }
 
 struct Group {
     int row = -1;     // -1: idle
@@ -101,7 +102,7 @@ std::string build_sweep(int n, const std::vector<std::vector<std::pair<int, doub
     // position s0 if its last p - s0 terms are the rows s0 .. p-1 in order ----
     std::vector<int> blk(n, -1), nout(nt);
     std::vector<Block> blocks;
-    const int max_block = block_rows_for_ring(ring_stages);
+    const int max_block = kMaxBlockRows;
     {
         int s0 = 0;
         for (int p = 1; p <= n; p++) {
@@ -136,7 +137,7 @@ std::string build_sweep(int n, const std::vector<std::vector<std::pair<int, doub
         const int i = row_at(n - 1 - s);   // dependents first
         double best = 0.0;
         for (int d : dependents[i]) best = std::max(best, prio[d]);
-        prio[i] = best + (blk[i] >= 0 ? kCBRound / 4 + kCBRow + kCBlk * std::ceil(nout[i] / (double)kTermSteps)
+        prio[i] = best + (blk[i] >= 0 ? kCBRound / 4 + kCBlk * std::ceil(nout[i] / (double)kTermSteps)
                                       : kC2 + kCCtrl + kCBlk * std::ceil(nt[i] / (double)kTermSteps));
     }
 
@@ -370,23 +371,27 @@ std::string build_sweep(int n, const std::vector<std::vector<std::pair<int, doub
             br.flags = kCtrlBlock;
             for (size_t i = 0; i < waits.size(); i++) br.wait[i] = (uint16_t)waits[i];
             // values round by round (layout in sbenv_dev.h); v(i, j) is row i's
-            // in-block term from row j
+            // in-block term from row j. A round that would run past the end of
+            // the kernel's ring starts at the ring's start instead (zero padding).
             auto v = [&](int i, int j) { return terms[B.rows[i]][nout[B.rows[i]] + j]; };
+            for (int i = 1; i < s; i++)
+                for (int j = 0; j < i; j++)
+                    if (v(i, j).first != B.rows[j]) return "dense block term out of order";
+            const size_t ring_bytes = (size_t)ring_stages * kStageBytes;
+            const size_t vstart = P.rec.size() + kRecordBytes;   // stream byte of the first value
             std::vector<double> vals;
-            vals.reserve(block_values(s));
             for (int c0 = 0; c0 < s; c0 += 4) {
+                const size_t rbytes = 8 * (size_t)(kRoundHead + 4 * c0);
+                const size_t pos = vstart + vals.size() * 8;
+                if (pos % ring_bytes + rbytes > ring_bytes) vals.resize(vals.size() + (ring_bytes - pos % ring_bytes) / 8, 0.0);
                 for (int k = 0; k < 4; k++) vals.push_back(backward && c0 + k < s ? diag[B.rows[c0 + k]] : 0.0);
                 for (int r = 1; r < 4; r++)
                     for (int k = 0; k < r; k++) vals.push_back(c0 + r < s ? v(c0 + r, c0 + k).second : 0.0);
                 vals.push_back(0.0);
                 vals.push_back(0.0);
-                for (int i = c0 + 4; i < s; i++)
-                    for (int k = 0; k < 4; k++) vals.push_back(v(i, c0 + k).second);
+                for (int q = 0; q < 4; q++)
+                    for (int j = 0; j < c0; j++) vals.push_back(c0 + q < s ? v(c0 + q, j).second : 0.0);
             }
-            for (int i = 1; i < s; i++)
-                for (int j = 0; j < i; j++)
-                    if (v(i, j).first != B.rows[j]) return "dense block term out of order";
-            if ((int)vals.size() != block_values(s)) return "dense block value count";
             br.nrec = (uint16_t)((vals.size() * 8 + kRecordBytes - 1) / kRecordBytes);
             memcpy(new_record(P, 1), &br, sizeof(br));
             const size_t at = P.rec.size();

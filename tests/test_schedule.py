@@ -40,20 +40,27 @@ def _programs(lib, blob, sweep, ring_stages):
     return out
 
 
-def _block_terms(vals, size, backward):
-    """(diag[j], v[i][j]) of a block from its round layout: per round of rows
-    c0..c0+3, 4 diagonals, the 6 in-round terms, 2 zeros, then four terms per
-    later row."""
-    diag, v, p = [1.0] * size, {}, 0
+def _block_terms(stream, start, size, backward, ring_bytes):
+    """(diag[j], v[i][j]) of a block from its round layout at byte `start` of
+    the warp's stream: per round of rows c0..c0+3, 4 diagonals, the 6 in-round
+    terms, 2 zeros, then for each row c0+q its terms from rows 0..c0-1 (zeros
+    past the block); a round that would run past the end of the ring
+    (ring_bytes of the stream per ring turn) starts at the next turn, zeros
+    before it. Returns also the byte after the last round."""
+    diag, v, pos = [1.0] * size, {}, start
     for c0 in range(0, size, 4):
+        rbytes = 8 * (12 + 4 * c0)
+        if pos % ring_bytes + rbytes > ring_bytes:
+            pad = ring_bytes - pos % ring_bytes
+            assert not any(stream[pos:pos + pad]), "ring padding not zero"
+            pos += pad
+        vals = np.frombuffer(stream, "<f8", rbytes // 8, pos)
         for k in range(4):
-            if c0 + k < size:
-                diag[c0 + k] = float(vals[p + k]) if backward else 1.0
+            if c0 + k < size and backward:
+                diag[c0 + k] = float(vals[k])
             else:
-                assert vals[p + k] == 0.0
-            if not backward:
-                assert vals[p + k] == 0.0
-        t = p + 4
+                assert vals[k] == 0.0
+        t = 4
         for r in range(1, 4):
             for k in range(r):
                 if c0 + r < size:
@@ -61,17 +68,21 @@ def _block_terms(vals, size, backward):
                 else:
                     assert vals[t] == 0.0
                 t += 1
-        assert vals[p + 10] == 0.0 and vals[p + 11] == 0.0
-        p += 12
-        for i in range(c0 + 4, size):
-            for k in range(4):
-                v[(i, c0 + k)] = float(vals[p])
-                p += 1
-    assert p == len(vals)
-    return diag, v
+        assert vals[10] == 0.0 and vals[11] == 0.0
+        t = 12
+        for q in range(4):
+            for j in range(c0):
+                if c0 + q < size:
+                    v[(c0 + q, j)] = float(vals[t])
+                else:
+                    assert vals[t] == 0.0
+                t += 1
+        pos += rbytes
+    assert len(v) == size * (size - 1) // 2
+    return (diag, v), pos
 
 
-def _parse(stream, n, backward):
+def _parse(stream, n, backward, ring):
     """Records of one warp program: ("ctrl", rows, gflags, waits, diag),
     ("term", vals[4][4], cols[4][4]) or ("block", rows, waits, publish, vals);
     it starts with a control record and ends with one carrying the end flag,
@@ -91,11 +102,10 @@ def _parse(stream, n, backward):
                 assert bw == int(backward) and 1 <= size <= 48 and not flags & C_END
                 rows = [first - j if backward else first + j for j in range(size)]
                 assert all(0 <= r < n for r in rows) and publish >> size == 0
-                nv = sum(12 + 4 * max(0, size - c0 - 4) for c0 in range(0, size, 4))
-                assert nrec == (nv * 8 + REC - 1) // REC
-                vals = np.frombuffer(stream, "<f8", nv, pos + REC)
-                assert not any(stream[pos + REC + 8 * nv:pos + REC * (1 + nrec)]), "block padding not zero"
-                recs.append(("block", rows, waits, publish, _block_terms(vals, size, backward)))
+                vals, vend = _block_terms(stream, pos + REC, size, backward, ring * STAGE)
+                assert nrec == (vend - pos - REC + REC - 1) // REC
+                assert not any(stream[vend:pos + REC * (1 + nrec)]), "block padding not zero"
+                recs.append(("block", rows, waits, publish, vals))
                 pos += REC * (1 + nrec)
                 assert flags & C_NEXT, "a block is followed by a control or block record"
                 continue
@@ -138,7 +148,7 @@ class _Warp:
         return self.i >= len(self.recs)
 
 
-def _execute(programs, x, n, backward, pick, expect):
+def _execute(programs, x, n, backward, pick, expect, ring):
     """Runs the warps' records (a dense block one step at a time) in the order
     pick() chooses."""
     x = list(x) + [0.0]
@@ -152,7 +162,7 @@ def _execute(programs, x, n, backward, pick, expect):
     writer = [None] * (n + 1)           # warp that last stored the row
     acquired = [set() for _ in programs]   # rows whose partial flag a warp has acquired
     got = [[] for _ in range(n)]
-    warps = [_Warp(k, _parse(p, n, backward)) for k, p in enumerate(programs)]
+    warps = [_Warp(k, _parse(p, n, backward, ring)) for k, p in enumerate(programs)]
 
     def waits_met(waits):
         return all(partial[r & ~W_PARTIAL] or ready[r & ~W_PARTIAL] if r & W_PARTIAL else ready[r] for r in waits)
@@ -319,8 +329,8 @@ def test_schedule_replays_reference_solve(built, tmp_path, config, index, ring):
     rhs = np.random.default_rng(index).standard_normal(n) * 300.0
     ref = _push_reference(L, U, rhs)
     for k, pick in enumerate(_pickers(index)):
-        y = _execute(fwd, rhs, n, False, pick, tl)
-        z = _execute(bwd, y, n, True, pick, tu)
+        y = _execute(fwd, rhs, n, False, pick, tl, ring)
+        z = _execute(bwd, y, n, True, pick, tu, ring)
         assert np.array_equal(z, ref), f"interleaving {k}"
 
 
@@ -337,7 +347,7 @@ def test_schedule_stats(built, tmp_path):
     for sweep in (0, 1):
         assert lib.sb_sweep_stats(str(blob).encode(), sweep, 5, st) == 0
         progs = _programs(lib, blob, sweep, 5)
-        recs = [r for p in progs for r in _parse(p, n, sweep == 1)]
+        recs = [r for p in progs for r in _parse(p, n, sweep == 1, 5)]
         ctrl = [r for r in recs if r[0] == "ctrl"]
         blocks = [r for r in recs if r[0] == "block"]
         assert st[0] == L.nnz - n
@@ -354,3 +364,19 @@ def test_schedule_stats(built, tmp_path):
     assert lib.sb_sweep_stats(str(blob).encode(), 2, 5, st) == -1         # no such sweep
     assert lib.sb_sweep_stats(str(blob).encode(), 0, 3, st) == -1         # ring too shallow
     assert b"ring" in lib.sb_last_error()
+
+
+@pytest.mark.parametrize("config,index", [(1, 0), (2, 5)])
+def test_ring_protocol(built, tmp_path, config, index):
+    """Every warp program, walked through a CPU model of the kernel's stage
+    ring at each ring depth, reads only landed stages and refills a slot only
+    after its copy has landed."""
+    import neurips2026_smart_building_challenge_b200 as pkg
+    from ring_emu import walk
+
+    blob = pkg.write_scenario(tmp_path / "s.sbb", pkg.preset(config, index, n_steps=10))
+    lib = pkg.env_lib()
+    for ring in range(4, 9):
+        for sweep in (0, 1):
+            for prog in _programs(lib, blob, sweep, ring):
+                walk(prog, ring)
