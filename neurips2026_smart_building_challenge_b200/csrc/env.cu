@@ -373,6 +373,7 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
         gd.zone_of_row = E.arena.upload(h.zone_of_row, ok);
         auto put_sweep = [&](const HostSweep& hsw, Sweep& s) {
             s.stream = E.arena.upload(hsw.bytes, ok);
+            s.total_bytes = (uint32_t)hsw.bytes.size();
             for (int w = 0; w < kSweepWarps; w++) {
                 s.warp_off[w] = hsw.warp_off[w];
                 s.warp_stages[w] = hsw.warp_stages[w];

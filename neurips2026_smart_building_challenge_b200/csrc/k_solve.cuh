@@ -119,65 +119,56 @@ struct StageRing {
     }
 };
 
+// L1 prefetch of the 128-byte lines of [p, p + bytes): one line per lane.
+__device__ __forceinline__ void prefetch_lines(const uint8_t* p, uint32_t bytes, int lane) {
+    const uintptr_t l0 = reinterpret_cast<uintptr_t>(p) >> 7;
+    const uintptr_t l1 = (reinterpret_cast<uintptr_t>(p) + bytes - 1) >> 7;
+    for (uintptr_t l = l0 + (uintptr_t)lane; l <= l1; l += 32) asm volatile("prefetch.global.L1 [%0];" ::"l"(l << 7));
+}
+
 // One dense block record (format in sbenv_dev.h), the cursor at its header
-// (stage rg.head, record hq). Lane group g holds the block's rows i = g mod 4,
-// one lane per env. Round c0: group g's row c0 + g loads its partial sum,
-// pulls its terms from rows 0..c0-1 (final values in shared memory), then the
-// round's four rows finish in turn, x_k from group k to all lanes by a
-// shuffle. A round lies contiguous in the ring, so its values are read at
-// fixed offsets from one pointer. Returns the record index after the block's
-// values, or 0xFFFFFFFF on an error (reported in sh.abort).
-__device__ inline uint32_t run_block(const SolveShared& sh, StageRing& rg, uint32_t hq, double* __restrict__ xe,
-                                     bool owns, uint32_t n, uint32_t fin) {
+// (stage rg.head, record hq); its values are read from global memory (the
+// sweep's value region, sw_base + values) through L1, the next round's lines
+// prefetched while the current one runs. Lane group g holds the block's rows
+// i = g mod 4, one lane per env. Round c0: group g's row c0 + g loads its
+// partial sum, pulls its terms from rows 0..c0-1 (final values in shared
+// memory), then the round's four rows finish in turn, x_k from group k to all
+// lanes by a shuffle. Returns false on an error (reported in sh.abort).
+__device__ inline bool run_block(const SolveShared& sh, const StageRing& rg, uint32_t hq, const uint8_t* sw_base,
+                                 uint32_t sw_bytes, double* __restrict__ xe, bool owns, uint32_t n, uint32_t fin) {
     const unsigned full = 0xffffffffu;
     const int lane = threadIdx.x & 31, e = lane & 7;
     const uint32_t g = (uint32_t)lane >> 3;
     const BlockRecord* b = reinterpret_cast<const BlockRecord*>(rg.ring + (size_t)rg.hslot * kStageBytes + hq * kRecordBytes);
-    const uint32_t first = b->first, size = b->size, bw = b->backward, nw = b->nwait, nrec = b->nrec;
+    const uint32_t first = b->first, size = b->size, bw = b->backward, nw = b->nwait, voff = b->values;
     const uint64_t pubm = b->publish;
     const uint32_t lastrow = bw ? first - (size - 1) : first + (size - 1);
-    const uint32_t hidx = rg.head * kRecordsPerStage + hq;
-    const uint32_t vend = (hidx + 1 + nrec) * kRecordBytes;   // stream byte after the values
-    if (size == 0 || size > (uint32_t)kMaxBlockRows || bw > 1 || first >= n || lastrow >= n ||
-        nrec * (uint32_t)kRecordBytes < (uint32_t)block_values((int)size) * 8u ||
-        (hidx + 1 + nrec) / kRecordsPerStage >= rg.nst) {
+    const uint32_t vbytes = (uint32_t)block_values((int)size) * 8u;
+    if (size == 0 || size > (uint32_t)kMaxBlockRows || bw > 1 || first >= n || lastrow >= n || (voff & 15u) ||
+        voff > sw_bytes || vbytes > sw_bytes - voff) {
         atomicCAS((int*)sh.abort, 0, kErrBadBundle);
-        return 0xFFFFFFFFu;
+        return false;
     }
-    if (nw && !wait_rows(sh, b->wait, min(nw, (uint32_t)kCtrlWaits), n, fin)) return 0xFFFFFFFFu;
+    const uint8_t* __restrict__ vals = sw_base + voff;
+    prefetch_lines(vals, min(vbytes, 2048u), lane);
+    if (nw && !wait_rows(sh, b->wait, min(nw, (uint32_t)kCtrlWaits), n, fin)) return false;
     const int dir = bw ? -1 : 1;
-    const uint32_t RB = rg.R * kStageBytes;
     const double* __restrict__ xb = xe + (int)first;   // block row j at xb[dir * j]
-    // value cursor: stream byte vo, its ring offset vr
-    uint32_t vo = (hidx + 1) * kRecordBytes;
-    uint32_t vr = rg.hslot * kStageBytes + (hq + 1) * kRecordBytes;
-    if (vr >= RB) vr -= RB;
     // this group's in-round terms (k < g at triangle index g(g-1)/2 + k)
     const uint32_t tri0 = g * (g - 1) / 2;
     const uint32_t o0 = 32 + 8 * min(tri0 + 0, 5u), o1 = 32 + 8 * min(tri0 + 1, 5u), o2 = 32 + 8 * min(tri0 + 2, 5u);
+    const uint8_t* __restrict__ rp = vals;
     for (uint32_t c0 = 0; c0 < size; c0 += 4) {
         const uint32_t rbytes = (kRoundHead + 4 * c0) * 8;
-        if (vr + rbytes > RB) {   // the round starts at the ring's start
-            vo += RB - vr;
-            vr = 0;
-        }
-        if (vo + rbytes > vend) {
-            atomicCAS((int*)sh.abort, 0, kErrBadBundle);
-            return 0xFFFFFFFFu;
-        }
-        if (!rg.consume(vo / kStageBytes, lane) || !rg.land((vo + rbytes - 1) / kStageBytes)) {
-            atomicCAS((int*)sh.abort, 0, kErrRingTimeout);
-            return 0xFFFFFFFFu;
-        }
-        const uint8_t* __restrict__ rp = rg.ring + vr;
+        if (c0 + 4 < size) prefetch_lines(rp + rbytes, rbytes + 128, lane);   // the next round
         const bool mine = c0 + g < size;
         const int row = (int)first + dir * (int)(c0 + g);
         // the row's partial sum, then its terms from the earlier rounds in order
         double a = xe[mine ? row : (int)first];
         const uint8_t* __restrict__ tv = rp + kRoundHead * 8 + 8 * c0 * g;
         for (uint32_t j = 0; j < c0; j += 4) {
-            const double2 v01 = *reinterpret_cast<const double2*>(tv + 8 * j);
-            const double2 v23 = *reinterpret_cast<const double2*>(tv + 8 * j + 16);
+            const double2 v01 = __ldg(reinterpret_cast<const double2*>(tv + 8 * j));
+            const double2 v23 = __ldg(reinterpret_cast<const double2*>(tv + 8 * j + 16));
             const double x0 = xb[dir * (int)j], x1 = xb[dir * (int)(j + 1)];
             const double x2 = xb[dir * (int)(j + 2)], x3 = xb[dir * (int)(j + 3)];
             a = dsub(a, dmul(v01.x, x0));
@@ -185,10 +176,10 @@ __device__ inline uint32_t run_block(const SolveShared& sh, StageRing& rg, uint3
             a = dsub(a, dmul(v23.x, x2));
             a = dsub(a, dmul(v23.y, x3));
         }
-        const double dg = bw ? *reinterpret_cast<const double*>(rp + 8 * g) : 1.0;
-        const double t0 = *reinterpret_cast<const double*>(rp + o0);
-        const double t1 = *reinterpret_cast<const double*>(rp + o1);
-        const double t2 = *reinterpret_cast<const double*>(rp + o2);
+        const double dg = bw ? __ldg(reinterpret_cast<const double*>(rp + 8 * g)) : 1.0;
+        const double t0 = __ldg(reinterpret_cast<const double*>(rp + o0));
+        const double t1 = __ldg(reinterpret_cast<const double*>(rp + o1));
+        const double t2 = __ldg(reinterpret_cast<const double*>(rp + o2));
         // the four rows in turn: group k's row is final at stage k
         const double x0 = __shfl_sync(full, bw ? ddiv(a, dg) : a, e);
         if (g > 0) a = dsub(a, dmul(t0, x0));
@@ -207,11 +198,9 @@ __device__ inline uint32_t run_block(const SolveShared& sh, StageRing& rg, uint3
             __threadfence_block();
             st_release_u8(sh.ready + row, fin);
         }
-        vo += rbytes;
-        vr += rbytes;
-        if (vr == RB) vr = 0;
+        rp += rbytes;
     }
-    return hidx + 1 + nrec;
+    return true;
 }
 
 // One triangular sweep. Every warp runs its own program from its stage ring;
@@ -259,38 +248,34 @@ __device__ inline void run_sweep(const SolveShared& sh, const Sweep& sw, int B, 
             const ControlRecord* c = reinterpret_cast<const ControlRecord*>(rp);
             const uint32_t cf = c->flags;
             if (cf & kCtrlBlock) {
-                const uint32_t next = run_block(sh, rg, q, xe, owns, un, fin);
-                if (next == 0xFFFFFFFFu) { err = kErrBadBundle; break; }
-                if (!rg.consume(next / kRecordsPerStage, lane) || !rg.land(rg.head)) { err = kErrRingTimeout; break; }
-                q = next % kRecordsPerStage;
-                rp = rg.ring + (size_t)rg.hslot * kStageBytes + q * kRecordBytes;
+                if (!run_block(sh, rg, q, sw.stream, sw.total_bytes, xe, owns, un, fin)) { err = kErrBadBundle; break; }
                 ctrl = true;   // a block is followed by a control or block record
-                continue;
-            }
-            const uint32_t gf = c->gflags[g];
-            const uint32_t newrow = min((uint32_t)c->row[g], un);
-            const uint32_t nw = c->nwait;
-            const bool ending = (gf & kGSwitch) && row < un;
-            if (cf & kCtrlDivide) {
-                const double dq = ddiv(acc, c->diag[g]);
-                if (gf & kGDivide) acc = dq;
-            }
-            if (ending && owns) xe[row] = acc;   // final value, partial sum, or paused row
-            if (cf & kCtrlPublish) {
-                __syncwarp();
-                if (ending && e == 0 && (gf & (kGPublish | kGPartial))) {
-                    __threadfence_block();
-                    st_release_u8(sh.ready + row, (gf & kGPublish) ? fin : fin - 1);
+            } else {
+                const uint32_t gf = c->gflags[g];
+                const uint32_t newrow = min((uint32_t)c->row[g], un);
+                const uint32_t nw = c->nwait;
+                const bool ending = (gf & kGSwitch) && row < un;
+                if (cf & kCtrlDivide) {
+                    const double dq = ddiv(acc, c->diag[g]);
+                    if (gf & kGDivide) acc = dq;
                 }
+                if (ending && owns) xe[row] = acc;   // final value, partial sum, or paused row
+                if (cf & kCtrlPublish) {
+                    __syncwarp();
+                    if (ending && e == 0 && (gf & (kGPublish | kGPartial))) {
+                        __threadfence_block();
+                        st_release_u8(sh.ready + row, (gf & kGPublish) ? fin : fin - 1);
+                    }
+                }
+                if (nw && !wait_rows(sh, c->wait, min(nw, (uint32_t)kCtrlWaits), un, fin)) { err = kErrWaitTimeout; break; }
+                __syncwarp();   // stores of every group before any group's new loads
+                if (gf & kGSwitch) {
+                    row = newrow;
+                    acc = xe[row];
+                }
+                if (cf & kCtrlEnd) break;
+                ctrl = (cf & kCtrlNext) != 0;
             }
-            if (nw && !wait_rows(sh, c->wait, min(nw, (uint32_t)kCtrlWaits), un, fin)) { err = kErrWaitTimeout; break; }
-            __syncwarp();   // stores of every group before any group's new loads
-            if (gf & kGSwitch) {
-                row = newrow;
-                acc = xe[row];
-            }
-            if (cf & kCtrlEnd) break;
-            ctrl = (cf & kCtrlNext) != 0;
         }
         // next record
         if (++q == kRecordsPerStage) {

@@ -68,14 +68,11 @@ enum : int {
 // from outside the block are applied before, as ordinary segments; the end of
 // such a segment publishes a "partial" flag where another warp runs the
 // block. Ready flags: a finished row holds 2 epoch, a row whose outside terms
-// are applied 2 epoch - 1. The block's values follow the block record, round
-// after round: 4 diagonals (U; zero in L), the 6 in-round terms (c0+1,c0)
-// (c0+2,c0) (c0+2,c0+1) (c0+3,c0) (c0+3,c0+1) (c0+3,c0+2), 2 zeros, then for
-// each row c0+q (q = 0..3) its terms (c0+q, 0..c0-1) (zeros for rows past the
-// block). A round never wraps around the end of the kernel's ring
-// (ring_stages * kStageBytes bytes of the warp's stream map onto the ring):
-// one that would is moved to the next ring start, zeros before it. The last
-// record is padded with zeros.
+// are applied 2 epoch - 1. The block's values sit after all warps' programs
+// in the sweep's buffer (read through L1, not the stage ring), round after
+// round: 4 diagonals (U; zero in L), the 6 in-round terms (c0+1,c0) (c0+2,c0)
+// (c0+2,c0+1) (c0+3,c0) (c0+3,c0+1) (c0+3,c0+2), 2 zeros, then for each row
+// c0+q (q = 0..3) its terms (c0+q, 0..c0-1) (zeros for rows past the block).
 //
 // A program is a sequence of kRecordBytes records, three to a ring stage;
 // it starts with a control record, and a control record with kCtrlEnd ends it.
@@ -121,21 +118,21 @@ struct ControlRecord {
 };
 struct BlockRecord {
     uint16_t first;              // the block's first row
-    uint16_t size;               // rows (2..kMaxBlockRows)
+    uint16_t size;               // rows (1..kMaxBlockRows)
     uint8_t backward;            // 0: rows first, first+1, ..; 1: first, first-1, .. (divides)
     uint8_t pad0[7];
     uint8_t nwait;               // at ControlRecord.nwait's offset
-    uint8_t flags;               // at ControlRecord.flags' offset: kCtrlBlock | kCtrlNext | kCtrlEnd
-    uint16_t nrec;               // value records that follow
+    uint8_t flags;               // at ControlRecord.flags' offset: kCtrlBlock | kCtrlNext
+    uint16_t pad1;
     uint64_t publish;            // bit i: publish row i when it is final
-    uint8_t pad1[24];
+    uint32_t values;             // byte offset of the block's values from the start of the sweep's buffer
+    uint8_t pad2[20];
     uint16_t wait[kCtrlWaits];   // rows to acquire first (kWaitPartial: outside terms only)
 };
 static_assert(sizeof(TermRecord) == kRecordBytes && sizeof(ControlRecord) == kRecordBytes &&
                   sizeof(BlockRecord) == kRecordBytes, "record size");
 constexpr int kRoundHead = 12;           // doubles of a block round before its rows' terms
-static_assert((kRoundHead + 4 * ((kMaxBlockRows - 1) / 4 * 4)) * 8 <= kStagesMin * kStageBytes, "a round fits the ring");
-// Doubles of a block's values (all rounds, without ring padding).
+// Doubles of a block's values (all rounds).
 SB_HD constexpr int block_values(int size) {
     int v = 0;
     for (int c0 = 0; c0 < size; c0 += 4) v += kRoundHead + 4 * c0;
@@ -169,7 +166,8 @@ SB_HD constexpr size_t solve_smem_bytes(int n, int B, int ring_stages) {
 
 // One triangular sweep: per-warp byte streams, each a whole number of stages.
 struct Sweep {
-    const uint8_t* stream;                 // all warps' streams back to back
+    const uint8_t* stream;                 // all warps' streams back to back, then the block value region
+    uint32_t total_bytes;                  // the whole buffer
     uint32_t warp_off[kSweepWarps];        // stage index where warp w's stream starts
     uint32_t warp_stages[kSweepWarps];     // stages in warp w's stream
     uint32_t ring_stages;                  // ring depth the streams were laid out for

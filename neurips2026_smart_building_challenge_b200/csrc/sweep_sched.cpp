@@ -235,6 +235,7 @@ std::string build_sweep(int n, const std::vector<std::vector<std::pair<int, doub
     }
     auto lim = [&](int r) { return blk[r] >= 0 ? nout[r] : nt[r]; };   // terms a row's segments cover
     std::vector<WarpProg> wp(W);
+    std::vector<double> block_vals;   // all blocks' values (region after the programs)
     std::vector<int> cand;
     std::vector<uint64_t> Kb(WD), Ksave;
     int seq = 0;
@@ -370,33 +371,23 @@ std::string build_sweep(int n, const std::vector<std::vector<std::pair<int, doub
             br.nwait = (uint8_t)waits.size();
             br.flags = kCtrlBlock;
             for (size_t i = 0; i < waits.size(); i++) br.wait[i] = (uint16_t)waits[i];
-            // values round by round (layout in sbenv_dev.h); v(i, j) is row i's
-            // in-block term from row j. A round that would run past the end of
-            // the kernel's ring starts at the ring's start instead (zero padding).
+            // values round by round (layout in sbenv_dev.h) into the sweep's
+            // value region; v(i, j) is row i's in-block term from row j
             auto v = [&](int i, int j) { return terms[B.rows[i]][nout[B.rows[i]] + j]; };
             for (int i = 1; i < s; i++)
                 for (int j = 0; j < i; j++)
                     if (v(i, j).first != B.rows[j]) return "dense block term out of order";
-            const size_t ring_bytes = (size_t)ring_stages * kStageBytes;
-            const size_t vstart = P.rec.size() + kRecordBytes;   // stream byte of the first value
-            std::vector<double> vals;
+            br.values = (uint32_t)(block_vals.size() * 8);   // region-relative until serialised
             for (int c0 = 0; c0 < s; c0 += 4) {
-                const size_t rbytes = 8 * (size_t)(kRoundHead + 4 * c0);
-                const size_t pos = vstart + vals.size() * 8;
-                if (pos % ring_bytes + rbytes > ring_bytes) vals.resize(vals.size() + (ring_bytes - pos % ring_bytes) / 8, 0.0);
-                for (int k = 0; k < 4; k++) vals.push_back(backward && c0 + k < s ? diag[B.rows[c0 + k]] : 0.0);
+                for (int k = 0; k < 4; k++) block_vals.push_back(backward && c0 + k < s ? diag[B.rows[c0 + k]] : 0.0);
                 for (int r = 1; r < 4; r++)
-                    for (int k = 0; k < r; k++) vals.push_back(c0 + r < s ? v(c0 + r, c0 + k).second : 0.0);
-                vals.push_back(0.0);
-                vals.push_back(0.0);
+                    for (int k = 0; k < r; k++) block_vals.push_back(c0 + r < s ? v(c0 + r, c0 + k).second : 0.0);
+                block_vals.push_back(0.0);
+                block_vals.push_back(0.0);
                 for (int q = 0; q < 4; q++)
-                    for (int j = 0; j < c0; j++) vals.push_back(c0 + q < s ? v(c0 + q, j).second : 0.0);
+                    for (int j = 0; j < c0; j++) block_vals.push_back(c0 + q < s ? v(c0 + q, j).second : 0.0);
             }
-            br.nrec = (uint16_t)((vals.size() * 8 + kRecordBytes - 1) / kRecordBytes);
             memcpy(new_record(P, 1), &br, sizeof(br));
-            const size_t at = P.rec.size();
-            P.rec.resize(at + (size_t)br.nrec * kRecordBytes, 0);
-            memcpy(P.rec.data() + at, vals.data(), vals.size() * 8);
             double tj = std::max(t, ready) + kCCtrl;
             for (int j = 0; j < s; j++) {
                 const int r = B.rows[j];
@@ -594,7 +585,6 @@ std::string build_sweep(int n, const std::vector<std::vector<std::pair<int, doub
                 }
                 out.block_rows += b->size;
                 ctrl = (b->flags & kCtrlNext) != 0;
-                i += b->nrec;
                 continue;
             }
             out.bundles++;
@@ -619,6 +609,28 @@ std::string build_sweep(int n, const std::vector<std::vector<std::pair<int, doub
         out.warp_stages[w] = (uint32_t)stages;
         out.bytes.insert(out.bytes.end(), P.rec.begin(), P.rec.end());
     }
+    // the value region after the programs; block records point into it
+    const uint32_t region = (uint32_t)out.bytes.size();
+    if ((uint64_t)region + block_vals.size() * 8 > 0xFFFFFFF0ull) return "sweep buffer too large";
+    for (int w = 0; w < W; w++) {
+        uint8_t* base = out.bytes.data() + (size_t)out.warp_off[w] * kStageBytes;
+        const int nrec = (int)(out.warp_stages[w] * kRecordsPerStage);
+        bool ctrl = true;
+        for (int i = 0; i < nrec; i++) {
+            uint8_t* r = base + (size_t)i * kRecordBytes;
+            if (!ctrl) {
+                ctrl = (reinterpret_cast<TermRecord*>(r)->col[0][0] & kNextIsCtrl) != 0;
+                continue;
+            }
+            ControlRecord* c = reinterpret_cast<ControlRecord*>(r);
+            if (c->flags & kCtrlBlock) reinterpret_cast<BlockRecord*>(r)->values += region;
+            else if (c->flags & kCtrlEnd) break;
+            ctrl = (c->flags & kCtrlNext) != 0;
+        }
+    }
+    const size_t at = out.bytes.size();
+    out.bytes.resize(at + block_vals.size() * 8);
+    if (!block_vals.empty()) memcpy(out.bytes.data() + at, block_vals.data(), block_vals.size() * 8);
     return "";
 }
 

@@ -51,29 +51,14 @@ def walk(stream, R):
             ctrl = bool(struct.unpack_from("<H", stream, off + 128)[0] & NEXT_CTRL)
         else:
             flags = stream[off + 13]
-            if flags & C_BLOCK:
-                size = struct.unpack_from("<H", stream, off + 2)[0]
-                nrec = struct.unpack_from("<H", stream, off + 14)[0]
-                vend = (rec + 1 + nrec) * REC
-                vo = (rec + 1) * REC
-                RB = R * STAGE
-                vr = vo % RB
-                for c0 in range(0, size, 4):
-                    rbytes = 8 * (12 + 4 * c0)
-                    if vr + rbytes > RB:
-                        vo += RB - vr
-                        vr = 0
-                    assert vo + rbytes <= vend
-                    consume(vo // STAGE)
-                    land((vo + rbytes - 1) // STAGE)
-                    read(vo, rbytes)
-                    vo += rbytes
-                    vr = (vr + rbytes) % RB
-                nxt = rec + 1 + nrec
-                consume(nxt // 3)
-                land(st["head"])
-                rec = nxt
+            if flags & C_BLOCK:   # its values are read from the value region, not the ring
+                assert flags & C_NEXT
                 ctrl = True
+                rec += 1
+                if rec % 3 == 0:
+                    consume(st["head"] + 1)
+                    assert st["head"] < nst
+                    land(st["head"])
                 continue
             if flags & C_END:
                 break

@@ -34,27 +34,30 @@ def _programs(lib, blob, sweep, ring_stages):
     raw, out, pos = bytes(buf), [], 0
     for w in range(NW):
         size = stages[w] * STAGE
-        out.append(raw[pos:pos + size])
+        out.append(_Program(raw[pos:pos + size], raw))
         pos += size
-    assert pos == len(raw)
+    assert pos <= len(raw) and (len(raw) - pos) % 16 == 0   # the block value region follows
     return out
 
 
-def _block_terms(stream, start, size, backward, ring_bytes):
+class _Program(bytes):
+    """One warp's record stream; .buffer is the whole sweep buffer (block values)."""
+
+    def __new__(cls, stream, buffer):
+        obj = super().__new__(cls, stream)
+        obj.buffer = buffer
+        return obj
+
+
+def _block_terms(buffer, start, size, backward):
     """(diag[j], v[i][j]) of a block from its round layout at byte `start` of
-    the warp's stream: per round of rows c0..c0+3, 4 diagonals, the 6 in-round
+    the sweep buffer: per round of rows c0..c0+3, 4 diagonals, the 6 in-round
     terms, 2 zeros, then for each row c0+q its terms from rows 0..c0-1 (zeros
-    past the block); a round that would run past the end of the ring
-    (ring_bytes of the stream per ring turn) starts at the next turn, zeros
-    before it. Returns also the byte after the last round."""
+    past the block)."""
     diag, v, pos = [1.0] * size, {}, start
     for c0 in range(0, size, 4):
         rbytes = 8 * (12 + 4 * c0)
-        if pos % ring_bytes + rbytes > ring_bytes:
-            pad = ring_bytes - pos % ring_bytes
-            assert not any(stream[pos:pos + pad]), "ring padding not zero"
-            pos += pad
-        vals = np.frombuffer(stream, "<f8", rbytes // 8, pos)
+        vals = np.frombuffer(buffer, "<f8", rbytes // 8, pos)
         for k in range(4):
             if c0 + k < size and backward:
                 diag[c0 + k] = float(vals[k])
@@ -79,7 +82,7 @@ def _block_terms(stream, start, size, backward, ring_bytes):
                 t += 1
         pos += rbytes
     assert len(v) == size * (size - 1) // 2
-    return (diag, v), pos
+    return diag, v
 
 
 def _parse(stream, n, backward, ring):
@@ -97,16 +100,14 @@ def _parse(stream, n, backward, ring):
             assert nwait <= 56 and all((r & ~W_PARTIAL) <= n for r in waits)
             if flags & C_BLOCK:
                 first, size, bw = struct.unpack_from("<HHB", stream, pos)
-                nrec = struct.unpack_from("<H", stream, pos + 14)[0]
-                publish = struct.unpack_from("<Q", stream, pos + 16)[0]
+                publish, voff = struct.unpack_from("<QI", stream, pos + 16)
                 assert bw == int(backward) and 1 <= size <= 48 and not flags & C_END
                 rows = [first - j if backward else first + j for j in range(size)]
                 assert all(0 <= r < n for r in rows) and publish >> size == 0
-                vals, vend = _block_terms(stream, pos + REC, size, backward, ring * STAGE)
-                assert nrec == (vend - pos - REC + REC - 1) // REC
-                assert not any(stream[vend:pos + REC * (1 + nrec)]), "block padding not zero"
+                assert voff % 16 == 0
+                vals = _block_terms(stream.buffer, voff, size, backward)
                 recs.append(("block", rows, waits, publish, vals))
-                pos += REC * (1 + nrec)
+                pos += REC
                 assert flags & C_NEXT, "a block is followed by a control or block record"
                 continue
             rows = struct.unpack_from("<4H", stream, pos)
@@ -357,7 +358,7 @@ def test_schedule_stats(built, tmp_path):
         assert st[4] == sum(len(r[3]) for r in ctrl) + sum(len(r[2]) for r in blocks)
         assert st[5] == (sum(int(bool(r[2][g] & (G_PUBLISH | G_PARTIAL))) for r in ctrl for g in range(4)) +
                          sum(bin(r[3]).count("1") for r in blocks))
-        assert st[7] == sum(len(p) for p in progs)
+        assert st[7] == len(progs[0].buffer)
         assert st[8] == len(blocks) > 0
         assert st[9] == sum(len(r[1]) for r in blocks)
     assert lib.sb_sweep_stats(str(blob).encode(), 0, 0, st) == 0          # default depth
