@@ -142,6 +142,10 @@ int sb_get_temp(int env, double* out, int n_cvs);
 int sb_get_mass(int env, double* out, int n_solved);
 /* Copies the last step's per-env reward (double) and log terms [n][8] to host memory. */
 int sb_get_reward_f64(double* reward, double* parts);
+/* Verification entry: solves n dense k x k systems (row-major m [n][k][k], right
+ * sides b [n][k]) with the air-side solver of k_dense (partial pivoting in the
+ * reference's order); solutions to out [n][k]. Host pointers; synchronous. */
+int sb_dense_check(int k, int n, const double* m_rowmajor, const double* b, double* out);
 /* Number of hot-path kernel launches one puf_step enqueues. */
 int sb_kernels_per_step(void);
 /* Measurement: runs one step with CUDA events around each kernel on the bound

@@ -108,6 +108,7 @@ struct Engine {
     cudaStream_t stream = nullptr, own_stream = nullptr, side = nullptr, hi = nullptr;
     cudaEvent_t ev_fork = nullptr, ev_join = nullptr, ev_solve = nullptr;
     size_t smem_solve = 0, smem_pre = 0, smem_post = 0, smem_rng = 0, smem_dense = 0;
+    int dense_threads = 32;          // k_dense block (dense_threads(k_max))
     int max_ncv = 0;
     bool ready = false;
     ~Engine() { destroy(); }
@@ -213,7 +214,7 @@ cudaError_t launch_solve(Engine& E) {
     cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess) e = launch_rng_after_solve(E, E.hi, 0);
     if (e != cudaSuccess) return e;
-    k_dense<<<(unsigned)E.n_env, kMaxK, E.smem_dense, E.hi>>>(E.d_ctx);
+    k_dense<<<(unsigned)E.n_env, (unsigned)E.dense_threads, E.smem_dense, E.hi>>>(E.d_ctx);
     k_solve<1><<<slabs, kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
     return cudaGetLastError();
 }
@@ -386,6 +387,12 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
         gd.sn_x = E.arena.upload(h.sn_x, ok);
         gd.ap_rp = E.arena.upload(h.ap_rp, ok); gd.ap_col = E.arena.upload(h.ap_col, ok);
         gd.ap_x = E.arena.upload(h.ap_x, ok); gd.S = E.arena.upload(h.S, ok);
+        {
+            std::vector<double> st(h.S.size());
+            for (int i = 0; i < h.k; i++)
+                for (int j = 0; j < h.k; j++) st[(size_t)j * h.k + i] = h.S[(size_t)i * h.k + j];
+            gd.St = E.arena.upload(st, ok);
+        }
         gd.room_off = E.arena.upload(h.room_off, ok); gd.room_pos = E.arena.upload(h.room_pos, ok);
         gd.cell_of_pos = E.arena.upload(h.cell_of_pos, ok); gd.pos_of_cell = E.arena.upload(h.pos_of_cell, ok);
         gd.cv_off = E.arena.upload(h.cv_off, ok); gd.cv_pos = E.arena.upload(h.cv_pos, ok);
@@ -499,7 +506,8 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
         });
         C.dense_order = E.arena.upload(order, ok);
     }
-    E.smem_dense = std::max<size_t>(16, dense_env_doubles(k_max) * sizeof(double));
+    E.smem_dense = std::max<size_t>(16, dense_smem_doubles(k_max) * sizeof(double));
+    E.dense_threads = dense_threads(std::max(k_max, 1));
     double* vbuf = E.arena.zeros<double>((size_t)3 * G * nz_max, ok);
     C.V_step = vbuf;
     C.V_prime = vbuf + (size_t)G * nz_max;
@@ -847,6 +855,30 @@ int sb_get_reward_f64(double* reward, double* parts) {
 
 int sb_kernels_per_step(void) { return 6; }
 
+int sb_dense_check(int k, int n, const double* m_rowmajor, const double* b, double* out) {
+    if (k < 1 || k > kMaxK || n < 1 || !m_rowmajor || !b || !out) { set_err("sb_dense_check: bad arguments"); return -1; }
+    const size_t kk = (size_t)k * k;
+    std::vector<double> mt(kk * n);
+    for (int s = 0; s < n; s++)
+        for (int i = 0; i < k; i++)
+            for (int j = 0; j < k; j++) mt[s * kk + (size_t)j * k + i] = m_rowmajor[s * kk + (size_t)i * k + j];
+    double *dm = nullptr, *db = nullptr, *dout = nullptr;
+    const size_t smem = std::max<size_t>(16, dense_smem_doubles(k) * sizeof(double));
+    bool ok = cudaMalloc(&dm, mt.size() * 8) == cudaSuccess && cudaMalloc(&db, (size_t)n * k * 8) == cudaSuccess &&
+              cudaMalloc(&dout, (size_t)n * k * 8) == cudaSuccess;
+    ok = ok && cudaMemcpy(dm, mt.data(), mt.size() * 8, cudaMemcpyHostToDevice) == cudaSuccess &&
+         cudaMemcpy(db, b, (size_t)n * k * 8, cudaMemcpyHostToDevice) == cudaSuccess &&
+         cudaFuncSetAttribute(k_dense_check, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) == cudaSuccess;
+    if (ok) {
+        k_dense_check<<<(unsigned)n, (unsigned)dense_threads(k), smem>>>(k, dm, db, dout);
+        ok = cudaGetLastError() == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess &&
+             cudaMemcpy(out, dout, (size_t)n * k * 8, cudaMemcpyDeviceToHost) == cudaSuccess;
+    }
+    cudaFree(dm); cudaFree(db); cudaFree(dout);
+    if (!ok) { set_err("sb_dense_check: CUDA error"); return -1; }
+    return 0;
+}
+
 int sb_step_timed(float* ms) {
     if (!g_eng || !g_eng->ready || !ms) return -1;
     Engine& E = *g_eng;
@@ -864,7 +896,7 @@ int sb_step_timed(float* ms) {
     k_solve<0><<<slabs, kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
     launch_rng_after_solve(E, E.hi, 0);
     cudaEventRecord(ev[4], E.hi);
-    k_dense<<<(unsigned)E.n_env, kMaxK, E.smem_dense, E.hi>>>(E.d_ctx);
+    k_dense<<<(unsigned)E.n_env, (unsigned)E.dense_threads, E.smem_dense, E.hi>>>(E.d_ctx);
     cudaEventRecord(ev[5], E.hi);
     k_solve<1><<<slabs, kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
     cudaEventRecord(ev[2], E.hi);

@@ -307,6 +307,8 @@ __device__ inline void run_sweep(const SolveShared& sh, const Sweep& sw, int B, 
 //   red  [2][team warps][2] doubles of scratch for the pivot reduction
 //   z    [k] solution by position, then [1] diagonal scratch
 __host__ __device__ constexpr size_t dense_env_doubles(int k) { return (size_t)k * (k + 1) + 16 + 2 * (size_t)k; }
+__host__ __device__ constexpr size_t dense_smem_doubles(int k) { return dense_env_doubles(k); }
+__host__ __device__ constexpr int dense_threads(int k) { return 32 * ((k + 31) / 32); }
 
 __device__ inline void team_sync(int bar, int T) {
     asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(T) : "memory");
@@ -414,6 +416,7 @@ __device__ inline void dense_team(double* M, int k, int ttid, int T, int bar) {
 // the right side ctx->airq as column k, solved by dense_team; the solution
 // replaces the right side in ctx->airq. Envs whose VAV gains are all zero
 // (or whose building couples no VAV) have no air side and return at once.
+// Launched with dense_threads(k_max) threads per CTA.
 __global__ void __launch_bounds__(kMaxK) k_dense(const StepCtx* __restrict__ ctx) {
     extern __shared__ __align__(16) double dsm[];
     const int env = ctx->dense_order[blockIdx.x];
@@ -423,18 +426,37 @@ __global__ void __launch_bounds__(kMaxK) k_dense(const StepCtx* __restrict__ ctx
     const int k = g.k, tid = threadIdx.x;
     if (k == 0) return;
     const double* D = ctx->Dst + (size_t)env * L.nd;
-    if (!__syncthreads_or(tid < k && D[L.ag + tid] != 0.0)) return;
+    int any = 0;
+    for (int i = tid; i < k; i += blockDim.x) any |= D[L.ag + i] != 0.0;
+    if (!__syncthreads_or(any)) return;
     double* q = ctx->airq + (size_t)env * ctx->k_max;
     const int per = k * (k + 1);
     for (int idx = tid; idx < per; idx += blockDim.x) {
         const int j = idx / k, i = idx % k;
-        dsm[idx] = j < k ? dadd(i == j ? 1.0 : 0.0, dmul(D[L.ag + i], g.S[(size_t)i * k + j])) : q[i];
+        dsm[idx] = j < k ? dadd(i == j ? 1.0 : 0.0, dmul(D[L.ag + i], g.St[idx])) : q[i];
     }
     __syncthreads();
-    const int T = ((k + 31) >> 5) * 32;
+    const int T = dense_threads(k);
     if (tid < T) dense_team(dsm, k, tid, T, 1);
     __syncthreads();
     for (int i = tid; i < k; i += blockDim.x) q[i] = dsm[per + 16 + i];
+}
+
+// Test entry of the dense solver: n systems of size k, Mt [n][k][k] the
+// matrices transposed (column-major), b [n][k]; the solutions to out [n][k].
+// One CTA per system, dense_threads(k) threads, the path of k_dense.
+__global__ void __launch_bounds__(kMaxK) k_dense_check(int k, const double* __restrict__ Mt,
+                                                       const double* __restrict__ b, double* __restrict__ out) {
+    extern __shared__ __align__(16) double dsm[];
+    const size_t sys = blockIdx.x;
+    const double* A = Mt + sys * k * k;
+    const int T = dense_threads(k), tid = threadIdx.x;
+    const int per = k * (k + 1);
+    for (int idx = tid; idx < per; idx += blockDim.x) dsm[idx] = idx < k * k ? A[idx] : b[sys * k + idx - k * k];
+    __syncthreads();
+    if (tid < T) dense_team(dsm, k, tid, T, 1);
+    __syncthreads();
+    for (int i = tid; i < k; i += blockDim.x) out[sys * k + i] = dsm[per + 16 + i];
 }
 
 // Phase 0: forcing, first L/U solve, sensed air-side right side (to

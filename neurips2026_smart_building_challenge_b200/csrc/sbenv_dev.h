@@ -191,6 +191,7 @@ struct GroupDev {
     const int32_t *ap_rp, *ap_col;  // applied by row position, coupled columns ascending
     const double* ap_x;
     const double* S;                // k x k sensed response
+    const double* St;               // its transpose (column j of S contiguous)
     // rooms: cells of each room in extended positions
     const int32_t *room_off, *room_pos;
     const int32_t* cell_of_pos;     // extended position -> cell index (field mean order)
