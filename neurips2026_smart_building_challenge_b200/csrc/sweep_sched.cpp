@@ -37,15 +37,15 @@ namespace {
 
 // Cost model of one warp, in SM cycles (measured with clock64 traces of the
 // kernel on B200). Only used to order the work.
-constexpr double kCCtrl = 350;    // a control record: finish rows, waits, start rows
-constexpr double kCBlk = 150;     // a term record
-constexpr double kC2 = 400;       // release store until the waiting warp has seen it
-constexpr double kCBRound = 300;  // one round (four rows) of a block record ...
-constexpr double kCBRow = 10;     // ... plus this per row of the earlier rounds
+constexpr double kCCtrl = 500;    // a control record: finish rows, waits, start rows
+constexpr double kCBlk = 250;     // a term record
+constexpr double kC2 = 600;       // release store until the waiting warp has seen it
+constexpr double kCBRound = 1800; // one round (four rows) of a block record ...
+constexpr double kCBRow = 17;     // ... plus this per row of the earlier rounds
 constexpr double kSlack = 150;    // a row may be picked this long before its next input is ready
 constexpr int kMinSeg = 16;       // shortest segment worth a control record (unless the row ends sooner)
 constexpr double kCritical = 0.9; // rows within this fraction of the top priority start at any length
-constexpr int kMinBlock = 8;      // shortest run of rows solved as a dense block
+constexpr int kMinBlock = 16;     // shortest run of rows solved as a dense block
 constexpr int kUnsched = std::numeric_limits<int>::max();
 constexpr double kInf = std::numeric_limits<double>::infinity();
 
@@ -71,6 +71,7 @@ struct WarpProg {
     int last_kind = 0;          // 0 term, 1 control or block
     bool ended = false;
     bool idle = false;          // found nothing to do at T in the current state
+    double wake = 0;            // when idle: the earliest time it could start something
 };
 
 struct Block {
@@ -335,17 +336,36 @@ std::string build_sweep(int n, const std::vector<std::vector<std::pair<int, doub
         std::vector<int> waits;
         double ready = t;
 
-        // (b) the most urgent ready block, if it beats every row this warp could start
+        // rows this warp could start now, most urgent first
+        cand.clear();
+        double next_event = kInf;
+        for (int r : open) {
+            if (!may_take(w, r)) continue;
+            if (prog[r] < lim(r)) {
+                const int c = terms[r][prog[r]].first;
+                if (!test(Kw, c)) {
+                    if (fseq[c] == kUnsched) continue;
+                    if (done[c] + kC2 - kSlack > t) { next_event = std::min(next_event, done[c] + kC2 - kSlack); continue; }
+                }
+            }
+            cand.push_back(r);
+        }
+        std::sort(cand.begin(), cand.end(), [&](int a, int b) {
+            if (prio[a] != prio[b]) return prio[a] > prio[b];
+            return backward ? a > b : a < b;
+        });
+        double top_open = 0.0;   // the most urgent row this warp may take (started or not)
+        for (int r : open)
+            if (may_take(w, r)) top_open = std::max(top_open, prio[r]);
+
+        // (b) the most urgent ready block, if it beats every row this warp can start now
         int pick_block = -1;
         for (size_t b = 0; b < blocks.size(); b++)
             if (block_ready((int)b, w, t) && (pick_block < 0 || prio[blocks[b].rows[0]] > prio[blocks[pick_block].rows[0]]))
                 pick_block = (int)b;
         bool groups_idle = true;
         for (int g = 0; g < kBundleRows; g++) groups_idle &= P.g[g].row < 0;
-        double top_open = 0.0;   // the most urgent row this warp may start
-        for (int r : open)
-            if (may_take(w, r)) top_open = std::max(top_open, prio[r]);
-        const bool block_first = pick_block >= 0 && prio[blocks[pick_block].rows[0]] >= top_open;
+        const bool block_first = pick_block >= 0 && (cand.empty() || prio[blocks[pick_block].rows[0]] >= prio[cand[0]]);
         if (block_first && groups_idle && !any) {
             Block& B = blocks[pick_block];
             B.scheduled = true;
@@ -410,24 +430,7 @@ std::string build_sweep(int n, const std::vector<std::vector<std::pair<int, doub
 
         // (c) new segments for the free groups, most urgent rows first (none
         // while a more urgent block waits for this warp's groups to drain)
-        cand.clear();
-        double next_event = kInf;
-        for (int r : open) {
-            if (!may_take(w, r)) continue;
-            if (prog[r] < lim(r)) {
-                const int c = terms[r][prog[r]].first;
-                if (!test(Kw, c)) {
-                    if (fseq[c] == kUnsched) continue;
-                    if (done[c] + kC2 - kSlack > t) { next_event = std::min(next_event, done[c] + kC2 - kSlack); continue; }
-                }
-            }
-            cand.push_back(r);
-        }
         if (block_first) cand.clear();
-        std::sort(cand.begin(), cand.end(), [&](int a, int b) {
-            if (prio[a] != prio[b]) return prio[a] > prio[b];
-            return backward ? a > b : a < b;
-        });
         bool others_busy = false;   // another warp may still change the state
         for (int q = 0; q < W; q++)
             if (q != w && !wp[q].ended && (wp[q].T > t || !wp[q].idle)) others_busy = true;
@@ -549,9 +552,14 @@ std::string build_sweep(int n, const std::vector<std::vector<std::pair<int, doub
         for (int q = 0; q < W; q++) {
             if (q == w || wp[q].ended) continue;
             if (wp[q].T > t) next_event = std::min(next_event, wp[q].T);
+            if (wp[q].T == t && wp[q].idle) next_event = std::min(next_event, wp[q].wake);
             other_now |= (wp[q].T == t && !wp[q].idle);
         }
-        if (other_now) { P.idle = true; continue; }
+        if (other_now) {
+            P.idle = true;
+            P.wake = next_event;
+            continue;
+        }
         if (!std::isfinite(next_event)) return "sweep schedule deadlocked";
         P.T = next_event;
         P.idle = false;
