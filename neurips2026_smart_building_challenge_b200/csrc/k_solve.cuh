@@ -126,33 +126,15 @@ __device__ __forceinline__ void prefetch_lines(const uint8_t* p, uint32_t bytes,
     for (uintptr_t l = l0 + (uintptr_t)lane; l <= l1; l += 32) asm volatile("prefetch.global.L1 [%0];" ::"l"(l << 7));
 }
 
-// One dense block record (format in sbenv_dev.h), the cursor at its header
-// (stage rg.head, record hq); its values are read from global memory (the
-// sweep's value region, sw_base + values) through L1, the next round's lines
-// prefetched while the current one runs. Lane group g holds the block's rows
-// i = g mod 4, one lane per env. Round c0: group g's row c0 + g loads its
-// partial sum, pulls its terms from rows 0..c0-1 (final values in shared
-// memory), then the round's four rows finish in turn, x_k from group k to all
-// lanes by a shuffle. Returns false on an error (reported in sh.abort).
-__device__ inline bool run_block(const SolveShared& sh, const StageRing& rg, uint32_t hq, const uint8_t* sw_base,
-                                 uint32_t sw_bytes, double* __restrict__ xe, bool owns, uint32_t n, uint32_t fin) {
+// The rounds of one block (BW: the U sweep, rows descending, each finished
+// by a division), after its header has been checked and its waits acquired.
+template <bool BW>
+__device__ inline void block_rounds(const SolveShared& sh, const uint8_t* __restrict__ vals, uint32_t first,
+                                    uint32_t size, uint64_t pubm, double* __restrict__ xe, bool owns, uint32_t fin) {
     const unsigned full = 0xffffffffu;
     const int lane = threadIdx.x & 31, e = lane & 7;
     const uint32_t g = (uint32_t)lane >> 3;
-    const BlockRecord* b = reinterpret_cast<const BlockRecord*>(rg.ring + (size_t)rg.hslot * kStageBytes + hq * kRecordBytes);
-    const uint32_t first = b->first, size = b->size, bw = b->backward, nw = b->nwait, voff = b->values;
-    const uint64_t pubm = b->publish;
-    const uint32_t lastrow = bw ? first - (size - 1) : first + (size - 1);
-    const uint32_t vbytes = (uint32_t)block_values((int)size) * 8u;
-    if (size == 0 || size > (uint32_t)kMaxBlockRows || bw > 1 || first >= n || lastrow >= n || (voff & 15u) ||
-        voff > sw_bytes || vbytes > sw_bytes - voff) {
-        atomicCAS((int*)sh.abort, 0, kErrBadBundle);
-        return false;
-    }
-    const uint8_t* __restrict__ vals = sw_base + voff;
-    prefetch_lines(vals, min(vbytes, 2048u), lane);
-    if (nw && !wait_rows(sh, b->wait, min(nw, (uint32_t)kCtrlWaits), n, fin)) return false;
-    const int dir = bw ? -1 : 1;
+    constexpr int dir = BW ? -1 : 1;
     const double* __restrict__ xb = xe + (int)first;   // block row j at xb[dir * j]
     // this group's in-round terms (k < g at triangle index g(g-1)/2 + k)
     const uint32_t tri0 = g * (g - 1) / 2;
@@ -163,6 +145,10 @@ __device__ inline bool run_block(const SolveShared& sh, const StageRing& rg, uin
         if (c0 + 4 < size) prefetch_lines(rp + rbytes, rbytes + 128, lane);   // the next round
         const bool mine = c0 + g < size;
         const int row = (int)first + dir * (int)(c0 + g);
+        const double t0 = __ldg(reinterpret_cast<const double*>(rp + o0));
+        const double t1 = __ldg(reinterpret_cast<const double*>(rp + o1));
+        const double t2 = __ldg(reinterpret_cast<const double*>(rp + o2));
+        const double dg = BW ? __ldg(reinterpret_cast<const double*>(rp + 8 * g)) : 1.0;
         // the row's partial sum, then its terms from the earlier rounds in order
         double a = xe[mine ? row : (int)first];
         const uint8_t* __restrict__ tv = rp + kRoundHead * 8 + 8 * c0 * g;
@@ -176,21 +162,23 @@ __device__ inline bool run_block(const SolveShared& sh, const StageRing& rg, uin
             a = dsub(a, dmul(v23.x, x2));
             a = dsub(a, dmul(v23.y, x3));
         }
-        const double dg = bw ? __ldg(reinterpret_cast<const double*>(rp + 8 * g)) : 1.0;
-        const double t0 = __ldg(reinterpret_cast<const double*>(rp + o0));
-        const double t1 = __ldg(reinterpret_cast<const double*>(rp + o1));
-        const double t2 = __ldg(reinterpret_cast<const double*>(rp + o2));
         // the four rows in turn: group k's row is final at stage k
-        const double x0 = __shfl_sync(full, bw ? ddiv(a, dg) : a, e);
+        double xm;
+        const double f0 = BW ? ddiv(a, dg) : a;
+        xm = f0;
+        const double x0 = __shfl_sync(full, f0, e);
         if (g > 0) a = dsub(a, dmul(t0, x0));
-        const double x1 = __shfl_sync(full, bw ? ddiv(a, dg) : a, 8 | e);
+        const double f1 = BW ? ddiv(a, dg) : a;
+        if (g == 1) xm = f1;
+        const double x1 = __shfl_sync(full, f1, 8 | e);
         if (g > 1) a = dsub(a, dmul(t1, x1));
-        const double x2 = __shfl_sync(full, bw ? ddiv(a, dg) : a, 16 | e);
+        const double f2 = BW ? ddiv(a, dg) : a;
+        if (g == 2) xm = f2;
+        const double x2 = __shfl_sync(full, f2, 16 | e);
         if (g > 2) a = dsub(a, dmul(t2, x2));
-        const double x3 = __shfl_sync(full, bw ? ddiv(a, dg) : a, 24 | e);
+        if (g == 3) xm = BW ? ddiv(a, dg) : a;
         // the round's rows are final: store (later rounds read them), publish
         // those other warps read
-        const double xm = g == 0 ? x0 : g == 1 ? x1 : g == 2 ? x2 : x3;
         if (mine && owns) xe[row] = xm;
         __syncwarp();
         const uint32_t pb = (uint32_t)(pubm >> c0) & 0xFu;
@@ -200,6 +188,35 @@ __device__ inline bool run_block(const SolveShared& sh, const StageRing& rg, uin
         }
         rp += rbytes;
     }
+}
+
+// One dense block record (format in sbenv_dev.h), the cursor at its header
+// (stage rg.head, record hq); its values are read from global memory (the
+// sweep's value region, sw_base + values) through L1, the next round's lines
+// prefetched while the current one runs. Lane group g holds the block's rows
+// i = g mod 4, one lane per env. Round c0: group g's row c0 + g loads its
+// partial sum, pulls its terms from rows 0..c0-1 (final values in shared
+// memory), then the round's four rows finish in turn, x_k from group k to all
+// lanes by a shuffle (group 3's value is only stored). Returns false on an
+// error (reported in sh.abort).
+__device__ inline bool run_block(const SolveShared& sh, const StageRing& rg, uint32_t hq, const uint8_t* sw_base,
+                                 uint32_t sw_bytes, double* __restrict__ xe, bool owns, uint32_t n, uint32_t fin) {
+    const int lane = threadIdx.x & 31;
+    const BlockRecord* b = reinterpret_cast<const BlockRecord*>(rg.ring + (size_t)rg.hslot * kStageBytes + hq * kRecordBytes);
+    const uint32_t first = b->first, size = b->size, bw = b->backward, nw = b->nwait, voff = b->values;
+    const uint64_t pubm = b->publish;
+    const uint32_t lastrow = bw ? first - (size - 1) : first + (size - 1);
+    const uint32_t vbytes = (uint32_t)block_values((int)size) * 8u;
+    if (size == 0 || size > (uint32_t)kMaxBlockRows || bw > 1 || first >= n || lastrow >= n || (voff & 15u) ||
+        voff > sw_bytes || vbytes > sw_bytes - voff) {
+        atomicCAS((int*)sh.abort, 0, kErrBadBundle);
+        return false;
+    }
+    const uint8_t* __restrict__ vals = sw_base + voff;
+    prefetch_lines(vals, min(vbytes, 2048u), lane);
+    if (nw && !wait_rows(sh, b->wait, min(nw, (uint32_t)kCtrlWaits), n, fin)) return false;
+    if (bw) block_rounds<true>(sh, vals, first, size, pubm, xe, owns, fin);
+    else block_rounds<false>(sh, vals, first, size, pubm, xe, owns, fin);
     return true;
 }
 
