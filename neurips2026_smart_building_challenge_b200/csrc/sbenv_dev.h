@@ -74,17 +74,17 @@ enum : int {
 // (c0+2,c0+1) (c0+3,c0) (c0+3,c0+1) (c0+3,c0+2), 2 zeros, then for each row
 // c0+q (q = 0..3) its terms (c0+q, 0..c0-1) (zeros for rows past the block).
 //
-// A program is a sequence of kRecordBytes records, three to a ring stage;
+// A program is a sequence of kRecordBytes records, kRecordsPerStage to a ring stage;
 // it starts with a control record, and a control record with kCtrlEnd ends it.
 constexpr int kSweepWarps = kSolveThreads / 32;   // warps that run sweep programs
 constexpr int kGroupLanes = 8;           // envs per lane group (slab_envs <= 8)
 constexpr int kBundleRows = 4;           // lane groups per warp
 constexpr int kTermSteps = 4;            // terms per group per term record
 constexpr int kRecordBytes = 160;
-constexpr int kRecordsPerStage = 3;
+constexpr int kRecordsPerStage = 9;
 constexpr int kStageBytes = kRecordBytes * kRecordsPerStage;   // one copy into a warp's ring
-constexpr int kStagesMin = 4;            // ring depth per warp (stages), chosen per group
-constexpr int kStagesMax = 8;
+constexpr int kStagesMin = 2;            // ring depth per warp (stages), chosen per group
+constexpr int kStagesMax = 3;
 constexpr int kCtrlWaits = 56;           // wait rows per control record
 constexpr int kMaxBlockRows = 48;        // rows of a dense block record (12 register slots per lane group)
 constexpr uint16_t kWaitPartial = 0x8000; // wait entry: the row's outside terms only

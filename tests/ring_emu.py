@@ -6,7 +6,7 @@ slot holds it, a slot is refilled only after its previous copy has landed,
 and every wait is on a stage that was issued."""
 import struct
 
-REC, STAGE = 160, 480
+REC, STAGE = 160, 1440   # nine records per ring stage (csrc/sbenv_dev.h)
 C_NEXT, C_END, C_BLOCK = 1, 2, 4
 NEXT_CTRL = 0x8000
 
@@ -55,7 +55,7 @@ def walk(stream, R):
                 assert flags & C_NEXT
                 ctrl = True
                 rec += 1
-                if rec % 3 == 0:
+                if rec % (STAGE // REC) == 0:
                     consume(st["head"] + 1)
                     assert st["head"] < nst
                     land(st["head"])
@@ -64,7 +64,7 @@ def walk(stream, R):
                 break
             ctrl = bool(flags & C_NEXT)
         rec += 1
-        if rec % 3 == 0:
+        if rec % (STAGE // REC) == 0:
             consume(st["head"] + 1)
             assert st["head"] < nst
             land(st["head"])
