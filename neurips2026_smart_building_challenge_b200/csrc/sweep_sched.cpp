@@ -39,7 +39,7 @@ namespace {
 // kernel on B200). Only used to order the work.
 constexpr double kCCtrl = 500;    // a control record: finish rows, waits, start rows
 constexpr double kCBlk = 250;     // a term record
-constexpr double kC2 = 600;       // release store until the waiting warp has seen it
+constexpr double kC2 = 800;       // release store until the waiting warp has seen it
 constexpr double kCBRound = 1800; // one round (four rows) of a block record ...
 constexpr double kCBRow = 17;     // ... plus this per row of the earlier rounds
 constexpr double kSlack = 150;    // a row may be picked this long before its next input is ready
