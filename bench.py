@@ -9,6 +9,13 @@ One step = one puf_step of every env (decode, HVAC, fp64 thermal solve with the
 air side, convection, occupancy, observation, reward, episode log).
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+    python bench.py --rollout [--gpus N --steps K --warmup W]
+
+--rollout measures BASELINE configuration 5 instead: the end-to-end env+policy
+step rate of policy-in-loop rollouts (a random-init shared MLP, hidden 128, tanh,
+in PyTorch; Beta heads with floor 1 and concentration cap 12 drawn by the
+library's sampler; one env+policy step captured in a CUDA graph and replayed
+over 128-step rollout horizons), 960 envs per GPU.
 
 N > 1 is launched with torch.distributed.run: every rank owns a disjoint slice of
 960 envs (weak scaling, no per-step collective); episode statistics are summed
@@ -50,6 +57,8 @@ def parse_args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--envs", type=int, default=ENVS_PER_GPU, help="envs per GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--rollout", action="store_true", help="configuration 5: env+policy steps in a CUDA graph")
+    ap.add_argument("--horizon", type=int, default=128, help="rollout horizon (--rollout)")
     return ap.parse_args()
 
 
@@ -346,10 +355,112 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+ROLLOUT_METRIC = "env+policy building-steps/s"
+ROLLOUT_WORKLOAD = ("config5: policy-in-loop rollouts, 960 envs per GPU over the config-2 scenario mix; "
+                    "random-init shared MLP 1024-128-128 tanh (f32, PyTorch) -> Beta heads (floor 1, cap 12) "
+                    "+ categorical discrete heads drawn by the library sampler; one env+policy step per CUDA "
+                    "graph replay, 128-step horizons")
+
+
+def run_rollout(args) -> None:
+    """Configuration 5: timed env+policy steps (graph replays), horizons of args.horizon steps."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300))
+    from neurips2026_smart_building_challenge_b200 import SmartBuildingsVec, config_dir
+    from neurips2026_smart_building_challenge_b200.rollout import Rollout, ZonePolicy
+
+    d = config_dir(2, ROOT / ".sbb_cache" / f"bench_rank{rank}")
+    n = args.envs
+    env = SmartBuildingsVec(n, blob_dir=str(d), groups=30, device=f"cuda:{local}")
+    env.reset()
+    ro = Rollout(env, ZonePolicy(env.device, seed=17), seed=1000 + rank, beta_floor=1.0, beta_cap=12.0)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=env.device)   # > 126 MB L2
+    s = env.stream
+    for i in range(args.warmup):
+        ro.step()
+    env.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            if i % args.horizon == 0:
+                env.reset()   # a new rollout: every env restarts its episode (untimed)
+            with torch.cuda.stream(s):
+                flush.fill_(i & 0xFF)
+            starts[i].record(s)
+            ro.step()
+            ends[i].record(s)
+        env.synchronize()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms_t = torch.tensor([sum(a.elapsed_time(b) for a, b in zip(starts, ends))], dtype=torch.float64,
+                        device=env.device)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_total = float(ms_t.item())
+    value = world * n * args.steps / (ms_total / 1e3)
+
+    # end to end through the public API: graph replay + rewards and terminals read back every step
+    h_rew = torch.empty(n, dtype=torch.float32).pin_memory()
+    h_term = torch.empty(n, dtype=torch.float32).pin_memory()
+    e_steps = max(3, min(args.steps, 64))
+    env.reset()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for i in range(e_steps):
+        ro.step()
+        with torch.cuda.stream(s):
+            h_rew.copy_(env.rewards, non_blocking=True)
+            h_term.copy_(env.terminals, non_blocking=True)
+    e1.record(s)
+    env.synchronize()
+    e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=env.device)
+    if world > 1:
+        dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+    e2e = {"value": world * n * e_steps / (float(e_ms.item()) / 1e3), "unit": UNIT,
+           "h2d_bytes_per_step": 0, "d2h_bytes_per_step": n * 2 * 4}
+    status = env.status()
+    k_ms = {}
+    for _ in range(3):
+        for k, v in env.step_timed().items():
+            k_ms.setdefault(k, []).append(v)
+    k_ms = {k: float(np.mean(v)) for k, v in k_ms.items()}
+    launches = (env.lib.sb_kernels_per_step() + 1) * args.steps   # the env's kernels + the sampler
+    env.close()
+    if rank == 0:
+        line = {"metric": ROLLOUT_METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_total / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f64 env, f32 policy", "data": "synthetic",
+                "config": {"workload": ROLLOUT_WORKLOAD, "envs_per_gpu": n, "total_envs": n * world,
+                           "horizon": args.horizon, "l2": "flushed between timed steps (256 MiB write, untimed)",
+                           "parallelism": f"env-sharded x{world}, no per-step collective"},
+                "env_kernel_ms": k_ms, "e2e": e2e, "gpu_launches": launches, "clocks": clk.summary(),
+                "device_status": status}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.rollout:
+        run_rollout(args)
     else:
         run_ours(args)
 

@@ -142,6 +142,24 @@ int sb_get_temp(int env, double* out, int n_cvs);
 int sb_get_mass(int env, double* out, int n_solved);
 /* Copies the last step's per-env reward (double) and log terms [n][8] to host memory. */
 int sb_get_reward_f64(double* reward, double* parts);
+/* Policy-in-loop rollouts: actions drawn from a
+ * policy's logits, as the reference trainer's mixed heads do
+ * (patches/pufferlib_core.diff:2490-2580; beta_floor / beta_conc_max of
+ * config/smart_buildings.ini). raw: two device f32 blocks [2][n][288] (the
+ * second at raw + n * 288): block 0 = the 256 continuous heads' u, then the 16
+ * discrete heads' class logits (off, on); block 1 = the continuous heads' v.
+ * Continuous head: alpha = softplus(u) + floor_c, beta = softplus(v) + floor_c,
+ * both scaled down so that alpha + beta <= cap (cap <= 0: no cap; else cap must
+ * exceed 2 floor_c), action 2x - 1 with x ~ Beta(alpha, beta). Discrete head:
+ * the drawn class index (0.0 / 1.0). mask: device u8 [n][288] as puf_mask_init
+ * writes it, or NULL for all heads active; a head with no unmasked entry gets
+ * action 0.0, a masked class is never drawn. Draws come from Philox4x32-10
+ * streams keyed by seed and counted by *call (a device u64 the caller advances
+ * between draws, so a captured graph draws fresh numbers on every replay).
+ * actions: device f32 [n][272], as puf_vec_create's actions. Enqueued on the
+ * bound stream (capturable). 0 ok, -1 bad arguments / launch error. */
+int sb_beta_actions(const float* raw, const unsigned char* mask, float* actions, int n, float floor_c, float cap,
+                    unsigned long long seed, const unsigned long long* call);
 /* Verification entry: solves n dense k x k systems (row-major m [n][k][k], right
  * sides b [n][k]) with the air-side solver of k_dense (partial pivoting in the
  * reference's order); solutions to out [n][k]. Host pointers; synchronous. */

@@ -39,7 +39,7 @@ ENV_SYMBOLS = ["sb_dict_new", "sb_dict_free", "dict_find", "dict_set", "dict_set
                "puf_live_log", "puf_mask_init", "sb_last_error", "sb_device_status", "sb_shape",
                "sb_env_info", "sb_get_temp", "sb_get_mass", "sb_get_reward_f64", "sb_kernels_per_step",
                "sb_solve_schedule", "sb_sweep_warps", "sb_sweep_stats", "sb_debug_state", "sb_step_timed", "sb_solve_bytes",
-               "sb_dense_check"]
+               "sb_dense_check", "sb_beta_actions"]
 GEN_SYMBOLS = ["sbgen_preset", "sbgen_write", "sbgen_factor_stats"]
 
 
@@ -117,6 +117,8 @@ def env_lib() -> ctypes.CDLL:
         lib.sb_debug_state.argtypes = [ctypes.c_int, dp, ctypes.c_int]
         lib.sb_step_timed.argtypes = [ctypes.POINTER(ctypes.c_float)]
         lib.sb_solve_bytes.argtypes = [dp]
+        lib.sb_beta_actions.argtypes = [vp, vp, vp, ctypes.c_int, ctypes.c_float, ctypes.c_float,
+                                        ctypes.c_ulonglong, vp]
         lib._sb_typed = True
     return lib
 
@@ -307,8 +309,9 @@ class SmartBuildingsVec:
         ms = (ctypes.c_float * 7)()
         if self.lib.sb_step_timed(ms) != 0:
             raise RuntimeError("sb_step_timed failed")
-        return dict(zip(["k_rng", "k_pre", "k_solve", "k_post", "k_solve_phase0", "k_dense", "k_solve_phase1"],
-                        list(ms)))
+        # k_rng runs beside k_solve phase 0 on its stream and has no time of its own (-1)
+        names = ["k_rng", "k_pre", "k_solve", "k_post", "k_solve_phase0", "k_dense", "k_solve_phase1"]
+        return {k: v for k, v in zip(names, list(ms)) if v >= 0.0}
 
     def solve_bytes(self) -> float:
         b = ctypes.c_double()

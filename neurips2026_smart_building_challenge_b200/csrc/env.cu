@@ -33,6 +33,7 @@
 #include "k_pre.cuh"
 #include "k_rng.cuh"
 #include "k_solve.cuh"
+#include "k_policy.cuh"
 #include "tables.h"
 
 using namespace sbenv;
@@ -854,6 +855,20 @@ int sb_get_reward_f64(double* reward, double* parts) {
 }
 
 int sb_kernels_per_step(void) { return 6; }
+
+int sb_beta_actions(const float* raw, const unsigned char* mask, float* actions, int n, float floor_c, float cap,
+                    unsigned long long seed, const unsigned long long* call) {
+    if (!raw || !actions || !call || n < 1 || !(floor_c > 0.0f) || (cap > 0.0f && !(cap > 2.0f * floor_c))) {
+        set_err("sb_beta_actions: bad arguments");
+        return -1;
+    }
+    cudaStream_t st = (g_eng && g_eng->ready) ? g_eng->stream : (cudaStream_t)0;
+    const long total = (long)n * kAct;
+    k_beta_actions<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(raw, mask, actions, n, floor_c, cap,
+                                                                     (uint64_t)seed, call);
+    if (cudaGetLastError() != cudaSuccess) { set_err("sb_beta_actions: launch failed"); return -1; }
+    return 0;
+}
 
 int sb_dense_check(int k, int n, const double* m_rowmajor, const double* b, double* out) {
     if (k < 1 || k > kMaxK || n < 1 || !m_rowmajor || !b || !out) { set_err("sb_dense_check: bad arguments"); return -1; }

@@ -97,3 +97,18 @@ def test_env_requires_gpu_without_fallback(built):
 
     with pytest.raises(RuntimeError):
         pkg.SmartBuildingsVec(2, blob="/nonexistent.sbb")
+
+
+def test_sampler_rejects_bad_arguments(built):
+    """sb_beta_actions checks its arguments on the host, before any launch."""
+    import neurips2026_smart_building_challenge_b200 as pkg
+
+    lib = pkg.env_lib()
+    buf = (ctypes.c_float * 16)()
+    p = ctypes.cast(buf, ctypes.c_void_p)
+    assert lib.sb_beta_actions(None, None, p, 4, 1.0, 12.0, 0, p) == -1
+    assert lib.sb_beta_actions(p, None, p, 4, 1.0, 12.0, 0, None) == -1
+    assert lib.sb_beta_actions(p, None, p, 0, 1.0, 12.0, 0, p) == -1
+    assert lib.sb_beta_actions(p, None, p, 4, 0.0, 12.0, 0, p) == -1       # floor must be > 0
+    assert lib.sb_beta_actions(p, None, p, 4, 1.0, 1.5, 0, p) == -1        # cap must exceed 2 floor
+    assert b"sb_beta_actions" in lib.sb_last_error()
