@@ -320,10 +320,22 @@ __device__ inline void run_sweep(const SolveShared& sh, const Sweep& sw, int B, 
 // Thread p of the team owns matrix row p for the whole solve. Row exchanges
 // are virtual: each thread tracks the position its row currently holds in the
 // reference's (physically swapped) matrix, so a swap moves no data.
+//
+// One team barrier per column step c. Before it, every row publishes its
+// column-c value: the diagonal row its value, each warp its best candidate
+// below the diagonal, found by three warp reductions over the 64-bit pattern
+// of |value| (monotonic for non-negative doubles; a NaN is no candidate) and
+// the key position << 8 | row (lower position wins ties); then each row
+// finishes the previous step's update of columns c + 1 .. k while the other
+// warps reduce. After it, every thread picks the pivot from the published
+// entries with no further dependent loads, forms its multiplier and updates
+// column c + 1 first, which is the next step's candidate.
 //   M    column-major, k rows: element (r, j) at M[j * k + r]; column k is b
-//   red  [2][team warps][2] doubles of scratch for the pivot reduction
-//   z    [k] solution by position, then [1] diagonal scratch
-__host__ __device__ constexpr size_t dense_env_doubles(int k) { return (size_t)k * (k + 1) + 16 + 2 * (size_t)k; }
+//   red  [2 step parities][16] doubles: diagonal value and row, then per warp
+//        {|value| pattern, key, value}
+//   z    [k] solution by position
+constexpr int kDenseRed = 32;
+__host__ __device__ constexpr size_t dense_env_doubles(int k) { return (size_t)k * (k + 1) + kDenseRed + (size_t)k; }
 __host__ __device__ constexpr size_t dense_smem_doubles(int k) { return dense_env_doubles(k); }
 __host__ __device__ constexpr int dense_threads(int k) { return 32 * ((k + 31) / 32); }
 
@@ -331,71 +343,87 @@ __device__ inline void team_sync(int bar, int T) {
     asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(T) : "memory");
 }
 
+// M[j][p] -= f * M[j][pr] for columns j0 .. k (eight at a time, loads first)
+__device__ __forceinline__ void dense_update(double* M, int k, int p, int pr, double f, int j0) {
+    int j = j0;
+    for (; j + 8 <= k + 1; j += 8) {
+        double a[8], q[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            a[u] = M[(size_t)(j + u) * k + p];
+            q[u] = M[(size_t)(j + u) * k + pr];
+        }
+#pragma unroll
+        for (int u = 0; u < 8; u++) M[(size_t)(j + u) * k + p] = dsub(a[u], dmul(f, q[u]));
+    }
+    for (; j <= k; j++) M[(size_t)j * k + p] = dsub(M[(size_t)j * k + p], dmul(f, M[(size_t)j * k + pr]));
+}
+
 __device__ inline void dense_team(double* M, int k, int ttid, int T, int bar) {
+    const unsigned full = 0xffffffffu;
     const int lane = ttid & 31, tw = ttid >> 5, W = T >> 5;
-    double* red = M + (size_t)k * (k + 1);   // [2][W][2]
-    double* z = red + 16;                     // [k]
-    double* dg = z + k;                       // [k]: diagonal candidate per step parity slot
+    double* red = M + (size_t)k * (k + 1);
+    double* z = red + kDenseRed;
     const bool has_row = ttid < k;
     const int p = has_row ? ttid : 0;
     int mypos = ttid;
     bool stopped = false;
+    double cv = has_row ? M[p] : 0.0;   // this row's value in the current column
+    double fr = 0.0;                    // the previous step's multiplier (0: nothing pending)
+    int prow = 0;                       // the previous step's pivot row
     for (int c = 0; c < k; c++) {
-        // candidates below the diagonal: larger |value| wins, the lower position on
-        // ties (key: position << 8 | row); a NaN never compares greater, so never wins
-        double ba = -1.0;
-        int key = 0x7FFFFFFF;
-        if (has_row && mypos >= c) {
-            const double v = M[(size_t)c * k + p];
-            if (mypos == c) {
-                dg[c & 1] = (double)p;   // the diagonal row: read by everyone after the barrier
-            } else if (fabs(v) > -1.0) {
-                ba = fabs(v);
-                key = (mypos << 8) | p;
-            }
+        double* sl = red + (c & 1) * 16;
+        // publish: the diagonal, and the warp's best candidate below it
+        const double av = fabs(cv);
+        const uint64_t pat = (has_row && mypos > c && av == av) ? (uint64_t)__double_as_longlong(av) + 1ull : 0ull;
+        if (has_row && mypos == c) {
+            sl[0] = cv;
+            sl[1] = (double)p;
         }
-        for (int o = 16; o > 0; o >>= 1) {
-            const double oa = __shfl_xor_sync(0xffffffffu, ba, o);
-            const int ok = __shfl_xor_sync(0xffffffffu, key, o);
-            if (oa > ba || (oa == ba && ok < key)) { ba = oa; key = ok; }
-        }
-        double* rb = red + (size_t)(c & 1) * W * 2;
+        const unsigned hi = (unsigned)(pat >> 32);
+        const unsigned mhi = __reduce_max_sync(full, hi);
+        const unsigned mlo = __reduce_max_sync(full, hi == mhi ? (unsigned)pat : 0u);
+        const bool top = pat != 0ull && hi == mhi && (unsigned)pat == mlo;
+        const unsigned key = top ? ((unsigned)mypos << 8) | (unsigned)p : 0xFFFFFFFFu;
+        const unsigned mkey = __reduce_min_sync(full, key);
         if (lane == 0) {
-            rb[2 * tw] = ba;
-            rb[2 * tw + 1] = int_in_double(key);
+            sl[2 + 3 * tw] = __longlong_as_double((long long)(((uint64_t)mhi << 32) | mlo));
+            sl[3 + 3 * tw] = (double)mkey;
         }
+        if (top && key == mkey) sl[4 + 3 * tw] = cv;
+        // the rest of the previous step's update
+        if (fr != 0.0) dense_update(M, k, p, prow, fr, c + 1);
         team_sync(bar, T);
+        // the pivot: the best candidate if strictly larger than the diagonal
+        const double dv = sl[0];
+        const int drow = (int)sl[1];
+        uint64_t bp = 0ull;
+        unsigned bk = 0xFFFFFFFFu;
+        double bv = 0.0;
         for (int q = 0; q < W; q++) {
-            const double oa = rb[2 * q];
-            const int ok = int_from_double(rb[2 * q + 1]);
-            if (oa > ba || (oa == ba && ok < key)) { ba = oa; key = ok; }
+            const uint64_t qp = (uint64_t)__double_as_longlong(sl[2 + 3 * q]);
+            const unsigned qk = (unsigned)sl[3 + 3 * q];
+            const double qv = sl[4 + 3 * q];
+            if (qp > bp || (qp == bp && qk < bk)) { bp = qp; bk = qk; bv = qv; }
         }
-        // the reference: best = |diagonal|, replaced by a later row only if strictly larger
-        const int drow = (int)dg[c & 1];
-        const double dv = M[(size_t)c * k + drow];
-        int piv = c, prow = drow;
-        double pbest = fabs(dv);
-        if (key != 0x7FFFFFFF && ba > pbest) { piv = key >> 8; prow = key & 0xFF; pbest = ba; }
-        if (pbest == 0.0) { stopped = true; break; }
-        const double d = M[(size_t)c * k + prow];
+        int piv = c, pr = drow;
+        double d = dv;
+        if (bp != 0ull && fabs(bv) > fabs(dv)) { piv = (int)(bk >> 8); pr = (int)(bk & 0xFFu); d = bv; }
+        if (fabs(d) == 0.0) { stopped = true; break; }
         if (mypos == c) mypos = piv;
         else if (mypos == piv) mypos = c;
-        // eliminate below the pivot, eight columns at a time (all loads first)
+        // this step's multiplier; column c + 1 now (the next candidate), the rest later
+        fr = 0.0;
         if (has_row && mypos > c) {
-            const double fr = ddiv(M[(size_t)c * k + p], d);
-            if (fr != 0.0) {
-                int j = c + 1;
-                for (; j + 8 <= k + 1; j += 8) {
-                    double a[8], q[8];
-#pragma unroll
-                    for (int u = 0; u < 8; u++) {
-                        a[u] = M[(size_t)(j + u) * k + p];
-                        q[u] = M[(size_t)(j + u) * k + prow];
-                    }
-#pragma unroll
-                    for (int u = 0; u < 8; u++) M[(size_t)(j + u) * k + p] = dsub(a[u], dmul(fr, q[u]));
-                }
-                for (; j <= k; j++) M[(size_t)j * k + p] = dsub(M[(size_t)j * k + p], dmul(fr, M[(size_t)j * k + prow]));
+            const double f = ddiv(cv, d);
+            double* mc = M + (size_t)(c + 1) * k;
+            if (f != 0.0) {
+                fr = f;
+                prow = pr;
+                cv = dsub(mc[p], dmul(f, mc[pr]));
+                mc[p] = cv;
+            } else {
+                cv = mc[p];
             }
         }
     }
@@ -456,7 +484,7 @@ __global__ void __launch_bounds__(kMaxK) k_dense(const StepCtx* __restrict__ ctx
     const int T = dense_threads(k);
     if (tid < T) dense_team(dsm, k, tid, T, 1);
     __syncthreads();
-    for (int i = tid; i < k; i += blockDim.x) q[i] = dsm[per + 16 + i];
+    for (int i = tid; i < k; i += blockDim.x) q[i] = dsm[per + kDenseRed + i];
 }
 
 // Test entry of the dense solver: n systems of size k, Mt [n][k][k] the
@@ -473,7 +501,7 @@ __global__ void __launch_bounds__(kMaxK) k_dense_check(int k, const double* __re
     __syncthreads();
     if (tid < T) dense_team(dsm, k, tid, T, 1);
     __syncthreads();
-    for (int i = tid; i < k; i += blockDim.x) out[sys * k + i] = dsm[per + 16 + i];
+    for (int i = tid; i < k; i += blockDim.x) out[sys * k + i] = dsm[per + kDenseRed + i];
 }
 
 // Phase 0: forcing, first L/U solve, sensed air-side right side (to
