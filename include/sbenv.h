@@ -112,7 +112,11 @@ void puf_bind_stream(sb_stream_t stream);
 void puf_init(Env* env, Dict* kwargs);
 /* Restarts every env: state from the blob, occupancy primed, reset observation written. */
 void puf_reset(Env* envs);
-/* One batched step of every env (device only, graph-capturable). */
+/* One batched step of every env (device only, graph-capturable). With the
+ * environment variable SB_SNAPSHOT=<file> set it also writes a snapshot of env
+ * SB_SNAP_ENV (default 0) every SB_SNAP_EVERY-th call (default 1) that is not
+ * being captured, synchronising the stream, as the reference does
+ * (smart_buildings.cu:3015-3026); puf_live_log then writes one as well. */
 void puf_step(Env* envs);
 void puf_render(Env* env);
 void puf_close(Env* env);
@@ -164,6 +168,18 @@ int sb_beta_actions(const float* raw, const unsigned char* mask, float* actions,
  * sides b [n][k]) with the air-side solver of k_dense (partial pivoting in the
  * reference's order); solutions to out [n][k]. Host pointers; synchronous. */
 int sb_dense_check(int k, int n, const double* m_rowmajor, const double* b, double* out);
+/* Snapshot of one env's visible state to a file, the reference's headless
+ * viewer feed (SBS1, smart_buildings.cu:2205-2290), after the last step:
+ * "SBS1", i32[12] {1, step in the episode, episode length, env index in its
+ * solver group, zones, VAVs, AHUs, grid rows, grid columns, cells, actions, 0},
+ * f64[12] {reward, episode return, boiler setpoint, boiler return, the 8 reward
+ * terms}, char[512] scenario path, f32 field[cells] (K, cell order), f64 zone
+ * means / occupancy / flow setpoint / flow [zones each], f64 VAV heating and
+ * cooling setpoints / damper / reheat [VAVs each], f64 AHU supply temperature /
+ * flow [AHUs each], i32 AHU run [AHUs], f64 native actions [actions], all
+ * little-endian. Written to <path>.tmp, then renamed. Synchronises the bound
+ * stream (not capturable). 0 ok, 1 error (sb_last_error). */
+int sb_snapshot_write(int env, const char* path);
 /* Number of hot-path kernel launches one puf_step enqueues. */
 int sb_kernels_per_step(void);
 /* Measurement: runs one step with CUDA events around each kernel on the bound

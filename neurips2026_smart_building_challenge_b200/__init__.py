@@ -39,7 +39,7 @@ ENV_SYMBOLS = ["sb_dict_new", "sb_dict_free", "dict_find", "dict_set", "dict_set
                "puf_live_log", "puf_mask_init", "sb_last_error", "sb_device_status", "sb_shape",
                "sb_env_info", "sb_get_temp", "sb_get_mass", "sb_get_reward_f64", "sb_kernels_per_step",
                "sb_solve_schedule", "sb_sweep_warps", "sb_sweep_stats", "sb_debug_state", "sb_step_timed", "sb_solve_bytes",
-               "sb_dense_check", "sb_beta_actions"]
+               "sb_dense_check", "sb_beta_actions", "sb_snapshot_write"]
 GEN_SYMBOLS = ["sbgen_preset", "sbgen_write", "sbgen_factor_stats"]
 
 
@@ -119,6 +119,7 @@ def env_lib() -> ctypes.CDLL:
         lib.sb_solve_bytes.argtypes = [dp]
         lib.sb_beta_actions.argtypes = [vp, vp, vp, ctypes.c_int, ctypes.c_float, ctypes.c_float,
                                         ctypes.c_ulonglong, vp]
+        lib.sb_snapshot_write.argtypes = [ctypes.c_int, ctypes.c_char_p]
         lib._sb_typed = True
     return lib
 
@@ -300,6 +301,11 @@ class SmartBuildingsVec:
                                       p.ctypes.data_as(ctypes.POINTER(ctypes.c_double))) != 0:
             raise RuntimeError("sb_get_reward_f64 failed")
         return r, p
+
+    def snapshot(self, env: int, path) -> None:
+        """Writes env `env`'s visible state after the last step to an SBS1 file (`read_snapshot`)."""
+        if self.lib.sb_snapshot_write(env, str(path).encode()) != 0:
+            raise RuntimeError(self.lib.sb_last_error().decode())
 
     def status(self) -> int:
         return int(self.lib.sb_device_status())

@@ -111,6 +111,7 @@ struct Engine {
     size_t smem_solve = 0, smem_pre = 0, smem_post = 0, smem_rng = 0, smem_dense = 0;
     int dense_threads = 32;          // k_dense block (dense_threads(k_max))
     int max_ncv = 0;
+    double* d_snap = nullptr;     // snapshot staging (k_snapshot), sized for the largest scenario
     bool ready = false;
     ~Engine() { destroy(); }
     void destroy() {
@@ -177,7 +178,8 @@ StateLayout make_layout(int na, int nv, int nz, int k) {
     L.ahu_rec = D(na); L.ahu_sat = D(na); L.ahu_fan = D(na); L.ahu_flow = D(na);
     L.v_damp = D(nv); L.v_reh = D(nv); L.v_ratio = D(nv); L.v_hsp = D(nv); L.v_csp = D(nv);
     L.v_dcmd = D(nv); L.v_rcmd = D(nv); L.v_sense = D(nv); L.v_area = D(nv);
-    L.qdiv = D(nz); L.ag = D(k); L.aT = D(k); L.coil = D(k); L.V = D(nz);
+    L.qdiv = D(nz); L.ag = D(k); L.aT = D(k); L.coil = D(k); L.V = D(nz); L.zavg = D(nz);
+    L.zfsp = D(nz); L.zfact = D(nz);
     L.ff_sum = D(1); L.pump_head = D(1); L.b_sp = D(1); L.b_ret = D(1); L.b_cur = D(1); L.b_step = D(1);
     L.reheat_w = D(1);
     L.ahu_run = I(na); L.ahu_creq = I(na); L.v_mode = I(nv); L.v_prev = I(nv); L.v_dset = I(nv); L.v_rset = I(nv);
@@ -395,6 +397,7 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
             gd.St = E.arena.upload(st, ok);
         }
         gd.room_off = E.arena.upload(h.room_off, ok); gd.room_pos = E.arena.upload(h.room_pos, ok);
+        gd.room_cells = h.room_off.empty() ? 0 : h.room_off.back();
         gd.cell_of_pos = E.arena.upload(h.cell_of_pos, ok); gd.pos_of_cell = E.arena.upload(h.pos_of_cell, ok);
         gd.cv_off = E.arena.upload(h.cv_off, ok); gd.cv_pos = E.arena.upload(h.cv_pos, ok);
         gd.cand_off = E.arena.upload(h.cand_off, ok); gd.cand_idx = E.arena.upload(h.cand_idx, ok);
@@ -406,7 +409,7 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
         E.max_ncv = std::max(E.max_ncv, h.ncv);
         E.smem_pre = std::max(E.smem_pre, sizeof(double) * (size_t)(L.nd + 2 * nz_max + nv_max + 2 * na_max + 2 * k_max) +
                                               sizeof(int32_t) * (size_t)L.ni);
-        E.smem_post = std::max(E.smem_post, sizeof(double) * (size_t)(2 * h.ncv + 3 * nz_max + 2 * nv_max));
+        E.smem_post = std::max(E.smem_post, sizeof(double) * post_smem_doubles(h.ncv, nz_max, nv_max));
         const size_t rng_b = 4 * (size_t)(624 + 624 + 1248) + 4 * (4 * (size_t)h.cv_off.back() + 1 + h.cv_off.size());
         E.smem_rng = std::max(E.smem_rng, rng_b);
     }
@@ -436,6 +439,9 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
         s.vz_off = E.arena.upload(h.vz_off, ok); s.vz_idx = E.arena.upload(h.vz_idx, ok);
         s.v_ahu = E.arena.upload(h.v_ahu, ok); s.coupled = E.arena.upload(h.coupled, ok);
         s.zv_off = E.arena.upload(h.zv_off, ok); s.zv_idx = E.arena.upload(h.zv_idx, ok);
+        s.zc_off = E.arena.upload(h.zc_off, ok); s.zc_col = E.arena.upload(h.zc_col, ok);
+        s.ac_off = E.arena.upload(h.ac_off, ok); s.ac_col = E.arena.upload(h.ac_col, ok);
+        s.av_off = E.arena.upload(h.av_off, ok); s.av_idx = E.arena.upload(h.av_idx, ok);
         s.proom = E.arena.upload(h.proom, ok); s.room_ncell = E.arena.upload(h.room_ncell, ok);
         s.a_kind = E.arena.upload(h.a_kind, ok); s.a_act = E.arena.upload(h.a_act, ok);
         s.a_disc = E.arena.upload(h.a_disc, ok); s.a_idx = E.arena.upload(h.a_idx, ok);
@@ -490,6 +496,14 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     if (!(C.reward_scale > 0.0f)) C.reward_scale = 1.0f;
     C.rew_f64 = E.arena.zeros<double>(n, ok);
     C.parts_out = E.arena.zeros<double>((size_t)n * kParts, ok);
+    {
+        size_t snap = 16;
+        for (const HostScn& h : E.hs) {
+            const HostGroup& hg2 = E.hg[h.group];
+            snap = std::max(snap, snap_doubles(hg2.ncv, h.nz, h.nv, h.na, h.nact));
+        }
+        E.d_snap = E.arena.zeros<double>(snap, ok);
+    }
     C.epret_d = E.arena.zeros<double>(n, ok);
     C.live = E.arena.zeros<double>(2 + kParts, ok);
     C.live_scn = E.arena.zeros<double>((size_t)G * 4, ok);
@@ -566,6 +580,27 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     CK(cudaDeviceSynchronize());
     E.ready = true;
     return true;
+}
+
+// SB_SNAPSHOT=<file> turns per-step snapshots on (the reference's viewer
+// feed); SB_SNAP_ENV (default 0) picks the env, SB_SNAP_EVERY (default 1)
+// writes every Nth step.
+struct SnapCfg {
+    const char* path;
+    int env, every;
+};
+SnapCfg snap_cfg() {
+    static SnapCfg c = {nullptr, 0, 1};
+    static bool init = false;
+    if (!init) {
+        init = true;
+        const char* p = getenv("SB_SNAPSHOT");
+        if (p && p[0]) c.path = p;
+        if (const char* e = getenv("SB_SNAP_ENV")) c.env = atoi(e);
+        if (const char* e = getenv("SB_SNAP_EVERY")) c.every = atoi(e);
+        if (c.every < 1) c.every = 1;
+    }
+    return c;
 }
 
 bool do_reset(Engine& E) {
@@ -693,6 +728,14 @@ void puf_step(Env* envs) {
     (void)envs;
     if (!g_eng || !g_eng->ready) { set_err("puf_step: no env batch"); return; }
     launch_step(*g_eng);
+    // SB_SNAPSHOT: every SB_SNAP_EVERY-th step outside a capture (synchronises)
+    const SnapCfg sc = snap_cfg();
+    if (sc.path) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        cudaStreamIsCapturing(g_eng->stream, &cs);
+        static long long count = 0;
+        if (cs == cudaStreamCaptureStatusNone && ++count % sc.every == 0) sb_snapshot_write(sc.env, sc.path);
+    }
 }
 
 void puf_render(Env* env) { (void)env; }
@@ -728,6 +771,8 @@ void puf_live_log(Env* envs, Dict* out) {
     if (!g_eng || !out) return;
     Engine& E = *g_eng;
     if (cudaStreamSynchronize(E.stream) != cudaSuccess) return;
+    const SnapCfg sc = snap_cfg();
+    if (sc.path) sb_snapshot_write(sc.env, sc.path);
     double h[2 + kParts];
     std::vector<double> hs(E.sd.size() * 4), he(E.sd.size() * 2);
     cudaMemcpy(h, E.ctx.live, sizeof(h), cudaMemcpyDeviceToHost);
@@ -891,6 +936,74 @@ int sb_dense_check(int k, int n, const double* m_rowmajor, const double* b, doub
     }
     cudaFree(dm); cudaFree(db); cudaFree(dout);
     if (!ok) { set_err("sb_dense_check: CUDA error"); return -1; }
+    return 0;
+}
+
+int sb_snapshot_write(int env, const char* path) {
+    if (!g_eng || !g_eng->ready || env < 0 || env >= g_eng->n_env || !path || !path[0]) {
+        set_err("sb_snapshot_write: no env batch, env out of range or no path");
+        return 1;
+    }
+    Engine& E = *g_eng;
+    const EnvIndex ei = E.ei[env];
+    const HostScn& h = E.hs[ei.scn];
+    const HostGroup& hg = E.hg[ei.group];
+    const int nz = h.nz, nv = h.nv, na = h.na, nact = h.nact, ncv = hg.ncv;
+    std::vector<double> st(snap_doubles(ncv, nz, nv, na, nact));
+    double rew = 0.0, parts[kParts];
+    k_snapshot<<<1, 128, 0, E.stream>>>(E.d_ctx, env, E.d_snap);
+    bool ok = cudaGetLastError() == cudaSuccess && cudaStreamSynchronize(E.stream) == cudaSuccess;
+    ok = ok && cudaMemcpy(st.data(), E.d_snap, st.size() * sizeof(double), cudaMemcpyDeviceToHost) == cudaSuccess;
+    ok = ok && cudaMemcpy(&rew, E.ctx.rew_f64 + env, sizeof(double), cudaMemcpyDeviceToHost) == cudaSuccess;
+    ok = ok && cudaMemcpy(parts, E.ctx.parts_out + (size_t)env * kParts, sizeof(parts), cudaMemcpyDeviceToHost) ==
+                   cudaSuccess;
+    if (!ok) { set_err("sb_snapshot_write: device copy failed"); return 1; }
+    const double* f = st.data();
+    const double* zone = f + ncv;
+    const double* vav = zone + 4 * (size_t)nz;
+    const double* ahu = vav + 4 * (size_t)nv;
+    const double* native = ahu + 3 * (size_t)na;
+    const double* tail = native + nact;
+    // SBS1 (little-endian): "SBS1", i32[12], f64[12], char[512] blob, f32 field[ncv],
+    // f64 zone means / occupancy / flow setpoint / flow [nz], VAV heating and cooling
+    // setpoints / damper / reheat [nv], AHU supply temperature / flow [na], i32 AHU
+    // run [na], f64 native actions [nact]
+    std::vector<unsigned char> o;
+    auto put = [&o](const void* p, size_t n) {
+        const unsigned char* b = static_cast<const unsigned char*>(p);
+        o.insert(o.end(), b, b + n);
+    };
+    put("SBS1", 4);
+    const int32_t ints[12] = {1, (int32_t)tail[0], h.max_steps, ei.local, nz, nv, na, hg.rows, hg.cols, ncv, nact, 0};
+    put(ints, sizeof(ints));
+    double sc[12] = {rew, (double)E.envs[env].ep_ret, tail[1], tail[2]};
+    for (int q = 0; q < kParts; q++) sc[4 + q] = parts[q];
+    put(sc, sizeof(sc));
+    char bp[512] = {0};
+    snprintf(bp, sizeof(bp), "%s", h.path.c_str());
+    put(bp, sizeof(bp));
+    std::vector<float> fld(ncv);
+    for (int c = 0; c < ncv; c++) fld[c] = (float)f[c];
+    put(fld.data(), sizeof(float) * (size_t)ncv);
+    put(zone, sizeof(double) * 4 * (size_t)nz);
+    put(vav, sizeof(double) * 4 * (size_t)nv);
+    put(ahu, sizeof(double) * 2 * (size_t)na);
+    std::vector<int32_t> run(na);
+    for (int a = 0; a < na; a++) run[a] = (int32_t)ahu[2 * na + a];
+    put(run.data(), sizeof(int32_t) * (size_t)na);
+    put(native, sizeof(double) * (size_t)nact);
+    // written to <path>.tmp, then renamed: a reader never sees a torn file
+    const std::string tmp = std::string(path) + ".tmp";
+    FILE* fp = fopen(tmp.c_str(), "wb");
+    if (!fp) { set_err("sb_snapshot_write: cannot open %s", tmp.c_str()); return 1; }
+    const size_t wr = fwrite(o.data(), 1, o.size(), fp);
+    const int cl = fclose(fp);
+    if (wr != o.size() || cl != 0) {
+        remove(tmp.c_str());
+        set_err("sb_snapshot_write: write failed");
+        return 1;
+    }
+    if (rename(tmp.c_str(), path) != 0) { set_err("sb_snapshot_write: rename failed"); return 1; }
     return 0;
 }
 

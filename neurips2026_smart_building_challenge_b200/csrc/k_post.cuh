@@ -59,10 +59,18 @@ __device__ inline void write_obs(const EnvView& v, const ScnDev& s, int j, const
     }
     const double* aux = s.aux + (size_t)j * (s.n_aux - 1);
     for (int q = tid; q < s.n_aux - 1; q += blockDim.x) out[s.n_dev + q] = (float)aux[q];
-    if (tid == 0) {
+    if (tid < 32) {   // warp 0: the zones' occupancy loaded 32 at a time, summed in order on lane 0
         double occ = 0.0;
-        for (int z = 0; z < s.nz; z++) occ = dadd(occ, V[z]);
-        out[s.n_dev + s.n_aux - 1] = (float)(int)occ;
+        for (int base = 0; base < s.nz; base += 128) {
+            double vz[4];
+#pragma unroll
+            for (int c = 0; c < 4; c++) vz[c] = base + 32 * c + tid < s.nz ? V[base + 32 * c + tid] : 0.0;
+#pragma unroll
+            for (int c = 0; c < 4; c++)
+                for (int q = 0; q < 32 && base + 32 * c + q < s.nz; q++)
+                    occ = dadd(occ, __shfl_sync(0xffffffffu, vz[c], q));
+        }
+        if (tid == 0) out[s.n_dev + s.n_aux - 1] = (float)(int)occ;
     }
 }
 
@@ -108,7 +116,13 @@ __device__ inline void reset_state(const EnvView& v, const ScnDev& s) {
 // Shared-memory layout of k_post / k_reset: field, staging, zone scratch.
 struct PostShared {
     double *T, *stage, *zavg, *zterm, *zdev, *vws, *varea;
+    double* ahu;   // [3][kMaxAhu] per-AHU reward terms: intake, exhaust, cooling
+    double* sc;    // [kPostScalars] reward scalars handed to the final thread
 };
+constexpr int kPostScalars = 10;
+__host__ __device__ constexpr size_t post_smem_doubles(int ncv, int nz, int nv) {
+    return 2 * (size_t)ncv + 3 * (size_t)nz + 2 * (size_t)nv + 3 * kMaxAhu + kPostScalars;
+}
 __device__ inline PostShared post_shared(uint8_t* smem, int ncv, int nz, int nv) {
     PostShared p;
     p.T = reinterpret_cast<double*>(smem);
@@ -118,6 +132,8 @@ __device__ inline PostShared post_shared(uint8_t* smem, int ncv, int nz, int nv)
     p.zdev = p.zterm + nz;
     p.vws = p.zdev + nz;
     p.varea = p.vws + nv;
+    p.ahu = p.varea + nv;
+    p.sc = p.ahu + 3 * kMaxAhu;
     return p;
 }
 
@@ -136,6 +152,7 @@ __device__ inline void restart_env(const StepCtx* ctx, int env, const GroupDev& 
     zone_means(g, s, p.T, p.zavg);
     __syncthreads();
     vav_sensing(s, p.zavg, v.D + L.v_area, v.D + L.v_sense);
+    for (int z = threadIdx.x; z < s.nz; z += blockDim.x) v.d(L.zavg, z) = p.zavg[z];
     __syncthreads();
     float* o = ctx->obs + (size_t)env * kObs;
     write_obs(v, s, 0, Vprime, o);
@@ -158,7 +175,7 @@ __global__ void __launch_bounds__(128) k_post(const StepCtx* __restrict__ ctx) {
     double* Tg = g.T + (size_t)local * g.ncv;
 
     // ---- convection (sb_sim.c:489): apply this step's permutation ----
-    for (int i = tid; i < g.ncv; i += blockDim.x) p.T[i] = Tg[i];
+    block_copy(p.T, (const double*)Tg, g.ncv);
     __syncthreads();
     const int npairs = *s.conv_npairs;
     for (int q = tid; q < npairs; q += blockDim.x) p.stage[q] = p.T[s.conv_pairs[2 * q + 1]];
@@ -212,13 +229,46 @@ __global__ void __launch_bounds__(128) k_post(const StepCtx* __restrict__ ctx) {
     write_obs(v, s, j, Vin, o);
 
     // ---- reward (sb_reward.c:31-155) ----
-    zone_means(g, s, p.T, p.zavg);
+    // zone means (sb_sim.c:149-160): the field copied into room order (p.stage
+    // is free after the convection), then one thread per zone sums its cells
+    for (int t = tid; t < g.room_cells; t += blockDim.x) p.stage[t] = p.T[g.room_pos[t]];
+    __syncthreads();
+    for (int z = tid; z < nz; z += blockDim.x) {
+        const int rm = s.proom[z];
+        const int a = g.room_off[rm], b = g.room_off[rm + 1];
+        const double* r = p.stage + a;
+        double sum = 0.0;
+        int t = 0;
+        for (; t + 8 <= b - a; t += 8) {
+            double tv[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) tv[u] = r[t + u];
+#pragma unroll
+            for (int u = 0; u < 8; u++) sum = dadd(sum, tv[u]);
+        }
+        for (; t < b - a; t++) sum = dadd(sum, r[t]);
+        p.zavg[z] = ddiv(sum, (double)(b - a));
+    }
     __syncthreads();
     const double hsp = s.s_heat[j], csp = s.s_cool[j];
     const double dt = s.dt, inv_hour = 1.0 / 3600.0;
     const double max_pph = s.rw[0], min_pph = s.rw[1], ref = s.rw[2];
     for (int z = tid; z < nz; z += blockDim.x) {
         const double zt = p.zavg[z];
+        v.d(L.zavg, z) = zt;   // the next k_pre's zone means (the field is unchanged until then)
+        {   // zone flow setpoint and actual flow (sb_reward.c:44-56; snapshots show them)
+            double fsp = 0.0, fact = 0.0;
+            for (int t = s.zv_off[z]; t < s.zv_off[z + 1]; t++) {
+                const int vv = s.zv_idx[t];
+                const double va = v.d(L.v_area, vv);
+                if (va <= 0.0) continue;
+                const double share = ddiv(s.zarea[z], va);
+                fsp = dadd(fsp, dmul(s.vav_c[vv * 9], share));
+                fact = dadd(fact, dmul(dmul(vav_unrestricted(v, s, vv), v.d(L.v_ratio, vv)), share));
+            }
+            v.d(L.zfsp, z) = fsp;
+            v.d(L.zfact, z) = fact;
+        }
         double dev = dsub(zt, csp);
         if (dsub(hsp, zt) > dev) dev = dsub(hsp, zt);
         if (dev < 0.0) dev = 0.0;
@@ -237,38 +287,38 @@ __global__ void __launch_bounds__(128) k_post(const StepCtx* __restrict__ ctx) {
         p.varea[vv] = area;
         p.vws[vv] = area > 0.0 ? dmul(ddiv(wt, area), area) : 0.0;
     }
+    if (tid == 0 && s.tmean_needed) {   // the field mean, for an AHU without VAV area
+        double tmean = 0.0;
+        for (int q = 0; q < g.ncv; q++) tmean = dadd(tmean, p.T[g.pos_of_cell[q]]);
+        p.sc[0] = ddiv(tmean, (double)g.ncv);
+    }
     __syncthreads();
-    if (tid == 0) {
-        const double ambient = s.amb[j];
-        const int hour = (int)s.r_hour[j], month = (int)s.r_month[j], wd = (int)s.r_wd[j];
-        double ws[kMaxAhu], at[kMaxAhu];
-        for (int a = 0; a < na; a++) { ws[a] = 0.0; at[a] = 0.0; }
-        for (int vv = 0; vv < nv; vv++) {
+    // the reward's independent terms in parallel: per AHU (its VAVs in ascending
+    // order), boiler and pump, and the two zone sums; the final thread adds them
+    // up in the reference's order
+    const double ambient = s.amb[j];
+    if (tid < na) {
+        const int a = tid;
+        double ws = 0.0, at = 0.0;
+        for (int q = s.av_off[a]; q < s.av_off[a + 1]; q++) {
+            const int vv = s.av_idx[q];
             if (p.varea[vv] > 0.0) {
-                const int a = s.v_ahu[vv];
-                ws[a] = dadd(ws[a], p.vws[vv]);
-                at[a] = dadd(at[a], p.varea[vv]);
+                ws = dadd(ws, p.vws[vv]);
+                at = dadd(at, p.varea[vv]);
             }
         }
-        double tmean = 0.0;
-        if (s.tmean_needed) {
-            for (int q = 0; q < g.ncv; q++) tmean = dadd(tmean, p.T[g.pos_of_cell[q]]);
-            tmean = ddiv(tmean, (double)g.ncv);
-        }
-        double intake = 0.0, exhaust = 0.0, cooling = 0.0;
-        for (int a = 0; a < na; a++) {
-            const double recirc = at[a] > 0.0 ? ddiv(ws[a], at[a]) : tmean;
-            const double st = ahu_static_p(v, s, a);
-            const double fe = s.ahu_c[a * 9 + 5];
-            const double flow = v.iv(L.ahu_run, a) == 1 ? v.d(L.ahu_flow, a) : 0.0;
-            const double rec = v.d(L.ahu_rec, a);
-            intake = dadd(intake, ddiv(dmul(flow, st), fe));
-            exhaust = dadd(exhaust, ddiv(dmul(dmul(flow, dsub(1.0, rec)), st), fe));
-            const double mixed = dadd(dmul(rec, recirc), dmul(dsub(1.0, rec), ambient));
-            const double sat = (mixed > v.d(L.ahu_sat, a) && v.iv(L.ahu_run, a) == 1) ? v.d(L.ahu_sat, a) : mixed;
-            cooling = dadd(cooling, ddiv(dmul(dmul(dmul(flow, RHO_AIR), CP_AIR), dsub(sat, mixed)), s.ahu_c[a * 9 + 4]));
-        }
-        const double blower = dadd(intake, exhaust);
+        const double recirc = at > 0.0 ? ddiv(ws, at) : p.sc[0];
+        const double st = ahu_static_p(v, s, a);
+        const double fe = s.ahu_c[a * 9 + 5];
+        const double flow = v.iv(L.ahu_run, a) == 1 ? v.d(L.ahu_flow, a) : 0.0;
+        const double rec = v.d(L.ahu_rec, a);
+        p.ahu[a] = ddiv(dmul(flow, st), fe);
+        p.ahu[kMaxAhu + a] = ddiv(dmul(dmul(flow, dsub(1.0, rec)), st), fe);
+        const double mixed = dadd(dmul(rec, recirc), dmul(dsub(1.0, rec), ambient));
+        const double sat = (mixed > v.d(L.ahu_sat, a) && v.iv(L.ahu_run, a) == 1) ? v.d(L.ahu_sat, a) : mixed;
+        p.ahu[2 * kMaxAhu + a] = ddiv(dmul(dmul(dmul(flow, RHO_AIR), CP_AIR), dsub(sat, mixed)), s.ahu_c[a * 9 + 4]);
+    }
+    if (tid == 32) {
         const double tf = water_flow(v, s);
         // boiler gas rate (sb_reward.c:12-29); log(r2/c6)/c8 precomputed on the host
         double gas_rate;
@@ -290,17 +340,44 @@ __global__ void __launch_bounds__(128) k_post(const StepCtx* __restrict__ ctx) {
             const double tot = dadd(dadd(flow, diss), tank);
             gas_rate = tot > 0.0 ? tot : 0.0;
         }
-        const double pump_e = ddiv(dmul(dmul(dmul(tf, RHO_W), GRAV), v.d(L.pump_head)), s.pump_eff);
-        double total_occ = 0.0, cum = 0.0, dsum = 0.0, dmax = 0.0;
-        int oob = 0;
+        p.sc[1] = gas_rate;
+        p.sc[2] = ddiv(dmul(dmul(dmul(tf, RHO_W), GRAV), v.d(L.pump_head)), s.pump_eff);
+    }
+    if (tid == 64) {
+        double total_occ = 0.0, cum = 0.0;
         for (int z = 0; z < nz; z++) {
             total_occ = dadd(total_occ, Vst[z]);
             cum = dadd(cum, p.zterm[z]);
+        }
+        p.sc[3] = total_occ;
+        p.sc[4] = cum;
+    }
+    if (tid == 96) {
+        double dsum = 0.0, dmax = 0.0;
+        int oob = 0;
+        for (int z = 0; z < nz; z++) {
             const double dev = p.zdev[z];
             dsum = dadd(dsum, dev);
             if (dev > dmax) dmax = dev;
             if (dev > 0.0) oob++;
         }
+        p.sc[5] = dsum;
+        p.sc[6] = dmax;
+        p.sc[7] = (double)oob;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        const int hour = (int)s.r_hour[j], month = (int)s.r_month[j], wd = (int)s.r_wd[j];
+        double intake = 0.0, exhaust = 0.0, cooling = 0.0;
+        for (int a = 0; a < na; a++) {
+            intake = dadd(intake, p.ahu[a]);
+            exhaust = dadd(exhaust, p.ahu[kMaxAhu + a]);
+            cooling = dadd(cooling, p.ahu[2 * kMaxAhu + a]);
+        }
+        const double blower = dadd(intake, exhaust);
+        const double gas_rate = p.sc[1], pump_e = p.sc[2], total_occ = p.sc[3], cum = p.sc[4];
+        const double dsum = p.sc[5], dmax = p.sc[6];
+        const int oob = (int)p.sc[7];
         const double max_prod = dmul(dmul(dmul(max_pph, total_occ), dt), inv_hour);
         const double min_prod = dmul(dmul(dmul(min_pph, total_occ), dt), inv_hour);
         const double npr = (total_occ > 0.0 && dsub(max_prod, min_prod) != 0.0)
@@ -387,6 +464,56 @@ __global__ void __launch_bounds__(128) k_post(const StepCtx* __restrict__ ctx) {
                     ctx->V_zero + (size_t)ei.scn * ctx->nz_max);
     } else {
         for (int z = tid; z < nz; z += blockDim.x) v.d(L.V, z) = Vst[z];
+    }
+}
+
+// One env's visible state packed for a snapshot file (the reference's SBS1
+// writer, complete_port/gpu/smart_buildings.cu:2205-2290), in doubles:
+// field [ncv] in cell order, zone means, occupancy, zone flow setpoint and
+// actual [nz each], VAV heating / cooling setpoints, damper, reheat [nv each],
+// AHU supply temperature, flow, run [na each], native actions [nact], then
+// step, boiler setpoint, boiler return.
+__host__ __device__ constexpr size_t snap_doubles(int ncv, int nz, int nv, int na, int nact) {
+    return (size_t)ncv + 4 * (size_t)nz + 4 * (size_t)nv + 3 * (size_t)na + (size_t)nact + 3;
+}
+__global__ void __launch_bounds__(128) k_snapshot(const StepCtx* __restrict__ ctx, int env, double* __restrict__ out) {
+    const EnvIndex ei = ctx->envs[env];
+    const GroupDev& g = ctx->groups[ei.group];
+    const ScnDev& s = ctx->scns[ei.scn];
+    const StateLayout& L = ctx->lay;
+    EnvView v{ctx->Dst + (size_t)env * L.nd, ctx->Ist + (size_t)env * L.ni, &ctx->lay};
+    const int tid = threadIdx.x, nz = s.nz, nv = s.nv, na = s.na;
+    const double* Tg = g.T + (size_t)(env - g.env0) * g.ncv;
+    double* o = out;
+    for (int c = tid; c < g.ncv; c += blockDim.x) o[c] = Tg[g.pos_of_cell[c]];
+    o += g.ncv;
+    for (int z = tid; z < nz; z += blockDim.x) {
+        o[z] = v.d(L.zavg, z);
+        o[nz + z] = v.d(L.V, z);
+        o[2 * nz + z] = v.d(L.zfsp, z);
+        o[3 * nz + z] = v.d(L.zfact, z);
+    }
+    o += 4 * nz;
+    for (int q = tid; q < nv; q += blockDim.x) {
+        o[q] = v.d(L.v_hsp, q);
+        o[nv + q] = v.d(L.v_csp, q);
+        o[2 * nv + q] = v.d(L.v_damp, q);
+        o[3 * nv + q] = v.d(L.v_reh, q);
+    }
+    o += 4 * nv;
+    for (int a = tid; a < na; a += blockDim.x) {
+        o[a] = v.d(L.ahu_sat, a);
+        o[na + a] = v.d(L.ahu_flow, a);
+        o[2 * na + a] = (double)v.iv(L.ahu_run, a);
+    }
+    o += 3 * na;
+    const float* act = ctx->actions + (size_t)env * kAct;
+    for (int i = tid; i < s.nact; i += blockDim.x) o[i] = decode_native(s, i, act);
+    o += s.nact;
+    if (tid == 0) {
+        o[0] = (double)v.iv(L.step);
+        o[1] = v.d(L.b_sp);
+        o[2] = v.d(L.b_ret);
     }
 }
 

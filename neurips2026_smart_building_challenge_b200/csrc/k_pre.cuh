@@ -73,6 +73,42 @@ __device__ inline double reheat_energy(const EnvView& v, const ScnDev& s, int vv
     return dmul(dmul(dmul(dmul(eff, CP_AIR), RHO_AIR), vd), dsub(iwt, sat));
 }
 
+// Block-wide copy of n elements, eight loads in flight per thread before the stores.
+template <class T>
+__device__ inline void block_copy(T* __restrict__ dst, const T* __restrict__ src, int n) {
+    const int nt = (int)blockDim.x;
+    int base = 0;
+    for (; base + 8 * nt <= n; base += 8 * nt) {
+        T v[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) v[u] = src[base + u * nt + (int)threadIdx.x];
+#pragma unroll
+        for (int u = 0; u < 8; u++) dst[base + u * nt + (int)threadIdx.x] = v[u];
+    }
+    for (int i = base + (int)threadIdx.x; i < n; i += nt) dst[i] = src[i];
+}
+
+// Native value of action i from the framework's actions of one env
+// (pufferlib_cpu_env.h:218-234, sb_sim.c:557-576): continuous slots clamped to
+// [-1, 1] and mapped in float, discrete slots (+1 iff the action is 1.0) in double.
+__device__ inline double decode_native(const ScnDev& s, int i, const float* act) {
+    const int slot = s.a_slot[i];   // position in the packed continuous / discrete block
+    if (s.a_disc[i]) {
+        const double dv = (double)act[kCont + slot];
+        const double merged = dv == 1.0 ? 1.0 : -1.0;
+        return dadd(dmul(ddiv(dsub(merged, s.a_mnr[i]), dsub(s.a_mxr[i], s.a_mnr[i])), dsub(s.a_mx[i], s.a_mn[i])),
+                    s.a_mn[i]);
+    }
+    double a = (double)act[slot];
+    a = a > 1.0 ? 1.0 : (a < -1.0 ? -1.0 : a);
+    const float m = (float)a;
+    const float span_in = (float)dsub(s.a_mxr[i], s.a_mnr[i]);
+    const float span_out = (float)dsub(s.a_mx[i], s.a_mn[i]);
+    const float r =
+        __fadd_rn(__fmul_rn(__fdiv_rn(__fsub_rn(m, (float)s.a_mnr[i]), span_in), span_out), (float)s.a_mn[i]);
+    return (double)r;
+}
+
 // Field-averaged zone temperatures (sb_sim.c:149-160) from an extended-order
 // field in global memory: one thread per zone, cells fetched eight at a time,
 // summed in the reference's order.
@@ -131,8 +167,8 @@ __global__ void __launch_bounds__(128) k_pre(const StepCtx* __restrict__ ctx) {
     int32_t* Ig = ctx->Ist + (size_t)env * L.ni;
     double* Ds = reinterpret_cast<double*>(smem);          // [nd]
     int32_t* Is = reinterpret_cast<int32_t*>(Ds + L.nd);   // [ni]
-    for (int i = tid; i < L.nd; i += blockDim.x) Ds[i] = Dg[i];
-    for (int i = tid; i < L.ni; i += blockDim.x) Is[i] = Ig[i];
+    block_copy(Ds, Dg, L.nd);
+    block_copy(Is, Ig, L.ni);
     EnvView v{Ds, Is, &ctx->lay};
     double* zavg = reinterpret_cast<double*>(Is + L.ni);   // [nz] (ni is a multiple of 4)
     double* zq = zavg + nz;                           // [nz]
@@ -151,24 +187,7 @@ __global__ void __launch_bounds__(128) k_pre(const StepCtx* __restrict__ ctx) {
     // Actuator targets are unique per blob (checked on the host), so actions apply in parallel.
     const float* act = ctx->actions + (size_t)env * kAct;
     for (int i = tid; i < s.nact; i += blockDim.x) {
-        const uint8_t dsc = s.a_disc[i];
-        const int slot = s.a_slot[i];   // position in the packed continuous / discrete block
-        double val;
-        if (dsc) {
-            const double dv = (double)act[kCont + slot];
-            const double merged = dv == 1.0 ? 1.0 : -1.0;
-            val = dadd(dmul(ddiv(dsub(merged, s.a_mnr[i]), dsub(s.a_mxr[i], s.a_mnr[i])),
-                            dsub(s.a_mx[i], s.a_mn[i])), s.a_mn[i]);
-        } else {
-            double a = (double)act[slot];
-            a = a > 1.0 ? 1.0 : (a < -1.0 ? -1.0 : a);
-            const float m = (float)a;
-            const float span_in = (float)dsub(s.a_mxr[i], s.a_mnr[i]);
-            const float span_out = (float)dsub(s.a_mx[i], s.a_mn[i]);
-            const float r = __fadd_rn(__fmul_rn(__fdiv_rn(__fsub_rn(m, (float)s.a_mnr[i]), span_in), span_out),
-                                      (float)s.a_mn[i]);
-            val = (double)r;
-        }
+        const double val = decode_native(s, i, act);
         const int idx = s.a_idx[i], ac = s.a_act[i];
         if (s.a_kind[i] == 0) {
             if (ac == 0) v.d(L.ahu_sat, idx) = val;
@@ -187,11 +206,12 @@ __global__ void __launch_bounds__(128) k_pre(const StepCtx* __restrict__ ctx) {
             else { const int on = val == 1.0 ? 1 : 0; v.iv(L.hws_run) = on; v.iv(L.pump_run) = on; }
         }
     }
-    // ---- zone means from the field ----
+    // ---- zone means of the field: the previous k_post (or the reset) computed
+    // them from this same field (sb_sim.c:149-160) and left them in the state ----
     const double* Tg = g.T + (size_t)(env - g.env0) * g.ncv;
     __syncthreads();
     if (tid == 0) v.iv(L.hws_req) = nv;
-    zone_means(g, s, Tg, zavg);
+    for (int z = tid; z < nz; z += blockDim.x) zavg[z] = v.d(L.zavg, z);
     __syncthreads();
     // ---- VAV sensing, thermostat, damper/reheat (sb_sim.c:368-384, :316-355) ----
     for (int vv = tid; vv < nv; vv += blockDim.x) {
@@ -227,7 +247,32 @@ __global__ void __launch_bounds__(128) k_pre(const StepCtx* __restrict__ ctx) {
     }
     __syncthreads();
     // ---- ordered accumulations (sb_sim.c:367-392) ----
-    if (tid == 0) {
+    if (!s.tmean_needed) {
+        // every AHU sees VAV area (checked on the host): one thread per AHU sums
+        // its VAVs in ascending order, one thread the reheat flow factor
+        if (tid < na) {
+            const int a = tid;
+            double ws = 0.0, at = 0.0;
+            for (int q = s.av_off[a]; q < s.av_off[a + 1]; q++) {
+                const int vv = s.av_idx[q];
+                const double area = v.d(L.v_area, vv);
+                if (area <= 0.0) continue;
+                ws = dadd(ws, dmul(v.d(L.v_sense, vv), area));
+                at = dadd(at, area);
+            }
+            const double recirc = ddiv(ws, at);
+            const double rec = v.d(L.ahu_rec, a);
+            const double mixed = dadd(dmul(rec, recirc), dmul(dsub(1.0, rec), ambient));
+            sv[a] = (mixed > v.d(L.ahu_sat, a) && v.iv(L.ahu_run, a) == 1) ? v.d(L.ahu_sat, a) : mixed;
+            v.d(L.ahu_flow, a) = 0.0;
+            v.iv(L.ahu_creq, a) = 0;
+        }
+        if (tid == 64) {
+            double ff = 0.0;
+            for (int vv = 0; vv < nv; vv++) ff = dadd(ff, dmul(v.d(L.v_reh, vv), s.vav_c[vv * 9 + 1]));
+            v.d(L.ff_sum) = ff;
+        }
+    } else if (tid == 0) {
         double ws[kMaxAhu], at[kMaxAhu];
         for (int a = 0; a < na; a++) { ws[a] = 0.0; at[a] = 0.0; }
         for (int vv = 0; vv < nv; vv++) {
@@ -258,8 +303,11 @@ __global__ void __launch_bounds__(128) k_pre(const StepCtx* __restrict__ ctx) {
     __syncthreads();
     for (int vv = tid; vv < nv; vv += blockDim.x) unr[vv] = vav_unrestricted(v, s, vv);
     __syncthreads();
-    if (tid == 0)
-        for (int vv = 0; vv < nv; vv++) demand[s.v_ahu[vv]] = dadd(demand[s.v_ahu[vv]], unr[vv]);
+    if (tid < na) {   // each AHU's demand over its VAVs, ascending
+        double d = 0.0;
+        for (int q = s.av_off[tid]; q < s.av_off[tid + 1]; q++) d = dadd(d, unr[s.av_idx[q]]);
+        demand[tid] = d;
+    }
     __syncthreads();
     for (int vv = tid; vv < nv; vv += blockDim.x) {
         const int a = s.v_ahu[vv];
@@ -294,30 +342,44 @@ __global__ void __launch_bounds__(128) k_pre(const StepCtx* __restrict__ ctx) {
         v.d(L.ag, col) = flows ? dmul(dmul(vd, RHO_AIR), CP_AIR) : 0.0;
     }
     __syncthreads();
-    // ... and their order-dependent sums on one thread
-    if (tid == 0) {
-        double rsum = 0.0;
-        for (int col = 0; col < k; col++) {
+    // ... and their order-dependent sums: each zone's heat over its columns,
+    // each AHU's flow over its columns, the reheat total over all columns, each
+    // on one thread in ascending column order
+    for (int z = tid; z < nz; z += blockDim.x) {
+        double q = zq[z];
+        for (int e = s.zc_off[z]; e < s.zc_off[z + 1]; e++) {
+            const int col = s.zc_col[e];
             const int vv = s.coupled[col];
             const double area = v.d(L.v_area, vv);
-            if (area <= 0.0) continue;
-            const int a = s.v_ahu[vv];
-            rsum = dadd(rsum, rw[col]);
-            if (v.d(L.v_damp, vv) > 0.0 && s.vav_c[vv * 9] > 0.0)
-                for (int t = s.vz_off[vv]; t < s.vz_off[vv + 1]; t++) {
-                    const int z = s.vz_idx[t];
-                    zq[z] = dadd(zq[z], ddiv(dmul(rw[col], s.zarea[z]), area));
-                }
+            if (area <= 0.0 || !(v.d(L.v_damp, vv) > 0.0 && s.vav_c[vv * 9] > 0.0)) continue;
+            q = dadd(q, ddiv(dmul(rw[col], s.zarea[z]), area));
+        }
+        zq[z] = q;
+    }
+    const int last = (int)blockDim.x - 1;
+    if (tid == last) {
+        double rsum = 0.0;
+        for (int col = 0; col < k; col++)
+            if (v.d(L.v_area, s.coupled[col]) > 0.0) rsum = dadd(rsum, rw[col]);
+        v.d(L.reheat_w) = rsum;
+    }
+    if (tid < last && tid >= last - na) {
+        const int a = last - 1 - tid;
+        const double mf = s.ahu_c[a * 9 + 1];
+        double f = v.d(L.ahu_flow, a);
+        int creq = v.iv(L.ahu_creq, a);
+        for (int e = s.ac_off[a]; e < s.ac_off[a + 1]; e++) {
+            const int col = s.ac_col[e];
+            if (v.d(L.v_area, s.coupled[col]) <= 0.0) continue;
             const double fd = fdv[col];
             if (fd > 0.0) {
-                double f = dadd(v.d(L.ahu_flow, a), fd);
-                const double mf = s.ahu_c[a * 9 + 1];
+                f = dadd(f, fd);
                 if (f > mf) f = mf;
-                v.d(L.ahu_flow, a) = f;
-                v.iv(L.ahu_creq, a) += 1;
+                creq += 1;
             }
         }
-        v.d(L.reheat_w) = rsum;
+        v.d(L.ahu_flow, a) = f;
+        v.iv(L.ahu_creq, a) = creq;
     }
     __syncthreads();
     // ---- internal + occupant gains, per-cell applied heat (sb_sim.c:438-455) ----

@@ -119,6 +119,17 @@ struct StageRing {
     }
 };
 
+// L2 prefetch of [p, p + bytes) in 4 KB bulk requests spread over `workers`
+// threads (the tail below a 16-byte multiple is left out).
+__device__ __forceinline__ void prefetch_l2(const uint8_t* p, uint32_t bytes, uint32_t worker, uint32_t workers) {
+    constexpr uint32_t kChunk = 4096;
+    bytes &= ~15u;
+    for (uint32_t off = worker * kChunk; off < bytes; off += workers * kChunk) {
+        const uint32_t len = min(kChunk, bytes - off);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p + off), "r"(len) : "memory");
+    }
+}
+
 // L1 prefetch of the 128-byte lines of [p, p + bytes): one line per lane.
 __device__ __forceinline__ void prefetch_lines(const uint8_t* p, uint32_t bytes, int lane) {
     const uintptr_t l0 = reinterpret_cast<uintptr_t>(p) >> 7;
@@ -519,6 +530,12 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
     const int B = g.slab_envs, S = g.stride, n = g.n, ncv = g.ncv, k = g.k;
     const int nenv = sd.nenv;
     const int tid = threadIdx.x;
+    // the group's first slab pulls its sweep programs into L2 ahead of every
+    // slab's ring copies (the programs are shared by all slabs of the group)
+    if (sd.env0 == g.env0) {
+        prefetch_l2(g.fwd.stream, g.fwd.total_bytes, tid, blockDim.x);
+        prefetch_l2(g.bwd.stream, g.bwd.total_bytes, tid, blockDim.x);
+    }
 
     // shared memory: field [B][S] | rings | ready flags | misc (solve_smem_bytes)
     const int R = (int)g.fwd.ring_stages;

@@ -194,6 +194,7 @@ struct GroupDev {
     const double* St;               // its transpose (column j of S contiguous)
     // rooms: cells of each room in extended positions
     const int32_t *room_off, *room_pos;
+    int room_cells;                 // room_off[rooms]: cells in rooms, at most ncv
     const int32_t* cell_of_pos;     // extended position -> cell index (field mean order)
     const int32_t* pos_of_cell;
     // convection (room-local candidate lists in convection-cell numbering)
@@ -222,6 +223,10 @@ struct ScnDev {
     const uint8_t *o_wd, *r_wd;
     const double *ahu_c, *vav_c, *zarea;
     const int32_t *vz_off, *vz_idx, *v_ahu, *coupled, *zv_off, *zv_idx, *proom, *room_ncell;
+    // ascending lists: coupled columns per zone (zc), coupled columns per AHU
+    // (ac), VAVs per AHU (av) -- one thread per zone / AHU accumulates in the
+    // reference's loop order
+    const int32_t *zc_off, *zc_col, *ac_off, *ac_col, *av_off, *av_idx;
     const uint8_t *a_kind, *a_act, *a_disc;
     const int32_t *a_idx, *a_slot;
     const double *a_mn, *a_mx, *a_mnr, *a_mxr;
@@ -245,6 +250,8 @@ struct StateLayout {
     int ahu_rec, ahu_sat, ahu_fan, ahu_flow;
     int v_damp, v_reh, v_ratio, v_hsp, v_csp, v_dcmd, v_rcmd, v_sense, v_area;
     int qdiv, ag, aT, coil, V;   // step transients / occupancy
+    int zavg;                    // zone means of the field as the last step (or reset) left it
+    int zfsp, zfact;             // zone flow setpoint / actual of the last reward (snapshots)
     int ff_sum, pump_head, b_sp, b_ret, b_cur, b_step, reheat_w;
     int ahu_run, ahu_creq, v_mode, v_prev, v_dset, v_rset;
     int hws_req, hws_run, pump_run, step, gen, active;

@@ -120,6 +120,8 @@ std::string build_group(const sbb::Reader& b, HostGroup& g) {
     NEED(grid, "grid");
     const int nr = (int)grid[0], nc = (int)grid[1];
     g.ncv = nr * nc;
+    g.rows = nr;
+    g.cols = nc;
     const int64_t* solved = b.i64("solved");
     NEED(solved, "solved");
     Factor F;
@@ -185,6 +187,7 @@ std::string build_group(const sbb::Reader& b, HostGroup& g) {
     const int nrooms = (int)b.count("room_offsets") - 1;
     g.room_off = vec(room_off, (uint64_t)nrooms + 1);
     if ((uint64_t)2 * room_off[nrooms] > b.count("room_cells")) return "room_cells shorter than room_offsets";
+    if (room_off[nrooms] > g.ncv) return "more room cells than grid cells";
     g.room_pos.resize(room_off[nrooms]);
     for (int t = 0; t < room_off[nrooms]; t++) {
         const int r = room_cells[2 * t], c = room_cells[2 * t + 1];
@@ -335,6 +338,29 @@ std::string build_scenario(const sbb::Reader& b, const HostGroup& g, int max_ste
         if (c < 0 || c >= s.nv) return "coupled_vav_idx out of range";
     for (int z : s.vz_idx)
         if (z < 0 || z >= s.nz) return "vav_zone_idx out of range";
+    // per-zone coupled columns, per-AHU coupled columns and VAVs, ascending: the
+    // device accumulates each zone's and each AHU's sums on one thread in the
+    // order of the reference's single loops (sb_sim.c:367-392, :408-436)
+    {
+        std::vector<std::vector<int32_t>> zl(s.nz), al(s.na), vl(s.na);
+        for (int col = 0; col < s.k; col++) {
+            const int v = s.coupled[col];
+            for (int t = s.vz_off[v]; t < s.vz_off[v + 1]; t++) zl[s.vz_idx[t]].push_back(col);
+            al[s.v_ahu[v]].push_back(col);
+        }
+        for (int v = 0; v < s.nv; v++) vl[s.v_ahu[v]].push_back(v);
+        auto flat = [](const std::vector<std::vector<int32_t>>& ls, std::vector<int32_t>& off, std::vector<int32_t>& idx) {
+            off.assign(1, 0);
+            idx.clear();
+            for (const auto& l : ls) {
+                idx.insert(idx.end(), l.begin(), l.end());
+                off.push_back((int32_t)idx.size());
+            }
+        };
+        flat(zl, s.zc_off, s.zc_col);
+        flat(al, s.ac_off, s.ac_col);
+        flat(vl, s.av_off, s.av_idx);
+    }
     s.room_ncell.resize(s.nz);
     for (int z = 0; z < s.nz; z++) s.room_ncell[z] = g.room_off[s.proom[z] + 1] - g.room_off[s.proom[z]];
     // static: does some AHU see no VAV area (then the field mean feeds its recirculation)?

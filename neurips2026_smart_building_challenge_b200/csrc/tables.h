@@ -12,6 +12,7 @@ namespace sbenv {
 
 struct HostGroup {
     int n = 0, ncv = 0, k = 0, nz = 0, nv = 0, na = 0;
+    int rows = 0, cols = 0;   // the thermal grid
     int64_t nnzL = 0, nnzU = 0;
     std::vector<double> cap, dirx, mc, ret, gain;   // row order
     std::vector<int32_t> zone_of_row;
@@ -40,6 +41,7 @@ struct HostScn {
     std::vector<uint8_t> o_wd, r_wd;
     std::vector<double> ahu_c, vav_c, zarea;
     std::vector<int32_t> vz_off, vz_idx, v_ahu, coupled, zv_off, zv_idx, proom, room_ncell;
+    std::vector<int32_t> zc_off, zc_col, ac_off, ac_col, av_off, av_idx;   // per-zone / per-AHU ascending lists
     std::vector<uint8_t> a_kind, a_act, a_disc;
     std::vector<int32_t> a_idx, a_slot;
     std::vector<double> a_mn, a_mx, a_mnr, a_mxr;

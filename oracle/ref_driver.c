@@ -162,3 +162,4 @@ void sbo_reseed(SboEnv* e) {
 }
 
 int sbo_debug(const SboEnv* e, double* out) { (void)e; (void)out; return -1; }
+int sbo_visible(const SboEnv* e, double* out) { (void)e; (void)out; return -1; }

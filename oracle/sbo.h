@@ -53,6 +53,8 @@ void sbo_reseed(SboEnv* e);
 /* Inspection (restatement only): out = [air_g k][air_T k][per-cell zone heat nz]
  * [flow factor sum, reheat W, boiler T, boiler return, pump head] of the last step. */
 int sbo_debug(const SboEnv* e, double* out);
+/* Visible state after the last step (the snapshot fields); -1 where not exported. */
+int sbo_visible(const SboEnv* e, double* out);
 
 #ifdef __cplusplus
 }

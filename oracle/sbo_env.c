@@ -96,3 +96,31 @@ int sbo_debug(const SboEnv* e, double* out) {
     out[o++] = st->pump_head;
     return o;
 }
+
+/* One env's visible state after the last step, in the layout of the library's
+ * snapshot staging: field [ncv] in cell order, zone means, occupancy, zone flow
+ * setpoint and flow [nz each], VAV heating / cooling setpoints, damper, reheat
+ * [nv each], AHU supply temperature, flow, run [na each], native actions [nact],
+ * then step, boiler setpoint, boiler return. Returns the number of doubles. */
+int sbo_visible(const SboEnv* e, double* out) {
+    const SboScn* s = &e->scn;
+    const SboState* st = &e->st;
+    int o = 0;
+    for (int c = 0; c < s->ncv; c++) out[o++] = st->temp[c];
+    for (int z = 0; z < s->nz; z++) out[o++] = st->zavg[z];
+    for (int z = 0; z < s->nz; z++) out[o++] = st->V[z];
+    for (int z = 0; z < s->nz; z++) out[o++] = st->zfsp[z];
+    for (int z = 0; z < s->nz; z++) out[o++] = st->zfact[z];
+    for (int v = 0; v < s->nv; v++) out[o++] = st->v_hsp[v];
+    for (int v = 0; v < s->nv; v++) out[o++] = st->v_csp[v];
+    for (int v = 0; v < s->nv; v++) out[o++] = st->v_damp[v];
+    for (int v = 0; v < s->nv; v++) out[o++] = st->v_reh[v];
+    for (int a = 0; a < s->na; a++) out[o++] = st->ahu_sat[a];
+    for (int a = 0; a < s->na; a++) out[o++] = st->ahu_flow[a];
+    for (int a = 0; a < s->na; a++) out[o++] = (double)st->ahu_run[a];
+    for (int i = 0; i < s->nact; i++) out[o++] = st->native[i];
+    out[o++] = (double)e->st.step;
+    out[o++] = st->b_sp;
+    out[o++] = st->b_ret;
+    return o;
+}

@@ -25,7 +25,7 @@ def lib(path: Path) -> ctypes.CDLL:
         l.sbo_create.restype = ctypes.c_void_p
         l.sbo_create.argtypes = [ctypes.c_char_p, ctypes.c_int]
         for fn in ["sbo_destroy", "sbo_dims", "sbo_reset", "sbo_step", "sbo_get_temp", "sbo_get_mass",
-                   "sbo_step_index", "sbo_reseed"]:
+                   "sbo_step_index", "sbo_reseed", "sbo_visible"]:
             getattr(l, fn).argtypes = None
         _cache[key] = l
     return _cache[key]
@@ -69,6 +69,14 @@ class OracleEnv:
     def mass(self) -> np.ndarray:
         out = np.zeros(self.n)
         self.l.sbo_get_mass(self.h, _p(out))
+        return out
+
+    def visible(self) -> np.ndarray:
+        """Snapshot fields after the last step (oracle/sbo_env.c sbo_visible)."""
+        out = np.zeros(self.ncv + 4 * self.nz + 4 * self.nv + 3 * self.na + self.nact + 3)
+        self.l.sbo_visible.restype = ctypes.c_int
+        if self.l.sbo_visible(self.h, _p(out)) != len(out):
+            raise RuntimeError("this oracle build does not export the visible state")
         return out
 
     def close(self):

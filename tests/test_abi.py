@@ -112,3 +112,17 @@ def test_sampler_rejects_bad_arguments(built):
     assert lib.sb_beta_actions(p, None, p, 4, 0.0, 12.0, 0, p) == -1       # floor must be > 0
     assert lib.sb_beta_actions(p, None, p, 4, 1.0, 1.5, 0, p) == -1        # cap must exceed 2 floor
     assert b"sb_beta_actions" in lib.sb_last_error()
+
+
+def test_snapshot_reader_rejects_bad_records():
+    from neurips2026_smart_building_challenge_b200.sbs import parse_snapshot
+
+    with pytest.raises(ValueError):
+        parse_snapshot(b"XXXX" + bytes(700))
+    import struct
+    hdr = b"SBS1" + struct.pack("<12i", 1, 3, 100, 0, 1, 1, 1, 2, 2, 4, 1, 0) + struct.pack("<12d", *range(12))
+    body = hdr + b"blob".ljust(512, b"\0") + bytes(4 * 4 + 8 * (4 + 4 + 2) + 4 + 8)
+    snap = parse_snapshot(body)
+    assert snap["step"] == 3 and snap["blob"] == "blob" and snap["field"].shape == (2, 2)
+    with pytest.raises(ValueError):
+        parse_snapshot(body[:-1])
