@@ -618,6 +618,23 @@ bool do_reset(Engine& E) {
 
 }  // namespace
 
+// Fixed device scratch of sb_dense_solve_noalloc: the column-major working copy
+// of the systems, for callers that cannot allocate device memory. Every GPU
+// that loads this library holds it (4 MiB) until the process exits.
+constexpr size_t kDenseNoAllocDoubles = size_t(1) << 19;   // n * k * k at most
+static __device__ __align__(256) double g_dense_scratch[kDenseNoAllocDoubles];
+constexpr int kNoAllocDevices = 64;
+
+// m row-major [n][k][k] -> mt column-major per system (element (i, j) at j * k + i)
+__global__ void __launch_bounds__(256) k_dense_transpose(int k, int n, const double* __restrict__ m,
+                                                         double* __restrict__ mt) {
+    const size_t kk = (size_t)k * k, total = kk * (size_t)n;
+    for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (size_t)gridDim.x * blockDim.x) {
+        const size_t sys = idx / kk, r = idx % kk, i = r / k, j = r % k;
+        mt[sys * kk + j * k + i] = m[idx];
+    }
+}
+
 // ============================== C ABI ==============================
 
 extern "C" {
@@ -936,6 +953,51 @@ int sb_dense_check(int k, int n, const double* m_rowmajor, const double* b, doub
     }
     cudaFree(dm); cudaFree(db); cudaFree(dout);
     if (!ok) { set_err("sb_dense_check: CUDA error"); return -1; }
+    return 0;
+}
+
+int sb_dense_solve_noalloc(int k, int n, const double* m_rowmajor, const double* b, double* out) {
+    if (k < 1 || k > kMaxK || n < 1 || !m_rowmajor || !b || !out) {
+        set_err("sb_dense_solve_noalloc: bad arguments");
+        return -1;
+    }
+    const size_t need = (size_t)n * k * k;
+    if (need > kDenseNoAllocDoubles) {
+        set_err("sb_dense_solve_noalloc: n * k * k = %zu exceeds the fixed scratch of %zu doubles", need,
+                kDenseNoAllocDoubles);
+        return -1;
+    }
+    // once per device, with that device current: the scratch array's device
+    // address (in host code its name is only a stand-in) and the kernel's
+    // shared-memory limit
+    static double* scratch[kNoAllocDevices] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocDevices) {
+        set_err("sb_dense_solve_noalloc: no usable current device");
+        return -1;
+    }
+    if (!scratch[dev]) {
+        double* ptr = nullptr;
+        if (cudaGetSymbolAddress((void**)&ptr, g_dense_scratch) != cudaSuccess || !ptr) {
+            set_err("sb_dense_solve_noalloc: cudaGetSymbolAddress failed");
+            return -1;
+        }
+        if (cudaFuncSetAttribute(k_dense_check, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)(dense_smem_doubles(kMaxK) * sizeof(double))) != cudaSuccess) {
+            set_err("sb_dense_solve_noalloc: shared-memory attribute refused");
+            return -1;
+        }
+        scratch[dev] = ptr;
+    }
+    cudaStream_t st = (g_eng && g_eng->ready) ? g_eng->stream : (cudaStream_t)0;
+    const unsigned tb = (unsigned)std::min<size_t>((need + 255) / 256, 148 * 8);
+    k_dense_transpose<<<tb, 256, 0, st>>>(k, n, m_rowmajor, scratch[dev]);
+    const size_t smem = std::max<size_t>(16, dense_smem_doubles(k) * sizeof(double));
+    k_dense_check<<<(unsigned)n, (unsigned)dense_threads(k), smem, st>>>(k, scratch[dev], b, out);
+    if (cudaGetLastError() != cudaSuccess) {
+        set_err("sb_dense_solve_noalloc: launch failed");
+        return -1;
+    }
     return 0;
 }
 
