@@ -113,20 +113,25 @@ __device__ inline void reset_state(const EnvView& v, const ScnDev& s) {
     }
 }
 
-// Shared-memory layout of k_post / k_reset: field, staging, zone scratch.
+// Shared-memory layout of k_post / k_reset: the env's state blocks (k_post
+// works on a copy and writes it back), staging, zone scratch.
 struct PostShared {
-    double *T, *stage, *zavg, *zterm, *zdev, *vws, *varea;
+    double* D;
+    int32_t* I;
+    double *stage, *zavg, *zterm, *zdev, *vws, *varea;
     double* ahu;   // [3][kMaxAhu] per-AHU reward terms: intake, exhaust, cooling
     double* sc;    // [kPostScalars] reward scalars handed to the final thread
 };
 constexpr int kPostScalars = 10;
-__host__ __device__ constexpr size_t post_smem_doubles(int ncv, int nz, int nv) {
-    return 2 * (size_t)ncv + 3 * (size_t)nz + 2 * (size_t)nv + 3 * kMaxAhu + kPostScalars;
+// nd doubles and ni ints of state (ni a multiple of 4), then the rest
+__host__ __device__ constexpr size_t post_smem_doubles(int ncv, int nz, int nv, int nd, int ni) {
+    return (size_t)nd + (size_t)ni / 2 + (size_t)ncv + 3 * (size_t)nz + 2 * (size_t)nv + 3 * kMaxAhu + kPostScalars;
 }
-__device__ inline PostShared post_shared(uint8_t* smem, int ncv, int nz, int nv) {
+__device__ inline PostShared post_shared(uint8_t* smem, int ncv, int nz, int nv, int nd, int ni) {
     PostShared p;
-    p.T = reinterpret_cast<double*>(smem);
-    p.stage = p.T + ncv;
+    p.D = reinterpret_cast<double*>(smem);
+    p.I = reinterpret_cast<int32_t*>(p.D + nd);
+    p.stage = reinterpret_cast<double*>(p.I + ni);
     p.zavg = p.stage + ncv;
     p.zterm = p.zavg + nz;
     p.zdev = p.zterm + nz;
@@ -146,10 +151,10 @@ __device__ inline void restart_env(const StepCtx* ctx, int env, const GroupDev& 
     reset_state(v, s);
     double* Tg = g.T + (size_t)local * g.ncv;
     double* Mg = g.M + (size_t)local * g.n;
-    for (int i = threadIdx.x; i < g.ncv; i += blockDim.x) { p.T[i] = s.temp_init[i]; Tg[i] = s.temp_init[i]; }
-    for (int i = threadIdx.x; i < g.n; i += blockDim.x) Mg[i] = s.mass_init[i];
+    block_copy(Tg, s.temp_init, g.ncv);
+    block_copy(Mg, s.mass_init, g.n);
     __syncthreads();
-    zone_means(g, s, p.T, p.zavg);
+    zone_means(g, s, s.temp_init, p.zavg);
     __syncthreads();
     vav_sensing(s, p.zavg, v.D + L.v_area, v.D + L.v_sense);
     for (int z = threadIdx.x; z < s.nz; z += blockDim.x) v.d(L.zavg, z) = p.zavg[z];
@@ -167,24 +172,23 @@ __global__ void __launch_bounds__(128) k_post(const StepCtx* __restrict__ ctx) {
     const GroupDev& g = ctx->groups[ei.group];
     const ScnDev& s = ctx->scns[ei.scn];
     const StateLayout& L = ctx->lay;
-    EnvView v{ctx->Dst + (size_t)env * L.nd, ctx->Ist + (size_t)env * L.ni, &ctx->lay};
     const int tid = threadIdx.x;
     const int nz = s.nz, nv = s.nv, na = s.na, k = s.k;
-    PostShared p = post_shared(smem, g.ncv, nz, nv);
+    PostShared p = post_shared(smem, g.ncv, nz, nv, L.nd, L.ni);
+    double* Dg = ctx->Dst + (size_t)env * L.nd;
+    int32_t* Ig = ctx->Ist + (size_t)env * L.ni;
+    block_copy(p.D, (const double*)Dg, L.nd);
+    block_copy(p.I, (const int32_t*)Ig, L.ni);
+    EnvView v{p.D, p.I, &ctx->lay};
     const int local = env - g.env0;
     double* Tg = g.T + (size_t)local * g.ncv;
 
-    // ---- convection (sb_sim.c:489): apply this step's permutation ----
-    block_copy(p.T, (const double*)Tg, g.ncv);
-    __syncthreads();
+    // ---- convection (sb_sim.c:489): apply this step's permutation to the
+    // field in global memory, the moved values staged first ----
     const int npairs = *s.conv_npairs;
-    for (int q = tid; q < npairs; q += blockDim.x) p.stage[q] = p.T[s.conv_pairs[2 * q + 1]];
+    for (int q = tid; q < npairs; q += blockDim.x) p.stage[q] = Tg[s.conv_pairs[2 * q + 1]];
     __syncthreads();
-    for (int q = tid; q < npairs; q += blockDim.x) {
-        const int dst = s.conv_pairs[2 * q];
-        p.T[dst] = p.stage[q];
-        Tg[dst] = p.stage[q];
-    }
+    for (int q = tid; q < npairs; q += blockDim.x) Tg[s.conv_pairs[2 * q]] = p.stage[q];
     // ---- boiler return and setpoint ramp (sb_sim.c:491-521) ----
     const int kk = v.iv(L.step);
     if (tid == 0) {
@@ -231,7 +235,7 @@ __global__ void __launch_bounds__(128) k_post(const StepCtx* __restrict__ ctx) {
     // ---- reward (sb_reward.c:31-155) ----
     // zone means (sb_sim.c:149-160): the field copied into room order (p.stage
     // is free after the convection), then one thread per zone sums its cells
-    for (int t = tid; t < g.room_cells; t += blockDim.x) p.stage[t] = p.T[g.room_pos[t]];
+    block_gather(p.stage, Tg, g.room_pos, g.room_cells);
     __syncthreads();
     for (int z = tid; z < nz; z += blockDim.x) {
         const int rm = s.proom[z];
@@ -289,7 +293,7 @@ __global__ void __launch_bounds__(128) k_post(const StepCtx* __restrict__ ctx) {
     }
     if (tid == 0 && s.tmean_needed) {   // the field mean, for an AHU without VAV area
         double tmean = 0.0;
-        for (int q = 0; q < g.ncv; q++) tmean = dadd(tmean, p.T[g.pos_of_cell[q]]);
+        for (int q = 0; q < g.ncv; q++) tmean = dadd(tmean, Tg[g.pos_of_cell[q]]);
         p.sc[0] = ddiv(tmean, (double)g.ncv);
     }
     __syncthreads();
@@ -464,7 +468,10 @@ __global__ void __launch_bounds__(128) k_post(const StepCtx* __restrict__ ctx) {
                     ctx->V_zero + (size_t)ei.scn * ctx->nz_max);
     } else {
         for (int z = tid; z < nz; z += blockDim.x) v.d(L.V, z) = Vst[z];
+        __syncthreads();
     }
+    block_copy(Dg, (const double*)p.D, L.nd);
+    block_copy(Ig, (const int32_t*)p.I, L.ni);
 }
 
 // One env's visible state packed for a snapshot file (the reference's SBS1
@@ -526,7 +533,7 @@ __global__ void __launch_bounds__(128) k_reset(const StepCtx* __restrict__ ctx) 
     const ScnDev& s = ctx->scns[ei.scn];
     const StateLayout& L = ctx->lay;
     EnvView v{ctx->Dst + (size_t)env * L.nd, ctx->Ist + (size_t)env * L.ni, &ctx->lay};
-    PostShared p = post_shared(smem, g.ncv, s.nz, s.nv);
+    PostShared p = post_shared(smem, g.ncv, s.nz, s.nv, L.nd, L.ni);
     float* o = ctx->obs + (size_t)env * kObs;
     for (int i = threadIdx.x; i < kObs; i += blockDim.x) o[i] = 0.0f;
     if (threadIdx.x == 0) {
