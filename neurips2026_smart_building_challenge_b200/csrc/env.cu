@@ -110,6 +110,8 @@ struct Engine {
     cudaEvent_t ev_fork = nullptr, ev_join = nullptr, ev_solve = nullptr;
     size_t smem_solve = 0, smem_pre = 0, smem_post = 0, smem_rng = 0, smem_dense = 0;
     int dense_threads = 32;          // k_dense block (dense_threads(k_max))
+    struct DenseClass { int first, count, k; };
+    std::vector<DenseClass> dense_cls;   // runs of equal k in dense_order, heaviest first
     int max_ncv = 0;
     double* d_snap = nullptr;     // snapshot staging (k_snapshot), sized for the largest scenario
     bool ready = false;
@@ -208,6 +210,30 @@ cudaError_t launch_rng_after_solve(Engine& E, cudaStream_t st, int reset_only) {
     return cudaLaunchKernelEx(&cfg, k_rng, (const StepCtx*)E.d_ctx, E.d_scn_step, E.d_rng_out, reset_only);
 }
 
+// The dense air-side solves: one launch per class of equal k with its own
+// block and shared-memory size; every class after the first is a programmatic
+// dependent of the one before (it may start once that one's CTAs are resident,
+// and its CTAs wait for that one's completion before they exit).
+cudaError_t launch_dense(Engine& E, cudaStream_t st) {
+    for (size_t c = 0; c < E.dense_cls.size(); c++) {
+        const Engine::DenseClass& d = E.dense_cls[c];
+        const size_t smem = std::max<size_t>(16, dense_smem_doubles(d.k) * sizeof(double));
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)d.count);
+        cfg.blockDim = dim3((unsigned)dense_threads(d.k));
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = c == 0 ? 0 : 1;
+        const cudaError_t e = cudaLaunchKernelEx(&cfg, k_dense, (const StepCtx*)E.d_ctx, d.first);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
 // The solve on the high-priority stream: phase 0 (first L/U solve), the
 // random streams as its programmatic dependent, the dense air-side solves,
 // phase 1 (second L/U solve, mass, field).
@@ -217,7 +243,8 @@ cudaError_t launch_solve(Engine& E) {
     cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess) e = launch_rng_after_solve(E, E.hi, 0);
     if (e != cudaSuccess) return e;
-    k_dense<<<(unsigned)E.n_env, (unsigned)E.dense_threads, E.smem_dense, E.hi>>>(E.d_ctx);
+    e = launch_dense(E, E.hi);
+    if (e != cudaSuccess) return e;
     k_solve<1><<<slabs, kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
     return cudaGetLastError();
 }
@@ -520,6 +547,13 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
             return E.hs[E.ei[a].scn].k > E.hs[E.ei[b].scn].k;
         });
         C.dense_order = E.arena.upload(order, ok);
+        for (int i = 0; i < n;) {
+            const int k = E.hs[E.ei[order[i]].scn].k;
+            int j = i;
+            while (j < n && E.hs[E.ei[order[j]].scn].k == k) j++;
+            if (k > 0) E.dense_cls.push_back({i, j - i, k});
+            i = j;
+        }
     }
     E.smem_dense = std::max<size_t>(16, dense_smem_doubles(k_max) * sizeof(double));
     E.dense_threads = dense_threads(std::max(k_max, 1));
@@ -862,7 +896,7 @@ void sb_shape(int* out) {
         out[5] = std::max(out[5], s.n_disc);
     }
     out[6] = (int)E.slabs.size();
-    out[7] = 6;
+    out[7] = 5 + (int)E.dense_cls.size();
 }
 
 void sb_env_info(int* obs_len, int* scenario) {
@@ -916,7 +950,7 @@ int sb_get_reward_f64(double* reward, double* parts) {
     return 0;
 }
 
-int sb_kernels_per_step(void) { return 6; }
+int sb_kernels_per_step(void) { return 5 + (g_eng ? (int)g_eng->dense_cls.size() : 1); }
 
 int sb_beta_actions(const float* raw, const unsigned char* mask, float* actions, int n, float floor_c, float cap,
                     unsigned long long seed, const unsigned long long* call) {
@@ -1086,7 +1120,7 @@ int sb_step_timed(float* ms) {
     k_solve<0><<<slabs, kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
     launch_rng_after_solve(E, E.hi, 0);
     cudaEventRecord(ev[4], E.hi);
-    k_dense<<<(unsigned)E.n_env, (unsigned)E.dense_threads, E.smem_dense, E.hi>>>(E.d_ctx);
+    launch_dense(E, E.hi);
     cudaEventRecord(ev[5], E.hi);
     k_solve<1><<<slabs, kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
     cudaEventRecord(ev[2], E.hi);

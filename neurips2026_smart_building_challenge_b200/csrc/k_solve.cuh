@@ -472,10 +472,12 @@ __device__ inline void dense_team(double* M, int k, int ttid, int T, int bar) {
 // the right side ctx->airq as column k, solved by dense_team; the solution
 // replaces the right side in ctx->airq. Envs whose VAV gains are all zero
 // (or whose building couples no VAV) have no air side and return at once.
-// Launched with dense_threads(k_max) threads per CTA.
-__global__ void __launch_bounds__(kMaxK) k_dense(const StepCtx* __restrict__ ctx) {
+// One launch per class of equal k (heaviest class first), each sized for its k;
+// the classes after the first are programmatic dependents of the one before,
+// so they share the SMs, and each CTA waits for the previous class to complete
+// before it exits: the last class completes after all of them.
+__device__ inline void dense_env(const StepCtx* __restrict__ ctx, int env) {
     extern __shared__ __align__(16) double dsm[];
-    const int env = ctx->dense_order[blockIdx.x];
     const ScnDev& sc = ctx->scns[ctx->envs[env].scn];
     const GroupDev& g = ctx->groups[sc.group];
     const StateLayout& L = ctx->lay;
@@ -496,6 +498,12 @@ __global__ void __launch_bounds__(kMaxK) k_dense(const StepCtx* __restrict__ ctx
     if (tid < T) dense_team(dsm, k, tid, T, 1);
     __syncthreads();
     for (int i = tid; i < k; i += blockDim.x) q[i] = dsm[per + kDenseRed + i];
+}
+
+__global__ void __launch_bounds__(kMaxK) k_dense(const StepCtx* __restrict__ ctx, int first) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    dense_env(ctx, ctx->dense_order[first + blockIdx.x]);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 // Test entry of the dense solver: n systems of size k, Mt [n][k][k] the

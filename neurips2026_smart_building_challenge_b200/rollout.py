@@ -9,7 +9,7 @@ cap follow the reference trainer (patches/pufferlib_core.diff:2490-2580,
 config/smart_buildings.ini beta_floor = 1, beta_conc_max = 12 in the run this
 configuration names).
 
-One env+policy step (the policy's GEMMs, the sampler, the env's six kernels and
+One env+policy step (the policy's GEMMs, the sampler, the env's kernels and
 the draw counter's increment) is captured in a CUDA graph on the env's bound
 stream and replayed over the rollout horizon, as the reference trainer captures
 its rollout step.
