@@ -436,7 +436,7 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
         E.max_ncv = std::max(E.max_ncv, h.ncv);
         E.smem_pre = std::max(E.smem_pre, sizeof(double) * (size_t)(L.nd + 2 * nz_max + nv_max + 2 * na_max + 2 * k_max) +
                                               sizeof(int32_t) * (size_t)L.ni);
-        E.smem_post = std::max(E.smem_post, sizeof(double) * post_smem_doubles(h.ncv, nz_max, nv_max, L.nd, L.ni));
+        E.smem_post = std::max(E.smem_post, sizeof(double) * post_smem_doubles(h.ncv, nz_max, nv_max));
         const size_t rng_b = 4 * (size_t)(624 + 624 + 1248) + 4 * (4 * (size_t)h.cv_off.back() + 1 + h.cv_off.size());
         E.smem_rng = std::max(E.smem_rng, rng_b);
     }

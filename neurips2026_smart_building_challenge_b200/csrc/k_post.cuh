@@ -113,25 +113,21 @@ __device__ inline void reset_state(const EnvView& v, const ScnDev& s) {
     }
 }
 
-// Shared-memory layout of k_post / k_reset: the env's state blocks (k_post
-// works on a copy and writes it back), staging, zone scratch.
+// Shared-memory layout of k_post / k_reset: staging, zone scratch. Kept small
+// (the state and the field stay in global memory) so that seven 128-thread
+// CTAs fit on an SM and every env's CTA is resident in one wave.
 struct PostShared {
-    double* D;
-    int32_t* I;
     double *stage, *zavg, *zterm, *zdev, *vws, *varea;
     double* ahu;   // [3][kMaxAhu] per-AHU reward terms: intake, exhaust, cooling
     double* sc;    // [kPostScalars] reward scalars handed to the final thread
 };
 constexpr int kPostScalars = 10;
-// nd doubles and ni ints of state (ni a multiple of 4), then the rest
-__host__ __device__ constexpr size_t post_smem_doubles(int ncv, int nz, int nv, int nd, int ni) {
-    return (size_t)nd + (size_t)ni / 2 + (size_t)ncv + 3 * (size_t)nz + 2 * (size_t)nv + 3 * kMaxAhu + kPostScalars;
+__host__ __device__ constexpr size_t post_smem_doubles(int ncv, int nz, int nv) {
+    return (size_t)ncv + 3 * (size_t)nz + 2 * (size_t)nv + 3 * kMaxAhu + kPostScalars;
 }
-__device__ inline PostShared post_shared(uint8_t* smem, int ncv, int nz, int nv, int nd, int ni) {
+__device__ inline PostShared post_shared(uint8_t* smem, int ncv, int nz, int nv) {
     PostShared p;
-    p.D = reinterpret_cast<double*>(smem);
-    p.I = reinterpret_cast<int32_t*>(p.D + nd);
-    p.stage = reinterpret_cast<double*>(p.I + ni);
+    p.stage = reinterpret_cast<double*>(smem);
     p.zavg = p.stage + ncv;
     p.zterm = p.zavg + nz;
     p.zdev = p.zterm + nz;
@@ -174,12 +170,8 @@ __global__ void __launch_bounds__(128) k_post(const StepCtx* __restrict__ ctx) {
     const StateLayout& L = ctx->lay;
     const int tid = threadIdx.x;
     const int nz = s.nz, nv = s.nv, na = s.na, k = s.k;
-    PostShared p = post_shared(smem, g.ncv, nz, nv, L.nd, L.ni);
-    double* Dg = ctx->Dst + (size_t)env * L.nd;
-    int32_t* Ig = ctx->Ist + (size_t)env * L.ni;
-    block_copy(p.D, (const double*)Dg, L.nd);
-    block_copy(p.I, (const int32_t*)Ig, L.ni);
-    EnvView v{p.D, p.I, &ctx->lay};
+    PostShared p = post_shared(smem, g.ncv, nz, nv);
+    EnvView v{ctx->Dst + (size_t)env * L.nd, ctx->Ist + (size_t)env * L.ni, &ctx->lay};
     const int local = env - g.env0;
     double* Tg = g.T + (size_t)local * g.ncv;
 
@@ -468,10 +460,7 @@ __global__ void __launch_bounds__(128) k_post(const StepCtx* __restrict__ ctx) {
                     ctx->V_zero + (size_t)ei.scn * ctx->nz_max);
     } else {
         for (int z = tid; z < nz; z += blockDim.x) v.d(L.V, z) = Vst[z];
-        __syncthreads();
     }
-    block_copy(Dg, (const double*)p.D, L.nd);
-    block_copy(Ig, (const int32_t*)p.I, L.ni);
 }
 
 // One env's visible state packed for a snapshot file (the reference's SBS1
@@ -533,7 +522,7 @@ __global__ void __launch_bounds__(128) k_reset(const StepCtx* __restrict__ ctx) 
     const ScnDev& s = ctx->scns[ei.scn];
     const StateLayout& L = ctx->lay;
     EnvView v{ctx->Dst + (size_t)env * L.nd, ctx->Ist + (size_t)env * L.ni, &ctx->lay};
-    PostShared p = post_shared(smem, g.ncv, s.nz, s.nv, L.nd, L.ni);
+    PostShared p = post_shared(smem, g.ncv, s.nz, s.nv);
     float* o = ctx->obs + (size_t)env * kObs;
     for (int i = threadIdx.x; i < kObs; i += blockDim.x) o[i] = 0.0f;
     if (threadIdx.x == 0) {
