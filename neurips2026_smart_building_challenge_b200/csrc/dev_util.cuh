@@ -74,6 +74,39 @@ __device__ __forceinline__ void st_release_u8(uint8_t* p, uint32_t v) {
     asm volatile("st.release.cta.shared::cta.u8 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
 }
 
+// Block-wide copy of n elements, eight loads in flight per thread before the stores.
+template <class T>
+__device__ inline void block_copy(T* __restrict__ dst, const T* __restrict__ src, int n) {
+    const int nt = (int)blockDim.x;
+    int base = 0;
+    for (; base + 8 * nt <= n; base += 8 * nt) {
+        T v[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) v[u] = src[base + u * nt + (int)threadIdx.x];
+#pragma unroll
+        for (int u = 0; u < 8; u++) dst[base + u * nt + (int)threadIdx.x] = v[u];
+    }
+    for (int i = base + (int)threadIdx.x; i < n; i += nt) dst[i] = src[i];
+}
+
+// Block-wide gather dst[t] = src[idx[t]], eight loads in flight per thread.
+__device__ inline void block_gather(double* __restrict__ dst, const double* __restrict__ src,
+                                    const int32_t* __restrict__ idx, int n) {
+    const int nt = (int)blockDim.x;
+    int base = 0;
+    for (; base + 8 * nt <= n; base += 8 * nt) {
+        int ix[8];
+        double v[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) ix[u] = idx[base + u * nt + (int)threadIdx.x];
+#pragma unroll
+        for (int u = 0; u < 8; u++) v[u] = src[ix[u]];
+#pragma unroll
+        for (int u = 0; u < 8; u++) dst[base + u * nt + (int)threadIdx.x] = v[u];
+    }
+    for (int i = base + (int)threadIdx.x; i < n; i += nt) dst[i] = src[idx[i]];
+}
+
 __device__ __forceinline__ void set_error(int* status, int code) {
     if (status) atomicCAS(status, 0, code);
 }

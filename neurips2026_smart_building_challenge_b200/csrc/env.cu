@@ -417,6 +417,8 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
         gd.sn_x = E.arena.upload(h.sn_x, ok);
         gd.ap_rp = E.arena.upload(h.ap_rp, ok); gd.ap_col = E.arena.upload(h.ap_col, ok);
         gd.ap_x = E.arena.upload(h.ap_x, ok); gd.S = E.arena.upload(h.S, ok);
+        gd.sn_nnz = (int)h.sn_x.size();
+        gd.ap_nnz = (int)h.ap_x.size();
         {
             std::vector<double> st(h.S.size());
             for (int i = 0; i < h.k; i++)

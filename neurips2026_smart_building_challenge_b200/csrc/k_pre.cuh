@@ -73,39 +73,6 @@ __device__ inline double reheat_energy(const EnvView& v, const ScnDev& s, int vv
     return dmul(dmul(dmul(dmul(eff, CP_AIR), RHO_AIR), vd), dsub(iwt, sat));
 }
 
-// Block-wide copy of n elements, eight loads in flight per thread before the stores.
-template <class T>
-__device__ inline void block_copy(T* __restrict__ dst, const T* __restrict__ src, int n) {
-    const int nt = (int)blockDim.x;
-    int base = 0;
-    for (; base + 8 * nt <= n; base += 8 * nt) {
-        T v[8];
-#pragma unroll
-        for (int u = 0; u < 8; u++) v[u] = src[base + u * nt + (int)threadIdx.x];
-#pragma unroll
-        for (int u = 0; u < 8; u++) dst[base + u * nt + (int)threadIdx.x] = v[u];
-    }
-    for (int i = base + (int)threadIdx.x; i < n; i += nt) dst[i] = src[i];
-}
-
-// Block-wide gather dst[t] = src[idx[t]], eight loads in flight per thread.
-__device__ inline void block_gather(double* __restrict__ dst, const double* __restrict__ src,
-                                    const int32_t* __restrict__ idx, int n) {
-    const int nt = (int)blockDim.x;
-    int base = 0;
-    for (; base + 8 * nt <= n; base += 8 * nt) {
-        int ix[8];
-        double v[8];
-#pragma unroll
-        for (int u = 0; u < 8; u++) ix[u] = idx[base + u * nt + (int)threadIdx.x];
-#pragma unroll
-        for (int u = 0; u < 8; u++) v[u] = src[ix[u]];
-#pragma unroll
-        for (int u = 0; u < 8; u++) dst[base + u * nt + (int)threadIdx.x] = v[u];
-    }
-    for (int i = base + (int)threadIdx.x; i < n; i += nt) dst[i] = src[idx[i]];
-}
-
 // Native value of action i from the framework's actions of one env
 // (pufferlib_cpu_env.h:218-234, sb_sim.c:557-576): continuous slots clamped to
 // [-1, 1] and mapped in float, discrete slots (+1 iff the action is 1.0) in double.

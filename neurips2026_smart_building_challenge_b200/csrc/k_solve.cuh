@@ -543,6 +543,14 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
     if (sd.env0 == g.env0) {
         prefetch_l2(g.fwd.stream, g.fwd.total_bytes, tid, blockDim.x);
         prefetch_l2(g.bwd.stream, g.bwd.total_bytes, tid, blockDim.x);
+        // and the tables the phase reads after its sweeps
+        if (Phase == 0) {
+            prefetch_l2(reinterpret_cast<const uint8_t*>(g.sn_x), (uint32_t)g.sn_nnz * 8u, tid, blockDim.x);
+            prefetch_l2(reinterpret_cast<const uint8_t*>(g.sn_pos), (uint32_t)g.sn_nnz * 4u, tid, blockDim.x);
+        } else {
+            prefetch_l2(reinterpret_cast<const uint8_t*>(g.ret), (uint32_t)g.n * 8u, tid, blockDim.x);
+            prefetch_l2(reinterpret_cast<const uint8_t*>(g.gain), (uint32_t)g.n * 8u, tid, blockDim.x);
+        }
     }
 
     // shared memory: field [B][S] | rings | ready flags | misc (solve_smem_bytes)
@@ -618,6 +626,20 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
 
         // ---- air side (sb_fdm.c:155-181): the sensed right side to ctx->airq ----
         if (k > 0 && any_active) {
+            // the sensed terms staged in the (now idle) ring memory when they fit
+            const size_t ring_bytes = (size_t)kSweepWarps * R * kStageBytes;
+            const bool staged = (size_t)g.sn_nnz * 12 <= ring_bytes;
+            const double* snx = g.sn_x;
+            const int32_t* snp = g.sn_pos;
+            if (staged) {
+                double* sx = reinterpret_cast<double*>(sh.ring);
+                int32_t* sp = reinterpret_cast<int32_t*>(sh.ring + (size_t)g.sn_nnz * 8);
+                block_copy(sx, g.sn_x, g.sn_nnz);
+                block_copy(sp, g.sn_pos, g.sn_nnz);
+                snx = sx;
+                snp = sp;
+            }
+            __syncthreads();
             // sensed temperature of each coupled VAV: one thread per VAV for all
             // envs, its terms fetched eight at a time, summed in order per env
             for (int i = tid; i < k; i += blockDim.x) {
@@ -630,8 +652,8 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
                     int pos[8];
 #pragma unroll
                     for (int u = 0; u < 8; u++) {
-                        xv[u] = p + u < p1 ? g.sn_x[p + u] : 0.0;
-                        pos[u] = p + u < p1 ? g.sn_pos[p + u] : 0;
+                        xv[u] = p + u < p1 ? snx[p + u] : 0.0;
+                        pos[u] = p + u < p1 ? snp[p + u] : 0;
                     }
 #pragma unroll
                     for (int u = 0; u < 8; u++) {

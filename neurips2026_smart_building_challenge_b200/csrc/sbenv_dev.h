@@ -187,6 +187,7 @@ struct GroupDev {
     Sweep fwd, bwd;
     // air side in row positions
     const int32_t *sn_p, *sn_pos;   // sensed CSR, k rows
+    int sn_nnz, ap_nnz;             // sensed / applied term counts
     const double* sn_x;
     const int32_t *ap_rp, *ap_col;  // applied by row position, coupled columns ascending
     const double* ap_x;
