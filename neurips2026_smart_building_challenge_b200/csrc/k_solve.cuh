@@ -592,6 +592,16 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
         // ---- forcing (sb_fdm.c:146-152), written in row order: one thread per
         // row for all envs of the slab, the row's coefficients loaded once ----
         const int local0 = sd.env0 - g.env0;
+        // the envs' per-zone heat staged in the (not yet used) ring memory, so
+        // the row loop below has no dependent global load
+        double* qz = reinterpret_cast<double*>(sh.ring);   // [nenv][nz]
+        const bool qstaged = (size_t)nenv * g.nz * sizeof(double) <= (size_t)kSweepWarps * R * kStageBytes;
+        if (qstaged)
+            for (int t = tid; t < nenv * g.nz; t += blockDim.x) {
+                const int e = t / g.nz, z = t - e * g.nz;
+                qz[t] = ctx->Dst[(size_t)(sd.env0 + e) * L.nd + L.qdiv + z];
+            }
+        __syncthreads();
         for (int i = tid; i < n; i += blockDim.x) {
             const double cap = g.cap[i], dirx = g.dirx[i], mc = g.mc[i];
             const int z = g.zone_of_row[i];
@@ -601,7 +611,11 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
                 if (e >= nenv) break;
                 Ti[e] = g.T[(size_t)(local0 + e) * ncv + i];
                 Mi[e] = g.M[(size_t)(local0 + e) * n + i];
-                qi[e] = z >= 0 ? ctx->Dst[(size_t)(sd.env0 + e) * L.nd + L.qdiv + z] : 0.0;
+            }
+#pragma unroll
+            for (int e = 0; e < kGroupLanes; e++) {
+                if (e >= nenv) break;
+                qi[e] = z < 0 ? 0.0 : qstaged ? qz[e * g.nz + z] : ctx->Dst[(size_t)(sd.env0 + e) * L.nd + L.qdiv + z];
             }
 #pragma unroll
             for (int e = 0; e < kGroupLanes; e++) {
