@@ -699,7 +699,18 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
     // ascending column order, zero q skipped; one thread per row for all envs ----
     const int local0 = sd.env0 - g.env0;
     if (k > 0 && any_active) {
-        const double* q = ctx->airq;
+        // the slab's dense solutions staged in the (not yet used) ring memory
+        double* qs = reinterpret_cast<double*>(sh.ring);   // [nenv][k]
+        const bool qstaged = (size_t)nenv * k * sizeof(double) <= (size_t)kSweepWarps * R * kStageBytes;
+        if (qstaged)
+            for (int t = tid; t < nenv * k; t += blockDim.x) {
+                const int e = t / k, c = t - e * k;
+                qs[t] = ctx->airq[(size_t)(sd.env0 + e) * ctx->k_max + c];
+            }
+        __syncthreads();
+        const double* q = qstaged ? qs : ctx->airq;
+        const size_t qstride = qstaged ? (size_t)k : (size_t)ctx->k_max;
+        const size_t qbase = qstaged ? 0 : (size_t)sd.env0 * ctx->k_max;
         for (int i = tid; i < n; i += blockDim.x) {
             double acc[kGroupLanes];
 #pragma unroll
@@ -711,7 +722,7 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
 #pragma unroll
                 for (int e = 0; e < kGroupLanes; e++) {
                     if (e >= nenv) break;
-                    const double qj = q[(size_t)(sd.env0 + e) * ctx->k_max + col];
+                    const double qj = q[qbase + (size_t)e * qstride + col];
                     if (active[e] && qj != 0.0) acc[e] = dadd(acc[e], dmul(xv, qj));
                 }
             }
