@@ -180,3 +180,43 @@ def test_mask_and_shapes(scenario_cache):
             assert not obs[e, env.obs_len[e]:].any()
     finally:
         env.close()
+
+
+def test_config2_full_batch_sample(scenario_cache):
+    """The bench configuration itself (960 envs, slabs of 6-7 envs, six dense classes):
+    a sample of envs spread over the batch against the oracle, bit for bit."""
+    import torch
+
+    from neurips2026_smart_building_challenge_b200 import config_dir
+
+    d = config_dir(2, scenario_cache, n_steps=400)
+    n, steps = 960, 6
+    sample = [0, 1, 31, 159, 160, 479, 481, 700, 959]
+    env = _vec(n, d, groups=30)
+    try:
+        paths = _scenario_paths(env, d)
+        orc = {e: OracleEnv(paths[int(env.scenario[e])]) for e in sample}
+        env.reset()
+        env.synchronize()
+        obs = env.obs.cpu().numpy()
+        for e in sample:
+            o = orc[e].reset()
+            np.testing.assert_array_equal(obs[e].view(np.uint32), o.view(np.uint32), err_msg=f"reset env {e}")
+        rng = np.random.default_rng(21)
+        for s in range(steps):
+            a = np.zeros((n, 272), np.float32)
+            a[:, :256] = 2.0 * rng.beta(2.0, 2.0, size=(n, 256)) - 1.0
+            a[:, 256:] = (rng.random((n, 16)) < 0.9).astype(np.float32)
+            env.step(torch.from_numpy(a).to(env.device))
+            env.synchronize()
+            obs = env.obs.cpu().numpy()
+            rd, _ = env.reward_f64()
+            for e in sample:
+                o, _, _, r64, _, _ = orc[e].step(a[e])
+                assert np.array_equal(obs[e].view(np.uint32), o.view(np.uint32)), f"step {s} env {e}"
+                assert rd[e] == r64, f"step {s} env {e} reward"
+        for e in sample:
+            assert not (env.temp(e, orc[e].ncv) - orc[e].temp()).any(), f"field env {e}"
+        assert env.status() == 0
+    finally:
+        env.close()
