@@ -348,16 +348,21 @@ __device__ inline void run_sweep(const SolveShared& sh, const Sweep& sw, int B, 
 constexpr int kDenseRed = 32;
 __host__ __device__ constexpr size_t dense_env_doubles(int k) { return (size_t)k * (k + 1) + kDenseRed + (size_t)k; }
 __host__ __device__ constexpr size_t dense_smem_doubles(int k) { return dense_env_doubles(k); }
-__host__ __device__ constexpr int dense_threads(int k) { return 32 * ((k + 31) / 32); }
+// Above kDenseHelperK rows every row owner has a helper thread (the second half
+// of the team) that takes half of the row's deferred column updates.
+constexpr int kDenseHelperK = 48;
+__host__ __device__ constexpr int dense_threads(int k) {
+    return (k > kDenseHelperK ? 64 : 32) * ((k + 31) / 32);
+}
 
 __device__ inline void team_sync(int bar, int T) {
     asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(T) : "memory");
 }
 
-// M[j][p] -= f * M[j][pr] for columns j0 .. k (eight at a time, loads first)
-__device__ __forceinline__ void dense_update(double* M, int k, int p, int pr, double f, int j0) {
+// M[j][p] -= f * M[j][pr] for columns j0 .. j1 (eight at a time, loads first)
+__device__ __forceinline__ void dense_update(double* M, int k, int p, int pr, double f, int j0, int j1) {
     int j = j0;
-    for (; j + 8 <= k + 1; j += 8) {
+    for (; j + 8 <= j1 + 1; j += 8) {
         double a[8], q[8];
 #pragma unroll
         for (int u = 0; u < 8; u++) {
@@ -367,24 +372,27 @@ __device__ __forceinline__ void dense_update(double* M, int k, int p, int pr, do
 #pragma unroll
         for (int u = 0; u < 8; u++) M[(size_t)(j + u) * k + p] = dsub(a[u], dmul(f, q[u]));
     }
-    for (; j <= k; j++) M[(size_t)j * k + p] = dsub(M[(size_t)j * k + p], dmul(f, M[(size_t)j * k + pr]));
+    for (; j <= j1; j++) M[(size_t)j * k + p] = dsub(M[(size_t)j * k + p], dmul(f, M[(size_t)j * k + pr]));
 }
 
 __device__ inline void dense_team(double* M, int k, int ttid, int T, int bar) {
     const unsigned full = 0xffffffffu;
-    const int lane = ttid & 31, tw = ttid >> 5, W = T >> 5;
+    const int Tr = 32 * ((k + 31) / 32);   // row owners; threads Tr .. T-1 (if any) are their helpers
+    const bool helped = T > Tr, helper = ttid >= Tr;
+    const int rid = helper ? ttid - Tr : ttid;
+    const int lane = rid & 31, tw = rid >> 5, W = Tr >> 5;
     double* red = M + (size_t)k * (k + 1);
     double* z = red + kDenseRed;
-    const bool has_row = ttid < k;
-    const int p = has_row ? ttid : 0;
-    int mypos = ttid;
+    const bool has_row = rid < k;
+    const int p = has_row ? rid : 0;
+    int mypos = rid;
     bool stopped = false;
-    double cv = has_row ? M[p] : 0.0;   // this row's value in the current column
+    double cv = has_row && !helper ? M[p] : 0.0;   // the owner's value of its row in the current column
     double fr = 0.0;                    // the previous step's multiplier (0: nothing pending)
     int prow = 0;                       // the previous step's pivot row
     for (int c = 0; c < k; c++) {
         double* sl = red + (c & 1) * 16;
-        // publish: the diagonal, and the warp's best candidate below it
+        if (!helper) {   // publish: the diagonal, and the warp's best candidate below it
         const double av = fabs(cv);
         const uint64_t pat = (has_row && mypos > c && av == av) ? (uint64_t)__double_as_longlong(av) + 1ull : 0ull;
         if (has_row && mypos == c) {
@@ -402,8 +410,14 @@ __device__ inline void dense_team(double* M, int k, int ttid, int T, int bar) {
             sl[3 + 3 * tw] = (double)mkey;
         }
         if (top && key == mkey) sl[4 + 3 * tw] = cv;
-        // the rest of the previous step's update
-        if (fr != 0.0) dense_update(M, k, p, prow, fr, c + 1);
+        }
+        // the rest of the previous step's update (columns c + 1 .. k), split
+        // between the owner and its helper when there is one
+        if (fr != 0.0) {
+            const int mid = helped ? c + 1 + (k - c) / 2 : k + 1;
+            if (!helper) dense_update(M, k, p, prow, fr, c + 1, mid - 1);
+            else dense_update(M, k, p, prow, fr, mid, k);
+        }
         team_sync(bar, T);
         // the pivot: the best candidate if strictly larger than the diagonal
         const double dv = sl[0];
@@ -425,7 +439,15 @@ __device__ inline void dense_team(double* M, int k, int ttid, int T, int bar) {
         else if (mypos == piv) mypos = c;
         // this step's multiplier; column c + 1 now (the next candidate), the rest later
         fr = 0.0;
-        if (has_row && mypos > c) {
+        if (helper) {   // the same multiplier from the same value (written before this step's barrier)
+            if (has_row && mypos > c) {
+                const double f = ddiv(M[(size_t)c * k + p], d);
+                if (f != 0.0) {
+                    fr = f;
+                    prow = pr;
+                }
+            }
+        } else if (has_row && mypos > c) {
             const double f = ddiv(cv, d);
             double* mc = M + (size_t)(c + 1) * k;
             if (f != 0.0) {
@@ -443,9 +465,9 @@ __device__ inline void dense_team(double* M, int k, int ttid, int T, int bar) {
     // the position subtracts its products in ascending column order
     if (!stopped) {
         for (int pos = k - 1; pos >= 0; pos--) {
-            if (has_row && mypos <= pos && pos + 1 < k)
+            if (!helper && has_row && mypos <= pos && pos + 1 < k)
                 M[(size_t)(pos + 1) * k + p] = dmul(M[(size_t)(pos + 1) * k + p], z[pos + 1]);
-            if (has_row && mypos == pos) {
+            if (!helper && has_row && mypos == pos) {
                 double s = M[(size_t)k * k + p];
                 int j = pos + 1;
                 for (; j + 8 <= k; j += 8) {
@@ -462,7 +484,7 @@ __device__ inline void dense_team(double* M, int k, int ttid, int T, int bar) {
         }
     } else {
         // the reference leaves b as eliminated so far (in swapped order)
-        if (has_row) z[mypos] = M[(size_t)k * k + p];
+        if (!helper && has_row) z[mypos] = M[(size_t)k * k + p];
     }
     team_sync(bar, T);
 }
@@ -500,7 +522,7 @@ __device__ inline void dense_env(const StepCtx* __restrict__ ctx, int env) {
     for (int i = tid; i < k; i += blockDim.x) q[i] = dsm[per + kDenseRed + i];
 }
 
-__global__ void __launch_bounds__(kMaxK) k_dense(const StepCtx* __restrict__ ctx, int first) {
+__global__ void __launch_bounds__(2 * kMaxK) k_dense(const StepCtx* __restrict__ ctx, int first) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     dense_env(ctx, ctx->dense_order[first + blockIdx.x]);
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -509,7 +531,7 @@ __global__ void __launch_bounds__(kMaxK) k_dense(const StepCtx* __restrict__ ctx
 // Test entry of the dense solver: n systems of size k, Mt [n][k][k] the
 // matrices transposed (column-major), b [n][k]; the solutions to out [n][k].
 // One CTA per system, dense_threads(k) threads, the path of k_dense.
-__global__ void __launch_bounds__(kMaxK) k_dense_check(int k, const double* __restrict__ Mt,
+__global__ void __launch_bounds__(2 * kMaxK) k_dense_check(int k, const double* __restrict__ Mt,
                                                        const double* __restrict__ b, double* __restrict__ out) {
     extern __shared__ __align__(16) double dsm[];
     const size_t sys = blockIdx.x;
