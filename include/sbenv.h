@@ -176,12 +176,14 @@ int sb_dense_check(int k, int n, const double* m_rowmajor, const double* b, doub
  * owns. The column-major working copy goes to one fixed device array of 2^19
  * doubles (4 MiB, held by every GPU that loads the library): n * k * k above
  * that is rejected with -1 and a message, as are k outside 1..128 and null
- * pointers. The first call on a device looks up that array's device address and
- * sets the kernel's shared-memory limit, so make it before any stream capture.
- * Enqueued on the bound stream (the default stream without an env batch) and
- * asynchronous; every call shares the array, so calls that overlap on the GPU
- * (other streams, other threads) race. Nothing in the array needs to start at
- * zero: each call overwrites the part it reads. 0 ok, -1 error (sb_last_error). */
+ * pointers. The first call on a device (of this entry point or of
+ * sb_dense_check) looks up that array's device address and sets the kernel's
+ * shared-memory limit for the largest k, under a lock, so host threads may make
+ * it at the same time; make it before any stream capture. Enqueued on the bound
+ * stream (the default stream without an env batch) and asynchronous; every call
+ * shares the array, so calls that overlap on the GPU (other streams, other
+ * threads) race. Nothing in the array needs to start at zero: each call
+ * overwrites the part it reads. 0 ok, -1 error (sb_last_error). */
 int sb_dense_solve_noalloc(int k, int n, const double* m_rowmajor, const double* b, double* out);
 /* Snapshot of one env's visible state to a file, the reference's headless
  * viewer feed (SBS1, smart_buildings.cu:2205-2290), after the last step:

@@ -75,9 +75,25 @@ def build_env(verbose: bool = False, force: bool = False) -> Path:
     return out
 
 
+def reference_csim_dir() -> Path | None:
+    """The reference's C core sources: $SB_REFERENCE_DIR/complete_port/csim, else a
+    checkout named `reference` beside this repository; None when neither exists
+    (then oracle/_ref keeps whatever was built before)."""
+    env = os.environ.get("SB_REFERENCE_DIR")
+    for base in ([Path(env)] if env else []) + [ROOT.parent / "reference"]:
+        d = base / "complete_port" / "csim"
+        if (d / "sb_sim.c").exists():
+            return d
+    return None
+
+
 def build_oracle(verbose: bool = False) -> None:
     """Builds the CPU checker (TEST INFRASTRUCTURE) under oracle/."""
-    _run(["make", "-s", "-C", str(ROOT / "oracle"), "all"], verbose)
+    cmd = ["make", "-s", "-C", str(ROOT / "oracle"), "all"]
+    ref = reference_csim_dir()
+    if ref is not None:
+        cmd.append(f"REF_DIR={ref}")
+    _run(cmd, verbose)
 
 
 def build_all(verbose: bool = False, force: bool = False) -> None:

@@ -25,6 +25,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -661,6 +662,38 @@ constexpr size_t kDenseNoAllocDoubles = size_t(1) << 19;   // n * k * k at most
 static __device__ __align__(256) double g_dense_scratch[kDenseNoAllocDoubles];
 constexpr int kNoAllocDevices = 64;
 
+// Once per device, with that device current, under one lock (host threads
+// may make their first calls at the same time): k_dense_check's shared-memory
+// limit is raised to the largest system (k = kMaxK) and never lowered again,
+// so sb_dense_check and sb_dense_solve_noalloc can follow one another with any
+// k; and the device address of g_dense_scratch is looked up (in host code the
+// array's name is only a stand-in for it). scratch may be null.
+static bool dense_check_setup(double** scratch) {
+    static std::mutex mu;
+    static double* addr[kNoAllocDevices] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocDevices) {
+        set_err("dense solve: no usable current device");
+        return false;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        double* ptr = nullptr;
+        if (cudaGetSymbolAddress((void**)&ptr, g_dense_scratch) != cudaSuccess || !ptr) {
+            set_err("dense solve: cudaGetSymbolAddress failed");
+            return false;
+        }
+        if (cudaFuncSetAttribute(k_dense_check, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)(dense_smem_doubles(kMaxK) * sizeof(double))) != cudaSuccess) {
+            set_err("dense solve: shared-memory attribute refused");
+            return false;
+        }
+        addr[dev] = ptr;
+    }
+    if (scratch) *scratch = addr[dev];
+    return true;
+}
+
 // m row-major [n][k][k] -> mt column-major per system (element (i, j) at j * k + i)
 __global__ void __launch_bounds__(256) k_dense_transpose(int k, int n, const double* __restrict__ m,
                                                          double* __restrict__ mt) {
@@ -977,11 +1010,11 @@ int sb_dense_check(int k, int n, const double* m_rowmajor, const double* b, doub
             for (int j = 0; j < k; j++) mt[s * kk + (size_t)j * k + i] = m_rowmajor[s * kk + (size_t)i * k + j];
     double *dm = nullptr, *db = nullptr, *dout = nullptr;
     const size_t smem = std::max<size_t>(16, dense_smem_doubles(k) * sizeof(double));
+    if (!dense_check_setup(nullptr)) return -1;
     bool ok = cudaMalloc(&dm, mt.size() * 8) == cudaSuccess && cudaMalloc(&db, (size_t)n * k * 8) == cudaSuccess &&
               cudaMalloc(&dout, (size_t)n * k * 8) == cudaSuccess;
     ok = ok && cudaMemcpy(dm, mt.data(), mt.size() * 8, cudaMemcpyHostToDevice) == cudaSuccess &&
-         cudaMemcpy(db, b, (size_t)n * k * 8, cudaMemcpyHostToDevice) == cudaSuccess &&
-         cudaFuncSetAttribute(k_dense_check, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) == cudaSuccess;
+         cudaMemcpy(db, b, (size_t)n * k * 8, cudaMemcpyHostToDevice) == cudaSuccess;
     if (ok) {
         k_dense_check<<<(unsigned)n, (unsigned)dense_threads(k), smem>>>(k, dm, db, dout);
         ok = cudaGetLastError() == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess &&
@@ -1003,33 +1036,13 @@ int sb_dense_solve_noalloc(int k, int n, const double* m_rowmajor, const double*
                 kDenseNoAllocDoubles);
         return -1;
     }
-    // once per device, with that device current: the scratch array's device
-    // address (in host code its name is only a stand-in) and the kernel's
-    // shared-memory limit
-    static double* scratch[kNoAllocDevices] = {};
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocDevices) {
-        set_err("sb_dense_solve_noalloc: no usable current device");
-        return -1;
-    }
-    if (!scratch[dev]) {
-        double* ptr = nullptr;
-        if (cudaGetSymbolAddress((void**)&ptr, g_dense_scratch) != cudaSuccess || !ptr) {
-            set_err("sb_dense_solve_noalloc: cudaGetSymbolAddress failed");
-            return -1;
-        }
-        if (cudaFuncSetAttribute(k_dense_check, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)(dense_smem_doubles(kMaxK) * sizeof(double))) != cudaSuccess) {
-            set_err("sb_dense_solve_noalloc: shared-memory attribute refused");
-            return -1;
-        }
-        scratch[dev] = ptr;
-    }
+    double* scratch = nullptr;
+    if (!dense_check_setup(&scratch)) return -1;
     cudaStream_t st = (g_eng && g_eng->ready) ? g_eng->stream : (cudaStream_t)0;
     const unsigned tb = (unsigned)std::min<size_t>((need + 255) / 256, 148 * 8);
-    k_dense_transpose<<<tb, 256, 0, st>>>(k, n, m_rowmajor, scratch[dev]);
+    k_dense_transpose<<<tb, 256, 0, st>>>(k, n, m_rowmajor, scratch);
     const size_t smem = std::max<size_t>(16, dense_smem_doubles(k) * sizeof(double));
-    k_dense_check<<<(unsigned)n, (unsigned)dense_threads(k), smem, st>>>(k, scratch[dev], b, out);
+    k_dense_check<<<(unsigned)n, (unsigned)dense_threads(k), smem, st>>>(k, scratch, b, out);
     if (cudaGetLastError() != cudaSuccess) {
         set_err("sb_dense_solve_noalloc: launch failed");
         return -1;

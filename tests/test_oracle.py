@@ -69,6 +69,54 @@ def test_port_matches_reference(built, tmp_path, config, index, over, steps, max
     np.testing.assert_array_equal(a_env.mass(), b_env.mass())
 
 
+def test_port_matches_reference_month_golden(built, tmp_path):
+    """The restatement through configuration 1's whole month (8,640 steps from
+    Monday 16 January: four weekends, the month roll, every occupancy window)
+    and into the next episode, against the digests recorded from the reference."""
+    from golden.make_golden import MONTH_HOUR, digest, month_actions, month_blob
+
+    g = np.load(GOLD / "ref_month.npz")
+    p = month_blob(tmp_path / "month.sbb")
+    assert hashlib.sha256(p.read_bytes()).hexdigest() == str(g["sha256"])
+    env = OracleEnv(p, path=PORT)
+    assert digest(env.reset()) == g["obs_digest"][0]
+    h = 0
+    for s, a in enumerate(month_actions(env.n_cont, env.n_disc)):
+        o, r, t, rd, _, _ = env.step(a)
+        assert digest(o) == g["obs_digest"][s + 1], f"obs step {s}"
+        assert rd == g["rew64"][s] and np.float32(r) == g["rew32"][s] and t == g["term"][s], f"reward step {s}"
+        if s % MONTH_HOUR == MONTH_HOUR - 1:
+            assert digest(env.temp()) == g["temp_digest"][h] and digest(env.mass()) == g["mass_digest"][h], s
+            h += 1
+    np.testing.assert_array_equal(env.temp(), g["temp_end"])
+    np.testing.assert_array_equal(env.mass(), g["mass_end"])
+
+
+@pytest.mark.skipif(not REF.exists(), reason="reference C core not built (reference tree absent)")
+@pytest.mark.parametrize("index", [0, 7, 14, 16, 23, 29])
+def test_port_matches_reference_weekend_span(built, tmp_path, index):
+    """Configuration-2 scenarios (every layout) from Friday 27 January 18:00 for
+    1,300 steps: the evening departure window, a weekend at the weekend tariff,
+    Monday's arrivals and departures, and the roll into February."""
+    from neurips2026_smart_building_challenge_b200 import preset, write_scenario
+
+    p = write_scenario(tmp_path / "s.sbb", preset(2, index, start_doy=26, start_hour=18, n_steps=1400))
+    a_env, b_env = OracleEnv(p, 0, PORT), OracleEnv(p, 0, REF)
+    np.testing.assert_array_equal(a_env.reset().view(np.uint32), b_env.reset().view(np.uint32))
+    rng = np.random.default_rng(100 + index)
+    al = rng.uniform(0.5, 12.0, size=a_env.n_cont)
+    be = rng.uniform(0.5, 12.0, size=a_env.n_cont)
+    for s in range(1300):
+        a = actions(rng, 1, a_env.n_cont, a_env.n_disc, alpha=al, beta=be)[0]
+        ra, rb = a_env.step(a), b_env.step(a)
+        np.testing.assert_array_equal(ra[0].view(np.uint32), rb[0].view(np.uint32), err_msg=f"obs {s}")
+        assert ra[1:4] == rb[1:4], s
+        np.testing.assert_array_equal(ra[4], rb[4])
+        if s % 12 == 11:
+            np.testing.assert_array_equal(a_env.temp(), b_env.temp())
+    np.testing.assert_array_equal(a_env.mass(), b_env.mass())
+
+
 class _Mt(ctypes.Structure):
     _fields_ = [("s", ctypes.c_uint32 * 624), ("pos", ctypes.c_int)]
 

@@ -13,7 +13,7 @@ import numpy as np
 import pytest
 
 from oracle_util import OracleEnv
-from test_env_gpu import _scenario_paths
+from parity_util import scenario_paths
 
 pytestmark = pytest.mark.gpu
 
@@ -140,7 +140,7 @@ def test_rollout_graph_parity(scenario_cache):
     n, steps = 12, 40
     env = SmartBuildingsVec(n, blob_dir=str(d))
     try:
-        paths = _scenario_paths(env, d)
+        paths = scenario_paths(d)
         orc = [OracleEnv(paths[int(env.scenario[e])]) for e in range(n)]
         env.reset()
         for o in orc:

@@ -14,7 +14,7 @@ import numpy as np
 import pytest
 
 from oracle_util import OracleEnv, actions
-from test_env_gpu import _scenario_paths
+from parity_util import scenario_paths
 
 pytestmark = pytest.mark.gpu
 
@@ -49,7 +49,7 @@ def test_snapshot_matches_oracle(scenario_cache, tmp_path):
     n = 8
     env = SmartBuildingsVec(n, blob_dir=str(d), groups=30)
     try:
-        paths = _scenario_paths(env, d)
+        paths = scenario_paths(d)
         orc = [OracleEnv(paths[int(env.scenario[e])]) for e in range(n)]
         env.reset()
         for o in orc:

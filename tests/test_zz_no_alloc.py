@@ -60,6 +60,33 @@ def test_noalloc_matches_allocating_solve(built):
         assert np.array_equal(got.view(np.uint64), ref.view(np.uint64)), f"k={k} n={n}"
 
 
+def test_noalloc_after_a_smaller_check(built):
+    """A check with a small k, then a no-alloc solve with a large k: the kernel's
+    shared-memory limit set for one entry point must serve the other."""
+    import torch
+
+    from neurips2026_smart_building_challenge_b200 import env_lib
+
+    lib = env_lib()
+    lib.sb_dense_solve_noalloc.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
+                                           ctypes.c_void_p]
+    lib.sb_dense_check.argtypes = [ctypes.c_int, ctypes.c_int] + [ctypes.POINTER(ctypes.c_double)] * 3
+    Ms, bs = _systems(8, 4, 5)
+    _check(lib, 8, 4, Ms, bs)
+    for k, n, seed in [(81, 40, 6), (128, 16, 7)]:
+        M, b = _systems(k, n, seed)
+        Md = torch.from_numpy(M).cuda()
+        bd = torch.from_numpy(b).cuda()
+        out = torch.zeros((n, k), dtype=torch.float64, device="cuda")
+        torch.cuda.synchronize()
+        assert lib.sb_dense_solve_noalloc(k, n, Md.data_ptr(), bd.data_ptr(), out.data_ptr()) == 0, \
+            lib.sb_last_error()
+        torch.cuda.synchronize()
+        ref = _check(lib, k, n, M, b)
+        assert np.array_equal(out.cpu().numpy().view(np.uint64), ref.view(np.uint64)), f"k={k} n={n}"
+        _check(lib, 8, 4, Ms, bs)
+
+
 def test_noalloc_rejects_batches_beyond_its_array(built):
     import torch
 
