@@ -59,6 +59,9 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--rollout", action="store_true", help="configuration 5: env+policy steps in a CUDA graph")
     ap.add_argument("--horizon", type=int, default=128, help="rollout horizon (--rollout)")
+    ap.add_argument("--solve", default="exact", choices=["exact", "folded"],
+                    help="exact: the reference core's two triangular solves, bit for bit; folded: one L/U "
+                         "pair (the reference GPU backend's folded air side, 1e-9 per-step contract)")
     return ap.parse_args()
 
 
@@ -286,7 +289,8 @@ def run_ours(args) -> None:
     cache = ROOT / ".sbb_cache" / f"bench_rank{rank}"
     d = config_dir(2, cache)
     n = args.envs
-    env = SmartBuildingsVec(n, blob_dir=str(d), groups=30, device=f"cuda:{local}")
+    env = SmartBuildingsVec(n, blob_dir=str(d), groups=30, device=f"cuda:{local}",
+                            solve_exact=1 if args.solve == "exact" else 0)
     env.reset()
     pool = torch.from_numpy(action_pool(n, 8, seed=1234 + rank)).to(env.device)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=env.device)   # > 126 MB L2
@@ -387,7 +391,7 @@ def run_ours(args) -> None:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-                "config": {"workload": WORKLOAD, "envs_per_gpu": n, "total_envs": n * world,
+                "config": {"workload": WORKLOAD, "envs_per_gpu": n, "total_envs": n * world, "solve": args.solve,
                            "l2": "flushed between timed steps (256 MiB write, untimed)",
                            "parallelism": f"env-sharded x{world}, no per-step collective"},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,

@@ -105,7 +105,11 @@ void dict_set_str(Dict* d, const char* key, const char* value);
  * spread round-robin by building (smart_buildings.cu:2497-2560). Other keys:
  * groups (scenario count, 0 = n/32), max_steps (0 = the blob's episode
  * length), merge_weathers (share one solver group across weathers of a
- * building, default 1), reward_scale (default 1). Returns NULL on error. */
+ * building, default 1), reward_scale (default 1), solve_exact (1, default:
+ * the reference core's two triangular solves per step, bit for bit; 0: the
+ * folded air side of the reference's GPU backend, one L and one U sweep per
+ * step, agreeing with the reference within 1e-9 relative per step). Returns
+ * NULL on error. */
 Env* puf_vec_create(int n, Dict* kwargs, obs_t* observations, float* actions, float* rewards,
                     float* terminals);
 void puf_bind_stream(sb_stream_t stream);

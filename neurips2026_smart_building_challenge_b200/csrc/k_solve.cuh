@@ -566,10 +566,17 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
         prefetch_l2(g.fwd.stream, g.fwd.total_bytes, tid, blockDim.x);
         prefetch_l2(g.bwd.stream, g.bwd.total_bytes, tid, blockDim.x);
         // and the tables the phase reads after its sweeps
-        if (Phase == 0) {
+        if (Phase == 0 && g.fold) {
+            prefetch_l2(reinterpret_cast<const uint8_t*>(g.rs_x), (uint32_t)g.rs_nnz * 8u, tid, blockDim.x);
+            prefetch_l2(reinterpret_cast<const uint8_t*>(g.rs_pos), (uint32_t)g.rs_nnz * 4u, tid, blockDim.x);
+        } else if (Phase == 0) {
             prefetch_l2(reinterpret_cast<const uint8_t*>(g.sn_x), (uint32_t)g.sn_nnz * 8u, tid, blockDim.x);
             prefetch_l2(reinterpret_cast<const uint8_t*>(g.sn_pos), (uint32_t)g.sn_nnz * 4u, tid, blockDim.x);
         } else {
+            if (g.fold) {
+                prefetch_l2(reinterpret_cast<const uint8_t*>(g.zr_x), (uint32_t)g.zr_nnz * 8u, tid, blockDim.x);
+                prefetch_l2(reinterpret_cast<const uint8_t*>(g.zr_col), (uint32_t)g.zr_nnz * 4u, tid, blockDim.x);
+            }
             prefetch_l2(reinterpret_cast<const uint8_t*>(g.ret), (uint32_t)g.n * 8u, tid, blockDim.x);
             prefetch_l2(reinterpret_cast<const uint8_t*>(g.gain), (uint32_t)g.n * 8u, tid, blockDim.x);
         }
@@ -650,18 +657,54 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
         }
         __syncthreads();
 
-        // ---- first solve ----
+        // ---- first solve (the folded build: its forward half only) ----
         if (tid < kSweepWarps * 32) run_sweep(sh, g.fwd, B, S, n, 1);
         __syncthreads();
-        if (tid < kSweepWarps * 32) run_sweep(sh, g.bwd, B, S, n, 2);
-        __syncthreads();
+        if (!g.fold) {
+            if (tid < kSweepWarps * 32) run_sweep(sh, g.bwd, B, S, n, 2);
+            __syncthreads();
+        }
         if (*sh.abort) {   // uniform: read after the barrier
             if (tid == 0) set_error(ctx->status, *sh.abort);
             return;
         }
 
+        // ---- folded air side: sensed = R z, one warp per sensor, its terms
+        // spread over the lanes, a warp reduction per env ----
+        if (g.fold && k > 0 && any_active) {
+            const int lane = tid & 31;
+            for (int r = tid >> 5; r < k; r += (int)(blockDim.x >> 5)) {
+                double acc[kGroupLanes];
+#pragma unroll
+                for (int e = 0; e < kGroupLanes; e++) acc[e] = 0.0;
+                const int p1 = g.rs_p[r + 1];
+                for (int p = g.rs_p[r] + lane; p < p1; p += 32) {
+                    const double xv = g.rs_x[p];
+                    const int pos = g.rs_pos[p];
+#pragma unroll
+                    for (int e = 0; e < kGroupLanes; e++)
+                        if (e < nenv) acc[e] = fma(xv, sh.X[(size_t)e * S + pos], acc[e]);
+                }
+#pragma unroll
+                for (int e = 0; e < kGroupLanes; e++) {
+                    double v = acc[e];
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                    acc[e] = v;
+                }
+                if (lane == 0) {
+#pragma unroll
+                    for (int e = 0; e < kGroupLanes; e++) {
+                        if (e >= nenv) break;
+                        if (!active[e]) continue;
+                        const double* D = ctx->Dst + (size_t)(sd.env0 + e) * L.nd;
+                        ctx->airq[(size_t)(sd.env0 + e) * ctx->k_max + r] = dmul(D[L.ag + r], dsub(D[L.aT + r], acc[e]));
+                    }
+                }
+            }
+        }
         // ---- air side (sb_fdm.c:155-181): the sensed right side to ctx->airq ----
-        if (k > 0 && any_active) {
+        if (!g.fold && k > 0 && any_active) {
             // the sensed terms staged in the (now idle) ring memory when they fit
             const size_t ring_bytes = (size_t)kSweepWarps * R * kStageBytes;
             const bool staged = (size_t)g.sn_nnz * 12 <= ring_bytes;
@@ -708,7 +751,7 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
                 }
             }
         }
-        // y -> the field array (row positions); the second solve adds to it
+        // y (folded build: z) -> the field array (row positions); phase 1 adds to it
         for (int i = tid; i < n; i += blockDim.x) {
 #pragma unroll
             for (int e = 0; e < kGroupLanes; e++)
@@ -717,10 +760,54 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
         return;
     }   // Phase 0
 
+    const int local0 = sd.env0 - g.env0;
+    // ---- folded build: the U sweep from z + Z q (z from phase 0 in the field
+    // array, q k_dense's solution staged in the idle ring memory) ----
+    if (g.fold) {
+        double* qs = reinterpret_cast<double*>(sh.ring);   // [nenv][k]
+        const bool air = k > 0 && any_active;
+        const bool qstaged = (size_t)nenv * k * sizeof(double) <= (size_t)kSweepWarps * R * kStageBytes;
+        if (air && qstaged)
+            for (int t = tid; t < nenv * k; t += blockDim.x) {
+                const int e = t / k, c = t - e * k;
+                qs[t] = ctx->airq[(size_t)(sd.env0 + e) * ctx->k_max + c];
+            }
+        __syncthreads();
+        const double* q = qstaged ? qs : ctx->airq;
+        const size_t qstride = qstaged ? (size_t)k : (size_t)ctx->k_max;
+        const size_t qbase = qstaged ? 0 : (size_t)sd.env0 * ctx->k_max;
+        for (int i = tid; i < n; i += blockDim.x) {
+            double acc[kGroupLanes];
+#pragma unroll
+            for (int e = 0; e < kGroupLanes; e++)
+                acc[e] = e < nenv ? g.T[(size_t)(local0 + e) * ncv + i] : 0.0;
+            if (air) {
+                const int p0 = g.zr_p[i], p1 = g.zr_p[i + 1];
+                for (int p = p0; p < p1; p++) {
+                    const int col = g.zr_col[p];
+                    const double xv = g.zr_x[p];
+#pragma unroll
+                    for (int e = 0; e < kGroupLanes; e++) {
+                        if (e >= nenv) break;
+                        if (active[e]) acc[e] = fma(xv, q[qbase + (size_t)e * qstride + col], acc[e]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int e = 0; e < kGroupLanes; e++)
+                if (e < B) sh.X[(size_t)e * S + i] = acc[e];
+        }
+        __syncthreads();
+        if (tid < kSweepWarps * 32) run_sweep(sh, g.bwd, B, S, n, 1);
+        __syncthreads();
+        if (*sh.abort) {
+            if (tid == 0) set_error(ctx->status, *sh.abort);
+            return;
+        }
+    }
     // ---- second solve: r = applied q (k_dense's solution), pulled per row in
     // ascending column order, zero q skipped; one thread per row for all envs ----
-    const int local0 = sd.env0 - g.env0;
-    if (k > 0 && any_active) {
+    if (!g.fold && k > 0 && any_active) {
         // the slab's dense solutions staged in the (not yet used) ring memory
         double* qs = reinterpret_cast<double*>(sh.ring);   // [nenv][k]
         const bool qstaged = (size_t)nenv * k * sizeof(double) <= (size_t)kSweepWarps * R * kStageBytes;
@@ -777,7 +864,8 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
         for (int e = 0; e < kGroupLanes; e++) {
             if (e >= nenv) break;
             double ye = y[e];
-            if (k > 0 && active[e]) ye = dadd(ye, sh.X[(size_t)e * S + i]);
+            if (g.fold) ye = sh.X[(size_t)e * S + i];
+            else if (k > 0 && active[e]) ye = dadd(ye, sh.X[(size_t)e * S + i]);
             g.M[(size_t)(local0 + e) * n + i] = dadd(dmul(m[e], ret), dmul(gain, ye));
             g.T[(size_t)(local0 + e) * ncv + i] = ye;
         }

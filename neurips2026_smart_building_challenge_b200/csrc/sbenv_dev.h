@@ -201,8 +201,17 @@ struct GroupDev {
     // convection (room-local candidate lists in convection-cell numbering)
     const int32_t *cv_off, *cv_pos, *cand_off, *cand_idx;
     int conv_nrooms, conv_maxroom;
+    // folded air side (fold = 1): phase 0 runs the L sweep only and reads the
+    // sensed values as R z; phase 1 starts the U sweep from z + Z q
+    int fold;
+    int zr_nnz, rs_nnz;
+    const int32_t *zr_p, *zr_col;   // Z = L^-1 applied, CSR by row position (coupled columns)
+    const double* zr_x;
+    const int32_t *rs_p, *rs_pos;   // R = sensed U^-1, CSR by sensor (row positions)
+    const double* rs_x;
     // per-env state
-    double* T;     // [n_env][ncv] extended row order
+    double* T;     // [n_env][ncv] extended row order (between the phases of the
+                   // folded build: z = L^-1 b in the solved rows)
     double* M;     // [n_env][n] interior mass, row order
 };
 

@@ -517,4 +517,64 @@ std::string build_sweeps(HostGroup& g, int ring_stages) {
     return e;
 }
 
+// Folded air side (the reference GPU backend's fast path,
+// complete_port/gpu/smart_buildings.cu:686-826 and sb_gpu_lusolve.cuh:190-259):
+// with z = L^-1 b the first solve's forward half, the sensed values are
+// sensed . U^-1 z = R z with R = sensed U^-1 (k x n, row r = U^-T sensed_r),
+// and the corrected field is U^-1 (z + Z q) with Z = L^-1 applied (n x k), so
+// one L sweep and one U sweep replace the exact build's two pairs. Both
+// matrices are formed here in row order from the same sweep terms the device
+// replays; exact zeros are dropped.
+std::string build_fold(HostGroup& g) {
+    const int n = g.n, k = g.k;
+    g.zr_p.assign(n + 1, 0);
+    g.zr_col.clear();
+    g.zr_x.clear();
+    g.rs_p.assign(k + 1, 0);
+    g.rs_pos.clear();
+    g.rs_x.clear();
+    if (k == 0) return "";
+    // Z, column by column (forward substitution with the L sweep's terms)
+    std::vector<std::vector<std::pair<int32_t, double>>> zrows(n);
+    std::vector<double> a(n);
+    for (int c = 0; c < k; c++) {
+        std::fill(a.begin(), a.end(), 0.0);
+        for (int i = 0; i < n; i++)
+            for (int q = g.ap_rp[i]; q < g.ap_rp[i + 1]; q++)
+                if (g.ap_col[q] == c) a[i] += g.ap_x[q];
+        for (int i = 0; i < n; i++) {
+            double v = a[i];
+            for (const auto& t : g.lt[i]) v -= t.second * a[t.first];
+            a[i] = v;
+            if (v != 0.0) zrows[i].push_back({c, v});
+        }
+    }
+    for (int i = 0; i < n; i++) {
+        for (const auto& t : zrows[i]) {
+            g.zr_col.push_back(t.first);
+            g.zr_x.push_back(t.second);
+        }
+        g.zr_p[i + 1] = (int32_t)g.zr_col.size();
+    }
+    // R, sensor by sensor (forward substitution with U^T, pushed over U's rows)
+    std::vector<double> w(n);
+    for (int r = 0; r < k; r++) {
+        std::fill(w.begin(), w.end(), 0.0);
+        for (int q = g.sn_p[r]; q < g.sn_p[r + 1]; q++) w[g.sn_pos[q]] += g.sn_x[q];
+        for (int i = 0; i < n; i++) {
+            if (w[i] == 0.0) continue;
+            const double ri = w[i] / g.udiag[i];
+            w[i] = ri;
+            for (const auto& t : g.ut[i]) w[t.first] -= t.second * ri;
+        }
+        for (int i = 0; i < n; i++)
+            if (w[i] != 0.0) {
+                g.rs_pos.push_back(i);
+                g.rs_x.push_back(w[i]);
+            }
+        g.rs_p[r + 1] = (int32_t)g.rs_pos.size();
+    }
+    return "";
+}
+
 }  // namespace sbenv

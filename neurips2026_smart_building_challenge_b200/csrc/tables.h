@@ -25,6 +25,9 @@ struct HostGroup {
     std::vector<int32_t> cv_off, cv_pos, cand_off, cand_idx;
     int conv_maxroom = 0;
     std::vector<int32_t> row_of_solved;   // solved index t -> row position
+    // folded air side (build_fold): Z = L^-1 applied by row, R = sensed U^-1 by sensor
+    std::vector<int32_t> zr_p, zr_col, rs_p, rs_pos;
+    std::vector<double> zr_x, rs_x;
 };
 
 struct HostScn {
@@ -60,6 +63,8 @@ std::string build_group(const sbb::Reader& b, HostGroup& g);
 int solve_ring_stages(int n, int B, size_t smem_cap);
 // Builds the group's L and U sweep programs for a per-warp ring of ring_stages.
 std::string build_sweeps(HostGroup& g, int ring_stages);
+// Builds the folded air side's Z = L^-1 applied and R = sensed U^-1 (row order).
+std::string build_fold(HostGroup& g);
 // Builds the per-scenario tables (needs the group's position maps).
 std::string build_scenario(const sbb::Reader& b, const HostGroup& g, int max_steps_kw, HostScn& s);
 // True when b can share a's group: every geometry / solver section identical.

@@ -70,12 +70,24 @@ def pre_stage_diff(env, orc, e):
     return "pre-stage: " + ("; ".join(out) if out else "identical")
 
 
+# Tolerances of the folded build (solve_exact = 0), the north star's contract:
+# temperatures within 1e-9 relative (the field and interior mass, every check),
+# rewards within 1e-9 relative, observations equal up to the float32 rounding of
+# a value that moved by that much (1e-4 of the field's scale).
+TOL_FIELD = 1e-9
+TOL_REWARD = 1e-9
+TOL_OBS = 1e-4
+
+
 def run_parity(blob_dir, n, steps, max_steps=0, seed=0, temp_every=10, groups=0, beta_mix=False,
-               oracle="port", wild=True, env_kw=None, first_lengths=None, start_offsets=None):
+               oracle="port", wild=True, env_kw=None, first_lengths=None, start_offsets=None,
+               tolerant=False):
     """Steps n device envs and n oracle envs with the same seeded actions and
-    compares them bit for bit after every step. first_lengths / start_offsets
-    (per env) give the oracle envs the first-episode cut and calendar offsets the
-    device env chose (episode options); the device env's own choice is passed in."""
+    compares them bit for bit after every step (tolerant: within the folded
+    build's tolerances above; the largest differences seen are returned).
+    first_lengths / start_offsets (per env) give the oracle envs the
+    first-episode cut and calendar offsets the device env chose (episode
+    options); the device env's own choice is passed in."""
     import torch
 
     from neurips2026_smart_building_challenge_b200 import SB_NUM_ATNS
@@ -83,6 +95,7 @@ def run_parity(blob_dir, n, steps, max_steps=0, seed=0, temp_every=10, groups=0,
     env = vec(n, blob_dir, max_steps=max_steps, groups=groups, **(env_kw or {}))
     path = oracle_path(oracle)
     against_ref = path == REF
+    worst = {"field_rel": 0.0, "field_abs_K": 0.0, "reward_rel": 0.0, "obs_abs": 0.0, "obs_fields_differing": 0}
     try:
         paths = scenario_paths(blob_dir)
         orc = [OracleEnv(paths[int(env.scenario[e])], max_steps=max_steps, path=path) for e in range(n)]
@@ -115,26 +128,48 @@ def run_parity(blob_dir, n, steps, max_steps=0, seed=0, temp_every=10, groups=0,
                 o, r, t, r64, p12, log8 = orc[e].step(a[e])
                 where = f"step {s} env {e} scenario {int(env.scenario[e])}"
                 bad = []
-                if not np.array_equal(obs[e].view(np.uint32), o.view(np.uint32)):
-                    bad.append(f"obs fields {np.nonzero(obs[e] != o)[0][:8].tolist()}")
-                if rew[e] != np.float32(r) or rd[e] != r64:
-                    bad.append(f"reward {rd[e]!r} vs {r64!r}")
                 if term[e] != t:
                     bad.append("terminal")
                 cmp = slice(0, 7) if against_ref else slice(0, 8)
-                if not np.array_equal(parts[e][cmp], log8[cmp]):
-                    bad.append(f"log terms {np.nonzero(parts[e][cmp] != log8[cmp])[0].tolist()}")
+                if tolerant:
+                    do = np.abs(obs[e].astype(np.float64) - o.astype(np.float64))
+                    worst["obs_abs"] = max(worst["obs_abs"], float(do.max()))
+                    worst["obs_fields_differing"] += int(np.count_nonzero(do))
+                    if (do > TOL_OBS * np.maximum(1.0, np.abs(o))).any():
+                        bad.append(f"obs fields {np.nonzero(do > TOL_OBS)[0][:8].tolist()} differ by {do.max():.3e}")
+                    rel = abs(rd[e] - r64) / max(abs(r64), 1e-2)
+                    worst["reward_rel"] = max(worst["reward_rel"], rel)
+                    if rel > TOL_REWARD:
+                        bad.append(f"reward {rd[e]!r} vs {r64!r}")
+                    pr = np.abs(parts[e][cmp] - log8[cmp]) / np.maximum(np.abs(log8[cmp]), 1e-2)
+                    if (pr > TOL_REWARD).any():
+                        bad.append(f"log terms {np.nonzero(pr > TOL_REWARD)[0].tolist()}")
+                else:
+                    if not np.array_equal(obs[e].view(np.uint32), o.view(np.uint32)):
+                        bad.append(f"obs fields {np.nonzero(obs[e] != o)[0][:8].tolist()}")
+                    if rew[e] != np.float32(r) or rd[e] != r64:
+                        bad.append(f"reward {rd[e]!r} vs {r64!r}")
+                    if not np.array_equal(parts[e][cmp], log8[cmp]):
+                        bad.append(f"log terms {np.nonzero(parts[e][cmp] != log8[cmp])[0].tolist()}")
                 if bad or s % temp_every == 0 or s == steps - 1:
-                    dT = env.temp(e, orc[e].ncv) - orc[e].temp()
-                    dM = env.mass(e, orc[e].n) - orc[e].mass()
-                    if dT.any():
-                        bad.append(f"T differs at {np.count_nonzero(dT)} cells, max {np.abs(dT).max():.3e}")
-                    if dM.any():
-                        bad.append(f"M differs at {np.count_nonzero(dM)} cells, max {np.abs(dM).max():.3e}")
-                if bad and not against_ref:
+                    To, Mo = orc[e].temp(), orc[e].mass()
+                    dT = env.temp(e, orc[e].ncv) - To
+                    dM = env.mass(e, orc[e].n) - Mo
+                    if tolerant:
+                        scale = max(np.abs(To).max(), np.abs(Mo).max())
+                        worst["field_abs_K"] = max(worst["field_abs_K"], float(np.abs(dT).max()), float(np.abs(dM).max()))
+                        worst["field_rel"] = max(worst["field_rel"], worst["field_abs_K"] / scale)
+                        if np.abs(dT).max() > TOL_FIELD * scale or np.abs(dM).max() > TOL_FIELD * scale:
+                            bad.append(f"field differs by {np.abs(dT).max():.3e} K, mass by {np.abs(dM).max():.3e} K")
+                    else:
+                        if dT.any():
+                            bad.append(f"T differs at {np.count_nonzero(dT)} cells, max {np.abs(dT).max():.3e}")
+                        if dM.any():
+                            bad.append(f"M differs at {np.count_nonzero(dM)} cells, max {np.abs(dM).max():.3e}")
+                if bad and not against_ref and not tolerant:
                     bad.append(pre_stage_diff(env, orc[e], e))
                 assert not bad, f"{where} ({path.name}): " + "; ".join(bad)
         assert env.status() == 0
-        return env
+        return worst
     finally:
         env.close()
