@@ -58,10 +58,31 @@ typedef struct Log {
     float n;
 } Log;
 
+/* PufferLib's per-agent buffer record (pufferenv.h of PufferLib 5.0, which is
+ * not vendored): the five pointers the env fills. A translation unit that has
+ * PufferLib's own Agent defines SB_HAVE_AGENT before including this header;
+ * the layout below must then be the same as PufferLib's. */
+#ifndef SB_HAVE_AGENT
+typedef struct Agent {
+    float* observations;
+    float* actions;
+    float* rewards;
+    float* terminals;
+    unsigned char* action_mask;
+} Agent;
+#endif
+
 /* One environment record; an array of n of them is returned by puf_vec_create
- * in managed memory (smart_buildings.cu:116-143). The step writes log / ep_* /
- * step on the device; the host reads them only after synchronising. */
+ * in managed memory. The members and their order are the reference GPU
+ * backend's (complete_port/gpu/smart_buildings.cu:116-143, non-entity build),
+ * so a trainer indexing envs[i] with the reference's struct reads the same
+ * fields; `scenario` is an addition after them. agents[0] points into the
+ * caller's buffers (env i's slices); cont / disc / native are NULL (the device
+ * step keeps its decoded actions on the device). The step writes log / ep_* /
+ * step / max_steps / start_* on the device; the host reads them only after
+ * synchronising. */
 typedef struct Env {
+    Agent agents[1];
     Log log;
     float ep_ret;
     float ep_part[SB_NPARTS_ENV];
@@ -70,13 +91,20 @@ typedef struct Env {
     int tag;
     int boundary_reached;
     int step;
-    int max_steps;
+    int max_steps;            /* this episode's length (desync: the first one is cut) */
+    int start_offset;         /* calendar row of this episode's first step (random_start) */
+    int start_day;            /* start_offset / 288 */
+    unsigned long long start_rng;   /* the env's random-start stream (SplitMix64) */
+    unsigned int start_draws; /* start days drawn so far */
     int n_act, n_cont, n_disc;
     int loaded;
     unsigned int rng;
     int seed;
+    double* cont;
+    double* disc;
+    double* native;
     int env_id;
-    int scenario;
+    int scenario;             /* addition: the env's scenario index */
 } Env;
 
 /* PufferLib's keyword dictionary, minimal layout: a key with a numeric value
@@ -108,8 +136,19 @@ void dict_set_str(Dict* d, const char* key, const char* value);
  * building, default 1), reward_scale (default 1), solve_exact (1, default:
  * the reference core's two triangular solves per step, bit for bit; 0: the
  * folded air side of the reference's GPU backend, one L and one U sweep per
- * step, agreeing with the reference within 1e-9 relative per step). Returns
- * NULL on error. */
+ * step, agreeing with the reference within 1e-9 relative per step).
+ * Episode options of the reference's GPU backend (smart_buildings.cu:2583-2608,
+ * 2806-2816, 1636-1657, 1936-2050): desync (1: env i's first episode ends at a
+ * step in [1, episode length] drawn from i; later episodes are whole, the cut
+ * first ones stay out of the log), random_start (1: every episode starts at a
+ * calendar offset of d * 288 steps, d in 0..6 drawn per env and episode from a
+ * SplitMix64 stream seeded by random_start_seed and the env index; needs
+ * blobs with random_start_offsets and tables 6 * 288 rows longer than the
+ * episode; desync is then ignored), rew_norm (1: the reward buffer holds
+ * (r - mean) * inv_std per scenario, the statistics moved by 0.1 towards each
+ * puf_live_log window, starting at mean 0 and variance 0.217) and rew_center
+ * (1: (r - mean) only, the mean moved by center_beta, default 0.01; rew_norm
+ * wins when both are set). Returns NULL on error. */
 Env* puf_vec_create(int n, Dict* kwargs, obs_t* observations, float* actions, float* rewards,
                     float* terminals);
 void puf_bind_stream(sb_stream_t stream);
@@ -150,6 +189,10 @@ int sb_get_temp(int env, double* out, int n_cvs);
 int sb_get_mass(int env, double* out, int n_solved);
 /* Copies the last step's per-env reward (double) and log terms [n][8] to host memory. */
 int sb_get_reward_f64(double* reward, double* parts);
+/* Episode options as set up at creation: per env the first episode's length
+ * (desync) and the initial random-start stream state (the value before the
+ * first draw), host arrays of n (either may be NULL). Returns 0 or -1. */
+int sb_episode_options(int* first_len, unsigned long long* start_rng);
 /* Policy-in-loop rollouts: actions drawn from a
  * policy's logits, as the reference trainer's mixed heads do
  * (patches/pufferlib_core.diff:2490-2580; beta_floor / beta_conc_max of
@@ -204,9 +247,11 @@ int sb_snapshot_write(int env, const char* path);
 /* Number of hot-path kernel launches one puf_step enqueues. */
 int sb_kernels_per_step(void);
 /* Measurement: runs one step with CUDA events around each kernel on the bound
- * streams (not for graph capture). ms[7] = {k_rng, k_pre, solve, k_post, solve
- * phase 0, k_dense, solve phase 1}; solve = phase 0 + k_dense + phase 1; k_rng
- * runs beside phase 0, inside its interval, and reports -1. */
+ * streams (not for graph capture). ms[7] = {random inputs, k_pre, solve,
+ * k_post, solve phase 0, k_dense, solve phase 1}; solve = phase 0 + k_dense +
+ * phase 1; the random inputs of the next transition (k_conv, k_occ) run on
+ * their own streams beside the solve, ms[0] from the end of k_pre to the later
+ * of the two. */
 int sb_step_timed(float* ms);
 /* Algorithmic bytes one solve launch must move for the loaded batch: per env the
  * field and interior mass read and written plus the per-zone heat and air-side

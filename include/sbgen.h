@@ -41,6 +41,9 @@ typedef struct {
     uint64_t layout_seed;      /* geometry, conductances, HVAC constants */
     uint64_t climate_seed;     /* weather noise */
     int64_t occ_seed, conv_seed;
+    int random_start_days;     /* 0, or 7: calendar tables 6 * 288 rows longer than the
+                                  episode, the priming hour per row and
+                                  random_start_offsets (for the env's random_start) */
 } SbGenParams;
 
 /* Fills `out` with the parameters of one BASELINE configuration scenario.

@@ -39,7 +39,8 @@ ENV_SYMBOLS = ["sb_dict_new", "sb_dict_free", "dict_find", "dict_set", "dict_set
                "puf_live_log", "puf_mask_init", "sb_last_error", "sb_device_status", "sb_shape",
                "sb_env_info", "sb_get_temp", "sb_get_mass", "sb_get_reward_f64", "sb_kernels_per_step",
                "sb_solve_schedule", "sb_sweep_warps", "sb_sweep_stats", "sb_debug_state", "sb_step_timed", "sb_solve_bytes",
-               "sb_dense_check", "sb_beta_actions", "sb_snapshot_write", "sb_dense_solve_noalloc"]
+               "sb_dense_check", "sb_beta_actions", "sb_snapshot_write", "sb_dense_solve_noalloc",
+               "sb_episode_options"]
 GEN_SYMBOLS = ["sbgen_preset", "sbgen_write", "sbgen_factor_stats"]
 
 
@@ -47,13 +48,21 @@ class Log(ctypes.Structure):
     _fields_ = [(f, ctypes.c_float) for f in LOG_FIELDS]
 
 
+class Agent(ctypes.Structure):
+    _fields_ = [("observations", ctypes.c_void_p), ("actions", ctypes.c_void_p), ("rewards", ctypes.c_void_p),
+                ("terminals", ctypes.c_void_p), ("action_mask", ctypes.c_void_p)]
+
+
 class EnvRecord(ctypes.Structure):
-    _fields_ = [("log", Log), ("ep_ret", ctypes.c_float), ("ep_part", ctypes.c_float * SB_NPARTS),
-                ("ep_worst", ctypes.c_float), ("num_agents", ctypes.c_int), ("tag", ctypes.c_int),
-                ("boundary_reached", ctypes.c_int), ("step", ctypes.c_int), ("max_steps", ctypes.c_int),
-                ("n_act", ctypes.c_int), ("n_cont", ctypes.c_int), ("n_disc", ctypes.c_int),
-                ("loaded", ctypes.c_int), ("rng", ctypes.c_uint), ("seed", ctypes.c_int),
-                ("env_id", ctypes.c_int), ("scenario", ctypes.c_int)]
+    """include/sbenv.h Env: the reference GPU backend's member order, then `scenario`."""
+    _fields_ = [("agents", Agent * 1), ("log", Log), ("ep_ret", ctypes.c_float),
+                ("ep_part", ctypes.c_float * SB_NPARTS), ("ep_worst", ctypes.c_float), ("num_agents", ctypes.c_int),
+                ("tag", ctypes.c_int), ("boundary_reached", ctypes.c_int), ("step", ctypes.c_int),
+                ("max_steps", ctypes.c_int), ("start_offset", ctypes.c_int), ("start_day", ctypes.c_int),
+                ("start_rng", ctypes.c_ulonglong), ("start_draws", ctypes.c_uint), ("n_act", ctypes.c_int),
+                ("n_cont", ctypes.c_int), ("n_disc", ctypes.c_int), ("loaded", ctypes.c_int), ("rng", ctypes.c_uint),
+                ("seed", ctypes.c_int), ("cont", ctypes.c_void_p), ("disc", ctypes.c_void_p),
+                ("native", ctypes.c_void_p), ("env_id", ctypes.c_int), ("scenario", ctypes.c_int)]
 
 
 class DictItem(ctypes.Structure):
@@ -71,7 +80,7 @@ class SbGenParams(ctypes.Structure):
                [(n, ctypes.c_double) for n in
                 ["cv_size_cm", "dt_sec", "t_mean_c", "t_amp_k", "ar_phi", "ar_sigma_k", "conv_p"]] + \
                [("layout_seed", ctypes.c_uint64), ("climate_seed", ctypes.c_uint64),
-                ("occ_seed", ctypes.c_int64), ("conv_seed", ctypes.c_int64)]
+                ("occ_seed", ctypes.c_int64), ("conv_seed", ctypes.c_int64), ("random_start_days", ctypes.c_int)]
 
 
 _LIBS: dict[str, ctypes.CDLL] = {}
@@ -120,6 +129,7 @@ def env_lib() -> ctypes.CDLL:
         lib.sb_beta_actions.argtypes = [vp, vp, vp, ctypes.c_int, ctypes.c_float, ctypes.c_float,
                                         ctypes.c_ulonglong, vp]
         lib.sb_snapshot_write.argtypes = [ctypes.c_int, ctypes.c_char_p]
+        lib.sb_episode_options.argtypes = [ip, ctypes.POINTER(ctypes.c_ulonglong)]
         lib._sb_typed = True
     return lib
 
@@ -307,6 +317,15 @@ class SmartBuildingsVec:
         if self.lib.sb_snapshot_write(env, str(path).encode()) != 0:
             raise RuntimeError(self.lib.sb_last_error().decode())
 
+    def episode_options(self) -> tuple[np.ndarray, np.ndarray]:
+        """Per env: the first episode's length (desync) and the random-start
+        stream's state before its first draw."""
+        fl = (ctypes.c_int * self.n)()
+        sr = (ctypes.c_ulonglong * self.n)()
+        if self.lib.sb_episode_options(fl, sr) != 0:
+            raise RuntimeError("sb_episode_options failed")
+        return np.array(fl[:], dtype=np.int64), np.array(sr[:], dtype=np.uint64)
+
     def status(self) -> int:
         return int(self.lib.sb_device_status())
 
@@ -315,8 +334,8 @@ class SmartBuildingsVec:
         ms = (ctypes.c_float * 7)()
         if self.lib.sb_step_timed(ms) != 0:
             raise RuntimeError("sb_step_timed failed")
-        # k_rng runs beside k_solve phase 0 on its stream and has no time of its own (-1)
-        names = ["k_rng", "k_pre", "k_solve", "k_post", "k_solve_phase0", "k_dense", "k_solve_phase1"]
+        # random_inputs: the next transition's k_conv + k_occ, on their own streams beside the solve
+        names = ["random_inputs", "k_pre", "k_solve", "k_post", "k_solve_phase0", "k_dense", "k_solve_phase1"]
         return {k: v for k, v in zip(names, list(ms)) if v >= 0.0}
 
     def solve_bytes(self) -> float:

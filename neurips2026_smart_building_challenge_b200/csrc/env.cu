@@ -3,17 +3,19 @@
 // Reference interface: complete_port/gpu/smart_buildings.cu:2497-3323
 // (puf_vec_create, puf_bind_stream, puf_init, puf_reset, puf_step, puf_close,
 // puf_log, puf_live_log, puf_mask_init). One step enqueues, on the bound
-// stream and two streams forked from it:
+// stream and three streams forked from it:
 //   k_pre      (main)  decode, actuators, zone sensing, VAV/AHU/boiler pre-step
-//   k_solve<0> (side, after k_pre) forcing and first L/U solve over slabs of
-//              envs in shared memory, one slab per SM; air-side right side
-//   k_rng      (side, a programmatic dependent of k_solve<0>) per-scenario
-//              convection permutation + occupancy chains: it starts once every
-//              slab is resident and runs on the SMs the slabs leave free
-//   k_dense    (side) the air-side dense solve of every env, one CTA each
-//   k_solve<1> (side) applied heat, second L/U solve, interior mass, field
-//   k_post     (main, after the side stream) convection apply, boiler,
-//              observation, reward, episode log, in-step restart
+//   k_solve<0> (hi, after k_pre) forcing and first L/U solve (folded build: the
+//              L sweep) over slabs of envs in shared memory, one slab per SM;
+//              air-side right side
+//   k_dense    (hi) the air-side dense solve of every env, one CTA each
+//   k_solve<1> (hi) applied heat, second L/U solve (folded build: the U sweep),
+//              interior mass, field
+//   k_post     (main, after hi) convection apply, boiler, observation, reward,
+//              episode log, in-step restart
+//   k_conv, k_occ (two low-priority streams, forked after k_pre and joined at
+//              the end of the step) the next transition's convection
+//              permutations and occupancy chains, beside the whole step
 // No host synchronisation, allocation or attribute change happens inside
 // puf_step, so a caller can capture it in a CUDA graph.
 #include <cuda_runtime.h>
@@ -104,12 +106,18 @@ struct Engine {
     DevArena arena;
     StepCtx* d_ctx = nullptr;
     SlabDesc* d_slabs = nullptr;
-    int* d_scn_step = nullptr;
-    RngOut* d_rng_out = nullptr;
     Env* envs = nullptr;          // managed
-    cudaStream_t stream = nullptr, own_stream = nullptr, side = nullptr, hi = nullptr;
-    cudaEvent_t ev_fork = nullptr, ev_join = nullptr, ev_solve = nullptr;
-    size_t smem_solve = 0, smem_pre = 0, smem_post = 0, smem_rng = 0, smem_dense = 0;
+    cudaStream_t stream = nullptr, own_stream = nullptr, rng_a = nullptr, rng_b = nullptr, hi = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr, ev_rng_a = nullptr, ev_rng_b = nullptr;
+    size_t smem_solve = 0, smem_pre = 0, smem_post = 0, smem_conv = 0, smem_occ = 0, smem_dense = 0;
+    unsigned occ_ctas = 0;
+    // episode options and the learning-reward statistics (host EMA state)
+    bool rew_norm = false, rew_center = false, random_start = false;
+    double center_beta = 0.01;
+    std::vector<double> rn_mu, rn_var, last_sc;
+    float* d_rnorm = nullptr;
+    std::vector<int> first_len;
+    std::vector<unsigned long long> start_rng0;
     int dense_threads = 32;          // k_dense block (dense_threads(k_max))
     struct DenseClass { int first, count, k; };
     std::vector<DenseClass> dense_cls;   // runs of equal k in dense_order, heaviest first
@@ -118,14 +126,10 @@ struct Engine {
     bool ready = false;
     ~Engine() { destroy(); }
     void destroy() {
-        if (side) cudaStreamDestroy(side);
-        if (hi) cudaStreamDestroy(hi);
-        if (own_stream) cudaStreamDestroy(own_stream);
-        if (ev_fork) cudaEventDestroy(ev_fork);
-        if (ev_join) cudaEventDestroy(ev_join);
-        if (ev_solve) cudaEventDestroy(ev_solve);
-        side = hi = own_stream = nullptr;
-        ev_fork = ev_join = ev_solve = nullptr;
+        for (cudaStream_t* q : {&rng_a, &rng_b, &hi, &own_stream})
+            if (*q) { cudaStreamDestroy(*q); *q = nullptr; }
+        for (cudaEvent_t* q : {&ev_fork, &ev_join, &ev_rng_a, &ev_rng_b})
+            if (*q) { cudaEventDestroy(*q); *q = nullptr; }
         if (envs) cudaFree(envs);
         envs = nullptr;
         arena.release();
@@ -187,28 +191,24 @@ StateLayout make_layout(int na, int nv, int nz, int k) {
     L.reheat_w = D(1);
     L.ahu_run = I(na); L.ahu_creq = I(na); L.v_mode = I(nv); L.v_prev = I(nv); L.v_dset = I(nv); L.v_rset = I(nv);
     L.hws_req = I(1); L.hws_run = I(1); L.pump_run = I(1); L.step = I(1); L.gen = I(1); L.active = I(1);
+    L.cal = I(1); L.off = I(1); L.eplen = I(1); L.tseq = I(1);
     L.nd = (d + 1) & ~1;
     L.ni = (i + 3) & ~3;
     return L;
 }
 
-// k_rng as a programmatic dependent of k_solve on the same stream: every
-// solve CTA signals at its start, so the random streams begin once all slabs
-// are resident and take the SMs the slab count leaves free. k_rng reads
-// nothing k_solve writes; it ends by waiting for k_solve's completion, so the
-// side stream's work is complete when k_rng is.
-cudaError_t launch_rng_after_solve(Engine& E, cudaStream_t st, int reset_only) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)E.sd.size());
-    cfg.blockDim = dim3(32);
-    cfg.dynamicSmemBytes = E.smem_rng;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, k_rng, (const StepCtx*)E.d_ctx, E.d_scn_step, E.d_rng_out, reset_only);
+// The next transition's random inputs on the two low-priority streams (forked
+// from the main stream at `after`): convection per scenario, occupancy per stream.
+cudaError_t launch_rng(Engine& E, cudaEvent_t after) {
+    cudaError_t e = cudaStreamWaitEvent(E.rng_a, after, 0);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(E.rng_b, after, 0);
+    if (e != cudaSuccess) return e;
+    k_conv<<<(unsigned)E.sd.size(), 32, E.smem_conv, E.rng_a>>>(E.d_ctx, 0);
+    k_occ<<<E.occ_ctas, 32 * kOccWarps, E.smem_occ, E.rng_b>>>(E.d_ctx, 0);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaEventRecord(E.ev_rng_a, E.rng_a);
+    if (e == cudaSuccess) e = cudaEventRecord(E.ev_rng_b, E.rng_b);
+    return e;
 }
 
 // The dense air-side solves: one launch per class of equal k with its own
@@ -236,13 +236,15 @@ cudaError_t launch_dense(Engine& E, cudaStream_t st) {
 }
 
 // The solve on the high-priority stream: phase 0 (first L/U solve), the
-// random streams as its programmatic dependent, the dense air-side solves,
-// phase 1 (second L/U solve, mass, field).
+// dense air-side solves, phase 1 (second L/U solve, mass, field). The random
+// inputs of the next transition are enqueued on their own streams right after
+// phase 0, so the slabs are placed first and the producers take the SMs the
+// slabs leave free.
 cudaError_t launch_solve(Engine& E) {
     const unsigned slabs = (unsigned)E.slabs.size();
     k_solve<0><<<slabs, kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
     cudaError_t e = cudaGetLastError();
-    if (e == cudaSuccess) e = launch_rng_after_solve(E, E.hi, 0);
+    if (e == cudaSuccess) e = launch_rng(E, E.ev_fork);
     if (e != cudaSuccess) return e;
     e = launch_dense(E, E.hi);
     if (e != cudaSuccess) return e;
@@ -260,6 +262,9 @@ bool launch_step(Engine& E) {
     CK(cudaStreamWaitEvent(E.stream, E.ev_join, 0));
     k_post<<<(unsigned)E.n_env, 128, E.smem_post, E.stream>>>(E.d_ctx);
     CK(cudaGetLastError());
+    // the producers of the next transition join at the end of the step
+    CK(cudaStreamWaitEvent(E.stream, E.ev_rng_a, 0));
+    CK(cudaStreamWaitEvent(E.stream, E.ev_rng_b, 0));
     return true;
 }
 
@@ -288,6 +293,18 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     // solve_exact = 1 (default): the reference's two L/U solves, bit for bit;
     // 0: the folded air side (one L/U pair; within the 1e-9 per-step contract)
     const bool fold = kw_num(kw, "solve_exact", 1.0) == 0.0;
+    // episode options of the reference GPU backend (smart_buildings.cu:2583-2608)
+    E.random_start = kw_num(kw, "random_start", 0.0) != 0.0;
+    const bool desync = !E.random_start && kw_num(kw, "desync", 0.0) != 0.0;
+    const unsigned long long start_seed = (unsigned long long)(long long)kw_num(kw, "random_start_seed", 0.0);
+    E.rew_norm = kw_num(kw, "rew_norm", 0.0) != 0.0;
+    E.rew_center = !E.rew_norm && kw_num(kw, "rew_center", 0.0) != 0.0;
+    {
+        const double cb = kw_num(kw, "center_beta", 0.01);
+        if (cb > 0.0 && cb <= 1.0) E.center_beta = cb;
+    }
+    // occupancy chains per env once the envs of a scenario leave lock step
+    const bool per_env_occ = desync || E.random_start;
     // optional cap on the envs one solve CTA holds (1..8; default: as many as fit)
     const int slab_cap = std::max(1, std::min(kGroupLanes, (int)kw_num(kw, "slab_envs", (double)kGroupLanes)));
     for (int i = 0; i < G; i++) {
@@ -313,7 +330,7 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     }
     E.hs.resize(G);
     for (int i = 0; i < G; i++) {
-        std::string e = build_scenario(*E.blobs[i], E.hg[scn_group[i]], max_steps_kw, E.hs[i]);
+        std::string e = build_scenario(*E.blobs[i], E.hg[scn_group[i]], max_steps_kw, E.random_start, E.hs[i]);
         if (!e.empty()) { set_err("%s: %s", paths[i].c_str(), e.c_str()); return false; }
         E.hs[i].group = scn_group[i];
     }
@@ -451,8 +468,8 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
         E.smem_pre = std::max(E.smem_pre, sizeof(double) * (size_t)(L.nd + 2 * nz_max + nv_max + 2 * na_max + 2 * k_max) +
                                               sizeof(int32_t) * (size_t)L.ni);
         E.smem_post = std::max(E.smem_post, sizeof(double) * post_smem_doubles(h.ncv, nz_max, nv_max));
-        const size_t rng_b = 4 * (size_t)(624 + 624 + 1248) + 4 * (4 * (size_t)h.cv_off.back() + 1 + h.cv_off.size());
-        E.smem_rng = std::max(E.smem_rng, rng_b);
+        const size_t conv_b = 4 * (size_t)(624 + 624 + 1248) + 4 * (4 * (size_t)h.cv_off.back() + 1 + h.cv_off.size());
+        E.smem_conv = std::max(E.smem_conv, conv_b);
     }
     // ---- scenario tables + random streams ----
     for (int i = 0; i < G; i++) {
@@ -504,20 +521,38 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
             return m;
         };
         s.conv_mt = E.arena.upload(seeded(h.conv_seed), ok);
-        s.occ_mt = E.arena.upload(seeded(h.occ_seed), ok);
-        s.occ_state0 = E.arena.zeros<int>((size_t)h.nz * std::max(h.assign, 1), ok);
+        s.conv_ckpt = E.arena.zeros<uint32_t>(625, ok);
         const HostGroup& hgp = E.hg[scn_group[i]];
-        s.conv_pairs = E.arena.zeros<int32_t>(2 * (size_t)hgp.ncv + 2, ok);
-        s.conv_npairs = E.arena.zeros<int>(1, ok);
+        s.conv_stride = 2 * hgp.ncv + 2;
+        s.conv_pairs = E.arena.zeros<int32_t>(2 * (size_t)s.conv_stride, ok);
+        s.conv_npairs = E.arena.zeros<int>(2, ok);
+        s.o_hour_m1 = E.arena.upload(h.o_hour_m1, ok);
+        s.o_wd_m1 = E.arena.upload(h.o_wd_m1, ok);
+        s.m1_rows = (int)h.o_hour_m1.size();
     }
-    for (int i = 0; i < G; i++) E.smem_rng = std::max(E.smem_rng, 4 * (size_t)(624 + 624 + 1248) + 4 * (size_t)E.hs[i].nz * E.hs[i].assign);
     // ---- env index ----
     E.ei.resize(n);
     for (int i = 0; i < G; i++)
         for (int q = 0; q < scnt[i]; q++) {
             const int env = scn_env0[i] + q;
-            E.ei[env] = {scn_group[i], i, env - E.gd[scn_group[i]].env0, q == 0 ? 1 : 0};
+            E.ei[env] = {scn_group[i], i, env - E.gd[scn_group[i]].env0, per_env_occ ? env : i};
         }
+    // ---- episode options: first-episode lengths (desync) and the random-start
+    // streams, per global env index (smart_buildings.cu:2806-2816) ----
+    E.first_len.resize(n);
+    E.start_rng0.resize(n);
+    for (int env = 0; env < n; env++) {
+        const int ep_len = E.hs[E.ei[env].scn].max_steps;
+        E.first_len[env] = ep_len;
+        if (desync) {
+            unsigned long long h = 0x9E3779B97F4A7C15ULL * (unsigned long long)(env + 1);
+            h ^= h >> 31;
+            h *= 0xBF58476D1CE4E5B9ULL;
+            h ^= h >> 29;
+            E.first_len[env] = 1 + (int)(h % (unsigned long long)ep_len);
+        }
+        E.start_rng0[env] = start_mix(start_seed ^ (0x9e3779b97f4a7c15ULL * (unsigned long long)(env + 1)));
+    }
     // ---- context ----
     StepCtx& C = E.ctx;
     C.n_env = n;
@@ -551,6 +586,63 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     C.ep_scn = E.arena.zeros<double>((size_t)G * 2, ok);
     C.status = E.arena.zeros<int>(1, ok);
     C.nz_max = nz_max;
+    // ---- occupancy streams and the producers' slots ----
+    {
+        const int NO = per_env_occ ? n : G;
+        int assign_max = 1;
+        for (auto& h : E.hs) assign_max = std::max(assign_max, h.assign);
+        C.n_ostreams = NO;
+        C.ostream_per_env = per_env_occ ? 1 : 0;
+        C.random_start = E.random_start ? 1 : 0;
+        C.occ_stride = nz_max * assign_max;
+        std::vector<int> oscn(NO);
+        std::vector<uint32_t> mts((size_t)NO * 625);
+        for (int u = 0; u < NO; u++) {
+            oscn[u] = per_env_occ ? E.ei[u].scn : u;
+            const uint32_t seed = E.hs[oscn[u]].occ_seed;
+            uint32_t* m = mts.data() + (size_t)u * 625;
+            m[0] = seed;
+            for (int q = 1; q < 624; q++) m[q] = 1812433253u * (m[q - 1] ^ (m[q - 1] >> 30)) + (uint32_t)q;
+            m[624] = 624;
+        }
+        C.ostream_scn = E.arena.upload(oscn, ok);
+        C.occ_mt = E.arena.upload(mts, ok);
+        C.occ_state = E.arena.zeros<int>((size_t)NO * C.occ_stride, ok);
+        C.ostep = E.arena.zeros<int>(NO, ok);
+        C.oeplen = E.arena.zeros<int>(NO, ok);
+        C.ooff = E.arena.zeros<int>(NO, ok);
+        C.oseq = E.arena.zeros<int>(NO, ok);
+        C.orng = E.arena.zeros<unsigned long long>(NO, ok);
+        C.ck_mt = E.arena.zeros<uint32_t>((size_t)NO * 625, ok);
+        C.ck_state = E.arena.zeros<int>((size_t)NO * C.occ_stride, ok);
+        C.produced = E.arena.zeros<int>(1, ok);
+        C.cseq = E.arena.zeros<int>(G, ok);
+        C.V_step = E.arena.zeros<double>((size_t)kRngSlots * NO * nz_max, ok);
+        C.V_prime = E.arena.zeros<double>((size_t)kRngSlots * NO * nz_max, ok);
+        C.V_zero = E.arena.zeros<double>((size_t)kRngSlots * NO * nz_max, ok);
+        C.new_off = E.arena.zeros<int>((size_t)kRngSlots * NO, ok);
+        C.new_rng = E.arena.zeros<unsigned long long>((size_t)kRngSlots * NO, ok);
+        C.env_rng = E.arena.upload(E.start_rng0, ok);
+        C.start_draws = E.arena.zeros<double>((size_t)G * 2 * kStartDays, ok);
+        C.ep_start = E.arena.zeros<double>((size_t)G * kStartDays * 7, ok);
+        E.occ_ctas = (unsigned)((NO + kOccWarps - 1) / kOccWarps);
+        E.smem_occ = (size_t)kOccWarps * (kOccWarpSmem + 4 * (size_t)C.occ_stride);
+    }
+    // ---- learning-reward normalisation (smart_buildings.cu:2758-2795) ----
+    if (E.rew_norm || E.rew_center) {
+        const double var0 = E.rew_norm ? 0.217 : 1.0;   // rew_norm's steady-state start, inv_std 2.147
+        E.rn_mu.assign(G, 0.0);
+        E.rn_var.assign(G, var0);
+        std::vector<float> rn(2 * (size_t)G);
+        for (int i = 0; i < G; i++) {
+            rn[2 * i] = 0.0f;
+            rn[2 * i + 1] = E.rew_norm ? (float)(1.0 / std::sqrt(var0)) : 1.0f;
+        }
+        E.d_rnorm = E.arena.upload(rn, ok);
+        C.rnorm = E.d_rnorm;
+        if (E.rew_norm) C.znclip = E.arena.zeros<double>(3, ok);
+    }
+    E.last_sc.assign(G, 0.0);
     // air side: right side / solution per env; k_dense runs the heaviest envs first
     C.k_max = std::max(k_max, 1);
     C.airq = E.arena.zeros<double>((size_t)n * C.k_max, ok);
@@ -571,22 +663,17 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     }
     E.smem_dense = std::max<size_t>(16, dense_smem_doubles(k_max) * sizeof(double));
     E.dense_threads = dense_threads(std::max(k_max, 1));
-    double* vbuf = E.arena.zeros<double>((size_t)3 * G * nz_max, ok);
-    C.V_step = vbuf;
-    C.V_prime = vbuf + (size_t)G * nz_max;
-    C.V_zero = vbuf + (size_t)2 * G * nz_max;
-    std::vector<RngOut> ro(G);
-    for (int i = 0; i < G; i++)
-        ro[i] = {vbuf + (size_t)i * nz_max, vbuf + (size_t)(G + i) * nz_max, vbuf + (size_t)(2 * G + i) * nz_max};
-    E.d_rng_out = E.arena.upload(ro, ok);
-    E.d_scn_step = E.arena.zeros<int>(G, ok);
     E.d_slabs = E.arena.upload(E.slabs, ok);
     if (!ok) return false;
-    // per-env state that persists across resets (pump head set once at init, sb_sim.c:71-75)
+    // per-env state that persists across resets (pump head set once at init,
+    // sb_sim.c:71-75; the current episode's length, cut for desync)
     {
         std::vector<double> Dh((size_t)n * L.nd, 0.0);
         for (int env = 0; env < n; env++) Dh[(size_t)env * L.nd + L.pump_head] = E.hs[E.ei[env].scn].pump_head0;
         CK(cudaMemcpy(C.Dst, Dh.data(), Dh.size() * sizeof(double), cudaMemcpyHostToDevice));
+        std::vector<int32_t> Ih((size_t)n * L.ni, 0);
+        for (int env = 0; env < n; env++) Ih[(size_t)env * L.ni + L.eplen] = E.first_len[env];
+        CK(cudaMemcpy(C.Ist, Ih.data(), Ih.size() * sizeof(int32_t), cudaMemcpyHostToDevice));
     }
     // managed Env records
     CK(cudaMallocManaged((void**)&E.envs, sizeof(Env) * (size_t)n));
@@ -594,8 +681,14 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     for (int env = 0; env < n; env++) {
         const HostScn& s = E.hs[E.ei[env].scn];
         Env& r = E.envs[env];
+        r.agents[0].observations = obs + (size_t)env * SB_OBS;
+        r.agents[0].actions = act + (size_t)env * SB_NUM_ATNS;
+        r.agents[0].rewards = rew + env;
+        r.agents[0].terminals = term + env;
+        r.agents[0].action_mask = nullptr;
         r.num_agents = 1;
-        r.max_steps = s.max_steps;
+        r.max_steps = E.first_len[env];
+        r.start_rng = E.start_rng0[env];
         r.n_act = s.nact; r.n_cont = s.n_cont; r.n_disc = s.n_disc;
         r.loaded = 1;
         r.env_id = env;
@@ -613,17 +706,24 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     CK(cudaFuncSetAttribute(k_pre, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_pre));
     CK(cudaFuncSetAttribute(k_post, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_post));
     CK(cudaFuncSetAttribute(k_reset, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_post));
-    CK(cudaFuncSetAttribute(k_rng, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_rng));
+    if (E.smem_conv > smem_cap || E.smem_occ > smem_cap) {
+        set_err("random-stream kernels need %zu / %zu B of shared memory", E.smem_conv, E.smem_occ);
+        return false;
+    }
+    CK(cudaFuncSetAttribute(k_conv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_conv));
+    CK(cudaFuncSetAttribute(k_occ, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_occ));
     CK(cudaStreamCreateWithFlags(&E.own_stream, cudaStreamNonBlocking));
-    CK(cudaStreamCreateWithFlags(&E.side, cudaStreamNonBlocking));
     {
         int least = 0, greatest = 0;
         CK(cudaDeviceGetStreamPriorityRange(&least, &greatest));
         CK(cudaStreamCreateWithPriority(&E.hi, cudaStreamNonBlocking, greatest));
+        CK(cudaStreamCreateWithPriority(&E.rng_a, cudaStreamNonBlocking, least));
+        CK(cudaStreamCreateWithPriority(&E.rng_b, cudaStreamNonBlocking, least));
     }
     CK(cudaEventCreateWithFlags(&E.ev_fork, cudaEventDisableTiming));
     CK(cudaEventCreateWithFlags(&E.ev_join, cudaEventDisableTiming));
-    CK(cudaEventCreateWithFlags(&E.ev_solve, cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&E.ev_rng_a, cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&E.ev_rng_b, cudaEventDisableTiming));
     if (!E.stream) E.stream = E.own_stream;
     CK(cudaDeviceSynchronize());
     E.ready = true;
@@ -651,15 +751,21 @@ SnapCfg snap_cfg() {
     return c;
 }
 
+// puf_reset's device work (the stream is idle when it starts): each occupancy
+// stream draws its start day, primes and takes its first interval (slot
+// kResetSlot); the producers make the first transition's inputs; every env
+// restarts from them.
 bool do_reset(Engine& E) {
-    CK(cudaEventRecord(E.ev_fork, E.stream));
-    CK(cudaStreamWaitEvent(E.side, E.ev_fork, 0));
-    k_rng<<<(unsigned)E.sd.size(), 32, E.smem_rng, E.side>>>(E.d_ctx, E.d_scn_step, E.d_rng_out, 1);
+    k_conv<<<(unsigned)E.sd.size(), 32, E.smem_conv, E.stream>>>(E.d_ctx, 1);
+    k_occ<<<E.occ_ctas, 32 * kOccWarps, E.smem_occ, E.stream>>>(E.d_ctx, 1);
     CK(cudaGetLastError());
-    CK(cudaEventRecord(E.ev_join, E.side));
-    CK(cudaStreamWaitEvent(E.stream, E.ev_join, 0));
+    CK(cudaMemsetAsync(E.ctx.cseq, 0, sizeof(int) * E.sd.size(), E.stream));
+    CK(cudaEventRecord(E.ev_fork, E.stream));
+    CK(launch_rng(E, E.ev_fork));
     k_reset<<<(unsigned)E.n_env, 128, E.smem_post, E.stream>>>(E.d_ctx);
     CK(cudaGetLastError());
+    CK(cudaStreamWaitEvent(E.stream, E.ev_rng_a, 0));
+    CK(cudaStreamWaitEvent(E.stream, E.ev_rng_b, 0));
     CK(cudaStreamSynchronize(E.stream));
     return true;
 }
@@ -808,10 +914,6 @@ void puf_reset(Env* envs) {
     if (!g_eng || !g_eng->ready) { set_err("puf_reset: no env batch"); return; }
     Engine& E = *g_eng;
     if (cudaStreamSynchronize(E.stream) != cudaSuccess) { set_err("puf_reset: stream error"); return; }
-    if (cudaMemsetAsync(E.d_scn_step, 0, sizeof(int) * E.sd.size(), E.stream) != cudaSuccess) {
-        set_err("puf_reset: memset failed");
-        return;
-    }
     for (int env = 0; env < E.n_env; env++) {
         E.envs[env].step = 0;
         E.envs[env].ep_ret = 0.0f;
@@ -863,6 +965,10 @@ void puf_log(Log* log, Dict* out) {
     dict_set(out, "n", log->n);
 }
 
+// Step-level and per-scenario metrics since the previous call, with the
+// reference's keys (smart_buildings.cu:3069-3229); the per-scenario learning-
+// reward statistics of rew_norm / rew_center move towards this window and
+// reach the device for the next steps (one window of lag, as in the reference).
 void puf_live_log(Env* envs, Dict* out) {
     (void)envs;
     if (!g_eng || !out) return;
@@ -870,21 +976,89 @@ void puf_live_log(Env* envs, Dict* out) {
     if (cudaStreamSynchronize(E.stream) != cudaSuccess) return;
     const SnapCfg sc = snap_cfg();
     if (sc.path) sb_snapshot_write(sc.env, sc.path);
+    const size_t G = E.sd.size();
     double h[2 + kParts];
-    std::vector<double> hs(E.sd.size() * 4), he(E.sd.size() * 2);
+    std::vector<double> hs(G * 4), he(G * 2);
     cudaMemcpy(h, E.ctx.live, sizeof(h), cudaMemcpyDeviceToHost);
     cudaMemcpy(hs.data(), E.ctx.live_scn, hs.size() * sizeof(double), cudaMemcpyDeviceToHost);
     cudaMemcpy(he.data(), E.ctx.ep_scn, he.size() * sizeof(double), cudaMemcpyDeviceToHost);
     cudaMemset(E.ctx.live, 0, sizeof(h));
     cudaMemset(E.ctx.live_scn, 0, hs.size() * sizeof(double));
     cudaMemset(E.ctx.ep_scn, 0, he.size() * sizeof(double));
-    for (size_t i = 0; i < E.sd.size(); i++) {
-        if (hs[i * 4 + 2] > 0.0) {
+    if (E.ctx.znclip) {
+        double zn[3];
+        cudaMemcpy(zn, E.ctx.znclip, sizeof(zn), cudaMemcpyDeviceToHost);
+        cudaMemset(E.ctx.znclip, 0, sizeof(zn));
+        if (h[0] > 0.0) {
+            dict_set(out, "live/rew_z_gt1_frac", zn[0] / h[0]);
+            dict_set(out, "live/rew_z_gt3_frac", zn[1] / h[0]);
+            dict_set(out, "live/rew_z_gt5_frac", zn[2] / h[0]);
+        }
+    }
+    if (G > 1)
+        for (size_t i = 0; i < G; i++) {
+            if (hs[i * 4 + 2] <= 0.0) continue;
             dict_set(out, ("scenario/" + E.hs[i].name + "/reward").c_str(), hs[i * 4] / hs[i * 4 + 2]);
             dict_set(out, ("scenario/" + E.hs[i].name + "/comfort_dev_K").c_str(), hs[i * 4 + 1] / hs[i * 4 + 2]);
         }
-        if (he[i * 2 + 1] > 0.0)
-            dict_set(out, ("scenario/" + E.hs[i].name + "/episode_score").c_str(), -he[i * 2] / he[i * 2 + 1]);
+    if (E.d_rnorm) {
+        // rew_norm: mean and variance move by 0.1; rew_center: the mean by center_beta, inv_std 1
+        const double b = E.rew_center ? E.center_beta : 0.1;
+        std::vector<float> rn(2 * G);
+        double mu_sum = 0.0, sd_sum = 0.0;
+        for (size_t i = 0; i < G; i++) {
+            if (hs[i * 4 + 2] > 0.0) {
+                const double mw = hs[i * 4] / hs[i * 4 + 2];
+                E.rn_mu[i] = (1.0 - b) * E.rn_mu[i] + b * mw;
+                if (E.rew_norm) {
+                    double vw = hs[i * 4 + 3] / hs[i * 4 + 2] - mw * mw;
+                    if (vw < 1e-12) vw = 1e-12;
+                    E.rn_var[i] = (1.0 - b) * E.rn_var[i] + b * vw;
+                }
+            }
+            const double var = E.rn_var[i] < 1e-12 ? 1e-12 : E.rn_var[i];
+            rn[2 * i] = (float)E.rn_mu[i];
+            rn[2 * i + 1] = E.rew_center ? 1.0f : (float)(1.0 / std::sqrt(var));
+            mu_sum += E.rn_mu[i];
+            sd_sum += rn[2 * i + 1];
+        }
+        cudaMemcpy(E.d_rnorm, rn.data(), rn.size() * sizeof(float), cudaMemcpyHostToDevice);
+        dict_set(out, "norm/reward_mean", mu_sum / (double)G);
+        dict_set(out, "norm/reward_inv_std", sd_sum / (double)G);
+    }
+    {
+        double ss = 0.0;
+        for (size_t i = 0; i < G; i++) {
+            if (he[i * 2 + 1] > 0.0) E.last_sc[i] = -he[i * 2] / he[i * 2 + 1];
+            dict_set(out, ("scenario/" + E.hs[i].name + "/episode_score").c_str(), E.last_sc[i]);
+            ss += E.last_sc[i];
+        }
+        dict_set(out, "env/episode_score_scen_mean", ss / (double)G);
+        dict_set(out, "env/episode_score_n_scen", (double)G);
+    }
+    if (E.random_start) {
+        std::vector<double> hd(G * 2 * kStartDays), hp(G * kStartDays * 7);
+        cudaMemcpy(hd.data(), E.ctx.start_draws, hd.size() * sizeof(double), cudaMemcpyDeviceToHost);
+        cudaMemcpy(hp.data(), E.ctx.ep_start, hp.size() * sizeof(double), cudaMemcpyDeviceToHost);
+        cudaMemset(E.ctx.start_draws, 0, hd.size() * sizeof(double));
+        cudaMemset(E.ctx.ep_start, 0, hp.size() * sizeof(double));
+        static const char* cols[6] = {"score", "productivity", "energy_cost", "carbon", "elec_kwh", "gas_kwh"};
+        for (size_t i = 0; i < G; i++) {
+            const std::string base = "scenario/" + E.hs[i].name + "/start_day_";
+            for (int first = 0; first < 2; first++)
+                for (int d = 0; d < kStartDays; d++) {
+                    const double v = hd[(i * 2 + first) * kStartDays + d];
+                    if (v <= 0.0) continue;
+                    dict_set(out, (base + std::to_string(d) + (first == 0 ? "/initial_draws" : "/later_draws")).c_str(), v);
+                }
+            for (int d = 0; d < kStartDays; d++) {
+                const double* e = &hp[(i * kStartDays + d) * 7];
+                if (e[0] <= 0.0) continue;
+                dict_set(out, (base + std::to_string(d) + "/count").c_str(), e[0]);
+                for (int c = 0; c < 6; c++)
+                    dict_set(out, (base + std::to_string(d) + "/" + cols[c]).c_str(), (c == 0 ? -1.0 : 1.0) * e[c + 1] / e[0]);
+            }
+        }
     }
     const double c = h[0];
     if (c <= 0.0) return;
@@ -942,7 +1116,7 @@ void sb_shape(int* out) {
         out[5] = std::max(out[5], s.n_disc);
     }
     out[6] = (int)E.slabs.size();
-    out[7] = 5 + (int)E.dense_cls.size();
+    out[7] = 6 + (int)E.dense_cls.size();
 }
 
 void sb_env_info(int* obs_len, int* scenario) {
@@ -996,7 +1170,17 @@ int sb_get_reward_f64(double* reward, double* parts) {
     return 0;
 }
 
-int sb_kernels_per_step(void) { return 5 + (g_eng ? (int)g_eng->dense_cls.size() : 1); }
+// k_pre, k_solve x 2, k_post, k_conv, k_occ and one k_dense launch per class of equal k
+int sb_kernels_per_step(void) { return 6 + (g_eng ? (int)g_eng->dense_cls.size() : 1); }
+
+int sb_episode_options(int* first_len, unsigned long long* start_rng) {
+    if (!g_eng) return -1;
+    for (int env = 0; env < g_eng->n_env; env++) {
+        if (first_len) first_len[env] = g_eng->first_len[env];
+        if (start_rng) start_rng[env] = g_eng->start_rng0[env];
+    }
+    return 0;
+}
 
 int sb_beta_actions(const float* raw, const unsigned char* mask, float* actions, int n, float floor_c, float cap,
                     unsigned long long seed, const unsigned long long* call) {
@@ -1132,11 +1316,12 @@ int sb_snapshot_write(int env, const char* path) {
 int sb_step_timed(float* ms) {
     if (!g_eng || !g_eng->ready || !ms) return -1;
     Engine& E = *g_eng;
-    cudaEvent_t ev[9];
+    cudaEvent_t ev[10];
     for (auto& e : ev)
         if (cudaEventCreate(&e) != cudaSuccess) return -1;
-    // the step of launch_step with events around each kernel (k_solve phase 0
-    // and k_rng share their stream: ev[4] closes both)
+    // the step of launch_step with events around each kernel; the producers of
+    // the next transition run on their own streams from ev[1] (k_conv ends at
+    // ev[7], k_occ at ev[8])
     cudaEventRecord(ev[0], E.stream);
     k_pre<<<(unsigned)E.n_env, 128, E.smem_pre, E.stream>>>(E.d_ctx);
     cudaEventRecord(ev[1], E.stream);
@@ -1144,8 +1329,10 @@ int sb_step_timed(float* ms) {
     cudaStreamWaitEvent(E.hi, E.ev_fork, 0);
     const unsigned slabs = (unsigned)E.slabs.size();
     k_solve<0><<<slabs, kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
-    launch_rng_after_solve(E, E.hi, 0);
     cudaEventRecord(ev[4], E.hi);
+    launch_rng(E, E.ev_fork);
+    cudaEventRecord(ev[7], E.rng_a);
+    cudaEventRecord(ev[8], E.rng_b);
     launch_dense(E, E.hi);
     cudaEventRecord(ev[5], E.hi);
     k_solve<1><<<slabs, kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
@@ -1154,13 +1341,19 @@ int sb_step_timed(float* ms) {
     cudaEventRecord(ev[6], E.stream);
     k_post<<<(unsigned)E.n_env, 128, E.smem_post, E.stream>>>(E.d_ctx);
     cudaEventRecord(ev[3], E.stream);
-    const bool ok = cudaEventSynchronize(ev[3]) == cudaSuccess;
+    cudaStreamWaitEvent(E.stream, E.ev_rng_a, 0);
+    cudaStreamWaitEvent(E.stream, E.ev_rng_b, 0);
+    cudaEventRecord(ev[9], E.stream);
+    const bool ok = cudaEventSynchronize(ev[9]) == cudaSuccess;
     if (ok) {
-        ms[0] = -1.0f;                                 // k_rng runs beside k_solve phase 0, inside ms[4]
+        float a = 0.0f, b = 0.0f;
+        cudaEventElapsedTime(&a, ev[1], ev[7]);
+        cudaEventElapsedTime(&b, ev[1], ev[8]);
+        ms[0] = a > b ? a : b;                         // k_conv, k_occ (beside the solve)
         cudaEventElapsedTime(&ms[1], ev[0], ev[1]);   // k_pre
         cudaEventElapsedTime(&ms[2], ev[1], ev[2]);   // the solve: phase 0, k_dense, phase 1
         cudaEventElapsedTime(&ms[3], ev[6], ev[3]);   // k_post
-        cudaEventElapsedTime(&ms[4], ev[1], ev[4]);   // phase 0 (with k_rng beside it)
+        cudaEventElapsedTime(&ms[4], ev[1], ev[4]);   // phase 0
         cudaEventElapsedTime(&ms[5], ev[4], ev[5]);   // k_dense
         cudaEventElapsedTime(&ms[6], ev[5], ev[2]);   // phase 1
     }

@@ -113,6 +113,25 @@ __device__ inline void reset_state(const EnvView& v, const ScnDev& s) {
     }
 }
 
+// The consumer's side of a restart's random-start draw: the env's episode
+// offset, its Env record and the start-day statistics (smart_buildings.cu:1643-1657).
+__device__ inline void take_start(const StepCtx* ctx, int env, int scn, const EnvView& v, int off,
+                                  unsigned long long rng) {
+    const StateLayout& L = ctx->lay;
+    v.iv(L.off) = off;
+    v.iv(L.cal) = off;
+    Env* er = reinterpret_cast<Env*>(ctx->env_records) + env;
+    er->start_offset = off;
+    er->start_day = off / kStepsPerDay;
+    if (ctx->random_start) {
+        ctx->env_rng[env] = rng;
+        er->start_rng = rng;
+        atomicAdd(&ctx->start_draws[((size_t)scn * 2 + (er->start_draws == 0 ? 0 : 1)) * kStartDays + off / kStepsPerDay],
+                  1.0);
+        er->start_draws += 1;
+    }
+}
+
 // Shared-memory layout of k_post / k_reset: staging, zone scratch. Kept small
 // (the state and the field stay in global memory) so that seven 128-thread
 // CTAs fit on an SM and every env's CTA is resident in one wave.
@@ -121,7 +140,7 @@ struct PostShared {
     double* ahu;   // [3][kMaxAhu] per-AHU reward terms: intake, exhaust, cooling
     double* sc;    // [kPostScalars] reward scalars handed to the final thread
 };
-constexpr int kPostScalars = 10;
+constexpr int kPostScalars = 10;   // [0..7] reward scalars, [8] the done flag
 __host__ __device__ constexpr size_t post_smem_doubles(int ncv, int nz, int nv) {
     return (size_t)ncv + 3 * (size_t)nz + 2 * (size_t)nv + 3 * kMaxAhu + kPostScalars;
 }
@@ -139,12 +158,15 @@ __device__ inline PostShared post_shared(uint8_t* smem, int ncv, int nz, int nv)
 }
 
 // Restart one env in place: state, field, interior mass, sensing, reset
-// observation with the primed occupancy (pufferlib_cpu_env.h:187-208).
+// observation with the primed occupancy (pufferlib_cpu_env.h:187-208), at the
+// new episode's calendar offset off (random_start; else 0).
 __device__ inline void restart_env(const StepCtx* ctx, int env, const GroupDev& g, const ScnDev& s,
-                                   const EnvView& v, PostShared& p, const double* Vprime, const double* Vzero) {
+                                   const EnvView& v, PostShared& p, const double* Vprime, const double* Vzero,
+                                   int off, unsigned long long rng) {
     const StateLayout& L = ctx->lay;
     const int local = env - g.env0;
     reset_state(v, s);
+    if (threadIdx.x == 0) take_start(ctx, env, ctx->envs[env].scn, v, off, rng);
     double* Tg = g.T + (size_t)local * g.ncv;
     double* Mg = g.M + (size_t)local * g.n;
     block_copy(Tg, s.temp_init, g.ncv);
@@ -156,7 +178,7 @@ __device__ inline void restart_env(const StepCtx* ctx, int env, const GroupDev& 
     for (int z = threadIdx.x; z < s.nz; z += blockDim.x) v.d(L.zavg, z) = p.zavg[z];
     __syncthreads();
     float* o = ctx->obs + (size_t)env * kObs;
-    write_obs(v, s, 0, Vprime, o);
+    write_obs(v, s, off, Vprime, o);
     for (int z = threadIdx.x; z < s.nz; z += blockDim.x) v.d(L.V, z) = Vzero[z];
     __syncthreads();
 }
@@ -175,14 +197,19 @@ __global__ void __launch_bounds__(128) k_post(const StepCtx* __restrict__ ctx) {
     const int local = env - g.env0;
     double* Tg = g.T + (size_t)local * g.ncv;
 
+    // this transition's random inputs (produced one step ahead): slot tseq & 1
+    const int slot = v.iv(L.tseq) & 1;
+    const size_t vslot = ((size_t)slot * ctx->n_ostreams + ei.ostream) * ctx->nz_max;
     // ---- convection (sb_sim.c:489): apply this step's permutation to the
     // field in global memory, the moved values staged first ----
-    const int npairs = *s.conv_npairs;
-    for (int q = tid; q < npairs; q += blockDim.x) p.stage[q] = Tg[s.conv_pairs[2 * q + 1]];
+    const int npairs = s.conv_npairs[slot];
+    const int32_t* pairs = s.conv_pairs + (size_t)slot * s.conv_stride;
+    for (int q = tid; q < npairs; q += blockDim.x) p.stage[q] = Tg[pairs[2 * q + 1]];
     __syncthreads();
-    for (int q = tid; q < npairs; q += blockDim.x) Tg[s.conv_pairs[2 * q]] = p.stage[q];
+    for (int q = tid; q < npairs; q += blockDim.x) Tg[pairs[2 * q]] = p.stage[q];
     // ---- boiler return and setpoint ramp (sb_sim.c:491-521) ----
     const int kk = v.iv(L.step);
+    const int cal = v.iv(L.cal);
     if (tid == 0) {
         const double wcap = dmul(CP_W * RHO_W, water_flow(v, s));
         if (wcap > 0.0 && k > 0) {
@@ -214,15 +241,18 @@ __global__ void __launch_bounds__(128) k_post(const StepCtx* __restrict__ ctx) {
         v.d(L.b_cur) = cur;
         v.d(L.b_step) = dsub(cur, begin);
         v.iv(L.step) = kk + 1;
+        v.iv(L.cal) = cal + 1;
+        v.iv(L.tseq) += 1;
     }
     __syncthreads();
-    const int j = kk + 1;   // observation and reward index of this transition
+    const int j = kk + 1;     // episode step after this transition
+    const int jc = cal + 1;   // its calendar row: observation and reward index
     const double* Vin = v.D + L.V;
-    const double* Vst = ctx->V_step + (size_t)ei.scn * ctx->nz_max;
+    const double* Vst = ctx->V_step + vslot;
 
     // ---- observation at ts_j with the interval that just ran (pufferlib_cpu_env.h:237-239) ----
     float* o = ctx->obs + (size_t)env * kObs;
-    write_obs(v, s, j, Vin, o);
+    write_obs(v, s, jc, Vin, o);
 
     // ---- reward (sb_reward.c:31-155) ----
     // zone means (sb_sim.c:149-160): the field copied into room order (p.stage
@@ -246,7 +276,7 @@ __global__ void __launch_bounds__(128) k_post(const StepCtx* __restrict__ ctx) {
         p.zavg[z] = ddiv(sum, (double)(b - a));
     }
     __syncthreads();
-    const double hsp = s.s_heat[j], csp = s.s_cool[j];
+    const double hsp = s.s_heat[jc], csp = s.s_cool[jc];
     const double dt = s.dt, inv_hour = 1.0 / 3600.0;
     const double max_pph = s.rw[0], min_pph = s.rw[1], ref = s.rw[2];
     for (int z = tid; z < nz; z += blockDim.x) {
@@ -292,7 +322,7 @@ __global__ void __launch_bounds__(128) k_post(const StepCtx* __restrict__ ctx) {
     // the reward's independent terms in parallel: per AHU (its VAVs in ascending
     // order), boiler and pump, and the two zone sums; the final thread adds them
     // up in the reference's order
-    const double ambient = s.amb[j];
+    const double ambient = s.amb[jc];
     if (tid < na) {
         const int a = tid;
         double ws = 0.0, at = 0.0;
@@ -363,7 +393,7 @@ __global__ void __launch_bounds__(128) k_post(const StepCtx* __restrict__ ctx) {
     }
     __syncthreads();
     if (tid == 0) {
-        const int hour = (int)s.r_hour[j], month = (int)s.r_month[j], wd = (int)s.r_wd[j];
+        const int hour = (int)s.r_hour[jc], month = (int)s.r_month[jc], wd = (int)s.r_wd[jc];
         double intake = 0.0, exhaust = 0.0, cooling = 0.0;
         for (int a = 0; a < na; a++) {
             intake = dadd(intake, p.ahu[a]);
@@ -409,12 +439,24 @@ __global__ void __launch_bounds__(128) k_post(const StepCtx* __restrict__ ctx) {
 
         // ---- finalize (smart_buildings.cu:1936-2050) ----
         const float r = (float)rew;
-        ctx->rewards[env] = r * ctx->reward_scale;
+        if (ctx->rnorm) {   // rew_norm / rew_center: the learning signal only; logs keep r
+            const float* rn = ctx->rnorm + 2 * (size_t)ei.scn;
+            const float z = (r - rn[0]) * rn[1];
+            ctx->rewards[env] = z;
+            if (ctx->znclip) {
+                const float az = fabsf(z);
+                if (az > 1.0f) atomicAdd(&ctx->znclip[0], 1.0);
+                if (az > 3.0f) atomicAdd(&ctx->znclip[1], 1.0);
+                if (az > 5.0f) atomicAdd(&ctx->znclip[2], 1.0);
+            }
+        } else {
+            ctx->rewards[env] = r * ctx->reward_scale;
+        }
         ctx->rew_f64[env] = rew;
         for (int q = 0; q < kParts; q++) ctx->parts_out[(size_t)env * kParts + q] = parts[q];
         Env* er = reinterpret_cast<Env*>(ctx->env_records) + env;
         er->step = j;
-        const bool done = j >= s.max_steps;
+        const bool done = j >= v.iv(L.eplen);
         ctx->terminals[env] = done ? 1.0f : 0.0f;
         er->ep_ret += r;
         ctx->epret_d[env] += rew;
@@ -429,35 +471,52 @@ __global__ void __launch_bounds__(128) k_post(const StepCtx* __restrict__ ctx) {
         atomicAdd(&ls[2], 1.0);
         atomicAdd(&ls[3], (double)r * (double)r);
         if (done) {
+            // only whole episodes enter the log: a first episode cut short by
+            // desync is a truncation
             const float st = (float)j;
-            const float mean = er->ep_ret / st;
-            atomicAdd(&ctx->ep_scn[(size_t)ei.scn * 2], ctx->epret_d[env] / (double)j);
-            atomicAdd(&ctx->ep_scn[(size_t)ei.scn * 2 + 1], 1.0);
-            er->log.perf += mean;
-            er->log.score += mean;
-            er->log.episode_return += er->ep_ret;
-            er->log.episode_length += st;
-            er->log.productivity += er->ep_part[0] / st;
-            er->log.energy_cost_norm += er->ep_part[1] / st;
-            er->log.carbon_norm += er->ep_part[2] / st;
-            er->log.comfort_dev_K += er->ep_part[3] / st;
-            er->log.worst_dev_K += er->ep_worst;
-            er->log.out_of_band_frac += er->ep_part[5] / st;
-            er->log.elec_kwh += er->ep_part[6];
-            er->log.gas_kwh += er->ep_part[7];
-            er->log.n += 1.0f;
+            if (j >= s.max_steps) {
+                const float mean = er->ep_ret / st;
+                const double mean_d = ctx->epret_d[env] / (double)j;
+                atomicAdd(&ctx->ep_scn[(size_t)ei.scn * 2], mean_d);
+                atomicAdd(&ctx->ep_scn[(size_t)ei.scn * 2 + 1], 1.0);
+                if (ctx->random_start) {
+                    double* es = ctx->ep_start + ((size_t)ei.scn * kStartDays + v.iv(L.off) / kStepsPerDay) * 7;
+                    atomicAdd(&es[0], 1.0);
+                    atomicAdd(&es[1], mean_d);
+                    for (int q = 0; q < 3; q++) atomicAdd(&es[2 + q], (double)(er->ep_part[q] / st));
+                    atomicAdd(&es[5], (double)er->ep_part[6]);
+                    atomicAdd(&es[6], (double)er->ep_part[7]);
+                }
+                er->log.perf += mean;
+                er->log.score += mean;
+                er->log.episode_return += er->ep_ret;
+                er->log.episode_length += st;
+                er->log.productivity += er->ep_part[0] / st;
+                er->log.energy_cost_norm += er->ep_part[1] / st;
+                er->log.carbon_norm += er->ep_part[2] / st;
+                er->log.comfort_dev_K += er->ep_part[3] / st;
+                er->log.worst_dev_K += er->ep_worst;
+                er->log.out_of_band_frac += er->ep_part[5] / st;
+                er->log.elec_kwh += er->ep_part[6];
+                er->log.gas_kwh += er->ep_part[7];
+                er->log.n += 1.0f;
+            }
+            er->max_steps = s.max_steps;   // every later episode has the scenario's full length
+            v.iv(L.eplen) = s.max_steps;
             er->ep_ret = 0.0f;
             ctx->epret_d[env] = 0.0;
             for (int q = 0; q < kParts; q++) er->ep_part[q] = 0.0f;
             er->ep_worst = 0.0f;
             er->step = 0;
         }
+        p.sc[8] = done ? 1.0 : 0.0;
     }
     __syncthreads();
-    const bool done = j >= s.max_steps;
+    const bool done = p.sc[8] != 0.0;
     if (done) {
-        restart_env(ctx, env, g, s, v, p, ctx->V_prime + (size_t)ei.scn * ctx->nz_max,
-                    ctx->V_zero + (size_t)ei.scn * ctx->nz_max);
+        const size_t so = (size_t)slot * ctx->n_ostreams + ei.ostream;
+        restart_env(ctx, env, g, s, v, p, ctx->V_prime + vslot, ctx->V_zero + vslot, ctx->new_off[so],
+                    ctx->new_rng[so]);
     } else {
         for (int z = tid; z < nz; z += blockDim.x) v.d(L.V, z) = Vst[z];
     }
@@ -513,7 +572,7 @@ __global__ void __launch_bounds__(128) k_snapshot(const StepCtx* __restrict__ ct
     }
 }
 
-// Explicit restart of every env (puf_reset), after k_rng ran in reset mode.
+// Explicit restart of every env (puf_reset), after k_occ ran in reset mode.
 __global__ void __launch_bounds__(128) k_reset(const StepCtx* __restrict__ ctx) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int env = blockIdx.x;
@@ -532,10 +591,12 @@ __global__ void __launch_bounds__(128) k_reset(const StepCtx* __restrict__ ctx) 
         er->ep_worst = 0.0f;
         for (int q = 0; q < kParts; q++) er->ep_part[q] = 0.0f;
         ctx->epret_d[env] = 0.0;
+        v.iv(L.tseq) = 0;
     }
     __syncthreads();
-    restart_env(ctx, env, g, s, v, p, ctx->V_prime + (size_t)ei.scn * ctx->nz_max,
-                ctx->V_zero + (size_t)ei.scn * ctx->nz_max);
+    const size_t so = (size_t)kResetSlot * ctx->n_ostreams + ei.ostream;
+    const size_t vslot = so * ctx->nz_max;
+    restart_env(ctx, env, g, s, v, p, ctx->V_prime + vslot, ctx->V_zero + vslot, ctx->new_off[so], ctx->new_rng[so]);
 }
 
 }  // namespace sbenv

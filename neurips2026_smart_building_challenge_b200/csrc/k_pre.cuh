@@ -164,7 +164,7 @@ __global__ void __launch_bounds__(128) k_pre(const StepCtx* __restrict__ ctx) {
     double* fdv = rw + k;                             // [k]
 
     __syncthreads();
-    const int kk = v.iv(L.step);
+    const int kk = v.iv(L.cal);   // calendar row of this step
     const double ambient = s.amb[kk];
     const int comfort = s.s_comf[kk] != 0.0;
 

@@ -603,8 +603,8 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
     if (tid < nenv) {
         const int env = sd.env0 + tid;
         const ScnDev& sc = ctx->scns[ctx->envs[env].scn];
-        const int step = ctx->Ist[(size_t)env * L.ni + L.step];
-        amb_e[tid] = sc.amb[step];
+        const int cal = ctx->Ist[(size_t)env * L.ni + L.cal];   // calendar row of this step
+        amb_e[tid] = sc.amb[cal];
         const double* D = ctx->Dst + (size_t)env * L.nd;
         int act = 0;
         for (int c = 0; c < k; c++)

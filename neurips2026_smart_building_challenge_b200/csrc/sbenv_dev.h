@@ -245,12 +245,19 @@ struct ScnDev {
     const double *f_mean, *f_var;
     const double *rw, *e_wd, *e_we, *e_c, *g_p;
     const double *temp_init, *mass_init;   // extended row order / row order
-    // random streams (per scenario): MT19937 raw state + position
+    // occupancy priming calendar: the hour / workday of the interval before
+    // calendar row r (m1_rows entries; one entry unless the blob carries them
+    // per row for random starts)
+    const int64_t* o_hour_m1;
+    const uint8_t* o_wd_m1;
+    int m1_rows;
+    // convection stream (per scenario): MT19937 raw state + position, and its
+    // swap lists of the next two transitions (slot q & 1 for transition q)
     uint32_t* conv_mt;   // 625 words: 624 state + position
-    uint32_t* occ_mt;    // [2][625] double-buffered by env generation parity
-    int* occ_state0;     // [2][nz*assign] occupant states, same buffering
-    int32_t* conv_pairs; // [2*ncv]: (dst, src) extended positions
-    int* conv_npairs;
+    uint32_t* conv_ckpt; // 625 words: the state before the last transition produced
+    int32_t* conv_pairs; // [2][conv_stride]: (dst, src) extended positions
+    int* conv_npairs;    // [2]
+    int conv_stride;     // 2 * ncv + 2
     int scn_index;
 };
 
@@ -265,12 +272,24 @@ struct StateLayout {
     int ff_sum, pump_head, b_sp, b_ret, b_cur, b_step, reheat_w;
     int ahu_run, ahu_creq, v_mode, v_prev, v_dset, v_rset;
     int hws_req, hws_run, pump_run, step, gen, active;
+    int cal;       // calendar row of the current step (episode offset + step)
+    int off;       // calendar offset of the current episode
+    int eplen;     // length of the current episode
+    int tseq;      // transitions since the last puf_reset (slot parity)
 };
 
 struct EnvIndex {   // global env -> its group and scenario
     int group, scn, local;   // local: index inside the group
-    int writer;              // 1: this env writes its scenario's next occupancy stream
+    int ostream;             // the env's occupancy stream (its scenario's, or its own)
 };
+
+// Random inputs are produced one transition ahead of their consumer (k_conv /
+// k_occ on their own streams, beside the whole step): transition q (counted
+// from puf_reset) uses slot q & 1; slot 2 holds what puf_reset consumes.
+constexpr int kRngSlots = 3;
+constexpr int kResetSlot = 2;
+constexpr int kStartDays = 7;
+constexpr int kStepsPerDay = 288;
 
 // Everything one step launch needs; copied to device memory once.
 struct StepCtx {
@@ -296,11 +315,44 @@ struct StepCtx {
     double* live_scn;     // [n_scns][4]: reward, mean deviation, count, reward^2
     double* ep_scn;       // [n_scns][2]: completed-episode mean rewards, count
     int* status;          // device error word
-    // per-scenario random-stream results of the current step
-    const double* V_step;   // [n_scns][nz_max]
-    const double* V_prime;
-    const double* V_zero;
+    // occupancy streams: one per scenario while its envs step in lock step,
+    // one per env with desync or random_start (complete_port/csim/sb_occup.c;
+    // the reference GPU backend keeps one per env, gpu/sb_gpu_kernels.cuh:385-422)
+    int n_ostreams, ostream_per_env, random_start;
+    const int* ostream_scn;     // [n_ostreams] the stream's scenario
+    uint32_t* occ_mt;           // [n_ostreams][625] MT19937 state + position
+    int* occ_state;             // [n_ostreams][occ_stride] occupant states
+    int occ_stride;
+    int* ostep;                 // [n_ostreams] producer: step in the current episode
+    int* oeplen;                // [n_ostreams] producer: current episode's length
+    int* ooff;                  // [n_ostreams] producer: current episode's calendar offset
+    int* oseq;                  // [n_ostreams] transitions produced since puf_reset
+    unsigned long long* orng;   // [n_ostreams] producer: random-start stream
+    // each stream's MT state and occupant states before its last production
+    // (a transition produced ahead and never consumed is undone by puf_reset;
+    // the episode counters restart from the consumer's then)
+    uint32_t* ck_mt;            // [n_ostreams][625]
+    int* ck_state;              // [n_ostreams][occ_stride]
+    int* produced;              // 1 once a transition was produced since creation
+    int* cseq;                  // [n_scns] convection transitions produced since creation
+    // producer outputs, [kRngSlots][n_ostreams]...: occupancy after the
+    // transition (reward), of the priming interval (reset observation), of
+    // the new episode's first interval, and the new episode's offset and
+    // random-start stream state
+    double* V_step;             // [slot][n_ostreams][nz_max]
+    double* V_prime;
+    double* V_zero;
+    int* new_off;               // [slot][n_ostreams]
+    unsigned long long* new_rng;// [slot][n_ostreams]
     int nz_max;
+    unsigned long long* env_rng;// [n_env] the consumer's random-start stream state
+    double* start_draws;        // [n_scns][2][kStartDays] start days drawn (first draw, later)
+    double* ep_start;           // [n_scns][kStartDays][7] whole episodes by start day
+    int full_len_max;           // longest episode length (calendar rows needed)
+    // learning-reward normalisation (rew_norm / rew_center): per scenario
+    // (mean, inv_std); null: rewards scaled by reward_scale
+    const float* rnorm;
+    double* znclip;             // [3] rewards beyond 1 / 3 / 5 (rew_norm only)
     // air side: per env the dense system's right side (k_solve phase 0), then
     // its solution (k_dense), read by k_solve phase 1
     double* airq;           // [n_env][k_max]

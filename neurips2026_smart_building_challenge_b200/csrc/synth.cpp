@@ -235,6 +235,8 @@ std::string build(const SbGenParams& P, Built& out) {
     if (R < 4 || C < 4 || P.n_rooms < 1 || P.n_ahu < 1 || P.n_ahu > P.n_rooms)
         return "invalid grid/room/AHU counts";
     if (P.n_steps < 1 || P.dt_sec <= 0.0) return "invalid episode length";
+    if (P.random_start_days != 0 && (P.random_start_days != 7 || P.dt_sec != 300.0))
+        return "random_start_days must be 0 or 7 (with 300 s steps)";
     Rng rng(P.layout_seed);
     const double cv = P.cv_size_cm / 100.0;
     const double a_cell = cv * cv;
@@ -412,11 +414,13 @@ std::string build(const SbGenParams& P, Built& out) {
     // weather first: exterior cells start at the first ambient value
     Rng wr(P.climate_seed);
     const long T = P.n_steps;
-    std::vector<double> amb(T + 1);
+    // calendar rows beyond the episode: random starts begin up to six days in
+    const long TR = T + (P.random_start_days > 0 ? 6L * 288 : 0L);
+    std::vector<double> amb(TR + 1);
     {
         const double sd_innov = P.ar_sigma_k * std::sqrt(std::max(0.0, 1.0 - P.ar_phi * P.ar_phi));
         double ar = P.ar_sigma_k * wr.normal();
-        for (long s = 0; s <= T; s++) {
+        for (long s = 0; s <= TR; s++) {
             if (s > 0) ar = P.ar_phi * ar + sd_innov * wr.normal();
             Calendar c = calendar_at(P, s);
             amb[s] = 273.15 + P.t_mean_c + P.t_amp_k * std::sin(2.0 * kPi * (c.hod - 9.0) / 24.0) + ar;
@@ -690,11 +694,11 @@ std::string build(const SbGenParams& P, Built& out) {
 
     // --- calendars, schedules, weather ---
     {
-        std::vector<double> aux((size_t)(T + 1) * (n_aux - 1));
-        std::vector<double> sc(T + 1), sh(T + 1), sco(T + 1);
-        std::vector<int64_t> oh(T + 1), rh(T + 1), rm(T + 1);
-        std::vector<uint8_t> ow(T + 1), rw(T + 1);
-        for (long s = 0; s <= T; s++) {
+        std::vector<double> aux((size_t)(TR + 1) * (n_aux - 1));
+        std::vector<double> sc(TR + 1), sh(TR + 1), sco(TR + 1);
+        std::vector<int64_t> oh(TR + 1), rh(TR + 1), rm(TR + 1);
+        std::vector<uint8_t> ow(TR + 1), rw(TR + 1);
+        for (long s = 0; s <= TR; s++) {
             Calendar c = calendar_at(P, s);
             bool cm = comfort_at(P, 0.0, s);
             double* a = &aux[(size_t)s * (n_aux - 1)];
@@ -713,19 +717,32 @@ std::string build(const SbGenParams& P, Built& out) {
             rm[s] = c.month;
             rw[s] = c.workday ? 1 : 0;
         }
-        w.add("aux_time", sbb::F64, aux.data(), {(uint64_t)(T + 1), (uint64_t)(n_aux - 1)});
+        w.add("aux_time", sbb::F64, aux.data(), {(uint64_t)(TR + 1), (uint64_t)(n_aux - 1)});
         w.add_f64("obs_meta", {1.0, 1.0, 1.0, (double)T, P.dt_sec});
         w.add_f64("sched_comfort", sc);
         w.add_f64("sched_heat_sp", sh);
         w.add_f64("sched_cool_sp", sco);
         w.add_f64("weather_ambient", amb);
-        std::vector<double> wconv(T, h_conv);
+        std::vector<double> wconv(TR, h_conv);
         w.add_f64("weather_convection", wconv);
         w.add_i64("occ_hour", oh);
         w.add_u8("occ_workday", ow);
-        Calendar cm1 = calendar_at(P, -1);
-        w.add_i64("occ_hour_m1", {cm1.hour});
-        w.add_u8("occ_workday_m1", {(uint8_t)(cm1.workday ? 1 : 0)});
+        // the interval before each possible episode start: one entry, or one per
+        // calendar row for random starts
+        std::vector<int64_t> hm1;
+        std::vector<uint8_t> wm1;
+        for (long r = 0; r <= (P.random_start_days > 0 ? TR : 0); r++) {
+            Calendar cm1 = calendar_at(P, r - 1);
+            hm1.push_back(cm1.hour);
+            wm1.push_back((uint8_t)(cm1.workday ? 1 : 0));
+        }
+        w.add_i64("occ_hour_m1", hm1);
+        w.add_u8("occ_workday_m1", wm1);
+        if (P.random_start_days > 0) {
+            std::vector<int64_t> offs;
+            for (int d = 0; d < P.random_start_days; d++) offs.push_back((int64_t)d * 288);
+            w.add_i64("random_start_offsets", offs);
+        }
         w.add_i64("rew_hour", rh);
         w.add_i64("rew_month", rm);
         w.add_u8("rew_workday", rw);

@@ -301,7 +301,8 @@ std::string build_group(const sbb::Reader& b, HostGroup& g) {
     return "";
 }
 
-std::string build_scenario(const sbb::Reader& b, const HostGroup& g, int max_steps_kw, HostScn& s) {
+std::string build_scenario(const sbb::Reader& b, const HostGroup& g, int max_steps_kw, bool random_start,
+                           HostScn& s) {
     s.path = b.path();
     {
         const size_t sl = s.path.find_last_of('/');
@@ -426,7 +427,19 @@ std::string build_scenario(const sbb::Reader& b, const HostGroup& g, int max_ste
         if (max_steps_kw > 0 && max_steps_kw < ep) ep = max_steps_kw;
     }
     s.max_steps = ep;
-    const uint64_t rows = (uint64_t)ep + 1;
+    // calendar rows the episodes read: random starts begin up to six days in
+    const uint64_t rows = (uint64_t)ep + 1 + (random_start ? (uint64_t)6 * kStepsPerDay : 0);
+    if (random_start) {
+        const int64_t* off = b.i64("random_start_offsets");
+        const double* op5 = b.f64("occ_params");
+        if (!off || b.count("random_start_offsets") != (uint64_t)kStartDays || !op5 || b.count("occ_params") < 6 ||
+            op5[5] != 300.0)
+            return "random_start needs a seven-day random-start blob with five-minute steps";
+        for (int d = 0; d < kStartDays; d++)
+            if (off[d] != (int64_t)d * kStepsPerDay) return "random_start_offsets malformed";
+        if (b.count("occ_hour_m1") < rows || b.count("occ_workday_m1") < rows)
+            return "random_start section occ_hour_m1 / occ_workday_m1 too short";
+    }
     auto need_rows = [&](const char* nm) { return b.count(nm) >= rows; };
     for (const char* nm : {"weather_ambient", "sched_comfort", "sched_heat_sp", "sched_cool_sp", "occ_hour",
                            "occ_workday", "rew_hour", "rew_month", "rew_workday"})
@@ -477,6 +490,13 @@ std::string build_scenario(const sbb::Reader& b, const HostGroup& g, int max_ste
     {
         const uint8_t* wm = b.u8("occ_workday_m1");
         s.wd_m1 = wm ? wm[0] : 0;
+    }
+    if (random_start) {
+        s.o_hour_m1 = vec(b.i64("occ_hour_m1"), rows);
+        s.o_wd_m1 = vec(b.u8("occ_workday_m1"), rows);
+    } else {
+        s.o_hour_m1.assign(1, s.hour_m1);
+        s.o_wd_m1.assign(1, (uint8_t)s.wd_m1);
     }
     s.occ_seed = (uint32_t)b.i64_1("occ_seed", 17321);
     // convection

@@ -53,6 +53,8 @@ struct HostScn {
     std::vector<double> f_mean, f_var;
     std::vector<double> rw, e_wd, e_we, e_c, g_p;
     std::vector<double> temp_init, mass_init;   // extended row order / row order
+    std::vector<int64_t> o_hour_m1;             // priming hour per calendar row (or one entry)
+    std::vector<uint8_t> o_wd_m1;
     int obs_len() const { return n_dev + n_aux; }
 };
 
@@ -66,7 +68,11 @@ std::string build_sweeps(HostGroup& g, int ring_stages);
 // Builds the folded air side's Z = L^-1 applied and R = sensed U^-1 (row order).
 std::string build_fold(HostGroup& g);
 // Builds the per-scenario tables (needs the group's position maps).
-std::string build_scenario(const sbb::Reader& b, const HostGroup& g, int max_steps_kw, HostScn& s);
+// random_start: the blob must carry the seven start offsets (d * 288) and
+// calendar tables 6 * 288 rows longer than the episode
+// (complete_port/gpu/smart_buildings.cu:2460-2495).
+std::string build_scenario(const sbb::Reader& b, const HostGroup& g, int max_steps_kw, bool random_start,
+                           HostScn& s);
 // True when b can share a's group: every geometry / solver section identical.
 bool same_geometry(const sbb::Reader& a, const sbb::Reader& b);
 

@@ -30,6 +30,10 @@ struct SboEnv {
     SbSim sim;
     const uint8_t* is_disc;
     int n_act, n_cont, n_disc, obs_len, step, max_steps;
+    int cur_len, off, random_start, m1_rows;
+    unsigned long long start_rng;
+    const int64_t* hour_m1;
+    const uint8_t* wd_m1;
     double cont[SBO_CONT], disc[SBO_DISC], native[SBO_NACT], parts[12];
 };
 
@@ -62,8 +66,25 @@ SboEnv* sbo_create(const char* path, int max_steps) {
         }
     }
     e->max_steps = max_steps;
+    e->cur_len = max_steps;
+    /* the priming hour per calendar row, where the blob carries it for random starts */
+    e->hour_m1 = sb_i64(&e->blob, "occ_hour_m1");
+    e->wd_m1 = sb_u8(&e->blob, "occ_workday_m1");
+    {
+        const SbSection* h = sb_find(&e->blob, "occ_hour_m1");
+        const SbSection* w = sb_find(&e->blob, "occ_workday_m1");
+        e->m1_rows = (h && w && e->hour_m1 && e->wd_m1) ? (int)(h->count < w->count ? h->count : w->count) : 0;
+    }
     return e;
 }
+
+void sbo_set_episode(SboEnv* e, int first_len, unsigned long long start_rng, int random_start) {
+    e->cur_len = first_len > 0 ? first_len : e->max_steps;
+    e->start_rng = start_rng;
+    e->random_start = random_start;
+}
+
+int sbo_episode_offset(const SboEnv* e) { return e->off; }
 
 void sbo_destroy(SboEnv* e) {
     if (!e) return;
@@ -87,12 +108,18 @@ static void write_obs(SboEnv* e, int j, float* obs) {
 }
 
 void sbo_reset(SboEnv* e, float* obs) {
+    e->off = e->random_start ? SBO_DAY_STEPS * sbo_start_draw(&e->start_rng) : 0;
     sb_sim_reset(&e->sim, &e->blob);
+    e->sim.step_index = e->off;   /* the calendar row the simulator reads */
+    if (e->off < e->m1_rows) {
+        e->occ.hour_m1 = (int)e->hour_m1[e->off];
+        e->occ.workday_m1 = e->wd_m1[e->off];
+    }
     sb_occup_prime(&e->occ);
     e->step = 0;
     for (int i = 0; i < e->n_act; i++) e->native[i] = 0.0;
-    write_obs(e, 0, obs);
-    sb_occup_advance(&e->occ, 0);
+    write_obs(e, e->off, obs);
+    sb_occup_advance(&e->occ, e->off);
 }
 
 void sbo_step(SboEnv* e, const float* act, float* obs, float* reward, float* terminal,
@@ -111,15 +138,16 @@ void sbo_step(SboEnv* e, const float* act, float* obs, float* reward, float* ter
     sb_sim_apply_native(s, e->native);
     sb_sim_step(s, e->occ.V);
     e->step += 1;
-    write_obs(e, e->step, obs);
-    sb_occup_advance(&e->occ, e->step);
-    double rew = sb_reward(s, e->occ.V, e->step, e->parts);
+    const int j = e->off + e->step;   /* calendar row */
+    write_obs(e, j, obs);
+    sb_occup_advance(&e->occ, j);
+    double rew = sb_reward(s, e->occ.V, j, e->parts);
     if (reward) *reward = (float)rew;
     if (reward_f64) *reward_f64 = rew;
     if (parts12) memcpy(parts12, e->parts, sizeof(e->parts));
     if (log8) {
         /* sb_reward leaves the post-step zone means in s->avg_temp */
-        const int kv = e->step;
+        const int kv = j;
         const double hsp = s->sched_heat_sp[kv], csp = s->sched_cool_sp[kv];
         double dsum = 0.0, dmax = 0.0;
         int oob = 0;
@@ -141,9 +169,12 @@ void sbo_step(SboEnv* e, const float* act, float* obs, float* reward, float* ter
         log8[6] = fabs(elec_rate) * s->dt_sec / 3.6e6;
         log8[7] = NAN;  /* the gas rate is internal to sb_reward */
     }
-    const int done = e->step >= e->max_steps;
+    const int done = e->step >= e->cur_len;
     if (terminal) *terminal = done ? 1.0f : 0.0f;
-    if (done) sbo_reset(e, obs);
+    if (done) {
+        e->cur_len = e->max_steps;   /* every later episode is whole */
+        sbo_reset(e, obs);
+    }
 }
 
 void sbo_get_temp(const SboEnv* e, double* out) {

@@ -28,6 +28,19 @@ extern "C" {
 #define SBO_CONT 256
 #define SBO_DISC 16
 #define SBO_NACT (SBO_CONT + SBO_DISC)
+#define SBO_DAY_STEPS 288
+
+/* The env's start-day stream: SplitMix64's output function (Steele, Lea and
+ * Flood, OOPSLA 2014) over a golden-ratio increment. */
+static inline unsigned long long sbo_start_mix(unsigned long long x) {
+    x = (x ^ (x >> 30)) * 0xbf58476d1ce4e5b9ULL;
+    x = (x ^ (x >> 27)) * 0x94d049bb133111ebULL;
+    return x ^ (x >> 31);
+}
+static inline int sbo_start_draw(unsigned long long* rng) {
+    *rng += 0x9e3779b97f4a7c15ULL;
+    return (int)(sbo_start_mix(*rng) % 7ULL);
+}
 
 typedef struct SboEnv SboEnv;
 
@@ -50,6 +63,15 @@ int sbo_step_index(const SboEnv* e);               /* steps in the current episo
 /* Re-seeds the occupancy and convection generators from the blob (tests that
  * compare two passes of one env need identical random streams). */
 void sbo_reseed(SboEnv* e);
+/* Episode options of the reference GPU backend (gpu/smart_buildings.cu:1636-1657,
+ * 2806-2816, 1936-2050), which its CPU env lacks: the first episode's length
+ * (desync; <= 0 keeps the blob's), and random starts -- at every reset the
+ * SplitMix64 stream start_rng draws a day d in 0..6 and the episode runs from
+ * calendar row d * 288 (priming with that row's occ_hour_m1 entry when the
+ * blob has one per row). Call before the first reset. */
+void sbo_set_episode(SboEnv* e, int first_len, unsigned long long start_rng, int random_start);
+/* Calendar offset of the current episode. */
+int sbo_episode_offset(const SboEnv* e);
 /* Inspection (restatement only): out = [air_g k][air_T k][per-cell zone heat nz]
  * [flow factor sum, reheat W, boiler T, boiler return, pump head] of the last step. */
 int sbo_debug(const SboEnv* e, double* out);

@@ -10,6 +10,10 @@
 struct SboEnv {
     SboScn scn;
     SboState st;
+    int cur_len;                 /* this episode's length (desync cuts the first) */
+    int off;                     /* this episode's calendar offset */
+    int random_start;
+    unsigned long long start_rng;
 };
 
 SboEnv* sbo_create(const char* path, int max_steps) {
@@ -22,8 +26,17 @@ SboEnv* sbo_create(const char* path, int max_steps) {
         return NULL;
     }
     sbo_state_alloc(&e->st, &e->scn);
+    e->cur_len = e->scn.max_steps;
     return e;
 }
+
+void sbo_set_episode(SboEnv* e, int first_len, unsigned long long start_rng, int random_start) {
+    e->cur_len = first_len > 0 ? first_len : e->scn.max_steps;
+    e->start_rng = start_rng;
+    e->random_start = random_start;
+}
+
+int sbo_episode_offset(const SboEnv* e) { return e->off; }
 
 void sbo_destroy(SboEnv* e) {
     if (!e) return;
@@ -44,12 +57,19 @@ static void write_obs(SboEnv* e, int j, float* obs) {
 }
 
 void sbo_reset(SboEnv* e, float* obs) {
-    sbo_sim_reset(&e->st, &e->scn);
-    sbo_occ_advance(&e->st, &e->scn, e->scn.hour_m1, e->scn.wd_m1);   /* prime [ts_-1, ts_0) */
+    const SboScn* s = &e->scn;
+    e->off = e->random_start ? SBO_DAY_STEPS * sbo_start_draw(&e->start_rng) : 0;
+    const int off = e->off;
+    sbo_sim_reset(&e->st, s);
+    e->st.step_index = off;
+    if (off > 0 && off < s->m1_rows)   /* prime [ts_off-1, ts_off) */
+        sbo_occ_advance(&e->st, s, (int)s->o_hour_m1[off], (int)s->o_wd_m1[off]);
+    else
+        sbo_occ_advance(&e->st, s, s->hour_m1, s->wd_m1);
     e->st.step = 0;
     memset(e->st.native, 0, sizeof(e->st.native));
-    write_obs(e, 0, obs);
-    sbo_occ_advance(&e->st, &e->scn, (int)e->scn.o_hour[0], (int)e->scn.o_wd[0]);
+    write_obs(e, off, obs);
+    sbo_occ_advance(&e->st, s, (int)s->o_hour[off], (int)s->o_wd[off]);
 }
 
 void sbo_step(SboEnv* e, const float* act, float* obs, float* reward, float* terminal,
@@ -60,14 +80,18 @@ void sbo_step(SboEnv* e, const float* act, float* obs, float* reward, float* ter
     sbo_apply_native(st, s, st->native);
     sbo_sim_step(st, s);
     st->step += 1;
-    write_obs(e, st->step, obs);
-    sbo_occ_advance(st, s, (int)s->o_hour[st->step], (int)s->o_wd[st->step]);
-    const double rew = sbo_reward(st, s, st->step, parts12, log8);
+    const int j = e->off + st->step;   /* calendar row */
+    write_obs(e, j, obs);
+    sbo_occ_advance(st, s, (int)s->o_hour[j], (int)s->o_wd[j]);
+    const double rew = sbo_reward(st, s, j, parts12, log8);
     if (reward) *reward = (float)rew;
     if (reward_f64) *reward_f64 = rew;
-    const int done = st->step >= s->max_steps;
+    const int done = st->step >= e->cur_len;
     if (terminal) *terminal = done ? 1.0f : 0.0f;
-    if (done) sbo_reset(e, obs);
+    if (done) {
+        e->cur_len = s->max_steps;   /* every later episode is whole */
+        sbo_reset(e, obs);
+    }
 }
 
 void sbo_get_temp(const SboEnv* e, double* out) {

@@ -75,6 +75,9 @@ typedef struct {
     const uint8_t* r_wd;
     /* occupancy */
     int assign, ea, la, ed, ld, hour_m1, wd_m1;
+    const int64_t* o_hour_m1;   /* priming hour per calendar row (m1_rows entries) */
+    const uint8_t* o_wd_m1;
+    int m1_rows;
     double p_arr, p_dep;
     const int64_t* o_hour;
     const uint8_t* o_wd;

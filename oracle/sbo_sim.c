@@ -172,6 +172,10 @@ int sbo_scn_load(SboScn* s, const char* path, int max_steps) {
         const uint8_t* wm = GETB("occ_workday_m1");
         s->wd_m1 = wm ? wm[0] : 0;
     }
+    s->o_hour_m1 = GETL("occ_hour_m1");
+    s->o_wd_m1 = GETB("occ_workday_m1");
+    s->m1_rows = (s->o_hour_m1 && s->o_wd_m1) ? cnt(s, "occ_hour_m1") : 0;
+    if (s->o_wd_m1 && cnt(s, "occ_workday_m1") < s->m1_rows) s->m1_rows = cnt(s, "occ_workday_m1");
     s->occ_seed = (uint32_t)sbo_blob_i64_1(&s->blob, "occ_seed", 17321);
     /* convection (sb_convect.c:6-30) */
     s->conv_p = sbo_blob_f64_1(&s->blob, "conv_p", 0.0);

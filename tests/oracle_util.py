@@ -27,6 +27,8 @@ def lib(path: Path) -> ctypes.CDLL:
         for fn in ["sbo_destroy", "sbo_dims", "sbo_reset", "sbo_step", "sbo_get_temp", "sbo_get_mass",
                    "sbo_step_index", "sbo_reseed", "sbo_visible"]:
             getattr(l, fn).argtypes = None
+        l.sbo_set_episode.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_ulonglong, ctypes.c_int]
+        l.sbo_episode_offset.argtypes = [ctypes.c_void_p]
         _cache[key] = l
     return _cache[key]
 
@@ -48,6 +50,14 @@ class OracleEnv:
         (self.ncv, self.n, self.k, self.nz, self.nv, self.na, self.nact, self.n_cont, self.n_disc,
          self.obs_len) = list(d)
         self.obs = np.zeros(1024, np.float32)
+
+    def set_episode(self, first_len: int, start_rng: int = 0, random_start: bool = False) -> None:
+        """The device env's episode options for this env: first-episode length
+        (desync) and random-start stream (oracle/sbo.h sbo_set_episode)."""
+        self.l.sbo_set_episode(self.h, int(first_len), int(start_rng), 1 if random_start else 0)
+
+    def episode_offset(self) -> int:
+        return int(self.l.sbo_episode_offset(self.h))
 
     def reset(self) -> np.ndarray:
         self.l.sbo_reset(self.h, _p(self.obs))

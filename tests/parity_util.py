@@ -80,14 +80,13 @@ TOL_OBS = 1e-4
 
 
 def run_parity(blob_dir, n, steps, max_steps=0, seed=0, temp_every=10, groups=0, beta_mix=False,
-               oracle="port", wild=True, env_kw=None, first_lengths=None, start_offsets=None,
-               tolerant=False):
+               oracle="port", wild=True, env_kw=None, tolerant=False, on_step=None):
     """Steps n device envs and n oracle envs with the same seeded actions and
     compares them bit for bit after every step (tolerant: within the folded
     build's tolerances above; the largest differences seen are returned).
-    first_lengths / start_offsets (per env) give the oracle envs the
-    first-episode cut and calendar offsets the device env chose (episode
-    options); the device env's own choice is passed in."""
+    With the episode options desync / random_start in env_kw, each oracle env
+    gets the device env's first-episode length and random-start stream. on_step
+    (if given) is called as on_step(step, env, oracles) after the comparisons."""
     import torch
 
     from neurips2026_smart_building_challenge_b200 import SB_NUM_ATNS
@@ -99,12 +98,13 @@ def run_parity(blob_dir, n, steps, max_steps=0, seed=0, temp_every=10, groups=0,
     try:
         paths = scenario_paths(blob_dir)
         orc = [OracleEnv(paths[int(env.scenario[e])], max_steps=max_steps, path=path) for e in range(n)]
+        kw = env_kw or {}
+        if kw.get("desync") or kw.get("random_start"):
+            fl, sr = env.episode_options()
+            for e in range(n):
+                orc[e].set_episode(int(fl[e]), int(sr[e]), bool(kw.get("random_start")))
         env.reset()
         env.synchronize()
-        if first_lengths is not None or start_offsets is not None:
-            fl, so = env.episode_options()
-            for e in range(n):
-                orc[e].set_episode(int(fl[e]), int(so[e]))
         obs = env.obs.cpu().numpy()
         for e in range(n):
             o = orc[e].reset()
@@ -116,8 +116,8 @@ def run_parity(blob_dir, n, steps, max_steps=0, seed=0, temp_every=10, groups=0,
         for s in range(steps):
             a = np.zeros((n, SB_NUM_ATNS), np.float32)
             for e in range(n):
-                kw = dict(alpha=al[e, :orc[e].n_cont], beta=be[e, :orc[e].n_cont]) if beta_mix else {}
-                a[e] = actions(rng, 1, orc[e].n_cont, orc[e].n_disc, wild=wild, **kw)[0]
+                bkw = dict(alpha=al[e, :orc[e].n_cont], beta=be[e, :orc[e].n_cont]) if beta_mix else {}
+                a[e] = actions(rng, 1, orc[e].n_cont, orc[e].n_disc, wild=wild, **bkw)[0]
             env.step(torch.from_numpy(a).to(env.device))
             env.synchronize()
             obs = env.obs.cpu().numpy()
@@ -169,6 +169,8 @@ def run_parity(blob_dir, n, steps, max_steps=0, seed=0, temp_every=10, groups=0,
                 if bad and not against_ref and not tolerant:
                     bad.append(pre_stage_diff(env, orc[e], e))
                 assert not bad, f"{where} ({path.name}): " + "; ".join(bad)
+            if on_step is not None:
+                on_step(s, env, orc)
         assert env.status() == 0
         return worst
     finally:

@@ -126,3 +126,26 @@ def test_snapshot_reader_rejects_bad_records():
     assert snap["step"] == 3 and snap["blob"] == "blob" and snap["field"].shape == (2, 2)
     with pytest.raises(ValueError):
         parse_snapshot(body[:-1])
+
+
+def test_env_record_layout_matches_header(built, tmp_path):
+    """The Python mirror of Env has the C layout (offsets and size from a probe
+    compiled against include/sbenv.h), and its members follow the reference
+    GPU backend's order (complete_port/gpu/smart_buildings.cu:116-143)."""
+    import subprocess
+
+    import neurips2026_smart_building_challenge_b200 as pkg
+
+    names = [f for f, _ in pkg.EnvRecord._fields_]
+    assert names[:24] == ["agents", "log", "ep_ret", "ep_part", "ep_worst", "num_agents", "tag", "boundary_reached",
+                          "step", "max_steps", "start_offset", "start_day", "start_rng", "start_draws", "n_act",
+                          "n_cont", "n_disc", "loaded", "rng", "seed", "cont", "disc", "native", "env_id"]
+    src = tmp_path / "probe.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "sbenv.h"\nint main(void) {\n' +
+                   "".join(f'  printf("%zu\\n", offsetof(Env, {n}));\n' for n in names) +
+                   '  printf("%zu\\n", sizeof(Env));\n  return 0;\n}\n')
+    exe = tmp_path / "probe"
+    subprocess.run(["gcc", "-std=c11", f"-I{ROOT / 'include'}", str(src), "-o", str(exe)], check=True)
+    got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    want = [getattr(pkg.EnvRecord, n).offset for n in names] + [ctypes.sizeof(pkg.EnvRecord)]
+    assert got == want
