@@ -247,11 +247,10 @@ int sb_snapshot_write(int env, const char* path);
 /* Number of hot-path kernel launches one puf_step enqueues. */
 int sb_kernels_per_step(void);
 /* Measurement: runs one step with CUDA events around each kernel on the bound
- * streams (not for graph capture). ms[7] = {random inputs, k_pre, solve,
- * k_post, solve phase 0, k_dense, solve phase 1}; solve = phase 0 + k_dense +
- * phase 1; the random inputs of the next transition (k_conv, k_occ) run on
- * their own streams beside the solve, ms[0] from the end of k_pre to the later
- * of the two. */
+ * streams (not for graph capture). ms[7] = {-1, k_pre, solve, k_post, solve
+ * phase 0, k_dense, solve phase 1}; solve = phase 0 + k_dense + phase 1; the
+ * random inputs of the next transition (k_conv, k_occ) run beside phase 1,
+ * inside its interval, and have no time of their own (ms[0] = -1). */
 int sb_step_timed(float* ms);
 /* Algorithmic bytes one solve launch must move for the loaded batch: per env the
  * field and interior mass read and written plus the per-zone heat and air-side

@@ -334,7 +334,7 @@ class SmartBuildingsVec:
         ms = (ctypes.c_float * 7)()
         if self.lib.sb_step_timed(ms) != 0:
             raise RuntimeError("sb_step_timed failed")
-        # random_inputs: the next transition's k_conv + k_occ, on their own streams beside the solve
+        # the next transition's k_conv + k_occ run beside phase 1 and have no time of their own (-1)
         names = ["random_inputs", "k_pre", "k_solve", "k_post", "k_solve_phase0", "k_dense", "k_solve_phase1"]
         return {k: v for k, v in zip(names, list(ms)) if v >= 0.0}
 

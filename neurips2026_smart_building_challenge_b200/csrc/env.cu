@@ -11,11 +11,11 @@
 //   k_dense    (hi) the air-side dense solve of every env, one CTA each
 //   k_solve<1> (hi) applied heat, second L/U solve (folded build: the U sweep),
 //              interior mass, field
+//   k_conv, k_occ (hi, programmatic dependents of k_solve<1>) the next
+//              transition's convection permutations and occupancy chains, on
+//              the SMs phase 1's slabs leave free, beside phase 1
 //   k_post     (main, after hi) convection apply, boiler, observation, reward,
 //              episode log, in-step restart
-//   k_conv, k_occ (two low-priority streams, forked after k_pre and joined at
-//              the end of the step) the next transition's convection
-//              permutations and occupancy chains, beside the whole step
 // No host synchronisation, allocation or attribute change happens inside
 // puf_step, so a caller can capture it in a CUDA graph.
 #include <cuda_runtime.h>
@@ -107,8 +107,8 @@ struct Engine {
     StepCtx* d_ctx = nullptr;
     SlabDesc* d_slabs = nullptr;
     Env* envs = nullptr;          // managed
-    cudaStream_t stream = nullptr, own_stream = nullptr, rng_a = nullptr, rng_b = nullptr, hi = nullptr;
-    cudaEvent_t ev_fork = nullptr, ev_join = nullptr, ev_rng_a = nullptr, ev_rng_b = nullptr;
+    cudaStream_t stream = nullptr, own_stream = nullptr, hi = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
     size_t smem_solve = 0, smem_pre = 0, smem_post = 0, smem_conv = 0, smem_occ = 0, smem_dense = 0;
     unsigned occ_ctas = 0;
     // episode options and the learning-reward statistics (host EMA state)
@@ -126,9 +126,9 @@ struct Engine {
     bool ready = false;
     ~Engine() { destroy(); }
     void destroy() {
-        for (cudaStream_t* q : {&rng_a, &rng_b, &hi, &own_stream})
+        for (cudaStream_t* q : {&hi, &own_stream})
             if (*q) { cudaStreamDestroy(*q); *q = nullptr; }
-        for (cudaEvent_t* q : {&ev_fork, &ev_join, &ev_rng_a, &ev_rng_b})
+        for (cudaEvent_t* q : {&ev_fork, &ev_join})
             if (*q) { cudaEventDestroy(*q); *q = nullptr; }
         if (envs) cudaFree(envs);
         envs = nullptr;
@@ -197,18 +197,27 @@ StateLayout make_layout(int na, int nv, int nz, int k) {
     return L;
 }
 
-// The next transition's random inputs on the two low-priority streams (forked
-// from the main stream at `after`): convection per scenario, occupancy per stream.
-cudaError_t launch_rng(Engine& E, cudaEvent_t after) {
-    cudaError_t e = cudaStreamWaitEvent(E.rng_a, after, 0);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(E.rng_b, after, 0);
+// The next transition's random inputs: convection per scenario, occupancy per
+// stream. pdl: as programmatic dependents of the kernel before them on `st`
+// (they start once its CTAs are all resident and take the SMs they leave free;
+// each completes only after that kernel has).
+cudaError_t launch_rng(Engine& E, cudaStream_t st, bool pdl) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    cfg.gridDim = dim3((unsigned)E.sd.size());
+    cfg.blockDim = dim3(32);
+    cfg.dynamicSmemBytes = E.smem_conv;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k_conv, (const StepCtx*)E.d_ctx, 0);
     if (e != cudaSuccess) return e;
-    k_conv<<<(unsigned)E.sd.size(), 32, E.smem_conv, E.rng_a>>>(E.d_ctx, 0);
-    k_occ<<<E.occ_ctas, 32 * kOccWarps, E.smem_occ, E.rng_b>>>(E.d_ctx, 0);
-    e = cudaGetLastError();
-    if (e == cudaSuccess) e = cudaEventRecord(E.ev_rng_a, E.rng_a);
-    if (e == cudaSuccess) e = cudaEventRecord(E.ev_rng_b, E.rng_b);
-    return e;
+    cfg.gridDim = dim3(E.occ_ctas);
+    cfg.blockDim = dim3(32 * kOccWarps);
+    cfg.dynamicSmemBytes = E.smem_occ;
+    return cudaLaunchKernelEx(&cfg, k_occ, (const StepCtx*)E.d_ctx, 0);
 }
 
 // The dense air-side solves: one launch per class of equal k with its own
@@ -236,20 +245,20 @@ cudaError_t launch_dense(Engine& E, cudaStream_t st) {
 }
 
 // The solve on the high-priority stream: phase 0 (first L/U solve), the
-// dense air-side solves, phase 1 (second L/U solve, mass, field). The random
-// inputs of the next transition are enqueued on their own streams right after
-// phase 0, so the slabs are placed first and the producers take the SMs the
-// slabs leave free.
+// dense air-side solves, phase 1 (second L/U solve, mass, field), and beside
+// phase 1 the random inputs of the next transition (k_post of this step reads
+// the ones made during the step before).
 cudaError_t launch_solve(Engine& E) {
     const unsigned slabs = (unsigned)E.slabs.size();
     k_solve<0><<<slabs, kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
     cudaError_t e = cudaGetLastError();
-    if (e == cudaSuccess) e = launch_rng(E, E.ev_fork);
     if (e != cudaSuccess) return e;
     e = launch_dense(E, E.hi);
     if (e != cudaSuccess) return e;
     k_solve<1><<<slabs, kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
-    return cudaGetLastError();
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    return launch_rng(E, E.hi, true);
 }
 
 bool launch_step(Engine& E) {
@@ -262,9 +271,6 @@ bool launch_step(Engine& E) {
     CK(cudaStreamWaitEvent(E.stream, E.ev_join, 0));
     k_post<<<(unsigned)E.n_env, 128, E.smem_post, E.stream>>>(E.d_ctx);
     CK(cudaGetLastError());
-    // the producers of the next transition join at the end of the step
-    CK(cudaStreamWaitEvent(E.stream, E.ev_rng_a, 0));
-    CK(cudaStreamWaitEvent(E.stream, E.ev_rng_b, 0));
     return true;
 }
 
@@ -717,13 +723,9 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
         int least = 0, greatest = 0;
         CK(cudaDeviceGetStreamPriorityRange(&least, &greatest));
         CK(cudaStreamCreateWithPriority(&E.hi, cudaStreamNonBlocking, greatest));
-        CK(cudaStreamCreateWithPriority(&E.rng_a, cudaStreamNonBlocking, least));
-        CK(cudaStreamCreateWithPriority(&E.rng_b, cudaStreamNonBlocking, least));
     }
     CK(cudaEventCreateWithFlags(&E.ev_fork, cudaEventDisableTiming));
     CK(cudaEventCreateWithFlags(&E.ev_join, cudaEventDisableTiming));
-    CK(cudaEventCreateWithFlags(&E.ev_rng_a, cudaEventDisableTiming));
-    CK(cudaEventCreateWithFlags(&E.ev_rng_b, cudaEventDisableTiming));
     if (!E.stream) E.stream = E.own_stream;
     CK(cudaDeviceSynchronize());
     E.ready = true;
@@ -760,12 +762,9 @@ bool do_reset(Engine& E) {
     k_occ<<<E.occ_ctas, 32 * kOccWarps, E.smem_occ, E.stream>>>(E.d_ctx, 1);
     CK(cudaGetLastError());
     CK(cudaMemsetAsync(E.ctx.cseq, 0, sizeof(int) * E.sd.size(), E.stream));
-    CK(cudaEventRecord(E.ev_fork, E.stream));
-    CK(launch_rng(E, E.ev_fork));
+    CK(launch_rng(E, E.stream, false));
     k_reset<<<(unsigned)E.n_env, 128, E.smem_post, E.stream>>>(E.d_ctx);
     CK(cudaGetLastError());
-    CK(cudaStreamWaitEvent(E.stream, E.ev_rng_a, 0));
-    CK(cudaStreamWaitEvent(E.stream, E.ev_rng_b, 0));
     CK(cudaStreamSynchronize(E.stream));
     return true;
 }
@@ -1316,12 +1315,11 @@ int sb_snapshot_write(int env, const char* path) {
 int sb_step_timed(float* ms) {
     if (!g_eng || !g_eng->ready || !ms) return -1;
     Engine& E = *g_eng;
-    cudaEvent_t ev[10];
+    cudaEvent_t ev[7];
     for (auto& e : ev)
         if (cudaEventCreate(&e) != cudaSuccess) return -1;
     // the step of launch_step with events around each kernel; the producers of
-    // the next transition run on their own streams from ev[1] (k_conv ends at
-    // ev[7], k_occ at ev[8])
+    // the next transition run beside phase 1, inside its interval
     cudaEventRecord(ev[0], E.stream);
     k_pre<<<(unsigned)E.n_env, 128, E.smem_pre, E.stream>>>(E.d_ctx);
     cudaEventRecord(ev[1], E.stream);
@@ -1330,32 +1328,24 @@ int sb_step_timed(float* ms) {
     const unsigned slabs = (unsigned)E.slabs.size();
     k_solve<0><<<slabs, kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
     cudaEventRecord(ev[4], E.hi);
-    launch_rng(E, E.ev_fork);
-    cudaEventRecord(ev[7], E.rng_a);
-    cudaEventRecord(ev[8], E.rng_b);
     launch_dense(E, E.hi);
     cudaEventRecord(ev[5], E.hi);
     k_solve<1><<<slabs, kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
+    launch_rng(E, E.hi, true);
     cudaEventRecord(ev[2], E.hi);
     cudaStreamWaitEvent(E.stream, ev[2], 0);
     cudaEventRecord(ev[6], E.stream);
     k_post<<<(unsigned)E.n_env, 128, E.smem_post, E.stream>>>(E.d_ctx);
     cudaEventRecord(ev[3], E.stream);
-    cudaStreamWaitEvent(E.stream, E.ev_rng_a, 0);
-    cudaStreamWaitEvent(E.stream, E.ev_rng_b, 0);
-    cudaEventRecord(ev[9], E.stream);
-    const bool ok = cudaEventSynchronize(ev[9]) == cudaSuccess;
+    const bool ok = cudaEventSynchronize(ev[3]) == cudaSuccess;
     if (ok) {
-        float a = 0.0f, b = 0.0f;
-        cudaEventElapsedTime(&a, ev[1], ev[7]);
-        cudaEventElapsedTime(&b, ev[1], ev[8]);
-        ms[0] = a > b ? a : b;                         // k_conv, k_occ (beside the solve)
+        ms[0] = -1.0f;                                 // k_conv, k_occ: beside phase 1, inside ms[6]
         cudaEventElapsedTime(&ms[1], ev[0], ev[1]);   // k_pre
         cudaEventElapsedTime(&ms[2], ev[1], ev[2]);   // the solve: phase 0, k_dense, phase 1
         cudaEventElapsedTime(&ms[3], ev[6], ev[3]);   // k_post
         cudaEventElapsedTime(&ms[4], ev[1], ev[4]);   // phase 0
         cudaEventElapsedTime(&ms[5], ev[4], ev[5]);   // k_dense
-        cudaEventElapsedTime(&ms[6], ev[5], ev[2]);   // phase 1
+        cudaEventElapsedTime(&ms[6], ev[5], ev[2]);   // phase 1 (with the producers beside it)
     }
     for (auto& e : ev) cudaEventDestroy(e);
     return ok ? 0 : -1;

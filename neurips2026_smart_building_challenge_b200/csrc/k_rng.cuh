@@ -19,6 +19,9 @@
 //     each new episode's start day (gpu/smart_buildings.cu:1636-1657).
 // Transition q (counted from puf_reset) is written to slot q & 1 and read by
 // that step's k_post; k_occ's reset mode writes slot kResetSlot for puf_reset.
+// In a step both run as programmatic dependents of the solve's phase 1 (on the
+// SMs its slabs leave free, once every slab is resident) and complete only
+// after it (griddepcontrol.wait at their end, reached by every CTA).
 #pragma once
 #include "dev_util.cuh"
 
@@ -71,20 +74,10 @@ __device__ inline void occ_prime(WarpMt& m, const ScnDev& s, int* st, int off, d
     occ_advance(m, s, st, (int)s.o_hour_m1[r], (int)s.o_wd_m1[r], V);
 }
 
-// restore = 1 (puf_reset): the stream goes back to its state before the last
-// transition produced, which no step consumed. restore = 0: the next
-// transition's swaps into slot cseq & 1, the state before it kept.
-__global__ void __launch_bounds__(32) k_conv(const StepCtx* __restrict__ ctx, int restore) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    const int si = blockIdx.x;
-    const ScnDev& s = ctx->scns[si];
-    const GroupDev& g = ctx->groups[s.group];
-    const int lane = threadIdx.x & 31;
-    if (restore) {
-        if (*ctx->produced)
-            for (int x = lane; x < 625; x += 32) s.conv_mt[x] = s.conv_ckpt[x];
-        return;
-    }
+// One transition's convection of one scenario (k_conv's body).
+__device__ inline void conv_transition(const StepCtx* __restrict__ ctx, const ScnDev& s, const GroupDev& g,
+                                       uint8_t* smem, int lane) {
+    const int si = s.scn_index;
     for (int x = lane; x < 625; x += 32) s.conv_ckpt[x] = s.conv_mt[x];
     __syncwarp();
     // shared memory: MT state 624 | next state 624 | tempered blocks 1248 |
@@ -186,6 +179,22 @@ __global__ void __launch_bounds__(32) k_conv(const StepCtx* __restrict__ ctx, in
     }
 }
 
+// restore = 1 (puf_reset): the stream goes back to its state before the last
+// transition produced, which no step consumed. restore = 0: the next
+// transition's swaps into slot cseq & 1, the state before it kept.
+__global__ void __launch_bounds__(32) k_conv(const StepCtx* __restrict__ ctx, int restore) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int si = blockIdx.x;
+    const ScnDev& s = ctx->scns[si];
+    const GroupDev& g = ctx->groups[s.group];
+    const int lane = threadIdx.x & 31;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (!restore) conv_transition(ctx, s, g, smem, lane);
+    else if (*ctx->produced)
+        for (int x = lane; x < 625; x += 32) s.conv_mt[x] = s.conv_ckpt[x];
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // One warp per occupancy stream, kOccWarps streams per CTA. reset = 1: the
 // puf_reset of the stream (start day, priming, first interval) into slot
 // kResetSlot; the producer's episode state restarts from the consumer's
@@ -193,11 +202,19 @@ __global__ void __launch_bounds__(32) k_conv(const StepCtx* __restrict__ ctx, in
 // stream's next transition into slot oseq & 1.
 constexpr int kOccWarps = 4;
 constexpr size_t kOccWarpSmem = 4 * (624 + 624 + 1248);   // MT blocks; occupant states follow
+__device__ inline void occ_stream(const StepCtx* __restrict__ ctx, int u, int reset, uint8_t* smem);
+
 __global__ void __launch_bounds__(32 * kOccWarps) k_occ(const StepCtx* __restrict__ ctx, int reset) {
     extern __shared__ __align__(128) uint8_t smem[];
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int u = blockIdx.x * kOccWarps + (threadIdx.x >> 5);
+    if (u < ctx->n_ostreams) occ_stream(ctx, u, reset, smem);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// One occupancy stream (one warp of k_occ).
+__device__ inline void occ_stream(const StepCtx* __restrict__ ctx, int u, int reset, uint8_t* smem) {
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int u = blockIdx.x * kOccWarps + w;
-    if (u >= ctx->n_ostreams) return;
     const ScnDev& s = ctx->scns[ctx->ostream_scn[u]];
     const size_t per_warp = kOccWarpSmem + 4 * (size_t)ctx->occ_stride;
     uint32_t* st = reinterpret_cast<uint32_t*>(smem + (size_t)w * per_warp);
