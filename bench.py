@@ -9,7 +9,14 @@ One step = one puf_step of every env (decode, HVAC, fp64 thermal solve with the
 air side, convection, occupancy, observation, reward, episode log).
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+                    [--workload config2|config3|config4] [--envs E] [--solve folded|exact]
     python bench.py --rollout [--gpus N --steps K --warmup W]
+    python bench.py --month
+
+The stated build is the folded air side (--solve folded, the default): one L/U
+pair per step, within the north star's 1e-9 per-step / 1e-6 K per-month
+contract (tests/test_fold_gpu.py); the bit-exact build's numbers are reported
+beside it under "variants".
 
 --rollout measures BASELINE configuration 5 instead: the end-to-end env+policy
 step rate of policy-in-loop rollouts (a random-init shared MLP, hidden 128, tanh,
@@ -18,8 +25,10 @@ library's sampler; one env+policy step captured in a CUDA graph and replayed
 over 128-step rollout horizons), 960 envs per GPU.
 
 N > 1 is launched with torch.distributed.run: every rank owns a disjoint slice of
-960 envs (weak scaling, no per-step collective); episode statistics are summed
-over ranks with one NCCL all-reduce after the timed region.
+the job's envs (dist.shard; weak scaling, no per-step collective); the
+per-scenario episode statistics are summed over ranks with one NCCL all-reduce
+after the timed region. --month times configuration 1 (one building, one month)
+on the GPU and on one host thread.
 """
 from __future__ import annotations
 
@@ -41,9 +50,21 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "fp64 building-steps/s"
 UNIT = "building-steps/s"
-ENVS_PER_GPU = 960
-WORKLOAD = ("config2: 960 synthetic buildings per GPU = 6 seeded layouts (41-81 zones, 1-4 AHUs, "
-            "64x48 grid) x 5 climates x 32 envs; seeded Beta(a,b) actions, a,b~U(0.5,12)")
+# workloads: config2 is the metric's configuration at N = 1
+WORKLOADS = {
+    "config2": dict(config=2, envs=960, groups=30,
+                    desc="config2: 960 synthetic buildings per GPU = 6 seeded layouts (41-81 zones, 1-4 AHUs, "
+                         "64x48 grid) x 5 climates x 32 envs; seeded Beta(a,b) actions, a,b~U(0.5,12)"),
+    "config3": dict(config=3, envs=960, groups=1,
+                    desc="config3: 960 envs of the largest building (128x96 grid, 81 zones, 4 AHUs, dense "
+                         "interior walls); seeded Beta(a,b) actions, a,b~U(0.5,12)"),
+    "config4": dict(config=2, envs=7680, groups=30,
+                    desc="config4: 7,680 synthetic buildings per GPU over the config-2 mix (6 layouts x 5 "
+                         "climates); seeded Beta(a,b) actions, a,b~U(0.5,12)"),
+}
+SOLVE_NOTE = {"folded": "folded air side (solve_exact=0): one L/U pair per step; within the north star's 1e-9 "
+                        "per step / 1e-6 K per month contract (tests/test_fold_gpu.py)",
+              "exact": "exact (solve_exact=1): the reference core's two L/U solves, bit for bit"}
 SMI_Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
@@ -55,14 +76,28 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--envs", type=int, default=ENVS_PER_GPU, help="envs per GPU")
+    ap.add_argument("--workload", default="config2", choices=sorted(WORKLOADS))
+    ap.add_argument("--envs", type=int, default=0, help="envs per GPU (0: the workload's)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--rollout", action="store_true", help="configuration 5: env+policy steps in a CUDA graph")
     ap.add_argument("--horizon", type=int, default=128, help="rollout horizon (--rollout)")
-    ap.add_argument("--solve", default="exact", choices=["exact", "folded"],
+    ap.add_argument("--solve", default="folded", choices=["exact", "folded"],
                     help="exact: the reference core's two triangular solves, bit for bit; folded: one L/U "
                          "pair (the reference GPU backend's folded air side, 1e-9 per-step contract)")
-    return ap.parse_args()
+    ap.add_argument("--month", action="store_true",
+                    help="configuration 1: one building for its whole month, GPU and the reference core (1 thread)")
+    args = ap.parse_args()
+    if args.envs <= 0:
+        args.envs = WORKLOADS[args.workload]["envs"]
+    return args
+
+
+def bench_config(args, world: int) -> dict:
+    """The `config` object both arms print (the same keys and values)."""
+    w = WORKLOADS[args.workload]
+    return {"workload": w["desc"], "envs_per_gpu": args.envs, "total_envs": args.envs * world,
+            "solve": args.solve, "l2": "flushed between timed steps (256 MiB write, untimed)",
+            "parallelism": f"env-sharded x{world}, no per-step collective"}
 
 
 # ---------------------------------------------------------------- clocks
@@ -143,35 +178,54 @@ def cpu_kind() -> str:
     return "reference" if (ROOT / "oracle" / "_ref" / "libcsimref.so").exists() else "port"
 
 
-def blob_list(cache: Path, n_env: int) -> list[Path]:
+def workload_dir(workload: str, cache: Path) -> Path:
     from neurips2026_smart_building_challenge_b200 import config_dir
 
-    d = config_dir(2, cache)
-    scen = sorted(d.glob("*.sbb"))
-    return [scen[i % len(scen)] for i in range(n_env)]
+    return config_dir(WORKLOADS[workload]["config"], cache)
 
 
-def cpu_baseline(cache: Path, seconds: float = 12.0) -> dict:
-    """Bounded sample: every host core steps one env of a different config-2 scenario for ~12 s."""
+def blob_list(cache: Path, n_env: int, workload: str = "config2") -> list[Path]:
+    """The scenario of every env in the device env's own assignment (groups of
+    consecutive envs per scenario, building-first round-robin scenario order)."""
+    sys.path.insert(0, str(ROOT / "tests"))
+    from parity_util import scenario_paths
+
+    scen = scenario_paths(workload_dir(workload, cache))
+    G = max(1, min(WORKLOADS[workload]["groups"], len(scen), n_env))
+    out = []
+    for i in range(G):
+        out += [scen[i]] * (n_env // G + (1 if i < n_env % G else 0))
+    return out
+
+
+def cpu_baseline(cache: Path, workload: str, seconds: float = 12.0) -> dict:
+    """Bounded sample: every host core steps one env of a different scenario of the
+    workload for ~12 s (one env per process keeps its state in the core's cache;
+    the reference arm, many envs per process, is the stated end-to-end baseline)."""
     cores = os.cpu_count() or 1
-    blobs = blob_list(cache, 30)
-    work = [(cpu_kind(), [blobs[i % 30]], 0, seconds, i) for i in range(cores)]
+    scen = sorted(set(blob_list(cache, 960, workload)))
+    work = [(cpu_kind(), [scen[i % len(scen)]], 0, seconds, i) for i in range(cores)]
     with mp.get_context("spawn").Pool(cores) as pool:
         res = pool.map(_cpu_worker, work)
     steps = sum(r[0] for r in res)
     wall = max(r[1] for r in res)
     return {"value": steps / wall, "unit": UNIT, "cores": cores, "kind": cpu_kind(),
-            "sample": f"{cores} processes x 1 env (config-2 scenarios round robin), ~{seconds:.0f} s each, "
-                      f"{steps} env-steps"}
+            "sample": f"{cores} processes x 1 env ({workload} scenarios round robin), ~{seconds:.0f} s each, "
+                      f"{steps} env-steps",
+            "note": "one env per core; the reference arm (--impl reference: the whole workload, many envs "
+                    "per core) is the stated baseline of the end-to-end comparison"}
 
 
 def run_reference(args) -> None:
-    """Reference arm: the reference's own C core stepping the same 960-env workload on all host cores."""
+    """Reference arm: the reference's own C core stepping the same workload on all
+    host cores -- at N GPUs the N x envs_per_gpu envs of the whole job, on rank 0."""
     if int(os.environ.get("RANK", "0")) != 0:
         return
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     cache = ROOT / ".sbb_cache" / "bench"
-    blobs = blob_list(cache, args.envs)
-    cores = min(os.cpu_count() or 1, args.envs)
+    total_envs = args.envs * world
+    blobs = blob_list(cache, total_envs, args.workload)
+    cores = min(os.cpu_count() or 1, total_envs)
     slices = [blobs[i::cores] for i in range(cores)]
     total = args.warmup + args.steps
     work = [(cpu_kind(), s, total, 0.0, i) for i, s in enumerate(slices)]
@@ -180,13 +234,14 @@ def run_reference(args) -> None:
     # a step ends when the slowest core finishes its slice
     per_step = np.max(np.array([r[2] for r in res]), axis=0)[args.warmup:]
     ms = float(per_step.sum() / len(per_step) * 1e3)
-    value = args.envs / (ms / 1e3)
-    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+    value = total_envs / (ms / 1e3)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "envs": args.envs},
+            "config": bench_config(args, world),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": cpu_kind(),
-                             "sample": f"{args.envs} envs over {cores} processes, {args.steps} timed steps"},
+                             "sample": f"{total_envs} envs over {cores} processes "
+                                       f"({total_envs / cores:.0f} per process), {args.steps} timed steps"},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -269,6 +324,63 @@ class E2EPipe:
         self.started[k] = True
 
 
+def timed_steps(env, pool, flush, steps: int, warmup: int, world: int, torch, dist, clk=None) -> float:
+    """Device time (ms, max over ranks) of `steps` env steps after `warmup`
+    untimed ones; L2 flushed (untimed) and the next actions copied before each."""
+    s = env.stream
+
+    def prep(i):
+        with torch.cuda.stream(s):
+            env.actions.copy_(pool[i % len(pool)], non_blocking=True)
+            flush.fill_(i & 0xFF)
+
+    for i in range(warmup):
+        prep(i)
+        env.step()
+    env.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ctx = clk if clk is not None else _Null()
+    with ctx:
+        for i in range(steps):
+            prep(i)
+            starts[i].record(s)
+            env.step()
+            ends[i].record(s)
+        env.synchronize()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = torch.tensor([sum(a.elapsed_time(b) for a, b in zip(starts, ends))], dtype=torch.float64,
+                      device=env.device)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    return float(ms.item())
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+
+def kernel_times(env, pool, flush, torch, reps: int = 5) -> dict:
+    kt = {}
+    for i in range(reps):
+        with torch.cuda.stream(env.stream):
+            env.actions.copy_(pool[i % len(pool)], non_blocking=True)
+            flush.fill_(i & 0xFF)
+        env.synchronize()
+        for k, v in env.step_timed().items():
+            kt.setdefault(k, []).append(v)
+    return {k: float(np.mean(v)) for k, v in kt.items()}
+
+
 def run_ours(args) -> None:
     import torch
     import torch.distributed as dist
@@ -280,64 +392,48 @@ def run_ours(args) -> None:
     # the CPU baseline's process pool starts before the first GPU call (spawned)
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(ROOT / ".sbb_cache" / "bench")
+        cpu = cpu_baseline(ROOT / ".sbb_cache" / "bench", args.workload)
     torch.cuda.set_device(local)
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300))
-    from neurips2026_smart_building_challenge_b200 import SmartBuildingsVec, config_dir, env_lib
+    from neurips2026_smart_building_challenge_b200 import SmartBuildingsVec, env_lib, fp64_peak_tflops
+    from neurips2026_smart_building_challenge_b200 import dist as sbdist
 
     cache = ROOT / ".sbb_cache" / f"bench_rank{rank}"
-    d = config_dir(2, cache)
+    d = workload_dir(args.workload, cache)
     n = args.envs
-    env = SmartBuildingsVec(n, blob_dir=str(d), groups=30, device=f"cuda:{local}",
-                            solve_exact=1 if args.solve == "exact" else 0)
-    env.reset()
-    pool = torch.from_numpy(action_pool(n, 8, seed=1234 + rank)).to(env.device)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=env.device)   # > 126 MB L2
-    s = env.stream
-
-    def one_step(i):
-        with torch.cuda.stream(s):
-            env.actions.copy_(pool[i % len(pool)], non_blocking=True)
-            flush.fill_(i & 0xFF)
-
-    for i in range(args.warmup):
-        one_step(i)
-        env.step()
-    env.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    with ClockSampler(local) as clk:
-        for i in range(args.steps):
-            one_step(i)
-            starts[i].record(s)
-            env.step()
-            ends[i].record(s)
-        env.synchronize()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    ms_local = sum(a.elapsed_time(b) for a, b in zip(starts, ends))
-    ms_t = torch.tensor([ms_local], dtype=torch.float64, device=env.device)
-    if world > 1:
-        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-    ms_total = float(ms_t.item())
+    # this rank's slice of the job's envs (the per-env draws follow the global index)
+    start, count = sbdist.shard(n * world, world, rank)
+    assert count == n
+    groups = WORKLOADS[args.workload]["groups"]
+    pool_np = action_pool(n, 8, seed=1234 + rank)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=f"cuda:{local}")   # > 126 MB L2
+    variants = {}
+    other = "exact" if args.solve == "folded" else "folded"
+    # the other build first (value and per-kernel times only), then the stated one
+    for solve in (other, args.solve):
+        env = SmartBuildingsVec(n, blob_dir=str(d), groups=groups, device=f"cuda:{local}",
+                                solve_exact=1 if solve == "exact" else 0, env_offset=start)
+        env.reset()
+        pool = torch.from_numpy(pool_np).to(env.device)
+        if solve == other:
+            ms_total = timed_steps(env, pool, flush, args.steps, args.warmup, world, torch, dist)
+            variants[solve] = {"value": world * n * args.steps / (ms_total / 1e3),
+                               "ms_per_step": ms_total / args.steps, "note": SOLVE_NOTE[solve],
+                               "per_kernel_ms": kernel_times(env, pool, flush, torch)}
+            env.close()
+            continue
+        with ClockSampler(local) as clk:
+            ms_total = timed_steps(env, pool, flush, args.steps, args.warmup, world, torch, dist, clk)
+        break
     ms_per_step = ms_total / args.steps
     value = world * n * args.steps / (ms_total / 1e3)
     status = env.status()
 
-    # per-kernel durations (diagnostic steps after the timed region)
-    kt = {}
-    for i in range(5):
-        one_step(i)
-        env.synchronize()
-        for k, v in env.step_timed().items():
-            kt.setdefault(k, []).append(v)
-    k_ms = {k: float(np.mean(v)) for k, v in kt.items()}
+    # roofline of the solve (HBM, the north star's bound) and its fp64 issue share
+    k_ms = kernel_times(env, pool, flush, torch)
     bytes_launch = env.solve_bytes()
+    flops_launch = env.solve_flops()
     peaks = {}
     try:
         peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
@@ -346,15 +442,21 @@ def run_ours(args) -> None:
     peak = peaks.get("hbm_gbs")
     peak_src = "measured" if peak else "fallback"
     peak = peak or 6650.0
+    fp64_peak = fp64_peak_tflops()
     achieved = bytes_launch / (k_ms["k_solve"] / 1e3) / 1e9
+    fp64_achieved = flops_launch / (k_ms["k_solve"] / 1e3) / 1e12
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                "traffic": profile_traffic(), "kernel": "k_solve", "peak_source": peak_src,
-                "kernel_ms": k_ms["k_solve"], "algorithmic_bytes_per_launch": bytes_launch,
-                "per_kernel_ms": k_ms}
+                "traffic": profile_traffic(), "kernel": "k_solve (phase 0 + k_dense + phase 1)",
+                "peak_source": peak_src, "kernel_ms": k_ms["k_solve"], "algorithmic_bytes_per_launch": bytes_launch,
+                "per_kernel_ms": k_ms,
+                "fp64": {"achieved_tflops": fp64_achieved, "peak_tflops": fp64_peak, "frac": fp64_achieved / fp64_peak,
+                         "flops_per_launch": flops_launch,
+                         "peak_source": "measured in this run (sb_fp64_peak: independent DFMA chains on every SM)"}}
 
     # end to end through the C ABI: pinned host actions in, obs/rewards/terminals out, every
     # step; the copies run on two copy streams (double-buffered device staging) and overlap
     # the neighbouring steps' kernels, as a trainer feeding the env would run them
+    s = env.stream
     h_act = torch.from_numpy(action_pool(n, 2, seed=99 + rank)).pin_memory()
     e_steps = max(3, min(args.steps, 20))
     pipe = E2EPipe(env, h_act, torch)
@@ -379,27 +481,76 @@ def run_ours(args) -> None:
            "h2d_bytes_per_step": n * 272 * 4, "d2h_bytes_per_step": n * (1024 + 2) * 4,
            "copies": "pinned host buffers, two copy streams overlapping the kernels"}
 
-    # episode statistics gathered over ranks (the path's only collective)
-    live = env.live_log()
-    stats = torch.tensor([live.get("live/reward", 0.0), live.get("live/comfort_dev_K", 0.0), 1.0],
-                         dtype=torch.float64, device=env.device)
-    if world > 1:
-        dist.all_reduce(stats)
+    # episode statistics: the per-scenario matrix of every rank summed over NCCL
+    # (the path's only collective)
+    stats = sbdist.allreduce_stats(env.scenario_stats(clear=True), device=env.device)
+    summary = sbdist.summarize(stats)
     launches = env_lib().sb_kernels_per_step() * args.steps
     env.close()
     if rank == 0:
+        config = bench_config(args, world)
+        config["solve_note"] = SOLVE_NOTE[args.solve]
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-                "config": {"workload": WORKLOAD, "envs_per_gpu": n, "total_envs": n * world, "solve": args.solve,
-                           "l2": "flushed between timed steps (256 MiB write, untimed)",
-                           "parallelism": f"env-sharded x{world}, no per-step collective"},
+                "vs_baseline": None, "dtype": "f64", "data": "synthetic", "config": config,
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
-                "clocks": clk.summary(), "device_status": status,
-                "episode_stats_allreduce": {"mean_live_reward": float(stats[0] / stats[2])}}
+                "clocks": clk.summary(), "device_status": status, "variants": variants,
+                "episode_stats_allreduce": {"scenarios": int(stats.shape[0]), "ranks": world, **summary}}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def run_month(args) -> None:
+    """Configuration 1 as BASELINE.md plans it: one building for its whole month
+    (8,640 steps), Beta(2,2) actions with seed 0 -- the device env (one env, one
+    GPU, latency-bound) and the reference's C core on one host thread."""
+    import torch
+
+    sys.path.insert(0, str(ROOT / "tests"))
+    from golden.make_golden import month_actions
+    from oracle_util import PORT, REF, OracleEnv
+
+    from neurips2026_smart_building_challenge_b200 import SmartBuildingsVec, config_dir
+
+    d = config_dir(1, ROOT / ".sbb_cache" / "bench")
+    blob = sorted(d.glob("*.sbb"))[0]
+    path = REF if REF.exists() else PORT
+    orc = OracleEnv(blob, path=path)
+    acts = list(month_actions(orc.n_cont, orc.n_disc))[:8640]
+    orc.reset()
+    t0 = time.perf_counter()
+    for a in acts:
+        orc.step(a)
+    cpu_s = time.perf_counter() - t0
+    line = {"metric": "seconds per simulated month (config 1, one building)", "higher_is_better": False,
+            "config": {"workload": "config1: one 64x48 / 41-zone building, 8,640 steps of 300 s, Beta(2,2) "
+                                   "actions seed 0"},
+            "cpu": {"seconds_per_month": cpu_s, "env_steps_per_s": 8640 / cpu_s, "cores": 1,
+                    "kind": "reference" if path == REF else "port"}}
+    torch.cuda.set_device(0)
+    dev_actions = torch.from_numpy(np.stack(acts)).cuda()
+    for solve in ("exact", "folded"):
+        env = SmartBuildingsVec(1, blob_dir=str(d), device="cuda:0", solve_exact=1 if solve == "exact" else 0)
+        env.reset()
+        s = env.stream
+        for i in range(20):   # warm-up
+            with torch.cuda.stream(s):
+                env.actions.copy_(dev_actions[i:i + 1], non_blocking=True)
+            env.step()
+        env.reset()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for i in range(8640):
+            with torch.cuda.stream(s):
+                env.actions.copy_(dev_actions[i:i + 1], non_blocking=True)
+            env.step()
+        e1.record(s)
+        env.synchronize()
+        g_s = e0.elapsed_time(e1) / 1e3
+        line[f"gpu_{solve}"] = {"seconds_per_month": g_s, "env_steps_per_s": 8640 / g_s, "n_gpus": 1}
+        env.close()
+    print(json.dumps(line), flush=True)
 
 
 ROLLOUT_METRIC = "env+policy building-steps/s"
@@ -506,6 +657,8 @@ def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.month:
+        run_month(args)
     elif args.rollout:
         run_rollout(args)
     else:

@@ -148,12 +148,15 @@ void dict_set_str(Dict* d, const char* key, const char* value);
  * (r - mean) * inv_std per scenario, the statistics moved by 0.1 towards each
  * puf_live_log window, starting at mean 0 and variance 0.217) and rew_center
  * (1: (r - mean) only, the mean moved by center_beta, default 0.01; rew_norm
- * wins when both are set). Returns NULL on error. */
+ * wins when both are set). env_offset: the global index of this batch's first
+ * env when a batch is sharded over several GPUs (the per-env draws follow the
+ * global index; default 0). Returns NULL on error. */
 Env* puf_vec_create(int n, Dict* kwargs, obs_t* observations, float* actions, float* rewards,
                     float* terminals);
 void puf_bind_stream(sb_stream_t stream);
 void puf_init(Env* env, Dict* kwargs);
-/* Restarts every env: state from the blob, occupancy primed, reset observation written. */
+/* Restarts every env: state from the blob, occupancy primed, reset observation
+ * written; clears the device status word (sb_device_status). */
 void puf_reset(Env* envs);
 /* One batched step of every env (device only, graph-capturable). With the
  * environment variable SB_SNAPSHOT=<file> set it also writes a snapshot of env
@@ -174,10 +177,21 @@ void puf_mask_init(unsigned char* mask, int width, int nagents);
 
 /* Last error text of this thread ("" if none). */
 const char* sb_last_error(void);
-/* Device status word: 0, or the first kernel-detected error code: 1 a solve
- * schedule chunk never arrived (bounded wait expired), 2 a corrupt schedule
- * chunk, 3 a convection swap list overflow. */
+/* Device status word: 0, or the first kernel-detected error code since the
+ * last puf_reset: 1 a sweep program stage never arrived (bounded mbarrier
+ * wait expired), 3 a convection swap list overflow, 5 a row's ready flag never
+ * arrived within the bounded wait, 6 a malformed or truncated sweep program.
+ * The kernel that detects one leaves its sweep and returns; the env's state
+ * for that step is then meaningless until puf_reset. Synchronises the bound
+ * stream. */
 int sb_device_status(void);
+/* Failure test of the bounded waits (no counterpart in the reference): on = 1
+ * makes warp 0 of every solve CTA wait, at the start of its L sweep, for a
+ * row of the sweep program that no warp publishes, polling at most
+ * spin_limit times (0: the production limit, 2^22 polls, about a second), so
+ * the wait runs out and the next puf_step reports code 5 without a fault or a
+ * hang; on = 0 turns it off (and restores the limit). Synchronises. 0 or -1. */
+int sb_test_stall(int on, unsigned int spin_limit);
 /* Shape of the loaded batch: out[8] = {n_env, n_scenarios, n_groups, obs_len_max,
  * n_cont_max, n_disc_max, slab_ctas, kernels_per_step}. */
 void sb_shape(int* out);
@@ -256,6 +270,19 @@ int sb_step_timed(float* ms);
  * field and interior mass read and written plus the per-zone heat and air-side
  * vectors; per solver group the factor and coupling tables once. */
 int sb_solve_bytes(double* per_launch);
+/* fp64 operations one solve launch performs for the loaded batch (the
+ * triangular solves' multiply / subtract / divide, forcing, coupling products,
+ * the dense systems' elimination, the mass / field update). */
+int sb_solve_flops(double* per_launch);
+/* Measured fp64 issue rate of the current GPU in TFLOP/s: a plain timed kernel
+ * of independent fused multiply-add chains over every SM (changes no setting). */
+int sb_fp64_peak(double* tflops);
+/* Per-scenario episode statistics since creation or the last clear, out
+ * [n_scenarios][6] = {reward sum, mean-deviation sum, steps, reward^2 sum,
+ * sum of whole-episode mean rewards, whole episodes}; clear != 0 zeroes the
+ * sums (puf_live_log reads and clears the same sums). Returns the scenario
+ * count, -1 on error. Synchronises the bound stream. */
+int sb_scenario_stats(double* out, int clear);
 /* Inspection: one env's last pre-stage results, out = [air conductance k][supply
  * air temperature k][applied heat per zone cell nz][flow factor sum, reheat W,
  * boiler temperature, boiler return, pump head]. Returns the count or -1. */

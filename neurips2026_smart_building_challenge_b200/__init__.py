@@ -40,7 +40,7 @@ ENV_SYMBOLS = ["sb_dict_new", "sb_dict_free", "dict_find", "dict_set", "dict_set
                "sb_env_info", "sb_get_temp", "sb_get_mass", "sb_get_reward_f64", "sb_kernels_per_step",
                "sb_solve_schedule", "sb_sweep_warps", "sb_sweep_stats", "sb_debug_state", "sb_step_timed", "sb_solve_bytes",
                "sb_dense_check", "sb_beta_actions", "sb_snapshot_write", "sb_dense_solve_noalloc",
-               "sb_episode_options"]
+               "sb_episode_options", "sb_solve_flops", "sb_fp64_peak", "sb_scenario_stats", "sb_test_stall"]
 GEN_SYMBOLS = ["sbgen_preset", "sbgen_write", "sbgen_factor_stats"]
 
 
@@ -130,6 +130,10 @@ def env_lib() -> ctypes.CDLL:
                                         ctypes.c_ulonglong, vp]
         lib.sb_snapshot_write.argtypes = [ctypes.c_int, ctypes.c_char_p]
         lib.sb_episode_options.argtypes = [ip, ctypes.POINTER(ctypes.c_ulonglong)]
+        lib.sb_solve_flops.argtypes = [dp]
+        lib.sb_fp64_peak.argtypes = [dp]
+        lib.sb_scenario_stats.argtypes = [dp, ctypes.c_int]
+        lib.sb_test_stall.argtypes = [ctypes.c_int, ctypes.c_uint]
         lib._sb_typed = True
     return lib
 
@@ -344,6 +348,19 @@ class SmartBuildingsVec:
             raise RuntimeError("sb_solve_bytes failed")
         return b.value
 
+    def solve_flops(self) -> float:
+        f = ctypes.c_double()
+        if self.lib.sb_solve_flops(ctypes.byref(f)) != 0:
+            raise RuntimeError("sb_solve_flops failed")
+        return f.value
+
+    def scenario_stats(self, clear: bool = False) -> np.ndarray:
+        """[n_scenarios][6] episode-statistics sums (dist.STAT_KEYS order)."""
+        out = np.zeros((self.shape[1], 6))
+        if self.lib.sb_scenario_stats(out.ctypes.data_as(ctypes.POINTER(ctypes.c_double)), 1 if clear else 0) < 0:
+            raise RuntimeError("sb_scenario_stats failed")
+        return out
+
     def _check(self) -> None:
         err = self.lib.sb_last_error().decode()
         if err:
@@ -359,6 +376,14 @@ class SmartBuildingsVec:
             self.close()
         except Exception:
             pass
+
+
+def fp64_peak_tflops() -> float:
+    """Measured fp64 issue rate of the current GPU (libsbenv's probe kernel)."""
+    t = ctypes.c_double()
+    if env_lib().sb_fp64_peak(ctypes.byref(t)) != 0:
+        raise RuntimeError(env_lib().sb_last_error().decode())
+    return t.value
 
 
 def _dict_to_py(d) -> dict:

@@ -116,6 +116,7 @@ struct Engine {
     double center_beta = 0.01;
     std::vector<double> rn_mu, rn_var, last_sc;
     float* d_rnorm = nullptr;
+    int* d_test_ctl = nullptr;   // sb_test_stall's {on, spin limit}
     std::vector<int> first_len;
     std::vector<unsigned long long> start_rng0;
     int dense_threads = 32;          // k_dense block (dense_threads(k_max))
@@ -303,6 +304,9 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     E.random_start = kw_num(kw, "random_start", 0.0) != 0.0;
     const bool desync = !E.random_start && kw_num(kw, "desync", 0.0) != 0.0;
     const unsigned long long start_seed = (unsigned long long)(long long)kw_num(kw, "random_start_seed", 0.0);
+    // index of this batch's first env in a batch sharded over several GPUs: the
+    // per-env draws (desync cut, random-start stream) follow the global index
+    const long long env_offset = std::max(0LL, (long long)kw_num(kw, "env_offset", 0.0));
     E.rew_norm = kw_num(kw, "rew_norm", 0.0) != 0.0;
     E.rew_center = !E.rew_norm && kw_num(kw, "rew_center", 0.0) != 0.0;
     {
@@ -428,6 +432,7 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
         if (se.empty() && fold) se = build_fold(h);
         if (!se.empty()) { set_err("group %d: %s", c, se.c_str()); return false; }
         gd.fold = fold ? 1 : 0;
+        gd.stall_row = h.fwd.unpublished_row;
         if (fold) {
             gd.zr_p = E.arena.upload(h.zr_p, ok); gd.zr_col = E.arena.upload(h.zr_col, ok);
             gd.zr_x = E.arena.upload(h.zr_x, ok); gd.zr_nnz = (int)h.zr_x.size();
@@ -550,14 +555,15 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     for (int env = 0; env < n; env++) {
         const int ep_len = E.hs[E.ei[env].scn].max_steps;
         E.first_len[env] = ep_len;
+        const unsigned long long gid = (unsigned long long)(env_offset + env);
         if (desync) {
-            unsigned long long h = 0x9E3779B97F4A7C15ULL * (unsigned long long)(env + 1);
+            unsigned long long h = 0x9E3779B97F4A7C15ULL * (gid + 1);
             h ^= h >> 31;
             h *= 0xBF58476D1CE4E5B9ULL;
             h ^= h >> 29;
             E.first_len[env] = 1 + (int)(h % (unsigned long long)ep_len);
         }
-        E.start_rng0[env] = start_mix(start_seed ^ (0x9e3779b97f4a7c15ULL * (unsigned long long)(env + 1)));
+        E.start_rng0[env] = start_mix(start_seed ^ (0x9e3779b97f4a7c15ULL * (gid + 1)));
     }
     // ---- context ----
     StepCtx& C = E.ctx;
@@ -591,6 +597,7 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     C.live_scn = E.arena.zeros<double>((size_t)G * 4, ok);
     C.ep_scn = E.arena.zeros<double>((size_t)G * 2, ok);
     C.status = E.arena.zeros<int>(1, ok);
+    C.test_ctl = E.d_test_ctl = E.arena.zeros<int>(2, ok);
     C.nz_max = nz_max;
     // ---- occupancy streams and the producers' slots ----
     {
@@ -820,6 +827,24 @@ __global__ void __launch_bounds__(256) k_dense_transpose(int k, int n, const dou
     }
 }
 
+// fp64 issue-rate probe: every thread runs kFmaChains independent fused
+// multiply-add chains (two flops each) in registers; the result is stored so
+// the work stays live. A plain timed kernel, no clock setting is touched.
+constexpr int kFmaChains = 8;
+__global__ void __launch_bounds__(256) k_fp64_probe(int iters, double a, double b, double* out) {
+    double x[kFmaChains];
+#pragma unroll
+    for (int c = 0; c < kFmaChains; c++) x[c] = (double)(threadIdx.x + c);
+    for (int i = 0; i < iters; i++) {
+#pragma unroll
+        for (int c = 0; c < kFmaChains; c++) x[c] = fma(x[c], a, b);
+    }
+    double s = 0.0;
+#pragma unroll
+    for (int c = 0; c < kFmaChains; c++) s += x[c];
+    if (s == 12345.678) out[blockIdx.x * blockDim.x + threadIdx.x] = s;   // practically never taken
+}
+
 // ============================== C ABI ==============================
 
 extern "C" {
@@ -913,6 +938,8 @@ void puf_reset(Env* envs) {
     if (!g_eng || !g_eng->ready) { set_err("puf_reset: no env batch"); return; }
     Engine& E = *g_eng;
     if (cudaStreamSynchronize(E.stream) != cudaSuccess) { set_err("puf_reset: stream error"); return; }
+    // a restart clears the device status word of the previous episodes
+    if (cudaMemset(E.ctx.status, 0, sizeof(int)) != cudaSuccess) { set_err("puf_reset: memset failed"); return; }
     for (int env = 0; env < E.n_env; env++) {
         E.envs[env].step = 0;
         E.envs[env].ep_ret = 0.0f;
@@ -1368,6 +1395,95 @@ int sb_solve_bytes(double* per_launch) {
         total += per_env * E.gd[c].n_env + shared;
     }
     *per_launch = total;
+    return 0;
+}
+
+int sb_solve_flops(double* per_launch) {
+    // fp64 operations of one solve launch: per env and triangular solve, a
+    // multiply and a subtract per off-diagonal factor term and a divide per U
+    // row; the forcing (7 per row), the coupling products (2 per term: sensed
+    // and applied, or R and Z), the dense system (2/3 k^3 + 2 k^2) and the
+    // mass / field update (3 per row). The exact build runs two solves, the
+    // folded one a single one.
+    if (!g_eng || !per_launch) return -1;
+    Engine& E = *g_eng;
+    double total = 0.0;
+    for (size_t c = 0; c < E.gd.size(); c++) {
+        const HostGroup& h = E.hg[c];
+        const bool fold = E.gd[c].fold != 0;
+        const double tri = 2.0 * (double)(h.nnzL - h.n) + 2.0 * (double)(h.nnzU - h.n) + (double)h.n;
+        const double coupling = fold ? 2.0 * (double)(h.zr_x.size() + h.rs_x.size())
+                                     : 2.0 * (double)(h.ap_x.size() + h.sn_x.size());
+        const double k = h.k;
+        const double per_env = (fold ? 1.0 : 2.0) * tri + coupling + 7.0 * h.n + 3.0 * h.n +
+                               (2.0 / 3.0) * k * k * k + 2.0 * k * k;
+        total += per_env * E.gd[c].n_env;
+    }
+    *per_launch = total;
+    return 0;
+}
+
+int sb_fp64_peak(double* tflops) {
+    if (!tflops) return -1;
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return -1;
+    const int blocks = sms * 8, threads = 256, iters = 1 << 14;
+    double* out = nullptr;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    bool ok = cudaMalloc(&out, sizeof(double) * (size_t)blocks * threads) == cudaSuccess &&
+              cudaEventCreate(&e0) == cudaSuccess && cudaEventCreate(&e1) == cudaSuccess;
+    float best = 1e30f;
+    for (int rep = 0; ok && rep < 4; rep++) {
+        cudaEventRecord(e0);
+        k_fp64_probe<<<blocks, threads>>>(iters, 1.0000001, 1e-9, out);
+        cudaEventRecord(e1);
+        ok = cudaEventSynchronize(e1) == cudaSuccess;
+        float ms = 0.0f;
+        if (ok) cudaEventElapsedTime(&ms, e0, e1);
+        if (rep > 0 && ms < best) best = ms;   // the first launch warms up
+    }
+    cudaFree(out);
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    if (!ok) { set_err("sb_fp64_peak: CUDA error"); return -1; }
+    *tflops = 2.0 * kFmaChains * (double)iters * blocks * threads / (best * 1e-3) / 1e12;
+    return 0;
+}
+
+int sb_scenario_stats(double* out, int clear) {
+    // [n_scenarios][6]: step reward sum, mean-deviation sum, steps, reward^2
+    // sum, sum of whole-episode mean rewards, whole episodes
+    if (!g_eng || !out) return -1;
+    Engine& E = *g_eng;
+    const size_t G = E.sd.size();
+    std::vector<double> hs(G * 4), he(G * 2);
+    if (cudaStreamSynchronize(E.stream) != cudaSuccess ||
+        cudaMemcpy(hs.data(), E.ctx.live_scn, hs.size() * sizeof(double), cudaMemcpyDeviceToHost) != cudaSuccess ||
+        cudaMemcpy(he.data(), E.ctx.ep_scn, he.size() * sizeof(double), cudaMemcpyDeviceToHost) != cudaSuccess)
+        return -1;
+    for (size_t i = 0; i < G; i++) {
+        for (int q = 0; q < 4; q++) out[i * 6 + q] = hs[i * 4 + q];
+        out[i * 6 + 4] = he[i * 2];
+        out[i * 6 + 5] = he[i * 2 + 1];
+    }
+    if (clear) {
+        cudaMemset(E.ctx.live_scn, 0, hs.size() * sizeof(double));
+        cudaMemset(E.ctx.ep_scn, 0, he.size() * sizeof(double));
+    }
+    return (int)G;
+}
+
+int sb_test_stall(int on, unsigned int spin_limit) {
+    if (!g_eng || !g_eng->ready) { set_err("sb_test_stall: no env batch"); return -1; }
+    for (const GroupDev& g : g_eng->gd)
+        if (on && g.stall_row < 0) { set_err("sb_test_stall: a group's L sweep publishes every row"); return -1; }
+    const int v[2] = {on ? 1 : 0, (int)std::min<unsigned int>(spin_limit, 1u << 30)};
+    if (cudaStreamSynchronize(g_eng->stream) != cudaSuccess ||
+        cudaMemcpy(g_eng->d_test_ctl, v, sizeof(v), cudaMemcpyHostToDevice) != cudaSuccess) {
+        set_err("sb_test_stall: copy failed");
+        return -1;
+    }
     return 0;
 }
 

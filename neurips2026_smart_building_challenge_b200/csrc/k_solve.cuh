@@ -23,7 +23,7 @@ struct SlabDesc {
     int pad;
 };
 
-constexpr uint32_t kSpinLimit = 1u << 22;   // polls of one ready flag before the wait gives up
+constexpr uint32_t kSpinLimit = 1u << 22;   // polls of one ready flag before the wait gives up (about a second)
 
 struct SolveShared {
     double* X;            // [B][stride]
@@ -31,6 +31,7 @@ struct SolveShared {
     uint8_t* ready;       // [n + 1] row ready flags: 2 epoch final, 2 epoch - 1 outside terms applied
     uint64_t* bars;       // [kSweepWarps][kStagesMax] completion barriers of the ring stages
     volatile int* abort;  // first error of this CTA
+    uint32_t spin_limit;  // polls of one ready flag (kSpinLimit unless a failure test lowers it)
 };
 
 // Waits (acquire) until every listed row's ready flag reaches its target:
@@ -46,7 +47,7 @@ __device__ inline bool wait_rows(const SolveShared& sh, const uint16_t* list, ui
         const uint32_t need = (w & kWaitPartial) ? fin - 1 : fin;
         uint32_t spins = 0;
         while (ld_acquire_u8(sh.ready + r) < need) {
-            if (++spins >= kSpinLimit) {
+            if (++spins >= sh.spin_limit) {
                 atomicCAS((int*)sh.abort, 0, kErrWaitTimeout);
                 ok = false;
                 break;
@@ -237,7 +238,10 @@ __device__ inline bool run_block(const SolveShared& sh, const StageRing& rg, uin
 // for other warps' rows, load the new rows. Block records: run_block.
 // Every branch on a record's contents is warp-uniform (record-level flags),
 // so the warp never needs a vote on the hot path.
-__device__ inline void run_sweep(const SolveShared& sh, const Sweep& sw, int B, int S, int n, uint32_t epoch) {
+// stall_row >= 0 (failure test only): warp 0 first waits for that row, which
+// no warp publishes, so the bounded wait runs out and the sweep aborts.
+__device__ inline void run_sweep(const SolveShared& sh, const Sweep& sw, int B, int S, int n, uint32_t epoch,
+                                 int stall_row = -1) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int g = lane >> 3, e = lane & 7;
     const uint32_t fin = 2 * epoch, un = (uint32_t)n;
@@ -254,6 +258,10 @@ __device__ inline void run_sweep(const SolveShared& sh, const Sweep& sw, int B, 
 
     rg.start(lane);
     int err = rg.nst == 0 ? kErrBadBundle : (rg.land(0) ? kErrNone : kErrRingTimeout);
+    if (stall_row >= 0 && w == 0 && err == kErrNone) {
+        const uint16_t wr = (uint16_t)stall_row;
+        if (!wait_rows(sh, &wr, 1, un, fin)) err = kErrWaitTimeout;
+    }
     const uint8_t* rp = rg.ring;
     uint32_t q = 0;
     bool ctrl = true;
@@ -594,6 +602,8 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
     double* amb_e = reinterpret_cast<double*>(misc + 4);   // [8]
     int* active = reinterpret_cast<int*>(amb_e + 8);        // [8]
     if (tid == 0) misc[0] = 0;
+    const int stall = ctx->test_ctl[0] ? g.stall_row : -1;
+    sh.spin_limit = ctx->test_ctl[1] > 0 ? (uint32_t)ctx->test_ctl[1] : kSpinLimit;
     for (int i = tid; i <= n; i += blockDim.x) sh.ready[i] = i < n ? 0 : 0xFF;   // slot n: "no row"
     // padding slots (the zero column of padded terms) and envs the slab does not fill
     for (int e = 0; e < B; e++) {
@@ -658,7 +668,7 @@ k_solve(const StepCtx* __restrict__ ctx, const SlabDesc* __restrict__ slabs) {
         __syncthreads();
 
         // ---- first solve (the folded build: its forward half only) ----
-        if (tid < kSweepWarps * 32) run_sweep(sh, g.fwd, B, S, n, 1);
+        if (tid < kSweepWarps * 32) run_sweep(sh, g.fwd, B, S, n, 1, stall);
         __syncthreads();
         if (!g.fold) {
             if (tid < kSweepWarps * 32) run_sweep(sh, g.bwd, B, S, n, 2);

@@ -204,6 +204,7 @@ struct GroupDev {
     // folded air side (fold = 1): phase 0 runs the L sweep only and reads the
     // sensed values as R z; phase 1 starts the U sweep from z + Z q
     int fold;
+    int stall_row;                  // a row of the L sweep no warp publishes (failure test)
     int zr_nnz, rs_nnz;
     const int32_t *zr_p, *zr_col;   // Z = L^-1 applied, CSR by row position (coupled columns)
     const double* zr_x;
@@ -353,6 +354,9 @@ struct StepCtx {
     // (mean, inv_std); null: rewards scaled by reward_scale
     const float* rnorm;
     double* znclip;             // [3] rewards beyond 1 / 3 / 5 (rew_norm only)
+    // failure test (sb_test_stall): {1: warp 0 of every slab waits at the start
+    // of the L sweep for a row no warp publishes, spin limit (0: the default)}
+    const int* test_ctl;
     // air side: per env the dense system's right side (k_solve phase 0), then
     // its solution (k_dense), read by k_solve phase 1
     double* airq;           // [n_env][k_max]

@@ -566,6 +566,8 @@ std::string build_sweep(int n, const std::vector<std::vector<std::pair<int, doub
     }
     if (remaining != 0) return "sweep schedule left rows unfinished";
 
+    for (int r = 0; r < n && out.unpublished_row < 0; r++)
+        if (!waited[r] && !owaited[r]) out.unpublished_row = r;
     // ---- publish bits and record summaries, then stage padding. A control
     // record finishes the row its group was given before; a block publishes
     // the rows another warp waits for.

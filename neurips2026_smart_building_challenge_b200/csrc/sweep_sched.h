@@ -20,6 +20,7 @@ struct HostSweep {
     int64_t terms = 0, bundles = 0, blocks = 0, prewaits = 0, publishes = 0, pieces = 0;
     int64_t dense_blocks = 0, block_rows = 0;
     double sim_cycles = 0;                  // modelled length of the sweep (cycles of one warp)
+    int unpublished_row = -1;               // a row no warp waits for (its ready flag is never set)
 };
 
 // Builds the program of one triangular sweep.

@@ -257,3 +257,56 @@ def test_second_reset_matches_oracle(scenario_cache):
         assert env.status() == 0
     finally:
         env.close()
+
+
+def test_bounded_wait_runs_out_and_reports(scenario_cache):
+    """A sweep wait that can never be satisfied (sb_test_stall: warp 0 waits for
+    a row no warp publishes, under a short spin limit) ends with status 5 and
+    no fault or hang; after puf_reset the env steps exactly as the oracle does."""
+    import torch
+
+    from neurips2026_smart_building_challenge_b200 import config_dir
+
+    d = config_dir(1, scenario_cache, n_steps=60)
+    n = 2
+    env = vec(n, d)
+    try:
+        path = scenario_paths(d)[0]
+        rng = np.random.default_rng(16)
+        # the oracle envs step beside the device env throughout, so their random
+        # streams are where the device env's are when both restart
+        orc = [OracleEnv(path) for _ in range(n)]
+
+        def act():
+            return np.concatenate([actions(rng, 1, orc[e].n_cont, orc[e].n_disc) for e in range(n)])
+
+        env.reset()
+        for e in range(n):
+            orc[e].reset()
+        for stalled in (False, True):
+            if stalled:
+                assert env.lib.sb_test_stall(1, 1 << 12) == 0
+            a = act()
+            env.step(torch.from_numpy(a).to(env.device))
+            env.synchronize()
+            for e in range(n):
+                orc[e].step(a[e])
+            assert env.status() == (5 if stalled else 0)
+        assert env.lib.sb_test_stall(0, 0) == 0
+        env.reset()
+        assert env.status() == 0
+        env.synchronize()
+        obs = env.obs.cpu().numpy()
+        for e in range(n):
+            assert np.array_equal(obs[e].view(np.uint32), orc[e].reset().view(np.uint32))
+        for s in range(5):
+            a = act()
+            env.step(torch.from_numpy(a).to(env.device))
+            env.synchronize()
+            obs = env.obs.cpu().numpy()
+            for e in range(n):
+                o = orc[e].step(a[e])[0]
+                assert np.array_equal(obs[e].view(np.uint32), o.view(np.uint32)), (s, e)
+        assert env.status() == 0
+    finally:
+        env.close()
