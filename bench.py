@@ -9,14 +9,14 @@ One step = one puf_step of every env (decode, HVAC, fp64 thermal solve with the
 air side, convection, occupancy, observation, reward, episode log).
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
-                    [--workload config2|config3|config4] [--envs E] [--solve folded|exact]
+                    [--workload config2|config3|config4] [--envs E] [--solve corrected|folded|exact]
     python bench.py --rollout [--gpus N --steps K --warmup W]
     python bench.py --month
 
-The stated build is the folded air side (--solve folded, the default): one L/U
-pair per step, within the north star's 1e-9 per-step / 1e-6 K per-month
-contract (tests/test_fold_gpu.py); the bit-exact build's numbers are reported
-beside it under "variants".
+The stated build is the corrected air side (--solve corrected, the default): one
+L/U pair per step plus W q, within the north star's 1e-9 per-step / 1e-6 K
+per-month contract (tests/test_fold_gpu.py); the bit-exact and folded builds'
+numbers are reported beside it under "variants".
 
 --rollout measures BASELINE configuration 5 instead: the end-to-end env+policy
 step rate of policy-in-loop rollouts (a random-init shared MLP, hidden 128, tanh,
@@ -62,9 +62,13 @@ WORKLOADS = {
                     desc="config4: 7,680 synthetic buildings per GPU over the config-2 mix (6 layouts x 5 "
                          "climates); seeded Beta(a,b) actions, a,b~U(0.5,12)"),
 }
-SOLVE_NOTE = {"folded": "folded air side (solve_exact=0): one L/U pair per step; within the north star's 1e-9 "
-                        "per step / 1e-6 K per month contract (tests/test_fold_gpu.py)",
+SOLVE_NOTE = {"corrected": "corrected air side (solve_exact=0): one L/U pair per step plus W q with W = A^-1 applied "
+                           "precomputed; within the north star's 1e-9 per step / 1e-6 K per month contract "
+                           "(tests/test_fold_gpu.py)",
+              "folded": "folded air side (solve_exact=0, fold=1): one L/U pair per step, the reference GPU "
+                        "backend's method; within the same contract (tests/test_fold_gpu.py)",
               "exact": "exact (solve_exact=1): the reference core's two L/U solves, bit for bit"}
+SOLVE_KW = {"corrected": {"solve_exact": 0}, "folded": {"solve_exact": 0, "fold": 1}, "exact": {"solve_exact": 1}}
 SMI_Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
@@ -81,9 +85,9 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--rollout", action="store_true", help="configuration 5: env+policy steps in a CUDA graph")
     ap.add_argument("--horizon", type=int, default=128, help="rollout horizon (--rollout)")
-    ap.add_argument("--solve", default="folded", choices=["exact", "folded"],
-                    help="exact: the reference core's two triangular solves, bit for bit; folded: one L/U "
-                         "pair (the reference GPU backend's folded air side, 1e-9 per-step contract)")
+    ap.add_argument("--solve", default="corrected", choices=sorted(SOLVE_NOTE),
+                    help="exact: the reference core's two triangular solves, bit for bit; corrected / folded: "
+                         "one L/U pair per step (1e-9 per-step contract)")
     ap.add_argument("--month", action="store_true",
                     help="configuration 1: one building for its whole month, GPU and the reference core (1 thread)")
     args = ap.parse_args()
@@ -409,14 +413,14 @@ def run_ours(args) -> None:
     pool_np = action_pool(n, 8, seed=1234 + rank)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=f"cuda:{local}")   # > 126 MB L2
     variants = {}
-    other = "exact" if args.solve == "folded" else "folded"
-    # the other build first (value and per-kernel times only), then the stated one
-    for solve in (other, args.solve):
-        env = SmartBuildingsVec(n, blob_dir=str(d), groups=groups, device=f"cuda:{local}",
-                                solve_exact=1 if solve == "exact" else 0, env_offset=start)
+    others = [v for v in sorted(SOLVE_NOTE) if v != args.solve]
+    # the other builds first (value and per-kernel times only), then the stated one
+    for solve in others + [args.solve]:
+        env = SmartBuildingsVec(n, blob_dir=str(d), groups=groups, device=f"cuda:{local}", env_offset=start,
+                                **SOLVE_KW[solve])
         env.reset()
         pool = torch.from_numpy(pool_np).to(env.device)
-        if solve == other:
+        if solve != args.solve:
             ms_total = timed_steps(env, pool, flush, args.steps, args.warmup, world, torch, dist)
             variants[solve] = {"value": world * n * args.steps / (ms_total / 1e3),
                                "ms_per_step": ms_total / args.steps, "note": SOLVE_NOTE[solve],
@@ -530,8 +534,8 @@ def run_month(args) -> None:
                     "kind": "reference" if path == REF else "port"}}
     torch.cuda.set_device(0)
     dev_actions = torch.from_numpy(np.stack(acts)).cuda()
-    for solve in ("exact", "folded"):
-        env = SmartBuildingsVec(1, blob_dir=str(d), device="cuda:0", solve_exact=1 if solve == "exact" else 0)
+    for solve in sorted(SOLVE_NOTE):
+        env = SmartBuildingsVec(1, blob_dir=str(d), device="cuda:0", **SOLVE_KW[solve])
         env.reset()
         s = env.stream
         for i in range(20):   # warm-up

@@ -134,9 +134,11 @@ void dict_set_str(Dict* d, const char* key, const char* value);
  * groups (scenario count, 0 = n/32), max_steps (0 = the blob's episode
  * length), merge_weathers (share one solver group across weathers of a
  * building, default 1), reward_scale (default 1), solve_exact (1, default:
- * the reference core's two triangular solves per step, bit for bit; 0: the
- * folded air side of the reference's GPU backend, one L and one U sweep per
- * step, agreeing with the reference within 1e-9 relative per step).
+ * the reference core's two triangular solves per step, bit for bit; 0: one L
+ * and one U sweep per step, agreeing with the reference within 1e-9 relative
+ * per step -- the air-side correction added as W q with W = A^-1 applied
+ * precomputed per building (default), or with fold = 1 folded into the sweep
+ * pair as the reference's GPU backend does).
  * Episode options of the reference's GPU backend (smart_buildings.cu:2583-2608,
  * 2806-2816, 1636-1657, 1936-2050): desync (1: env i's first episode ends at a
  * step in [1, episode length] drawn from i; later episodes are whole, the cut

@@ -36,6 +36,7 @@
 #include "k_pre.cuh"
 #include "k_rng.cuh"
 #include "k_solve.cuh"
+#include "k_correct.cuh"
 #include "k_policy.cuh"
 #include "tables.h"
 
@@ -102,6 +103,10 @@ struct Engine {
     std::vector<ScnDev> sd;
     std::vector<EnvIndex> ei;
     std::vector<SlabDesc> slabs;
+    std::vector<CorrTile> ctiles;   // k_correct's tiles (corrected build)
+    CorrTile* d_ctiles = nullptr;
+    int solve_mode = 0;             // 0 exact, 1 folded, 2 corrected
+    size_t smem_corr = 0;
     StepCtx ctx{};
     DevArena arena;
     StepCtx* d_ctx = nullptr;
@@ -246,20 +251,30 @@ cudaError_t launch_dense(Engine& E, cudaStream_t st) {
 }
 
 // The solve on the high-priority stream: phase 0 (first L/U solve), the
-// dense air-side solves, phase 1 (second L/U solve, mass, field), and beside
-// phase 1 the random inputs of the next transition (k_post of this step reads
-// the ones made during the step before).
+// dense air-side solves, then phase 1 (second L/U solve, mass, field) or, in
+// the corrected build, k_correct (y + W q, mass, field). The random inputs of
+// the next transition run beside the longest solve kernel (k_post of this step
+// reads the ones made during the step before).
+cudaError_t launch_phase1(Engine& E) {
+    if (E.solve_mode == 2) {
+        k_correct<<<(unsigned)E.ctiles.size(), kCorrThreads, E.smem_corr, E.hi>>>(E.d_ctx, E.d_ctiles);
+    } else {
+        k_solve<1><<<(unsigned)E.slabs.size(), kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
+    }
+    return cudaGetLastError();
+}
+
 cudaError_t launch_solve(Engine& E) {
     const unsigned slabs = (unsigned)E.slabs.size();
+    const bool corr = E.solve_mode == 2;
     k_solve<0><<<slabs, kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
     cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess && corr) e = launch_rng(E, E.hi, true);
     if (e != cudaSuccess) return e;
     e = launch_dense(E, E.hi);
-    if (e != cudaSuccess) return e;
-    k_solve<1><<<slabs, kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-    return launch_rng(E, E.hi, true);
+    if (e == cudaSuccess) e = launch_phase1(E);
+    if (e == cudaSuccess && !corr) e = launch_rng(E, E.hi, true);
+    return e;
 }
 
 bool launch_step(Engine& E) {
@@ -298,8 +313,12 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     const bool merge = kw_num(kw, "merge_weathers", 1.0) != 0.0;
     const int max_steps_kw = (int)kw_num(kw, "max_steps", 0.0);
     // solve_exact = 1 (default): the reference's two L/U solves, bit for bit;
-    // 0: the folded air side (one L/U pair; within the 1e-9 per-step contract)
-    const bool fold = kw_num(kw, "solve_exact", 1.0) == 0.0;
+    // 0: one L/U pair, within the 1e-9 per-step contract -- the air side
+    // corrected by W q (default) or folded into the pair (fold = 1)
+    const bool fast = kw_num(kw, "solve_exact", 1.0) == 0.0;
+    const bool fold = fast && kw_num(kw, "fold", 0.0) != 0.0;
+    const bool corr = fast && !fold;
+    E.solve_mode = fold ? 1 : (corr ? 2 : 0);
     // episode options of the reference GPU backend (smart_buildings.cu:2583-2608)
     E.random_start = kw_num(kw, "random_start", 0.0) != 0.0;
     const bool desync = !E.random_start && kw_num(kw, "desync", 0.0) != 0.0;
@@ -432,7 +451,22 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
         if (se.empty() && fold) se = build_fold(h);
         if (!se.empty()) { set_err("group %d: %s", c, se.c_str()); return false; }
         gd.fold = fold ? 1 : 0;
+        gd.corr = corr ? 1 : 0;
         gd.stall_row = h.fwd.unpublished_row;
+        if (corr) {
+            // W in row tiles of kCorrRows, each tile [k][kCorrRows] (rows past n zero)
+            const int nt = (h.n + kCorrRows - 1) / kCorrRows;
+            std::vector<double> wt((size_t)nt * h.k * kCorrRows, 0.0);
+            for (int i = 0; i < h.n; i++)
+                for (int q = 0; q < h.k; q++)
+                    wt[((size_t)(i / kCorrRows) * h.k + q) * kCorrRows + i % kCorrRows] = h.W[(size_t)i * h.k + q];
+            gd.W = E.arena.upload(wt, ok);
+            E.smem_corr = std::max(E.smem_corr, corr_smem_bytes(h.k));
+            for (int rt = 0; rt < nt; rt++)
+                for (int e0 = 0; e0 < gd.n_env; e0 += kCorrEnvs)
+                    E.ctiles.push_back({c, rt * kCorrRows, gd.env0 + e0, std::min(kCorrEnvs, gd.n_env - e0),
+                                        (long long)rt * h.k * kCorrRows});
+        }
         if (fold) {
             gd.zr_p = E.arena.upload(h.zr_p, ok); gd.zr_col = E.arena.upload(h.zr_col, ok);
             gd.zr_x = E.arena.upload(h.zr_x, ok); gd.zr_nnz = (int)h.zr_x.size();
@@ -677,6 +711,7 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     E.smem_dense = std::max<size_t>(16, dense_smem_doubles(k_max) * sizeof(double));
     E.dense_threads = dense_threads(std::max(k_max, 1));
     E.d_slabs = E.arena.upload(E.slabs, ok);
+    if (!E.ctiles.empty()) E.d_ctiles = E.arena.upload(E.ctiles, ok);
     if (!ok) return false;
     // per-env state that persists across resets (pump head set once at init,
     // sb_sim.c:71-75; the current episode's length, cut for desync)
@@ -724,6 +759,9 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
         return false;
     }
     CK(cudaFuncSetAttribute(k_conv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_conv));
+    if (E.smem_corr > smem_cap) { set_err("correction kernel needs %zu B of shared memory", E.smem_corr); return false; }
+    if (E.smem_corr > 0)
+        CK(cudaFuncSetAttribute(k_correct, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_corr));
     CK(cudaFuncSetAttribute(k_occ, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_occ));
     CK(cudaStreamCreateWithFlags(&E.own_stream, cudaStreamNonBlocking));
     {
@@ -1353,12 +1391,14 @@ int sb_step_timed(float* ms) {
     cudaEventRecord(E.ev_fork, E.stream);
     cudaStreamWaitEvent(E.hi, E.ev_fork, 0);
     const unsigned slabs = (unsigned)E.slabs.size();
+    const bool corr = E.solve_mode == 2;
     k_solve<0><<<slabs, kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
+    if (corr) launch_rng(E, E.hi, true);
     cudaEventRecord(ev[4], E.hi);
     launch_dense(E, E.hi);
     cudaEventRecord(ev[5], E.hi);
-    k_solve<1><<<slabs, kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
-    launch_rng(E, E.hi, true);
+    launch_phase1(E);
+    if (!corr) launch_rng(E, E.hi, true);
     cudaEventRecord(ev[2], E.hi);
     cudaStreamWaitEvent(E.stream, ev[2], 0);
     cudaEventRecord(ev[6], E.stream);
@@ -1366,13 +1406,13 @@ int sb_step_timed(float* ms) {
     cudaEventRecord(ev[3], E.stream);
     const bool ok = cudaEventSynchronize(ev[3]) == cudaSuccess;
     if (ok) {
-        ms[0] = -1.0f;                                 // k_conv, k_occ: beside phase 1, inside ms[6]
+        ms[0] = -1.0f;                                 // k_conv, k_occ: beside a phase, inside its interval
         cudaEventElapsedTime(&ms[1], ev[0], ev[1]);   // k_pre
         cudaEventElapsedTime(&ms[2], ev[1], ev[2]);   // the solve: phase 0, k_dense, phase 1
         cudaEventElapsedTime(&ms[3], ev[6], ev[3]);   // k_post
         cudaEventElapsedTime(&ms[4], ev[1], ev[4]);   // phase 0
         cudaEventElapsedTime(&ms[5], ev[4], ev[5]);   // k_dense
-        cudaEventElapsedTime(&ms[6], ev[5], ev[2]);   // phase 1 (with the producers beside it)
+        cudaEventElapsedTime(&ms[6], ev[5], ev[2]);   // phase 1 or k_correct
     }
     for (auto& e : ev) cudaEventDestroy(e);
     return ok ? 0 : -1;
@@ -1388,10 +1428,12 @@ int sb_solve_bytes(double* per_launch) {
     for (size_t c = 0; c < E.gd.size(); c++) {
         const HostGroup& h = E.hg[c];
         const double per_env = 8.0 * (2.0 * h.ncv + 2.0 * h.n) + 8.0 * (h.nz + 3.0 * h.k);
-        // coupling tables: applied + sensed (exact build) or Z + R (folded build)
-        const double coupling = E.gd[c].fold ? (double)(h.zr_x.size() + h.rs_x.size())
-                                             : (double)(h.ap_x.size() + h.sn_x.size());
-        const double shared = 12.0 * (double)(h.nnzL + h.nnzU) + 12.0 * coupling + 8.0 * (double)h.k * h.k;
+        // coupling tables: applied + sensed (exact build), Z + R (folded build),
+        // sensed + the dense response W (corrected build)
+        const double coupling = E.gd[c].fold ? 12.0 * (double)(h.zr_x.size() + h.rs_x.size())
+                                : E.gd[c].corr ? 12.0 * (double)h.sn_x.size() + 8.0 * (double)h.n * h.k
+                                               : 12.0 * (double)(h.ap_x.size() + h.sn_x.size());
+        const double shared = 12.0 * (double)(h.nnzL + h.nnzU) + coupling + 8.0 * (double)h.k * h.k;
         total += per_env * E.gd[c].n_env + shared;
     }
     *per_launch = total;
@@ -1410,12 +1452,13 @@ int sb_solve_flops(double* per_launch) {
     double total = 0.0;
     for (size_t c = 0; c < E.gd.size(); c++) {
         const HostGroup& h = E.hg[c];
-        const bool fold = E.gd[c].fold != 0;
+        const bool fold = E.gd[c].fold != 0, corr = E.gd[c].corr != 0;
         const double tri = 2.0 * (double)(h.nnzL - h.n) + 2.0 * (double)(h.nnzU - h.n) + (double)h.n;
         const double coupling = fold ? 2.0 * (double)(h.zr_x.size() + h.rs_x.size())
-                                     : 2.0 * (double)(h.ap_x.size() + h.sn_x.size());
+                                : corr ? 2.0 * (double)h.sn_x.size() + 2.0 * (double)h.n * h.k
+                                       : 2.0 * (double)(h.ap_x.size() + h.sn_x.size());
         const double k = h.k;
-        const double per_env = (fold ? 1.0 : 2.0) * tri + coupling + 7.0 * h.n + 3.0 * h.n +
+        const double per_env = (fold || corr ? 1.0 : 2.0) * tri + coupling + 7.0 * h.n + 3.0 * h.n +
                                (2.0 / 3.0) * k * k * k + 2.0 * k * k;
         total += per_env * E.gd[c].n_env;
     }

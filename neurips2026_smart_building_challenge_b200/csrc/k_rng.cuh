@@ -19,9 +19,11 @@
 //     each new episode's start day (gpu/smart_buildings.cu:1636-1657).
 // Transition q (counted from puf_reset) is written to slot q & 1 and read by
 // that step's k_post; k_occ's reset mode writes slot kResetSlot for puf_reset.
-// In a step both run as programmatic dependents of the solve's phase 1 (on the
-// SMs its slabs leave free, once every slab is resident) and complete only
-// after it (griddepcontrol.wait at their end, reached by every CTA).
+// In a step both run as programmatic dependents of the solve's longest kernel
+// (on the SMs its slabs leave free, once every slab is resident). Only CTA 0
+// of each waits for its primary (griddepcontrol.wait) before it exits, so the
+// producer completes after the primary while its other CTAs free their SMs as
+// soon as their work is done.
 #pragma once
 #include "dev_util.cuh"
 
@@ -192,7 +194,7 @@ __global__ void __launch_bounds__(32) k_conv(const StepCtx* __restrict__ ctx, in
     if (!restore) conv_transition(ctx, s, g, smem, lane);
     else if (*ctx->produced)
         for (int x = lane; x < 625; x += 32) s.conv_mt[x] = s.conv_ckpt[x];
-    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (blockIdx.x == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 // One warp per occupancy stream, kOccWarps streams per CTA. reset = 1: the
@@ -209,7 +211,7 @@ __global__ void __launch_bounds__(32 * kOccWarps) k_occ(const StepCtx* __restric
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int u = blockIdx.x * kOccWarps + (threadIdx.x >> 5);
     if (u < ctx->n_ostreams) occ_stream(ctx, u, reset, smem);
-    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (blockIdx.x == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 // One occupancy stream (one warp of k_occ).

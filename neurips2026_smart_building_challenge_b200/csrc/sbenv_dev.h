@@ -204,6 +204,12 @@ struct GroupDev {
     // folded air side (fold = 1): phase 0 runs the L sweep only and reads the
     // sensed values as R z; phase 1 starts the U sweep from z + Z q
     int fold;
+    // corrected air side (corr = 1): phase 0 is the exact build's first solve
+    // (y and the sensed right side), and k_correct forms y + W q with the
+    // precomputed response W = A^-1 applied ([n][k], row order) instead of a
+    // second triangular solve
+    int corr;
+    const double* W;                // row tiles of k_correct, each [k][kCorrRows]
     int stall_row;                  // a row of the L sweep no warp publishes (failure test)
     int zr_nnz, rs_nnz;
     const int32_t *zr_p, *zr_col;   // Z = L^-1 applied, CSR by row position (coupled columns)

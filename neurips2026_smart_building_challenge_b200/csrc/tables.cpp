@@ -258,13 +258,16 @@ std::string build_group(const sbb::Reader& b, HostGroup& g) {
             for (auto& e2 : rows[i]) { g.ap_col.push_back(e2.first); g.ap_x.push_back(e2.second); }
             g.ap_rp[i + 1] = (int32_t)g.ap_col.size();
         }
-        // S = sensed A^-1 applied (complete_port/csim/sb_fdm.c:103-114)
+        // S = sensed A^-1 applied (complete_port/csim/sb_fdm.c:103-114); the
+        // columns A^-1 applied are kept in row order as W
         g.S.assign((size_t)k * k, 0.0);
+        g.W.assign((size_t)n * k, 0.0);
         std::vector<double> r(n), yr;
         for (int j = 0; j < k; j++) {
             std::fill(r.begin(), r.end(), 0.0);
             for (int q = ap[j]; q < ap[j + 1]; q++) r[ai[q]] = ax[q];
             replay(F, r, yr);
+            for (int t = 0; t < n; t++) g.W[(size_t)g.row_of_solved[t] * k + j] = yr[t];
             for (int i = 0; i < k; i++) {
                 double acc = 0.0;
                 for (int q = sp[i]; q < sp[i + 1]; q++) acc += sx[q] * yr[si[q]];

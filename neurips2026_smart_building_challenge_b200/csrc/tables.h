@@ -25,6 +25,9 @@ struct HostGroup {
     std::vector<int32_t> cv_off, cv_pos, cand_off, cand_idx;
     int conv_maxroom = 0;
     std::vector<int32_t> row_of_solved;   // solved index t -> row position
+    // air-side response W = A^-1 applied in row order, [n][k] (the columns the
+    // reference core computes to form S); the corrected build adds W q to y
+    std::vector<double> W;
     // folded air side (build_fold): Z = L^-1 applied by row, R = sensed U^-1 by sensor
     std::vector<int32_t> zr_p, zr_col, rs_p, rs_pos;
     std::vector<double> zr_x, rs_x;

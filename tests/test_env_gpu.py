@@ -109,3 +109,44 @@ def test_config2_full_batch_sample(scenario_cache):
         assert env.status() == 0
     finally:
         env.close()
+
+
+def test_config4_multiwave_sample(scenario_cache):
+    """Configuration 4's per-GPU batch (7,680 envs over the config-2 mix): about
+    960 slabs, so the solve runs in several waves of CTAs; a sample of envs from
+    every group and wave position against the oracle, bit for bit."""
+    import torch
+
+    from neurips2026_smart_building_challenge_b200 import config_dir
+
+    d = config_dir(2, scenario_cache, n_steps=400)
+    n, steps = 7680, 5
+    sample = [0, 1, 255, 256, 1279, 1280, 2561, 3839, 4000, 5119, 6400, 7679]
+    env = _vec(n, d, groups=30)
+    try:
+        assert env.shape[6] > 2 * 148, "expected several waves of slabs"
+        paths = scenario_paths(d)
+        orc = {e: OracleEnv(paths[int(env.scenario[e])]) for e in sample}
+        env.reset()
+        env.synchronize()
+        obs = env.obs.cpu().numpy()
+        for e in sample:
+            assert np.array_equal(obs[e].view(np.uint32), orc[e].reset().view(np.uint32)), f"reset env {e}"
+        rng = np.random.default_rng(22)
+        for s in range(steps):
+            a = np.zeros((n, 272), np.float32)
+            a[:, :256] = 2.0 * rng.beta(2.0, 2.0, size=(n, 256)) - 1.0
+            a[:, 256:] = 1.0
+            env.step(torch.from_numpy(a).to(env.device))
+            env.synchronize()
+            obs = env.obs.cpu().numpy()
+            rd, _ = env.reward_f64()
+            for e in sample:
+                o, _, _, r64, _, _ = orc[e].step(a[e])
+                assert np.array_equal(obs[e].view(np.uint32), o.view(np.uint32)), f"step {s} env {e}"
+                assert rd[e] == r64, f"step {s} env {e} reward"
+        for e in sample:
+            assert not (env.temp(e, orc[e].ncv) - orc[e].temp()).any(), f"field env {e}"
+        assert env.status() == 0
+    finally:
+        env.close()

@@ -1,10 +1,13 @@
-"""The folded build (solve_exact = 0) against the reference's C core (GPU).
+"""The fast builds (solve_exact = 0) against the reference's C core (GPU).
 
-The reference's GPU backend folds the air-side correction into one triangular
-solve (complete_port/gpu/smart_buildings.cu:686-826): the sensed values come
-from R z with R = sensed U^-1, and the U sweep starts from z + Z q with
-Z = L^-1 applied. The arithmetic then differs from the reference core's two
-solves in association order only, so the north star's tolerances apply:
+Both replace the reference core's second triangular solve. The corrected
+build (default) adds W q to the first solution, W = A^-1 applied precomputed
+per building (the columns the core forms to build S, complete_port/csim/
+sb_fdm.c:103-114). The folded build (fold = 1) folds the correction into one
+L/U pair as the reference's GPU backend does (complete_port/gpu/
+smart_buildings.cu:686-826): sensed values from R z with R = sensed U^-1, the
+U sweep from z + Z q with Z = L^-1 applied. The arithmetic then differs from
+the core's in association order only, so the north star's tolerances apply:
 temperatures within 1e-9 relative at every check (1e-6 K after the month is
 implied), rewards within 1e-9 relative, observations equal up to float32
 rounding (tests/parity_util.py). The month test runs configuration 1 through
@@ -16,29 +19,34 @@ from parity_util import run_parity
 
 pytestmark = pytest.mark.gpu
 
-FOLD = {"solve_exact": 0}
+BUILDS = {"corrected": {"solve_exact": 0}, "folded": {"solve_exact": 0, "fold": 1}}
 
 
-def test_fold_config1_month(scenario_cache):
+@pytest.fixture(params=sorted(BUILDS))
+def build(request):
+    return BUILDS[request.param]
+
+
+def test_fold_config1_month(scenario_cache, build):
     from neurips2026_smart_building_challenge_b200 import config_dir
 
     d = config_dir(1, scenario_cache)
     w = run_parity(d, n=2, steps=8640 + 24, seed=0, temp_every=12, oracle="reference", wild=False,
-                   env_kw=FOLD, tolerant=True)
-    print("folded build, configuration-1 month:", w)
+                   env_kw=build, tolerant=True)
+    print(build, "configuration-1 month:", w)
     assert w["field_abs_K"] < 1e-6
 
 
-def test_fold_config2_mix(scenario_cache):
+def test_fold_config2_mix(scenario_cache, build):
     from neurips2026_smart_building_challenge_b200 import config_dir
 
     d = config_dir(2, scenario_cache, n_steps=400)
-    w = run_parity(d, n=60, steps=40, seed=2, temp_every=5, groups=30, beta_mix=True, env_kw=FOLD,
+    w = run_parity(d, n=60, steps=40, seed=2, temp_every=5, groups=30, beta_mix=True, env_kw=build,
                    tolerant=True)
-    print("folded build, configuration-2 mix:", w)
+    print(build, "configuration-2 mix:", w)
 
 
-def test_fold_notch_and_restarts(scenario_cache):
+def test_fold_notch_and_restarts(scenario_cache, build):
     from neurips2026_smart_building_challenge_b200 import preset, write_scenario
 
     d = scenario_cache / "notch"
@@ -46,12 +54,12 @@ def test_fold_notch_and_restarts(scenario_cache):
     p = d / "notch__w0.sbb"
     if not p.exists():
         write_scenario(p, preset(1, 0, notch_rows=3, notch_cols=4, n_steps=60, start_hour=7, conv_p=0.5))
-    run_parity(d, n=3, steps=130, seed=3, temp_every=7, env_kw=FOLD, tolerant=True)
+    run_parity(d, n=3, steps=130, seed=3, temp_every=7, env_kw=build, tolerant=True)
 
 
-def test_fold_config3(scenario_cache):
+def test_fold_config3(scenario_cache, build):
     from neurips2026_smart_building_challenge_b200 import config_dir
 
     d = config_dir(3, scenario_cache, n_steps=200)
-    w = run_parity(d, n=2, steps=24, seed=4, temp_every=4, env_kw=FOLD, tolerant=True)
-    print("folded build, configuration 3:", w)
+    w = run_parity(d, n=2, steps=24, seed=4, temp_every=4, env_kw=build, tolerant=True)
+    print(build, "configuration 3:", w)
