@@ -83,6 +83,10 @@ def parse_args():
     ap.add_argument("--workload", default="config2", choices=sorted(WORKLOADS))
     ap.add_argument("--envs", type=int, default=0, help="envs per GPU (0: the workload's)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-variants", action="store_true", help="time only the stated build")
+    ap.add_argument("--profile", action="store_true",
+                    help="the profiled command: create the batch, reset, warm-up + steps with L2 flushes, no "
+                         "timing extras (for ncu launch lists and kernel captures)")
     ap.add_argument("--rollout", action="store_true", help="configuration 5: env+policy steps in a CUDA graph")
     ap.add_argument("--horizon", type=int, default=128, help="rollout horizon (--rollout)")
     ap.add_argument("--solve", default="corrected", choices=sorted(SOLVE_NOTE),
@@ -413,7 +417,7 @@ def run_ours(args) -> None:
     pool_np = action_pool(n, 8, seed=1234 + rank)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=f"cuda:{local}")   # > 126 MB L2
     variants = {}
-    others = [v for v in sorted(SOLVE_NOTE) if v != args.solve]
+    others = [] if args.no_variants else [v for v in sorted(SOLVE_NOTE) if v != args.solve]
     # the other builds first (value and per-kernel times only), then the stated one
     for solve in others + [args.solve]:
         env = SmartBuildingsVec(n, blob_dir=str(d), groups=groups, device=f"cuda:{local}", env_offset=start,
@@ -503,6 +507,31 @@ def run_ours(args) -> None:
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def run_profile(args) -> None:
+    """The command ncu captures: the stated build of the workload, reset, then
+    warm-up + steps, each after an (untimed) L2 flush; nothing else runs."""
+    import torch
+
+    from neurips2026_smart_building_challenge_b200 import SmartBuildingsVec
+
+    d = workload_dir(args.workload, ROOT / ".sbb_cache" / "bench_rank0")
+    n = args.envs
+    env = SmartBuildingsVec(n, blob_dir=str(d), groups=WORKLOADS[args.workload]["groups"], device="cuda:0",
+                            **SOLVE_KW[args.solve])
+    env.reset()
+    pool = torch.from_numpy(action_pool(n, 2, seed=1234)).to(env.device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=env.device)
+    for i in range(args.warmup + args.steps):
+        with torch.cuda.stream(env.stream):
+            env.actions.copy_(pool[i % 2], non_blocking=True)
+            flush.fill_(i & 0xFF)
+        env.step()
+    env.synchronize()
+    print(json.dumps({"profile": args.workload, "envs": n, "solve": args.solve, "steps": args.warmup + args.steps,
+                      "kernels_per_step": env.lib.sb_kernels_per_step(), "status": env.status()}), flush=True)
+    env.close()
 
 
 def run_month(args) -> None:
@@ -663,6 +692,8 @@ def main():
         run_reference(args)
     elif args.month:
         run_month(args)
+    elif args.profile:
+        run_profile(args)
     elif args.rollout:
         run_rollout(args)
     else:

@@ -34,7 +34,7 @@ constexpr int kCorrThreads = 256;
 constexpr int kCorrRowsPerLane = kCorrRows / 64;   // two row halves of 64 rows
 constexpr int kCorrEnvsPerThread = kCorrEnvs / 4;  // four env groups of 8
 __host__ __device__ constexpr size_t corr_smem_bytes(int k) {
-    return sizeof(double) * ((size_t)k * kCorrRows + (size_t)k * kCorrEnvs + kCorrEnvs) + 16;
+    return sizeof(double) * ((size_t)k * kCorrRows + (size_t)k * kCorrEnvs + kCorrEnvs) + 16 + 4 * kCorrEnvs;
 }
 
 __global__ void __launch_bounds__(kCorrThreads) k_correct(const StepCtx* __restrict__ ctx,
@@ -70,21 +70,25 @@ __global__ void __launch_bounds__(kCorrThreads) k_correct(const StepCtx* __restr
             mas[i][j] = in ? g.M[local * n + r] : 0.0;
         }
     // the envs' dense solutions (zero for an env whose air side is off this
-    // step: its right side was never formed) and calendar ambient; each warp
-    // takes four envs, its lanes the columns
-    for (int q = 0; q < kCorrEnvs / 8; q++) {
-        const int e = w * (kCorrEnvs / 8) + q;
-        const int env = t.env0 + (e < t.nenv ? e : 0);
-        const double* D = ctx->Dst + (size_t)env * L.nd;
-        int a = 0;
-        for (int c = lane; c < k; c += 32) a |= D[L.ag + c] != 0.0;
-        a = __any_sync(0xffffffffu, a) && e < t.nenv;
-        const double* qg = ctx->airq + (size_t)env * ctx->k_max;
-        for (int c = lane; c < k; c += 32) Q[(size_t)c * kCorrEnvs + e] = a ? qg[c] : 0.0;
-        if (lane == 0) {
-            const ScnDev& sc = ctx->scns[ctx->envs[env].scn];
-            amb[e] = sc.amb[ctx->Ist[(size_t)env * L.ni + L.cal]];
-        }
+    // step: its right side was never formed) and calendar ambient; every load
+    // of the prologue is independent of the others, so they are all in flight
+    // together with the W block and the field values above
+    int* act = reinterpret_cast<int*>(bar + 1);         // [kCorrEnvs]
+    if (tid < kCorrEnvs) act[tid] = 0;
+    __syncthreads();
+    for (int idx = tid; idx < t.nenv * k; idx += kCorrThreads) {
+        const int e = idx / k, c = idx - e * k;
+        if (ctx->Dst[(size_t)(t.env0 + e) * L.nd + L.ag + c] != 0.0) act[e] = 1;
+    }
+    if (tid < t.nenv) {
+        const int env = t.env0 + tid;
+        const ScnDev& sc = ctx->scns[ctx->envs[env].scn];
+        amb[tid] = sc.amb[ctx->Ist[(size_t)env * L.ni + L.cal]];
+    }
+    __syncthreads();
+    for (int idx = tid; idx < k * kCorrEnvs; idx += kCorrThreads) {
+        const int c = idx / kCorrEnvs, e = idx - c * kCorrEnvs;
+        Q[idx] = (e < t.nenv && act[e]) ? ctx->airq[(size_t)(t.env0 + e) * ctx->k_max + c] : 0.0;
     }
     __syncthreads();
     bool landed = true;

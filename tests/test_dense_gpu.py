@@ -3,7 +3,8 @@ row, the matrix in shared memory) against a restatement of the reference's parti
 Gaussian elimination (complete_port/csim/sb_fdm.c:9-38, as the oracle's
 gauss_solve in oracle/sbo_sim.c), bit for bit: random systems, systems with
 tied magnitudes and zero multipliers, a singular system (the elimination
-stops), a NaN off the pivot path, and sizes across the warp boundaries."""
+stops), a NaN off the pivot path, rows scaled over 600 decades (overflowing
+and subnormal intermediates), and sizes across the warp boundaries."""
 import ctypes
 
 import numpy as np
@@ -57,6 +58,8 @@ def _cases(k, rng):
         N = rng.standard_normal((k, k)) + np.eye(k) * 4.0
         N[k - 1, 0] = np.nan                                       # never a pivot; propagates
         out.append((N, rng.standard_normal(k)))
+        X = (rng.standard_normal((k, k)) + np.eye(k) * 2.0) * (10.0 ** rng.uniform(-300, 300, size=(k, 1)))
+        out.append((X, rng.standard_normal(k) * 1e-300))          # rows over 600 decades, subnormal sums
     return out
 
 
