@@ -127,6 +127,16 @@ struct Engine {
     int dense_threads = 32;          // k_dense block (dense_threads(k_max))
     struct DenseClass { int first, count, k; };
     std::vector<DenseClass> dense_cls;   // runs of equal k in dense_order, heaviest first
+    // phase 1 by dense class: each class's dense solves and then its groups'
+    // phase-1 work (k_correct tiles or k_solve<1> slabs) on a stream of their
+    // own, so a class's phase 1 starts as soon as its own dense systems are
+    // solved; the groups without an air side (dense = -1) run on hi
+    struct PhaseClass { int dense, tile0, ntiles, slab0, nslabs; };
+    std::vector<PhaseClass> pcls;
+    SlabDesc* d_slabs1 = nullptr;         // the slabs in pcls order (k_solve<1>)
+    std::vector<cudaStream_t> cls_st;     // one per dense class (empty: one class, all on hi)
+    std::vector<cudaEvent_t> cls_ev;
+    cudaEvent_t ev_dfork = nullptr;
     int max_ncv = 0;
     double* d_snap = nullptr;     // snapshot staging (k_snapshot), sized for the largest scenario
     bool ready = false;
@@ -134,8 +144,14 @@ struct Engine {
     void destroy() {
         for (cudaStream_t* q : {&hi, &own_stream})
             if (*q) { cudaStreamDestroy(*q); *q = nullptr; }
-        for (cudaEvent_t* q : {&ev_fork, &ev_join})
+        for (cudaEvent_t* q : {&ev_fork, &ev_join, &ev_dfork})
             if (*q) { cudaEventDestroy(*q); *q = nullptr; }
+        for (cudaStream_t& q : cls_st)
+            if (q) cudaStreamDestroy(q);
+        for (cudaEvent_t& q : cls_ev)
+            if (q) cudaEventDestroy(q);
+        cls_st.clear();
+        cls_ev.clear();
         if (envs) cudaFree(envs);
         envs = nullptr;
         arena.release();
@@ -226,55 +242,94 @@ cudaError_t launch_rng(Engine& E, cudaStream_t st, bool pdl) {
     return cudaLaunchKernelEx(&cfg, k_occ, (const StepCtx*)E.d_ctx, 0);
 }
 
-// The dense air-side solves: one launch per class of equal k with its own
-// block and shared-memory size; every class after the first is a programmatic
-// dependent of the one before (it may start once that one's CTAs are resident,
-// and its CTAs wait for that one's completion before they exit).
+// One class of dense air-side solves (equal k): its own block and
+// shared-memory size; with pdl a programmatic dependent of the kernel before
+// it on the stream (it may start once that one's CTAs are resident, and its
+// CTAs wait for that one's completion before they exit).
+cudaError_t launch_dense_class(Engine& E, size_t c, cudaStream_t st, bool pdl) {
+    const Engine::DenseClass& d = E.dense_cls[c];
+    const size_t smem = std::max<size_t>(16, dense_smem_doubles(d.k) * sizeof(double));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)d.count);
+    cfg.blockDim = dim3((unsigned)dense_threads(d.k));
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k_dense, (const StepCtx*)E.d_ctx, d.first);
+}
+
+// Every dense class on one stream, heaviest first, the later ones chained as
+// programmatic dependents so that they share the SMs.
 cudaError_t launch_dense(Engine& E, cudaStream_t st) {
     for (size_t c = 0; c < E.dense_cls.size(); c++) {
-        const Engine::DenseClass& d = E.dense_cls[c];
-        const size_t smem = std::max<size_t>(16, dense_smem_doubles(d.k) * sizeof(double));
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((unsigned)d.count);
-        cfg.blockDim = dim3((unsigned)dense_threads(d.k));
-        cfg.dynamicSmemBytes = smem;
-        cfg.stream = st;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = c == 0 ? 0 : 1;
-        const cudaError_t e = cudaLaunchKernelEx(&cfg, k_dense, (const StepCtx*)E.d_ctx, d.first);
+        const cudaError_t e = launch_dense_class(E, c, st, c > 0);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
 }
 
-// The solve on the high-priority stream: phase 0 (first L/U solve), the
-// dense air-side solves, then phase 1 (second L/U solve, mass, field) or, in
-// the corrected build, k_correct (y + W q, mass, field). The random inputs of
-// the next transition run beside the longest solve kernel (k_post of this step
-// reads the ones made during the step before).
-cudaError_t launch_phase1(Engine& E) {
+// Phase 1: the second L/U solve, interior mass and field (k_solve<1>) or, in
+// the corrected build, k_correct (y + W q, mass, field); all of it, or one
+// phase class's share.
+cudaError_t launch_phase1(Engine& E, cudaStream_t st, const Engine::PhaseClass* pc = nullptr) {
     if (E.solve_mode == 2) {
-        k_correct<<<(unsigned)E.ctiles.size(), kCorrThreads, E.smem_corr, E.hi>>>(E.d_ctx, E.d_ctiles);
+        const unsigned n = pc ? (unsigned)pc->ntiles : (unsigned)E.ctiles.size();
+        if (n) k_correct<<<n, kCorrThreads, E.smem_corr, st>>>(E.d_ctx, E.d_ctiles + (pc ? pc->tile0 : 0));
     } else {
-        k_solve<1><<<(unsigned)E.slabs.size(), kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
+        const unsigned n = pc ? (unsigned)pc->nslabs : (unsigned)E.slabs.size();
+        if (n) k_solve<1><<<n, kSolveThreads, E.smem_solve, st>>>(E.d_ctx, pc ? E.d_slabs1 + pc->slab0 : E.d_slabs);
     }
     return cudaGetLastError();
 }
 
+// The solve on the high-priority stream: phase 0 (first L/U solve) with the
+// random inputs of the next transition beside it (programmatic dependents of
+// phase 0; k_post of this step reads the ones made during the step before),
+// then the dense air-side solves and phase 1. With several dense classes each
+// class and its phase-1 share run on their own stream, forked after phase 0
+// and joined back into hi: the lighter classes' phase 1 overlaps the heaviest
+// class's dense solves. No kernel waits on a flag another kernel writes.
 cudaError_t launch_solve(Engine& E) {
     const unsigned slabs = (unsigned)E.slabs.size();
-    const bool corr = E.solve_mode == 2;
     k_solve<0><<<slabs, kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
     cudaError_t e = cudaGetLastError();
-    if (e == cudaSuccess && corr) e = launch_rng(E, E.hi, true);
+    if (e == cudaSuccess) e = launch_rng(E, E.hi, true);
     if (e != cudaSuccess) return e;
-    e = launch_dense(E, E.hi);
-    if (e == cudaSuccess) e = launch_phase1(E);
-    if (e == cudaSuccess && !corr) e = launch_rng(E, E.hi, true);
-    return e;
+    if (E.cls_st.empty()) {
+        e = launch_dense(E, E.hi);
+        return e == cudaSuccess ? launch_phase1(E, E.hi) : e;
+    }
+    if ((e = cudaEventRecord(E.ev_dfork, E.hi)) != cudaSuccess) return e;
+    for (const Engine::PhaseClass& pc : E.pcls) {
+        if (pc.dense < 0) {
+            if ((e = launch_phase1(E, E.hi, &pc)) != cudaSuccess) return e;
+            continue;
+        }
+        cudaStream_t st = E.cls_st[pc.dense];
+        if ((e = cudaStreamWaitEvent(st, E.ev_dfork, 0)) != cudaSuccess) return e;
+        if ((e = launch_dense_class(E, (size_t)pc.dense, st, false)) != cudaSuccess) return e;
+        if ((e = launch_phase1(E, st, &pc)) != cudaSuccess) return e;
+        if ((e = cudaEventRecord(E.cls_ev[pc.dense], st)) != cudaSuccess) return e;
+    }
+    for (cudaEvent_t ev : E.cls_ev)
+        if ((e = cudaStreamWaitEvent(E.hi, ev, 0)) != cudaSuccess) return e;
+    return cudaSuccess;
+}
+
+// k_pre, k_solve<0>, k_conv, k_occ, k_post, one k_dense launch per class of
+// equal k, and phase 1: one launch, or one per phase class with work when the
+// classes run on their own streams
+int kernels_per_step(const Engine& E) {
+    int p1 = 1;
+    if (!E.cls_st.empty()) {
+        p1 = 0;
+        for (const Engine::PhaseClass& pc : E.pcls) p1 += (E.solve_mode == 2 ? pc.ntiles : pc.nslabs) > 0 ? 1 : 0;
+    }
+    return 5 + (int)E.dense_cls.size() + p1;
 }
 
 bool launch_step(Engine& E) {
@@ -710,6 +765,26 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     }
     E.smem_dense = std::max<size_t>(16, dense_smem_doubles(k_max) * sizeof(double));
     E.dense_threads = dense_threads(std::max(k_max, 1));
+    // phase 1 by dense class: the tiles / slabs of the groups whose k is the
+    // class's, heaviest class first, then the groups without an air side
+    {
+        std::vector<CorrTile> tiles;
+        std::vector<SlabDesc> slabs1;
+        auto add = [&](int dense, int k) {
+            Engine::PhaseClass pc{dense, (int)tiles.size(), 0, (int)slabs1.size(), 0};
+            for (const CorrTile& t : E.ctiles)
+                if (E.gd[t.group].k == k) tiles.push_back(t);
+            for (const SlabDesc& sl : E.slabs)
+                if (E.gd[sl.group].k == k) slabs1.push_back(sl);
+            pc.ntiles = (int)tiles.size() - pc.tile0;
+            pc.nslabs = (int)slabs1.size() - pc.slab0;
+            if (dense >= 0 || pc.ntiles > 0 || pc.nslabs > 0) E.pcls.push_back(pc);
+        };
+        for (size_t c = 0; c < E.dense_cls.size(); c++) add((int)c, E.dense_cls[c].k);
+        add(-1, 0);
+        E.ctiles = tiles;
+        E.d_slabs1 = E.arena.upload(slabs1, ok);
+    }
     E.d_slabs = E.arena.upload(E.slabs, ok);
     if (!E.ctiles.empty()) E.d_ctiles = E.arena.upload(E.ctiles, ok);
     if (!ok) return false;
@@ -771,6 +846,19 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     }
     CK(cudaEventCreateWithFlags(&E.ev_fork, cudaEventDisableTiming));
     CK(cudaEventCreateWithFlags(&E.ev_join, cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&E.ev_dfork, cudaEventDisableTiming));
+    // a stream per dense class once there are two or more (the classes and
+    // their phase-1 shares then run side by side)
+    if (E.dense_cls.size() > 1) {
+        int least = 0, greatest = 0;
+        CK(cudaDeviceGetStreamPriorityRange(&least, &greatest));
+        E.cls_st.assign(E.dense_cls.size(), nullptr);
+        E.cls_ev.assign(E.dense_cls.size(), nullptr);
+        for (size_t c = 0; c < E.dense_cls.size(); c++) {
+            CK(cudaStreamCreateWithPriority(&E.cls_st[c], cudaStreamNonBlocking, greatest));
+            CK(cudaEventCreateWithFlags(&E.cls_ev[c], cudaEventDisableTiming));
+        }
+    }
     if (!E.stream) E.stream = E.own_stream;
     CK(cudaDeviceSynchronize());
     E.ready = true;
@@ -1180,7 +1268,7 @@ void sb_shape(int* out) {
         out[5] = std::max(out[5], s.n_disc);
     }
     out[6] = (int)E.slabs.size();
-    out[7] = 6 + (int)E.dense_cls.size();
+    out[7] = kernels_per_step(E);
 }
 
 void sb_env_info(int* obs_len, int* scenario) {
@@ -1234,8 +1322,7 @@ int sb_get_reward_f64(double* reward, double* parts) {
     return 0;
 }
 
-// k_pre, k_solve x 2, k_post, k_conv, k_occ and one k_dense launch per class of equal k
-int sb_kernels_per_step(void) { return 6 + (g_eng ? (int)g_eng->dense_cls.size() : 1); }
+int sb_kernels_per_step(void) { return g_eng ? kernels_per_step(*g_eng) : 7; }
 
 int sb_episode_options(int* first_len, unsigned long long* start_rng) {
     if (!g_eng) return -1;
@@ -1380,41 +1467,70 @@ int sb_snapshot_write(int env, const char* path) {
 int sb_step_timed(float* ms) {
     if (!g_eng || !g_eng->ready || !ms) return -1;
     Engine& E = *g_eng;
-    cudaEvent_t ev[7];
-    for (auto& e : ev)
-        if (cudaEventCreate(&e) != cudaSuccess) return -1;
-    // the step of launch_step with events around each kernel; the producers of
-    // the next transition run beside phase 1, inside its interval
-    cudaEventRecord(ev[0], E.stream);
-    k_pre<<<(unsigned)E.n_env, 128, E.smem_pre, E.stream>>>(E.d_ctx);
-    cudaEventRecord(ev[1], E.stream);
-    cudaEventRecord(E.ev_fork, E.stream);
-    cudaStreamWaitEvent(E.hi, E.ev_fork, 0);
-    const unsigned slabs = (unsigned)E.slabs.size();
-    const bool corr = E.solve_mode == 2;
-    k_solve<0><<<slabs, kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
-    if (corr) launch_rng(E, E.hi, true);
-    cudaEventRecord(ev[4], E.hi);
-    launch_dense(E, E.hi);
-    cudaEventRecord(ev[5], E.hi);
-    launch_phase1(E);
-    if (!corr) launch_rng(E, E.hi, true);
-    cudaEventRecord(ev[2], E.hi);
-    cudaStreamWaitEvent(E.stream, ev[2], 0);
-    cudaEventRecord(ev[6], E.stream);
-    k_post<<<(unsigned)E.n_env, 128, E.smem_post, E.stream>>>(E.d_ctx);
-    cudaEventRecord(ev[3], E.stream);
-    const bool ok = cudaEventSynchronize(ev[3]) == cudaSuccess;
+    const size_t nc = E.cls_st.size();
+    std::vector<cudaEvent_t> ev(7 + nc, nullptr);
+    bool ok = true;
+    for (auto& e : ev) ok = ok && cudaEventCreate(&e) == cudaSuccess;
+    // the step of launch_step with events around each part; the producers of
+    // the next transition run beside phase 0, inside its interval. With one
+    // stream per dense class, k_dense is the interval until the last class's
+    // dense solves end and phase 1 the rest of the solve.
     if (ok) {
-        ms[0] = -1.0f;                                 // k_conv, k_occ: beside a phase, inside its interval
+        cudaEventRecord(ev[0], E.stream);
+        k_pre<<<(unsigned)E.n_env, 128, E.smem_pre, E.stream>>>(E.d_ctx);
+        cudaEventRecord(ev[1], E.stream);
+        cudaEventRecord(E.ev_fork, E.stream);
+        cudaStreamWaitEvent(E.hi, E.ev_fork, 0);
+        k_solve<0><<<(unsigned)E.slabs.size(), kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
+        launch_rng(E, E.hi, true);
+        cudaEventRecord(ev[4], E.hi);
+        if (nc == 0) {
+            launch_dense(E, E.hi);
+            cudaEventRecord(ev[5], E.hi);
+            launch_phase1(E, E.hi);
+        } else {
+            cudaEventRecord(E.ev_dfork, E.hi);
+            for (const Engine::PhaseClass& pc : E.pcls) {
+                if (pc.dense < 0) {
+                    launch_phase1(E, E.hi, &pc);
+                    continue;
+                }
+                cudaStream_t st = E.cls_st[pc.dense];
+                cudaStreamWaitEvent(st, E.ev_dfork, 0);
+                launch_dense_class(E, (size_t)pc.dense, st, false);
+                cudaEventRecord(ev[7 + pc.dense], st);
+                launch_phase1(E, st, &pc);
+                cudaEventRecord(E.cls_ev[pc.dense], st);
+            }
+            for (cudaEvent_t c : E.cls_ev) cudaStreamWaitEvent(E.hi, c, 0);
+        }
+        cudaEventRecord(ev[2], E.hi);
+        cudaStreamWaitEvent(E.stream, ev[2], 0);
+        cudaEventRecord(ev[6], E.stream);
+        k_post<<<(unsigned)E.n_env, 128, E.smem_post, E.stream>>>(E.d_ctx);
+        cudaEventRecord(ev[3], E.stream);
+        ok = cudaGetLastError() == cudaSuccess && cudaEventSynchronize(ev[3]) == cudaSuccess;
+    }
+    if (ok) {
+        ms[0] = -1.0f;                                 // k_conv, k_occ: beside phase 0, inside its interval
         cudaEventElapsedTime(&ms[1], ev[0], ev[1]);   // k_pre
         cudaEventElapsedTime(&ms[2], ev[1], ev[2]);   // the solve: phase 0, k_dense, phase 1
         cudaEventElapsedTime(&ms[3], ev[6], ev[3]);   // k_post
         cudaEventElapsedTime(&ms[4], ev[1], ev[4]);   // phase 0
-        cudaEventElapsedTime(&ms[5], ev[4], ev[5]);   // k_dense
-        cudaEventElapsedTime(&ms[6], ev[5], ev[2]);   // phase 1 or k_correct
+        if (nc == 0) {
+            cudaEventElapsedTime(&ms[5], ev[4], ev[5]);   // k_dense
+            cudaEventElapsedTime(&ms[6], ev[5], ev[2]);   // phase 1 or k_correct
+        } else {
+            float last = 0.0f, t = 0.0f, all = 0.0f;
+            for (size_t c = 0; c < nc; c++)
+                if (cudaEventElapsedTime(&t, ev[4], ev[7 + c]) == cudaSuccess) last = std::max(last, t);
+            cudaEventElapsedTime(&all, ev[4], ev[2]);
+            ms[5] = last;                                 // until the last dense class ends
+            ms[6] = std::max(0.0f, all - last);           // the phase-1 work after it
+        }
     }
-    for (auto& e : ev) cudaEventDestroy(e);
+    for (auto& e : ev)
+        if (e) cudaEventDestroy(e);
     return ok ? 0 : -1;
 }
 
