@@ -290,46 +290,57 @@ cudaError_t launch_phase1(Engine& E, cudaStream_t st, const Engine::PhaseClass* 
 // random inputs of the next transition beside it (programmatic dependents of
 // phase 0; k_post of this step reads the ones made during the step before),
 // then the dense air-side solves and phase 1. With several dense classes each
-// class and its phase-1 share run on their own stream, forked after phase 0
-// and joined back into hi: the lighter classes' phase 1 overlaps the heaviest
-// class's dense solves. No kernel waits on a flag another kernel writes.
+// class runs its whole solve -- phase 0 of its groups' slabs, its dense
+// systems, its phase-1 share -- on its own stream, forked after k_pre and
+// joined back into hi, so one class's dense solves and phase 1 fill the SMs
+// the other classes' slabs leave free. No kernel waits on a flag another
+// kernel writes.
 cudaError_t launch_solve(Engine& E) {
-    const unsigned slabs = (unsigned)E.slabs.size();
-    k_solve<0><<<slabs, kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
-    cudaError_t e = cudaGetLastError();
-    if (e == cudaSuccess) e = launch_rng(E, E.hi, true);
-    if (e != cudaSuccess) return e;
+    cudaError_t e = cudaSuccess;
     if (E.cls_st.empty()) {
-        e = launch_dense(E, E.hi);
-        return e == cudaSuccess ? launch_phase1(E, E.hi) : e;
+        k_solve<0><<<(unsigned)E.slabs.size(), kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        if ((e = launch_rng(E, E.hi, true)) != cudaSuccess) return e;
+        if ((e = launch_dense(E, E.hi)) != cudaSuccess) return e;
+        return launch_phase1(E, E.hi);
     }
     if ((e = cudaEventRecord(E.ev_dfork, E.hi)) != cudaSuccess) return e;
+    bool rng = false;
     for (const Engine::PhaseClass& pc : E.pcls) {
-        if (pc.dense < 0) {
-            if ((e = launch_phase1(E, E.hi, &pc)) != cudaSuccess) return e;
-            continue;
+        cudaStream_t st = pc.dense >= 0 ? E.cls_st[pc.dense] : E.hi;
+        if (st != E.hi && (e = cudaStreamWaitEvent(st, E.ev_dfork, 0)) != cudaSuccess) return e;
+        if (pc.nslabs > 0) {
+            k_solve<0><<<(unsigned)pc.nslabs, kSolveThreads, E.smem_solve, st>>>(E.d_ctx, E.d_slabs1 + pc.slab0);
+            if ((e = cudaGetLastError()) != cudaSuccess) return e;
+            if (!rng) {
+                // beside the first (heaviest) class's phase 0
+                if ((e = launch_rng(E, st, true)) != cudaSuccess) return e;
+                rng = true;
+            }
         }
-        cudaStream_t st = E.cls_st[pc.dense];
-        if ((e = cudaStreamWaitEvent(st, E.ev_dfork, 0)) != cudaSuccess) return e;
-        if ((e = launch_dense_class(E, (size_t)pc.dense, st, false)) != cudaSuccess) return e;
+        if (pc.dense >= 0 && (e = launch_dense_class(E, (size_t)pc.dense, st, false)) != cudaSuccess) return e;
         if ((e = launch_phase1(E, st, &pc)) != cudaSuccess) return e;
-        if ((e = cudaEventRecord(E.cls_ev[pc.dense], st)) != cudaSuccess) return e;
+        if (st != E.hi && (e = cudaEventRecord(E.cls_ev[pc.dense], st)) != cudaSuccess) return e;
     }
+    if (!rng && (e = launch_rng(E, E.hi, false)) != cudaSuccess) return e;
     for (cudaEvent_t ev : E.cls_ev)
         if ((e = cudaStreamWaitEvent(E.hi, ev, 0)) != cudaSuccess) return e;
     return cudaSuccess;
 }
 
-// k_pre, k_solve<0>, k_conv, k_occ, k_post, one k_dense launch per class of
-// equal k, and phase 1: one launch, or one per phase class with work when the
+// k_pre, k_conv, k_occ, k_post, one k_dense launch per class of equal k, and
+// phases 0 and 1: one launch each, or one per phase class with work when the
 // classes run on their own streams
 int kernels_per_step(const Engine& E) {
-    int p1 = 1;
+    int p0 = 1, p1 = 1;
     if (!E.cls_st.empty()) {
-        p1 = 0;
-        for (const Engine::PhaseClass& pc : E.pcls) p1 += (E.solve_mode == 2 ? pc.ntiles : pc.nslabs) > 0 ? 1 : 0;
+        p0 = p1 = 0;
+        for (const Engine::PhaseClass& pc : E.pcls) {
+            p0 += pc.nslabs > 0 ? 1 : 0;
+            p1 += (E.solve_mode == 2 ? pc.ntiles : pc.nslabs) > 0 ? 1 : 0;
+        }
     }
-    return 5 + (int)E.dense_cls.size() + p1;
+    return 4 + p0 + (int)E.dense_cls.size() + p1;
 }
 
 bool launch_step(Engine& E) {
@@ -1467,41 +1478,46 @@ int sb_snapshot_write(int env, const char* path) {
 int sb_step_timed(float* ms) {
     if (!g_eng || !g_eng->ready || !ms) return -1;
     Engine& E = *g_eng;
-    const size_t nc = E.cls_st.size();
-    std::vector<cudaEvent_t> ev(7 + nc, nullptr);
+    const size_t nc = E.cls_st.size(), np = E.pcls.size();
+    std::vector<cudaEvent_t> ev(7 + 2 * np, nullptr);
     bool ok = true;
     for (auto& e : ev) ok = ok && cudaEventCreate(&e) == cudaSuccess;
     // the step of launch_step with events around each part; the producers of
     // the next transition run beside phase 0, inside its interval. With one
-    // stream per dense class, k_dense is the interval until the last class's
-    // dense solves end and phase 1 the rest of the solve.
+    // stream per dense class the classes overlap: phase 0 is the interval until
+    // the last class's phase 0 ends, k_dense from there until the last class's
+    // dense solves end, and phase 1 the rest of the solve.
     if (ok) {
         cudaEventRecord(ev[0], E.stream);
         k_pre<<<(unsigned)E.n_env, 128, E.smem_pre, E.stream>>>(E.d_ctx);
         cudaEventRecord(ev[1], E.stream);
         cudaEventRecord(E.ev_fork, E.stream);
         cudaStreamWaitEvent(E.hi, E.ev_fork, 0);
-        k_solve<0><<<(unsigned)E.slabs.size(), kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
-        launch_rng(E, E.hi, true);
-        cudaEventRecord(ev[4], E.hi);
         if (nc == 0) {
+            k_solve<0><<<(unsigned)E.slabs.size(), kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
+            launch_rng(E, E.hi, true);
+            cudaEventRecord(ev[4], E.hi);
             launch_dense(E, E.hi);
             cudaEventRecord(ev[5], E.hi);
             launch_phase1(E, E.hi);
         } else {
             cudaEventRecord(E.ev_dfork, E.hi);
-            for (const Engine::PhaseClass& pc : E.pcls) {
-                if (pc.dense < 0) {
-                    launch_phase1(E, E.hi, &pc);
-                    continue;
+            bool rng = false;
+            for (size_t i = 0; i < np; i++) {
+                const Engine::PhaseClass& pc = E.pcls[i];
+                cudaStream_t st = pc.dense >= 0 ? E.cls_st[pc.dense] : E.hi;
+                if (st != E.hi) cudaStreamWaitEvent(st, E.ev_dfork, 0);
+                if (pc.nslabs > 0) {
+                    k_solve<0><<<(unsigned)pc.nslabs, kSolveThreads, E.smem_solve, st>>>(E.d_ctx, E.d_slabs1 + pc.slab0);
+                    if (!rng) { launch_rng(E, st, true); rng = true; }
                 }
-                cudaStream_t st = E.cls_st[pc.dense];
-                cudaStreamWaitEvent(st, E.ev_dfork, 0);
-                launch_dense_class(E, (size_t)pc.dense, st, false);
-                cudaEventRecord(ev[7 + pc.dense], st);
+                cudaEventRecord(ev[7 + 2 * i], st);
+                if (pc.dense >= 0) launch_dense_class(E, (size_t)pc.dense, st, false);
+                cudaEventRecord(ev[8 + 2 * i], st);
                 launch_phase1(E, st, &pc);
-                cudaEventRecord(E.cls_ev[pc.dense], st);
+                if (st != E.hi) cudaEventRecord(E.cls_ev[pc.dense], st);
             }
+            if (!rng) launch_rng(E, E.hi, false);
             for (cudaEvent_t c : E.cls_ev) cudaStreamWaitEvent(E.hi, c, 0);
         }
         cudaEventRecord(ev[2], E.hi);
@@ -1516,17 +1532,19 @@ int sb_step_timed(float* ms) {
         cudaEventElapsedTime(&ms[1], ev[0], ev[1]);   // k_pre
         cudaEventElapsedTime(&ms[2], ev[1], ev[2]);   // the solve: phase 0, k_dense, phase 1
         cudaEventElapsedTime(&ms[3], ev[6], ev[3]);   // k_post
-        cudaEventElapsedTime(&ms[4], ev[1], ev[4]);   // phase 0
         if (nc == 0) {
+            cudaEventElapsedTime(&ms[4], ev[1], ev[4]);   // phase 0
             cudaEventElapsedTime(&ms[5], ev[4], ev[5]);   // k_dense
             cudaEventElapsedTime(&ms[6], ev[5], ev[2]);   // phase 1 or k_correct
         } else {
-            float last = 0.0f, t = 0.0f, all = 0.0f;
-            for (size_t c = 0; c < nc; c++)
-                if (cudaEventElapsedTime(&t, ev[4], ev[7 + c]) == cudaSuccess) last = std::max(last, t);
-            cudaEventElapsedTime(&all, ev[4], ev[2]);
-            ms[5] = last;                                 // until the last dense class ends
-            ms[6] = std::max(0.0f, all - last);           // the phase-1 work after it
+            float p0 = 0.0f, d = 0.0f, t = 0.0f;
+            for (size_t i = 0; i < np; i++) {
+                if (cudaEventElapsedTime(&t, ev[1], ev[7 + 2 * i]) == cudaSuccess) p0 = std::max(p0, t);
+                if (cudaEventElapsedTime(&t, ev[1], ev[8 + 2 * i]) == cudaSuccess) d = std::max(d, t);
+            }
+            ms[4] = p0;                                   // until the last class's phase 0 ends
+            ms[5] = std::max(0.0f, d - p0);               // then until the last class's dense solves end
+            ms[6] = std::max(0.0f, ms[2] - std::max(d, p0));   // the phase-1 work after that
         }
     }
     for (auto& e : ev)
