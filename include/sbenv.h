@@ -152,7 +152,12 @@ void dict_set_str(Dict* d, const char* key, const char* value);
  * (1: (r - mean) only, the mean moved by center_beta, default 0.01; rew_norm
  * wins when both are set). env_offset: the global index of this batch's first
  * env when a batch is sharded over several GPUs (the per-env draws follow the
- * global index; default 0). Returns NULL on error. */
+ * global index; default 0). overlap (scheduling only, results unchanged):
+ * with several classes of equal air-side size k, 1 runs each class's dense
+ * systems and then its phase-1 work (the correction or the second solve) on a
+ * stream of its own, 2 its first solve too, 0 every part on one stream in
+ * turn; default -1: 2 when the first solve's slabs are more than one wave of
+ * the GPU's SMs, else 1. Returns NULL on error. */
 Env* puf_vec_create(int n, Dict* kwargs, obs_t* observations, float* actions, float* rewards,
                     float* terminals);
 void puf_bind_stream(sb_stream_t stream);

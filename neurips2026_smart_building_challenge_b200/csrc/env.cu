@@ -134,7 +134,9 @@ struct Engine {
     struct PhaseClass { int dense, tile0, ntiles, slab0, nslabs; };
     std::vector<PhaseClass> pcls;
     SlabDesc* d_slabs1 = nullptr;         // the slabs in pcls order (k_solve<1>)
-    std::vector<cudaStream_t> cls_st;     // one per dense class (empty: one class, all on hi)
+    std::vector<cudaStream_t> cls_st;     // one per dense class (empty: all on hi)
+    bool split_phase0 = false;            // phase 0 per class too (slabs beyond one wave)
+    int overlap = -1;                     // kwarg overlap (-1 automatic)
     std::vector<cudaEvent_t> cls_ev;
     cudaEvent_t ev_dfork = nullptr;
     int max_ncv = 0;
@@ -289,12 +291,14 @@ cudaError_t launch_phase1(Engine& E, cudaStream_t st, const Engine::PhaseClass* 
 // The solve on the high-priority stream: phase 0 (first L/U solve) with the
 // random inputs of the next transition beside it (programmatic dependents of
 // phase 0; k_post of this step reads the ones made during the step before),
-// then the dense air-side solves and phase 1. With several dense classes each
-// class runs its whole solve -- phase 0 of its groups' slabs, its dense
-// systems, its phase-1 share -- on its own stream, forked after k_pre and
-// joined back into hi, so one class's dense solves and phase 1 fill the SMs
-// the other classes' slabs leave free. No kernel waits on a flag another
-// kernel writes.
+// then the dense air-side solves and phase 1. With several dense classes
+// (kwarg overlap, default on) each class runs its dense systems and then its
+// phase-1 share on its own stream, forked after phase 0 and joined back into
+// hi, so the lighter classes' phase 1 runs while the heaviest class's dense
+// systems are still being solved. When the slabs are more than one wave
+// (split_phase0), each class runs its phase 0 on its stream as well, so one
+// class's dense solves fill the SMs the other classes' slabs leave free. No
+// kernel waits on a flag another kernel writes.
 cudaError_t launch_solve(Engine& E) {
     cudaError_t e = cudaSuccess;
     if (E.cls_st.empty()) {
@@ -304,12 +308,19 @@ cudaError_t launch_solve(Engine& E) {
         if ((e = launch_dense(E, E.hi)) != cudaSuccess) return e;
         return launch_phase1(E, E.hi);
     }
-    if ((e = cudaEventRecord(E.ev_dfork, E.hi)) != cudaSuccess) return e;
     bool rng = false;
+    if (!E.split_phase0) {
+        // every slab in one wave: phase 0 in one launch, then the classes
+        k_solve<0><<<(unsigned)E.slabs.size(), kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        if ((e = launch_rng(E, E.hi, true)) != cudaSuccess) return e;
+        rng = true;
+    }
+    if ((e = cudaEventRecord(E.ev_dfork, E.hi)) != cudaSuccess) return e;
     for (const Engine::PhaseClass& pc : E.pcls) {
         cudaStream_t st = pc.dense >= 0 ? E.cls_st[pc.dense] : E.hi;
         if (st != E.hi && (e = cudaStreamWaitEvent(st, E.ev_dfork, 0)) != cudaSuccess) return e;
-        if (pc.nslabs > 0) {
+        if (E.split_phase0 && pc.nslabs > 0) {
             k_solve<0><<<(unsigned)pc.nslabs, kSolveThreads, E.smem_solve, st>>>(E.d_ctx, E.d_slabs1 + pc.slab0);
             if ((e = cudaGetLastError()) != cudaSuccess) return e;
             if (!rng) {
@@ -334,9 +345,10 @@ cudaError_t launch_solve(Engine& E) {
 int kernels_per_step(const Engine& E) {
     int p0 = 1, p1 = 1;
     if (!E.cls_st.empty()) {
-        p0 = p1 = 0;
+        p0 = E.split_phase0 ? 0 : 1;
+        p1 = 0;
         for (const Engine::PhaseClass& pc : E.pcls) {
-            p0 += pc.nslabs > 0 ? 1 : 0;
+            if (E.split_phase0) p0 += pc.nslabs > 0 ? 1 : 0;
             p1 += (E.solve_mode == 2 ? pc.ntiles : pc.nslabs) > 0 ? 1 : 0;
         }
     }
@@ -392,6 +404,7 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     // index of this batch's first env in a batch sharded over several GPUs: the
     // per-env draws (desync cut, random-start stream) follow the global index
     const long long env_offset = std::max(0LL, (long long)kw_num(kw, "env_offset", 0.0));
+    E.overlap = (int)kw_num(kw, "overlap", -1.0);
     E.rew_norm = kw_num(kw, "rew_norm", 0.0) != 0.0;
     E.rew_center = !E.rew_norm && kw_num(kw, "rew_center", 0.0) != 0.0;
     {
@@ -859,8 +872,13 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     CK(cudaEventCreateWithFlags(&E.ev_join, cudaEventDisableTiming));
     CK(cudaEventCreateWithFlags(&E.ev_dfork, cudaEventDisableTiming));
     // a stream per dense class once there are two or more (the classes and
-    // their phase-1 shares then run side by side)
-    if (E.dense_cls.size() > 1) {
+    // their phase-1 shares then run side by side); kwarg overlap: 0 every part
+    // of the solve on hi in turn, 1 phase 1 by class, 2 the whole solve by
+    // class, -1 (default) 2 when the slabs are more than one wave, else 1
+    if (E.dense_cls.size() > 1 && E.overlap != 0) {
+        int sms = 0;
+        CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0));
+        E.split_phase0 = E.overlap == 2 || (E.overlap < 0 && (int)E.slabs.size() > sms);
         int least = 0, greatest = 0;
         CK(cudaDeviceGetStreamPriorityRange(&least, &greatest));
         E.cls_st.assign(E.dense_cls.size(), nullptr);
@@ -1501,13 +1519,18 @@ int sb_step_timed(float* ms) {
             cudaEventRecord(ev[5], E.hi);
             launch_phase1(E, E.hi);
         } else {
-            cudaEventRecord(E.ev_dfork, E.hi);
             bool rng = false;
+            if (!E.split_phase0) {
+                k_solve<0><<<(unsigned)E.slabs.size(), kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
+                launch_rng(E, E.hi, true);
+                rng = true;
+            }
+            cudaEventRecord(E.ev_dfork, E.hi);
             for (size_t i = 0; i < np; i++) {
                 const Engine::PhaseClass& pc = E.pcls[i];
                 cudaStream_t st = pc.dense >= 0 ? E.cls_st[pc.dense] : E.hi;
                 if (st != E.hi) cudaStreamWaitEvent(st, E.ev_dfork, 0);
-                if (pc.nslabs > 0) {
+                if (E.split_phase0 && pc.nslabs > 0) {
                     k_solve<0><<<(unsigned)pc.nslabs, kSolveThreads, E.smem_solve, st>>>(E.d_ctx, E.d_slabs1 + pc.slab0);
                     if (!rng) { launch_rng(E, st, true); rng = true; }
                 }
