@@ -80,7 +80,7 @@ SMI_Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,c
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="config4", choices=sorted(WORKLOADS))
@@ -123,7 +123,7 @@ class ClockSampler:
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={SMI_Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
@@ -278,9 +278,10 @@ def action_pool(n: int, n_batches: int, seed: int = 0) -> np.ndarray:
     return out
 
 
-def profile_traffic() -> float | None:
-    """DRAM bytes per solve launch from the committed ncu summary, if present."""
-    p = ROOT / "profiles" / "k_solve_config2_960.md"
+def profile_traffic(workload: str) -> float | None:
+    """DRAM bytes of one step's solve kernels from the committed ncu summary of
+    the workload (profiles/solve_<workload>_<envs>.md), if present."""
+    p = ROOT / "profiles" / f"solve_{workload}_{WORKLOADS[workload]['envs']}.md"
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
@@ -465,7 +466,7 @@ def run_ours(args) -> None:
     achieved = bytes_launch / (k_ms["k_solve"] / 1e3) / 1e9
     fp64_achieved = flops_launch / (k_ms["k_solve"] / 1e3) / 1e12
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                "traffic": profile_traffic(), "kernel": "k_solve (phase 0 + k_dense + phase 1)",
+                "traffic": profile_traffic(args.workload) if args.envs == WORKLOADS[args.workload]["envs"] else None, "kernel": "the solve: k_solve<0> (first L/U sweep pair), k_dense, phase 1 (k_correct in the corrected build), by dense class",
                 "peak_source": peak_src, "kernel_ms": k_ms["k_solve"], "algorithmic_bytes_per_launch": bytes_launch,
                 "per_kernel_ms": k_ms,
                 "fp64": {"achieved_tflops": fp64_achieved, "peak_tflops": fp64_peak, "frac": fp64_achieved / fp64_peak,
