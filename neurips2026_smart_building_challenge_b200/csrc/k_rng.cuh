@@ -1,6 +1,6 @@
 // The step's random inputs, produced one transition ahead of the step that
-// consumes them, on their own streams beside the whole step (none of them
-// depends on temperatures):
+// consumes them, beside the thermal solve (none of them depends on
+// temperatures):
 //   * k_conv, one warp per scenario: the convection draws of one transition
 //     (complete_port/csim/sb_convect.c:39-73) -- Bernoulli cell picks,
 //     candidate draws, Fisher-Yates shuffle and swaps -- composed into one
@@ -19,11 +19,12 @@
 //     each new episode's start day (gpu/smart_buildings.cu:1636-1657).
 // Transition q (counted from puf_reset) is written to slot q & 1 and read by
 // that step's k_post; k_occ's reset mode writes slot kResetSlot for puf_reset.
-// In a step both run as programmatic dependents of the solve's longest kernel
-// (on the SMs its slabs leave free, once every slab is resident). Only CTA 0
-// of each waits for its primary (griddepcontrol.wait) before it exits, so the
-// producer completes after the primary while its other CTAs free their SMs as
-// soon as their work is done.
+// In a step both run as programmatic dependents of the first solve (its
+// heaviest class's launch when the first solve runs by class), on the SMs its
+// slabs leave free once every slab is resident. Only CTA 0 of each waits for
+// its primary (griddepcontrol.wait) before it exits, so the producer completes
+// after the primary while its other CTAs free their SMs as soon as their work
+// is done.
 #pragma once
 #include "dev_util.cuh"
 
