@@ -131,7 +131,7 @@ struct Engine {
     // phase-1 work (k_correct tiles or k_solve<1> slabs) on a stream of their
     // own, so a class's phase 1 starts as soon as its own dense systems are
     // solved; the groups without an air side (dense = -1) run on hi
-    struct PhaseClass { int dense, tile0, ntiles, slab0, nslabs; };
+    struct PhaseClass { int dense, tile0, ntiles, slab0, nslabs, env0, nenv; };   // env0: into dense_order
     std::vector<PhaseClass> pcls;
     SlabDesc* d_slabs1 = nullptr;         // the slabs in pcls order (k_solve<1>)
     std::vector<cudaStream_t> cls_st;     // one per dense class (empty: all on hi)
@@ -288,83 +288,139 @@ cudaError_t launch_phase1(Engine& E, cudaStream_t st, const Engine::PhaseClass* 
     return cudaGetLastError();
 }
 
-// The solve on the high-priority stream: phase 0 (first L/U solve) with the
-// random inputs of the next transition beside it (programmatic dependents of
-// phase 0; k_post of this step reads the ones made during the step before),
-// then the dense air-side solves and phase 1. With several dense classes
-// (kwarg overlap, default on) each class runs its dense systems and then its
-// phase-1 share on its own stream, forked after phase 0 and joined back into
-// hi, so the lighter classes' phase 1 runs while the heaviest class's dense
-// systems are still being solved. When the slabs are more than one wave
-// (split_phase0), each class runs its phase 0 on its stream as well, so one
-// class's dense solves fill the SMs the other classes' slabs leave free. No
-// kernel waits on a flag another kernel writes.
-cudaError_t launch_solve(Engine& E) {
+// Events of one step for sb_step_timed: per phase class the ends of its
+// k_pre, phase 0, dense systems and phase 1 (recorded on the stream that ran
+// them; the same moment for every class where the part is one launch), and
+// the step's start and end on the bound stream.
+struct StepMarks {
+    std::vector<cudaEvent_t> pre, p0, dense, p1;
+    cudaEvent_t start = nullptr, end = nullptr;
+};
+
+// One step. k_pre and k_post run on the bound stream, the solve on the
+// highest-priority stream hi: phase 0 (first L/U solve) with the random inputs
+// of the next transition beside it (programmatic dependents of phase 0; k_post
+// of this step reads the ones made during the step before), the dense
+// air-side systems and phase 1. With several dense classes (kwarg overlap,
+// default on) each class runs its dense systems, its phase-1 share and the
+// k_post of its envs on a stream of its own, forked after phase 0 and joined
+// back before the step ends, so the lighter classes finish while the heaviest
+// class's dense systems are still being solved. When the slabs are more than
+// one wave (split_phase0) each class also runs the k_pre and phase 0 of its
+// envs on its stream: the classes are independent pipelines and one class's
+// dense solves fill the SMs the other classes' slabs leave free. No kernel
+// waits on a flag another kernel writes.
+cudaError_t enqueue_step(Engine& E, StepMarks* mk) {
     cudaError_t e = cudaSuccess;
-    if (E.cls_st.empty()) {
-        k_solve<0><<<(unsigned)E.slabs.size(), kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
-        if ((e = launch_rng(E, E.hi, true)) != cudaSuccess) return e;
-        if ((e = launch_dense(E, E.hi)) != cudaSuccess) return e;
-        return launch_phase1(E, E.hi);
+#define SB_EQ(x)                                  \
+    do {                                          \
+        if ((e = (x)) != cudaSuccess) return e;   \
+    } while (0)
+    auto mark = [&](std::vector<cudaEvent_t> StepMarks::*v, size_t i, cudaStream_t st) -> cudaError_t {
+        if (!mk || i >= (mk->*v).size()) return cudaSuccess;
+        return cudaEventRecord((mk->*v)[i], st);
+    };
+    auto mark_all = [&](std::vector<cudaEvent_t> StepMarks::*v, cudaStream_t st) -> cudaError_t {
+        cudaError_t r = cudaSuccess;
+        if (mk)
+            for (size_t i = 0; i < (mk->*v).size() && r == cudaSuccess; i++) r = cudaEventRecord((mk->*v)[i], st);
+        return r;
+    };
+    const bool classes = !E.cls_st.empty();
+    const bool split0 = classes && E.split_phase0;
+    const unsigned all_slabs = (unsigned)E.slabs.size();
+    if (mk) SB_EQ(cudaEventRecord(mk->start, E.stream));
+    if (!split0) {
+        k_pre<<<(unsigned)E.n_env, 128, E.smem_pre, E.stream>>>(E.d_ctx, -1);
+        SB_EQ(cudaGetLastError());
+        SB_EQ(mark_all(&StepMarks::pre, E.stream));
     }
-    bool rng = false;
-    if (!E.split_phase0) {
-        // every slab in one wave: phase 0 in one launch, then the classes
-        k_solve<0><<<(unsigned)E.slabs.size(), kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
-        if ((e = launch_rng(E, E.hi, true)) != cudaSuccess) return e;
-        rng = true;
-    }
-    if ((e = cudaEventRecord(E.ev_dfork, E.hi)) != cudaSuccess) return e;
-    for (const Engine::PhaseClass& pc : E.pcls) {
-        cudaStream_t st = pc.dense >= 0 ? E.cls_st[pc.dense] : E.hi;
-        if (st != E.hi && (e = cudaStreamWaitEvent(st, E.ev_dfork, 0)) != cudaSuccess) return e;
-        if (E.split_phase0 && pc.nslabs > 0) {
-            k_solve<0><<<(unsigned)pc.nslabs, kSolveThreads, E.smem_solve, st>>>(E.d_ctx, E.d_slabs1 + pc.slab0);
-            if ((e = cudaGetLastError()) != cudaSuccess) return e;
-            if (!rng) {
-                // beside the first (heaviest) class's phase 0
-                if ((e = launch_rng(E, st, true)) != cudaSuccess) return e;
-                rng = true;
-            }
+    SB_EQ(cudaEventRecord(E.ev_fork, E.stream));
+    SB_EQ(cudaStreamWaitEvent(E.hi, E.ev_fork, 0));
+    if (!classes) {
+        k_solve<0><<<all_slabs, kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
+        SB_EQ(cudaGetLastError());
+        SB_EQ(launch_rng(E, E.hi, true));
+        SB_EQ(mark_all(&StepMarks::p0, E.hi));
+        SB_EQ(launch_dense(E, E.hi));
+        SB_EQ(mark_all(&StepMarks::dense, E.hi));
+        SB_EQ(launch_phase1(E, E.hi));
+        SB_EQ(mark_all(&StepMarks::p1, E.hi));
+        SB_EQ(cudaEventRecord(E.ev_join, E.hi));
+        SB_EQ(cudaStreamWaitEvent(E.stream, E.ev_join, 0));
+        k_post<<<(unsigned)E.n_env, 128, E.smem_post, E.stream>>>(E.d_ctx, -1);
+        SB_EQ(cudaGetLastError());
+    } else {
+        bool rng = false;
+        if (!split0) {
+            // every slab in one wave: phase 0 in one launch, then the classes
+            k_solve<0><<<all_slabs, kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
+            SB_EQ(cudaGetLastError());
+            SB_EQ(launch_rng(E, E.hi, true));
+            SB_EQ(mark_all(&StepMarks::p0, E.hi));
+            rng = true;
         }
-        if (pc.dense >= 0 && (e = launch_dense_class(E, (size_t)pc.dense, st, false)) != cudaSuccess) return e;
-        if ((e = launch_phase1(E, st, &pc)) != cudaSuccess) return e;
-        if (st != E.hi && (e = cudaEventRecord(E.cls_ev[pc.dense], st)) != cudaSuccess) return e;
+        SB_EQ(cudaEventRecord(E.ev_dfork, E.hi));
+        for (size_t i = 0; i < E.pcls.size(); i++) {
+            const Engine::PhaseClass& pc = E.pcls[i];
+            cudaStream_t st = pc.dense >= 0 ? E.cls_st[pc.dense] : E.hi;
+            if (st != E.hi) SB_EQ(cudaStreamWaitEvent(st, E.ev_dfork, 0));
+            if (split0) {
+                if (pc.nenv > 0) {
+                    k_pre<<<(unsigned)pc.nenv, 128, E.smem_pre, st>>>(E.d_ctx, pc.env0);
+                    SB_EQ(cudaGetLastError());
+                }
+                SB_EQ(mark(&StepMarks::pre, i, st));
+                if (pc.nslabs > 0) {
+                    k_solve<0><<<(unsigned)pc.nslabs, kSolveThreads, E.smem_solve, st>>>(E.d_ctx,
+                                                                                         E.d_slabs1 + pc.slab0);
+                    SB_EQ(cudaGetLastError());
+                    if (!rng) {
+                        // beside the first (heaviest) class's phase 0
+                        SB_EQ(launch_rng(E, st, true));
+                        rng = true;
+                    }
+                }
+                SB_EQ(mark(&StepMarks::p0, i, st));
+            }
+            if (pc.dense >= 0) SB_EQ(launch_dense_class(E, (size_t)pc.dense, st, false));
+            SB_EQ(mark(&StepMarks::dense, i, st));
+            SB_EQ(launch_phase1(E, st, &pc));
+            SB_EQ(mark(&StepMarks::p1, i, st));
+            if (pc.nenv > 0) {
+                k_post<<<(unsigned)pc.nenv, 128, E.smem_post, st>>>(E.d_ctx, pc.env0);
+                SB_EQ(cudaGetLastError());
+            }
+            if (st != E.hi) SB_EQ(cudaEventRecord(E.cls_ev[pc.dense], st));
+        }
+        if (!rng) SB_EQ(launch_rng(E, E.hi, false));
+        for (cudaEvent_t ev : E.cls_ev) SB_EQ(cudaStreamWaitEvent(E.hi, ev, 0));
+        SB_EQ(cudaEventRecord(E.ev_join, E.hi));
+        SB_EQ(cudaStreamWaitEvent(E.stream, E.ev_join, 0));
     }
-    if (!rng && (e = launch_rng(E, E.hi, false)) != cudaSuccess) return e;
-    for (cudaEvent_t ev : E.cls_ev)
-        if ((e = cudaStreamWaitEvent(E.hi, ev, 0)) != cudaSuccess) return e;
+    if (mk) SB_EQ(cudaEventRecord(mk->end, E.stream));
+#undef SB_EQ
     return cudaSuccess;
 }
 
-// k_pre, k_conv, k_occ, k_post, one k_dense launch per class of equal k, and
-// phases 0 and 1: one launch each, or one per phase class with work when the
-// classes run on their own streams
+// Kernels one step launches: k_conv and k_occ, and k_pre, phase 0, k_post (one
+// launch each, or one per phase class with envs), one k_dense per class, phase 1
+// (one launch, or one per phase class with work)
 int kernels_per_step(const Engine& E) {
-    int p0 = 1, p1 = 1;
-    if (!E.cls_st.empty()) {
-        p0 = E.split_phase0 ? 0 : 1;
-        p1 = 0;
-        for (const Engine::PhaseClass& pc : E.pcls) {
-            if (E.split_phase0) p0 += pc.nslabs > 0 ? 1 : 0;
-            p1 += (E.solve_mode == 2 ? pc.ntiles : pc.nslabs) > 0 ? 1 : 0;
-        }
+    if (E.cls_st.empty()) return 6 + (int)E.dense_cls.size();
+    int n = 2 + (int)E.dense_cls.size();
+    const bool split0 = E.split_phase0;
+    if (!split0) n += 2;   // k_pre, phase 0
+    for (const Engine::PhaseClass& pc : E.pcls) {
+        if (split0) n += (pc.nenv > 0 ? 1 : 0) + (pc.nslabs > 0 ? 1 : 0);
+        n += (E.solve_mode == 2 ? pc.ntiles : pc.nslabs) > 0 ? 1 : 0;
+        n += pc.nenv > 0 ? 1 : 0;
     }
-    return 4 + p0 + (int)E.dense_cls.size() + p1;
+    return n;
 }
 
 bool launch_step(Engine& E) {
-    k_pre<<<(unsigned)E.n_env, 128, E.smem_pre, E.stream>>>(E.d_ctx);
-    CK(cudaGetLastError());
-    CK(cudaEventRecord(E.ev_fork, E.stream));
-    CK(cudaStreamWaitEvent(E.hi, E.ev_fork, 0));
-    CK(launch_solve(E));
-    CK(cudaEventRecord(E.ev_join, E.hi));
-    CK(cudaStreamWaitEvent(E.stream, E.ev_join, 0));
-    k_post<<<(unsigned)E.n_env, 128, E.smem_post, E.stream>>>(E.d_ctx);
-    CK(cudaGetLastError());
+    CK(enqueue_step(E, nullptr));
     return true;
 }
 
@@ -794,15 +850,24 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     {
         std::vector<CorrTile> tiles;
         std::vector<SlabDesc> slabs1;
+        int env_end = 0;
         auto add = [&](int dense, int k) {
-            Engine::PhaseClass pc{dense, (int)tiles.size(), 0, (int)slabs1.size(), 0};
+            Engine::PhaseClass pc{dense, (int)tiles.size(), 0, (int)slabs1.size(), 0, 0, 0};
+            if (dense >= 0) {
+                pc.env0 = E.dense_cls[dense].first;
+                pc.nenv = E.dense_cls[dense].count;
+                env_end = std::max(env_end, pc.env0 + pc.nenv);
+            } else {
+                pc.env0 = env_end;   // the envs without an air side close dense_order
+                pc.nenv = n - env_end;
+            }
             for (const CorrTile& t : E.ctiles)
                 if (E.gd[t.group].k == k) tiles.push_back(t);
             for (const SlabDesc& sl : E.slabs)
                 if (E.gd[sl.group].k == k) slabs1.push_back(sl);
             pc.ntiles = (int)tiles.size() - pc.tile0;
             pc.nslabs = (int)slabs1.size() - pc.slab0;
-            if (dense >= 0 || pc.ntiles > 0 || pc.nslabs > 0) E.pcls.push_back(pc);
+            if (dense >= 0 || pc.ntiles > 0 || pc.nslabs > 0 || pc.nenv > 0) E.pcls.push_back(pc);
         };
         for (size_t c = 0; c < E.dense_cls.size(); c++) add((int)c, E.dense_cls[c].k);
         add(-1, 0);
@@ -1496,82 +1561,52 @@ int sb_snapshot_write(int env, const char* path) {
 int sb_step_timed(float* ms) {
     if (!g_eng || !g_eng->ready || !ms) return -1;
     Engine& E = *g_eng;
-    const size_t nc = E.cls_st.size(), np = E.pcls.size();
-    std::vector<cudaEvent_t> ev(7 + 2 * np, nullptr);
+    const size_t np = std::max<size_t>(1, E.pcls.size());
+    StepMarks mk;
     bool ok = true;
-    for (auto& e : ev) ok = ok && cudaEventCreate(&e) == cudaSuccess;
-    // the step of launch_step with events around each part; the producers of
-    // the next transition run beside phase 0, inside its interval. With one
-    // stream per dense class the classes overlap: phase 0 is the interval until
-    // the last class's phase 0 ends, k_dense from there until the last class's
-    // dense solves end, and phase 1 the rest of the solve.
-    if (ok) {
-        cudaEventRecord(ev[0], E.stream);
-        k_pre<<<(unsigned)E.n_env, 128, E.smem_pre, E.stream>>>(E.d_ctx);
-        cudaEventRecord(ev[1], E.stream);
-        cudaEventRecord(E.ev_fork, E.stream);
-        cudaStreamWaitEvent(E.hi, E.ev_fork, 0);
-        if (nc == 0) {
-            k_solve<0><<<(unsigned)E.slabs.size(), kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
-            launch_rng(E, E.hi, true);
-            cudaEventRecord(ev[4], E.hi);
-            launch_dense(E, E.hi);
-            cudaEventRecord(ev[5], E.hi);
-            launch_phase1(E, E.hi);
-        } else {
-            bool rng = false;
-            if (!E.split_phase0) {
-                k_solve<0><<<(unsigned)E.slabs.size(), kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
-                launch_rng(E, E.hi, true);
-                rng = true;
-            }
-            cudaEventRecord(E.ev_dfork, E.hi);
-            for (size_t i = 0; i < np; i++) {
-                const Engine::PhaseClass& pc = E.pcls[i];
-                cudaStream_t st = pc.dense >= 0 ? E.cls_st[pc.dense] : E.hi;
-                if (st != E.hi) cudaStreamWaitEvent(st, E.ev_dfork, 0);
-                if (E.split_phase0 && pc.nslabs > 0) {
-                    k_solve<0><<<(unsigned)pc.nslabs, kSolveThreads, E.smem_solve, st>>>(E.d_ctx, E.d_slabs1 + pc.slab0);
-                    if (!rng) { launch_rng(E, st, true); rng = true; }
-                }
-                cudaEventRecord(ev[7 + 2 * i], st);
-                if (pc.dense >= 0) launch_dense_class(E, (size_t)pc.dense, st, false);
-                cudaEventRecord(ev[8 + 2 * i], st);
-                launch_phase1(E, st, &pc);
-                if (st != E.hi) cudaEventRecord(E.cls_ev[pc.dense], st);
-            }
-            if (!rng) launch_rng(E, E.hi, false);
-            for (cudaEvent_t c : E.cls_ev) cudaStreamWaitEvent(E.hi, c, 0);
-        }
-        cudaEventRecord(ev[2], E.hi);
-        cudaStreamWaitEvent(E.stream, ev[2], 0);
-        cudaEventRecord(ev[6], E.stream);
-        k_post<<<(unsigned)E.n_env, 128, E.smem_post, E.stream>>>(E.d_ctx);
-        cudaEventRecord(ev[3], E.stream);
-        ok = cudaGetLastError() == cudaSuccess && cudaEventSynchronize(ev[3]) == cudaSuccess;
+    for (auto* v : {&mk.pre, &mk.p0, &mk.dense, &mk.p1}) {
+        v->assign(np, nullptr);
+        for (auto& e : *v) ok = ok && cudaEventCreate(&e) == cudaSuccess;
     }
+    ok = ok && cudaEventCreate(&mk.start) == cudaSuccess && cudaEventCreate(&mk.end) == cudaSuccess;
+    // the step of puf_step with events at the end of each part of each class.
+    // The parts of different classes overlap, so each is reported as the time
+    // from the last class's end of the part before it to the last class's end
+    // of this part (the parts then add up to the step); the solve is the span
+    // from the first class's k_pre end to the last class's phase-1 end, and the
+    // producers (k_conv, k_occ) run inside phase 0.
+    ok = ok && enqueue_step(E, &mk) == cudaSuccess && cudaEventSynchronize(mk.end) == cudaSuccess;
     if (ok) {
-        ms[0] = -1.0f;                                 // k_conv, k_occ: beside phase 0, inside its interval
-        cudaEventElapsedTime(&ms[1], ev[0], ev[1]);   // k_pre
-        cudaEventElapsedTime(&ms[2], ev[1], ev[2]);   // the solve: phase 0, k_dense, phase 1
-        cudaEventElapsedTime(&ms[3], ev[6], ev[3]);   // k_post
-        if (nc == 0) {
-            cudaEventElapsedTime(&ms[4], ev[1], ev[4]);   // phase 0
-            cudaEventElapsedTime(&ms[5], ev[4], ev[5]);   // k_dense
-            cudaEventElapsedTime(&ms[6], ev[5], ev[2]);   // phase 1 or k_correct
-        } else {
-            float p0 = 0.0f, d = 0.0f, t = 0.0f;
-            for (size_t i = 0; i < np; i++) {
-                if (cudaEventElapsedTime(&t, ev[1], ev[7 + 2 * i]) == cudaSuccess) p0 = std::max(p0, t);
-                if (cudaEventElapsedTime(&t, ev[1], ev[8 + 2 * i]) == cudaSuccess) d = std::max(d, t);
-            }
-            ms[4] = p0;                                   // until the last class's phase 0 ends
-            ms[5] = std::max(0.0f, d - p0);               // then until the last class's dense solves end
-            ms[6] = std::max(0.0f, ms[2] - std::max(d, p0));   // the phase-1 work after that
+        auto span = [&](cudaEvent_t a, cudaEvent_t b) {
+            float t = 0.0f;
+            cudaEventElapsedTime(&t, a, b);
+            return t;
+        };
+        float pre = 0.0f, p0 = 0.0f, d = 0.0f, p1 = 0.0f, first_pre = 1e30f, total = span(mk.start, mk.end);
+        for (size_t i = 0; i < np; i++) {
+            const float a = span(mk.start, mk.pre[i]);
+            pre = std::max(pre, a);
+            first_pre = std::min(first_pre, a);
+            p0 = std::max(p0, span(mk.start, mk.p0[i]));
+            d = std::max(d, span(mk.start, mk.dense[i]));
+            p1 = std::max(p1, span(mk.start, mk.p1[i]));
         }
+        p0 = std::max(p0, pre);
+        d = std::max(d, p0);
+        p1 = std::max(p1, d);
+        ms[0] = -1.0f;                 // k_conv, k_occ: beside phase 0, inside its interval
+        ms[1] = pre;                   // k_pre
+        ms[2] = p1 - first_pre;        // the solve
+        ms[3] = std::max(0.0f, total - p1);   // k_post (after the last class's phase 1)
+        ms[4] = p0 - pre;              // phase 0
+        ms[5] = d - p0;                // k_dense
+        ms[6] = p1 - d;                // phase 1 or k_correct
     }
-    for (auto& e : ev)
-        if (e) cudaEventDestroy(e);
+    for (auto* v : {&mk.pre, &mk.p0, &mk.dense, &mk.p1})
+        for (auto& e : *v)
+            if (e) cudaEventDestroy(e);
+    if (mk.start) cudaEventDestroy(mk.start);
+    if (mk.end) cudaEventDestroy(mk.end);
     return ok ? 0 : -1;
 }
 

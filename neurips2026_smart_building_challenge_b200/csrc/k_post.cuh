@@ -183,9 +183,11 @@ __device__ inline void restart_env(const StepCtx* ctx, int env, const GroupDev& 
     __syncthreads();
 }
 
-__global__ void __launch_bounds__(128) k_post(const StepCtx* __restrict__ ctx) {
+// One CTA per env: env blockIdx.x (first < 0) or dense_order[first + blockIdx.x]
+// (one class's envs)
+__global__ void __launch_bounds__(128) k_post(const StepCtx* __restrict__ ctx, int first) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const int env = blockIdx.x;
+    const int env = first < 0 ? (int)blockIdx.x : ctx->dense_order[first + blockIdx.x];
     const EnvIndex ei = ctx->envs[env];
     const GroupDev& g = ctx->groups[ei.group];
     const ScnDev& s = ctx->scns[ei.scn];

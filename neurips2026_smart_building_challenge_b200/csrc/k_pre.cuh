@@ -137,9 +137,11 @@ __device__ __forceinline__ void mode_default(int& mode, double zt, double hsp, d
     else mode = M_OFF;
 }
 
-__global__ void __launch_bounds__(128) k_pre(const StepCtx* __restrict__ ctx) {
+// One CTA per env: env blockIdx.x (first < 0) or dense_order[first + blockIdx.x]
+// (one class's envs)
+__global__ void __launch_bounds__(128) k_pre(const StepCtx* __restrict__ ctx, int first) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const int env = blockIdx.x;
+    const int env = first < 0 ? (int)blockIdx.x : ctx->dense_order[first + blockIdx.x];
     const EnvIndex ei = ctx->envs[env];
     const GroupDev& g = ctx->groups[ei.group];
     const ScnDev& s = ctx->scns[ei.scn];
