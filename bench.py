@@ -85,6 +85,8 @@ def parse_args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="config4", choices=sorted(WORKLOADS))
     ap.add_argument("--envs", type=int, default=0, help="envs per GPU (0: the workload's)")
+    ap.add_argument("--strong", action="store_true",
+                    help="strong scaling: --envs (default the workload's) is the job's total, split over the GPUs")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-variants", action="store_true", help="time only the stated build")
     ap.add_argument("--profile", action="store_true",
@@ -103,10 +105,16 @@ def parse_args():
     return args
 
 
+def job_envs(args, world: int) -> int:
+    """Envs of the whole job: per GPU x N (weak scaling) or --envs (strong)."""
+    return args.envs if args.strong else args.envs * world
+
+
 def bench_config(args, world: int) -> dict:
     """The `config` object both arms print (the same keys and values)."""
     w = WORKLOADS[args.workload]
-    return {"workload": w["desc"], "envs_per_gpu": args.envs, "total_envs": args.envs * world,
+    total = job_envs(args, world)
+    return {"workload": w["desc"], "envs_per_gpu": total / world, "total_envs": total,
             "solve": args.solve, "l2": "flushed between timed steps (256 MiB write, untimed)",
             "parallelism": f"env-sharded x{world}, no per-step collective"}
 
@@ -234,7 +242,7 @@ def run_reference(args) -> None:
         return
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     cache = ROOT / ".sbb_cache" / "bench"
-    total_envs = args.envs * world
+    total_envs = job_envs(args, world)
     blobs = blob_list(cache, total_envs, args.workload)
     cores = min(os.cpu_count() or 1, total_envs)
     # a bounded sample of the job's envs (the same scenario mix, at most 120
@@ -255,8 +263,8 @@ def run_reference(args) -> None:
     ms = total_envs / value * 1e3   # the job's step at that rate
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-            "config": bench_config(args, world),
+            "scaling": "strong" if args.strong else "weak", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic", "config": bench_config(args, world),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": cpu_kind(),
                              "sample": f"{sample} of the job's {total_envs} envs (same scenario mix) over "
                                        f"{cores} processes ({sample / cores:.0f} per process), {args.steps} "
@@ -421,10 +429,9 @@ def run_ours(args) -> None:
 
     cache = ROOT / ".sbb_cache" / f"bench_rank{rank}"
     d = workload_dir(args.workload, cache)
-    n = args.envs
     # this rank's slice of the job's envs (the per-env draws follow the global index)
-    start, count = sbdist.shard(n * world, world, rank)
-    assert count == n
+    total = job_envs(args, world)
+    start, n = sbdist.shard(total, world, rank)
     groups = WORKLOADS[args.workload]["groups"]
     pool_np = action_pool(n, 8, seed=1234 + rank)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=f"cuda:{local}")   # > 126 MB L2
@@ -438,7 +445,7 @@ def run_ours(args) -> None:
         pool = torch.from_numpy(pool_np).to(env.device)
         if solve != args.solve:
             ms_total = timed_steps(env, pool, flush, args.steps, args.warmup, world, torch, dist)
-            variants[solve] = {"value": world * n * args.steps / (ms_total / 1e3),
+            variants[solve] = {"value": total * args.steps / (ms_total / 1e3),
                                "ms_per_step": ms_total / args.steps, "note": SOLVE_NOTE[solve],
                                "per_kernel_ms": kernel_times(env, pool, flush, torch)}
             env.close()
@@ -447,7 +454,7 @@ def run_ours(args) -> None:
             ms_total = timed_steps(env, pool, flush, args.steps, args.warmup, world, torch, dist, clk)
         break
     ms_per_step = ms_total / args.steps
-    value = world * n * args.steps / (ms_total / 1e3)
+    value = total * args.steps / (ms_total / 1e3)
     status = env.status()
 
     # roofline of the solve (HBM, the north star's bound) and its fp64 issue share
@@ -466,7 +473,7 @@ def run_ours(args) -> None:
     achieved = bytes_launch / (k_ms["k_solve"] / 1e3) / 1e9
     fp64_achieved = flops_launch / (k_ms["k_solve"] / 1e3) / 1e12
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                "traffic": profile_traffic(args.workload) if args.envs == WORKLOADS[args.workload]["envs"] else None, "kernel": "the solve: k_solve<0> (first L/U sweep pair), k_dense, phase 1 (k_correct in the corrected build), by dense class",
+                "traffic": profile_traffic(args.workload) if n == WORKLOADS[args.workload]["envs"] else None, "kernel": "the solve: k_solve<0> (first L/U sweep pair), k_dense, phase 1 (k_correct in the corrected build), by dense class",
                 "peak_source": peak_src, "kernel_ms": k_ms["k_solve"], "algorithmic_bytes_per_launch": bytes_launch,
                 "per_kernel_ms": k_ms,
                 "fp64": {"achieved_tflops": fp64_achieved, "peak_tflops": fp64_peak, "frac": fp64_achieved / fp64_peak,
@@ -497,8 +504,8 @@ def run_ours(args) -> None:
     e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=env.device)
     if world > 1:
         dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
-    e2e = {"value": world * n * e_steps / (float(e_ms.item()) / 1e3), "unit": UNIT,
-           "h2d_bytes_per_step": n * 272 * 4, "d2h_bytes_per_step": n * (1024 + 2) * 4,
+    e2e = {"value": total * e_steps / (float(e_ms.item()) / 1e3), "unit": UNIT,
+           "h2d_bytes_per_step": total * 272 * 4, "d2h_bytes_per_step": total * (1024 + 2) * 4,
            "copies": "pinned host buffers, two copy streams overlapping the kernels"}
 
     # episode statistics: the per-scenario matrix of every rank summed over NCCL
@@ -511,7 +518,8 @@ def run_ours(args) -> None:
         config = bench_config(args, world)
         config["solve_note"] = SOLVE_NOTE[args.solve]
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+                "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+                "scaling": "strong" if args.strong else "weak",
                 "vs_baseline": None, "dtype": "f64", "data": "synthetic", "config": config,
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
                 "clocks": clk.summary(), "device_status": status, "variants": variants,
