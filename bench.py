@@ -101,7 +101,8 @@ def parse_args():
                     help="configuration 1: one building for its whole month, GPU and the reference core (1 thread)")
     args = ap.parse_args()
     if args.envs <= 0:
-        args.envs = WORKLOADS[args.workload]["envs"]
+        # configuration 5 (--rollout) is 960 envs per GPU whatever the workload
+        args.envs = 960 if args.rollout else WORKLOADS[args.workload]["envs"]
     return args
 
 
@@ -630,7 +631,7 @@ def run_rollout(args) -> None:
 
     d = config_dir(2, ROOT / ".sbb_cache" / f"bench_rank{rank}")
     n = args.envs
-    env = SmartBuildingsVec(n, blob_dir=str(d), groups=30, device=f"cuda:{local}")
+    env = SmartBuildingsVec(n, blob_dir=str(d), groups=30, device=f"cuda:{local}", **SOLVE_KW[args.solve])
     env.reset()
     ro = Rollout(env, ZonePolicy(env.device, seed=17), seed=1000 + rank, beta_floor=1.0, beta_cap=12.0)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=env.device)   # > 126 MB L2
@@ -697,6 +698,7 @@ def run_rollout(args) -> None:
                 "warmup": args.warmup, "ms_per_step": ms_total / args.steps, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f64 env, f32 policy", "data": "synthetic",
                 "config": {"workload": ROLLOUT_WORKLOAD, "envs_per_gpu": n, "total_envs": n * world,
+                           "solve": args.solve,
                            "horizon": args.horizon, "l2": "flushed between timed steps (256 MiB write, untimed)",
                            "parallelism": f"env-sharded x{world}, no per-step collective"},
                 "env_kernel_ms": k_ms, "e2e": e2e, "gpu_launches": launches, "clocks": clk.summary(),
