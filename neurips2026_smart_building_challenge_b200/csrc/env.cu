@@ -1442,6 +1442,10 @@ int sb_beta_actions(const float* raw, const unsigned char* mask, float* actions,
 }
 
 int sb_dense_check(int k, int n, const double* m_rowmajor, const double* b, double* out) {
+    return sb_dense_check_mode(k, n, m_rowmajor, b, out, 0);
+}
+
+int sb_dense_check_mode(int k, int n, const double* m_rowmajor, const double* b, double* out, int fast_back) {
     if (k < 1 || k > kMaxK || n < 1 || !m_rowmajor || !b || !out) { set_err("sb_dense_check: bad arguments"); return -1; }
     const size_t kk = (size_t)k * k;
     std::vector<double> mt(kk * n);
@@ -1456,7 +1460,7 @@ int sb_dense_check(int k, int n, const double* m_rowmajor, const double* b, doub
     ok = ok && cudaMemcpy(dm, mt.data(), mt.size() * 8, cudaMemcpyHostToDevice) == cudaSuccess &&
          cudaMemcpy(db, b, (size_t)n * k * 8, cudaMemcpyHostToDevice) == cudaSuccess;
     if (ok) {
-        k_dense_check<<<(unsigned)n, (unsigned)dense_threads(k), smem>>>(k, dm, db, dout);
+        k_dense_check<<<(unsigned)n, (unsigned)dense_threads(k), smem>>>(k, dm, db, dout, fast_back);
         ok = cudaGetLastError() == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess &&
              cudaMemcpy(out, dout, (size_t)n * k * 8, cudaMemcpyDeviceToHost) == cudaSuccess;
     }
@@ -1482,7 +1486,7 @@ int sb_dense_solve_noalloc(int k, int n, const double* m_rowmajor, const double*
     const unsigned tb = (unsigned)std::min<size_t>((need + 255) / 256, 148 * 8);
     k_dense_transpose<<<tb, 256, 0, st>>>(k, n, m_rowmajor, scratch);
     const size_t smem = std::max<size_t>(16, dense_smem_doubles(k) * sizeof(double));
-    k_dense_check<<<(unsigned)n, (unsigned)dense_threads(k), smem, st>>>(k, scratch, b, out);
+    k_dense_check<<<(unsigned)n, (unsigned)dense_threads(k), smem, st>>>(k, scratch, b, out, 0);
     if (cudaGetLastError() != cudaSuccess) {
         set_err("sb_dense_solve_noalloc: launch failed");
         return -1;

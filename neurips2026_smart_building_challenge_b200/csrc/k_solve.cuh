@@ -383,7 +383,7 @@ __device__ __forceinline__ void dense_update(double* M, int k, int p, int pr, do
     for (; j <= j1; j++) M[(size_t)j * k + p] = dsub(M[(size_t)j * k + p], dmul(f, M[(size_t)j * k + pr]));
 }
 
-__device__ inline void dense_team(double* M, int k, int ttid, int T, int bar) {
+__device__ inline void dense_team(double* M, int k, int ttid, int T, int bar, bool fast_back) {
     const unsigned full = 0xffffffffu;
     const int Tr = 32 * ((k + 31) / 32);   // row owners; threads Tr .. T-1 (if any) are their helpers
     const bool helped = T > Tr, helper = ttid >= Tr;
@@ -468,10 +468,22 @@ __device__ inline void dense_team(double* M, int k, int ttid, int T, int bar) {
             }
         }
     }
-    // back substitution position by position (columns are not permuted): every
-    // pending row forms its product with the newest z in place, the owner of
-    // the position subtracts its products in ascending column order
-    if (!stopped) {
+    // back substitution position by position (columns are not permuted)
+    if (!stopped && fast_back) {
+        // the corrected and folded builds (1e-9 contract): column-oriented --
+        // every pending row subtracts its product with the newest z from its
+        // running sum at once, so the sums are formed in descending column
+        // order (the reference's ascending order only changes the rounding)
+        // and each position costs one division and one barrier
+        double s = !helper && has_row ? M[(size_t)k * k + p] : 0.0;
+        for (int pos = k - 1; pos >= 0; pos--) {
+            if (!helper && has_row && mypos == pos) z[pos] = ddiv(s, M[(size_t)pos * k + p]);
+            team_sync(bar, T);
+            if (!helper && has_row && mypos < pos) s = dsub(s, dmul(M[(size_t)pos * k + p], z[pos]));
+        }
+    } else if (!stopped) {
+        // every pending row forms its product with the newest z in place, the
+        // owner of the position subtracts its products in ascending column order
         for (int pos = k - 1; pos >= 0; pos--) {
             if (!helper && has_row && mypos <= pos && pos + 1 < k)
                 M[(size_t)(pos + 1) * k + p] = dmul(M[(size_t)(pos + 1) * k + p], z[pos + 1]);
@@ -525,7 +537,7 @@ __device__ inline void dense_env(const StepCtx* __restrict__ ctx, int env) {
     }
     __syncthreads();
     const int T = dense_threads(k);
-    if (tid < T) dense_team(dsm, k, tid, T, 1);
+    if (tid < T) dense_team(dsm, k, tid, T, 1, g.corr || g.fold);
     __syncthreads();
     for (int i = tid; i < k; i += blockDim.x) q[i] = dsm[per + kDenseRed + i];
 }
@@ -538,9 +550,11 @@ __global__ void __launch_bounds__(2 * kMaxK) k_dense(const StepCtx* __restrict__
 
 // Test entry of the dense solver: n systems of size k, Mt [n][k][k] the
 // matrices transposed (column-major), b [n][k]; the solutions to out [n][k].
-// One CTA per system, dense_threads(k) threads, the path of k_dense.
+// One CTA per system, dense_threads(k) threads, the path of k_dense (fast_back:
+// the corrected and folded builds' back substitution).
 __global__ void __launch_bounds__(2 * kMaxK) k_dense_check(int k, const double* __restrict__ Mt,
-                                                       const double* __restrict__ b, double* __restrict__ out) {
+                                                       const double* __restrict__ b, double* __restrict__ out,
+                                                       int fast_back) {
     extern __shared__ __align__(16) double dsm[];
     const size_t sys = blockIdx.x;
     const double* A = Mt + sys * k * k;
@@ -548,7 +562,7 @@ __global__ void __launch_bounds__(2 * kMaxK) k_dense_check(int k, const double* 
     const int per = k * (k + 1);
     for (int idx = tid; idx < per; idx += blockDim.x) dsm[idx] = idx < k * k ? A[idx] : b[sys * k + idx - k * k];
     __syncthreads();
-    if (tid < T) dense_team(dsm, k, tid, T, 1);
+    if (tid < T) dense_team(dsm, k, tid, T, 1, fast_back != 0);
     __syncthreads();
     for (int i = tid; i < k; i += blockDim.x) out[sys * k + i] = dsm[per + kDenseRed + i];
 }

@@ -84,3 +84,32 @@ def test_dense_solver_matches_reference(built, k):
         nan = np.isnan(ref)
         np.testing.assert_array_equal(np.isnan(out[i]), nan, err_msg=f"case {i}: NaN positions")
         np.testing.assert_array_equal(out[i][~nan].view(np.uint64), ref[~nan].view(np.uint64), err_msg=f"case {i}")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("k", [1, 5, 33, 81, 128])
+def test_fast_back_substitution_agrees_to_rounding(built, k):
+    """The corrected and folded builds' back substitution (descending column
+    order, one barrier per position) against the exact one: the same pivots
+    and elimination, so the solutions agree to rounding (1e-12 relative on
+    systems whose condition keeps the reordering's effect small); a stopped
+    elimination (singular system) returns the same bits."""
+    import neurips2026_smart_building_challenge_b200 as pkg
+
+    lib = pkg.env_lib()
+    lib.sb_dense_check_mode.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
+                                        ctypes.c_void_p, ctypes.c_int]
+    rng = np.random.default_rng(100 + k)
+    A = rng.standard_normal((4, k, k)) + np.eye(k) * (2.0 * np.sqrt(k))   # well conditioned
+    if k >= 3:
+        A[3, :, k // 2] = 0.0                                                 # the elimination stops
+    b = rng.standard_normal((4, k))
+    A, b = np.ascontiguousarray(A), np.ascontiguousarray(b)
+    exact, fast = np.zeros_like(b), np.zeros_like(b)
+    assert lib.sb_dense_check_mode(k, 4, A.ctypes.data, b.ctypes.data, exact.ctypes.data, 0) == 0
+    assert lib.sb_dense_check_mode(k, 4, A.ctypes.data, b.ctypes.data, fast.ctypes.data, 1) == 0
+    scale = np.maximum(np.abs(exact).max(axis=1, keepdims=True), 1e-300)
+    if k >= 3:
+        np.testing.assert_array_equal(fast[3].view(np.uint64), exact[3].view(np.uint64))
+        fast, exact, scale = fast[:3], exact[:3], scale[:3]
+    assert (np.abs(fast - exact) <= 1e-12 * scale).all()
