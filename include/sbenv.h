@@ -236,12 +236,13 @@ int sb_beta_actions(const float* raw, const unsigned char* mask, float* actions,
  * sides b [n][k]) with the air-side solver of k_dense (partial pivoting in the
  * reference's order); solutions to out [n][k]. Host pointers; synchronous. */
 int sb_dense_check(int k, int n, const double* m_rowmajor, const double* b, double* out);
-/* sb_dense_check with the back substitution of the corrected and folded builds
- * when fast_back != 0 (column-oriented: every pending row subtracts its product
+/* sb_dense_check with the solver of the corrected and folded builds when
+ * tolerant != 0: the same pivoting, fused multiply-add row updates and a
+ * column-oriented back substitution (every pending row subtracts its product
  * with the newest solution value at once, so the sums are formed in descending
- * column order and agree with the reference's to rounding); fast_back = 0 is
- * sb_dense_check. */
-int sb_dense_check_mode(int k, int n, const double* m_rowmajor, const double* b, double* out, int fast_back);
+ * column order); the solutions agree with the reference's to rounding.
+ * tolerant = 0 is sb_dense_check. */
+int sb_dense_check_mode(int k, int n, const double* m_rowmajor, const double* b, double* out, int tolerant);
 /* The same dense solves as sb_dense_check, on device buffers and without
  * allocating anything: for callers that cannot call cudaMalloc, such as a host
  * program whose device memory is owned by another allocator or code that runs

@@ -1445,7 +1445,7 @@ int sb_dense_check(int k, int n, const double* m_rowmajor, const double* b, doub
     return sb_dense_check_mode(k, n, m_rowmajor, b, out, 0);
 }
 
-int sb_dense_check_mode(int k, int n, const double* m_rowmajor, const double* b, double* out, int fast_back) {
+int sb_dense_check_mode(int k, int n, const double* m_rowmajor, const double* b, double* out, int tolerant) {
     if (k < 1 || k > kMaxK || n < 1 || !m_rowmajor || !b || !out) { set_err("sb_dense_check: bad arguments"); return -1; }
     const size_t kk = (size_t)k * k;
     std::vector<double> mt(kk * n);
@@ -1460,7 +1460,7 @@ int sb_dense_check_mode(int k, int n, const double* m_rowmajor, const double* b,
     ok = ok && cudaMemcpy(dm, mt.data(), mt.size() * 8, cudaMemcpyHostToDevice) == cudaSuccess &&
          cudaMemcpy(db, b, (size_t)n * k * 8, cudaMemcpyHostToDevice) == cudaSuccess;
     if (ok) {
-        k_dense_check<<<(unsigned)n, (unsigned)dense_threads(k), smem>>>(k, dm, db, dout, fast_back);
+        k_dense_check<<<(unsigned)n, (unsigned)dense_threads(k), smem>>>(k, dm, db, dout, tolerant);
         ok = cudaGetLastError() == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess &&
              cudaMemcpy(out, dout, (size_t)n * k * 8, cudaMemcpyDeviceToHost) == cudaSuccess;
     }

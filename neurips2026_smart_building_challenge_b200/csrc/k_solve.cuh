@@ -367,7 +367,14 @@ __device__ inline void team_sync(int bar, int T) {
     asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(T) : "memory");
 }
 
-// M[j][p] -= f * M[j][pr] for columns j0 .. j1 (eight at a time, loads first)
+// M[j][p] -= f * M[j][pr] for columns j0 .. j1 (eight at a time, loads first);
+// Fused: one fused multiply-add per element (the corrected and folded builds)
+// instead of the reference's multiply then subtract
+template <bool Fused>
+__device__ __forceinline__ double dense_axpy(double a, double f, double q) {
+    return Fused ? __fma_rn(-f, q, a) : dsub(a, dmul(f, q));
+}
+template <bool Fused>
 __device__ __forceinline__ void dense_update(double* M, int k, int p, int pr, double f, int j0, int j1) {
     int j = j0;
     for (; j + 8 <= j1 + 1; j += 8) {
@@ -378,12 +385,16 @@ __device__ __forceinline__ void dense_update(double* M, int k, int p, int pr, do
             q[u] = M[(size_t)(j + u) * k + pr];
         }
 #pragma unroll
-        for (int u = 0; u < 8; u++) M[(size_t)(j + u) * k + p] = dsub(a[u], dmul(f, q[u]));
+        for (int u = 0; u < 8; u++) M[(size_t)(j + u) * k + p] = dense_axpy<Fused>(a[u], f, q[u]);
     }
-    for (; j <= j1; j++) M[(size_t)j * k + p] = dsub(M[(size_t)j * k + p], dmul(f, M[(size_t)j * k + pr]));
+    for (; j <= j1; j++) M[(size_t)j * k + p] = dense_axpy<Fused>(M[(size_t)j * k + p], f, M[(size_t)j * k + pr]);
 }
 
-__device__ inline void dense_team(double* M, int k, int ttid, int T, int bar, bool fast_back) {
+// Tolerant: the corrected and folded builds (1e-9 contract) -- fused
+// multiply-add updates and the column-oriented back substitution; otherwise
+// the reference's operations in the reference's order.
+template <bool Tolerant>
+__device__ inline void dense_team(double* M, int k, int ttid, int T, int bar) {
     const unsigned full = 0xffffffffu;
     const int Tr = 32 * ((k + 31) / 32);   // row owners; threads Tr .. T-1 (if any) are their helpers
     const bool helped = T > Tr, helper = ttid >= Tr;
@@ -423,8 +434,8 @@ __device__ inline void dense_team(double* M, int k, int ttid, int T, int bar, bo
         // between the owner and its helper when there is one
         if (fr != 0.0) {
             const int mid = helped ? c + 1 + (k - c) / 2 : k + 1;
-            if (!helper) dense_update(M, k, p, prow, fr, c + 1, mid - 1);
-            else dense_update(M, k, p, prow, fr, mid, k);
+            if (!helper) dense_update<Tolerant>(M, k, p, prow, fr, c + 1, mid - 1);
+            else dense_update<Tolerant>(M, k, p, prow, fr, mid, k);
         }
         team_sync(bar, T);
         // the pivot: the best candidate if strictly larger than the diagonal
@@ -461,7 +472,7 @@ __device__ inline void dense_team(double* M, int k, int ttid, int T, int bar, bo
             if (f != 0.0) {
                 fr = f;
                 prow = pr;
-                cv = dsub(mc[p], dmul(f, mc[pr]));
+                cv = dense_axpy<Tolerant>(mc[p], f, mc[pr]);
                 mc[p] = cv;
             } else {
                 cv = mc[p];
@@ -469,7 +480,7 @@ __device__ inline void dense_team(double* M, int k, int ttid, int T, int bar, bo
         }
     }
     // back substitution position by position (columns are not permuted)
-    if (!stopped && fast_back) {
+    if (!stopped && Tolerant) {
         // the corrected and folded builds (1e-9 contract): column-oriented --
         // every pending row subtracts its product with the newest z from its
         // running sum at once, so the sums are formed in descending column
@@ -537,7 +548,10 @@ __device__ inline void dense_env(const StepCtx* __restrict__ ctx, int env) {
     }
     __syncthreads();
     const int T = dense_threads(k);
-    if (tid < T) dense_team(dsm, k, tid, T, 1, g.corr || g.fold);
+    if (tid < T) {
+        if (g.corr || g.fold) dense_team<true>(dsm, k, tid, T, 1);
+        else dense_team<false>(dsm, k, tid, T, 1);
+    }
     __syncthreads();
     for (int i = tid; i < k; i += blockDim.x) q[i] = dsm[per + kDenseRed + i];
 }
@@ -550,11 +564,11 @@ __global__ void __launch_bounds__(2 * kMaxK) k_dense(const StepCtx* __restrict__
 
 // Test entry of the dense solver: n systems of size k, Mt [n][k][k] the
 // matrices transposed (column-major), b [n][k]; the solutions to out [n][k].
-// One CTA per system, dense_threads(k) threads, the path of k_dense (fast_back:
-// the corrected and folded builds' back substitution).
+// One CTA per system, dense_threads(k) threads, the path of k_dense (tolerant:
+// the corrected and folded builds' solver).
 __global__ void __launch_bounds__(2 * kMaxK) k_dense_check(int k, const double* __restrict__ Mt,
                                                        const double* __restrict__ b, double* __restrict__ out,
-                                                       int fast_back) {
+                                                       int tolerant) {
     extern __shared__ __align__(16) double dsm[];
     const size_t sys = blockIdx.x;
     const double* A = Mt + sys * k * k;
@@ -562,7 +576,10 @@ __global__ void __launch_bounds__(2 * kMaxK) k_dense_check(int k, const double* 
     const int per = k * (k + 1);
     for (int idx = tid; idx < per; idx += blockDim.x) dsm[idx] = idx < k * k ? A[idx] : b[sys * k + idx - k * k];
     __syncthreads();
-    if (tid < T) dense_team(dsm, k, tid, T, 1, fast_back != 0);
+    if (tid < T) {
+        if (tolerant) dense_team<true>(dsm, k, tid, T, 1);
+        else dense_team<false>(dsm, k, tid, T, 1);
+    }
     __syncthreads();
     for (int i = tid; i < k; i += blockDim.x) out[sys * k + i] = dsm[per + kDenseRed + i];
 }

@@ -88,12 +88,13 @@ def test_dense_solver_matches_reference(built, k):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("k", [1, 5, 33, 81, 128])
-def test_fast_back_substitution_agrees_to_rounding(built, k):
-    """The corrected and folded builds' back substitution (descending column
-    order, one barrier per position) against the exact one: the same pivots
-    and elimination, so the solutions agree to rounding (1e-12 relative on
-    systems whose condition keeps the reordering's effect small); a stopped
-    elimination (singular system) returns the same bits."""
+def test_tolerant_solver_agrees_to_rounding(built, k):
+    """The corrected and folded builds' dense solver (fused multiply-add row
+    updates, back substitution in descending column order with one barrier
+    per position) against the exact one: the same pivots here, so the
+    solutions agree to rounding (1e-12 relative on systems whose condition
+    keeps the reordering's effect small); a stopped elimination (singular
+    system) returns the right side as eliminated, again to rounding."""
     import neurips2026_smart_building_challenge_b200 as pkg
 
     lib = pkg.env_lib()
@@ -109,7 +110,4 @@ def test_fast_back_substitution_agrees_to_rounding(built, k):
     assert lib.sb_dense_check_mode(k, 4, A.ctypes.data, b.ctypes.data, exact.ctypes.data, 0) == 0
     assert lib.sb_dense_check_mode(k, 4, A.ctypes.data, b.ctypes.data, fast.ctypes.data, 1) == 0
     scale = np.maximum(np.abs(exact).max(axis=1, keepdims=True), 1e-300)
-    if k >= 3:
-        np.testing.assert_array_equal(fast[3].view(np.uint64), exact[3].view(np.uint64))
-        fast, exact, scale = fast[:3], exact[:3], scale[:3]
     assert (np.abs(fast - exact) <= 1e-12 * scale).all()
