@@ -582,7 +582,7 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
         const int rs = solve_ring_stages(h.n, B, smem_cap);
         gd.slab_envs = B;
         E.smem_solve = std::max(E.smem_solve, solve_smem_bytes(h.n, B, rs));
-        std::string se = build_sweeps(h, rs);
+        std::string se = build_sweeps(h, rs, fast);
         if (se.empty() && fold) se = build_fold(h);
         if (!se.empty()) { set_err("group %d: %s", c, se.c_str()); return false; }
         gd.fold = fold ? 1 : 0;
@@ -619,9 +619,11 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
                 s.warp_stages[w] = hsw.warp_stages[w];
             }
             s.ring_stages = (uint32_t)hsw.ring_stages;
+            s.recip = 0;
         };
         put_sweep(h.fwd, gd.fwd);
         put_sweep(h.bwd, gd.bwd);
+        gd.bwd.recip = fast ? 1u : 0u;
         gd.sn_p = E.arena.upload(h.sn_p, ok); gd.sn_pos = E.arena.upload(h.sn_pos, ok);
         gd.sn_x = E.arena.upload(h.sn_x, ok);
         gd.ap_rp = E.arena.upload(h.ap_rp, ok); gd.ap_col = E.arena.upload(h.ap_col, ok);

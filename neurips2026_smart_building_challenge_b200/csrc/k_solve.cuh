@@ -139,8 +139,14 @@ __device__ __forceinline__ void prefetch_lines(const uint8_t* p, uint32_t bytes,
 }
 
 // The rounds of one block (BW: the U sweep, rows descending, each finished
-// by a division), after its header has been checked and its waits acquired.
-template <bool BW>
+// by a division -- Recip: a multiplication by the stored reciprocal of the
+// diagonal, the corrected and folded builds), after its header has been
+// checked and its waits acquired.
+template <bool BW, bool Recip>
+__device__ __forceinline__ double block_finish(double a, double dg) {
+    return BW ? (Recip ? dmul(a, dg) : ddiv(a, dg)) : a;
+}
+template <bool BW, bool Recip>
 __device__ inline void block_rounds(const SolveShared& sh, const uint8_t* __restrict__ vals, uint32_t first,
                                     uint32_t size, uint64_t pubm, double* __restrict__ xe, bool owns, uint32_t fin) {
     const unsigned full = 0xffffffffu;
@@ -176,19 +182,19 @@ __device__ inline void block_rounds(const SolveShared& sh, const uint8_t* __rest
         }
         // the four rows in turn: group k's row is final at stage k
         double xm;
-        const double f0 = BW ? ddiv(a, dg) : a;
+        const double f0 = block_finish<BW, Recip>(a, dg);
         xm = f0;
         const double x0 = __shfl_sync(full, f0, e);
         if (g > 0) a = dsub(a, dmul(t0, x0));
-        const double f1 = BW ? ddiv(a, dg) : a;
+        const double f1 = block_finish<BW, Recip>(a, dg);
         if (g == 1) xm = f1;
         const double x1 = __shfl_sync(full, f1, 8 | e);
         if (g > 1) a = dsub(a, dmul(t1, x1));
-        const double f2 = BW ? ddiv(a, dg) : a;
+        const double f2 = block_finish<BW, Recip>(a, dg);
         if (g == 2) xm = f2;
         const double x2 = __shfl_sync(full, f2, 16 | e);
         if (g > 2) a = dsub(a, dmul(t2, x2));
-        if (g == 3) xm = BW ? ddiv(a, dg) : a;
+        if (g == 3) xm = block_finish<BW, Recip>(a, dg);
         // the round's rows are final: store (later rounds read them), publish
         // those other warps read
         if (mine && owns) xe[row] = xm;
@@ -212,7 +218,8 @@ __device__ inline void block_rounds(const SolveShared& sh, const uint8_t* __rest
 // lanes by a shuffle (group 3's value is only stored). Returns false on an
 // error (reported in sh.abort).
 __device__ inline bool run_block(const SolveShared& sh, const StageRing& rg, uint32_t hq, const uint8_t* sw_base,
-                                 uint32_t sw_bytes, double* __restrict__ xe, bool owns, uint32_t n, uint32_t fin) {
+                                 uint32_t sw_bytes, double* __restrict__ xe, bool owns, uint32_t n, uint32_t fin,
+                                 bool recip) {
     const int lane = threadIdx.x & 31;
     const BlockRecord* b = reinterpret_cast<const BlockRecord*>(rg.ring + (size_t)rg.hslot * kStageBytes + hq * kRecordBytes);
     const uint32_t first = b->first, size = b->size, bw = b->backward, nw = b->nwait, voff = b->values;
@@ -227,8 +234,9 @@ __device__ inline bool run_block(const SolveShared& sh, const StageRing& rg, uin
     const uint8_t* __restrict__ vals = sw_base + voff;
     prefetch_lines(vals, min(vbytes, 2048u), lane);
     if (nw && !wait_rows(sh, b->wait, min(nw, (uint32_t)kCtrlWaits), n, fin)) return false;
-    if (bw) block_rounds<true>(sh, vals, first, size, pubm, xe, owns, fin);
-    else block_rounds<false>(sh, vals, first, size, pubm, xe, owns, fin);
+    if (bw && recip) block_rounds<true, true>(sh, vals, first, size, pubm, xe, owns, fin);
+    else if (bw) block_rounds<true, false>(sh, vals, first, size, pubm, xe, owns, fin);
+    else block_rounds<false, false>(sh, vals, first, size, pubm, xe, owns, fin);
     return true;
 }
 
@@ -284,7 +292,10 @@ __device__ inline void run_sweep(const SolveShared& sh, const Sweep& sw, int B, 
             const ControlRecord* c = reinterpret_cast<const ControlRecord*>(rp);
             const uint32_t cf = c->flags;
             if (cf & kCtrlBlock) {
-                if (!run_block(sh, rg, q, sw.stream, sw.total_bytes, xe, owns, un, fin)) { err = kErrBadBundle; break; }
+                if (!run_block(sh, rg, q, sw.stream, sw.total_bytes, xe, owns, un, fin, sw.recip != 0)) {
+                    err = kErrBadBundle;
+                    break;
+                }
                 ctrl = true;   // a block is followed by a control or block record
             } else {
                 const uint32_t gf = c->gflags[g];
@@ -292,7 +303,8 @@ __device__ inline void run_sweep(const SolveShared& sh, const Sweep& sw, int B, 
                 const uint32_t nw = c->nwait;
                 const bool ending = (gf & kGSwitch) && row < un;
                 if (cf & kCtrlDivide) {
-                    const double dq = ddiv(acc, c->diag[g]);
+                    // the diagonal, or its reciprocal (corrected and folded builds)
+                    const double dq = sw.recip ? dmul(acc, c->diag[g]) : ddiv(acc, c->diag[g]);
                     if (gf & kGDivide) acc = dq;
                 }
                 if (ending && owns) xe[row] = acc;   // final value, partial sum, or paused row

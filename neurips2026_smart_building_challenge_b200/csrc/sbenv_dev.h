@@ -171,6 +171,7 @@ struct Sweep {
     uint32_t warp_off[kSweepWarps];        // stage index where warp w's stream starts
     uint32_t warp_stages[kSweepWarps];     // stages in warp w's stream
     uint32_t ring_stages;                  // ring depth the streams were laid out for
+    uint32_t recip;                        // 1: U-sweep records hold 1 / diagonal (multiply, not divide)
 };
 
 // Geometry + solver tables of one group and the state of its envs.

@@ -534,9 +534,16 @@ int solve_ring_stages(int n, int B, size_t smem_cap) {
     return 0;
 }
 
-std::string build_sweeps(HostGroup& g, int ring_stages) {
+std::string build_sweeps(HostGroup& g, int ring_stages, bool recip) {
     std::string e = build_sweep(g.n, g.lt, false, g.udiag, ring_stages, g.fwd);
-    if (e.empty()) e = build_sweep(g.n, g.ut, true, g.udiag, ring_stages, g.bwd);
+    if (e.empty()) {
+        // the corrected and folded builds finish U rows with a multiplication
+        // by the diagonal's reciprocal (rounded once, here) instead of a division
+        std::vector<double> d = g.udiag;
+        if (recip)
+            for (double& x : d) x = 1.0 / x;
+        e = build_sweep(g.n, g.ut, true, d, ring_stages, g.bwd);
+    }
     return e;
 }
 
