@@ -534,13 +534,37 @@ int solve_ring_stages(int n, int B, size_t smem_cap) {
     return 0;
 }
 
-std::string build_sweeps(HostGroup& g, int ring_stages, bool recip) {
-    std::string e = build_sweep(g.n, g.lt, false, g.udiag, ring_stages, g.fwd);
+// The terms of every row sorted by the depth of their source row in the
+// sweep's dependency graph (rows with no terms: depth 0; a row: one more than
+// its deepest source), stable otherwise: a row can then start with the terms
+// whose sources finish first. Changes the summation order, so only for the
+// builds held to a tolerance.
+static std::vector<std::vector<std::pair<int, double>>> terms_by_depth(
+    const std::vector<std::vector<std::pair<int, double>>>& t, bool backward) {
+    const int n = (int)t.size();
+    std::vector<int> depth(n, 0);
+    for (int p = 0; p < n; p++) {
+        const int i = backward ? n - 1 - p : p;
+        int d = 0;
+        for (const auto& x : t[i]) d = std::max(d, depth[x.first] + 1);
+        depth[i] = d;
+    }
+    auto out = t;
+    for (auto& r : out)
+        std::stable_sort(r.begin(), r.end(), [&](const std::pair<int, double>& a, const std::pair<int, double>& b) {
+            return depth[a.first] < depth[b.first];
+        });
+    return out;
+}
+
+std::string build_sweeps(HostGroup& g, int ring_stages, bool tolerant) {
+    // the corrected and folded builds: the L sweep's terms by source depth, and
+    // U rows finished with a multiplication by the diagonal's reciprocal
+    // (rounded once, here) instead of a division
+    std::string e = build_sweep(g.n, tolerant ? terms_by_depth(g.lt, false) : g.lt, false, g.udiag, ring_stages, g.fwd);
     if (e.empty()) {
-        // the corrected and folded builds finish U rows with a multiplication
-        // by the diagonal's reciprocal (rounded once, here) instead of a division
         std::vector<double> d = g.udiag;
-        if (recip)
+        if (tolerant)
             for (double& x : d) x = 1.0 / x;
         e = build_sweep(g.n, g.ut, true, d, ring_stages, g.bwd);
     }

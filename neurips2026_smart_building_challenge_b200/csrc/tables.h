@@ -67,9 +67,11 @@ std::string build_group(const sbb::Reader& b, HostGroup& g);
 // n-cell field leaves room for within smem_cap bytes; 0 if not even kStagesMin.
 int solve_ring_stages(int n, int B, size_t smem_cap);
 // Builds the group's L and U sweep programs for a per-warp ring of ring_stages.
-// recip: the U sweep's diagonal entries hold 1 / diagonal (the corrected and
-// folded builds multiply; the exact build divides)
-std::string build_sweeps(HostGroup& g, int ring_stages, bool recip = false);
+// tolerant (the corrected and folded builds): the L sweep's terms of every row
+// ordered by the depth of their source rows instead of the reference's push
+// order, and the U sweep's diagonal entries hold 1 / diagonal (multiplied,
+// not divided); the exact build keeps the reference's order and divisions
+std::string build_sweeps(HostGroup& g, int ring_stages, bool tolerant = false);
 // Builds the folded air side's Z = L^-1 applied and R = sensed U^-1 (row order).
 std::string build_fold(HostGroup& g);
 // Builds the per-scenario tables (needs the group's position maps).
