@@ -97,6 +97,8 @@ def parse_args():
     ap.add_argument("--solve", default="corrected", choices=sorted(SOLVE_NOTE),
                     help="exact: the reference core's two triangular solves, bit for bit; corrected / folded: "
                          "one L/U pair per step (1e-9 per-step contract)")
+    ap.add_argument("--wide", type=int, default=-1, choices=[-1, 0, 1],
+                    help="first solve on 32-env tiles in L1/L2 (1), on shared-memory slabs (0), or by batch size (-1)")
     ap.add_argument("--month", action="store_true",
                     help="configuration 1: one building for its whole month, GPU and the reference core (1 thread)")
     args = ap.parse_args()
@@ -441,7 +443,7 @@ def run_ours(args) -> None:
     # the other builds first (value and per-kernel times only), then the stated one
     for solve in others + [args.solve]:
         env = SmartBuildingsVec(n, blob_dir=str(d), groups=groups, device=f"cuda:{local}", env_offset=start,
-                                **SOLVE_KW[solve])
+                                wide=args.wide, **SOLVE_KW[solve])
         env.reset()
         pool = torch.from_numpy(pool_np).to(env.device)
         if solve != args.solve:
@@ -457,6 +459,9 @@ def run_ours(args) -> None:
     ms_per_step = ms_total / args.steps
     value = total * args.steps / (ms_total / 1e3)
     status = env.status()
+    # slabs hold at most 8 envs, wide tiles 32 (sb_shape out[6]: the first solve's CTAs)
+    first_solve = ("wide: 32-env tiles in L1/L2 (k_wide0)" if env.shape[6] * 8 < n
+                   else "slabs: up to 8 envs in shared memory (k_solve<0>)")
 
     # roofline of the solve (HBM, the north star's bound) and its fp64 issue share
     k_ms = kernel_times(env, pool, flush, torch)
@@ -518,6 +523,7 @@ def run_ours(args) -> None:
     if rank == 0:
         config = bench_config(args, world)
         config["solve_note"] = SOLVE_NOTE[args.solve]
+        config["first_solve"] = first_solve
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
                 "scaling": "strong" if args.strong else "weak",
@@ -540,7 +546,7 @@ def run_profile(args) -> None:
     d = workload_dir(args.workload, ROOT / ".sbb_cache" / "bench_rank0")
     n = args.envs
     env = SmartBuildingsVec(n, blob_dir=str(d), groups=WORKLOADS[args.workload]["groups"], device="cuda:0",
-                            **SOLVE_KW[args.solve])
+                            wide=args.wide, **SOLVE_KW[args.solve])
     env.reset()
     pool = torch.from_numpy(action_pool(n, 2, seed=1234)).to(env.device)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=env.device)

@@ -157,7 +157,12 @@ void dict_set_str(Dict* d, const char* key, const char* value);
  * systems and then its phase-1 work (the correction or the second solve) on a
  * stream of its own, 2 its first solve too, 0 every part on one stream in
  * turn; default -1: 2 when the first solve's slabs are more than one wave of
- * the GPU's SMs, else 1. Returns NULL on error. */
+ * the GPU's SMs, else 1. wide (scheduling only, results unchanged): 1 runs
+ * the first solve on tiles of 32 envs whose vectors stay in L1/L2 (level
+ * programs streamed to 16 solver warps, per-row ready counts), 0 on slabs of
+ * up to 8 envs held in shared memory (per-warp programs, ready flags);
+ * default -1: 1 when the slabs would be three or more waves of the GPU's SMs.
+ * Returns NULL on error. */
 Env* puf_vec_create(int n, Dict* kwargs, obs_t* observations, float* actions, float* rewards,
                     float* terminals);
 void puf_bind_stream(sb_stream_t stream);
@@ -200,7 +205,8 @@ int sb_device_status(void);
  * hang; on = 0 turns it off (and restores the limit). Synchronises. 0 or -1. */
 int sb_test_stall(int on, unsigned int spin_limit);
 /* Shape of the loaded batch: out[8] = {n_env, n_scenarios, n_groups, obs_len_max,
- * n_cont_max, n_disc_max, slab_ctas, kernels_per_step}. */
+ * n_cont_max, n_disc_max, first-solve CTAs (slabs, or 32-env tiles with the wide
+ * solve), kernels_per_step}. */
 void sb_shape(int* out);
 /* Per-env observation length / scenario index (host arrays of n). */
 void sb_env_info(int* obs_len, int* scenario);
@@ -315,6 +321,21 @@ int sb_sweep_warps(void);
  * term records, row segments, waits, published rows and partial sums,
  * modelled cycles, stream bytes, dense block records, rows they finish}. */
 int sb_sweep_stats(const char* blob_path, int sweep, int ring_stages, double* out);
+/* Host-only: the wide solve's level program of the blob's L (sweep 0) or U
+ * (sweep 1) sweep; the U program's stages and ready counts continue the L
+ * program's. info[8] receives {levels, segments, chunks, partial segments,
+ * terms, modelled cycles, bytes of all level blocks, largest level block};
+ * with lev_off (levels + 1 uint32: each level block's byte offset) and blocks
+ * (the level blocks: two int32 tables of sb_wide_warps() + 1 entries --
+ * first segment and first wait of each warp -- padded to 144 bytes, the
+ * waits (uint32 row << 16 | count, padded to 16 bytes), 16-byte segments
+ * {row, first chunk, chunks, finish | count << 16}, 48-byte chunks {four
+ * f64 values, four uint32 byte offsets}) both non-null the program is copied
+ * out and 0 returned, else 1; -1 on error. No counterpart in the reference
+ * (its CPU core has no schedule). */
+int sb_wide_schedule(const char* blob_path, int sweep, int64_t* info, uint32_t* lev_off, uint8_t* blocks);
+/* Solver warps of a wide-solve CTA (level program columns). */
+int sb_wide_warps(void);
 
 #ifdef __cplusplus
 }

@@ -40,7 +40,8 @@ ENV_SYMBOLS = ["sb_dict_new", "sb_dict_free", "dict_find", "dict_set", "dict_set
                "sb_env_info", "sb_get_temp", "sb_get_mass", "sb_get_reward_f64", "sb_kernels_per_step",
                "sb_solve_schedule", "sb_sweep_warps", "sb_sweep_stats", "sb_debug_state", "sb_step_timed", "sb_solve_bytes",
                "sb_dense_check", "sb_dense_check_mode", "sb_beta_actions", "sb_snapshot_write", "sb_dense_solve_noalloc",
-               "sb_episode_options", "sb_solve_flops", "sb_fp64_peak", "sb_scenario_stats", "sb_test_stall"]
+               "sb_episode_options", "sb_solve_flops", "sb_fp64_peak", "sb_scenario_stats", "sb_test_stall",
+               "sb_wide_schedule", "sb_wide_warps"]
 GEN_SYMBOLS = ["sbgen_preset", "sbgen_write", "sbgen_factor_stats"]
 
 

@@ -61,7 +61,7 @@ def build_env(verbose: bool = False, force: bool = False) -> Path:
         return out
     BUILD.mkdir(exist_ok=True)
     host_objs = []
-    for name in ["tables.cpp", "sweep_sched.cpp", "sbb.cpp"]:
+    for name in ["tables.cpp", "sweep_sched.cpp", "wide_sched.cpp", "sbb.cpp"]:
         obj = BUILD / (name + ".o")
         _run([CXX, "-O2", "-std=c++17", "-fPIC", "-ffp-contract=off", "-Wall", "-Wextra",
               f"-I{INCLUDE}", f"-I{CSRC}", "-c", str(CSRC / name), "-o", str(obj)], verbose)

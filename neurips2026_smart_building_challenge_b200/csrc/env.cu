@@ -37,8 +37,10 @@
 #include "k_rng.cuh"
 #include "k_solve.cuh"
 #include "k_correct.cuh"
+#include "k_wide.cuh"
 #include "k_policy.cuh"
 #include "tables.h"
+#include "wide_sched.h"
 
 using namespace sbenv;
 
@@ -103,6 +105,11 @@ struct Engine {
     std::vector<ScnDev> sd;
     std::vector<EnvIndex> ei;
     std::vector<SlabDesc> slabs;
+    // the wide solve's tiles (kwarg wide): phase 0 on k_wide0
+    bool wide = false;
+    std::vector<WideTile> wtiles;
+    WideTile* d_wtiles1 = nullptr;    // the tiles in pcls order
+    size_t smem_wide = 16;            // k_wide0 (wide_smem_bytes of the largest group)
     std::vector<CorrTile> ctiles;   // k_correct's tiles (corrected build)
     CorrTile* d_ctiles = nullptr;
     int solve_mode = 0;             // 0 exact, 1 folded, 2 corrected
@@ -131,7 +138,7 @@ struct Engine {
     // phase-1 work (k_correct tiles or k_solve<1> slabs) on a stream of their
     // own, so a class's phase 1 starts as soon as its own dense systems are
     // solved; the groups without an air side (dense = -1) run on hi
-    struct PhaseClass { int dense, tile0, ntiles, slab0, nslabs, env0, nenv; };   // env0: into dense_order
+    struct PhaseClass { int dense, tile0, ntiles, slab0, nslabs, env0, nenv, wtile0, nwtiles; };   // env0: into dense_order
     std::vector<PhaseClass> pcls;
     SlabDesc* d_slabs1 = nullptr;         // the slabs in pcls order (k_solve<1>)
     std::vector<cudaStream_t> cls_st;     // one per dense class (empty: all on hi)
@@ -288,6 +295,25 @@ cudaError_t launch_phase1(Engine& E, cudaStream_t st, const Engine::PhaseClass* 
     return cudaGetLastError();
 }
 
+// Phase 0 (forcing, first L/U solve, sensed right side, y to the field): the
+// wide solve's tiles (k_wide0) or the shared-memory slabs (k_solve<0>); all of
+// it, or one phase class's share.
+cudaError_t launch_phase0(Engine& E, cudaStream_t st, const Engine::PhaseClass* pc = nullptr) {
+    if (E.wide) {
+        const unsigned n = pc ? (unsigned)pc->nwtiles : (unsigned)E.wtiles.size();
+        const WideTile* t = E.d_wtiles1 + (pc ? pc->wtile0 : 0);
+        if (n && E.solve_mode == 0) k_wide0<false><<<n, kWideThreads, E.smem_wide, st>>>(E.d_ctx, t);
+        else if (n) k_wide0<true><<<n, kWideThreads, E.smem_wide, st>>>(E.d_ctx, t);
+    } else {
+        const unsigned n = pc ? (unsigned)pc->nslabs : (unsigned)E.slabs.size();
+        if (n) k_solve<0><<<n, kSolveThreads, E.smem_solve, st>>>(E.d_ctx, pc ? E.d_slabs1 + pc->slab0 : E.d_slabs);
+    }
+    return cudaGetLastError();
+}
+
+// Phase-0 launch units of one class (wide tiles or slabs).
+inline int phase0_units(const Engine& E, const Engine::PhaseClass& pc) { return E.wide ? pc.nwtiles : pc.nslabs; }
+
 // Events of one step for sb_step_timed: per phase class the ends of its
 // k_pre, phase 0, dense systems and phase 1 (recorded on the stream that ran
 // them; the same moment for every class where the part is one launch), and
@@ -328,7 +354,6 @@ cudaError_t enqueue_step(Engine& E, StepMarks* mk) {
     };
     const bool classes = !E.cls_st.empty();
     const bool split0 = classes && E.split_phase0;
-    const unsigned all_slabs = (unsigned)E.slabs.size();
     if (mk) SB_EQ(cudaEventRecord(mk->start, E.stream));
     if (!split0) {
         k_pre<<<(unsigned)E.n_env, 128, E.smem_pre, E.stream>>>(E.d_ctx, -1);
@@ -338,8 +363,7 @@ cudaError_t enqueue_step(Engine& E, StepMarks* mk) {
     SB_EQ(cudaEventRecord(E.ev_fork, E.stream));
     SB_EQ(cudaStreamWaitEvent(E.hi, E.ev_fork, 0));
     if (!classes) {
-        k_solve<0><<<all_slabs, kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
-        SB_EQ(cudaGetLastError());
+        SB_EQ(launch_phase0(E, E.hi));
         SB_EQ(launch_rng(E, E.hi, true));
         SB_EQ(mark_all(&StepMarks::p0, E.hi));
         SB_EQ(launch_dense(E, E.hi));
@@ -353,9 +377,8 @@ cudaError_t enqueue_step(Engine& E, StepMarks* mk) {
     } else {
         bool rng = false;
         if (!split0) {
-            // every slab in one wave: phase 0 in one launch, then the classes
-            k_solve<0><<<all_slabs, kSolveThreads, E.smem_solve, E.hi>>>(E.d_ctx, E.d_slabs);
-            SB_EQ(cudaGetLastError());
+            // every slab (tile) in one wave: phase 0 in one launch, then the classes
+            SB_EQ(launch_phase0(E, E.hi));
             SB_EQ(launch_rng(E, E.hi, true));
             SB_EQ(mark_all(&StepMarks::p0, E.hi));
             rng = true;
@@ -371,10 +394,8 @@ cudaError_t enqueue_step(Engine& E, StepMarks* mk) {
                     SB_EQ(cudaGetLastError());
                 }
                 SB_EQ(mark(&StepMarks::pre, i, st));
-                if (pc.nslabs > 0) {
-                    k_solve<0><<<(unsigned)pc.nslabs, kSolveThreads, E.smem_solve, st>>>(E.d_ctx,
-                                                                                         E.d_slabs1 + pc.slab0);
-                    SB_EQ(cudaGetLastError());
+                if (phase0_units(E, pc) > 0) {
+                    SB_EQ(launch_phase0(E, st, &pc));
                     if (!rng) {
                         // beside the first (heaviest) class's phase 0
                         SB_EQ(launch_rng(E, st, true));
@@ -412,7 +433,7 @@ int kernels_per_step(const Engine& E) {
     const bool split0 = E.split_phase0;
     if (!split0) n += 2;   // k_pre, phase 0
     for (const Engine::PhaseClass& pc : E.pcls) {
-        if (split0) n += (pc.nenv > 0 ? 1 : 0) + (pc.nslabs > 0 ? 1 : 0);
+        if (split0) n += (pc.nenv > 0 ? 1 : 0) + (phase0_units(E, pc) > 0 ? 1 : 0);
         n += (E.solve_mode == 2 ? pc.ntiles : pc.nslabs) > 0 ? 1 : 0;
         n += pc.nenv > 0 ? 1 : 0;
     }
@@ -461,6 +482,9 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     // per-env draws (desync cut, random-start stream) follow the global index
     const long long env_offset = std::max(0LL, (long long)kw_num(kw, "env_offset", 0.0));
     E.overlap = (int)kw_num(kw, "overlap", -1.0);
+    // phase 0 on the wide solve (1) or on shared-memory slabs (0); -1
+    // (default): decided below from the batch's size
+    const int wide_kw = (int)kw_num(kw, "wide", -1.0);
     E.rew_norm = kw_num(kw, "rew_norm", 0.0) != 0.0;
     E.rew_center = !E.rew_norm && kw_num(kw, "rew_center", 0.0) != 0.0;
     {
@@ -572,6 +596,15 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     }
     std::vector<int> bsel(NG);
     for (int c = 0; c < NG; c++) bsel[c] = width(c, bwave);
+    // the wide solve pays off once the slabs are several waves of the GPU: a
+    // slab holds at most eight envs per SM, two wide tiles 64, but a tile's
+    // sweeps take a few times a slab's
+    {
+        long slabs = 0;
+        for (int c = 0; c < NG; c++) slabs += (E.gd[c].n_env + bsel[c] - 1) / bsel[c];
+        const long waves = (slabs + sm_budget - 1) / std::max<long>(1, sm_budget);
+        E.wide = wide_kw < 0 ? waves >= 3 : wide_kw != 0;
+    }
     for (int c = 0; c < NG; c++) {
         HostGroup& h = E.hg[c];
         GroupDev& gd = E.gd[c];
@@ -646,6 +679,32 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
         gd.T = E.arena.zeros<double>((size_t)gd.n_env * h.ncv, ok);
         gd.M = E.arena.zeros<double>((size_t)gd.n_env * h.n, ok);
         for (int e0 = 0; e0 < gd.n_env; e0 += B) E.slabs.push_back({c, gd.env0 + e0, std::min(B, gd.n_env - e0), 0});
+        if (E.wide) {
+            // level programs in the reference's push order for every build; the
+            // U rows' diagonal (exact) or its reciprocal, rounded once here
+            HostWide wf, wb;
+            WideFlags wfl(h.n);
+            std::string we = build_wide(h.n, h.lt, false, 0, wfl, wf);
+            if (we.empty()) we = build_wide(h.n, h.ut, true, wf.nlev, wfl, wb);
+            if (!we.empty()) { set_err("group %d: %s", c, we.c_str()); return false; }
+            auto put_wide = [&](const HostWide& hw, WideSweep& s) {
+                s.blocks = E.arena.upload(hw.blocks, ok);
+                s.lev_off = E.arena.upload(hw.lev_off, ok);
+                s.nlev = hw.nlev;
+            };
+            put_wide(wf, gd.wfwd);
+            put_wide(wb, gd.wbwd);
+            std::vector<double> wd = h.udiag;
+            if (fast)
+                for (double& x : wd) x = 1.0 / x;
+            gd.wdiag = E.arena.upload(wd, ok);
+            const int ntile = (gd.n_env + kWideEnvs - 1) / kWideEnvs;
+            // scratch rows n of every tile stay zero (the padding terms' source)
+            gd.X = E.arena.zeros<double>((size_t)ntile * (h.n + 1) * kWideEnvs, ok);
+            E.smem_wide = std::max(E.smem_wide, wide_smem_bytes(h.n));
+            for (int t = 0; t < ntile; t++)
+                E.wtiles.push_back({c, gd.env0 + t * kWideEnvs, std::min(kWideEnvs, gd.n_env - t * kWideEnvs), t});
+        }
         E.max_ncv = std::max(E.max_ncv, h.ncv);
         E.smem_pre = std::max(E.smem_pre, sizeof(double) * (size_t)(L.nd + 2 * nz_max + nv_max + 2 * na_max + 2 * k_max) +
                                               sizeof(int32_t) * (size_t)L.ni);
@@ -852,9 +911,10 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     {
         std::vector<CorrTile> tiles;
         std::vector<SlabDesc> slabs1;
+        std::vector<WideTile> wtiles1;
         int env_end = 0;
         auto add = [&](int dense, int k) {
-            Engine::PhaseClass pc{dense, (int)tiles.size(), 0, (int)slabs1.size(), 0, 0, 0};
+            Engine::PhaseClass pc{dense, (int)tiles.size(), 0, (int)slabs1.size(), 0, 0, 0, (int)wtiles1.size(), 0};
             if (dense >= 0) {
                 pc.env0 = E.dense_cls[dense].first;
                 pc.nenv = E.dense_cls[dense].count;
@@ -869,12 +929,19 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
                 if (E.gd[sl.group].k == k) slabs1.push_back(sl);
             pc.ntiles = (int)tiles.size() - pc.tile0;
             pc.nslabs = (int)slabs1.size() - pc.slab0;
+            for (const WideTile& t : E.wtiles)
+                if (E.gd[t.group].k == k) wtiles1.push_back(t);
+            pc.nwtiles = (int)wtiles1.size() - pc.wtile0;
             if (dense >= 0 || pc.ntiles > 0 || pc.nslabs > 0 || pc.nenv > 0) E.pcls.push_back(pc);
         };
         for (size_t c = 0; c < E.dense_cls.size(); c++) add((int)c, E.dense_cls[c].k);
         add(-1, 0);
         E.ctiles = tiles;
         E.d_slabs1 = E.arena.upload(slabs1, ok);
+        if (E.wide) {
+            if (wtiles1.size() != E.wtiles.size()) { set_err("wide tiles: a group outside every phase class"); return false; }
+            E.d_wtiles1 = E.arena.upload(wtiles1, ok);
+        }
     }
     E.d_slabs = E.arena.upload(E.slabs, ok);
     if (!E.ctiles.empty()) E.d_ctiles = E.arena.upload(E.ctiles, ok);
@@ -917,6 +984,16 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     CK(cudaFuncSetAttribute(k_solve<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_solve));
     CK(cudaFuncSetAttribute(k_solve<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_solve));
     CK(cudaFuncSetAttribute(k_dense, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_dense));
+    // the wide solve keeps its vectors in L1: no more shared memory than two
+    // CTAs' stage rings and ready counts, the rest of the SM's 256 KB is L1
+    if (E.wide) {
+        if (E.smem_wide > smem_cap) { set_err("wide solve needs %zu B of shared memory", E.smem_wide); return false; }
+        const int pct = (int)std::min<size_t>(100, (100 * (2 * E.smem_wide + 2048) + smem_cap - 1) / smem_cap);
+        for (const void* f : {(const void*)k_wide0<false>, (const void*)k_wide0<true>}) {
+            CK(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_wide));
+            CK(cudaFuncSetAttribute(f, cudaFuncAttributePreferredSharedMemoryCarveout, pct));
+        }
+    }
     CK(cudaFuncSetAttribute(k_pre, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_pre));
     CK(cudaFuncSetAttribute(k_post, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_post));
     CK(cudaFuncSetAttribute(k_reset, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_post));
@@ -945,7 +1022,9 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     if (E.dense_cls.size() > 1 && E.overlap != 0) {
         int sms = 0;
         CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0));
-        E.split_phase0 = E.overlap == 2 || (E.overlap < 0 && (int)E.slabs.size() > sms);
+        // more than one wave: of slabs (one per SM) or of wide tiles (two per SM)
+        const int units = E.wide ? (int)E.wtiles.size() : (int)E.slabs.size();
+        E.split_phase0 = E.overlap == 2 || (E.overlap < 0 && units > (E.wide ? 2 * sms : sms));
         int least = 0, greatest = 0;
         CK(cudaDeviceGetStreamPriorityRange(&least, &greatest));
         E.cls_st.assign(E.dense_cls.size(), nullptr);
@@ -1363,7 +1442,7 @@ void sb_shape(int* out) {
         out[4] = std::max(out[4], s.n_cont);
         out[5] = std::max(out[5], s.n_disc);
     }
-    out[6] = (int)E.slabs.size();
+    out[6] = E.wide ? (int)E.wtiles.size() : (int)E.slabs.size();
     out[7] = kernels_per_step(E);
 }
 
@@ -1776,6 +1855,40 @@ int sb_solve_schedule(const char* blob_path, int sweep, int ring_stages, uint8_t
 }
 
 int sb_sweep_warps(void) { return kSweepWarps; }
+
+int sb_wide_schedule(const char* blob_path, int sweep, int64_t* info, uint32_t* lev_off, uint8_t* blocks) {
+    HostGroup g;
+    sbb::Reader r;
+    std::string e = r.open(blob_path ? blob_path : "");
+    if (e.empty()) e = build_group(r, g);
+    if (e.empty() && sweep != 0 && sweep != 1) e = "sweep must be 0 (L) or 1 (U)";
+    HostWide w;
+    if (e.empty()) {
+        // the L sweep's program, then (sweep 1) the U sweep's, which continues
+        // the rows' ready counts and stage numbering
+        WideFlags fl(g.n);
+        e = build_wide(g.n, g.lt, false, 0, fl, w);
+        if (e.empty() && sweep == 1) {
+            const int nl = w.nlev;
+            e = build_wide(g.n, g.ut, true, nl, fl, w);
+        }
+    }
+    if (!e.empty() || !info) { set_err("%s", e.empty() ? "null info" : e.c_str()); return -1; }
+    info[0] = w.nlev;
+    info[1] = w.segs;
+    info[2] = w.chunks;
+    info[3] = w.partial;
+    info[4] = w.terms;
+    info[5] = (int64_t)w.sim_cycles;
+    info[6] = (int64_t)w.blocks.size();
+    info[7] = w.max_bytes;
+    if (!lev_off || !blocks) return 1;
+    memcpy(lev_off, w.lev_off.data(), w.lev_off.size() * sizeof(uint32_t));
+    memcpy(blocks, w.blocks.data(), w.blocks.size());
+    return 0;
+}
+
+int sb_wide_warps(void) { return kWideWarps; }
 
 int sb_sweep_stats(const char* blob_path, int sweep, int ring_stages, double* out) {
     HostGroup g;

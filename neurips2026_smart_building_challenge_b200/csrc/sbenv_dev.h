@@ -174,6 +174,62 @@ struct Sweep {
     uint32_t recip;                        // 1: U-sweep records hold 1 / diagonal (multiply, not divide)
 };
 
+// Wide solve (level programs, built on the host by build_wide,
+// wide_sched.cpp): one CTA holds a tile of up to kWideEnvs envs of one group;
+// lane l of each of its kWideWarps solver warps works for env l. The tile's
+// vectors live in a global scratch array X [n + 1][kWideEnvs] (row n always
+// zero), cached in L1/L2 rather than held in shared memory, so that an SM is
+// not limited to the eight envs whose fields fit in its shared memory. A
+// sweep is a sequence of levels; in each level every solver warp runs its
+// list of segments. A segment applies a contiguous run of one row's terms, in
+// the reference's push order, to the row's value in X and, when it is the
+// row's last, finishes the row (U sweep: the diagonal).
+//
+// Synchronisation: each row has a ready count in shared memory, the number
+// of its segments completed so far (over both sweeps); a warp publishes it
+// after each segment. A segment reads rows that are complete before its
+// level or finished earlier by its own warp. A level's program is one block
+// of at most kWideStageBytes that a producer warp streams, by one bulk copy,
+// into a ring of kWideStages shared-memory stages; a stage is refilled only
+// after every solver warp has released it, so when a warp works on stage t
+// every warp has finished stage t - kWideStages. Each warp's list in a level
+// starts with the (row, count) pairs it must acquire: the rows it reads (and
+// its own row's previous segment) produced by another warp less than
+// kWideStages stages earlier. Block layout: a header of two int32 tables --
+// warp w's segments are [seg[w], seg[w + 1]) and its waits [wait[w],
+// wait[w + 1]) -- padded to kWideHdrBytes, the waits (uint32 row << 16 |
+// count, padded to 16 bytes), the segments (chunk0 relative to the block's
+// first chunk), then the chunks.
+constexpr int kWideWarps = 16;
+constexpr int kWideEnvs = 32;
+constexpr int kWideStageBytes = 16384;
+constexpr int kWideStages = 4;
+constexpr int kWideHdrBytes = 144;
+constexpr int kWideGroup = 3;   // chunks whose source loads a solver warp issues together
+static_assert(kWideHdrBytes >= 8 * (kWideWarps + 1) && kWideHdrBytes % 16 == 0, "level header");
+struct WideSeg {
+    uint32_t row;      // the row whose value the segment updates
+    uint32_t chunk0;   // its first chunk (relative to the level block's chunks)
+    uint32_t nchunk;   // chunks (terms / 4, rounded up)
+    uint32_t fin;      // bit 0: the segment finishes a U row (diagonal); bits 16-31: the row's ready count after it
+};
+struct WideChunk {
+    double v[4];       // term values (padding: 0)
+    uint32_t off[4];   // byte offset of the term's source row in X (row * kWideEnvs * 8; padding: row n)
+};
+static_assert(sizeof(WideChunk) == 48 && sizeof(WideSeg) == 16, "wide record sizes");
+struct WideSweep {
+    const uint8_t* blocks;     // the level blocks back to back
+    const uint32_t* lev_off;   // [nlev + 1] byte offset of level l's block
+    int nlev;
+};
+struct WideTile {
+    int group;
+    int env0;   // first global env
+    int nenv;   // envs in the tile (<= kWideEnvs)
+    int tile;   // index of the tile in its group (its scratch block)
+};
+
 // Geometry + solver tables of one group and the state of its envs.
 struct GroupDev {
     int n, ncv, k, nz, nv, na;
@@ -217,6 +273,12 @@ struct GroupDev {
     const double* zr_x;
     const int32_t *rs_p, *rs_pos;   // R = sensed U^-1, CSR by sensor (row positions)
     const double* rs_x;
+    // wide solve: level programs, the U diagonal (exact build) or its
+    // reciprocal (corrected and folded builds) by row, and the scratch
+    // vectors of the group's tiles, [tiles][n + 1][kWideEnvs]
+    WideSweep wfwd, wbwd;
+    const double* wdiag;
+    double* X;
     // per-env state
     double* T;     // [n_env][ncv] extended row order (between the phases of the
                    // folded build: z = L^-1 b in the solved rows)

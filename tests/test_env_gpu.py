@@ -111,10 +111,12 @@ def test_config2_full_batch_sample(scenario_cache):
         env.close()
 
 
-def test_config4_multiwave_sample(scenario_cache):
-    """Configuration 4's per-GPU batch (7,680 envs over the config-2 mix): about
-    960 slabs, so the solve runs in several waves of CTAs; a sample of envs from
-    every group and wave position against the oracle, bit for bit."""
+@pytest.mark.parametrize("wide", [0, 1], ids=["slabs", "wide"])
+def test_config4_multiwave_sample(scenario_cache, wide):
+    """Configuration 4's per-GPU batch (7,680 envs over the config-2 mix): the
+    first solve on about 960 slabs, several waves of CTAs, or on 240 wide
+    tiles of 32 envs; a sample of envs from every group and wave position
+    against the oracle, bit for bit."""
     import torch
 
     from neurips2026_smart_building_challenge_b200 import config_dir
@@ -122,9 +124,12 @@ def test_config4_multiwave_sample(scenario_cache):
     d = config_dir(2, scenario_cache, n_steps=400)
     n, steps = 7680, 5
     sample = [0, 1, 255, 256, 1279, 1280, 2561, 3839, 4000, 5119, 6400, 7679]
-    env = _vec(n, d, groups=30)
+    env = _vec(n, d, groups=30, wide=wide)
     try:
-        assert env.shape[6] > 2 * 148, "expected several waves of slabs"
+        if wide:
+            assert env.shape[6] == n // 32, "one wide tile per 32 envs of a group"
+        else:
+            assert env.shape[6] > 2 * 148, "expected several waves of slabs"
         paths = scenario_paths(d)
         orc = {e: OracleEnv(paths[int(env.scenario[e])]) for e in sample}
         env.reset()

@@ -53,3 +53,18 @@ def test_overlap_modes_agree_bit_for_bit(scenario_cache, build):
             for what, x, y in zip(("obs", "reward", "log terms", "terminals"), a, b):
                 assert np.array_equal(x, y), f"overlap {overlap}, step {s}: {what} differ"
         assert np.array_equal(base_fields, fields), f"overlap {overlap}: fields differ"
+
+
+def test_wide_and_slab_solves_agree_bit_for_bit(scenario_cache):
+    """The exact build's first solve on the wide kernel (k_wide0: tiles of 32
+    envs in an L1/L2-resident scratch, level programs) and on the
+    shared-memory slabs (k_solve<0>) give the same bits."""
+    from neurips2026_smart_building_challenge_b200 import config_dir
+
+    d = config_dir(2, scenario_cache, n_steps=400)
+    slab_trace, slab_fields = _run(d, -1, {"solve_exact": 1, "wide": 0})
+    wide_trace, wide_fields = _run(d, -1, {"solve_exact": 1, "wide": 1})
+    for s, (a, b) in enumerate(zip(slab_trace, wide_trace)):
+        for what, x, y in zip(("obs", "reward", "log terms", "terminals"), a, b):
+            assert np.array_equal(x, y), f"step {s}: {what} differ"
+    assert np.array_equal(slab_fields, wide_fields)

@@ -381,3 +381,161 @@ def test_ring_protocol(built, tmp_path, config, index):
         for sweep in (0, 1):
             for prog in _programs(lib, blob, sweep, ring):
                 walk(prog, ring)
+
+
+WIDE_STAGES, WIDE_HDR = 4, 144   # csrc/sbenv_dev.h kWideStages, kWideHdrBytes
+
+
+def _wide_program(lib, blob, sweep):
+    """The wide solve's level program (csrc/wide_sched.cpp) of one sweep (the U
+    sweep's stages follow the L sweep's): a list of levels, each a list over
+    the warps of (waits {row: count}, [(row, fin, count, [(value, offset)...])]),
+    and the info vector."""
+    lib.sb_wide_schedule.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(ctypes.c_int64), ctypes.c_void_p,
+                                     ctypes.c_void_p]
+    b = str(blob).encode()
+    info = (ctypes.c_int64 * 8)()
+    assert lib.sb_wide_schedule(b, sweep, info, None, None) == 1
+    nlev, nbytes = info[0], info[6]
+    W = lib.sb_wide_warps()
+    off = np.zeros(nlev + 1, np.uint32)
+    raw = np.zeros(max(nbytes, 1), np.uint8)
+    assert lib.sb_wide_schedule(b, sweep, info, off.ctypes.data, raw.ctypes.data) == 0
+    assert off[0] == 0 and off[-1] == nbytes
+    levels = []
+    for lv in range(nlev):
+        blk = raw[off[lv]:off[lv + 1]].tobytes()
+        assert len(blk) <= 16384 and len(blk) % 16 == 0
+        hdr = struct.unpack_from(f"<{2 * (W + 1)}i", blk, 0)
+        seg0, wait0 = hdr[:W + 1], hdr[W + 1:]
+        nseg, nwait = seg0[W], wait0[W]
+        waits = struct.unpack_from(f"<{nwait}I", blk, WIDE_HDR)
+        s0 = WIDE_HDR + 4 * ((nwait + 3) // 4 * 4)
+        segs = np.frombuffer(blk, "<u4", 4 * nseg, s0).reshape(nseg, 4)
+        c0 = s0 + 16 * nseg
+        nch = (len(blk) - c0) // 48
+        assert c0 + 48 * nch == len(blk)
+        ch = np.frombuffer(blk, np.uint8, 48 * nch, c0).reshape(nch, 48)
+        vals = ch[:, :32].copy().view("<f8").reshape(nch, 4)
+        offs = ch[:, 32:].copy().view("<u4").reshape(nch, 4)
+        warps = []
+        for w in range(W):
+            wl = {}
+            for i in range(wait0[w], wait0[w + 1]):
+                r, c = waits[i] >> 16, waits[i] & 0xFFFF
+                assert r not in wl
+                wl[r] = c
+            lst = []
+            for q in range(seg0[w], seg0[w + 1]):
+                row, k0, nc, fin = (int(v) for v in segs[q])
+                assert k0 + nc <= nch
+                lst.append((row, fin & 1, fin >> 16,
+                            [(float(vals[c][u]), int(offs[c][u])) for c in range(k0, k0 + nc) for u in range(4)]))
+            warps.append((wl, lst))
+        levels.append(warps)
+    return levels, list(info)
+
+
+class _WideState:
+    """One env's values and the rows' progress over the sweeps of a step, as the
+    kernel keeps them (X and the ready counts)."""
+
+    def __init__(self, rhs, n):
+        self.n = n
+        self.x = list(rhs) + [0.0]
+        self.cnt = [0] * n
+        self.stage = [-(1 << 29)] * n
+        self.warp = [-1] * n
+        self.next_stage = 0
+
+
+def _wide_execute(prog, st, backward, terms, diag):
+    """Runs a sweep's levels on one env's vector with the kernel's semantics
+    (exact build: a rounded product and a rounded subtraction per term, the
+    division by the diagonal) and checks the schedule's rules on the way: a
+    segment reads rows final before its level or finished earlier in the
+    level by its own warp; every row another warp produced less than
+    kWideStages stages before -- a source, or the row's own previous segment --
+    is in the warp's wait list for the level with a count it reaches; no row
+    has two segments in one level; the published counts advance by one."""
+    levels, _ = prog
+    n = st.n
+    applied = [0] * n
+    final = [not backward and not terms[i] for i in range(n)]
+    for lv, warps in enumerate(levels):
+        S = st.next_stage + lv             # stages run on over the sweeps
+        touched, done = set(), []
+        for w, (waits, segs) in enumerate(warps):
+            def covered(r, count):
+                if count <= 0 or st.warp[r] == w or st.stage[r] <= S - WIDE_STAGES:
+                    return True
+                return waits.get(r, 0) >= count
+
+            for row, fin, count, tl in segs:
+                assert 0 <= row < n and row not in touched and not final[row], (lv, w, row)
+                touched.add(row)
+                assert covered(row, st.cnt[row]), f"stage {S}: row {row}'s previous segment not acquired"
+                assert count == st.cnt[row] + 1
+                acc = st.x[row]
+                for v, off in tl:
+                    src = off // (32 * 8)
+                    assert off % 256 == 0
+                    if src == n:                      # padding: a zero term on the zero row
+                        assert v == 0.0
+                        continue
+                    k = applied[row]
+                    assert k < len(terms[row]) and terms[row][k] == (src, v), (row, k)
+                    assert final[src] or (src in done and st.warp[src] == w), \
+                        f"stage {S}: row {row} reads unfinished row {src}"
+                    assert covered(src, st.cnt[src]), f"stage {S}: source {src} of row {row} not acquired"
+                    acc = acc - v * st.x[src]
+                    applied[row] += 1
+                if fin:
+                    assert backward and applied[row] == len(terms[row])
+                    acc = acc / diag[row]
+                st.x[row] = acc
+                st.cnt[row] = count
+                st.stage[row] = S
+                st.warp[row] = w
+                if applied[row] == len(terms[row]) and (fin or not backward):
+                    done.append(row)
+        for r in done:
+            final[r] = True
+    assert all(final)
+    st.next_stage += len(levels)
+    return np.array(st.x[:n])
+
+
+@pytest.mark.parametrize("config,index", [(1, 0), (2, 23), (3, 0)])
+def test_wide_program_replays_reference_solve(built, tmp_path, config, index):
+    """The wide solve's level programs: every row receives exactly the
+    reference's terms in push order, a segment reads only complete rows, every
+    row produced recently by another warp is acquired, and the L then U replay
+    equals the column-push solve bit for bit."""
+    import neurips2026_smart_building_challenge_b200 as pkg
+
+    blob = pkg.write_scenario(tmp_path / "s.sbb", pkg.preset(config, index, n_steps=10))
+    b = Blob(blob)
+    L, U = b.csc("lu_L"), b.csc("lu_U")
+    n = L.shape[0]
+    lib = pkg.env_lib()
+    fwd, bwd = _wide_program(lib, blob, 0), _wide_program(lib, blob, 1)
+    tl, tu = _terms(L, False), _terms(U, True)
+    assert fwd[1][4] == L.nnz - n and bwd[1][4] == U.nnz - n     # every term once
+    rhs = np.random.default_rng(index).standard_normal(n) * 300.0
+    st = _WideState(rhs, n)
+    _wide_execute(fwd, st, False, tl, None)
+    z = _wide_execute(bwd, st, True, tu, U.tocsc().diagonal())
+    assert np.array_equal(z, _push_reference(L, U, rhs))
+
+
+def test_wide_program_errors(built, tmp_path):
+    import neurips2026_smart_building_challenge_b200 as pkg
+
+    blob = pkg.write_scenario(tmp_path / "s.sbb", pkg.preset(1, 0, n_steps=10))
+    lib = pkg.env_lib()
+    info = (ctypes.c_int64 * 8)()
+    lib.sb_wide_schedule.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(ctypes.c_int64), ctypes.c_void_p,
+                                     ctypes.c_void_p]
+    assert lib.sb_wide_schedule(str(blob).encode(), 2, info, None, None) == -1
+    assert lib.sb_wide_schedule(str(tmp_path / "missing.sbb").encode(), 0, info, None, None) == -1
