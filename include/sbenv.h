@@ -322,22 +322,18 @@ int sb_sweep_warps(void);
  * modelled cycles, stream bytes, dense block records, rows they finish}. */
 int sb_sweep_stats(const char* blob_path, int sweep, int ring_stages, double* out);
 /* Host-only: the wide solve's level program of the blob's L (sweep 0) or U
- * (sweep 1) sweep, with the `slots` rows deepest in the L sweep's dependency
- * graph kept in shared memory (their row indices to slot_rows[slots] when
- * non-null); the U program's stages and ready counts continue the L
+ * (sweep 1) sweep; the U program's stages and ready counts continue the L
  * program's. info[8] receives {levels, segments, chunks, partial segments,
  * terms, modelled cycles, bytes of all level blocks, largest level block};
  * with lev_off (levels + 1 uint32: each level block's byte offset) and blocks
- * (the level blocks: two int32 tables of sb_wide_warps() + 1 entries -- first
- * segment and first wait of each warp -- padded to 144 bytes, the waits
- * (uint32 row << 16 | count, padded to 16 bytes), 16-byte segments {row,
- * first chunk | chunks << 16, location, finish | count << 16}, 48-byte chunks
- * {four f64 values, four uint32 locations}; a location with bit 31 set is a
- * shared-memory slot's byte offset, else a row's) both non-null the program
- * is copied out and 0 returned, else 1; -1 on error. No counterpart in the
- * reference (its CPU core has no schedule). */
-int sb_wide_schedule(const char* blob_path, int sweep, int slots, int64_t* info, uint32_t* lev_off, uint8_t* blocks,
-                     int32_t* slot_rows);
+ * (the level blocks: two int32 tables of sb_wide_warps() + 1 entries --
+ * first segment and first wait of each warp -- padded to 144 bytes, the
+ * waits (uint32 row << 16 | count, padded to 16 bytes), 16-byte segments
+ * {row, first chunk, chunks, finish | count << 16}, 48-byte chunks {four
+ * f64 values, four uint32 byte offsets}) both non-null the program is copied
+ * out and 0 returned, else 1; -1 on error. No counterpart in the reference
+ * (its CPU core has no schedule). */
+int sb_wide_schedule(const char* blob_path, int sweep, int64_t* info, uint32_t* lev_off, uint8_t* blocks);
 /* Solver warps of a wide-solve CTA (level program columns). */
 int sb_wide_warps(void);
 

@@ -682,17 +682,10 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
         if (E.wide) {
             // level programs in the reference's push order for every build; the
             // U rows' diagonal (exact) or its reciprocal, rounded once here
-            // shared-memory rows: what two CTAs per SM leave of shared memory
-            const size_t per_cta = smem_cap / 2 >= 1024 ? smem_cap / 2 - 1024 : 0;
-            const size_t base = wide_smem_bytes(h.n, 0);
-            const int nslots = per_cta > base ? (int)std::min<size_t>(h.n, (per_cta - base) / (kWideEnvs * 8)) : 0;
-            const std::vector<int> srows = wide_smem_rows(h.n, h.lt, nslots);
-            std::vector<int> slot(h.n, -1);
-            for (size_t q = 0; q < srows.size(); q++) slot[srows[q]] = (int)q;
             HostWide wf, wb;
             WideFlags wfl(h.n);
-            std::string we = build_wide(h.n, h.lt, false, 0, wfl, slot, wf);
-            if (we.empty()) we = build_wide(h.n, h.ut, true, wf.nlev, wfl, slot, wb);
+            std::string we = build_wide(h.n, h.lt, false, 0, wfl, wf);
+            if (we.empty()) we = build_wide(h.n, h.ut, true, wf.nlev, wfl, wb);
             if (!we.empty()) { set_err("group %d: %s", c, we.c_str()); return false; }
             auto put_wide = [&](const HostWide& hw, WideSweep& s) {
                 s.blocks = E.arena.upload(hw.blocks, ok);
@@ -708,9 +701,7 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
             const int ntile = (gd.n_env + kWideEnvs - 1) / kWideEnvs;
             // scratch rows n of every tile stay zero (the padding terms' source)
             gd.X = E.arena.zeros<double>((size_t)ntile * (h.n + 1) * kWideEnvs, ok);
-            gd.wslot_row = E.arena.upload(std::vector<int32_t>(srows.begin(), srows.end()), ok);
-            gd.wslots = (int)srows.size();
-            E.smem_wide = std::max(E.smem_wide, wide_smem_bytes(h.n, gd.wslots));
+            E.smem_wide = std::max(E.smem_wide, wide_smem_bytes(h.n));
             for (int t = 0; t < ntile; t++)
                 E.wtiles.push_back({c, gd.env0 + t * kWideEnvs, std::min(kWideEnvs, gd.n_env - t * kWideEnvs), t});
         }
@@ -1865,8 +1856,7 @@ int sb_solve_schedule(const char* blob_path, int sweep, int ring_stages, uint8_t
 
 int sb_sweep_warps(void) { return kSweepWarps; }
 
-int sb_wide_schedule(const char* blob_path, int sweep, int slots, int64_t* info, uint32_t* lev_off, uint8_t* blocks,
-                     int32_t* slot_rows) {
+int sb_wide_schedule(const char* blob_path, int sweep, int64_t* info, uint32_t* lev_off, uint8_t* blocks) {
     HostGroup g;
     sbb::Reader r;
     std::string e = r.open(blob_path ? blob_path : "");
@@ -1877,16 +1867,10 @@ int sb_wide_schedule(const char* blob_path, int sweep, int slots, int64_t* info,
         // the L sweep's program, then (sweep 1) the U sweep's, which continues
         // the rows' ready counts and stage numbering
         WideFlags fl(g.n);
-        const std::vector<int> srows = wide_smem_rows(g.n, g.lt, slots);
-        std::vector<int> slot(g.n, -1);
-        for (size_t q = 0; q < srows.size(); q++) {
-            slot[srows[q]] = (int)q;
-            if (slot_rows) slot_rows[q] = srows[q];
-        }
-        e = build_wide(g.n, g.lt, false, 0, fl, slot, w);
+        e = build_wide(g.n, g.lt, false, 0, fl, w);
         if (e.empty() && sweep == 1) {
             const int nl = w.nlev;
-            e = build_wide(g.n, g.ut, true, nl, fl, slot, w);
+            e = build_wide(g.n, g.ut, true, nl, fl, w);
         }
     }
     if (!e.empty() || !info) { set_err("%s", e.empty() ? "null info" : e.c_str()); return -1; }

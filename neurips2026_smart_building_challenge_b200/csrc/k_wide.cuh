@@ -24,18 +24,9 @@ constexpr int kWideThreads = (kWideWarps + 1) * 32;   // the solver warps and th
 constexpr uint32_t kWideSpin = 1u << 22;                // polls of one ready count before the wait gives up
 
 // Shared memory of a wide-solve CTA: the stage ring, its full and empty
-// mbarriers, the rows' ready counts, the shared-memory rows Xs and the abort
-// word.
-SB_HD constexpr size_t wide_ready_off() { return (size_t)kWideStages * kWideStageBytes + 2 * kWideStages * 8; }
-SB_HD constexpr size_t wide_xs_off(int n) { return wide_ready_off() + (((size_t)n + 1) * 2 + 15) / 16 * 16; }
-SB_HD constexpr size_t wide_smem_bytes(int n, int slots) {
-    return wide_xs_off(n) + (size_t)slots * kWideEnvs * 8 + 16;
-}
-
-// A value's location (kWideSmem: a slot of Xs, else a row of X) as a generic
-// pointer; xg = the tile's X + lane, xs = Xs + lane.
-__device__ __forceinline__ double* wide_loc(char* xg, char* xs, uint32_t o) {
-    return reinterpret_cast<double*>((o & kWideSmem) ? xs + (o & ~kWideSmem) : xg + o);
+// mbarriers, the rows' ready counts and the abort word.
+SB_HD constexpr size_t wide_smem_bytes(int n) {
+    return (size_t)kWideStages * kWideStageBytes + 2 * kWideStages * 8 + (((size_t)n + 1) * 2 + 15) / 16 * 16 + 16;
 }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
@@ -55,7 +46,6 @@ struct WideShared {
     uint64_t* full;     // [kWideStages] the stage's copy has landed
     uint64_t* empty;    // [kWideStages] every solver warp is done with the stage
     uint16_t* ready;    // [n + 1] the rows' ready counts
-    double* xs;         // [slots][kWideEnvs] the rows kept in shared memory
     volatile int* abort;
 };
 
@@ -98,8 +88,7 @@ __device__ void wide_produce(const GroupDev& g, const WideShared& sh, int total)
 template <bool Tol>
 __device__ __forceinline__ bool wide_level(const uint8_t* blk, const WideShared& sh, double* Xl,
                                            const double* __restrict__ wdiag, int warp, int lane) {
-    char* xg = reinterpret_cast<char*>(Xl);
-    char* xs = reinterpret_cast<char*>(sh.xs + lane);
+    const char* xb = reinterpret_cast<const char*>(Xl);
     const int32_t* hdr = reinterpret_cast<const int32_t*>(blk);
     const int a = hdr[warp], b = hdr[warp + 1], nseg = hdr[kWideWarps];
     const int w0 = hdr[kWideWarps + 1 + warp], w1 = hdr[kWideWarps + 2 + warp], nwait = hdr[2 * kWideWarps + 1];
@@ -126,23 +115,21 @@ __device__ __forceinline__ bool wide_level(const uint8_t* blk, const WideShared&
     __threadfence_block();   // what the acquiring lanes saw, for every lane of the warp
     for (int q = a; q < b; q++) {
         const uint4 sg = segs[q];
-        double* row = wide_loc(xg, xs, sg.z);
-        double acc = *row;
-        const WideChunk* ch = chunks + (sg.y & 0xFFFFu);
-        const uint32_t nch = sg.y >> 16;
+        double acc = Xl[(size_t)sg.x * kWideEnvs];
+        const WideChunk* ch = chunks + sg.y;
         // the source values of up to kWideGroup chunks are loaded together,
         // then those chunks' terms applied in order
-        for (uint32_t c0 = 0; c0 < nch; c0 += kWideGroup) {
-            const uint32_t m = min((uint32_t)kWideGroup, nch - c0);
+        for (uint32_t c0 = 0; c0 < sg.z; c0 += kWideGroup) {
+            const uint32_t m = min((uint32_t)kWideGroup, sg.z - c0);
             double x[kWideGroup][4];
 #pragma unroll
             for (int j = 0; j < kWideGroup; j++) {
                 if ((uint32_t)j < m) {
                     const uint4 o = *reinterpret_cast<const uint4*>(ch[c0 + j].off);
-                    x[j][0] = *wide_loc(xg, xs, o.x);
-                    x[j][1] = *wide_loc(xg, xs, o.y);
-                    x[j][2] = *wide_loc(xg, xs, o.z);
-                    x[j][3] = *wide_loc(xg, xs, o.w);
+                    x[j][0] = *reinterpret_cast<const double*>(xb + o.x);
+                    x[j][1] = *reinterpret_cast<const double*>(xb + o.y);
+                    x[j][2] = *reinterpret_cast<const double*>(xb + o.z);
+                    x[j][3] = *reinterpret_cast<const double*>(xb + o.w);
                 }
             }
 #pragma unroll
@@ -165,7 +152,7 @@ __device__ __forceinline__ bool wide_level(const uint8_t* blk, const WideShared&
             }
         }
         if (sg.w & 1u) acc = Tol ? dmul(acc, __ldg(wdiag + sg.x)) : ddiv(acc, __ldg(wdiag + sg.x));
-        *row = acc;
+        Xl[(size_t)sg.x * kWideEnvs] = acc;
         __syncwarp();   // every lane's store precedes the release below
         if (lane == 0) st_release_u16(sh.ready + sg.x, sg.w >> 16);
     }
@@ -211,9 +198,8 @@ k_wide0(const StepCtx* __restrict__ ctx, const WideTile* __restrict__ tiles) {
     sh.slots = wsm;
     sh.full = reinterpret_cast<uint64_t*>(wsm + (size_t)kWideStages * kWideStageBytes);
     sh.empty = sh.full + kWideStages;
-    sh.ready = reinterpret_cast<uint16_t*>(wsm + wide_ready_off());
-    sh.xs = reinterpret_cast<double*>(wsm + wide_xs_off(n));
-    sh.abort = reinterpret_cast<volatile int*>(wsm + wide_smem_bytes(n, g.wslots) - 16);
+    sh.ready = reinterpret_cast<uint16_t*>(sh.empty + kWideStages);
+    sh.abort = reinterpret_cast<volatile int*>(wsm + wide_smem_bytes(n) - 16);
     const int total = g.wfwd.nlev + (g.fold ? 0 : g.wbwd.nlev);
     if (tid == 0) {
         *sh.abort = 0;
@@ -258,10 +244,6 @@ k_wide0(const StepCtx* __restrict__ ctx, const WideTile* __restrict__ tiles) {
         }
     }
     __syncthreads();
-    // the shared-memory rows' right sides into Xs
-    for (int s = warp; solver && s < g.wslots; s += kWideWarps)
-        sh.xs[(size_t)s * kWideEnvs + lane] = Xl[(size_t)__ldg(g.wslot_row + s) * kWideEnvs];
-    __syncthreads();
 
     // ---- first solve (the folded build: its forward half only): the
     // producer warp streams the level blocks, the solver warps run them ----
@@ -269,9 +251,6 @@ k_wide0(const StepCtx* __restrict__ ctx, const WideTile* __restrict__ tiles) {
     else if (lane == 0) wide_produce(g, sh, total);
     __syncthreads();
     const int err = *sh.abort;
-    // the shared-memory rows' solutions back into X
-    for (int s = warp; !err && solver && s < g.wslots; s += kWideWarps)
-        Xl[(size_t)__ldg(g.wslot_row + s) * kWideEnvs] = sh.xs[(size_t)s * kWideEnvs + lane];
     if (tid == 0)
         for (int s = 0; s < kWideStages; s++) {
             mbar_inval(sh.full + s);
@@ -281,7 +260,6 @@ k_wide0(const StepCtx* __restrict__ ctx, const WideTile* __restrict__ tiles) {
         if (tid == 0) set_error(ctx->status, err);
         return;
     }
-    __syncthreads();
 
     // ---- air side: the sensed right side (sb_fdm.c:155-181) or, folded, R z;
     // one solver warp per coupled VAV ----

@@ -207,23 +207,15 @@ constexpr int kWideStages = 4;
 constexpr int kWideHdrBytes = 144;
 constexpr int kWideGroup = 3;   // chunks whose source loads a solver warp issues together
 static_assert(kWideHdrBytes >= 8 * (kWideWarps + 1) && kWideHdrBytes % 16 == 0, "level header");
-// Rows kept in shared memory: the rows deepest in the L sweep's dependency
-// graph -- the nested-dissection separators, whose chains of dependent rows
-// are the sweeps' critical paths in both directions -- live during the
-// sweeps in a shared-memory array Xs [slots][kWideEnvs] instead of X, so a
-// hop along those chains costs a shared-memory access, not a round trip to
-// L2. A value's location is a 32-bit offset: bit 31 clear, the byte offset of
-// its row in X; set, kWideSmem | the byte offset of its slot in Xs.
-constexpr uint32_t kWideSmem = 0x80000000u;
 struct WideSeg {
     uint32_t row;      // the row whose value the segment updates
-    uint32_t chunks;   // its first chunk (relative to the level block's chunks) | chunks << 16
-    uint32_t xoff;     // the location of the row's value
+    uint32_t chunk0;   // its first chunk (relative to the level block's chunks)
+    uint32_t nchunk;   // chunks (terms / 4, rounded up)
     uint32_t fin;      // bit 0: the segment finishes a U row (diagonal); bits 16-31: the row's ready count after it
 };
 struct WideChunk {
     double v[4];       // term values (padding: 0)
-    uint32_t off[4];   // location of the term's source value (padding: row n of X, always zero)
+    uint32_t off[4];   // byte offset of the term's source row in X (row * kWideEnvs * 8; padding: row n)
 };
 static_assert(sizeof(WideChunk) == 48 && sizeof(WideSeg) == 16, "wide record sizes");
 struct WideSweep {
@@ -287,8 +279,6 @@ struct GroupDev {
     WideSweep wfwd, wbwd;
     const double* wdiag;
     double* X;
-    const int32_t* wslot_row;   // [wslots] the row held in each shared-memory slot
-    int wslots;
     // per-env state
     double* T;     // [n_env][ncv] extended row order (between the phases of the
                    // folded build: z = L^-1 b in the solved rows)

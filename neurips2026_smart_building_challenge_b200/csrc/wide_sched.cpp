@@ -49,28 +49,10 @@ constexpr int kMinPartial = 8;      // shortest partial segment
 
 }  // namespace
 
-std::vector<int> wide_smem_rows(int n, const std::vector<std::vector<std::pair<int, double>>>& lterms, int count) {
-    std::vector<int> lev(n, 0), order(n);
-    for (int i = 0; i < n; i++) {
-        for (const auto& t : lterms[i]) lev[i] = std::max(lev[i], lev[t.first] + 1);
-        order[i] = i;
-    }
-    std::stable_sort(order.begin(), order.end(), [&](int a, int b) {
-        return lev[a] != lev[b] ? lev[a] > lev[b] : a > b;
-    });
-    order.resize(std::max(0, std::min(count, n)));
-    return order;
-}
-
 std::string build_wide(int n, const std::vector<std::vector<std::pair<int, double>>>& terms, bool backward,
-                       int stage0, WideFlags& flags, const std::vector<int>& slot, HostWide& out) {
+                       int stage0, WideFlags& flags, HostWide& out) {
     out = HostWide();
     if ((int)terms.size() != n) return "wide program: term lists do not match the row count";
-    if ((int)slot.size() != n) return "wide program: slot map does not match the row count";
-    auto loc = [&](int r) -> uint32_t {
-        return (r < n && slot[r] >= 0) ? (kWideSmem | (uint32_t)(slot[r] * kWideEnvs * 8))
-                                       : (uint32_t)r * kWideEnvs * 8;
-    };
     if ((int)flags.cnt.size() != n) return "wide program: progress state does not match the row count";
     if (n >= 0xFFFF) return "wide program: more than 65534 solved cells";
     for (int i = 0; i < n; i++)
@@ -244,8 +226,8 @@ std::string build_wide(int n, const std::vector<std::vector<std::pair<int, doubl
                 for (int a = it.from; a < it.to; a++) want(terms[it.row][a].first, flags.cnt[terms[it.row][a].first]);
                 WideSeg s;
                 s.row = (uint32_t)it.row;
-                s.chunks = (uint32_t)chunks.size() | ((uint32_t)chunks_of(it.from, it.to) << 16);
-                s.xoff = loc(it.row);
+                s.chunk0 = (uint32_t)chunks.size();
+                s.nchunk = (uint32_t)chunks_of(it.from, it.to);
                 flags.cnt[it.row]++;
                 flags.stage[it.row] = stage;
                 flags.warp[it.row] = w;
@@ -257,7 +239,7 @@ std::string build_wide(int n, const std::vector<std::vector<std::pair<int, doubl
                     for (int u = 0; u < 4; u++) {
                         const bool in = a + u < it.to;
                         ch.v[u] = in ? terms[it.row][a + u].second : 0.0;
-                        ch.off[u] = loc(in ? terms[it.row][a + u].first : n);
+                        ch.off[u] = (uint32_t)((in ? terms[it.row][a + u].first : n) * kWideEnvs * 8);
                     }
                     chunks.push_back(ch);
                 }

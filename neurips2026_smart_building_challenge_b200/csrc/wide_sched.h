@@ -38,14 +38,9 @@ struct WideFlags {
 //             terms too); forward rows without terms are final from the start;
 //   stage0    the stage index of the sweep's first level (the L sweep's levels
 //             come first, then the U sweep's);
-//   flags     the rows' progress before the sweep, updated;
-//   slot      per row its shared-memory slot, or -1 (the row stays in X).
+//   flags     the rows' progress before the sweep, updated.
 // Returns "" or an error.
 std::string build_wide(int n, const std::vector<std::vector<std::pair<int, double>>>& terms, bool backward,
-                       int stage0, WideFlags& flags, const std::vector<int>& slot, HostWide& out);
-
-// The rows to keep in shared memory: the `count` rows deepest in the L
-// sweep's dependency graph (ties: the later row), in slot order.
-std::vector<int> wide_smem_rows(int n, const std::vector<std::vector<std::pair<int, double>>>& lterms, int count);
+                       int stage0, WideFlags& flags, HostWide& out);
 
 }  // namespace sbenv

@@ -386,43 +386,21 @@ def test_ring_protocol(built, tmp_path, config, index):
 WIDE_STAGES, WIDE_HDR = 4, 144   # csrc/sbenv_dev.h kWideStages, kWideHdrBytes
 
 
-WIDE_SMEM = 0x80000000
-
-
-def _wide_argtypes(lib):
-    lib.sb_wide_schedule.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int64),
-                                     ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
-
-
-def _wide_program(lib, blob, sweep, slots, n):
+def _wide_program(lib, blob, sweep):
     """The wide solve's level program (csrc/wide_sched.cpp) of one sweep (the U
-    sweep's stages follow the L sweep's) with `slots` rows in shared memory: a
-    list of levels, each a list over the warps of (waits {row: count},
-    [(row, fin, count, [(value, source row)...])]), and the info vector. Every
-    location (a row of X, or bit 31 and a shared-memory slot) is decoded to
-    its row and checked against the slot map."""
-    _wide_argtypes(lib)
+    sweep's stages follow the L sweep's): a list of levels, each a list over
+    the warps of (waits {row: count}, [(row, fin, count, [(value, offset)...])]),
+    and the info vector."""
+    lib.sb_wide_schedule.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(ctypes.c_int64), ctypes.c_void_p,
+                                     ctypes.c_void_p]
     b = str(blob).encode()
     info = (ctypes.c_int64 * 8)()
-    assert lib.sb_wide_schedule(b, sweep, slots, info, None, None, None) == 1
+    assert lib.sb_wide_schedule(b, sweep, info, None, None) == 1
     nlev, nbytes = info[0], info[6]
     W = lib.sb_wide_warps()
     off = np.zeros(nlev + 1, np.uint32)
     raw = np.zeros(max(nbytes, 1), np.uint8)
-    srow = np.full(max(slots, 1), -1, np.int32)
-    assert lib.sb_wide_schedule(b, sweep, slots, info, off.ctypes.data, raw.ctypes.data, srow.ctypes.data) == 0
-    slot_of = {int(r): q for q, r in enumerate(srow[:slots])}
-    assert len(slot_of) == slots and all(0 <= r < n for r in slot_of)
-
-    def row_at(loc):
-        if loc & WIDE_SMEM:
-            q = (loc & ~WIDE_SMEM) // 256
-            assert (loc & ~WIDE_SMEM) % 256 == 0 and q < slots
-            return int(srow[q])
-        assert loc % 256 == 0
-        r = loc // 256
-        assert r == n or r not in slot_of, f"row {r} read from X but kept in shared memory"
-        return r
+    assert lib.sb_wide_schedule(b, sweep, info, off.ctypes.data, raw.ctypes.data) == 0
     assert off[0] == 0 and off[-1] == nbytes
     levels = []
     for lv in range(nlev):
@@ -449,11 +427,10 @@ def _wide_program(lib, blob, sweep, slots, n):
                 wl[r] = c
             lst = []
             for q in range(seg0[w], seg0[w + 1]):
-                row, packed, xoff, fin = (int(v) for v in segs[q])
-                k0, nc = packed & 0xFFFF, packed >> 16
-                assert k0 + nc <= nch and row_at(xoff) == row
+                row, k0, nc, fin = (int(v) for v in segs[q])
+                assert k0 + nc <= nch
                 lst.append((row, fin & 1, fin >> 16,
-                            [(float(vals[c][u]), row_at(int(offs[c][u]))) for c in range(k0, k0 + nc) for u in range(4)]))
+                            [(float(vals[c][u]), int(offs[c][u])) for c in range(k0, k0 + nc) for u in range(4)]))
             warps.append((wl, lst))
         levels.append(warps)
     return levels, list(info)
@@ -500,7 +477,9 @@ def _wide_execute(prog, st, backward, terms, diag):
                 assert covered(row, st.cnt[row]), f"stage {S}: row {row}'s previous segment not acquired"
                 assert count == st.cnt[row] + 1
                 acc = st.x[row]
-                for v, src in tl:
+                for v, off in tl:
+                    src = off // (32 * 8)
+                    assert off % 256 == 0
                     if src == n:                      # padding: a zero term on the zero row
                         assert v == 0.0
                         continue
@@ -527,8 +506,8 @@ def _wide_execute(prog, st, backward, terms, diag):
     return np.array(st.x[:n])
 
 
-@pytest.mark.parametrize("config,index,slots", [(1, 0, 0), (2, 23, 171), (3, 0, 99)])
-def test_wide_program_replays_reference_solve(built, tmp_path, config, index, slots):
+@pytest.mark.parametrize("config,index", [(1, 0), (2, 23), (3, 0)])
+def test_wide_program_replays_reference_solve(built, tmp_path, config, index):
     """The wide solve's level programs: every row receives exactly the
     reference's terms in push order, a segment reads only complete rows, every
     row produced recently by another warp is acquired, and the L then U replay
@@ -540,7 +519,7 @@ def test_wide_program_replays_reference_solve(built, tmp_path, config, index, sl
     L, U = b.csc("lu_L"), b.csc("lu_U")
     n = L.shape[0]
     lib = pkg.env_lib()
-    fwd, bwd = _wide_program(lib, blob, 0, slots, n), _wide_program(lib, blob, 1, slots, n)
+    fwd, bwd = _wide_program(lib, blob, 0), _wide_program(lib, blob, 1)
     tl, tu = _terms(L, False), _terms(U, True)
     assert fwd[1][4] == L.nnz - n and bwd[1][4] == U.nnz - n     # every term once
     rhs = np.random.default_rng(index).standard_normal(n) * 300.0
@@ -556,6 +535,7 @@ def test_wide_program_errors(built, tmp_path):
     blob = pkg.write_scenario(tmp_path / "s.sbb", pkg.preset(1, 0, n_steps=10))
     lib = pkg.env_lib()
     info = (ctypes.c_int64 * 8)()
-    _wide_argtypes(lib)
-    assert lib.sb_wide_schedule(str(blob).encode(), 2, 0, info, None, None, None) == -1
-    assert lib.sb_wide_schedule(str(tmp_path / "missing.sbb").encode(), 0, 0, info, None, None, None) == -1
+    lib.sb_wide_schedule.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(ctypes.c_int64), ctypes.c_void_p,
+                                     ctypes.c_void_p]
+    assert lib.sb_wide_schedule(str(blob).encode(), 2, info, None, None) == -1
+    assert lib.sb_wide_schedule(str(tmp_path / "missing.sbb").encode(), 0, info, None, None) == -1
