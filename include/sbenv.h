@@ -336,6 +336,10 @@ int sb_sweep_stats(const char* blob_path, int sweep, int ring_stages, double* ou
 int sb_wide_schedule(const char* blob_path, int sweep, int64_t* info, uint32_t* lev_off, uint8_t* blocks);
 /* Solver warps of a wide-solve CTA (level program columns). */
 int sb_wide_warps(void);
+/* The wide solve's build constants: out[6] = {solver warps, ring stages, stage
+ * bytes, level header bytes, chunks whose loads a warp issues together, CTAs
+ * per SM}. No counterpart in the reference. */
+void sb_wide_config(int* out);
 
 #ifdef __cplusplus
 }

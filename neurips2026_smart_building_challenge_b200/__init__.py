@@ -41,7 +41,7 @@ ENV_SYMBOLS = ["sb_dict_new", "sb_dict_free", "dict_find", "dict_set", "dict_set
                "sb_solve_schedule", "sb_sweep_warps", "sb_sweep_stats", "sb_debug_state", "sb_step_timed", "sb_solve_bytes",
                "sb_dense_check", "sb_dense_check_mode", "sb_beta_actions", "sb_snapshot_write", "sb_dense_solve_noalloc",
                "sb_episode_options", "sb_solve_flops", "sb_fp64_peak", "sb_scenario_stats", "sb_test_stall",
-               "sb_wide_schedule", "sb_wide_warps"]
+               "sb_wide_schedule", "sb_wide_warps", "sb_wide_config"]
 GEN_SYMBOLS = ["sbgen_preset", "sbgen_write", "sbgen_factor_stats"]
 
 

@@ -597,7 +597,7 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     std::vector<int> bsel(NG);
     for (int c = 0; c < NG; c++) bsel[c] = width(c, bwave);
     // the wide solve pays off once the slabs are several waves of the GPU: a
-    // slab holds at most eight envs per SM, two wide tiles 64, but a tile's
+    // slab holds at most eight envs per SM, a wide tile 32, but a tile's
     // sweeps take a few times a slab's
     {
         long slabs = 0;
@@ -984,11 +984,12 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     CK(cudaFuncSetAttribute(k_solve<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_solve));
     CK(cudaFuncSetAttribute(k_solve<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_solve));
     CK(cudaFuncSetAttribute(k_dense, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_dense));
-    // the wide solve keeps its vectors in L1: no more shared memory than two
+    // the wide solve keeps its vectors in L1: no more shared memory than its
     // CTAs' stage rings and ready counts, the rest of the SM's 256 KB is L1
     if (E.wide) {
         if (E.smem_wide > smem_cap) { set_err("wide solve needs %zu B of shared memory", E.smem_wide); return false; }
-        const int pct = (int)std::min<size_t>(100, (100 * (2 * E.smem_wide + 2048) + smem_cap - 1) / smem_cap);
+        const int pct = (int)std::min<size_t>(
+            100, (100 * (kWideCtas * (E.smem_wide + 1024)) + smem_cap - 1) / smem_cap);
         for (const void* f : {(const void*)k_wide0<false>, (const void*)k_wide0<true>}) {
             CK(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)E.smem_wide));
             CK(cudaFuncSetAttribute(f, cudaFuncAttributePreferredSharedMemoryCarveout, pct));
@@ -1022,9 +1023,9 @@ bool build_engine(Engine& E, int n, Dict* kw, obs_t* obs, float* act, float* rew
     if (E.dense_cls.size() > 1 && E.overlap != 0) {
         int sms = 0;
         CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0));
-        // more than one wave: of slabs (one per SM) or of wide tiles (two per SM)
+        // more than one wave: of slabs (one per SM) or of wide tiles (kWideCtas per SM)
         const int units = E.wide ? (int)E.wtiles.size() : (int)E.slabs.size();
-        E.split_phase0 = E.overlap == 2 || (E.overlap < 0 && units > (E.wide ? 2 * sms : sms));
+        E.split_phase0 = E.overlap == 2 || (E.overlap < 0 && units > (E.wide ? kWideCtas * sms : sms));
         int least = 0, greatest = 0;
         CK(cudaDeviceGetStreamPriorityRange(&least, &greatest));
         E.cls_st.assign(E.dense_cls.size(), nullptr);
@@ -1889,6 +1890,11 @@ int sb_wide_schedule(const char* blob_path, int sweep, int64_t* info, uint32_t* 
 }
 
 int sb_wide_warps(void) { return kWideWarps; }
+
+void sb_wide_config(int* out) {
+    const int v[6] = {kWideWarps, kWideStages, kWideStageBytes, kWideHdrBytes, kWideGroup, kWideCtas};
+    for (int i = 0; i < 6; i++) out[i] = v[i];
+}
 
 int sb_sweep_stats(const char* blob_path, int sweep, int ring_stages, double* out) {
     HostGroup g;

@@ -178,7 +178,7 @@ __device__ void wide_solve(const GroupDev& g, const WideShared& sh, int total, d
 }
 
 template <bool Tol>
-__global__ void __launch_bounds__(kWideThreads, 2)
+__global__ void __launch_bounds__(kWideThreads, kWideCtas)
 k_wide0(const StepCtx* __restrict__ ctx, const WideTile* __restrict__ tiles) {
     // a programmatic dependent (the random streams) may start once every CTA is resident
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");

@@ -200,12 +200,34 @@ struct Sweep {
 // wait[w + 1]) -- padded to kWideHdrBytes, the waits (uint32 row << 16 |
 // count, padded to 16 bytes), the segments (chunk0 relative to the block's
 // first chunk), then the chunks.
-constexpr int kWideWarps = 16;
+// Ring and occupancy of the wide solve (compile-time; the level programs are
+// built for the same values). Measured on B200 (config 4, corrected build):
+// two stages of 16 KB and one CTA per SM leave the most L1 to the tiles'
+// vectors (phase 0 1.30 ms against 1.69 ms with four stages and two CTAs per
+// SM, 1.75 ms with 8 KB stages); four chunks' loads in flight per warp beat
+// three and six.
+#ifndef SB_WIDE_STAGES
+#define SB_WIDE_STAGES 2
+#endif
+#ifndef SB_WIDE_STAGE_BYTES
+#define SB_WIDE_STAGE_BYTES 16384
+#endif
+#ifndef SB_WIDE_GROUP
+#define SB_WIDE_GROUP 4
+#endif
+#ifndef SB_WIDE_CTAS
+#define SB_WIDE_CTAS 1
+#endif
+#ifndef SB_WIDE_WARPS
+#define SB_WIDE_WARPS 16
+#endif
+constexpr int kWideWarps = SB_WIDE_WARPS;
 constexpr int kWideEnvs = 32;
-constexpr int kWideStageBytes = 16384;
-constexpr int kWideStages = 4;
-constexpr int kWideHdrBytes = 144;
-constexpr int kWideGroup = 3;   // chunks whose source loads a solver warp issues together
+constexpr int kWideStageBytes = SB_WIDE_STAGE_BYTES;
+constexpr int kWideStages = SB_WIDE_STAGES;
+constexpr int kWideHdrBytes = (8 * (kWideWarps + 1) + 15) / 16 * 16;
+constexpr int kWideGroup = SB_WIDE_GROUP;   // chunks whose source loads a solver warp issues together
+constexpr int kWideCtas = SB_WIDE_CTAS;     // wide-solve CTAs per SM (register and shared-memory budget)
 static_assert(kWideHdrBytes >= 8 * (kWideWarps + 1) && kWideHdrBytes % 16 == 0, "level header");
 struct WideSeg {
     uint32_t row;      // the row whose value the segment updates

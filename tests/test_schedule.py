@@ -383,7 +383,12 @@ def test_ring_protocol(built, tmp_path, config, index):
                 walk(prog, ring)
 
 
-WIDE_STAGES, WIDE_HDR = 4, 144   # csrc/sbenv_dev.h kWideStages, kWideHdrBytes
+def _wide_config(lib):
+    """(solver warps, ring stages, stage bytes, header bytes) of the build."""
+    cfg = (ctypes.c_int * 6)()
+    lib.sb_wide_config(cfg)
+    assert cfg[0] == lib.sb_wide_warps()
+    return cfg[0], cfg[1], cfg[2], cfg[3]
 
 
 def _wide_program(lib, blob, sweep):
@@ -397,7 +402,7 @@ def _wide_program(lib, blob, sweep):
     info = (ctypes.c_int64 * 8)()
     assert lib.sb_wide_schedule(b, sweep, info, None, None) == 1
     nlev, nbytes = info[0], info[6]
-    W = lib.sb_wide_warps()
+    W, _, stage_bytes, hdr_bytes = _wide_config(lib)
     off = np.zeros(nlev + 1, np.uint32)
     raw = np.zeros(max(nbytes, 1), np.uint8)
     assert lib.sb_wide_schedule(b, sweep, info, off.ctypes.data, raw.ctypes.data) == 0
@@ -405,12 +410,12 @@ def _wide_program(lib, blob, sweep):
     levels = []
     for lv in range(nlev):
         blk = raw[off[lv]:off[lv + 1]].tobytes()
-        assert len(blk) <= 16384 and len(blk) % 16 == 0
+        assert len(blk) <= stage_bytes and len(blk) % 16 == 0
         hdr = struct.unpack_from(f"<{2 * (W + 1)}i", blk, 0)
         seg0, wait0 = hdr[:W + 1], hdr[W + 1:]
         nseg, nwait = seg0[W], wait0[W]
-        waits = struct.unpack_from(f"<{nwait}I", blk, WIDE_HDR)
-        s0 = WIDE_HDR + 4 * ((nwait + 3) // 4 * 4)
+        waits = struct.unpack_from(f"<{nwait}I", blk, hdr_bytes)
+        s0 = hdr_bytes + 4 * ((nwait + 3) // 4 * 4)
         segs = np.frombuffer(blk, "<u4", 4 * nseg, s0).reshape(nseg, 4)
         c0 = s0 + 16 * nseg
         nch = (len(blk) - c0) // 48
@@ -449,7 +454,7 @@ class _WideState:
         self.next_stage = 0
 
 
-def _wide_execute(prog, st, backward, terms, diag):
+def _wide_execute(prog, st, backward, terms, diag, stages):
     """Runs a sweep's levels on one env's vector with the kernel's semantics
     (exact build: a rounded product and a rounded subtraction per term, the
     division by the diagonal) and checks the schedule's rules on the way: a
@@ -467,7 +472,7 @@ def _wide_execute(prog, st, backward, terms, diag):
         touched, done = set(), []
         for w, (waits, segs) in enumerate(warps):
             def covered(r, count):
-                if count <= 0 or st.warp[r] == w or st.stage[r] <= S - WIDE_STAGES:
+                if count <= 0 or st.warp[r] == w or st.stage[r] <= S - stages:
                     return True
                 return waits.get(r, 0) >= count
 
@@ -524,8 +529,9 @@ def test_wide_program_replays_reference_solve(built, tmp_path, config, index):
     assert fwd[1][4] == L.nnz - n and bwd[1][4] == U.nnz - n     # every term once
     rhs = np.random.default_rng(index).standard_normal(n) * 300.0
     st = _WideState(rhs, n)
-    _wide_execute(fwd, st, False, tl, None)
-    z = _wide_execute(bwd, st, True, tu, U.tocsc().diagonal())
+    stages = _wide_config(lib)[1]
+    _wide_execute(fwd, st, False, tl, None, stages)
+    z = _wide_execute(bwd, st, True, tu, U.tocsc().diagonal(), stages)
     assert np.array_equal(z, _push_reference(L, U, rhs))
 
 
