@@ -479,7 +479,7 @@ def run_ours(args) -> None:
     achieved = bytes_launch / (k_ms["k_solve"] / 1e3) / 1e9
     fp64_achieved = flops_launch / (k_ms["k_solve"] / 1e3) / 1e12
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                "traffic": profile_traffic(args.workload) if n == WORKLOADS[args.workload]["envs"] else None, "kernel": "the solve: k_solve<0> (first L/U sweep pair), k_dense, phase 1 (k_correct in the corrected build), by dense class",
+                "traffic": profile_traffic(args.workload) if n == WORKLOADS[args.workload]["envs"] else None, "kernel": "the solve: the first L/U sweep pair (k_wide0 on 32-env tiles, or k_solve<0> on slabs), k_dense, phase 1 (k_correct in the corrected build), by dense class",
                 "peak_source": peak_src, "kernel_ms": k_ms["k_solve"], "algorithmic_bytes_per_launch": bytes_launch,
                 "per_kernel_ms": k_ms,
                 "fp64": {"achieved_tflops": fp64_achieved, "peak_tflops": fp64_peak, "frac": fp64_achieved / fp64_peak,
