@@ -63,3 +63,31 @@ def test_fold_config3(scenario_cache, build):
     d = config_dir(3, scenario_cache, n_steps=200)
     w = run_parity(d, n=2, steps=24, seed=4, temp_every=4, env_kw=build, tolerant=True)
     print(build, "configuration 3:", w)
+
+
+def test_wide_corrected_config1_month(scenario_cache):
+    """The bench's stated path at the north star's batch sizes -- the corrected
+    build with the first solve on wide tiles (k_wide0: fused multiply-adds,
+    the diagonal's reciprocal) -- through a whole month against the
+    reference's C core, with no resynchronisation."""
+    from neurips2026_smart_building_challenge_b200 import config_dir
+
+    d = config_dir(1, scenario_cache)
+    w = run_parity(d, n=2, steps=8640 + 24, seed=0, temp_every=12, oracle="reference", wild=False,
+                   env_kw={**BUILDS["corrected"], "wide": 1}, tolerant=True)
+    print("wide corrected configuration-1 month:", w)
+    assert w["field_abs_K"] < 1e-6
+
+
+def test_wide_config2_mix_and_config3(scenario_cache, build):
+    """Both fast builds with the first solve on wide tiles: the config-2 mix
+    (six groups) and configuration 3 (128 x 96 cells, 81 coupled VAVs)."""
+    from neurips2026_smart_building_challenge_b200 import config_dir
+
+    kw = {**build, "wide": 1}
+    d = config_dir(2, scenario_cache, n_steps=400)
+    w = run_parity(d, n=60, steps=40, seed=2, temp_every=5, groups=30, beta_mix=True, env_kw=kw, tolerant=True)
+    print(build, "wide, configuration-2 mix:", w)
+    d = config_dir(3, scenario_cache, n_steps=200)
+    w = run_parity(d, n=2, steps=24, seed=4, temp_every=4, env_kw=kw, tolerant=True)
+    print(build, "wide, configuration 3:", w)
