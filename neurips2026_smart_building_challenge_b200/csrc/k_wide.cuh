@@ -22,6 +22,7 @@ namespace sbenv {
 
 constexpr int kWideThreads = (kWideWarps + 1) * 32;   // the solver warps and the producer warp
 constexpr uint32_t kWideSpin = 1u << 22;                // polls of one ready count before the wait gives up
+constexpr int kWideRun = 8;                             // rows of one forcing / write-back run of a warp
 
 // Shared memory of a wide-solve CTA: the stage ring, its full and empty
 // mbarriers, the rows' ready counts and the abort word.
@@ -221,12 +222,13 @@ k_wide0(const StepCtx* __restrict__ ctx, const WideTile* __restrict__ tiles) {
     const double* Tg = g.T + (size_t)local * ncv;
     const double* Mg = g.M + (size_t)local * n;
 
-    // ---- forcing (sb_fdm.c:146-152): runs of four rows per solver warp, so a
-    // lane's four field and mass loads share a sector ----
-    for (int i0 = warp * 4; solver && i0 < n; i0 += kWideWarps * 4) {
-        double Ti[4], Mi[4], qi[4];
+    // ---- forcing (sb_fdm.c:146-152): runs of kWideRun rows per solver warp,
+    // all their loads in flight together; a lane's loads of one run share
+    // sectors of its env's field and mass ----
+    for (int i0 = warp * kWideRun; solver && i0 < n; i0 += kWideWarps * kWideRun) {
+        double Ti[kWideRun], Mi[kWideRun], qi[kWideRun];
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
+        for (int j = 0; j < kWideRun; j++) {
             const int i = min(i0 + j, n - 1);
             const int z = __ldg(g.zone_of_row + i);
             Ti[j] = Tg[i];
@@ -234,7 +236,7 @@ k_wide0(const StepCtx* __restrict__ ctx, const WideTile* __restrict__ tiles) {
             qi[j] = z < 0 ? 0.0 : D[L.qdiv + z];
         }
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
+        for (int j = 0; j < kWideRun; j++) {
             const int i = i0 + j;
             if (i >= n) break;
             double b = dadd(dmul(__ldg(g.cap + i), Ti[j]), qi[j]);
@@ -273,9 +275,18 @@ k_wide0(const StepCtx* __restrict__ ctx, const WideTile* __restrict__ tiles) {
         for (int r = warp; solver && r < k; r += kWideWarps) {
             double acc = 0.0;
             const int p1 = __ldg(rp + r + 1);
-            for (int p = __ldg(rp + r); p < p1; p++) {
-                const double xv = Xl[(size_t)__ldg(rpos + p) * kWideEnvs];
-                acc = Tol ? fma(__ldg(rx + p), xv, acc) : dadd(acc, dmul(__ldg(rx + p), xv));
+            // four terms' loads in flight, then their products summed in order
+            for (int p0 = __ldg(rp + r); p0 < p1; p0 += 4) {
+                double xv[4], cv[4];
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const int p = min(p0 + u, p1 - 1);
+                    xv[u] = Xl[(size_t)__ldg(rpos + p) * kWideEnvs];
+                    cv[u] = __ldg(rx + p);
+                }
+#pragma unroll
+                for (int u = 0; u < 4; u++)
+                    if (p0 + u < p1) acc = Tol ? fma(cv[u], xv[u], acc) : dadd(acc, dmul(cv[u], xv[u]));
             }
             if (live && act) ctx->airq[(size_t)env * ctx->k_max + r] = dmul(D[L.ag + r], dsub(D[L.aT + r], acc));
         }
@@ -284,10 +295,14 @@ k_wide0(const StepCtx* __restrict__ ctx, const WideTile* __restrict__ tiles) {
     // adds to it ----
     if (live && solver) {
         double* Tw = g.T + (size_t)local * ncv;
-        for (int i0 = warp * 4; i0 < n; i0 += kWideWarps * 4)
+        for (int i0 = warp * kWideRun; i0 < n; i0 += kWideWarps * kWideRun) {
+            double y[kWideRun];
 #pragma unroll
-            for (int j = 0; j < 4; j++)
-                if (i0 + j < n) Tw[i0 + j] = Xl[(size_t)(i0 + j) * kWideEnvs];
+            for (int j = 0; j < kWideRun; j++) y[j] = Xl[(size_t)min(i0 + j, n - 1) * kWideEnvs];
+#pragma unroll
+            for (int j = 0; j < kWideRun; j++)
+                if (i0 + j < n) Tw[i0 + j] = y[j];
+        }
     }
 }
 
