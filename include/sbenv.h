@@ -199,10 +199,12 @@ const char* sb_last_error(void);
 int sb_device_status(void);
 /* Failure test of the bounded waits (no counterpart in the reference): on = 1
  * makes warp 0 of every solve CTA wait, at the start of its L sweep, for a
- * row of the sweep program that no warp publishes, polling at most
- * spin_limit times (0: the production limit, 2^22 polls, about a second), so
- * the wait runs out and the next puf_step reports code 5 without a fault or a
- * hang; on = 0 turns it off (and restores the limit). Synchronises. 0 or -1. */
+ * row of the sweep program that no warp publishes (wide tiles: for a ready
+ * count that no row reaches), polling at most spin_limit times (0: the
+ * production limit, 2^22 polls, about a second), so the wait runs out, the
+ * CTA's other warps and its program producer leave their waits, and the next
+ * puf_step reports code 5 without a fault or a hang; on = 0 turns it off (and
+ * restores the limit). Synchronises. 0 or -1. */
 int sb_test_stall(int on, unsigned int spin_limit);
 /* Shape of the loaded batch: out[8] = {n_env, n_scenarios, n_groups, obs_len_max,
  * n_cont_max, n_disc_max, first-solve CTAs (slabs, or 32-env tiles with the wide

@@ -48,7 +48,18 @@ struct WideShared {
     uint64_t* empty;    // [kWideStages] every solver warp is done with the stage
     uint16_t* ready;    // [n + 1] the rows' ready counts
     volatile int* abort;
+    uint32_t spin;      // polls of one ready count (kWideSpin unless a failure test lowers it)
+    bool stall;         // failure test: solver warp 0 waits for a count no row reaches
 };
+
+// Bounded mbarrier wait that also gives up once another warp has aborted.
+__device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort) {
+    for (uint32_t it = 0; it < (1u << 22); it++) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 255u) == 255u && *abort) return false;
+    }
+    return false;
+}
 
 // The level block of stage t: the L sweep's levels, then the U sweep's.
 __device__ __forceinline__ void stage_src(const GroupDev& g, int t, const uint8_t*& src, uint32_t& bytes) {
@@ -66,7 +77,7 @@ __device__ void wide_produce(const GroupDev& g, const WideShared& sh, int total)
     int issued = 0;
     for (int t = 0; t < total && !*sh.abort; t++) {
         const int slot = t % kWideStages;
-        if (t >= kWideStages && !mbar_wait_bounded(sh.empty + slot, (uint32_t)(t / kWideStages - 1) & 1u)) {
+        if (t >= kWideStages && !mbar_wait_or_abort(sh.empty + slot, (uint32_t)(t / kWideStages - 1) & 1u, sh.abort)) {
             atomicCAS((int*)sh.abort, 0, kErrRingTimeout);
             break;
         }
@@ -88,7 +99,7 @@ __device__ void wide_produce(const GroupDev& g, const WideShared& sh, int total)
 // (tolerant). Warp-uniform; false if a wait gave up.
 template <bool Tol>
 __device__ __forceinline__ bool wide_level(const uint8_t* blk, const WideShared& sh, double* Xl,
-                                           const double* __restrict__ wdiag, int warp, int lane) {
+                                           const double* __restrict__ wdiag, int warp, int lane, bool stall) {
     const char* xb = reinterpret_cast<const char*>(Xl);
     const int32_t* hdr = reinterpret_cast<const int32_t*>(blk);
     const int a = hdr[warp], b = hdr[warp + 1], nseg = hdr[kWideWarps];
@@ -98,13 +109,15 @@ __device__ __forceinline__ bool wide_level(const uint8_t* blk, const WideShared&
     const uint4* segs = reinterpret_cast<const uint4*>(segb);
     const WideChunk* chunks = reinterpret_cast<const WideChunk*>(segb + (size_t)nseg * sizeof(WideSeg));
     bool ok = true;
-    for (int i = w0 + lane; i < w1 && ok; i += 32) {
-        const uint32_t e = waits[i];
+    // failure test: lane 0 also waits for row 0 to reach a count no row reaches
+    const int first = stall ? w0 - 1 : w0;
+    for (int i = first + lane; i < w1 && ok; i += 32) {
+        const uint32_t e = i < w0 ? 0xFFFFu : waits[i];
         const uint16_t* f = sh.ready + (e >> 16);
         const uint32_t need = e & 0xFFFFu;
         uint32_t spins = 0;
         while (ld_acquire_u16(f) < need) {
-            if (++spins >= kWideSpin || ((spins & 1023u) == 0 && *sh.abort)) {
+            if (++spins >= sh.spin || ((spins & 1023u) == 0 && *sh.abort)) {
                 atomicCAS((int*)sh.abort, 0, kErrWaitTimeout);
                 ok = false;
                 break;
@@ -166,9 +179,11 @@ template <bool Tol>
 __device__ void wide_solve(const GroupDev& g, const WideShared& sh, int total, double* Xl, int warp, int lane) {
     for (int t = 0; t < total; t++) {
         const int slot = t % kWideStages;
-        bool ok = !*sh.abort && mbar_wait_bounded(sh.full + slot, (uint32_t)(t / kWideStages) & 1u);
+        bool ok = !*sh.abort && mbar_wait_or_abort(sh.full + slot, (uint32_t)(t / kWideStages) & 1u, sh.abort);
         ok = __all_sync(0xffffffffu, ok);
-        if (ok) ok = wide_level<Tol>(sh.slots + (size_t)slot * kWideStageBytes, sh, Xl, g.wdiag, warp, lane);
+        if (ok)
+            ok = wide_level<Tol>(sh.slots + (size_t)slot * kWideStageBytes, sh, Xl, g.wdiag, warp, lane,
+                                 sh.stall && warp == 0 && t == 0);
         __syncwarp();
         if (lane == 0) {
             if (!ok) atomicCAS((int*)sh.abort, 0, kErrRingTimeout);
@@ -201,6 +216,8 @@ k_wide0(const StepCtx* __restrict__ ctx, const WideTile* __restrict__ tiles) {
     sh.empty = sh.full + kWideStages;
     sh.ready = reinterpret_cast<uint16_t*>(sh.empty + kWideStages);
     sh.abort = reinterpret_cast<volatile int*>(wsm + wide_smem_bytes(n) - 16);
+    sh.stall = ctx->test_ctl[0] != 0;
+    sh.spin = ctx->test_ctl[1] > 0 ? (uint32_t)ctx->test_ctl[1] : kWideSpin;
     const int total = g.wfwd.nlev + (g.fold ? 0 : g.wbwd.nlev);
     if (tid == 0) {
         *sh.abort = 0;

@@ -259,19 +259,21 @@ def test_second_reset_matches_oracle(scenario_cache):
         env.close()
 
 
-def test_bounded_wait_runs_out_and_reports(scenario_cache):
+@pytest.mark.parametrize("wide", [0, 1], ids=["slabs", "wide"])
+def test_bounded_wait_runs_out_and_reports(scenario_cache, wide):
     """A sweep wait that can never be satisfied (sb_test_stall: warp 0 waits for
     a row no warp publishes, under a short spin limit) ends with status 5 and
     no fault or hang; after puf_reset the env steps exactly as the oracle does.
-    The flag waits that the failure test stalls belong to the shared-memory
-    slab solve (wide = 0)."""
+    Both first solves: the slabs' ready-flag waits (wide = 0) and the wide
+    tiles' ready-count waits (wide = 1), whose other warps and program producer
+    then leave their own waits."""
     import torch
 
     from neurips2026_smart_building_challenge_b200 import config_dir
 
     d = config_dir(1, scenario_cache, n_steps=60)
     n = 2
-    env = vec(n, d, wide=0)
+    env = vec(n, d, wide=wide)
     try:
         path = scenario_paths(d)[0]
         rng = np.random.default_rng(16)
