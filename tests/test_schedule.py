@@ -469,6 +469,11 @@ def _wide_execute(prog, st, backward, terms, diag, stages):
     final = [not backward and not terms[i] for i in range(n)]
     for lv, warps in enumerate(levels):
         S = st.next_stage + lv             # stages run on over the sweeps
+        # deadlock freedom: every count a warp waits for is made at an earlier
+        # stage, so the warp still running the earliest unfinished stage never waits
+        for w, (waits, _) in enumerate(warps):
+            for r, c in waits.items():
+                assert st.cnt[r] >= c and st.warp[r] != w, f"stage {S}: warp {w} waits for row {r} count {c}"
         touched, done = set(), []
         for w, (waits, segs) in enumerate(warps):
             def covered(r, count):
@@ -511,15 +516,16 @@ def _wide_execute(prog, st, backward, terms, diag, stages):
     return np.array(st.x[:n])
 
 
-@pytest.mark.parametrize("config,index", [(1, 0), (2, 23), (3, 0)])
-def test_wide_program_replays_reference_solve(built, tmp_path, config, index):
+@pytest.mark.parametrize("config,index,notch", [(1, 0, False), (1, 0, True), (2, 23, False), (3, 0, False)])
+def test_wide_program_replays_reference_solve(built, tmp_path, config, index, notch):
     """The wide solve's level programs: every row receives exactly the
     reference's terms in push order, a segment reads only complete rows, every
     row produced recently by another warp is acquired, and the L then U replay
     equals the column-push solve bit for bit."""
     import neurips2026_smart_building_challenge_b200 as pkg
 
-    blob = pkg.write_scenario(tmp_path / "s.sbb", pkg.preset(config, index, n_steps=10))
+    over = {"notch_rows": 3, "notch_cols": 4} if notch else {}   # unsolved cells: a factor of fewer rows
+    blob = pkg.write_scenario(tmp_path / "s.sbb", pkg.preset(config, index, n_steps=10, **over))
     b = Blob(blob)
     L, U = b.csc("lu_L"), b.csc("lu_U")
     n = L.shape[0]
